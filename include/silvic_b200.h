@@ -1,0 +1,309 @@
+/*
+ * silvic_b200.h — C ABI of the B200 (sm_100a) training backend for silvic.
+ *
+ * This header is the drop-in boundary. It mirrors silvic-core's device plugin API, `trait Backend`
+ * (crates/silvic-core/src/backend/mod.rs:115-179), method by method, with flat C types in place of the Rust
+ * structs. It also exports a device-resident trainer: the leaf-wise learner
+ * (crates/silvic-core/src/learner.rs:121-404) and the boosting loop (crates/silvic-core/src/boosting.rs:227-324),
+ * run on the GPU without host round trips per split.
+ *
+ * Conventions
+ *  - Every function returns an int status: SB2_OK (0) or one of the SB2_E* codes below, which map the kinds of
+ *    `SilvicError` (crates/silvic-core/src/error.rs:28-65). The message of the last failure on a handle is
+ *    available through sb2_last_error(); failures without a handle (creation) through sb2_global_error().
+ *  - Every pointer is a plain host pointer unless the name ends in `_dev` (device pointers, see the "kernel
+ *    entry points" section).
+ *  - A handle is not thread-safe: one thread at a time, as `&mut self` in Rust. Handles are independent.
+ *  - Multi-GPU: one process per GPU. Each process creates its handle on its own device with the rank's
+ *    contiguous row shard (`row_offset` = rows of lower ranks) and joins the ranks with sb2_join_ranks().
+ *    Histogram reductions then run over NCCL inside the handle, so the caller's own Collective sees one rank.
+ */
+#ifndef SILVIC_B200_H
+#define SILVIC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (SilvicError kinds) ---------------------------------------------------------------------- */
+enum {
+    SB2_OK = 0,
+    SB2_ECONFIG = 1,      /* SilvicError::Config */
+    SB2_EDATA = 2,        /* SilvicError::Data */
+    SB2_EINTERNAL = 3,    /* SilvicError::Internal */
+    SB2_EDEVICE = 4,      /* SilvicError::Device: CUDA failure, misuse, bad range or buffer length */
+    SB2_ECOLLECTIVE = 5,  /* SilvicError::Collective: NCCL failure or timeout */
+    SB2_EMODEL = 6,       /* SilvicError::Model */
+    SB2_EUNSUPPORTED = 7, /* SilvicError::Unsupported */
+};
+
+/* ---- data types (mirrors of silvic-core structs) ----------------------------------------------------------- */
+
+enum { SB2_NUMERICAL = 0, SB2_CATEGORICAL = 1, SB2_TRIVIAL = 2 };
+
+/* FeatureMeta (crates/silvic-core/src/data/mod.rs:25-36) with its BinMapper (data/bin_mapper.rs:26-41). */
+typedef struct sb2_feature {
+    uint32_t num_bins;    /* bins in the histogram, NaN bin included; 0 for a trivial feature */
+    uint32_t group;       /* the feature's group */
+    uint32_t column;      /* byte offset of the feature in its group's row */
+    uint32_t hist_offset; /* index of the feature's bin 0 in the flat histogram */
+    uint32_t kind;        /* SB2_NUMERICAL / SB2_CATEGORICAL / SB2_TRIVIAL */
+    uint32_t nan_bin;     /* numerical: the last bin holds NaN */
+    const double* upper_bounds; /* numerical: ascending bin upper bounds, the last +inf */
+    uint32_t num_upper_bounds;
+    uint32_t pad_;
+    double min_value, max_value; /* sampled min and max (feature_infos) */
+} sb2_feature;
+
+/* FeatureGroup (crates/silvic-core/src/data/mod.rs:49-59): row-major bins, data[row * row_stride + column]. */
+typedef struct sb2_group {
+    const uint8_t* data;
+    uint32_t row_stride;
+    uint32_t hist_offset;
+    uint32_t total_bins;
+    uint32_t num_features;
+    const uint32_t* features; /* indices into the feature array, in column order */
+} sb2_group;
+
+/* BinnedDataset (crates/silvic-core/src/data/mod.rs:62-74). The arrays are read during the call that takes the
+ * dataset (sb2_load copies them to the device) and are not kept. */
+typedef struct sb2_dataset {
+    uint64_t num_rows;
+    uint64_t row_offset; /* global id of local row 0 */
+    uint32_t num_features;
+    uint32_t num_groups;
+    uint32_t total_bins;
+    uint32_t num_queries;
+    const sb2_feature* features;
+    const sb2_group* groups;
+    const float* label;
+    const float* weight;              /* NULL when unweighted */
+    const uint32_t* query_boundaries; /* NULL, or num_queries + 1 row boundaries */
+} sb2_dataset;
+
+/* ObjectiveSetup (crates/silvic-core/src/backend/mod.rs:58-71), pointwise objectives. */
+enum { SB2_REGRESSION = 0, SB2_BINARY = 1, SB2_LAMBDARANK = 2 };
+typedef struct sb2_objective {
+    int32_t kind;
+    int32_t pad_;
+    double sigmoid; /* binary */
+} sb2_objective;
+
+/* LeafRange (crates/silvic-core/src/backend/mod.rs:17-22): partition[begin .. begin + count]. */
+typedef struct sb2_leaf_range {
+    uint32_t begin;
+    uint32_t count;
+} sb2_leaf_range;
+
+/* BinSplit (crates/silvic-core/src/backend/mod.rs:26-38): bins set in left_bins go left. */
+typedef struct sb2_bin_split {
+    uint32_t group;
+    uint32_t column;
+    uint32_t left_bins[8];
+} sb2_bin_split;
+
+/* DeviceNode (crates/silvic-core/src/backend/mod.rs:43-47): children >= 0 are nodes, < 0 are ~leaf. */
+typedef struct sb2_device_node {
+    sb2_bin_split split;
+    int32_t left;
+    int32_t right;
+} sb2_device_node;
+
+/* QuantSpec (crates/silvic-core/src/quantize.rs:35-51). */
+typedef struct sb2_quant_spec {
+    float inv_grad_scale;
+    float inv_hess_scale;
+    double grad_scale;
+    double hess_scale;
+    int32_t grad_max_q;
+    int32_t hess_max_q;
+    int32_t constant_hessian;
+    int32_t stochastic;
+    uint32_t seed;
+    uint32_t iteration;
+} sb2_quant_spec;
+
+/* GradientStats (crates/silvic-core/src/backend/mod.rs:75-78). */
+typedef struct sb2_gradient_stats {
+    double max_abs_grad;
+    double max_hess;
+} sb2_gradient_stats;
+
+/* BagSpec (crates/silvic-core/src/backend/mod.rs:82-90). kind 0 = All, 1 = Bernoulli. */
+typedef struct sb2_bag_spec {
+    int32_t kind;
+    uint32_t seed;
+    uint32_t round;
+    uint32_t pad_;
+    double fraction;
+} sb2_bag_spec;
+
+enum { SB2_LEFT = 0, SB2_RIGHT = 1 }; /* Side (crates/silvic-core/src/backend/mod.rs:94-113) */
+
+/* SplitConfig (crates/silvic-core/src/split.rs:50-61), numerical fields. */
+typedef struct sb2_split_config {
+    int64_t min_data_in_leaf;
+    double min_sum_hessian_in_leaf;
+    double lambda_l1;
+    double lambda_l2;
+    double min_gain_to_split;
+} sb2_split_config;
+
+/* SplitInfo (crates/silvic-core/src/split.rs:122-132) of a numerical split, plus LeafSplit::splittable. */
+typedef struct sb2_split_info {
+    int32_t found;        /* 0: the leaf has no split (LeafSplit::best == None) */
+    int32_t feature;
+    double gain;
+    uint32_t threshold;   /* SplitRule::Numerical: bins 0..=threshold go left */
+    int32_t default_left;
+    double left_grad, left_hess;   /* child sums in histogram units */
+    int64_t left_count;            /* estimated from hessians */
+    double right_grad, right_hess;
+    int64_t right_count;
+    double left_output, right_output;
+} sb2_split_info;
+
+/* Training parameters (crates/silvic-core/src/config.rs:73-116, defaults :123-165), the subset this backend
+ * trains with. sb2_default_params() fills the reference defaults. */
+typedef struct sb2_params {
+    int32_t objective;            /* SB2_REGRESSION / SB2_BINARY */
+    int32_t num_iterations;
+    double learning_rate;
+    int32_t num_leaves;
+    int32_t max_depth;            /* <= 0: no limit */
+    int64_t min_data_in_leaf;
+    double min_sum_hessian_in_leaf;
+    double lambda_l1;
+    double lambda_l2;
+    double min_gain_to_split;
+    double bagging_fraction;
+    int32_t bagging_freq;
+    uint32_t bagging_seed;
+    double feature_fraction;
+    uint32_t feature_fraction_seed;
+    uint32_t data_random_seed;
+    int32_t boost_from_average;
+    int32_t use_quantized_grad;
+    double sigmoid;
+    int32_t num_grad_quant_bins;
+    int32_t quant_train_renew_leaf;
+    int32_t stochastic_rounding;
+    int32_t pad_;
+} sb2_params;
+
+/* One tree in LightGBM 3.3.5 array layout (crates/silvic-core/src/tree.rs:47-73). The arrays belong to the
+ * model that returned the view and live as long as it. Internal-node arrays hold num_leaves - 1 entries. */
+typedef struct sb2_tree_view {
+    int32_t num_leaves;
+    int32_t pad_;
+    double shrinkage;
+    const int32_t* split_feature;
+    const float* split_gain;
+    const double* threshold;
+    const uint32_t* threshold_bin; /* the bin threshold of each split (bins <= threshold go left) */
+    const int8_t* decision_type;
+    const int32_t* left_child;
+    const int32_t* right_child;
+    const double* leaf_value;
+    const double* leaf_weight;
+    const int64_t* leaf_count;
+    const double* internal_value;
+    const double* internal_weight;
+    const int64_t* internal_count;
+} sb2_tree_view;
+
+typedef struct sb2_backend sb2_backend;
+typedef struct sb2_model sb2_model;
+
+/* ---- library ------------------------------------------------------------------------------------------------ */
+
+/* The last error of a call that had no handle to record it on (sb2_create, sb2_nccl_unique_id). */
+int sb2_global_error(char* buf, size_t len);
+
+/* Reference defaults of crates/silvic-core/src/config.rs:123-165. */
+void sb2_default_params(sb2_params* out);
+
+/* ---- backend handle: trait Backend (crates/silvic-core/src/backend/mod.rs:115-179) ------------------------- */
+
+/* A backend on CUDA device `device` (the calling process's GPU). */
+int sb2_create(int device, sb2_backend** out);
+int sb2_destroy(sb2_backend* b);
+int sb2_last_error(const sb2_backend* b, char* buf, size_t len);
+/* Backend::name */
+int sb2_name(const sb2_backend* b, char* buf, size_t len);
+
+/* Backend::load: copies the training set to the device and lays it out in 32-feature tiles. Datasets with
+ * categorical features return SB2_EUNSUPPORTED (no device categorical scan). */
+int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* objective);
+/* Backend::init_scores (dataset 0, the training set) */
+int sb2_init_scores(sb2_backend* b, int dataset, double value);
+/* Backend::compute_gradients */
+int sb2_compute_gradients(sb2_backend* b, sb2_gradient_stats* out);
+/* Backend::quantize */
+int sb2_quantize(sb2_backend* b, const sb2_quant_spec* spec);
+/* Backend::reset_partition */
+int sb2_reset_partition(sb2_backend* b, const sb2_bag_spec* bag, uint32_t* out_rows);
+/* Backend::set_histogram_features: used[f] != 0 for every feature whose bins the next histograms must fill. */
+int sb2_set_histogram_features(sb2_backend* b, const uint8_t* used, size_t num_features);
+/* Backend::histogram (quantized mode): out holds 2 * total_bins doubles, [g, h] integer units per bin. */
+int sb2_histogram(sb2_backend* b, sb2_leaf_range leaf, int quantized, double* out, size_t len);
+/* Backend::partition: stable, in place; returns the left count. */
+int sb2_partition(sb2_backend* b, sb2_leaf_range leaf, const sb2_bin_split* split, uint32_t* out_left);
+/* Backend::partition_and_histogram: partition, then the histogram of the `side` child. */
+int sb2_partition_and_histogram(sb2_backend* b, sb2_leaf_range leaf, const sb2_bin_split* split, int side,
+                                int quantized, double* out, size_t len, uint32_t* out_left);
+/* Backend::leaf_sums: out holds 2 * num_leaves int64, [sum rint(g*gs), sum rint(h*hs)] per leaf. */
+int sb2_leaf_sums(sb2_backend* b, const sb2_leaf_range* leaves, size_t num_leaves, float grad_scale,
+                  float hess_scale, int64_t* out);
+/* Backend::add_tree: nodes may be empty (single leaf). */
+int sb2_add_tree(sb2_backend* b, const sb2_device_node* nodes, size_t num_nodes, const float* leaf_values,
+                 size_t num_leaves);
+/* Backend::scores of the training set. */
+int sb2_scores(sb2_backend* b, int dataset, float* out, size_t len);
+
+/* Test access to backend state (CpuBackend's tests read the same fields). */
+int sb2_read_partition(sb2_backend* b, uint32_t* out, size_t len);
+int sb2_read_packed(sb2_backend* b, int32_t* out, size_t len);
+int sb2_write_gradients(sb2_backend* b, const float* grad, const float* hess, size_t len);
+int sb2_read_gradients(sb2_backend* b, float* grad, float* hess, size_t len);
+
+/* ---- split search: split::find_best_split (crates/silvic-core/src/split.rs:919-961) ------------------------ */
+
+/* The best numerical split of a leaf from its histogram `hist` (2 * total_bins doubles in histogram units,
+ * integer-valued), over the features with evaluate[f] != 0, run on the device. splittable (num_features bytes)
+ * receives LeafSplit::splittable. */
+int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const uint8_t* evaluate,
+                        double sum_grad, double sum_hess, int64_t count, double grad_scale, double hess_scale,
+                        const sb2_split_config* cfg, sb2_split_info* out, uint8_t* splittable);
+
+/* ---- multi-GPU --------------------------------------------------------------------------------------------- */
+
+/* An NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */
+int sb2_nccl_unique_id(uint8_t* out, size_t len);
+/* Joins `world` ranks (one process per GPU) through an NCCL communicator; call after sb2_load on every rank. */
+int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int world, int rank);
+
+/* ---- device-resident training: boosting::train (crates/silvic-core/src/boosting.rs:63-149) ------------------ */
+
+/* Trains params->num_iterations trees on the loaded training set. Every split runs on the device: partition,
+ * smaller-child histogram, (NCCL reduction), sibling subtraction, split scan and leaf choice; the host only reads
+ * each finished tree. `init_score` is computed by the caller over every rank's labels in row order
+ * (objective::init_score, crates/silvic-core/src/objective/mod.rs:92-109). */
+int sb2_train(sb2_backend* b, const sb2_params* params, double init_score, sb2_model** out);
+/* objective::init_score (crates/silvic-core/src/objective/mod.rs:92-109, regression.rs:8-17, binary.rs:8-21) over
+ * `n` labels in row order: BoostFromAverage, 0 when params->boost_from_average is off. */
+int sb2_boost_from_average(const sb2_params* params, const float* label, const float* weight, size_t n, double* out);
+int sb2_model_free(sb2_model* m);
+int sb2_model_num_trees(const sb2_model* m);
+int sb2_model_tree(const sb2_model* m, int index, sb2_tree_view* out);
+/* Seconds the device spent in each of the last sb2_train's iterations (CUDA events), and split steps taken. */
+int sb2_model_iteration_seconds(const sb2_model* m, double* out, size_t len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SILVIC_B200_H */

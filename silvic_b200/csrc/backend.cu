@@ -1,0 +1,1149 @@
+// backend.cu — the C ABI of include/silvic_b200.h: a B200 backend behind silvic's `trait Backend`
+// (crates/silvic-core/src/backend/mod.rs:115-179) and the device-resident trainer.
+//
+// The handle owns one GPU's copy of its row shard (tiles of bins, labels, scores, gradients, the two partition
+// buffers), the histogram staging and slot buffers, and the learner state the training kernels move. Every call
+// enqueues on the handle's stream; calls that return data wait for it. Misuse returns SB2_EDEVICE with a message,
+// as CpuBackend does (backend/cpu.rs:149-166), never a crash.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "iter.cuh"
+
+using namespace sb2;
+
+namespace {
+
+thread_local std::string g_global_error;
+
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    ~DeviceBuffer() {
+        if (ptr) cudaFree(ptr);
+    }
+    cudaError_t alloc(size_t n) {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = n;
+        return cudaMalloc(&ptr, n == 0 ? 16 : n);
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+struct HostTree {
+    int32_t num_leaves = 1;
+    double shrinkage = 1.0;
+    std::vector<int32_t> split_feature;
+    std::vector<float> split_gain;
+    std::vector<double> threshold;
+    std::vector<uint32_t> threshold_bin;
+    std::vector<int8_t> decision_type;
+    std::vector<int32_t> left_child, right_child;
+    std::vector<double> leaf_value, leaf_weight;
+    std::vector<int64_t> leaf_count;
+    std::vector<double> internal_value, internal_weight;
+    std::vector<int64_t> internal_count;
+};
+
+}  // namespace
+
+struct sb2_model {
+    std::vector<HostTree> trees;
+    std::vector<double> seconds;
+};
+
+struct sb2_backend {
+    int device = 0;
+    int sms = 148;
+    cudaStream_t stream = nullptr;
+    std::string error;
+    std::string name;
+    bool loaded = false;
+
+    // dataset
+    uint64_t num_rows = 0, row_offset = 0;
+    uint32_t num_features = 0, total_bins = 0;
+    sb2_objective objective{};
+    bool weighted = false;
+    std::vector<sb2_feature> features;                 // host copy (upper bounds below)
+    std::vector<std::vector<double>> upper_bounds;
+    std::vector<DevFeature> dev_features;
+    std::vector<Tile> tiles;
+    std::vector<Unit> units;
+    std::vector<std::vector<int32_t>> group_column_feature;  // [group][column] -> feature
+    int hist_smem = 0;
+    int hist_grid = 0;
+    DeviceBuffer bins, d_tiles, d_features, d_lane_feature, d_units;
+    DeviceBuffer label, weight, scores, grad, hess, packed;
+    DeviceBuffer rows[2], ordered[2], flags, tile_left;
+    DeviceBuffer staging, hist_job, step, iter, api_active, candidates, counter, maxima, misc;
+    std::vector<uint8_t> api_used;
+    bool api_used_all = true;
+
+    // multi-GPU
+    ncclComm_t comm = nullptr;
+    int world = 1, rank = 0;
+
+    ~sb2_backend() {
+        if (comm) ncclCommDestroy(comm);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    int fail(int code, const std::string& msg) {
+        error = msg;
+        return code;
+    }
+    int cuda(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return SB2_OK;
+        return fail(SB2_EDEVICE, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+
+    DevData dev_data() const {
+        DevData d{};
+        d.bins = bins.as<uint8_t>();
+        d.tiles = d_tiles.as<Tile>();
+        d.features = d_features.as<DevFeature>();
+        d.lane_feature = d_lane_feature.as<int32_t>();
+        d.num_tiles = static_cast<uint32_t>(tiles.size());
+        d.num_features = num_features;
+        d.total_bins = total_bins;
+        d.num_rows = num_rows;
+        d.row_offset = row_offset;
+        return d;
+    }
+
+    RowArgs row_args() const {
+        RowArgs r{};
+        r.num_rows = num_rows;
+        r.row_offset = row_offset;
+        r.objective = objective.kind;
+        r.sigmoid = objective.sigmoid;
+        r.label = label.as<float>();
+        r.weight = weighted ? weight.as<float>() : nullptr;
+        r.scores = scores.as<float>();
+        r.grad = grad.as<float>();
+        r.hess = hess.as<float>();
+        r.packed = packed.as<int32_t>();
+        return r;
+    }
+
+    // TrainArgs over the buffers the Backend API shares with training.
+    TrainArgs api_train_args() const {
+        TrainArgs a{};
+        a.d = dev_data();
+        a.total_bins = total_bins;
+        a.num_features = num_features;
+        a.step = step.as<Step>();
+        a.staging = staging.as<int>();
+        a.hist_job = hist_job.as<HistJob>();
+        a.iter = iter.as<IterState>();
+        for (int k = 0; k < 2; ++k) {
+            a.rows[k] = rows[k].as<uint32_t>();
+            a.ordered[k] = ordered[k].as<int32_t>();
+        }
+        a.flags = flags.as<uint32_t>();
+        a.tile_left = tile_left.as<uint32_t>();
+        a.candidates = candidates.ptr;
+        a.done_counter = counter.as<unsigned int>();
+        return a;
+    }
+
+    HistArgs hist_args(const uint8_t* active, int* out) const {
+        HistArgs h{};
+        h.d = dev_data();
+        h.units = d_units.as<Unit>();
+        h.num_units = static_cast<uint32_t>(units.size());
+        h.min_rows_per_cta = 2048;
+        h.job = hist_job.as<HistJob>();
+        for (int k = 0; k < 2; ++k) {
+            h.rows[k] = rows[k].as<uint32_t>();
+            h.ordered[k] = ordered[k].as<int32_t>();
+        }
+        h.packed = packed.as<int32_t>();
+        h.active = active;
+        h.out = out;
+        return h;
+    }
+
+    int row_grid() const { return sms * 8; }
+    int partition_grid() const { return sms * 4; }
+    int search_grid() const {
+        int g = static_cast<int>((num_features + 7) / 8);
+        return std::max(1, std::min(g, sms * 4));
+    }
+
+    int check_loaded() {
+        if (!loaded) return fail(SB2_EDEVICE, "b200 backend used before load");
+        return SB2_OK;
+    }
+    int check_range(sb2_leaf_range leaf) {
+        if (static_cast<uint64_t>(leaf.begin) + leaf.count > num_rows)
+            return fail(SB2_EDEVICE, "leaf rows " + std::to_string(leaf.begin) + ".." +
+                                         std::to_string(static_cast<uint64_t>(leaf.begin) + leaf.count) +
+                                         " outside the partition of " + std::to_string(num_rows) + " rows");
+        return SB2_OK;
+    }
+    int sync() { return cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize"); }
+};
+
+namespace {
+
+#define SB2_TRY(expr)                        \
+    do {                                     \
+        int sb2_status_ = (expr);            \
+        if (sb2_status_ != SB2_OK) return sb2_status_; \
+    } while (0)
+
+#define SB2_CUDA(b, expr) SB2_TRY((b)->cuda((expr), #expr))
+
+int nccl_status(sb2_backend* b, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return SB2_OK;
+    return b->fail(SB2_ECOLLECTIVE, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+void copy_string(const std::string& s, char* buf, size_t len) {
+    if (!buf || len == 0) return;
+    size_t n = std::min(len - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+}
+
+// feature_mask (split.rs:966-985): the features one tree may split on.
+void feature_mask(const std::vector<sb2_feature>& features, double fraction, uint32_t seed, uint32_t iteration,
+                  uint8_t* mask) {
+    std::vector<uint32_t> usable;
+    for (uint32_t f = 0; f < features.size(); ++f) {
+        mask[f] = 0;
+        if (features[f].num_bins != 0) usable.push_back(f);
+    }
+    if (fraction >= 1.0) {
+        for (uint32_t f : usable) mask[f] = 1;
+        return;
+    }
+    double scaled = static_cast<double>(usable.size()) * fraction + 0.5;  // Common::RoundInt
+    size_t count = std::max<size_t>(static_cast<size_t>(scaled), std::min<size_t>(usable.size(), 1));
+    std::vector<std::pair<float, uint32_t>> keyed;
+    for (uint32_t f : usable) keyed.emplace_back(uniform01(seed, 3u, iteration, f), f);
+    std::sort(keyed.begin(), keyed.end(), [](const auto& x, const auto& y) {
+        return x.first != y.first ? x.first < y.first : x.second < y.second;
+    });
+    for (size_t i = 0; i < std::min(count, keyed.size()); ++i) mask[keyed[i].second] = 1;
+}
+
+// Device form of a BinSplit: the tile and lane of its feature.
+int split_feature_of(sb2_backend* b, const sb2_bin_split& s, int32_t& feature) {
+    if (s.group >= b->group_column_feature.size() || s.column >= b->group_column_feature[s.group].size() ||
+        b->group_column_feature[s.group][s.column] < 0)
+        return b->fail(SB2_EDEVICE, "split on missing group " + std::to_string(s.group) + " column " +
+                                        std::to_string(s.column));
+    feature = b->group_column_feature[s.group][s.column];
+    return SB2_OK;
+}
+
+// Stable partition of [begin, begin + count) of buffer 0 by `st` (a split or a bag), written back into buffer 0.
+int run_partition(sb2_backend* b, Step st, uint32_t* out_left) {
+    TrainArgs a = b->api_train_args();
+    SB2_CUDA(b, cudaMemcpyAsync(b->step.ptr, &st, sizeof(Step), cudaMemcpyHostToDevice, b->stream));
+    launch_partition_flags(a, b->partition_grid(), b->stream);
+    launch_partition_scatter(a, b->partition_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    const size_t off = st.begin;
+    SB2_CUDA(b, cudaMemcpyAsync(b->rows[0].as<uint32_t>() + off, b->rows[1].as<uint32_t>() + off,
+                                sizeof(uint32_t) * st.count, cudaMemcpyDeviceToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->ordered[0].as<int32_t>() + off, b->ordered[1].as<int32_t>() + off,
+                                sizeof(int32_t) * st.count, cudaMemcpyDeviceToDevice, b->stream));
+    Step back{};
+    SB2_CUDA(b, cudaMemcpyAsync(&back, b->step.ptr, sizeof(Step), cudaMemcpyDeviceToHost, b->stream));
+    SB2_TRY(b->sync());
+    *out_left = back.local_left;
+    return SB2_OK;
+}
+
+// Histogram of buffer-0 positions [begin, begin + count) into `out` (2 * total_bins doubles).
+int run_histogram(sb2_backend* b, sb2_leaf_range leaf, double* out, size_t len) {
+    if (len != 2ull * b->total_bins)
+        return b->fail(SB2_EDEVICE, "histogram buffer of " + std::to_string(len) + " values, expected " +
+                                        std::to_string(2ull * b->total_bins));
+    SB2_CUDA(b, cudaMemsetAsync(b->staging.ptr, 0, sizeof(int) * (2ull * b->total_bins + 2), b->stream));
+    HistJob job{};
+    job.active = 1;
+    job.identity = 0;
+    job.begin = leaf.begin;
+    job.count = leaf.count;
+    job.which = 0;
+    SB2_CUDA(b, cudaMemcpyAsync(b->hist_job.ptr, &job, sizeof(job), cudaMemcpyHostToDevice, b->stream));
+    const uint8_t* active = b->api_used_all ? nullptr : b->api_active.as<uint8_t>();
+    launch_histogram(b->hist_args(active, b->staging.as<int>()), b->hist_grid, b->hist_smem, b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    std::vector<int> host(2ull * b->total_bins);
+    SB2_CUDA(b, cudaMemcpyAsync(host.data(), b->staging.ptr, sizeof(int) * host.size(), cudaMemcpyDeviceToHost,
+                                b->stream));
+    SB2_TRY(b->sync());
+    for (size_t i = 0; i < host.size(); ++i) out[i] = static_cast<double>(host[i]);
+    return SB2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb2_global_error(char* buf, size_t len) {
+    copy_string(g_global_error, buf, len);
+    return SB2_OK;
+}
+
+void sb2_default_params(sb2_params* p) {
+    std::memset(p, 0, sizeof(*p));
+    p->objective = SB2_REGRESSION;
+    p->num_iterations = 100;
+    p->learning_rate = 0.1;
+    p->num_leaves = 31;
+    p->max_depth = -1;
+    p->min_data_in_leaf = 20;
+    p->min_sum_hessian_in_leaf = 1e-3;
+    p->lambda_l1 = 0.0;
+    p->lambda_l2 = 0.0;
+    p->min_gain_to_split = 0.0;
+    p->bagging_fraction = 1.0;
+    p->bagging_freq = 0;
+    p->bagging_seed = 3;
+    p->feature_fraction = 1.0;
+    p->feature_fraction_seed = 2;
+    p->data_random_seed = 1;
+    p->boost_from_average = 1;
+    p->use_quantized_grad = 1;
+    p->sigmoid = 1.0;
+    p->num_grad_quant_bins = 4;
+    p->quant_train_renew_leaf = 1;
+    p->stochastic_rounding = 1;
+}
+
+int sb2_create(int device, sb2_backend** out) {
+    if (!out) {
+        g_global_error = "sb2_create: null output";
+        return SB2_EDEVICE;
+    }
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        g_global_error = std::string("no CUDA device: ") + cudaGetErrorString(e);
+        return SB2_EDEVICE;
+    }
+    if (device < 0 || device >= count) {
+        g_global_error = "CUDA device " + std::to_string(device) + " of " + std::to_string(count);
+        return SB2_EDEVICE;
+    }
+    auto b = std::make_unique<sb2_backend>();
+    b->device = device;
+    if ((e = cudaSetDevice(device)) != cudaSuccess || (e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        g_global_error = std::string("CUDA setup: ") + cudaGetErrorString(e);
+        return SB2_EDEVICE;
+    }
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major < 10) {
+        g_global_error = std::string("device ") + prop.name + " is not sm_100 (Blackwell)";
+        return SB2_EUNSUPPORTED;
+    }
+    b->sms = prop.multiProcessorCount;
+    b->name = std::string(prop.name) + " (cuda sm_" + std::to_string(prop.major) + std::to_string(prop.minor) + ")";
+    *out = b.release();
+    return SB2_OK;
+}
+
+int sb2_destroy(sb2_backend* b) {
+    if (!b) return SB2_OK;
+    cudaSetDevice(b->device);
+    delete b;
+    return SB2_OK;
+}
+
+int sb2_last_error(const sb2_backend* b, char* buf, size_t len) {
+    copy_string(b ? b->error : g_global_error, buf, len);
+    return SB2_OK;
+}
+
+int sb2_name(const sb2_backend* b, char* buf, size_t len) {
+    copy_string(b->name, buf, len);
+    return SB2_OK;
+}
+
+// Backend::load
+int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* objective) {
+    if (!b || !train || !objective) return SB2_EDEVICE;
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    if (train->num_rows > 0xFFFFFFFFull)
+        return b->fail(SB2_EUNSUPPORTED, std::to_string(train->num_rows) + " rows on one rank; the limit is 2^32 - 1");
+    if (objective->kind != SB2_REGRESSION && objective->kind != SB2_BINARY)
+        return b->fail(SB2_EUNSUPPORTED, "objective " + std::to_string(objective->kind) + " has no device gradients");
+    const uint32_t F = train->num_features;
+    b->features.assign(train->features, train->features + F);
+    b->upper_bounds.assign(F, {});
+    b->dev_features.assign(F, DevFeature{});
+    b->group_column_feature.assign(train->num_groups, {});
+    for (uint32_t g = 0; g < train->num_groups; ++g) {
+        const sb2_group& grp = train->groups[g];
+        b->group_column_feature[g].assign(grp.row_stride, -1);
+        for (uint32_t k = 0; k < grp.num_features; ++k) {
+            uint32_t f = grp.features[k];
+            if (f >= F) return b->fail(SB2_EDATA, "group lists a missing feature");
+            const sb2_feature& m = train->features[f];
+            if (m.column >= grp.row_stride || m.group != g || m.hist_offset < grp.hist_offset ||
+                m.hist_offset - grp.hist_offset + m.num_bins > grp.total_bins)
+                return b->fail(SB2_EDATA, "feature " + std::to_string(f) + " lies outside its group's bins or row");
+            b->group_column_feature[g][m.column] = static_cast<int32_t>(f);
+        }
+    }
+    // Tiles: the non-trivial features in order, 32 per tile.
+    std::vector<uint32_t> used;
+    for (uint32_t f = 0; f < F; ++f) {
+        const sb2_feature& m = train->features[f];
+        if (m.kind == SB2_CATEGORICAL)
+            return b->fail(SB2_EUNSUPPORTED, "categorical feature " + std::to_string(f) +
+                                                 ": the device split search is numerical only");
+        if (m.num_bins > 256) return b->fail(SB2_EDATA, "feature with more than 256 bins");
+        if (m.kind == SB2_NUMERICAL && m.num_bins > 0) {
+            size_t nb = m.num_bins - (m.nan_bin ? 1 : 0);
+            if (!m.upper_bounds || m.num_upper_bounds < nb)
+                return b->fail(SB2_EDATA, "numerical feature " + std::to_string(f) + " without its upper bounds");
+            b->upper_bounds[f].assign(m.upper_bounds, m.upper_bounds + m.num_upper_bounds);
+        }
+        b->features[f].upper_bounds = nullptr;
+        DevFeature& d = b->dev_features[f];
+        d.tile = -1;
+        d.lane = -1;
+        d.hist_offset = m.hist_offset;
+        d.num_bins = m.num_bins;
+        d.nan_bin = m.nan_bin;
+        d.kind = m.kind;
+        if (m.num_bins > 0 && m.kind != SB2_TRIVIAL) {
+            if (m.group >= train->num_groups) return b->fail(SB2_EDATA, "feature in a missing group");
+            used.push_back(f);
+        }
+    }
+    const uint64_t n = train->num_rows;
+    b->tiles.clear();
+    std::vector<int32_t> lane_feature;
+    uint64_t base = 0;
+    for (size_t i = 0; i < used.size(); i += kTileLanes) {
+        Tile t{};
+        t.nfeat = static_cast<uint32_t>(std::min<size_t>(kTileLanes, used.size() - i));
+        t.stride = (t.nfeat + 3) / 4 * 4;
+        t.base = base;
+        t.smem_bins = 0;
+        for (uint32_t l = 0; l < kTileLanes; ++l) {
+            int32_t f = l < t.nfeat ? static_cast<int32_t>(used[i + l]) : -1;
+            lane_feature.push_back(f);
+            if (f >= 0) {
+                b->dev_features[f].tile = static_cast<int32_t>(b->tiles.size());
+                b->dev_features[f].lane = static_cast<int32_t>(l);
+                t.smem_bins = std::max(t.smem_bins, train->features[f].num_bins);
+            }
+        }
+        base += (n * t.stride + 127) / 128 * 128;
+        b->tiles.push_back(t);
+    }
+    // Histogram units: consecutive tiles up to kMaxUnitTiles and a shared-memory budget.
+    constexpr size_t kUnitBudget = 96 * 1024;
+    b->units.clear();
+    size_t max_unit_bytes = 0;
+    for (size_t i = 0; i < b->tiles.size();) {
+        Unit u{};
+        u.first_tile = static_cast<uint32_t>(i);
+        size_t bytes = 0;
+        while (i < b->tiles.size() && u.num_tiles < static_cast<uint32_t>(kMaxUnitTiles)) {
+            size_t tb = 8ull * b->tiles[i].smem_bins * b->tiles[i].stride;
+            if (u.num_tiles > 0 && bytes + tb > kUnitBudget) break;
+            bytes += tb;
+            u.slots += b->tiles[i].smem_bins * b->tiles[i].stride;
+            ++u.num_tiles;
+            ++i;
+        }
+        max_unit_bytes = std::max(max_unit_bytes, bytes);
+        b->units.push_back(u);
+    }
+    b->hist_smem = static_cast<int>(std::max<size_t>(max_unit_bytes, 16));
+    SB2_CUDA(b, histogram_configure(b->hist_smem));
+    int per_sm = 1;
+    SB2_CUDA(b, histogram_occupancy(b->hist_smem, &per_sm));
+    per_sm = std::max(per_sm, 1);
+    int nu = std::max<int>(1, static_cast<int>(b->units.size()));
+    b->hist_grid = std::max(nu, b->sms * per_sm / nu * nu);
+
+    b->num_rows = n;
+    b->row_offset = train->row_offset;
+    b->num_features = F;
+    b->total_bins = train->total_bins;
+    b->objective = *objective;
+    b->weighted = train->weight != nullptr;
+
+    // Device buffers.
+    SB2_CUDA(b, b->bins.alloc(std::max<uint64_t>(base, 128)));
+    SB2_CUDA(b, b->d_tiles.alloc(sizeof(Tile) * std::max<size_t>(b->tiles.size(), 1)));
+    SB2_CUDA(b, b->d_features.alloc(sizeof(DevFeature) * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->d_lane_feature.alloc(sizeof(int32_t) * std::max<size_t>(lane_feature.size(), 1)));
+    SB2_CUDA(b, b->d_units.alloc(sizeof(Unit) * std::max<size_t>(b->units.size(), 1)));
+    SB2_CUDA(b, cudaMemcpyAsync(b->d_tiles.ptr, b->tiles.data(), sizeof(Tile) * b->tiles.size(), cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->d_features.ptr, b->dev_features.data(), sizeof(DevFeature) * F, cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->d_lane_feature.ptr, lane_feature.data(), sizeof(int32_t) * lane_feature.size(), cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->d_units.ptr, b->units.data(), sizeof(Unit) * b->units.size(), cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->bins.ptr, 0, b->bins.bytes, b->stream));
+    SB2_CUDA(b, b->counter.alloc(sizeof(unsigned int)));
+    SB2_CUDA(b, cudaMemsetAsync(b->counter.ptr, 0, sizeof(unsigned int), b->stream));
+    // Bins: each group uploaded once, its columns scattered into the tiles; every bin checked against its feature.
+    DeviceBuffer group_buf;
+    for (uint32_t g = 0; g < train->num_groups; ++g) {
+        const sb2_group& grp = train->groups[g];
+        if (n == 0) break;
+        SB2_CUDA(b, group_buf.alloc(n * grp.row_stride));
+        SB2_CUDA(b, cudaMemcpyAsync(group_buf.ptr, grp.data, n * grp.row_stride, cudaMemcpyHostToDevice, b->stream));
+        for (uint32_t k = 0; k < grp.num_features; ++k) {
+            uint32_t f = grp.features[k];
+            const DevFeature& d = b->dev_features[f];
+            if (d.tile < 0) continue;
+            const Tile& t = b->tiles[d.tile];
+            launch_repack(group_buf.as<uint8_t>(), n, grp.row_stride, train->features[f].column,
+                          b->bins.as<uint8_t>() + t.base, t.stride, static_cast<uint32_t>(d.lane), d.num_bins,
+                          b->counter.as<unsigned int>(), b->stream);
+        }
+        SB2_CUDA(b, cudaGetLastError());
+        SB2_TRY(b->sync());  // the group buffer is reused
+    }
+    // Rows.
+    SB2_CUDA(b, b->label.alloc(sizeof(float) * n));
+    SB2_CUDA(b, b->weight.alloc(sizeof(float) * (b->weighted ? n : 1)));
+    SB2_CUDA(b, b->scores.alloc(sizeof(float) * n));
+    SB2_CUDA(b, b->grad.alloc(sizeof(float) * n));
+    SB2_CUDA(b, b->hess.alloc(sizeof(float) * n));
+    SB2_CUDA(b, b->packed.alloc(sizeof(int32_t) * n));
+    for (int k = 0; k < 2; ++k) {
+        SB2_CUDA(b, b->rows[k].alloc(sizeof(uint32_t) * n));
+        SB2_CUDA(b, b->ordered[k].alloc(sizeof(int32_t) * n));
+    }
+    SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * (n / 32 + kPartitionTile / 32 + 1)));
+    SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * (n / kPartitionTile + 2)));
+    SB2_CUDA(b, b->staging.alloc(sizeof(int) * (2ull * b->total_bins + 2)));
+    SB2_CUDA(b, b->hist_job.alloc(sizeof(HistJob)));
+    SB2_CUDA(b, b->step.alloc(sizeof(Step)));
+    SB2_CUDA(b, b->iter.alloc(sizeof(IterState)));
+    SB2_CUDA(b, b->api_active.alloc(std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->maxima.alloc(2 * sizeof(unsigned long long)));
+    unsigned int bad_bins = 0;
+    SB2_CUDA(b, cudaMemcpyAsync(&bad_bins, b->counter.ptr, sizeof(unsigned int), cudaMemcpyDeviceToHost, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->counter.ptr, 0, sizeof(unsigned int), b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->iter.ptr, 0, sizeof(IterState), b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->scores.ptr, 0, sizeof(float) * n, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->grad.ptr, 0, sizeof(float) * n, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->hess.ptr, 0, sizeof(float) * n, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->packed.ptr, 0, sizeof(int32_t) * n, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->label.ptr, train->label, sizeof(float) * n, cudaMemcpyHostToDevice, b->stream));
+    if (b->weighted)
+        SB2_CUDA(b, cudaMemcpyAsync(b->weight.ptr, train->weight, sizeof(float) * n, cudaMemcpyHostToDevice, b->stream));
+    b->api_used.assign(F, 1);
+    b->api_used_all = true;
+    SB2_TRY(b->sync());
+    // Every bin inside its feature's bins: the histogram's shared slots rely on it.
+    if (bad_bins) return b->fail(SB2_EDATA, "a bin lies outside its feature's bins");
+    b->loaded = true;
+    return SB2_OK;
+}
+
+int sb2_init_scores(sb2_backend* b, int dataset, double value) {
+    SB2_TRY(b->check_loaded());
+    if (dataset != 0) return b->fail(SB2_EDEVICE, "no dataset " + std::to_string(dataset));
+    launch_fill(b->scores.as<float>(), b->num_rows, static_cast<float>(value), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    return b->sync();
+}
+
+int sb2_compute_gradients(sb2_backend* b, sb2_gradient_stats* out) {
+    SB2_TRY(b->check_loaded());
+    SB2_CUDA(b, cudaMemsetAsync(b->maxima.ptr, 0, 2 * sizeof(unsigned long long), b->stream));
+    launch_api_gradients(b->row_args(), b->maxima.as<unsigned long long>(), b->row_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    unsigned long long bits[2];
+    SB2_CUDA(b, cudaMemcpyAsync(bits, b->maxima.ptr, sizeof(bits), cudaMemcpyDeviceToHost, b->stream));
+    SB2_TRY(b->sync());
+    std::memcpy(&out->max_abs_grad, &bits[0], 8);
+    std::memcpy(&out->max_hess, &bits[1], 8);
+    return SB2_OK;
+}
+
+int sb2_quantize(sb2_backend* b, const sb2_quant_spec* spec) {
+    SB2_TRY(b->check_loaded());
+    launch_api_quantize(b->row_args(), *spec, b->row_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    return b->sync();
+}
+
+int sb2_reset_partition(sb2_backend* b, const sb2_bag_spec* bag, uint32_t* out_rows) {
+    SB2_TRY(b->check_loaded());
+    launch_api_iota(b->rows[0].as<uint32_t>(), b->ordered[0].as<int32_t>(), b->packed.as<int32_t>(), b->num_rows,
+                    b->row_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    if (bag->kind == 0) {
+        *out_rows = static_cast<uint32_t>(b->num_rows);
+        return b->sync();
+    }
+    Step st{};
+    st.active = 1;
+    st.begin = 0;
+    st.count = static_cast<uint32_t>(b->num_rows);
+    st.which = 0;
+    st.bag = 1;
+    st.bag_seed = bag->seed;
+    st.bag_round = bag->round;
+    st.bag_fraction = bag->fraction;
+    st.row_offset = b->row_offset;
+    if (b->tiles.empty()) return b->fail(SB2_EUNSUPPORTED, "bagging a dataset without features");
+    return run_partition(b, st, out_rows);
+}
+
+int sb2_set_histogram_features(sb2_backend* b, const uint8_t* used, size_t num_features) {
+    SB2_TRY(b->check_loaded());
+    if (num_features != b->num_features) return b->fail(SB2_EDEVICE, "feature mask of the wrong length");
+    b->api_used.assign(used, used + num_features);
+    b->api_used_all = std::all_of(b->api_used.begin(), b->api_used.end(), [](uint8_t u) { return u != 0; });
+    SB2_CUDA(b, cudaMemcpyAsync(b->api_active.ptr, b->api_used.data(), num_features, cudaMemcpyHostToDevice, b->stream));
+    return b->sync();
+}
+
+int sb2_histogram(sb2_backend* b, sb2_leaf_range leaf, int quantized, double* out, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (!quantized) return b->fail(SB2_EUNSUPPORTED, "float histograms: the device path is quantized only");
+    SB2_TRY(b->check_range(leaf));
+    return run_histogram(b, leaf, out, len);
+}
+
+int sb2_partition(sb2_backend* b, sb2_leaf_range leaf, const sb2_bin_split* split, uint32_t* out_left) {
+    SB2_TRY(b->check_loaded());
+    SB2_TRY(b->check_range(leaf));
+    int32_t f;
+    SB2_TRY(split_feature_of(b, *split, f));
+    Step st{};
+    st.active = 1;
+    st.begin = leaf.begin;
+    st.count = leaf.count;
+    st.which = 0;
+    st.split_tile = static_cast<uint32_t>(std::max(b->dev_features[f].tile, 0));
+    st.split_lane = static_cast<uint32_t>(std::max(b->dev_features[f].lane, 0));
+    std::memcpy(st.left_bins, split->left_bins, sizeof(st.left_bins));
+    if (leaf.count == 0) {
+        *out_left = 0;
+        return SB2_OK;
+    }
+    if (b->dev_features[f].tile < 0) return b->fail(SB2_EDEVICE, "split on a trivial feature");
+    return run_partition(b, st, out_left);
+}
+
+int sb2_partition_and_histogram(sb2_backend* b, sb2_leaf_range leaf, const sb2_bin_split* split, int side,
+                                int quantized, double* out, size_t len, uint32_t* out_left) {
+    if (!quantized) return b->fail(SB2_EUNSUPPORTED, "float histograms: the device path is quantized only");
+    SB2_TRY(sb2_partition(b, leaf, split, out_left));
+    sb2_leaf_range child = side == SB2_LEFT ? sb2_leaf_range{leaf.begin, *out_left}
+                                            : sb2_leaf_range{leaf.begin + *out_left, leaf.count - *out_left};
+    return run_histogram(b, child, out, len);
+}
+
+int sb2_leaf_sums(sb2_backend* b, const sb2_leaf_range* leaves, size_t num_leaves, float grad_scale,
+                  float hess_scale, int64_t* out) {
+    SB2_TRY(b->check_loaded());
+    for (size_t i = 0; i < num_leaves; ++i) SB2_TRY(b->check_range(leaves[i]));
+    DeviceBuffer ranges, sums;
+    SB2_CUDA(b, ranges.alloc(sizeof(sb2_leaf_range) * std::max<size_t>(num_leaves, 1)));
+    SB2_CUDA(b, sums.alloc(sizeof(int64_t) * 2 * std::max<size_t>(num_leaves, 1)));
+    SB2_CUDA(b, cudaMemcpyAsync(ranges.ptr, leaves, sizeof(sb2_leaf_range) * num_leaves, cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(sums.ptr, 0, sums.bytes, b->stream));
+    launch_api_leaf_sums(b->row_args(), b->rows[0].as<uint32_t>(), ranges.as<sb2_leaf_range>(),
+                         static_cast<uint32_t>(num_leaves), grad_scale, hess_scale, sums.as<int64_t>(), b->sms * 2,
+                         b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    SB2_CUDA(b, cudaMemcpyAsync(out, sums.ptr, sizeof(int64_t) * 2 * num_leaves, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_add_tree(sb2_backend* b, const sb2_device_node* nodes, size_t num_nodes, const float* leaf_values,
+                 size_t num_leaves) {
+    SB2_TRY(b->check_loaded());
+    if (num_leaves == 0 || num_leaves != num_nodes + 1)
+        return b->fail(SB2_EDEVICE, "tree with " + std::to_string(num_nodes) + " nodes and " +
+                                        std::to_string(num_leaves) + " leaves");
+    std::vector<TileNode> tn(num_nodes);
+    for (size_t k = 0; k < num_nodes; ++k) {
+        int32_t f;
+        SB2_TRY(split_feature_of(b, nodes[k].split, f));
+        if (b->dev_features[f].tile < 0) return b->fail(SB2_EDEVICE, "malformed device tree");
+        for (int32_t c : {nodes[k].left, nodes[k].right}) {
+            bool ok = c >= 0 ? (static_cast<size_t>(c) > k && static_cast<size_t>(c) < num_nodes)
+                             : (static_cast<size_t>(~c) < num_leaves);
+            if (!ok) return b->fail(SB2_EDEVICE, "malformed device tree");
+        }
+        tn[k].tile = static_cast<uint32_t>(b->dev_features[f].tile);
+        tn[k].lane = static_cast<uint32_t>(b->dev_features[f].lane);
+        std::memcpy(tn[k].left_bins, nodes[k].split.left_bins, sizeof(tn[k].left_bins));
+        tn[k].left = nodes[k].left;
+        tn[k].right = nodes[k].right;
+    }
+    DeviceBuffer dn, dv;
+    SB2_CUDA(b, dn.alloc(sizeof(TileNode) * std::max<size_t>(num_nodes, 1)));
+    SB2_CUDA(b, dv.alloc(sizeof(float) * num_leaves));
+    SB2_CUDA(b, cudaMemcpyAsync(dn.ptr, tn.data(), sizeof(TileNode) * num_nodes, cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(dv.ptr, leaf_values, sizeof(float) * num_leaves, cudaMemcpyHostToDevice, b->stream));
+    launch_api_add_tree(b->dev_data(), b->row_args(), dn.as<TileNode>(), static_cast<uint32_t>(num_nodes),
+                        dv.as<float>(), b->row_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    return b->sync();
+}
+
+int sb2_scores(sb2_backend* b, int dataset, float* out, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (dataset != 0) return b->fail(SB2_EDEVICE, "no dataset " + std::to_string(dataset));
+    if (len != b->num_rows) return b->fail(SB2_EDEVICE, "scores buffer of the wrong length");
+    SB2_CUDA(b, cudaMemcpyAsync(out, b->scores.ptr, sizeof(float) * len, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_read_partition(sb2_backend* b, uint32_t* out, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (len > b->num_rows) return b->fail(SB2_EDEVICE, "partition read past its rows");
+    SB2_CUDA(b, cudaMemcpyAsync(out, b->rows[0].ptr, sizeof(uint32_t) * len, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_read_packed(sb2_backend* b, int32_t* out, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (len != b->num_rows) return b->fail(SB2_EDEVICE, "packed buffer of the wrong length");
+    SB2_CUDA(b, cudaMemcpyAsync(out, b->packed.ptr, sizeof(int32_t) * len, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_write_gradients(sb2_backend* b, const float* grad, const float* hess, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (len != b->num_rows) return b->fail(SB2_EDEVICE, "gradient buffers of the wrong length");
+    SB2_CUDA(b, cudaMemcpyAsync(b->grad.ptr, grad, sizeof(float) * len, cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->hess.ptr, hess, sizeof(float) * len, cudaMemcpyHostToDevice, b->stream));
+    return b->sync();
+}
+
+int sb2_read_gradients(sb2_backend* b, float* grad, float* hess, size_t len) {
+    SB2_TRY(b->check_loaded());
+    if (len != b->num_rows) return b->fail(SB2_EDEVICE, "gradient buffers of the wrong length");
+    SB2_CUDA(b, cudaMemcpyAsync(grad, b->grad.ptr, sizeof(float) * len, cudaMemcpyDeviceToHost, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(hess, b->hess.ptr, sizeof(float) * len, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const uint8_t* evaluate, double sum_grad,
+                        double sum_hess, int64_t count, double grad_scale, double hess_scale,
+                        const sb2_split_config* cfg, sb2_split_info* out, uint8_t* splittable) {
+    SB2_TRY(b->check_loaded());
+    if (len != 2ull * b->total_bins) return b->fail(SB2_EDEVICE, "histogram of the wrong length");
+    std::vector<int> ih(len);
+    for (size_t i = 0; i < len; ++i) {
+        if (hist[i] != std::floor(hist[i]) || std::fabs(hist[i]) > 2147483647.0)
+            return b->fail(SB2_EUNSUPPORTED, "the device split search takes integer (quantized) histograms");
+        ih[i] = static_cast<int>(hist[i]);
+    }
+    DeviceBuffer dh, de, dout, dspl;
+    SB2_CUDA(b, dh.alloc(sizeof(int) * len));
+    SB2_CUDA(b, de.alloc(std::max<size_t>(b->num_features, 1)));
+    SB2_CUDA(b, dout.alloc(sizeof(sb2_split_info)));
+    SB2_CUDA(b, dspl.alloc(std::max<size_t>(b->num_features, 1)));
+    SB2_CUDA(b, cudaMemcpyAsync(dh.ptr, ih.data(), sizeof(int) * len, cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(de.ptr, evaluate, b->num_features, cudaMemcpyHostToDevice, b->stream));
+    launch_api_find_split(b->dev_data(), dh.as<int>(), de.as<uint8_t>(), sum_grad, sum_hess, count, grad_scale,
+                          hess_scale, *cfg, b->candidates.ptr, b->counter.as<unsigned int>(), dout.as<sb2_split_info>(),
+                          dspl.as<uint8_t>(), b->search_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    SB2_CUDA(b, cudaMemcpyAsync(out, dout.ptr, sizeof(sb2_split_info), cudaMemcpyDeviceToHost, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(splittable, dspl.ptr, b->num_features, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+int sb2_nccl_unique_id(uint8_t* out, size_t len) {
+    if (len < sizeof(ncclUniqueId)) {
+        g_global_error = "NCCL unique id buffer smaller than 128 bytes";
+        return SB2_ECOLLECTIVE;
+    }
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        g_global_error = std::string("ncclGetUniqueId: ") + ncclGetErrorString(r);
+        return SB2_ECOLLECTIVE;
+    }
+    std::memcpy(out, &id, sizeof(id));
+    return SB2_OK;
+}
+
+int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int world, int rank) {
+    if (len < sizeof(ncclUniqueId)) return b->fail(SB2_ECOLLECTIVE, "NCCL unique id shorter than 128 bytes");
+    if (world < 1 || rank < 0 || rank >= world) return b->fail(SB2_ECOLLECTIVE, "bad rank or world size");
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    if (b->comm) {
+        ncclCommDestroy(b->comm);
+        b->comm = nullptr;
+    }
+    b->world = world;
+    b->rank = rank;
+    if (world == 1) return SB2_OK;
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    return nccl_status(b, ncclCommInitRank(&b->comm, world, id, rank), "ncclCommInitRank");
+}
+
+}  // extern "C"
+
+// ---- device-resident training ------------------------------------------------------------------------------
+
+namespace {
+
+struct TrainBuffers {
+    DeviceBuffer leaves, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records, record_bufs;
+};
+
+// Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
+int carve_tree(sb2_backend* b, DeviceBuffer& buf, size_t count, size_t L, DevTree& t) {
+    size_t per = L * (4 + 4 + 4 + 1 + 4 + 4 + 8 + 8 + 8 + 8 + 8 + 8 + 4 + 4) + 64;
+    SB2_CUDA(b, buf.alloc(per * count + 256));
+    char* p = buf.as<char>();
+    auto take = [&](size_t bytes) {
+        char* q = p;
+        p += (bytes + 255) / 256 * 256;
+        return q;
+    };
+    const size_t n = count * L;
+    t.num_leaves = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * count));
+    t.split_feature = reinterpret_cast<int32_t*>(take(4 * n));
+    t.split_gain = reinterpret_cast<float*>(take(4 * n));
+    t.threshold_bin = reinterpret_cast<uint32_t*>(take(4 * n));
+    t.decision_type = reinterpret_cast<int8_t*>(take(n));
+    t.left_child = reinterpret_cast<int32_t*>(take(4 * n));
+    t.right_child = reinterpret_cast<int32_t*>(take(4 * n));
+    t.internal_value = reinterpret_cast<double*>(take(8 * n));
+    t.internal_weight = reinterpret_cast<double*>(take(8 * n));
+    t.internal_count = reinterpret_cast<int64_t*>(take(8 * n));
+    t.leaf_value = reinterpret_cast<double*>(take(8 * n));
+    t.leaf_weight = reinterpret_cast<double*>(take(8 * n));
+    t.leaf_count = reinterpret_cast<int64_t*>(take(8 * n));
+    t.leaf_parent = reinterpret_cast<int32_t*>(take(4 * n));
+    t.leaf_depth = reinterpret_cast<int32_t*>(take(4 * n));
+    if (static_cast<size_t>(p - buf.as<char>()) > buf.bytes) return b->fail(SB2_EINTERNAL, "tree buffer overrun");
+    return SB2_OK;
+}
+
+template <class T>
+int download(sb2_backend* b, std::vector<T>& v, const T* src, size_t n) {
+    v.resize(n);
+    if (n == 0) return SB2_OK;
+    return b->cuda(cudaMemcpyAsync(v.data(), src, sizeof(T) * n, cudaMemcpyDeviceToHost, b->stream), "download");
+}
+
+// One boosting iteration's launches (the body the CUDA graph captures).
+int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves) {
+    cudaStream_t s = b->stream;
+    const TrainArgs& t = ia.t;
+    const int row_grid = b->row_grid();
+    launch_gradients(ia, row_grid, s);
+    if (b->comm) {
+        SB2_TRY(nccl_status(b, ncclAllReduce(&t.iter->max_abs_grad_bits, &t.iter->max_abs_grad_bits, 2, ncclUint64,
+                                             ncclMax, b->comm, s),
+                            "ncclAllReduce(max)"));
+    }
+    launch_iteration_start(ia, row_grid, s);
+    HistArgs h = b->hist_args(t.evaluate, t.staging);
+    h.job = t.hist_job;
+    const size_t staging_len = 2ull * b->total_bins + 2;
+    launch_histogram(h, b->hist_grid, b->hist_smem, s);
+    if (b->comm)
+        SB2_TRY(nccl_status(b, ncclAllReduce(t.staging, t.staging, staging_len, ncclInt32, ncclSum, b->comm, s),
+                            "ncclAllReduce(histogram)"));
+    launch_search(t, b->search_grid(), s);
+    for (int step = 0; step + 1 < max_leaves; ++step) {
+        launch_partition_flags(t, b->partition_grid(), s);
+        launch_partition_scatter(t, b->partition_grid(), s);
+        launch_histogram(h, b->hist_grid, b->hist_smem, s);
+        if (b->comm)
+            SB2_TRY(nccl_status(b, ncclAllReduce(t.staging, t.staging, staging_len, ncclInt32, ncclSum, b->comm, s),
+                                "ncclAllReduce(histogram)"));
+        launch_search(t, b->search_grid(), s);
+    }
+    launch_leaf_sums(ia, row_grid, s);
+    if (b->comm)
+        SB2_TRY(nccl_status(b, ncclAllReduce(ia.leaf_sums, ia.leaf_sums, 2ull * max_leaves, ncclInt64, ncclSum,
+                                             b->comm, s),
+                            "ncclAllReduce(leaf sums)"));
+    launch_finalize(ia, s);
+    launch_add_tree_partition(ia, row_grid, s);
+    return b->cuda(cudaGetLastError(), "launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model** out) {
+    if (!b || !p || !out) return SB2_EDEVICE;
+    SB2_TRY(b->check_loaded());
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    if (p->objective != b->objective.kind) return b->fail(SB2_ECONFIG, "params objective differs from the loaded one");
+    if (!p->use_quantized_grad) return b->fail(SB2_EUNSUPPORTED, "the device trainer is quantized only");
+    if (p->bagging_fraction < 1.0 && p->bagging_freq > 0)
+        return b->fail(SB2_EUNSUPPORTED, "bagging in the device trainer");
+    if (p->num_leaves < 2 || p->num_leaves > 1024)
+        return b->fail(SB2_ECONFIG, "num_leaves must be in 2..=1024 on the device");
+    if (p->num_grad_quant_bins < 2 || p->num_grad_quant_bins > 64)
+        return b->fail(SB2_ECONFIG, "num_grad_quant_bins must be in 2..=64");
+    if (p->num_iterations < 0) return b->fail(SB2_ECONFIG, "negative num_iterations");
+    const uint64_t total_rows = b->num_rows;  // single rank; ranks add theirs below
+    int64_t global_rows = static_cast<int64_t>(total_rows);
+    const int L = p->num_leaves;
+    const int iters = p->num_iterations;
+    const uint32_t F = b->num_features;
+    if (static_cast<double>(b->num_rows) * b->world * std::max(p->num_grad_quant_bins, 1) >= 2147483647.0)
+        return b->fail(SB2_EUNSUPPORTED, "int32 histograms would overflow: rows * quant bins >= 2^31");
+    TrainBuffers tb;
+    SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
+    SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
+    SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
+    SB2_CUDA(b, tb.masks.alloc(static_cast<size_t>(std::max(iters, 1)) * std::max<uint32_t>(F, 1)));
+    SB2_CUDA(b, tb.slots.alloc(sizeof(int) * static_cast<size_t>(L) * 2 * b->total_bins));
+    SB2_CUDA(b, tb.leaf_sums.alloc(sizeof(int64_t) * 2 * L));
+    SB2_CUDA(b, tb.leaf_values.alloc(sizeof(float) * L));
+    SB2_CUDA(b, tb.records.alloc(sizeof(TreeRecordHeader) * std::max(iters, 1)));
+    DevTree work{}, rec{};
+    SB2_TRY(carve_tree(b, tb.tree_bufs, 1, L, work));
+    SB2_TRY(carve_tree(b, tb.record_bufs, std::max(iters, 1), L, rec));
+    std::vector<uint8_t> masks(static_cast<size_t>(std::max(iters, 1)) * F);
+    for (int i = 0; i < iters; ++i)
+        feature_mask(b->features, p->feature_fraction, p->feature_fraction_seed, static_cast<uint32_t>(i),
+                     masks.data() + static_cast<size_t>(i) * F);
+    SB2_CUDA(b, cudaMemcpyAsync(tb.masks.ptr, masks.data(), masks.size(), cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(tb.leaves.ptr, 0, tb.leaves.bytes, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(tb.splittable.ptr, 0, tb.splittable.bytes, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(tb.records.ptr, 0, tb.records.bytes, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->iter.ptr, 0, sizeof(IterState), b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->counter.ptr, 0, sizeof(unsigned int), b->stream));
+    if (b->comm) {
+        DeviceBuffer cnt;
+        SB2_CUDA(b, cnt.alloc(sizeof(int64_t)));
+        SB2_CUDA(b, cudaMemcpyAsync(cnt.ptr, &global_rows, sizeof(int64_t), cudaMemcpyHostToDevice, b->stream));
+        SB2_TRY(nccl_status(b, ncclAllReduce(cnt.ptr, cnt.ptr, 1, ncclInt64, ncclSum, b->comm, b->stream),
+                            "ncclAllReduce(rows)"));
+        SB2_CUDA(b, cudaMemcpyAsync(&global_rows, cnt.ptr, sizeof(int64_t), cudaMemcpyDeviceToHost, b->stream));
+        SB2_TRY(b->sync());
+    }
+    // Scores start at the initial score (Backend::init_scores).
+    SB2_TRY(sb2_init_scores(b, 0, init_score));
+
+    IterArgs ia{};
+    TrainArgs& t = ia.t;
+    t = b->api_train_args();
+    t.cfg.min_data_in_leaf = p->min_data_in_leaf;
+    t.cfg.min_sum_hessian_in_leaf = p->min_sum_hessian_in_leaf;
+    t.cfg.lambda_l1 = p->lambda_l1;
+    t.cfg.lambda_l2 = p->lambda_l2;
+    t.cfg.min_gain_to_split = p->min_gain_to_split;
+    t.max_leaves = L;
+    t.max_depth = p->max_depth;
+    t.sums_feature = -1;
+    for (uint32_t f = 0; f < F; ++f)
+        if (b->features[f].num_bins != 0) {
+            t.sums_feature = static_cast<int32_t>(f);
+            break;
+        }
+    t.num_iterations = iters;
+    t.leaves = tb.leaves.as<DevLeaf>();
+    t.splittable = tb.splittable.as<uint8_t>();
+    t.evaluate = tb.evaluate.as<uint8_t>();
+    t.masks = tb.masks.as<uint8_t>();
+    t.slots = tb.slots.as<int>();
+    t.tree = work;
+    ia.r = b->row_args();
+    ia.k.num_grad_quant_bins = p->num_grad_quant_bins;
+    ia.k.stochastic = p->stochastic_rounding;
+    ia.k.seed = p->data_random_seed;
+    ia.k.constant_hessian = (p->objective == SB2_REGRESSION && !b->weighted) ? 1 : 0;
+    ia.k.renew = p->quant_train_renew_leaf;
+    ia.k.learning_rate = p->learning_rate;
+    ia.k.init_score = init_score;
+    ia.k.total_rows = global_rows;
+    ia.leaf_sums = tb.leaf_sums.as<int64_t>();
+    ia.leaf_values_f32 = tb.leaf_values.as<float>();
+    ia.records = tb.records.as<TreeRecordHeader>();
+    ia.record_tree = rec;
+
+    // One iteration captured as a graph, replayed per iteration; CUDA events time each one.
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    SB2_CUDA(b, cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+    int st = enqueue_iteration(b, ia, L);
+    cudaError_t ce = cudaStreamEndCapture(b->stream, &graph);
+    if (st != SB2_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+    }
+    SB2_CUDA(b, ce);
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    SB2_CUDA(b, ce);
+    std::vector<cudaEvent_t> events(iters + 1);
+    for (auto& e : events) cudaEventCreate(&e);
+    cudaEventRecord(events[0], b->stream);
+    for (int i = 0; i < iters; ++i) {
+        ce = cudaGraphLaunch(exec, b->stream);
+        if (ce != cudaSuccess) break;
+        cudaEventRecord(events[i + 1], b->stream);
+    }
+    cudaError_t se = cudaStreamSynchronize(b->stream);
+    cudaGraphExecDestroy(exec);
+    auto model = std::make_unique<sb2_model>();
+    if (ce == cudaSuccess && se == cudaSuccess) {
+        for (int i = 0; i < iters; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, events[i], events[i + 1]);
+            model->seconds.push_back(ms / 1000.0);
+        }
+    }
+    for (auto& e : events) cudaEventDestroy(e);
+    SB2_CUDA(b, ce);
+    SB2_CUDA(b, se);
+    IterState it{};
+    SB2_CUDA(b, cudaMemcpy(&it, b->iter.ptr, sizeof(it), cudaMemcpyDeviceToHost));
+    if (it.error) return b->fail(SB2_EINTERNAL, "internal error " + std::to_string(it.error) + " at leaf " +
+                                                    std::to_string(it.error_info));
+    // Read the trees back.
+    std::vector<TreeRecordHeader> heads;
+    SB2_TRY(download(b, heads, tb.records.as<TreeRecordHeader>(), static_cast<size_t>(it.trees)));
+    const size_t n = static_cast<size_t>(it.trees) * L;
+    std::vector<int32_t> sf, lc, rc;
+    std::vector<float> sg;
+    std::vector<uint32_t> tbin;
+    std::vector<int8_t> dt;
+    std::vector<double> iv, iw, lv, lw;
+    std::vector<int64_t> ic, lcnt;
+    SB2_TRY(download(b, sf, rec.split_feature, n));
+    SB2_TRY(download(b, sg, rec.split_gain, n));
+    SB2_TRY(download(b, tbin, rec.threshold_bin, n));
+    SB2_TRY(download(b, dt, rec.decision_type, n));
+    SB2_TRY(download(b, lc, rec.left_child, n));
+    SB2_TRY(download(b, rc, rec.right_child, n));
+    SB2_TRY(download(b, iv, rec.internal_value, n));
+    SB2_TRY(download(b, iw, rec.internal_weight, n));
+    SB2_TRY(download(b, ic, rec.internal_count, n));
+    SB2_TRY(download(b, lv, rec.leaf_value, n));
+    SB2_TRY(download(b, lw, rec.leaf_weight, n));
+    SB2_TRY(download(b, lcnt, rec.leaf_count, n));
+    SB2_TRY(b->sync());
+    for (int k = 0; k < it.trees; ++k) {
+        HostTree ht;
+        const size_t o = static_cast<size_t>(k) * L;
+        const int nl = heads[k].num_leaves;
+        ht.num_leaves = nl;
+        ht.shrinkage = heads[k].shrinkage;
+        for (int j = 0; j + 1 < nl; ++j) {
+            const int32_t f = sf[o + j];
+            ht.split_feature.push_back(f);
+            ht.split_gain.push_back(sg[o + j]);
+            ht.threshold_bin.push_back(tbin[o + j]);
+            // apply_split (learner.rs:470-475): the bin's upper bound, f64::MAX for the +inf bound.
+            double bound = b->upper_bounds[f].at(tbin[o + j]);
+            ht.threshold.push_back(std::isfinite(bound) ? bound : std::numeric_limits<double>::max());
+            ht.decision_type.push_back(dt[o + j]);
+            ht.left_child.push_back(lc[o + j]);
+            ht.right_child.push_back(rc[o + j]);
+            ht.internal_value.push_back(iv[o + j]);
+            ht.internal_weight.push_back(iw[o + j]);
+            ht.internal_count.push_back(ic[o + j]);
+        }
+        for (int j = 0; j < nl; ++j) {
+            ht.leaf_value.push_back(lv[o + j]);
+            ht.leaf_weight.push_back(lw[o + j]);
+            ht.leaf_count.push_back(lcnt[o + j]);
+        }
+        model->trees.push_back(std::move(ht));
+    }
+    *out = model.release();
+    return SB2_OK;
+}
+
+int sb2_boost_from_average(const sb2_params* p, const float* label, const float* weight, size_t n, double* out) {
+    const double k_epsilon = static_cast<double>(1e-15f);
+    *out = 0.0;
+    if (!p->boost_from_average || p->objective == SB2_LAMBDARANK) return SB2_OK;
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(label[i])) {
+            g_global_error = "label of row " + std::to_string(i) + " is not finite";
+            return SB2_EDATA;
+        }
+    // [sum label * weight, sum weight] in row order; a binary label counts as 1 when positive.
+    double l = 0.0, w = 0.0;
+    for (size_t i = 0; i < n; ++i) {
+        const float y = p->objective == SB2_BINARY ? (label[i] > 0.0f ? 1.0f : 0.0f) : label[i];
+        if (weight) {
+            l += static_cast<double>(y * weight[i]);
+            w += static_cast<double>(weight[i]);
+        } else {
+            l += static_cast<double>(y);
+        }
+    }
+    if (!weight) w = static_cast<double>(n);
+    double score;
+    if (p->objective == SB2_BINARY) {
+        double rate = std::min(std::max(l / w, k_epsilon), 1.0 - k_epsilon);
+        score = std::log(rate / (1.0 - rate)) / p->sigmoid;
+    } else {
+        score = l / w;
+    }
+    // GBDT::BoostFromAverage drops an initial score indistinguishable from zero.
+    *out = std::fabs(score) > k_epsilon ? score : 0.0;
+    return SB2_OK;
+}
+
+int sb2_model_free(sb2_model* m) {
+    delete m;
+    return SB2_OK;
+}
+
+int sb2_model_num_trees(const sb2_model* m) { return static_cast<int>(m->trees.size()); }
+
+int sb2_model_tree(const sb2_model* m, int index, sb2_tree_view* v) {
+    if (index < 0 || static_cast<size_t>(index) >= m->trees.size()) return SB2_EDEVICE;
+    const HostTree& t = m->trees[index];
+    v->num_leaves = t.num_leaves;
+    v->shrinkage = t.shrinkage;
+    v->split_feature = t.split_feature.data();
+    v->split_gain = t.split_gain.data();
+    v->threshold = t.threshold.data();
+    v->threshold_bin = t.threshold_bin.data();
+    v->decision_type = t.decision_type.data();
+    v->left_child = t.left_child.data();
+    v->right_child = t.right_child.data();
+    v->leaf_value = t.leaf_value.data();
+    v->leaf_weight = t.leaf_weight.data();
+    v->leaf_count = t.leaf_count.data();
+    v->internal_value = t.internal_value.data();
+    v->internal_weight = t.internal_weight.data();
+    v->internal_count = t.internal_count.data();
+    return SB2_OK;
+}
+
+int sb2_model_iteration_seconds(const sb2_model* m, double* out, size_t len) {
+    size_t k = std::min(len, m->seconds.size());
+    std::copy(m->seconds.begin(), m->seconds.begin() + k, out);
+    return static_cast<int>(m->seconds.size());
+}
+
+}  // extern "C"

@@ -1,0 +1,525 @@
+// iter.cu — per-iteration kernels of the boosting loop and the Backend-API kernels.
+//
+//  gradients        objective::gradients (objective/regression.rs:20-43, binary.rs:27-50) and the local maxima of
+//                   CpuBackend::compute_gradients (backend/cpu.rs:757-780); binary gradients in f64, stored f32.
+//  iteration_start  QuantSpec::new (quantize.rs:56-84) from the reduced maxima, CpuBackend::quantize
+//                   (backend/cpu.rs:782-800), reset_partition(All) and the root's step.
+//  leaf_sums        CpuBackend::leaf_sums (backend/cpu.rs:886-908) for every leaf of the grown tree.
+//  finalize         Learner::renew_leaves (learner.rs:376-404) and Trainer::add (boosting.rs:313-324): renewal,
+//                   shrinkage, the first tree's bias, and the tree's record; a tree that cannot split ends training
+//                   (Trainer::single_leaf, boosting.rs:303-310).
+//  add_tree         the score update: each leaf's f32 value added to its rows (the partition holds every training
+//                   row in exactly one leaf without bagging), the same f32 add CpuBackend::add_tree makes.
+#include <cuda_runtime.h>
+
+#include "iter.cuh"
+
+namespace sb2 {
+
+namespace {
+
+constexpr double kZeroThreshold = static_cast<double>(1e-35f);
+
+__device__ __forceinline__ double round_to_zero(double v) { return fabs(v) > kZeroThreshold ? v : 0.0; }
+
+// quantize.rs:92-98
+__device__ __forceinline__ double positive_or_one(double v) { return (v > 0.0 && isfinite(v)) ? v : 1.0; }
+
+// QuantSpec::new (quantize.rs:56-84)
+__device__ sb2_quant_spec make_spec(double max_abs_grad, double max_hess, const IterConsts& k, uint32_t iteration) {
+    sb2_quant_spec s{};
+    s.grad_max_q = k.num_grad_quant_bins / 2;
+    s.hess_max_q = k.num_grad_quant_bins;
+    s.grad_scale = positive_or_one(__ddiv_rn(max_abs_grad, static_cast<double>(s.grad_max_q)));
+    s.hess_scale = k.constant_hessian ? 1.0 : positive_or_one(__ddiv_rn(max_hess, static_cast<double>(s.hess_max_q)));
+    s.inv_grad_scale = __double2float_rn(__ddiv_rn(1.0, s.grad_scale));
+    s.inv_hess_scale = __double2float_rn(__ddiv_rn(1.0, s.hess_scale));
+    s.constant_hessian = k.constant_hessian;
+    s.stochastic = k.stochastic;
+    s.seed = k.seed;
+    s.iteration = iteration;
+    return s;
+}
+
+// fixed_point_scale (quantize.rs:153-159): 2^(30 - ceil(log2 max_abs)). For the f32-valued maxima it is called with,
+// ceil(log2 x) is exactly the frexp exponent (less one at a power of two).
+__device__ float fixed_point_scale(double max_abs) {
+    if (!isfinite(max_abs) || max_abs <= 0.0) return 1.0f;
+    int e;
+    const double m = frexp(max_abs, &e);
+    const int ceil_log2 = (m == 0.5) ? e - 1 : e;
+    int exponent = 30 - ceil_log2;
+    exponent = exponent < -126 ? -126 : (exponent > 127 ? 127 : exponent);
+    return ldexpf(1.0f, exponent);
+}
+
+__device__ __forceinline__ int64_t to_fixed(float v, float scale) {
+    const float q = rintf(__fmul_rn(v, scale));
+    if (q != q) return 0;
+    if (q >= 9.2233720368547758e18f) return INT64_MAX;
+    if (q <= -9.2233720368547758e18f) return INT64_MIN;
+    return static_cast<int64_t>(q);
+}
+
+// Gradients of one row.
+__device__ __forceinline__ void row_gradient(const RowArgs& r, uint64_t row, float& g, float& h) {
+    if (r.objective == SB2_REGRESSION) {
+        const float residual = __fsub_rn(r.scores[row], r.label[row]);
+        if (r.weight) {
+            g = __fmul_rn(residual, r.weight[row]);
+            h = r.weight[row];
+        } else {
+            g = residual;
+            h = 1.0f;
+        }
+    } else {
+        const double sign = r.label[row] > 0.0f ? 1.0 : -1.0;
+        const double sigmoid = r.sigmoid;
+        const double response =
+            __ddiv_rn(__dmul_rn(-sign, sigmoid),
+                      __dadd_rn(1.0, exp(__dmul_rn(__dmul_rn(sign, sigmoid), static_cast<double>(r.scores[row])))));
+        const double abs_response = fabs(response);
+        const double w = r.weight ? static_cast<double>(r.weight[row]) : 1.0;
+        g = __double2float_rn(__dmul_rn(response, w));
+        h = __double2float_rn(__dmul_rn(__dmul_rn(abs_response, __dsub_rn(sigmoid, abs_response)), w));
+    }
+}
+
+__device__ __forceinline__ void block_max_pair(double& a, double& b) {
+    __shared__ double sa[kRowThreads / 32], sb[kRowThreads / 32];
+    for (int o = 16; o > 0; o >>= 1) {
+        a = fmax(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = fmax(b, __shfl_xor_sync(0xffffffffu, b, o));
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sa[warp] = a;
+        sb[warp] = b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < kRowThreads / 32; ++k) {
+            a = fmax(a, sa[k]);
+            b = fmax(b, sb[k]);
+        }
+        a = fmax(a, sa[0]);
+        b = fmax(b, sb[0]);
+    }
+}
+
+__device__ void gradients_body(const RowArgs& r, unsigned long long* max_g, unsigned long long* max_h) {
+    double mg = 0.0, mh = 0.0;
+    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; row < r.num_rows;
+         row += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+        float g, h;
+        row_gradient(r, row, g, h);
+        r.grad[row] = g;
+        r.hess[row] = h;
+        mg = fmax(mg, static_cast<double>(fabsf(g)));
+        mh = fmax(mh, static_cast<double>(fabsf(h)));
+    }
+    block_max_pair(mg, mh);
+    if (threadIdx.x == 0) {
+        // Non-negative doubles order like their bit patterns.
+        atomicMax(max_g, static_cast<unsigned long long>(__double_as_longlong(mg)));
+        atomicMax(max_h, static_cast<unsigned long long>(__double_as_longlong(mh)));
+    }
+}
+
+__global__ void __launch_bounds__(kRowThreads) gradients_kernel(IterArgs a) {
+    if (a.t.iter->stopped) return;
+    gradients_body(a.r, &a.t.iter->max_abs_grad_bits, &a.t.iter->max_hess_bits);
+}
+
+__device__ __forceinline__ bool may_split_root(const TrainArgs& t, int64_t count) {
+    const int64_t min_pair = 2 * t.cfg.min_data_in_leaf;
+    return (t.max_depth <= 0 || 0 < t.max_depth) && count >= min_pair;
+}
+
+__global__ void __launch_bounds__(kRowThreads) iteration_start_kernel(IterArgs a) {
+    __shared__ sb2_quant_spec s_spec;
+    IterState* it = a.t.iter;
+    const bool stopped = it->stopped;
+    if (threadIdx.x == 0) {
+        const double mg = __longlong_as_double(static_cast<long long>(it->max_abs_grad_bits));
+        const double mh = __longlong_as_double(static_cast<long long>(it->max_hess_bits));
+        s_spec = make_spec(mg, mh, a.k, static_cast<uint32_t>(it->iteration));
+    }
+    __syncthreads();
+    const uint32_t staging_len = 2 * a.t.total_bins + 2;
+    for (uint32_t i = blockIdx.x * kRowThreads + threadIdx.x; i < staging_len; i += gridDim.x * kRowThreads)
+        a.t.staging[i] = 0;
+    if (stopped) {
+        // Training ended: every later kernel of the iteration finds nothing to do.
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            a.t.step->active = 0;
+            a.t.hist_job->active = 0;
+        }
+        return;
+    }
+    const sb2_quant_spec spec = s_spec;
+    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; row < a.r.num_rows;
+         row += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+        const int32_t p = quantize_row(spec, a.r.grad[row], a.r.hess[row], a.r.row_offset + row);
+        a.r.packed[row] = p;
+        a.t.rows[0][row] = static_cast<uint32_t>(row);
+        a.t.ordered[0][row] = p;
+    }
+    if (blockIdx.x != 0) return;
+    const uint32_t F = a.t.num_features;
+    const uint8_t* mask = a.t.masks + static_cast<size_t>(it->iteration) * F;
+    for (uint32_t f = threadIdx.x; f < F; f += kRowThreads)
+        a.t.evaluate[f] = static_cast<uint8_t>(mask[f] || static_cast<int32_t>(f) == a.t.sums_feature);
+    for (int32_t i = threadIdx.x; i < 2 * a.t.max_leaves; i += kRowThreads) a.leaf_sums[i] = 0;
+    if (threadIdx.x == 0) {
+        it->spec = spec;
+        it->root_count = a.k.total_rows;
+        DevLeaf root{};
+        root.begin = 0;
+        root.count = static_cast<uint32_t>(a.r.num_rows);
+        root.which = 0;
+        root.depth = 0;
+        root.count_global = a.k.total_rows;
+        a.t.leaves[0] = root;
+        const DevTree& t = a.t.tree;
+        *t.num_leaves = 1;
+        t.leaf_value[0] = 0.0;
+        t.leaf_weight[0] = 0.0;
+        t.leaf_count[0] = 0;
+        t.leaf_parent[0] = -1;
+        t.leaf_depth[0] = 0;
+        Step s{};
+        s.active = 1;
+        s.root = 1;
+        *a.t.step = s;
+        HistJob job{};
+        job.active = a.t.sums_feature >= 0 && may_split_root(a.t, a.k.total_rows);
+        job.identity = 1;
+        job.begin = 0;
+        job.count = static_cast<uint32_t>(a.r.num_rows);
+        job.which = 0;
+        *a.t.hist_job = job;
+    }
+}
+
+// The leaves of the current tree sorted by first position, for position -> leaf lookups.
+struct LeafIndex {
+    uint32_t begin[1024];
+    uint16_t leaf[1024];
+    int n;
+};
+
+__device__ void build_leaf_index(const TrainArgs& t, LeafIndex& li) {
+    const int32_t L = *t.tree.num_leaves;
+    if (threadIdx.x == 0) li.n = 0;
+    __syncthreads();
+    for (int32_t l = threadIdx.x; l < L; l += blockDim.x) {
+        const DevLeaf lf = t.leaves[l];
+        if (lf.count == 0) continue;
+        int rank = 0;
+        for (int32_t m = 0; m < L; ++m) {
+            const DevLeaf o = t.leaves[m];
+            if (o.count != 0 && o.begin < lf.begin) ++rank;
+        }
+        li.begin[rank] = lf.begin;
+        li.leaf[rank] = static_cast<uint16_t>(l);
+        atomicAdd(&li.n, 1);
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ int leaf_of(const LeafIndex& li, uint32_t p) {
+    int lo = 0, hi = li.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (li.begin[mid] <= p)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
+    __shared__ LeafIndex li;
+    __shared__ long long sums[2 * 1024];
+    if (a.t.iter->stopped) return;
+    build_leaf_index(a.t, li);
+    const int32_t L = *a.t.tree.num_leaves;
+    for (int i = threadIdx.x; i < 2 * L; i += kRowThreads) sums[i] = 0;
+    __syncthreads();
+    const double mg = __longlong_as_double(static_cast<long long>(a.t.iter->max_abs_grad_bits));
+    const double mh = __longlong_as_double(static_cast<long long>(a.t.iter->max_hess_bits));
+    const float gs = fixed_point_scale(mg), hs = fixed_point_scale(mh);
+    const uint64_t n = a.r.num_rows;
+    const uint64_t lo = n * blockIdx.x / gridDim.x, hi = n * (blockIdx.x + 1) / gridDim.x;
+    const int lane = threadIdx.x & 31;
+    for (uint64_t base = lo + (threadIdx.x & ~31u); base < hi; base += kRowThreads) {
+        const uint64_t p = base + lane;
+        int k = -1;
+        long long g = 0, h = 0;
+        if (p < hi) {
+            k = leaf_of(li, static_cast<uint32_t>(p));
+            const DevLeaf& lf = a.t.leaves[li.leaf[k]];
+            const uint32_t row = a.t.rows[lf.which & 1][p];
+            g = to_fixed(a.r.grad[row], gs);
+            h = to_fixed(a.r.hess[row], hs);
+        }
+        const int k0 = __shfl_sync(0xffffffffu, k, 0);
+        if (__all_sync(0xffffffffu, k == k0 || k < 0) && k0 >= 0) {
+            for (int o = 16; o > 0; o >>= 1) {
+                g += __shfl_xor_sync(0xffffffffu, g, o);
+                h += __shfl_xor_sync(0xffffffffu, h, o);
+            }
+            if (lane == 0) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k0]]), static_cast<unsigned long long>(g));
+                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k0] + 1]), static_cast<unsigned long long>(h));
+            }
+        } else if (k >= 0) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k]]), static_cast<unsigned long long>(g));
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k] + 1]), static_cast<unsigned long long>(h));
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 2 * L; i += kRowThreads)
+        if (sums[i] != 0)
+            atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[i]), static_cast<unsigned long long>(sums[i]));
+}
+
+// split::leaf_output (split.rs:190-192)
+__device__ __forceinline__ double leaf_output(double g, double h, double l1, double l2) {
+    const double sg = static_cast<double>((g > 0.0) - (g < 0.0));
+    const double t = __dmul_rn(sg, fmax(__dsub_rn(fabs(g), l1), 0.0));
+    return __ddiv_rn(-t, __dadd_rn(h, l2));
+}
+
+__global__ void __launch_bounds__(kRowThreads) finalize_kernel(IterArgs a) {
+    IterState* it = a.t.iter;
+    if (it->stopped) return;
+    const DevTree& t = a.t.tree;
+    const int32_t L = *t.num_leaves;
+    const int32_t iteration = it->iteration;
+    const int32_t rec = it->trees;
+    const size_t base = static_cast<size_t>(rec) * a.t.max_leaves;
+    const bool first = rec == 0;
+    __syncthreads();
+    if (L == 1) {
+        // Trainer::single_leaf: the first tree becomes the constant init score; training stops either way.
+        if (threadIdx.x == 0) {
+            if (first) {
+                a.records[0].num_leaves = 1;
+                a.records[0].iteration = iteration;
+                a.records[0].shrinkage = 1.0;
+                a.record_tree.leaf_value[0] = a.k.init_score;
+                a.record_tree.leaf_weight[0] = 0.0;
+                a.record_tree.leaf_count[0] = 0;
+                it->trees = 1;
+            }
+            it->stopped = 1;
+        }
+        return;
+    }
+    const double mg = __longlong_as_double(static_cast<long long>(it->max_abs_grad_bits));
+    const double mh = __longlong_as_double(static_cast<long long>(it->max_hess_bits));
+    const float gs = fixed_point_scale(mg), hs = fixed_point_scale(mh);
+    const double lr = a.k.learning_rate;
+    const double bias = a.k.init_score;
+    const bool add_bias = first && bias != 0.0;
+    for (int32_t l = threadIdx.x; l < L; l += kRowThreads) {
+        double value = t.leaf_value[l];
+        double weight = t.leaf_weight[l];
+        if (a.k.renew) {
+            const double sg = __ddiv_rn(static_cast<double>(a.leaf_sums[2 * l]), static_cast<double>(gs));
+            const double sh = __ddiv_rn(static_cast<double>(a.leaf_sums[2 * l + 1]), static_cast<double>(hs));
+            value = round_to_zero(leaf_output(sg, sh, a.t.cfg.lambda_l1, a.t.cfg.lambda_l2));
+            weight = sh;
+        }
+        value = round_to_zero(__dmul_rn(value, lr));  // Tree::shrink
+        float add = __double2float_rn(value);
+        if (add_bias) {
+            value = round_to_zero(__dadd_rn(value, bias));  // Tree::add_bias
+            add = __double2float_rn(__dsub_rn(value, bias));  // replay::leaf_values
+        }
+        a.leaf_values_f32[l] = add;
+        a.record_tree.leaf_value[base + l] = value;
+        a.record_tree.leaf_weight[base + l] = weight;
+        a.record_tree.leaf_count[base + l] = t.leaf_count[l];
+    }
+    for (int32_t k = threadIdx.x; k + 1 < L; k += kRowThreads) {
+        double iv = round_to_zero(__dmul_rn(t.internal_value[k], lr));
+        if (add_bias) iv = round_to_zero(__dadd_rn(iv, bias));
+        a.record_tree.internal_value[base + k] = iv;
+        a.record_tree.internal_weight[base + k] = t.internal_weight[k];
+        a.record_tree.internal_count[base + k] = t.internal_count[k];
+        a.record_tree.split_feature[base + k] = t.split_feature[k];
+        a.record_tree.split_gain[base + k] = t.split_gain[k];
+        a.record_tree.threshold_bin[base + k] = t.threshold_bin[k];
+        a.record_tree.decision_type[base + k] = t.decision_type[k];
+        a.record_tree.left_child[base + k] = t.left_child[k];
+        a.record_tree.right_child[base + k] = t.right_child[k];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        a.records[rec].num_leaves = L;
+        a.records[rec].iteration = iteration;
+        a.records[rec].shrinkage = add_bias ? 1.0 : lr;
+        it->trees = rec + 1;
+        // The next iteration: its draws are keyed by the new index, its maxima start from zero.
+        it->iteration = iteration + 1;
+        it->max_abs_grad_bits = 0ull;
+        it->max_hess_bits = 0ull;
+    }
+}
+
+__global__ void __launch_bounds__(kRowThreads) add_tree_partition_kernel(IterArgs a) {
+    __shared__ LeafIndex li;
+    IterState* it = a.t.iter;
+    // finalize has recorded the tree; a stopped run adds nothing. The iteration advances here, after every kernel
+    // of this iteration has read it.
+    const bool stopped = it->stopped;
+    if (!stopped) {
+        build_leaf_index(a.t, li);
+        const uint64_t n = a.r.num_rows;
+        for (uint64_t p = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; p < n;
+             p += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+            const int k = leaf_of(li, static_cast<uint32_t>(p));
+            const int l = li.leaf[k];
+            const uint32_t row = a.t.rows[a.t.leaves[l].which & 1][p];
+            a.r.scores[row] = __fadd_rn(a.r.scores[row], a.leaf_values_f32[l]);
+        }
+    }
+}
+
+// ---- Backend API kernels ------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kRowThreads) api_gradients_kernel(RowArgs r, unsigned long long* bits) {
+    gradients_body(r, bits, bits + 1);
+}
+
+__global__ void __launch_bounds__(kRowThreads) api_quantize_kernel(RowArgs r, sb2_quant_spec spec) {
+    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; row < r.num_rows;
+         row += static_cast<uint64_t>(gridDim.x) * kRowThreads)
+        r.packed[row] = quantize_row(spec, r.grad[row], r.hess[row], r.row_offset + row);
+}
+
+__global__ void __launch_bounds__(kRowThreads) api_iota_kernel(uint32_t* rows, int32_t* ordered, const int32_t* packed,
+                                                               uint64_t n) {
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+        rows[i] = static_cast<uint32_t>(i);
+        ordered[i] = packed[i];
+    }
+}
+
+__global__ void __launch_bounds__(kRowThreads) api_leaf_sums_kernel(RowArgs r, const uint32_t* partition,
+                                                                    const sb2_leaf_range* ranges, uint32_t num,
+                                                                    float gs, float hs, int64_t* out) {
+    __shared__ long long sg[kRowThreads / 32], sh[kRowThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (uint32_t l = 0; l < num; ++l) {
+        const sb2_leaf_range rg = ranges[l];
+        long long g = 0, h = 0;
+        for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < rg.count;
+             i += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+            const uint32_t row = partition[rg.begin + i];
+            g += to_fixed(r.grad[row], gs);
+            h += to_fixed(r.hess[row], hs);
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            g += __shfl_xor_sync(0xffffffffu, g, o);
+            h += __shfl_xor_sync(0xffffffffu, h, o);
+        }
+        if (lane == 0) {
+            sg[warp] = g;
+            sh[warp] = h;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            long long tg = 0, th = 0;
+            for (int k = 0; k < kRowThreads / 32; ++k) {
+                tg += sg[k];
+                th += sh[k];
+            }
+            if (tg != 0) atomicAdd(reinterpret_cast<unsigned long long*>(out + 2 * l), static_cast<unsigned long long>(tg));
+            if (th != 0) atomicAdd(reinterpret_cast<unsigned long long*>(out + 2 * l + 1), static_cast<unsigned long long>(th));
+        }
+        __syncthreads();
+    }
+}
+
+// add_tree_to (backend/cpu.rs:605-695): walk each row's bins down the tree.
+__global__ void __launch_bounds__(kRowThreads) api_add_tree_kernel(DevData d, RowArgs r, const TileNode* nodes,
+                                                                   uint32_t num_nodes, const float* leaf_values) {
+    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; row < r.num_rows;
+         row += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
+        int32_t node = num_nodes == 0 ? -1 : 0;
+        while (node >= 0) {
+            const TileNode& nd = nodes[node];
+            const Tile tile = d.tiles[nd.tile];
+            const uint32_t bin = d.bins[tile.base + row * tile.stride + nd.lane];
+            node = ((nd.left_bins[bin >> 5] >> (bin & 31)) & 1u) ? nd.left : nd.right;
+        }
+        r.scores[row] = __fadd_rn(r.scores[row], leaf_values[~node]);
+    }
+}
+
+// One feature's column of a group moved into its tile lane; a bin past the feature's bins sets `bad` (the
+// histogram's shared slots hold exactly each feature's bins).
+__global__ void repack_kernel(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
+                              uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad) {
+    bool out_of_range = false;
+    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; row < rows;
+         row += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint8_t bin = src[row * src_stride + src_column];
+        out_of_range |= bin >= num_bins;
+        dst[row * dst_stride + dst_lane] = bin;
+    }
+    if (__any_sync(0xffffffffu, out_of_range) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+__global__ void fill_kernel(float* out, uint64_t n, float value) {
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        out[i] = value;
+}
+
+}  // namespace
+
+void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) { gradients_kernel<<<grid, kRowThreads, 0, s>>>(a); }
+void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s) {
+    iteration_start_kernel<<<grid, kRowThreads, 0, s>>>(a);
+}
+void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s) { leaf_sums_kernel<<<grid, kRowThreads, 0, s>>>(a); }
+void launch_finalize(const IterArgs& a, cudaStream_t s) { finalize_kernel<<<1, kRowThreads, 0, s>>>(a); }
+void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s) {
+    add_tree_partition_kernel<<<grid, kRowThreads, 0, s>>>(a);
+}
+void launch_api_gradients(const RowArgs& r, unsigned long long* bits, int grid, cudaStream_t s) {
+    api_gradients_kernel<<<grid, kRowThreads, 0, s>>>(r, bits);
+}
+void launch_api_quantize(const RowArgs& r, const sb2_quant_spec& spec, int grid, cudaStream_t s) {
+    api_quantize_kernel<<<grid, kRowThreads, 0, s>>>(r, spec);
+}
+void launch_api_iota(uint32_t* rows, int32_t* ordered, const int32_t* packed, uint64_t n, int grid, cudaStream_t s) {
+    api_iota_kernel<<<grid, kRowThreads, 0, s>>>(rows, ordered, packed, n);
+}
+void launch_api_leaf_sums(const RowArgs& r, const uint32_t* partition, const sb2_leaf_range* ranges, uint32_t num,
+                          float gs, float hs, int64_t* out, int grid, cudaStream_t s) {
+    api_leaf_sums_kernel<<<grid, kRowThreads, 0, s>>>(r, partition, ranges, num, gs, hs, out);
+}
+void launch_api_add_tree(const DevData& d, const RowArgs& r, const TileNode* nodes, uint32_t num_nodes,
+                         const float* leaf_values, int grid, cudaStream_t s) {
+    api_add_tree_kernel<<<grid, kRowThreads, 0, s>>>(d, r, nodes, num_nodes, leaf_values);
+}
+void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
+                   uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad, cudaStream_t s) {
+    const int grid = static_cast<int>(rows / 256 + 1 < 65535 ? rows / 256 + 1 : 65535);
+    repack_kernel<<<grid, 256, 0, s>>>(src, rows, src_stride, src_column, dst, dst_stride, dst_lane, num_bins, bad);
+}
+
+void launch_fill(float* out, uint64_t n, float value, cudaStream_t s) {
+    const int grid = static_cast<int>(n / 256 + 1 < 65535 ? n / 256 + 1 : 65535);
+    fill_kernel<<<grid, 256, 0, s>>>(out, n, value);
+}
+
+}  // namespace sb2

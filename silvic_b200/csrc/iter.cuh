@@ -1,0 +1,83 @@
+// iter.cuh — per-iteration kernels of the boosting loop (boosting.rs:227-324) and the Backend-API kernels.
+#pragma once
+
+#include "train.cuh"
+
+namespace sb2 {
+
+// The objective and the rows the gradient and score kernels read.
+struct RowArgs {
+    uint64_t num_rows;
+    uint64_t row_offset;
+    int32_t objective;   // SB2_REGRESSION / SB2_BINARY
+    int32_t pad_;
+    double sigmoid;
+    const float* label;
+    const float* weight;  // nullptr when unweighted
+    float* scores;
+    float* grad;
+    float* hess;
+    int32_t* packed;
+};
+
+// Training constants of one run (Params subset) the iteration kernels need.
+struct IterConsts {
+    int32_t num_grad_quant_bins;
+    int32_t stochastic;
+    uint32_t seed;             // data_random_seed
+    int32_t constant_hessian;  // objective::constant_hessian (objective/mod.rs:84-89)
+    int32_t renew;             // quant_train_renew_leaf
+    int32_t pad_;
+    double learning_rate;
+    double init_score;
+    int64_t total_rows;        // rows over every rank (root count without bagging)
+};
+
+// A finished tree as the host reads it back (one per iteration).
+struct TreeRecordHeader {
+    int32_t num_leaves;
+    int32_t iteration;
+    double shrinkage;
+};
+
+struct IterArgs {
+    TrainArgs t;
+    RowArgs r;
+    IterConsts k;
+    int64_t* leaf_sums;          // [2 * max_leaves], reduced over ranks between leaf_sums and finalize
+    float* leaf_values_f32;      // [max_leaves]: what add_tree adds
+    TreeRecordHeader* records;   // [num_iterations]
+    DevTree record_tree;         // arrays [num_iterations * max_leaves]
+};
+
+// A device node of Backend::add_tree in tile coordinates.
+struct TileNode {
+    uint32_t tile, lane;
+    uint32_t left_bins[8];
+    int32_t left, right;
+};
+
+constexpr int kRowThreads = 256;
+
+void launch_gradients(const IterArgs& a, int grid, cudaStream_t s);
+void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s);
+void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s);
+void launch_finalize(const IterArgs& a, cudaStream_t s);
+void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s);
+
+// Backend API helpers
+void launch_api_gradients(const RowArgs& r, unsigned long long* maxima_bits, int grid, cudaStream_t s);
+void launch_api_quantize(const RowArgs& r, const sb2_quant_spec& spec, int grid, cudaStream_t s);
+void launch_api_iota(uint32_t* rows, int32_t* ordered, const int32_t* packed, uint64_t n, int grid, cudaStream_t s);
+void launch_api_leaf_sums(const RowArgs& r, const uint32_t* partition, const sb2_leaf_range* ranges, uint32_t num,
+                          float gs, float hs, int64_t* out, int grid, cudaStream_t s);
+void launch_api_add_tree(const DevData& d, const RowArgs& r, const TileNode* nodes, uint32_t num_nodes,
+                         const float* leaf_values, int grid, cudaStream_t s);
+void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
+                   uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad, cudaStream_t s);
+void launch_fill(float* out, uint64_t n, float value, cudaStream_t s);
+void launch_api_find_split(const DevData& d, const int* hist, const uint8_t* evaluate, double ug, double uh,
+                           int64_t count, double gs, double hs, const sb2_split_config& cfg, void* cands,
+                           unsigned int* counter, sb2_split_info* out, uint8_t* splittable, int grid, cudaStream_t s);
+
+}  // namespace sb2

@@ -1,0 +1,139 @@
+// train.cuh — device-resident state of the leaf-wise learner (silvic-core learner.rs) and the kernels that move it.
+//
+// A tree grows as a fixed sequence of launches per split step, so the whole tree (and the whole boosting
+// iteration) can be enqueued without the host waiting on the device, and captured in one CUDA graph:
+//   partition_flags -> partition_scatter -> histogram (smaller child) -> [NCCL allreduce] -> search
+// `search` subtracts the sibling, scans both children, applies the split to the tree arrays and chooses the next
+// leaf (Learner::grow's loop, learner.rs:158-163), writing the next step. A step with nothing to split is a no-op
+// for every kernel, so the host always enqueues num_leaves - 1 steps.
+#pragma once
+
+#include "common.cuh"
+#include "hist.cuh"
+
+namespace sb2 {
+
+// A leaf being grown (learner.rs:87-94).
+struct DevLeaf {
+    uint32_t begin;   // this rank's rows: partition positions begin .. begin + count
+    uint32_t count;
+    uint32_t which;   // partition buffer holding them
+    int32_t depth;
+    double units_grad;  // LeafSums in histogram units, count over every rank
+    double units_hess;
+    int64_t count_global;
+    int32_t has_hist;   // Leaf::hist is Some: its histogram slot is valid for the evaluated features
+    int32_t has_best;
+    sb2_split_info best;
+};
+
+// One split step: the leaf being split and everything the step's kernels need.
+struct Step {
+    int32_t active;      // 0: nothing to split (the tree is finished); every kernel of the step returns
+    int32_t root;        // the root step: histogram of the root, no partition
+    int32_t leaf;        // leaf being split; its left child keeps the index
+    int32_t new_leaf;    // the right child's index
+    int32_t may_search;  // the children's histograms are built (learner.rs:266-268)
+    int32_t built_left;  // the histogram is built for the left child (learner.rs:271-275)
+    uint32_t begin, count, which;  // the parent's rows
+    uint32_t split_tile, split_lane;
+    uint32_t left_bins[8];
+    int64_t parent_count;
+    sb2_split_info info;
+    uint32_t local_left;  // this rank's left count, written by partition_scatter
+    int32_t bag;          // the partition is a Bernoulli bag: rows with quantize::in_bag go "left"
+    uint32_t bag_seed;
+    uint32_t bag_round;
+    double bag_fraction;
+    uint64_t row_offset;
+};
+
+// Tree arrays of one tree in LightGBM layout (tree.rs:47-73), `max_leaves` entries each.
+struct DevTree {
+    int32_t* num_leaves;        // [1]
+    int32_t* split_feature;
+    float* split_gain;
+    uint32_t* threshold_bin;
+    int8_t* decision_type;
+    int32_t* left_child;
+    int32_t* right_child;
+    double* internal_value;
+    double* internal_weight;
+    int64_t* internal_count;
+    double* leaf_value;
+    double* leaf_weight;
+    int64_t* leaf_count;
+    int32_t* leaf_parent;
+    int32_t* leaf_depth;
+};
+
+// Iteration state (boosting.rs:227-285).
+struct IterState {
+    int32_t iteration;     // global iteration index: keys quantization draws and the feature mask
+    int32_t stopped;       // a tree could not split: training is over
+    int32_t trees;         // trees added so far
+    int32_t error;         // non-zero: an internal error (code in error_info)
+    int64_t error_info;
+    unsigned long long max_abs_grad_bits;  // GradientStats maxima as the bits of non-negative doubles
+    unsigned long long max_hess_bits;
+    sb2_quant_spec spec;
+    int64_t root_count;    // bagged rows over every rank
+};
+
+// Everything the training kernels read, by value.
+struct TrainArgs {
+    DevData d;
+    sb2_split_config cfg;
+    int32_t max_leaves;      // params.num_leaves
+    int32_t max_depth;
+    int32_t sums_feature;    // first non-trivial feature (learner.rs:115), -1 when none
+    int32_t num_iterations;
+    uint32_t total_bins;
+    uint32_t num_features;
+    // learner state
+    DevLeaf* leaves;            // [max_leaves]
+    uint8_t* splittable;        // [max_leaves * num_features]
+    Step* step;
+    uint8_t* evaluate;          // [num_features]: the current step's evaluated features
+    const uint8_t* masks;       // [num_iterations * num_features]: per-iteration feature_mask
+    int* staging;               // [2 * total_bins + 2]: the step's new histogram and, after it, the left count
+    int* slots;                 // [max_leaves * 2 * total_bins]: one histogram per leaf
+    HistJob* hist_job;
+    IterState* iter;
+    DevTree tree;               // the tree being grown
+    // partition
+    uint32_t* rows[2];
+    int32_t* ordered[2];
+    uint32_t* flags;            // one bit per partition position
+    uint32_t* tile_left;        // left count per partition tile
+    // per-(child, feature) scan results and the search kernel's completion counter
+    void* candidates;
+    unsigned int* done_counter;
+};
+
+// The scan result of one feature for one child (split.rs:311-317 Candidate + FeatureResult::splittable).
+struct FeatureCandidate {
+    int32_t found;
+    int32_t splittable;
+    int32_t feature;
+    int32_t default_left;
+    double gain;        // best.gain - min_gain_shift
+    double best_gain;   // best.gain
+    uint32_t threshold;
+    uint32_t pad_;
+    double left_grad, left_hess;  // real sums as LightGBM keeps them (split.rs:300-307)
+    int64_t left_count;
+    double left_units_grad, left_units_hess;
+};
+
+static_assert(sizeof(FeatureCandidate) % 8 == 0, "candidates are copied as 64-bit words");
+
+constexpr int kPartitionTile = 4096;  // positions per partition tile
+constexpr int kPartitionThreads = 256;
+constexpr int kSearchThreads = 256;   // 8 warps, one feature each
+
+void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
+void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);
+void launch_search(const TrainArgs& a, int grid, cudaStream_t s);
+
+}  // namespace sb2

@@ -1,0 +1,55 @@
+"""Seeded synthetic datasets for the tests, built from silvic's counter hash (quantize.rs:16-31) so every rank can
+regenerate its rows."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from silvic_b200.dataset import BinnedDataset, numerical_mapper
+
+
+def mix32(x: np.ndarray) -> np.ndarray:
+    """lowbias32 (crates/silvic-core/src/quantize.rs:16-23) over uint32 arrays."""
+    x = np.asarray(x, dtype=np.uint32).copy()
+    with np.errstate(over="ignore"):
+        x ^= x >> np.uint32(16)
+        x *= np.uint32(0x7FEB352D)
+        x ^= x >> np.uint32(15)
+        x *= np.uint32(0x846CA68B)
+        x ^= x >> np.uint32(16)
+    return x
+
+
+def unit(stream: int, rows: np.ndarray) -> np.ndarray:
+    """A 24-bit uniform in [0, 1) per row from (stream, row)."""
+    h = mix32(mix32(rows.astype(np.uint32)) ^ mix32(np.uint32(stream)))
+    return (h >> np.uint32(8)).astype(np.float64) / 16777216.0
+
+
+def random_binned(rows: int, bins_per_feature: list[int], nan_bins: list[bool] | None = None, seed: int = 1,
+                  skew: float = 0.0, label_kind: str = "regression") -> BinnedDataset:
+    """Rows with hash-drawn bins per feature (a `skew` share of rows in bin 0) and a label that depends on a few
+    bins, so trees have structure."""
+    r = np.arange(rows, dtype=np.uint64)
+    nf = len(bins_per_feature)
+    nan_bins = nan_bins or [False] * nf
+    bins = np.empty((rows, nf), dtype=np.uint8)
+    for f, nb in enumerate(bins_per_feature):
+        u = unit(seed * 1000 + f, r)
+        b = (u * nb).astype(np.int64)
+        if skew > 0:
+            zero = unit(seed * 1000 + 500 + f, r) < skew
+            b[zero] = 0
+        bins[:, f] = np.minimum(b, nb - 1).astype(np.uint8)
+    signal = np.zeros(rows)
+    for f in range(min(nf, 6)):
+        signal += (bins[:, f].astype(np.float64) / max(bins_per_feature[f] - 1, 1) - 0.5) * (1.0 + f)
+    if nf >= 2:
+        signal += 0.5 * (bins[:, 0] > bins_per_feature[0] // 2) * (bins[:, 1] > bins_per_feature[1] // 2)
+    noise = unit(seed * 1000 + 999, r) - 0.5
+    if label_kind == "binary":
+        label = ((signal + noise) > 0).astype(np.float32)
+    else:
+        label = (signal + 0.3 * noise).astype(np.float32)
+    mappers = [numerical_mapper(f"f{f}", nb, nb > 2 and nan_bins[f]) for f, nb in enumerate(bins_per_feature)]
+    return BinnedDataset.from_bins(bins, mappers, label)

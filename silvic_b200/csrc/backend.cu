@@ -816,8 +816,10 @@ struct TrainBuffers {
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
 int carve_tree(sb2_backend* b, DeviceBuffer& buf, size_t count, size_t L, DevTree& t) {
-    size_t per = L * (4 + 4 + 4 + 1 + 4 + 4 + 8 + 8 + 8 + 8 + 8 + 8 + 4 + 4) + 64;
-    SB2_CUDA(b, buf.alloc(per * count + 256));
+    const size_t sizes[] = {4, 4, 4, 1, 4, 4, 8, 8, 8, 8, 8, 8, 4, 4};  // bytes per entry of each array below
+    size_t total = (sizeof(int32_t) * count + 255) / 256 * 256;
+    for (size_t s : sizes) total += (s * count * L + 255) / 256 * 256;
+    SB2_CUDA(b, buf.alloc(total));
     char* p = buf.as<char>();
     auto take = [&](size_t bytes) {
         char* q = p;

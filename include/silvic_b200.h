@@ -279,6 +279,23 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
                         double sum_grad, double sum_hess, int64_t count, double grad_scale, double hess_scale,
                         const sb2_split_config* cfg, sb2_split_info* out, uint8_t* splittable);
 
+/* ---- measurement -------------------------------------------------------------------------------------------- */
+
+/* Times `repeats` histograms of rows 0 .. rows - 1 (all rows when `rows` is 0) with every feature, as the trainer
+ * builds the root of an unbagged tree, with CUDA events on the handle's stream; *seconds gets the mean duration of
+ * one histogram (its kernels, launch to completion). Uses the current packed gradients (after sb2_quantize or
+ * sb2_train). */
+int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* seconds);
+
+/* sb2_train without the CUDA graph, each operation bracketed by CUDA events: seconds_by_op receives the device
+ * time of the last iteration per operation, in the order gradients, quantize (and the iteration's start),
+ * histogram, partition, split search, leaf sums, finalize (renewal and the tree record), score update, NCCL
+ * collectives, and the whole tree when one persistent kernel grows it (single GPU; the histogram, partition and
+ * search entries are then 0) (num_ops <= 10). The per-operation breakdown of the reference's `Timed` test backend
+ * (crates/silvic-core/tests/train_cpu.rs:434-484). `out` (may be NULL) receives the model. */
+int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_score, double* seconds_by_op,
+                      size_t num_ops, sb2_model** out);
+
 /* ---- multi-GPU --------------------------------------------------------------------------------------------- */
 
 /* An NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */

@@ -219,6 +219,27 @@ class B200Backend:
             spl.ctypes.data_as(C.POINTER(C.c_uint8))))
         return info, spl
 
+    def time_histogram(self, repeats: int = 10, rows: int = 0) -> float:
+        """Mean seconds of one histogram of the first `rows` rows (all when 0), CUDA events on the handle's
+        stream."""
+        secs = C.c_double()
+        self._check(self._lib.sb2_time_histogram(self._h, rows, repeats, C.byref(secs)))
+        return secs.value
+
+    PROFILE_OPS = ("gradients", "quantize", "histogram", "partition", "search", "leaf_sums", "finalize",
+                   "add_tree", "collectives", "tree", "tree.partition_flags", "tree.scatter", "tree.histogram",
+                   "tree.slab_reduce", "tree.search", "tree.finish", "tree.barriers")
+
+    def profile_train(self, params: _abi.Params, init_score: float) -> tuple[dict, "Model"]:
+        """Device seconds per operation of the last iteration (graph-free, CUDA events), and the model."""
+        secs = (C.c_double * len(self.PROFILE_OPS))()
+        m = C.c_void_p()
+        self._check(self._lib.sb2_profile_train(self._h, C.byref(params), init_score, secs, len(secs), C.byref(m)))
+        try:
+            return dict(zip(self.PROFILE_OPS, list(secs))), Model.from_handle(self._lib, m, init_score)
+        finally:
+            self._lib.sb2_model_free(m)
+
     # ---- multi-GPU ----
     @staticmethod
     def nccl_unique_id() -> bytes:

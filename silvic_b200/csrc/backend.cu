@@ -84,10 +84,17 @@ struct sb2_backend {
     std::vector<std::vector<int32_t>> group_column_feature;  // [group][column] -> feature
     int hist_smem = 0;
     int hist_grid = 0;
+    int grow_smem = 0;      // dynamic shared memory of the persistent tree kernel
+    bool grow_ok = false;   // it fits one CTA per SM
+    DeviceBuffer grid_barrier;
+    DeviceBuffer phase_ns;  // per-phase nanoseconds of the persistent kernel (profiling runs)
     DeviceBuffer bins, d_tiles, d_features, d_lane_feature, d_units;
     DeviceBuffer label, weight, scores, grad, hess, packed;
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, counter, maxima, misc;
+    DeviceBuffer slabs;        // histogram scratch: one slab per histogram CTA
+    uint32_t slab_ints = 0;    // ints per slab
+    uint32_t hist_slots = 0;   // gradient slots over every unit
     std::vector<uint8_t> api_used;
     bool api_used_all = true;
 
@@ -164,7 +171,7 @@ struct sb2_backend {
         h.d = dev_data();
         h.units = d_units.as<Unit>();
         h.num_units = static_cast<uint32_t>(units.size());
-        h.min_rows_per_cta = 2048;
+        h.min_rows_per_cta = 512;  // small leaves spread over many SMs; each CTA's zeroing and slab stay cheap
         h.job = hist_job.as<HistJob>();
         for (int k = 0; k < 2; ++k) {
             h.rows[k] = rows[k].as<uint32_t>();
@@ -173,7 +180,15 @@ struct sb2_backend {
         h.packed = packed.as<int32_t>();
         h.active = active;
         h.out = out;
+        h.slabs = slabs.as<int>();
+        h.slab_ints = slab_ints;
         return h;
+    }
+
+    // The histogram operation: per-CTA histograms into the slabs, then their sum into `h.out`.
+    void run_hist(const HistArgs& h, cudaStream_t s) const {
+        launch_histogram(h, hist_grid, hist_smem, s);
+        launch_histogram_reduce(h, hist_slots, s);
     }
 
     int row_grid() const { return sms * 8; }
@@ -195,6 +210,8 @@ struct sb2_backend {
         return SB2_OK;
     }
     int sync() { return cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize"); }
+    // Single-GPU training grows each tree in one persistent launch; with NCCL ranks, per-step launches.
+    bool persistent() const { return grow_ok && comm == nullptr; }
 };
 
 namespace {
@@ -284,7 +301,7 @@ int run_histogram(sb2_backend* b, sb2_leaf_range leaf, double* out, size_t len) 
     job.which = 0;
     SB2_CUDA(b, cudaMemcpyAsync(b->hist_job.ptr, &job, sizeof(job), cudaMemcpyHostToDevice, b->stream));
     const uint8_t* active = b->api_used_all ? nullptr : b->api_active.as<uint8_t>();
-    launch_histogram(b->hist_args(active, b->staging.as<int>()), b->hist_grid, b->hist_smem, b->stream);
+    b->run_hist(b->hist_args(active, b->staging.as<int>()), b->stream);
     SB2_CUDA(b, cudaGetLastError());
     std::vector<int> host(2ull * b->total_bins);
     SB2_CUDA(b, cudaMemcpyAsync(host.data(), b->staging.ptr, sizeof(int) * host.size(), cudaMemcpyDeviceToHost,
@@ -440,7 +457,9 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     for (size_t i = 0; i < used.size(); i += kTileLanes) {
         Tile t{};
         t.nfeat = static_cast<uint32_t>(std::min<size_t>(kTileLanes, used.size() - i));
-        t.stride = (t.nfeat + 3) / 4 * 4;
+        // Row bytes: 4, 8, 16 or 32, so a row is one aligned vector load.
+        t.stride = 4;
+        while (t.stride < t.nfeat) t.stride *= 2;
         t.base = base;
         t.smem_bins = 0;
         for (uint32_t l = 0; l < kTileLanes; ++l) {
@@ -452,35 +471,64 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 t.smem_bins = std::max(t.smem_bins, train->features[f].num_bins);
             }
         }
+        // 64, 128 or 256 bin slots per lane: the histogram kernel's shared addressing is specialised on these.
+        t.smem_bins = t.smem_bins <= 64 ? 64 : t.smem_bins <= 128 ? 128 : 256;
         base += (n * t.stride + 127) / 128 * 128;
         b->tiles.push_back(t);
     }
-    // Histogram units: consecutive tiles up to kMaxUnitTiles and a shared-memory budget.
-    constexpr size_t kUnitBudget = 96 * 1024;
+    // Histogram units: consecutive tiles, up to kMaxUnitTiles within a shared-memory budget (two int32 arrays of
+    // smem_bins * stride slots per tile).
+#ifndef SB2_UNIT_BUDGET_KB
+#define SB2_UNIT_BUDGET_KB 220  // of the 227 KB a CTA may hold, leaving room for the kernels' static shared memory
+#endif
+    constexpr size_t kUnitBudget = SB2_UNIT_BUDGET_KB * 1024;
     b->units.clear();
     size_t max_unit_bytes = 0;
+    std::vector<uint32_t> unit_features;
     for (size_t i = 0; i < b->tiles.size();) {
         Unit u{};
         u.first_tile = static_cast<uint32_t>(i);
         size_t bytes = 0;
+        uint32_t feats = 0;
         while (i < b->tiles.size() && u.num_tiles < static_cast<uint32_t>(kMaxUnitTiles)) {
             size_t tb = 8ull * b->tiles[i].smem_bins * b->tiles[i].stride;
             if (u.num_tiles > 0 && bytes + tb > kUnitBudget) break;
             bytes += tb;
             u.slots += b->tiles[i].smem_bins * b->tiles[i].stride;
+            feats += b->tiles[i].nfeat;
             ++u.num_tiles;
             ++i;
         }
         max_unit_bytes = std::max(max_unit_bytes, bytes);
         b->units.push_back(u);
+        unit_features.push_back(feats);
     }
-    b->hist_smem = static_cast<int>(std::max<size_t>(max_unit_bytes, 16));
+    // The kernel aligns its histogram to kHistAlign bytes inside the dynamic shared memory.
+    b->hist_smem = static_cast<int>(std::max<size_t>(max_unit_bytes, 16) + kHistAlign);
     SB2_CUDA(b, histogram_configure(b->hist_smem));
     int per_sm = 1;
     SB2_CUDA(b, histogram_occupancy(b->hist_smem, &per_sm));
     per_sm = std::max(per_sm, 1);
-    int nu = std::max<int>(1, static_cast<int>(b->units.size()));
-    b->hist_grid = std::max(nu, b->sms * per_sm / nu * nu);
+    // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
+    // per-warp bins (two children of 256 [g, h] pairs per warp) and the partition's scan.
+    b->grow_smem = std::max<int>(b->hist_smem, (grow_threads() / 32) * 2 * kMaxBins * 8);
+    int grow_per_sm = 0;
+    SB2_CUDA(b, grow_configure(b->grow_smem, &grow_per_sm));
+    b->grow_ok = grow_per_sm >= 1;
+    if (b->grow_ok) per_sm = std::min(per_sm, grow_per_sm);  // one grid for both paths: the units' CTA ranges
+    // CTAs in proportion to each unit's features (its share of the atomics), at least one each.
+    const int nu = static_cast<int>(b->units.size());
+    const uint32_t total_ctas = static_cast<uint32_t>(std::max(nu, b->sms * per_sm));
+    uint32_t all_feats = 0;
+    for (uint32_t f : unit_features) all_feats += f;
+    uint32_t next = 0;
+    for (int u = 0; u < nu; ++u) {
+        uint32_t share = all_feats ? static_cast<uint32_t>(static_cast<uint64_t>(total_ctas) * unit_features[u] / all_feats) : 1;
+        b->units[u].cta_begin = next;
+        b->units[u].cta_count = std::max<uint32_t>(share, 1);
+        next += b->units[u].cta_count;
+    }
+    b->hist_grid = static_cast<int>(std::max<uint32_t>(next, 1));
 
     b->num_rows = n;
     b->row_offset = train->row_offset;
@@ -532,15 +580,24 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         SB2_CUDA(b, b->rows[k].alloc(sizeof(uint32_t) * n));
         SB2_CUDA(b, b->ordered[k].alloc(sizeof(int32_t) * n));
     }
-    SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * (n / 32 + kPartitionTile / 32 + 1)));
-    SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * (n / kPartitionTile + 2)));
+    SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * (n / 32 + 2)));
+    SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * kMaxPartitionCtas));
     SB2_CUDA(b, b->staging.alloc(sizeof(int) * (2ull * b->total_bins + 2)));
+    b->slab_ints = 0;
+    b->hist_slots = 0;
+    for (const Unit& u : b->units) {
+        b->slab_ints = std::max(b->slab_ints, 2 * u.slots);
+        b->hist_slots += u.slots;
+    }
+    SB2_CUDA(b, b->slabs.alloc(sizeof(int) * static_cast<size_t>(b->hist_grid) * std::max<uint32_t>(b->slab_ints, 4)));
     SB2_CUDA(b, b->hist_job.alloc(sizeof(HistJob)));
     SB2_CUDA(b, b->step.alloc(sizeof(Step)));
     SB2_CUDA(b, b->iter.alloc(sizeof(IterState)));
     SB2_CUDA(b, b->api_active.alloc(std::max<size_t>(F, 1)));
     SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * std::max<size_t>(F, 1)));
     SB2_CUDA(b, b->maxima.alloc(2 * sizeof(unsigned long long)));
+    SB2_CUDA(b, b->grid_barrier.alloc(2 * sizeof(unsigned int)));
+    SB2_CUDA(b, cudaMemsetAsync(b->grid_barrier.ptr, 0, 2 * sizeof(unsigned int), b->stream));
     unsigned int bad_bins = 0;
     SB2_CUDA(b, cudaMemcpyAsync(&bad_bins, b->counter.ptr, sizeof(unsigned int), cudaMemcpyDeviceToHost, b->stream));
     SB2_CUDA(b, cudaMemsetAsync(b->counter.ptr, 0, sizeof(unsigned int), b->stream));
@@ -773,6 +830,44 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
     return b->sync();
 }
 
+int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* seconds) {
+    SB2_TRY(b->check_loaded());
+    if (repeats < 1) return b->fail(SB2_EDEVICE, "repeats must be positive");
+    if (rows == 0 || rows > b->num_rows) rows = b->num_rows;
+    HistJob job{};
+    job.active = 1;
+    job.identity = 1;
+    job.begin = 0;
+    job.count = static_cast<uint32_t>(rows);
+    job.which = 0;
+    SB2_CUDA(b, cudaMemcpyAsync(b->hist_job.ptr, &job, sizeof(job), cudaMemcpyHostToDevice, b->stream));
+    const HistArgs h = b->hist_args(nullptr, b->staging.as<int>());
+    const size_t staging_bytes = sizeof(int) * (2ull * b->total_bins + 2);
+    std::vector<cudaEvent_t> ev(2 * repeats);
+    for (auto& e : ev) SB2_CUDA(b, cudaEventCreate(&e));
+    // One untimed launch, then each timed launch between its own pair of events.
+    SB2_CUDA(b, cudaMemsetAsync(b->staging.ptr, 0, staging_bytes, b->stream));
+    b->run_hist(h, b->stream);
+    for (int i = 0; i < repeats; ++i) {
+        cudaMemsetAsync(b->staging.ptr, 0, staging_bytes, b->stream);
+        cudaEventRecord(ev[2 * i], b->stream);
+        b->run_hist(h, b->stream);
+        cudaEventRecord(ev[2 * i + 1], b->stream);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    double total = 0.0;
+    for (int i = 0; i < repeats && e == cudaSuccess; ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]);
+        total += ms / 1000.0;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    SB2_CUDA(b, e);
+    *seconds = total / repeats;
+    return SB2_OK;
+}
+
 int sb2_nccl_unique_id(uint8_t* out, size_t len) {
     if (len < sizeof(ncclUniqueId)) {
         g_global_error = "NCCL unique id buffer smaller than 128 bytes";
@@ -853,51 +948,114 @@ int download(sb2_backend* b, std::vector<T>& v, const T* src, size_t n) {
     return b->cuda(cudaMemcpyAsync(v.data(), src, sizeof(T) * n, cudaMemcpyDeviceToHost, b->stream), "download");
 }
 
-// One boosting iteration's launches (the body the CUDA graph captures).
-int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves) {
+// The operations of an iteration, as sb2_profile_train reports them (the reference's per-op `Timed` backend,
+// crates/silvic-core/tests/train_cpu.rs:434-484, on the device).
+enum Op { kOpGradients, kOpQuantize, kOpHistogram, kOpPartition, kOpSearch, kOpLeafSums, kOpFinalize, kOpAddTree,
+          kOpCollective, kOpTree, kOpCount };
+
+// CUDA events around each operation of one iteration (graph-free profiling runs only).
+struct OpTimer {
+    struct Mark {
+        int op;
+        cudaEvent_t start, stop;
+    };
+    std::vector<Mark> marks;
+    void begin(int op, cudaStream_t s) {
+        Mark m{op, nullptr, nullptr};
+        cudaEventCreate(&m.start);
+        cudaEventCreate(&m.stop);
+        cudaEventRecord(m.start, s);
+        marks.push_back(m);
+    }
+    void end(cudaStream_t s) { cudaEventRecord(marks.back().stop, s); }
+    void release() {
+        for (auto& m : marks) {
+            cudaEventDestroy(m.start);
+            cudaEventDestroy(m.stop);
+        }
+        marks.clear();
+    }
+};
+
+// One boosting iteration's launches (the body the CUDA graph captures); `timer` brackets each operation.
+int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTimer* timer) {
     cudaStream_t s = b->stream;
     const TrainArgs& t = ia.t;
     const int row_grid = b->row_grid();
-    launch_gradients(ia, row_grid, s);
-    if (b->comm) {
-        SB2_TRY(nccl_status(b, ncclAllReduce(&t.iter->max_abs_grad_bits, &t.iter->max_abs_grad_bits, 2, ncclUint64,
-                                             ncclMax, b->comm, s),
-                            "ncclAllReduce(max)"));
-    }
-    launch_iteration_start(ia, row_grid, s);
+    auto op = [&](int kind, auto&& launch) -> int {
+        if (timer) timer->begin(kind, s);
+        int st = launch();
+        if (timer) timer->end(s);
+        return st;
+    };
+    const size_t staging_len = 2ull * b->total_bins + 2;
+    auto reduce_histogram = [&]() -> int {
+        if (!b->comm) return SB2_OK;
+        return op(kOpCollective, [&] {
+            return nccl_status(b, ncclAllReduce(t.staging, t.staging, staging_len, ncclInt32, ncclSum, b->comm, s),
+                               "ncclAllReduce(histogram)");
+        });
+    };
     HistArgs h = b->hist_args(t.evaluate, t.staging);
     h.job = t.hist_job;
-    const size_t staging_len = 2ull * b->total_bins + 2;
-    launch_histogram(h, b->hist_grid, b->hist_smem, s);
+    SB2_TRY(op(kOpGradients, [&] { launch_gradients(ia, row_grid, s); return SB2_OK; }));
     if (b->comm)
-        SB2_TRY(nccl_status(b, ncclAllReduce(t.staging, t.staging, staging_len, ncclInt32, ncclSum, b->comm, s),
-                            "ncclAllReduce(histogram)"));
-    launch_search(t, b->search_grid(), s);
-    for (int step = 0; step + 1 < max_leaves; ++step) {
-        launch_partition_flags(t, b->partition_grid(), s);
-        launch_partition_scatter(t, b->partition_grid(), s);
-        launch_histogram(h, b->hist_grid, b->hist_smem, s);
-        if (b->comm)
-            SB2_TRY(nccl_status(b, ncclAllReduce(t.staging, t.staging, staging_len, ncclInt32, ncclSum, b->comm, s),
-                                "ncclAllReduce(histogram)"));
-        launch_search(t, b->search_grid(), s);
+        SB2_TRY(op(kOpCollective, [&] {
+            return nccl_status(b, ncclAllReduce(&t.iter->max_abs_grad_bits, &t.iter->max_abs_grad_bits, 2,
+                                                ncclUint64, ncclMax, b->comm, s),
+                               "ncclAllReduce(max)");
+        }));
+    SB2_TRY(op(kOpQuantize, [&] { launch_iteration_start(ia, row_grid, s); return SB2_OK; }));
+    if (b->persistent()) {
+        // One launch grows the whole tree (grow.cu).
+        SB2_TRY(op(kOpTree, [&] {
+            return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_slots, b->hist_grid,
+                                            b->grow_smem, s,
+                                            timer ? b->phase_ns.as<unsigned long long>() : nullptr),
+                           "cudaLaunchCooperativeKernel(grow_tree)");
+        }));
+        max_leaves = 1;  // no separate split steps
+    } else {
+        SB2_TRY(op(kOpHistogram, [&] { b->run_hist(h, s); return SB2_OK; }));
+        SB2_TRY(reduce_histogram());
+        SB2_TRY(op(kOpSearch, [&] { launch_search(t, b->search_grid(), s); return SB2_OK; }));
     }
-    launch_leaf_sums(ia, row_grid, s);
+    for (int step = 0; step + 1 < max_leaves; ++step) {
+        SB2_TRY(op(kOpPartition, [&] {
+            launch_partition_flags(t, b->partition_grid(), s);
+            launch_partition_scatter(t, b->partition_grid(), s);
+            return SB2_OK;
+        }));
+        SB2_TRY(op(kOpHistogram, [&] { b->run_hist(h, s); return SB2_OK; }));
+        SB2_TRY(reduce_histogram());
+        SB2_TRY(op(kOpSearch, [&] { launch_search(t, b->search_grid(), s); return SB2_OK; }));
+    }
+    SB2_TRY(op(kOpLeafSums, [&] { launch_leaf_sums(ia, row_grid, s); return SB2_OK; }));
     if (b->comm)
-        SB2_TRY(nccl_status(b, ncclAllReduce(ia.leaf_sums, ia.leaf_sums, 2ull * max_leaves, ncclInt64, ncclSum,
-                                             b->comm, s),
-                            "ncclAllReduce(leaf sums)"));
-    launch_finalize(ia, s);
-    launch_add_tree_partition(ia, row_grid, s);
+        SB2_TRY(op(kOpCollective, [&] {
+            return nccl_status(b, ncclAllReduce(ia.leaf_sums, ia.leaf_sums, 2ull * t.max_leaves, ncclInt64, ncclSum,
+                                                b->comm, s),
+                               "ncclAllReduce(leaf sums)");
+        }));
+    SB2_TRY(op(kOpFinalize, [&] { launch_finalize(ia, s); return SB2_OK; }));
+    SB2_TRY(op(kOpAddTree, [&] { launch_add_tree_partition(ia, row_grid, s); return SB2_OK; }));
     return b->cuda(cudaGetLastError(), "launch");
 }
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model** out) {
-    if (!b || !p || !out) return SB2_EDEVICE;
+// A training run's device state and launch arguments.
+struct Training {
+    TrainBuffers tb;
+    IterArgs ia{};
+    DevTree rec{};
+    int L = 0;
+    int iters = 0;
+};
+
+int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Training& tr) {
     SB2_TRY(b->check_loaded());
     SB2_CUDA(b, cudaSetDevice(b->device));
     if (p->objective != b->objective.kind) return b->fail(SB2_ECONFIG, "params objective differs from the loaded one");
@@ -916,7 +1074,9 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
     const uint32_t F = b->num_features;
     if (static_cast<double>(b->num_rows) * b->world * std::max(p->num_grad_quant_bins, 1) >= 2147483647.0)
         return b->fail(SB2_EUNSUPPORTED, "int32 histograms would overflow: rows * quant bins >= 2^31");
-    TrainBuffers tb;
+    tr.L = L;
+    tr.iters = iters;
+    TrainBuffers& tb = tr.tb;
     SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
@@ -925,7 +1085,8 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
     SB2_CUDA(b, tb.leaf_sums.alloc(sizeof(int64_t) * 2 * L));
     SB2_CUDA(b, tb.leaf_values.alloc(sizeof(float) * L));
     SB2_CUDA(b, tb.records.alloc(sizeof(TreeRecordHeader) * std::max(iters, 1)));
-    DevTree work{}, rec{};
+    DevTree work{};
+    DevTree& rec = tr.rec;
     SB2_TRY(carve_tree(b, tb.tree_bufs, 1, L, work));
     SB2_TRY(carve_tree(b, tb.record_bufs, std::max(iters, 1), L, rec));
     std::vector<uint8_t> masks(static_cast<size_t>(std::max(iters, 1)) * F);
@@ -950,7 +1111,7 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
     // Scores start at the initial score (Backend::init_scores).
     SB2_TRY(sb2_init_scores(b, 0, init_score));
 
-    IterArgs ia{};
+    IterArgs& ia = tr.ia;
     TrainArgs& t = ia.t;
     t = b->api_train_args();
     t.cfg.min_data_in_leaf = p->min_data_in_leaf;
@@ -986,47 +1147,18 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
     ia.leaf_values_f32 = tb.leaf_values.as<float>();
     ia.records = tb.records.as<TreeRecordHeader>();
     ia.record_tree = rec;
+    return SB2_OK;
+}
 
-    // One iteration captured as a graph, replayed per iteration; CUDA events time each one.
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    SB2_CUDA(b, cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
-    int st = enqueue_iteration(b, ia, L);
-    cudaError_t ce = cudaStreamEndCapture(b->stream, &graph);
-    if (st != SB2_OK) {
-        if (graph) cudaGraphDestroy(graph);
-        return st;
-    }
-    SB2_CUDA(b, ce);
-    ce = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    SB2_CUDA(b, ce);
-    std::vector<cudaEvent_t> events(iters + 1);
-    for (auto& e : events) cudaEventCreate(&e);
-    cudaEventRecord(events[0], b->stream);
-    for (int i = 0; i < iters; ++i) {
-        ce = cudaGraphLaunch(exec, b->stream);
-        if (ce != cudaSuccess) break;
-        cudaEventRecord(events[i + 1], b->stream);
-    }
-    cudaError_t se = cudaStreamSynchronize(b->stream);
-    cudaGraphExecDestroy(exec);
-    auto model = std::make_unique<sb2_model>();
-    if (ce == cudaSuccess && se == cudaSuccess) {
-        for (int i = 0; i < iters; ++i) {
-            float ms = 0.0f;
-            cudaEventElapsedTime(&ms, events[i], events[i + 1]);
-            model->seconds.push_back(ms / 1000.0);
-        }
-    }
-    for (auto& e : events) cudaEventDestroy(e);
-    SB2_CUDA(b, ce);
-    SB2_CUDA(b, se);
+// The trees of a finished run, read back into a host model.
+int collect_model(sb2_backend* b, Training& tr, std::unique_ptr<sb2_model>& model) {
+    const int L = tr.L;
+    const DevTree& rec = tr.rec;
+    TrainBuffers& tb = tr.tb;
     IterState it{};
     SB2_CUDA(b, cudaMemcpy(&it, b->iter.ptr, sizeof(it), cudaMemcpyDeviceToHost));
     if (it.error) return b->fail(SB2_EINTERNAL, "internal error " + std::to_string(it.error) + " at leaf " +
                                                     std::to_string(it.error_info));
-    // Read the trees back.
     std::vector<TreeRecordHeader> heads;
     SB2_TRY(download(b, heads, tb.records.as<TreeRecordHeader>(), static_cast<size_t>(it.trees)));
     const size_t n = static_cast<size_t>(it.trees) * L;
@@ -1077,6 +1209,68 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
         }
         model->trees.push_back(std::move(ht));
     }
+    return SB2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model** out) {
+    if (!b || !p || !out) return SB2_EDEVICE;
+    Training tr;
+    SB2_TRY(setup_training(b, p, init_score, tr));
+    const int L = tr.L, iters = tr.iters;
+    // Single GPU: each iteration is a handful of launches, the tree one persistent kernel. With NCCL ranks: one
+    // iteration (about four launches per split) captured as a graph and replayed. CUDA events time each iteration.
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t ce = cudaSuccess;
+    if (!b->persistent()) {
+        cudaGraph_t graph = nullptr;
+        SB2_CUDA(b, cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+        int st = enqueue_iteration(b, tr.ia, L, nullptr);
+        ce = cudaStreamEndCapture(b->stream, &graph);
+        if (st != SB2_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return st;
+        }
+        SB2_CUDA(b, ce);
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        SB2_CUDA(b, ce);
+    }
+    std::vector<cudaEvent_t> events(iters + 1);
+    for (auto& e : events) cudaEventCreate(&e);
+    cudaEventRecord(events[0], b->stream);
+    int launch_status = SB2_OK;
+    for (int i = 0; i < iters; ++i) {
+        if (exec) {
+            ce = cudaGraphLaunch(exec, b->stream);
+            if (ce != cudaSuccess) break;
+        } else {
+            launch_status = enqueue_iteration(b, tr.ia, L, nullptr);
+            if (launch_status != SB2_OK) break;
+        }
+        cudaEventRecord(events[i + 1], b->stream);
+    }
+    cudaError_t se = cudaStreamSynchronize(b->stream);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (launch_status != SB2_OK) {
+        for (auto& e : events) cudaEventDestroy(e);
+        return launch_status;
+    }
+    auto model = std::make_unique<sb2_model>();
+    if (ce == cudaSuccess && se == cudaSuccess) {
+        for (int i = 0; i < iters; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, events[i], events[i + 1]);
+            model->seconds.push_back(ms / 1000.0);
+        }
+    }
+    for (auto& e : events) cudaEventDestroy(e);
+    SB2_CUDA(b, ce);
+    SB2_CUDA(b, se);
+    SB2_TRY(collect_model(b, tr, model));
     *out = model.release();
     return SB2_OK;
 }
@@ -1111,6 +1305,43 @@ int sb2_boost_from_average(const sb2_params* p, const float* label, const float*
     }
     // GBDT::BoostFromAverage drops an initial score indistinguishable from zero.
     *out = std::fabs(score) > k_epsilon ? score : 0.0;
+    return SB2_OK;
+}
+
+int sb2_profile_train(sb2_backend* b, const sb2_params* p, double init_score, double* seconds_by_op, size_t num_ops,
+                      sb2_model** out) {
+    if (!b || !p || !seconds_by_op) return SB2_EDEVICE;
+    Training tr;
+    SB2_TRY(setup_training(b, p, init_score, tr));
+    std::vector<double> last(kOpCount + kGrowPhases, 0.0);
+    auto model = std::make_unique<sb2_model>();
+    SB2_CUDA(b, b->phase_ns.alloc(sizeof(unsigned long long) * kGrowPhases));
+    for (int i = 0; i < tr.iters; ++i) {
+        OpTimer timer;
+        SB2_CUDA(b, cudaMemsetAsync(b->phase_ns.ptr, 0, b->phase_ns.bytes, b->stream));
+        int st = enqueue_iteration(b, tr.ia, tr.L, &timer);
+        cudaError_t se = cudaStreamSynchronize(b->stream);
+        if (st == SB2_OK && se == cudaSuccess) {
+            std::fill(last.begin(), last.end(), 0.0);
+            double total = 0.0;
+            for (auto& m : timer.marks) {
+                float ms = 0.0f;
+                cudaEventElapsedTime(&ms, m.start, m.stop);
+                last[m.op] += ms / 1000.0;
+                total += ms / 1000.0;
+            }
+            model->seconds.push_back(total);
+            unsigned long long ns[kGrowPhases];
+            SB2_CUDA(b, cudaMemcpy(ns, b->phase_ns.ptr, sizeof(ns), cudaMemcpyDeviceToHost));
+            for (int k = 0; k < kGrowPhases; ++k) last[kOpCount + k] = ns[k] * 1e-9;
+        }
+        timer.release();
+        SB2_TRY(st);
+        SB2_CUDA(b, se);
+    }
+    for (size_t k = 0; k < num_ops && k < last.size(); ++k) seconds_by_op[k] = last[k];
+    SB2_TRY(collect_model(b, tr, model));
+    if (out) *out = model.release();
     return SB2_OK;
 }
 

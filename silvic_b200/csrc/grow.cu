@@ -1,0 +1,186 @@
+// grow.cu — one tree grown by one persistent kernel (Learner::grow, crates/silvic-core/src/learner.rs:121-169).
+//
+// A split step as separate launches costs a launch and a reload of the dataset's metadata per kernel, about 40 us
+// of fixed time per split on small leaves, which dominates a 255-leaf tree. Here one cooperative launch (every CTA
+// resident, one per SM) runs every step of the tree; its phases are separated by grid barriers:
+//   root:   histogram -> slab reduction -> search -> finish
+//   split:  partition flags -> scatter -> histogram of the smaller child -> slab reduction -> search -> finish
+// `finish` (apply the split, pick each child's best split, choose the next leaf) runs in the last CTA to arrive at
+// the search barrier before it releases the others. The phases are the device functions of partition.cuh,
+// hist_device.cuh and search.cuh, the same code the standalone kernels of the multi-GPU path run.
+//
+// Every barrier wait is bounded: a CTA that waits longer than kBarrierSpins polls records an error in the
+// iteration state and leaves the kernel, and every other CTA then leaves at its next barrier; the host reports the
+// error. Data another CTA wrote in the same launch is read with ld.global.cg (past the SM's L1).
+#include <cuda_runtime.h>
+
+#include "hist_device.cuh"
+#include "partition.cuh"
+#include "search.cuh"
+
+namespace sb2 {
+
+namespace {
+
+constexpr unsigned long long kBarrierSpins = 1ull << 26;  // ~3 s of 40 ns polls
+constexpr int kGrowThreads = kHistThreads;                // 512: the histogram phase needs it
+
+struct GrowArgs {
+    TrainArgs t;
+    HistArgs h;
+    unsigned int* barrier;        // [arrived, generation]
+    uint32_t hist_slots;
+    uint32_t pad_;
+    unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// CTA 0 adds the time since the previous mark to phase `k`'s total (when profiling).
+struct PhaseClock {
+    unsigned long long* out;
+    unsigned long long last;
+    __device__ void mark(int k) {
+        if (out == nullptr || blockIdx.x != 0 || threadIdx.x != 0) return;
+        const unsigned long long now = global_ns();
+        out[k] += now - last;
+        last = now;
+    }
+};
+
+// `*p`, which another CTA may have written in this launch, copied into shared memory once per CTA (one 32-bit word
+// per thread): every thread then reads the CTA's copy instead of all of them hitting the same L2 lines.
+template <class T>
+__device__ __forceinline__ void broadcast_cg(const T* p, T* shared_copy) {
+    static_assert(sizeof(T) % 4 == 0 && sizeof(T) / 4 <= kHistThreads, "copied as 32-bit words, one per thread");
+    __syncthreads();  // every thread is done with the previous copy
+    if (threadIdx.x < sizeof(T) / 4)
+        reinterpret_cast<unsigned int*>(shared_copy)[threadIdx.x] =
+            __ldcg(reinterpret_cast<const unsigned int*>(p) + threadIdx.x);
+    __syncthreads();
+}
+
+__device__ __forceinline__ bool failed(const GrowArgs& g) { return __ldcg(&g.t.iter->error) != 0; }
+
+// Grid barrier; the last CTA to arrive runs `tail(...)` (whole CTA) before releasing the others. Returns false
+// once any CTA has recorded an error.
+template <class Tail>
+__device__ bool grid_barrier(const GrowArgs& g, Tail tail) {
+    __shared__ unsigned int s_last, s_gen;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        volatile unsigned int* gen = g.barrier + 1;
+        s_gen = *gen;
+        __threadfence();
+        s_last = atomicAdd(g.barrier, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        tail();
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            g.barrier[0] = 0;
+            __threadfence();
+            atomicAdd(g.barrier + 1, 1u);
+        }
+    } else if (threadIdx.x == 0) {
+        volatile unsigned int* gen = g.barrier + 1;
+        unsigned long long spins = 0;
+        while (*gen == s_gen) {
+            if (++spins > kBarrierSpins) {
+                atomicCAS(&g.t.iter->error, 0, 3);  // a CTA never arrived
+                break;
+            }
+            __nanosleep(40);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return !failed(g);
+}
+
+__device__ __forceinline__ bool grid_barrier(const GrowArgs& g) {
+    return grid_barrier(g, [] {});
+}
+
+__global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) {
+    extern __shared__ __align__(16) int smem[];
+    const TrainArgs& a = g.t;
+    const uint32_t cta = blockIdx.x, ctas = gridDim.x;
+    const uint32_t warp = threadIdx.x >> 5, warps = kGrowThreads / 32;
+    const uint32_t gwarp = cta * warps + warp, gwarps = ctas * warps;
+    int2 (*search_buf)[kMaxBins] = reinterpret_cast<int2 (*)[kMaxBins]>(smem) + 2 * warp;
+    uint32_t* scratch_u32 = reinterpret_cast<uint32_t*>(smem);
+    PhaseClock clock{g.phase_ns, g.phase_ns ? global_ns() : 0ull};
+    __shared__ Step st;
+    __shared__ HistJob job;
+    __shared__ SearchCtx s;
+
+    for (int step = -1; step + 1 < a.max_leaves; ++step) {
+        broadcast_cg(a.step, &st);
+        if (!st.active) break;
+        if (!st.root) {
+            partition_flags_cta(a, st, cta, ctas, scratch_u32);
+            clock.mark(0);
+            if (!grid_barrier(g)) return;
+            clock.mark(6);
+            const uint32_t total_left = partition_scatter_cta(a, st, cta, ctas, scratch_u32);
+            if (cta == 0 && threadIdx.x == 0) partition_publish(a, *a.step, total_left);
+            clock.mark(1);
+            if (!grid_barrier(g)) return;
+            clock.mark(6);
+            broadcast_cg(a.step, &st);
+        }
+        // The new histogram (the root, or the smaller child), its slab reduction, the search.
+        broadcast_cg(a.hist_job, &job);
+        histogram_cta(g.h, job, cta, smem);
+        clock.mark(2);
+        if (!grid_barrier(g)) return;
+        clock.mark(6);
+        for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < g.hist_slots; i += ctas * kGrowThreads)
+            histogram_reduce_slot(g.h, job, i);
+        clock.mark(3);
+        if (!grid_barrier(g)) return;
+        clock.mark(6);
+        search_context_cta(a, st, &s);
+        if (s.searched)
+            for (uint32_t f = gwarp; f < a.num_features; f += gwarps) search_feature(a, st, s, f, search_buf);
+        clock.mark(4);
+        if (!grid_barrier(g, [&] { search_finish(a, st, s); })) return;
+        clock.mark(5);  // the barrier with the finish in it
+    }
+}
+
+}  // namespace
+
+int grow_threads() { return kGrowThreads; }
+
+cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
+    cudaError_t e = cudaFuncSetAttribute(grow_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, grow_tree_kernel, kGrowThreads, smem_bytes);
+}
+
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
+                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns) {
+    GrowArgs g{};
+    g.t = t;
+    g.h = h;
+    g.barrier = barrier;
+    g.hist_slots = hist_slots;
+    g.phase_ns = phase_ns;
+    cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet
+    if (e != cudaSuccess) return e;
+    void* args[] = {&g};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(grow_tree_kernel), dim3(grid), dim3(kGrowThreads),
+                                       args, static_cast<size_t>(smem_bytes), s);
+}
+
+}  // namespace sb2

@@ -1,14 +1,15 @@
 // hist.cuh — the quantized leaf histogram (silvic-core CpuBackend::histogram, backend/cpu.rs:838-864 and
 // histogram_quantized :479-513), as an sm_100a kernel.
 //
-// A CTA takes one "unit" (up to four consecutive tiles) over one chunk of the leaf's rows. Its shared memory holds
-// a private histogram of the unit in 64-bit packed (h << 32) + g slots, laid out bin-major per tile
-// (slot = bin * stride + lane), so lane j of a warp always hits the slot of its own feature: the 32 lanes of one row
-// fall in 32 consecutive slots, a conflict-free shared atomic. 64-bit slots never overflow for any row count a GPU
-// holds, so a CTA adds all its rows and flushes once, unpacking each non-zero slot into the int32 [g, h] pairs of
-// the output with global reductions. Rows come from the leaf's range of the row-id buffer with their packed
-// gradients from the ordered-gradient buffer (contiguous), or, for an identity partition (the root without
-// bagging), straight from the row index.
+// A CTA takes one "unit" (up to four consecutive tiles) over one chunk of the leaf's rows; units own CTA ranges in
+// proportion to their features. Its shared memory holds a private histogram of the unit: per tile an int32
+// gradient and an int32 hessian array, laid out bin-major (slot = bin * stride + feature lane), so a feature's bins
+// all sit in one bank. int32 sums never overflow for the rows one CTA adds, so a CTA flushes once: it stores its
+// shared histogram, in shared-memory order, to its own slab of a scratch buffer (coalesced stores, no atomics),
+// and a reduction kernel sums the slabs of the CTAs that took part into the flat [g, h] pairs of the output, one
+// writer per output value. Rows come from the leaf's range of the row-id buffer with their packed gradients from
+// the ordered-gradient buffer (contiguous), or, for an identity partition (the root without bagging), straight
+// from the row index.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -18,11 +19,15 @@
 namespace sb2 {
 
 constexpr int kMaxUnitTiles = 4;
+// Bytes of dynamic shared memory a histogram CTA needs beyond its unit's arrays: the kernel aligns them to this.
+constexpr uint32_t kHistAlign = 128;
 
 struct Unit {
     uint32_t first_tile;
     uint32_t num_tiles;
-    uint32_t slots;  // 64-bit shared slots of the unit
+    uint32_t slots;      // gradient slots of the unit (as many hessian slots follow each tile's)
+    uint32_t cta_begin;  // the unit's CTAs are cta_begin .. cta_begin + cta_count of the launch
+    uint32_t cta_count;
     uint32_t pad_;
 };
 
@@ -46,10 +51,22 @@ struct HistArgs {
     const int32_t* ordered[2];    // ordered packed gradients, by partition position
     const int32_t* packed;        // packed gradients by row (identity jobs)
     const uint8_t* active;        // per feature: its bins are wanted; nullptr for all
-    int* out;                     // 2 * total_bins int32, accumulated into
+    int* out;                     // 2 * total_bins int32: the wanted features' bins are overwritten
+    int* slabs;                   // scratch: one slab of slab_ints per CTA of the launch
+    uint32_t slab_ints;           // 2 * the largest unit's slots
+    uint32_t pad_;
 };
 
+// The CTAs a unit uses for a job of `count` rows (the histogram and its reduction agree on it).
+__host__ __device__ __forceinline__ uint32_t unit_chunks(const Unit& u, uint32_t count, uint32_t min_rows) {
+    uint32_t chunks = static_cast<uint32_t>(ceil_div(count, min_rows));
+    chunks = chunks < 1 ? 1 : chunks;
+    return chunks > u.cta_count ? u.cta_count : chunks;
+}
+
+// The histogram: each CTA's private histogram into its scratch slab, then the slabs summed into `out`.
 void launch_histogram(const HistArgs& a, int grid, int smem_bytes, cudaStream_t stream);
+void launch_histogram_reduce(const HistArgs& a, uint32_t total_slots, cudaStream_t stream);
 cudaError_t histogram_configure(int smem_bytes);
 cudaError_t histogram_occupancy(int smem_bytes, int* blocks_per_sm);
 int histogram_threads();

@@ -1,0 +1,288 @@
+// hist_device.cuh — the histogram's CTA-level device functions (see hist.cuh), shared by the standalone kernels
+// (hist.cu) and the persistent tree kernel (grow.cu).
+//
+// Shared memory of a CTA: for each tile of its unit, an int32 gradient array and an int32 hessian array of
+// smem_bins * stride slots, slot = bin * stride + feature lane. Native 32-bit shared atomics run 4-6x faster than
+// 64-bit ones on sm_100, so g and h are added separately rather than as one packed 64-bit value.
+//
+// Work per warp: 32 consecutive positions of the leaf, lane k owning position k's row. A lane loads its row's tile
+// bytes with 128-bit loads (a 32-byte row is one sector; a warp's 32 rows are in flight together), permutes them by
+// its lane index, and walks them: at step i lane k adds its row's (g, h) at feature i XOR (k mod stride), so in a
+// full tile the 32 lanes of every atomic hit 32 different features, i.e. 32 different banks. The arrays are
+// aligned and sized (64, 128 or 256 bins per lane) so that an element costs one multiply-add for its address and
+// two shared reductions, the hessian's at a compile-time offset. Rows whose packed gradient is zero add nothing and
+// skip their atomics.
+#pragma once
+
+#include "hist.cuh"
+
+namespace sb2 {
+
+constexpr int kHistThreads = 512;
+
+struct LaneTile {
+    const uint8_t* base;  // the tile's row 0
+    uint32_t stride;      // 4, 8, 16 or 32 bytes
+    uint32_t bins;        // 64, 128 or 256: bin slots per feature lane
+    uint32_t g_addr;      // shared address of the tile's gradient array (aligned to 4 * stride bytes)
+    uint32_t active;      // bit f: feature lane f is wanted (0: the tile is skipped)
+};
+
+// Permutes the `W` words of a row so that byte i becomes the row's byte i ^ k (k < 4 W): byte bits within each word
+// by one byte_perm, word bits by conditional swaps.
+template <int W>
+__device__ __forceinline__ void xor_bytes(uint32_t (&w)[W], uint32_t k) {
+    const uint32_t kb = k & 3;
+    const uint32_t sel = (0u ^ kb) | ((1u ^ kb) << 4) | ((2u ^ kb) << 8) | ((3u ^ kb) << 12);
+#pragma unroll
+    for (int j = 0; j < W; ++j) w[j] = __byte_perm(w[j], 0u, sel);
+    const uint32_t q = k >> 2;
+#pragma unroll
+    for (int bit = 1; bit < W; bit <<= 1) {
+        const bool swap = (q & bit) != 0;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            if (j & bit) continue;
+            const uint32_t lo = w[j], hi = w[j | bit];
+            w[j] = swap ? hi : lo;
+            w[j | bit] = swap ? lo : hi;
+        }
+    }
+}
+
+// Adds (g, h) at shared address `addr` (the gradient slot) and addr + kHessianOffset (the hessian slot), with
+// red.shared: no return value, never the generic path. No "memory" clobber: the compiler may move global loads
+// across these (the histogram is only read after a barrier).
+template <uint32_t kHessianOffset>
+__device__ __forceinline__ void shared_add_pair(uint32_t addr, int32_t g, int32_t h) {
+    asm volatile(
+        "red.shared.add.s32 [%0], %1;\n\t"
+        "red.shared.add.s32 [%0+%3], %2;" ::"r"(addr),
+        "r"(g), "r"(h), "n"(kHessianOffset));
+}
+
+// Issues the loads of one row of a tile (stride 4, 8, 16 or 32 bytes) into w[0 .. stride / 4).
+__device__ __forceinline__ void load_row(const LaneTile& t, uint32_t row, uint32_t (&w)[8]) {
+    const uint8_t* p = t.base + static_cast<uint64_t>(row) * t.stride;
+    if (t.stride == 32) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+        w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w, w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
+    } else if (t.stride == 16) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+        w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w;
+    } else if (t.stride == 8) {
+        const uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+        w[0] = a.x, w[1] = a.y;
+    } else {
+        w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+    }
+}
+
+// Adds one loaded row of one tile of `W` words (stride S = 4 W bytes) and `B` bins per lane: the lane's row's
+// (g, h) at feature i ^ k for i = 0 .. S-1, k = lane mod S. Slot (bin, f) of the gradient array is word
+// bin * S + f, so the S lanes of every step hit S different features, i.e. S different banks; with the array
+// aligned to 4 S bytes the slot's address is bin * 4S + (base | 4k) ^ 4i, one multiply-add per element. Every
+// feature of the tile is added, wanted or not: only wanted features' bins are ever read back.
+template <int W, int B>
+__device__ __forceinline__ void add_row(const LaneTile& t, uint32_t (&wrow)[8], int32_t g, int32_t h, uint32_t lane) {
+    constexpr uint32_t kStride = 4 * W;
+    uint32_t w[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) w[j] = wrow[j];
+    const uint32_t k = lane & (kStride - 1);
+    xor_bytes<W>(w, k);
+    const uint32_t base = t.g_addr | (4 * k);
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(kStride); ++i) {
+        const uint32_t bin = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        shared_add_pair<4 * B * kStride>(bin * (4 * kStride) + (base ^ (4u * i)), g, h);
+    }
+}
+
+template <int W>
+__device__ __forceinline__ void add_row_bins(const LaneTile& t, uint32_t (&wrow)[8], int32_t g, int32_t h,
+                                             uint32_t lane) {
+    if (t.bins == 256)
+        add_row<W, 256>(t, wrow, g, h, lane);
+    else if (t.bins == 128)
+        add_row<W, 128>(t, wrow, g, h, lane);
+    else
+        add_row<W, 64>(t, wrow, g, h, lane);
+}
+
+// The unit of histogram CTA `cta`.
+__device__ __forceinline__ uint32_t unit_of_cta(const HistArgs& a, uint32_t cta) {
+    uint32_t ui = 0;
+    while (ui + 1 < a.num_units && cta >= a.units[ui + 1].cta_begin) ++ui;
+    return ui;
+}
+
+// CTA `cta`'s share of `job`: its unit's rows of its chunk into shared memory, then into its slab. Needs
+// kHistThreads threads; returns without touching the slab when the CTA has no chunk.
+inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint32_t cta, int* sh) {
+    if (!job.active || job.count == 0) return;
+    const Unit unit = a.units[unit_of_cta(a, cta)];
+    const uint32_t chunk = cta - unit.cta_begin;
+    const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
+    if (chunk >= chunks) return;
+    const uint32_t lo = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * chunk / chunks);
+    const uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * (chunk + 1) / chunks);
+
+    // The histogram starts at the first 128-byte boundary of `sh` (the callers reserve kHistAlign more bytes).
+    const uint32_t sh_raw = static_cast<uint32_t>(__cvta_generic_to_shared(sh));
+    const uint32_t sh_addr = (sh_raw + kHistAlign - 1) & ~(kHistAlign - 1);
+    sh += (sh_addr - sh_raw) / 4;
+    {
+        int4* z = reinterpret_cast<int4*>(sh);
+        for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) z[i] = make_int4(0, 0, 0, 0);
+    }
+
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t warp = threadIdx.x >> 5;
+    constexpr uint32_t kWarps = kHistThreads / 32;
+    // The features of each tile the histogram wants, one bit per lane, read once per CTA (warp 0).
+    __shared__ uint32_t s_tile_active[kMaxUnitTiles];
+    if (warp == 0) {
+#pragma unroll
+        for (int t = 0; t < kMaxUnitTiles; ++t) {
+            bool on = false;
+            if (t < static_cast<int>(unit.num_tiles)) {
+                const int32_t f = a.d.lane_feature[(unit.first_tile + t) * kTileLanes + lane];
+                on = f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0);
+            }
+            const uint32_t bits = __ballot_sync(0xffffffffu, on);
+            if (lane == 0) s_tile_active[t] = bits;
+        }
+    }
+    LaneTile lt[kMaxUnitTiles];
+    __syncthreads();
+    uint32_t any = 0;
+    {
+        uint32_t slot = 0;  // words; every tile's arrays are 2 B S words, B >= 64: 512-word multiples
+#pragma unroll
+        for (int t = 0; t < kMaxUnitTiles; ++t) {
+            lt[t].active = 0;
+            lt[t].stride = 4;
+            lt[t].bins = 64;
+            lt[t].base = a.d.bins;
+            lt[t].g_addr = sh_addr;
+            if (t < static_cast<int>(unit.num_tiles)) {
+                const Tile tile = a.d.tiles[unit.first_tile + t];
+                lt[t].base = a.d.bins + tile.base;
+                lt[t].stride = tile.stride;
+                lt[t].bins = tile.smem_bins;
+                lt[t].g_addr = sh_addr + 4 * slot;
+                slot += 2 * tile.smem_bins * tile.stride;
+                lt[t].active = s_tile_active[t];
+                any |= lt[t].active;
+            }
+        }
+    }
+
+    const uint32_t span = hi - lo;
+    const uint32_t per_warp = static_cast<uint32_t>(ceil_div(ceil_div(span, kWarps), 32) * 32);
+    const uint32_t w_lo = lo + min(span, per_warp * warp);
+    const uint32_t w_hi = lo + min(span, per_warp * (warp + 1));
+    const uint32_t* rows = a.rows[job.which & 1];
+    const int32_t* ordered = a.ordered[job.which & 1];
+    // The row and packed gradient of position p (0 past the warp's range).
+    auto position = [&](uint32_t p, uint32_t& row, int32_t& packed) {
+        row = 0;
+        packed = 0;
+        if (p < w_hi) {
+            const uint32_t pos = job.begin + p;
+            if (job.identity) {
+                row = pos;
+                packed = __ldg(a.packed + pos);
+            } else {
+                row = __ldcg(rows + pos);  // written by this step's partition: not through the read-only path
+                packed = __ldcg(ordered + pos);
+            }
+        }
+    };
+    if (any != 0 && w_lo < w_hi) {
+        uint32_t next_row;
+        int32_t next_packed;
+        position(w_lo + lane, next_row, next_packed);
+        for (uint32_t p0 = w_lo; p0 < w_hi; p0 += 32) {
+            const uint32_t row = next_row;
+            const int32_t packed = next_packed;
+            // Every tile's bytes of this batch's rows in flight at once, and the next batch's positions.
+            uint32_t wd[kMaxUnitTiles][8];
+#pragma unroll
+            for (int t = 0; t < kMaxUnitTiles; ++t)
+                if (lt[t].active != 0) load_row(lt[t], row, wd[t]);
+            position(p0 + 32 + lane, next_row, next_packed);
+            // unpack (quantize.rs:140-143); a zero row adds nothing.
+            const int32_t g = static_cast<int16_t>(static_cast<uint16_t>(static_cast<uint32_t>(packed)));
+            const int32_t h = (packed - g) >> 16;
+            if (packed == 0) continue;
+#pragma unroll
+            for (int t = 0; t < kMaxUnitTiles; ++t) {
+                if (lt[t].active == 0) continue;
+                switch (lt[t].stride) {
+                    case 32:
+                        add_row_bins<8>(lt[t], wd[t], g, h, lane);
+                        break;
+                    case 16:
+                        add_row_bins<4>(lt[t], wd[t], g, h, lane);
+                        break;
+                    case 8:
+                        add_row_bins<2>(lt[t], wd[t], g, h, lane);
+                        break;
+                    default:
+                        add_row_bins<1>(lt[t], wd[t], g, h, lane);
+                        break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // Flush: the shared histogram, as laid out, to this CTA's slab (2 * unit.slots ints, a multiple of 4).
+    int4* slab = reinterpret_cast<int4*>(a.slabs + static_cast<size_t>(cta) * a.slab_ints);
+    const int4* src = reinterpret_cast<const int4*>(sh);
+    for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) __stcg(slab + i, src[i]);
+    __syncthreads();
+}
+
+// Gradient slot `i` over every unit: the sum of the slabs of the unit's CTAs that took part, written into the flat
+// [g, h] output when its feature is wanted.
+inline __device__ void histogram_reduce_slot(const HistArgs& a, const HistJob& job, uint32_t i) {
+    if (!job.active || job.count == 0) return;
+    for (uint32_t u = 0; u < a.num_units; ++u) {
+        const Unit unit = a.units[u];
+        if (i >= unit.slots) {
+            i -= unit.slots;
+            continue;
+        }
+        // The tile holding slot i of the unit, and the slot's offsets in the slab.
+        uint32_t off = 0, local = i, ti = unit.first_tile;
+        Tile tile = a.d.tiles[ti];
+        while (local >= tile.smem_bins * tile.stride) {
+            const uint32_t n = tile.smem_bins * tile.stride;
+            local -= n;
+            off += 2 * n;
+            tile = a.d.tiles[++ti];
+        }
+        const uint32_t n = tile.smem_bins * tile.stride;
+        const uint32_t bin = local / tile.stride, lane = local % tile.stride;
+        const int32_t f = a.d.lane_feature[ti * kTileLanes + lane];
+        if (f < 0 || (a.active != nullptr && __ldcg(a.active + f) == 0)) return;
+        const DevFeature feat = a.d.features[f];
+        if (bin >= feat.num_bins) return;
+        const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
+        const int* slab = a.slabs + static_cast<size_t>(unit.cta_begin) * a.slab_ints + off + local;
+        int g = 0, h = 0;
+#pragma unroll 4
+        for (uint32_t c = 0; c < chunks; ++c) {
+            g += __ldcg(slab + static_cast<size_t>(c) * a.slab_ints);
+            h += __ldcg(slab + static_cast<size_t>(c) * a.slab_ints + n);
+        }
+        __stcg(reinterpret_cast<int2*>(a.out) + feat.hist_offset + bin, make_int2(g, h));
+        return;
+    }
+}
+
+}  // namespace sb2

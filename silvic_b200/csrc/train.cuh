@@ -128,9 +128,18 @@ struct FeatureCandidate {
 
 static_assert(sizeof(FeatureCandidate) % 8 == 0, "candidates are copied as 64-bit words");
 
-constexpr int kPartitionTile = 4096;  // positions per partition tile
+constexpr int kMaxPartitionCtas = 8192;  // CTAs a partition launch may use (one left count each)
 constexpr int kPartitionThreads = 256;
 constexpr int kSearchThreads = 256;   // 8 warps, one feature each
+
+// The persistent tree kernel (grow.cu): every step of one tree in one cooperative launch.
+int grow_threads();
+cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
+// `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: partition flags,
+// scatter, histogram, slab reduction, search, the barrier that runs the finish, the other barriers.
+constexpr int kGrowPhases = 7;
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
+                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

@@ -249,6 +249,16 @@ def oracle_params():
     return dict(objective=_abi.BINARY, num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
 
 
+def set_rows(rows: int):
+    global ROWS
+    ROWS = rows
+
+
+def workload() -> str:
+    size = "10M" if ROWS == 10_000_000 else f"{ROWS:,} rows (reduced)"
+    return f"configs[1]: binary {size} x 100, 255 bins, 255 leaves"
+
+
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
@@ -260,12 +270,12 @@ def run_reference(args, rank: int, world: int):
     per_iter = max(warm_secs)
     k = int(max(1, min(args.steps, 60.0 // max(per_iter, 1e-3))))
     rate, secs, cores = oracle_rate(data, k, oracle_params())
-    sample = f"{len(secs)} boosting iterations of the full 10M x 100 config on {cores} threads"
+    sample = f"{len(secs)} boosting iterations of the full {ROWS:,} x 100 set on {cores} threads"
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "iters/s", "n_gpus": world,
             "steps": args.steps, "timed_steps": len(secs), "warmup": args.warmup,
             "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int32 histograms / f64 split search", "data": "synthetic",
-            "config": {"workload": "configs[1]: binary 10M x 100, 255 bins, 255 leaves", "rows": ROWS,
+            "config": {"workload": workload(), "rows": ROWS,
                        "features": FEATURES, "num_leaves": 255},
             "cpu_baseline": {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": rate, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -311,6 +321,7 @@ def run_b200(args, rank: int, world: int):
     # Roofline of the dominant kernel: the root histogram (every row, every feature).
     hist_s = backend.time_histogram(10)
     backend.close()
+    launches_persistent = world == 1  # one GPU grows each tree in one cooperative launch
     t = torch.tensor([timed, hist_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -358,7 +369,7 @@ def run_b200(args, rank: int, world: int):
         "vs_baseline": None,
         "dtype": "int32 histograms / f64 split search",
         "data": "synthetic",
-        "config": {"workload": "configs[1]: binary 10M x 100, 255 bins, 255 leaves", "rows": ROWS,
+        "config": {"workload": workload(), "rows": ROWS,
                    "features": FEATURES, "num_leaves": 255, "parallelism": f"rows sharded over {world} GPU(s)",
                    "l2": "inputs (1 GB binned) larger than L2; no flush"},
         "trees": trees,
@@ -370,12 +381,15 @@ def run_b200(args, rank: int, world: int):
         "clocks": clocks.summary(),
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
-        "gpu_launches": args.steps * (4 + 4 * 254 + 3),
+        # Our kernels per iteration: gradients, iteration start (quantize), the tree (one persistent launch, or
+        # histogram + reduction + search for the root and partition flags + scatter + histogram + reduction + search
+        # per split with NCCL ranks), leaf sums, finalize, score update.
+        "gpu_launches": args.steps * (6 if launches_persistent else 3 + 3 + 5 * (PARAMS["num_leaves"] - 1) + 3),
     }
     if world == 1 and not args.no_cpu_baseline:
         rate, secs, cores = oracle_rate(data, 2, oracle_params())
         line["cpu_baseline"] = {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port",
-                                "sample": f"2 boosting iterations of the same 10M x 100 dataset, "
+                                "sample": f"2 boosting iterations of the same {ROWS:,} x 100 dataset, "
                                           f"{sum(secs):.1f} s on {cores} threads"}
     print(json.dumps(line), flush=True)
 
@@ -387,7 +401,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="rows of the synthetic set (a smaller case for profiling; the benchmark is 10,000,000)")
     args = ap.parse_args()
+    set_rows(args.rows)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1:

@@ -279,6 +279,24 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
                         double sum_grad, double sum_hess, int64_t count, double grad_scale, double hess_scale,
                         const sb2_split_config* cfg, sb2_split_info* out, uint8_t* splittable);
 
+/* No counterpart in the reference: sb2_find_best_split for callers that cannot let a call allocate device memory
+ * (their HBM belongs to another allocator, or a cudaMalloc/cudaFree would stall their other streams). Same search,
+ * same result; every pointer is device memory of b's device that the caller owns:
+ *   hist        2 * total_bins int32, [g, h] histogram units per bin (len = 2 * total_bins)
+ *   evaluate    num_features bytes, nonzero = search the feature
+ *   out         one sb2_split_info, written
+ *   splittable  num_features bytes, written
+ * The call allocates nothing: its scratch is a fixed 320 KiB array in this library's device module, enough for
+ * datasets of at most 4096 features; larger ones return SB2_EUNSUPPORTED. The first call on each device looks up
+ * that array's address (cudaGetSymbolAddress, which may load the module), so make it before any stream capture.
+ * The call runs on the handle's stream and returns once the results are written; the caller's writes to `hist`
+ * and `evaluate` must be complete before it. All calls on one device share the one scratch array: calls that
+ * overlap (from other threads, or other handles on the same device) race and give wrong results. */
+int sb2_find_best_split_noalloc(sb2_backend* b, const int32_t* hist, size_t len, const uint8_t* evaluate,
+                                double sum_grad, double sum_hess, int64_t count, double grad_scale,
+                                double hess_scale, const sb2_split_config* cfg, sb2_split_info* out,
+                                uint8_t* splittable);
+
 /* ---- measurement -------------------------------------------------------------------------------------------- */
 
 /* Times `repeats` histograms of rows 0 .. rows - 1 (all rows when `rows` is 0) with every feature, as the trainer

@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -827,6 +828,91 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
     SB2_CUDA(b, cudaGetLastError());
     SB2_CUDA(b, cudaMemcpyAsync(out, dout.ptr, sizeof(sb2_split_info), cudaMemcpyDeviceToHost, b->stream));
     SB2_CUDA(b, cudaMemcpyAsync(splittable, dspl.ptr, b->num_features, cudaMemcpyDeviceToHost, b->stream));
+    return b->sync();
+}
+
+}  // extern "C"
+
+// ---- the split search without allocation ---------------------------------------------------------------------
+//
+// sb2_find_best_split copies its inputs into device buffers it allocates for the call. Some callers cannot let a
+// call allocate: a serving or training loop whose memory belongs to another allocator (a caching allocator that
+// holds nearly all of HBM, where a fresh cudaMalloc fails), a loop on other streams that cudaMalloc/cudaFree would
+// stall (they synchronize the device), or code that budgets its device memory up front. For them
+// sb2_find_best_split_noalloc takes device buffers the caller owns and runs the same search kernel with its scratch
+// (one candidate per feature and a CTA arrival counter) in a fixed array of this library's module, sized for
+// kNoAllocMaxFeatures features.
+namespace {
+
+constexpr uint32_t kNoAllocMaxFeatures = 4096;
+constexpr size_t kNoAllocCounterBytes = 256;  // the arrival counter, padded so the candidates stay 256-aligned
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + sizeof(FeatureCandidate) * kNoAllocMaxFeatures;
+constexpr int kNoAllocMaxDevices = 64;
+
+// [0, 4): the counter, which must be zero when a launch starts (each call clears it); then the candidates.
+static __device__ __align__(256) unsigned char g_noalloc_split_scratch[kNoAllocScratchBytes];
+
+// The scratch's device address on b's device, looked up once per device (with that device current) and kept.
+int noalloc_split_scratch(sb2_backend* b, unsigned char** out) {
+    static std::mutex lock;
+    static void* addresses[kNoAllocMaxDevices] = {};
+    if (b->device < 0 || b->device >= kNoAllocMaxDevices)
+        return b->fail(SB2_EUNSUPPORTED, "sb2_find_best_split_noalloc: device " + std::to_string(b->device) +
+                                             " beyond the " + std::to_string(kNoAllocMaxDevices) + " it keeps scratch for");
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[b->device] == nullptr) {
+        void* p = nullptr;
+        SB2_CUDA(b, cudaGetSymbolAddress(&p, g_noalloc_split_scratch));
+        addresses[b->device] = p;
+    }
+    *out = static_cast<unsigned char*>(addresses[b->device]);
+    return SB2_OK;
+}
+
+// SB2_OK when `p` is memory of b's device (device or managed); what the search reads and writes must be.
+int check_device_pointer(sb2_backend* b, const void* p, const char* what) {
+    if (p == nullptr) return b->fail(SB2_EDEVICE, std::string("sb2_find_best_split_noalloc: null ") + what);
+    cudaPointerAttributes attr{};
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // clear it: the pointer is the caller's mistake, not a device error
+        return b->fail(SB2_EDEVICE, std::string("sb2_find_best_split_noalloc: ") + what + " is not a CUDA pointer");
+    }
+    const bool on_device = attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+    if (!on_device || attr.device != b->device)
+        return b->fail(SB2_EDEVICE, std::string("sb2_find_best_split_noalloc: ") + what + " is not memory of device " +
+                                        std::to_string(b->device));
+    return SB2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb2_find_best_split_noalloc(sb2_backend* b, const int32_t* hist, size_t len, const uint8_t* evaluate,
+                                double sum_grad, double sum_hess, int64_t count, double grad_scale,
+                                double hess_scale, const sb2_split_config* cfg, sb2_split_info* out,
+                                uint8_t* splittable) {
+    if (!b) return SB2_EDEVICE;
+    SB2_TRY(b->check_loaded());
+    if (!cfg) return b->fail(SB2_EDEVICE, "sb2_find_best_split_noalloc: null split config");
+    if (len != 2ull * b->total_bins) return b->fail(SB2_EDEVICE, "histogram of the wrong length");
+    if (b->num_features > kNoAllocMaxFeatures)
+        return b->fail(SB2_EUNSUPPORTED, "sb2_find_best_split_noalloc: the dataset has " +
+                                             std::to_string(b->num_features) + " features, its scratch holds " +
+                                             std::to_string(kNoAllocMaxFeatures) + " (use sb2_find_best_split)");
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    SB2_TRY(check_device_pointer(b, hist, "histogram"));
+    SB2_TRY(check_device_pointer(b, evaluate, "evaluate flags"));
+    SB2_TRY(check_device_pointer(b, out, "split output"));
+    SB2_TRY(check_device_pointer(b, splittable, "splittable flags"));
+    unsigned char* scratch = nullptr;
+    SB2_TRY(noalloc_split_scratch(b, &scratch));
+    unsigned int* counter = reinterpret_cast<unsigned int*>(scratch);
+    SB2_CUDA(b, cudaMemsetAsync(counter, 0, sizeof(unsigned int), b->stream));
+    launch_api_find_split(b->dev_data(), hist, evaluate, sum_grad, sum_hess, count, grad_scale, hess_scale, *cfg,
+                          scratch + kNoAllocCounterBytes, counter, out, splittable, b->search_grid(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
     return b->sync();
 }
 

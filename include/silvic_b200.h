@@ -309,7 +309,9 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
  * time of the last iteration per operation, in the order gradients, quantize (and the iteration's start),
  * histogram, partition, split search, leaf sums, finalize (renewal and the tree record), score update, NCCL
  * collectives, and the whole tree when one persistent kernel grows it (single GPU; the histogram, partition and
- * search entries are then 0) (num_ops <= 10). The per-operation breakdown of the reference's `Timed` test backend
+ * search entries are then 0); then that kernel's phases summed over the tree's steps (device clock of its first
+ * CTA): partition flags, scatter, histogram, slab reduction, search, finish, and the time spent in grid barriers
+ * (num_ops <= 17; fewer fills a prefix). The per-operation breakdown of the reference's `Timed` test backend
  * (crates/silvic-core/tests/train_cpu.rs:434-484). `out` (may be NULL) receives the model. */
 int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_score, double* seconds_by_op,
                       size_t num_ops, sb2_model** out);

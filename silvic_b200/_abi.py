@@ -224,6 +224,7 @@ SIGNATURES = {
                                               C.c_double, C.c_double, P(SplitConfig), VP, VP]),
     "sb2_time_histogram": (C.c_int, [VP, C.c_uint64, C.c_int, P(C.c_double)]),
     "sb2_profile_train": (C.c_int, [VP, P(Params), C.c_double, P(C.c_double), C.c_size_t, P(VP)]),
+    "sb2_profile_steps": (C.c_int, [VP, P(Params), C.c_double, P(C.c_double), C.c_size_t, P(C.c_size_t)]),
     "sb2_nccl_unique_id": (C.c_int, [P(C.c_uint8), C.c_size_t]),
     "sb2_join_ranks": (C.c_int, [VP, P(C.c_uint8), C.c_size_t, C.c_int, C.c_int]),
     "sb2_train": (C.c_int, [VP, P(Params), C.c_double, P(VP)]),

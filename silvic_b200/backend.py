@@ -240,6 +240,18 @@ class B200Backend:
         finally:
             self._lib.sb2_model_free(m)
 
+    STEP_FIELDS = ("partition_flags", "scatter", "histogram", "slab_reduce", "search", "finish", "barriers",
+                   "hist_rows", "direct", "leaf_rows")
+
+    def profile_steps(self, params: _abi.Params, init_score: float, max_steps: int = 1 << 17) -> np.ndarray:
+        """Per split step of the last tree (row 0 the root): the tree kernel's phase seconds and the step's sizes,
+        columns STEP_FIELDS."""
+        rows = np.zeros((max_steps, len(self.STEP_FIELDS)), dtype=np.float64)
+        n = C.c_size_t()
+        self._check(self._lib.sb2_profile_steps(self._h, C.byref(params), init_score,
+                                                rows.ctypes.data_as(C.POINTER(C.c_double)), max_steps, C.byref(n)))
+        return rows[: n.value]
+
     # ---- multi-GPU ----
     @staticmethod
     def nccl_unique_id() -> bytes:

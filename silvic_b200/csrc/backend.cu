@@ -194,8 +194,8 @@ struct sb2_backend {
 
     int row_grid() const { return sms * 8; }
     int partition_grid() const { return sms * 4; }
-    int search_grid() const {
-        int g = static_cast<int>((num_features + 7) / 8);
+    int search_grid() const {  // a warp per (child, feature) item, 8 warps per CTA
+        int g = static_cast<int>((2 * num_features + 7) / 8);
         return std::max(1, std::min(g, sms * 4));
     }
 
@@ -511,8 +511,8 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, histogram_occupancy(b->hist_smem, &per_sm));
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
-    // per-warp bins (two children of 256 [g, h] pairs per warp) and the partition's scan.
-    b->grow_smem = std::max<int>(b->hist_smem, (grow_threads() / 32) * 2 * kMaxBins * 8);
+    // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
+    b->grow_smem = std::max<int>(b->hist_smem, (grow_threads() / 32) * kMaxBins * 8);
     int grow_per_sm = 0;
     SB2_CUDA(b, grow_configure(b->grow_smem, &grow_per_sm));
     b->grow_ok = grow_per_sm >= 1;
@@ -1097,7 +1097,8 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
         SB2_TRY(op(kOpTree, [&] {
             return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_slots, b->hist_grid,
                                             b->grow_smem, s,
-                                            timer ? b->phase_ns.as<unsigned long long>() : nullptr),
+                                            timer ? b->phase_ns.as<unsigned long long>() : nullptr,
+                                            timer ? max_leaves : 0),
                            "cudaLaunchCooperativeKernel(grow_tree)");
         }));
         max_leaves = 1;  // no separate split steps
@@ -1394,14 +1395,22 @@ int sb2_boost_from_average(const sb2_params* p, const float* label, const float*
     return SB2_OK;
 }
 
-int sb2_profile_train(sb2_backend* b, const sb2_params* p, double init_score, double* seconds_by_op, size_t num_ops,
-                      sb2_model** out) {
-    if (!b || !p || !seconds_by_op) return SB2_EDEVICE;
+}  // extern "C"
+
+namespace {
+
+// Training without the CUDA graph, each operation between CUDA events: `last` gets the last iteration's seconds per
+// operation (kOpCount) and per phase of the tree kernel (kGrowPhases); `trace` its per-step rows (kStepTrace values,
+// nanoseconds and row counts; empty when the tree kernel did not run).
+int profile_run(sb2_backend* b, const sb2_params* p, double init_score, std::vector<double>& last,
+                std::vector<unsigned long long>& trace, std::unique_ptr<sb2_model>& model) {
     Training tr;
     SB2_TRY(setup_training(b, p, init_score, tr));
-    std::vector<double> last(kOpCount + kGrowPhases, 0.0);
-    auto model = std::make_unique<sb2_model>();
-    SB2_CUDA(b, b->phase_ns.alloc(sizeof(unsigned long long) * kGrowPhases));
+    last.assign(kOpCount + kGrowPhases, 0.0);
+    trace.clear();
+    model = std::make_unique<sb2_model>();
+    const size_t words = kGrowPhases + static_cast<size_t>(tr.L) * kStepTrace;
+    SB2_CUDA(b, b->phase_ns.alloc(sizeof(unsigned long long) * words));
     for (int i = 0; i < tr.iters; ++i) {
         OpTimer timer;
         SB2_CUDA(b, cudaMemsetAsync(b->phase_ns.ptr, 0, b->phase_ns.bytes, b->stream));
@@ -1417,17 +1426,51 @@ int sb2_profile_train(sb2_backend* b, const sb2_params* p, double init_score, do
                 total += ms / 1000.0;
             }
             model->seconds.push_back(total);
-            unsigned long long ns[kGrowPhases];
-            SB2_CUDA(b, cudaMemcpy(ns, b->phase_ns.ptr, sizeof(ns), cudaMemcpyDeviceToHost));
+            std::vector<unsigned long long> ns(words);
+            SB2_CUDA(b, cudaMemcpy(ns.data(), b->phase_ns.ptr, sizeof(unsigned long long) * words,
+                                   cudaMemcpyDeviceToHost));
             for (int k = 0; k < kGrowPhases; ++k) last[kOpCount + k] = ns[k] * 1e-9;
+            if (b->persistent()) trace.assign(ns.begin() + kGrowPhases, ns.end());
         }
         timer.release();
         SB2_TRY(st);
         SB2_CUDA(b, se);
     }
+    return collect_model(b, tr, model);
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb2_profile_train(sb2_backend* b, const sb2_params* p, double init_score, double* seconds_by_op, size_t num_ops,
+                      sb2_model** out) {
+    if (!b || !p || !seconds_by_op) return SB2_EDEVICE;
+    std::vector<double> last;
+    std::vector<unsigned long long> trace;
+    std::unique_ptr<sb2_model> model;
+    SB2_TRY(profile_run(b, p, init_score, last, trace, model));
     for (size_t k = 0; k < num_ops && k < last.size(); ++k) seconds_by_op[k] = last[k];
-    SB2_TRY(collect_model(b, tr, model));
     if (out) *out = model.release();
+    return SB2_OK;
+}
+
+int sb2_profile_steps(sb2_backend* b, const sb2_params* p, double init_score, double* rows, size_t max_steps,
+                      size_t* num_steps) {
+    if (!b || !p || !rows || !num_steps) return SB2_EDEVICE;
+    std::vector<double> last;
+    std::vector<unsigned long long> trace;
+    std::unique_ptr<sb2_model> model;
+    SB2_TRY(profile_run(b, p, init_score, last, trace, model));
+    if (trace.empty()) return b->fail(SB2_EUNSUPPORTED, "step traces come from the single-GPU tree kernel only");
+    const size_t leaves = model->trees.empty() ? 0 : static_cast<size_t>(model->trees.back().num_leaves);
+    const size_t steps = std::min<size_t>(leaves, trace.size() / kStepTrace);
+    *num_steps = std::min(steps, max_steps);
+    for (size_t s = 0; s < *num_steps; ++s)
+        for (int k = 0; k < kStepTrace; ++k) {
+            const double v = static_cast<double>(trace[s * kStepTrace + k]);
+            rows[s * kStepTrace + k] = k < kGrowPhases ? v * 1e-9 : v;
+        }
     return SB2_OK;
 }
 

@@ -31,7 +31,9 @@ struct GrowArgs {
     unsigned int* barrier;        // [arrived, generation]
     uint32_t hist_slots;
     uint32_t pad_;
-    unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps
+    unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
+    int trace_steps;              // then per-step rows (kStepTrace) for this many steps
+    int pad2_;
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -40,17 +42,38 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// CTA 0 adds the time since the previous mark to phase `k`'s total (when profiling).
+// Phase clock of CTA 0's thread 0 (when profiling), kept in shared memory so it holds no registers across phases:
+// mark(k) adds the time since the previous mark to phase k's total, and to the current step's trace row if any.
 struct PhaseClock {
-    unsigned long long* out;
+    unsigned long long* row;
     unsigned long long last;
-    __device__ void mark(int k) {
-        if (out == nullptr || blockIdx.x != 0 || threadIdx.x != 0) return;
-        const unsigned long long now = global_ns();
-        out[k] += now - last;
-        last = now;
-    }
 };
+
+__device__ __forceinline__ bool clock_owner(const GrowArgs& g) {
+    return g.phase_ns != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
+}
+
+__device__ __forceinline__ void clock_mark(const GrowArgs& g, PhaseClock& c, int k) {
+    if (!clock_owner(g)) return;
+    const unsigned long long now = global_ns();
+    g.phase_ns[k] += now - c.last;
+    if (c.row) c.row[k] += now - c.last;
+    c.last = now;
+}
+
+// The trace row of step `step` (-1: the root).
+__device__ __forceinline__ void clock_step(const GrowArgs& g, PhaseClock& c, int step) {
+    if (!clock_owner(g)) return;
+    c.row = step + 1 < g.trace_steps ? g.phase_ns + kGrowPhases + static_cast<size_t>(step + 1) * kStepTrace : nullptr;
+}
+
+__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, bool direct,
+                                               uint32_t leaf_rows) {
+    if (!clock_owner(g) || c.row == nullptr) return;
+    c.row[kGrowPhases] = job_rows;
+    c.row[kGrowPhases + 1] = direct;
+    c.row[kGrowPhases + 2] = leaf_rows;
+}
 
 // `*p`, which another CTA may have written in this launch, copied into shared memory once per CTA (one 32-bit word
 // per thread): every thread then reads the CTA's copy instead of all of them hitting the same L2 lines.
@@ -116,45 +139,58 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     const uint32_t cta = blockIdx.x, ctas = gridDim.x;
     const uint32_t warp = threadIdx.x >> 5, warps = kGrowThreads / 32;
     const uint32_t gwarp = cta * warps + warp, gwarps = ctas * warps;
-    int2 (*search_buf)[kMaxBins] = reinterpret_cast<int2 (*)[kMaxBins]>(smem) + 2 * warp;
-    uint32_t* scratch_u32 = reinterpret_cast<uint32_t*>(smem);
-    PhaseClock clock{g.phase_ns, g.phase_ns ? global_ns() : 0ull};
     __shared__ Step st;
     __shared__ HistJob job;
     __shared__ SearchCtx s;
+    __shared__ PhaseClock clock;
+    if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
 
     for (int step = -1; step + 1 < a.max_leaves; ++step) {
+        clock_step(g, clock, step);
         broadcast_cg(a.step, &st);
         if (!st.active) break;
         if (!st.root) {
-            partition_flags_cta(a, st, cta, ctas, scratch_u32);
-            clock.mark(0);
+            // Zeros in the staging histogram (its previous contents were read before the last barrier): the
+            // direct histogram adds into it. The left count slot is written by the scatter.
+            for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < a.total_bins + 1; i += ctas * kGrowThreads)
+                reinterpret_cast<int2*>(a.staging)[i] = make_int2(0, 0);
+            partition_flags_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
+            clock_mark(g, clock, 0);
             if (!grid_barrier(g)) return;
-            clock.mark(6);
-            const uint32_t total_left = partition_scatter_cta(a, st, cta, ctas, scratch_u32);
+            clock_mark(g, clock, 6);
+            const uint32_t total_left = partition_scatter_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
             if (cta == 0 && threadIdx.x == 0) partition_publish(a, *a.step, total_left);
-            clock.mark(1);
+            clock_mark(g, clock, 1);
             if (!grid_barrier(g)) return;
-            clock.mark(6);
+            clock_mark(g, clock, 6);
             broadcast_cg(a.step, &st);
         }
-        // The new histogram (the root, or the smaller child), its slab reduction, the search.
+        // The new histogram (the root, or the smaller child): straight into staging for a small job, else per-CTA
+        // shared histograms and their slab reduction. Then the search.
         broadcast_cg(a.hist_job, &job);
-        histogram_cta(g.h, job, cta, smem);
-        clock.mark(2);
+        const bool direct = job.count <= kDirectRows;
+        clock_describe(g, clock, job.active ? job.count : 0u, direct, st.count);
+        if (direct)
+            histogram_direct_cta(g.h, job, cta, ctas);
+        else
+            histogram_cta(g.h, job, cta, smem);
+        clock_mark(g, clock, 2);
         if (!grid_barrier(g)) return;
-        clock.mark(6);
-        for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < g.hist_slots; i += ctas * kGrowThreads)
-            histogram_reduce_slot(g.h, job, i);
-        clock.mark(3);
-        if (!grid_barrier(g)) return;
-        clock.mark(6);
+        clock_mark(g, clock, 6);
+        if (!direct) {
+            for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < g.hist_slots; i += ctas * kGrowThreads)
+                histogram_reduce_slot(g.h, job, i);
+            clock_mark(g, clock, 3);
+            if (!grid_barrier(g)) return;
+            clock_mark(g, clock, 6);
+        }
         search_context_cta(a, st, &s);
         if (s.searched)
-            for (uint32_t f = gwarp; f < a.num_features; f += gwarps) search_feature(a, st, s, f, search_buf);
-        clock.mark(4);
+            for (uint32_t item = gwarp; item < search_items(a, st); item += gwarps)
+                search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
+        clock_mark(g, clock, 4);
         if (!grid_barrier(g, [&] { search_finish(a, st, s); })) return;
-        clock.mark(5);  // the barrier with the finish in it
+        clock_mark(g, clock, 5);  // the barrier with the finish in it
     }
 }
 
@@ -169,13 +205,15 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
 }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
-                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns) {
+                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns,
+                             int trace_steps) {
     GrowArgs g{};
     g.t = t;
     g.h = h;
     g.barrier = barrier;
     g.hist_slots = hist_slots;
     g.phase_ns = phase_ns;
+    g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet
     if (e != cudaSuccess) return e;
     void* args[] = {&g};

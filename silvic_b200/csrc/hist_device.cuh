@@ -141,44 +141,34 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t warp = threadIdx.x >> 5;
     constexpr uint32_t kWarps = kHistThreads / 32;
-    // The features of each tile the histogram wants, one bit per lane, read once per CTA (warp 0).
-    __shared__ uint32_t s_tile_active[kMaxUnitTiles];
-    if (warp == 0) {
-#pragma unroll
-        for (int t = 0; t < kMaxUnitTiles; ++t) {
-            bool on = false;
-            if (t < static_cast<int>(unit.num_tiles)) {
-                const int32_t f = a.d.lane_feature[(unit.first_tile + t) * kTileLanes + lane];
-                on = f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0);
+    // The unit's tiles as the lanes use them, in shared memory (read per tile per batch, broadcast), with the
+    // features the histogram wants as one bit per lane (warp t fills tile t).
+    __shared__ LaneTile s_lt[kMaxUnitTiles];
+    const uint32_t num_tiles = unit.num_tiles;
+    if (warp < num_tiles) {
+        const int32_t f = a.d.lane_feature[(unit.first_tile + warp) * kTileLanes + lane];
+        const bool on = f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0);
+        const uint32_t bits = __ballot_sync(0xffffffffu, on);
+        if (lane == 0) {
+            // words before tile `warp`: every tile's arrays are 2 B S words (B >= 64, so 512-word multiples)
+            uint32_t slot = 0;
+            for (uint32_t t = 0; t < warp; ++t) {
+                const Tile prev = a.d.tiles[unit.first_tile + t];
+                slot += 2 * prev.smem_bins * prev.stride;
             }
-            const uint32_t bits = __ballot_sync(0xffffffffu, on);
-            if (lane == 0) s_tile_active[t] = bits;
+            const Tile tile = a.d.tiles[unit.first_tile + warp];
+            LaneTile lt;
+            lt.base = a.d.bins + tile.base;
+            lt.stride = tile.stride;
+            lt.bins = tile.smem_bins;
+            lt.g_addr = sh_addr + 4 * slot;
+            lt.active = bits;
+            s_lt[warp] = lt;
         }
     }
-    LaneTile lt[kMaxUnitTiles];
     __syncthreads();
     uint32_t any = 0;
-    {
-        uint32_t slot = 0;  // words; every tile's arrays are 2 B S words, B >= 64: 512-word multiples
-#pragma unroll
-        for (int t = 0; t < kMaxUnitTiles; ++t) {
-            lt[t].active = 0;
-            lt[t].stride = 4;
-            lt[t].bins = 64;
-            lt[t].base = a.d.bins;
-            lt[t].g_addr = sh_addr;
-            if (t < static_cast<int>(unit.num_tiles)) {
-                const Tile tile = a.d.tiles[unit.first_tile + t];
-                lt[t].base = a.d.bins + tile.base;
-                lt[t].stride = tile.stride;
-                lt[t].bins = tile.smem_bins;
-                lt[t].g_addr = sh_addr + 4 * slot;
-                slot += 2 * tile.smem_bins * tile.stride;
-                lt[t].active = s_tile_active[t];
-                any |= lt[t].active;
-            }
-        }
-    }
+    for (uint32_t t = 0; t < num_tiles; ++t) any |= s_lt[t].active;
 
     const uint32_t span = hi - lo;
     const uint32_t per_warp = static_cast<uint32_t>(ceil_div(ceil_div(span, kWarps), 32) * 32);
@@ -208,33 +198,37 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
         for (uint32_t p0 = w_lo; p0 < w_hi; p0 += 32) {
             const uint32_t row = next_row;
             const int32_t packed = next_packed;
-            // Every tile's bytes of this batch's rows in flight at once, and the next batch's positions.
-            uint32_t wd[kMaxUnitTiles][8];
-#pragma unroll
-            for (int t = 0; t < kMaxUnitTiles; ++t)
-                if (lt[t].active != 0) load_row(lt[t], row, wd[t]);
+            // One tile ahead: tile t + 1's bytes are in flight while tile t's atomics issue (the first tile's
+            // together with the next batch's positions).
+            uint32_t cur[8] = {}, nxt[8] = {};
+            if (s_lt[0].active != 0) load_row(s_lt[0], row, cur);
             position(p0 + 32 + lane, next_row, next_packed);
             // unpack (quantize.rs:140-143); a zero row adds nothing.
             const int32_t g = static_cast<int16_t>(static_cast<uint16_t>(static_cast<uint32_t>(packed)));
             const int32_t h = (packed - g) >> 16;
-            if (packed == 0) continue;
 #pragma unroll
             for (int t = 0; t < kMaxUnitTiles; ++t) {
-                if (lt[t].active == 0) continue;
-                switch (lt[t].stride) {
-                    case 32:
-                        add_row_bins<8>(lt[t], wd[t], g, h, lane);
-                        break;
-                    case 16:
-                        add_row_bins<4>(lt[t], wd[t], g, h, lane);
-                        break;
-                    case 8:
-                        add_row_bins<2>(lt[t], wd[t], g, h, lane);
-                        break;
-                    default:
-                        add_row_bins<1>(lt[t], wd[t], g, h, lane);
-                        break;
+                if (t >= static_cast<int>(num_tiles)) break;
+                if (t + 1 < static_cast<int>(num_tiles) && s_lt[t + 1].active != 0) load_row(s_lt[t + 1], row, nxt);
+                const LaneTile lt = s_lt[t];
+                if (packed != 0 && lt.active != 0) {
+                    switch (lt.stride) {
+                        case 32:
+                            add_row_bins<8>(lt, cur, g, h, lane);
+                            break;
+                        case 16:
+                            add_row_bins<4>(lt, cur, g, h, lane);
+                            break;
+                        case 8:
+                            add_row_bins<2>(lt, cur, g, h, lane);
+                            break;
+                        default:
+                            add_row_bins<1>(lt, cur, g, h, lane);
+                            break;
+                    }
                 }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
             }
         }
     }
@@ -245,6 +239,96 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
     const int4* src = reinterpret_cast<const int4*>(sh);
     for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) __stcg(slab + i, src[i]);
     __syncthreads();
+}
+
+// Jobs of at most kDirectRows rows skip the shared histograms: every (row, feature) adds straight into the output
+// with global reductions, so there is nothing to clear, flush or reduce, which for a small leaf costs more than
+// its few atomics. The output must hold zeros in the wanted features' bins.
+constexpr uint32_t kDirectRows = 4096;
+
+__device__ __forceinline__ void global_add_pair(int* p, int32_t g, int32_t h) {
+    asm volatile(
+        "red.global.add.s32 [%0], %1;\n\t"
+        "red.global.add.s32 [%0+4], %2;" ::"l"(p),
+        "r"(g), "r"(h)
+        : "memory");
+}
+
+// One loaded row of a tile of `W` words into the output: step i adds feature i ^ (lane mod S), as in add_row.
+// `off_lane` is the output bin offset of feature lane `lane` (-1: not wanted); rows with `add` false only take part
+// in the shuffles.
+template <int W>
+__device__ __forceinline__ void direct_row(int* out, const uint32_t (&wrow)[8], int32_t off_lane, int32_t g,
+                                           int32_t h, bool add, uint32_t lane) {
+    constexpr uint32_t kStride = 4 * W;
+    uint32_t w[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) w[j] = wrow[j];
+    const uint32_t k = lane & (kStride - 1);
+    xor_bytes<W>(w, k);
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(kStride); ++i) {
+        const int32_t off = __shfl_sync(0xffffffffu, off_lane, static_cast<int>(i ^ k));
+        const uint32_t bin = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        if (add && off >= 0) global_add_pair(out + 2 * (static_cast<uint32_t>(off) + bin), g, h);
+    }
+}
+
+// CTA `cta` of `ctas`'s share of a direct job: warp items are (32-position batch, tile), the tiles of one batch on
+// consecutive warps.
+inline __device__ void histogram_direct_cta(const HistArgs& a, const HistJob& job, uint32_t cta, uint32_t ctas) {
+    if (!job.active || job.count == 0) return;
+    const uint32_t lane = threadIdx.x & 31;
+    constexpr uint32_t kWarps = kHistThreads / 32;
+    const uint32_t gwarp = cta * kWarps + (threadIdx.x >> 5), gwarps = ctas * kWarps;
+    const uint32_t T = a.d.num_tiles;
+    const uint32_t items = static_cast<uint32_t>(ceil_div(job.count, 32)) * T;
+    const uint32_t* rows = a.rows[job.which & 1];
+    const int32_t* ordered = a.ordered[job.which & 1];
+    for (uint32_t item = gwarp; item < items; item += gwarps) {
+        const uint32_t t = item % T, p = (item / T) * 32 + lane;
+        uint32_t row = 0;
+        int32_t packed = 0;
+        if (p < job.count) {
+            const uint32_t pos = job.begin + p;
+            if (job.identity) {
+                row = pos;
+                packed = __ldg(a.packed + pos);
+            } else {
+                row = __ldcg(rows + pos);
+                packed = __ldcg(ordered + pos);
+            }
+        }
+        const int32_t f = a.d.lane_feature[t * kTileLanes + lane];
+        int32_t off = -1;
+        if (f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0))
+            off = static_cast<int32_t>(a.d.features[f].hist_offset);
+        if (__ballot_sync(0xffffffffu, off >= 0) == 0) continue;  // no wanted feature in the tile
+        const Tile tile = a.d.tiles[t];
+        LaneTile lt;
+        lt.base = a.d.bins + tile.base;
+        lt.stride = tile.stride;
+        uint32_t wd[8];
+        load_row(lt, row, wd);  // row 0 for positions past the job: in bounds, and adds nothing
+        // unpack (quantize.rs:140-143)
+        const int32_t g = static_cast<int16_t>(static_cast<uint16_t>(static_cast<uint32_t>(packed)));
+        const int32_t h = (packed - g) >> 16;
+        const bool add = packed != 0;
+        switch (tile.stride) {
+            case 32:
+                direct_row<8>(a.out, wd, off, g, h, add, lane);
+                break;
+            case 16:
+                direct_row<4>(a.out, wd, off, g, h, add, lane);
+                break;
+            case 8:
+                direct_row<2>(a.out, wd, off, g, h, add, lane);
+                break;
+            default:
+                direct_row<1>(a.out, wd, off, g, h, add, lane);
+                break;
+        }
+    }
 }
 
 // Gradient slot `i` over every unit: the sum of the slabs of the unit's CTAs that took part, written into the flat

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(kPartitionThreads) partition_flags_kernel(Trai
 }
 
 __global__ void __launch_bounds__(kPartitionThreads) partition_scatter_kernel(TrainArgs a) {
-    __shared__ uint32_t scan[kPartitionThreads + 64];
+    __shared__ uint32_t scan[2 * kPartitionThreads + 64];
     const Step st = *a.step;
     if (!st.active || st.root) return;
     const uint32_t total_left = partition_scatter_cta(a, st, blockIdx.x, gridDim.x, scan);

@@ -34,20 +34,36 @@ inline __device__ void partition_flags_cta(const TrainArgs& a, const Step& st, u
     const uint8_t* column = a.d.bins + tile.base + st.split_lane;
     const uint32_t* rows = a.rows[st.which & 1] + st.begin;
     uint32_t mine = 0;
-    for (uint32_t w = w_lo + warp; w < w_hi; w += warps) {
-        const uint32_t p = w * 32 + lane;
-        bool left = false;
-        if (p < st.count) {
-            const uint32_t row = __ldcg(rows + p);  // written by an earlier step, maybe in the same kernel
-            if (st.bag)  // quantize::in_bag (quantize.rs:147-149)
-                left = static_cast<double>(uniform01(st.bag_seed, 2u, st.bag_round, st.row_offset + row)) <
-                       st.bag_fraction;
-            else
-                left = bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row) * tile.stride));
+    // kBatch words per warp at a time: their row ids, then their bins, are in flight together.
+    constexpr int kBatch = 4;
+    for (uint32_t w0 = w_lo + warp; w0 < w_hi; w0 += kBatch * warps) {
+        uint32_t row[kBatch];
+        bool valid[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const uint32_t w = w0 + j * warps, p = w * 32 + lane;
+            valid[j] = w < w_hi && p < st.count;
+            row[j] = valid[j] ? __ldcg(rows + p) : 0u;  // written by an earlier step, maybe in the same kernel
         }
-        const uint32_t word = __ballot_sync(0xffffffffu, left);
-        if (lane == 0) a.flags[w] = word;
-        mine += __popc(word);
+        bool left[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            left[j] = false;
+            if (!valid[j]) continue;
+            if (st.bag)  // quantize::in_bag (quantize.rs:147-149)
+                left[j] = static_cast<double>(uniform01(st.bag_seed, 2u, st.bag_round, st.row_offset + row[j])) <
+                          st.bag_fraction;
+            else
+                left[j] = bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row[j]) * tile.stride));
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const uint32_t w = w0 + j * warps;
+            if (w >= w_hi) break;  // warp-uniform
+            const uint32_t word = __ballot_sync(0xffffffffu, left[j]);
+            if (lane == 0) a.flags[w] = word;
+            mine += __popc(word);
+        }
     }
     if (lane == 0) red[warp] = mine;
     __syncthreads();
@@ -59,17 +75,26 @@ inline __device__ void partition_flags_cta(const TrainArgs& a, const Step& st, u
     __syncthreads();
 }
 
-// Phase 2: the scatter. `scan` holds blockDim + 64 words of shared memory. Returns the total left count.
+// Phase 2: the scatter. `scan` holds 2 blockDim + 64 words of shared memory. Returns the total left count.
 inline __device__ uint32_t partition_scatter_cta(const TrainArgs& a, const Step& st, uint32_t cta, uint32_t ctas, uint32_t* scan) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    uint32_t* warp_sums = scan + blockDim.x;  // 32 words
-    // Lefts of the CTAs before this one, and over all of them (warp 0: G counts).
+    uint32_t* words = scan + blockDim.x;           // the round's flag words
+    uint32_t* warp_sums = scan + 2 * blockDim.x;   // 32 words
+    // Lefts of the CTAs before this one, and over all of them (warp 0: G counts, four per lane in flight).
     if (warp == 0) {
         uint32_t before = 0, total = 0;
-        for (uint32_t c = lane; c < ctas; c += 32) {
-            const uint32_t v = __ldcg(a.tile_left + c);
-            total += v;
-            if (c < cta) before += v;
+        for (uint32_t c0 = 0; c0 < ctas; c0 += 128) {
+            uint32_t v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t c = c0 + 32u * j + lane;
+                v[j] = c < ctas ? __ldcg(a.tile_left + c) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                total += v[j];
+                if (c0 + 32u * j + lane < cta) before += v[j];
+            }
         }
         for (int o = 16; o > 0; o >>= 1) {
             before += __shfl_xor_sync(0xffffffffu, before, o);
@@ -96,6 +121,7 @@ inline __device__ uint32_t partition_scatter_cta(const TrainArgs& a, const Step&
         // Exclusive scan of this round's word counts, one word per thread.
         const uint32_t w = r0 + threadIdx.x;
         const uint32_t word = w < w_hi ? __ldcg(a.flags + w) : 0u;
+        words[threadIdx.x] = word;
         const uint32_t c = __popc(word);
         uint32_t incl = c;
         for (int o = 1; o < 32; o <<= 1) {
@@ -118,18 +144,31 @@ inline __device__ uint32_t partition_scatter_cta(const TrainArgs& a, const Step&
         scan[threadIdx.x] = carry + warp_sums[warp] + incl - c;  // lefts before word w over the whole parent
         const uint32_t round_total = *round_sum;
         __syncthreads();
-        // Positions of the round's words, a warp per word: coalesced row-id and gradient moves.
+        // Positions of the round's words, a warp per word, four words per warp in flight: coalesced row-id and
+        // gradient moves.
         const uint32_t round_words = min(blockDim.x, w_hi - r0);
-        for (uint32_t k = warp; k < round_words; k += warps) {
-            const uint32_t ww = r0 + k;
-            const uint32_t p = ww * 32 + lane;
-            if (p >= st.count) continue;
-            const uint32_t bits = __ldcg(a.flags + ww);
-            const bool left = (bits >> lane) & 1u;
-            const uint32_t lefts_before = scan[k] + __popc(bits & ((1u << lane) - 1u));
-            const uint32_t target = left ? lefts_before : total_left + (p - lefts_before);
-            rows_out[target] = __ldcg(rows_in + p);
-            gh_out[target] = __ldcg(gh_in + p);
+        constexpr int kBatch = 4;
+        for (uint32_t k0 = warp; k0 < round_words; k0 += kBatch * warps) {
+            uint32_t rid[kBatch];
+            int32_t gh[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const uint32_t k = k0 + j * warps, p = (r0 + k) * 32 + lane;
+                const bool ok = k < round_words && p < st.count;
+                rid[j] = ok ? __ldcg(rows_in + p) : 0u;
+                gh[j] = ok ? __ldcg(gh_in + p) : 0;
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const uint32_t k = k0 + j * warps, p = (r0 + k) * 32 + lane;
+                if (k >= round_words || p >= st.count) continue;
+                const uint32_t bits = words[k];
+                const bool left = (bits >> lane) & 1u;
+                const uint32_t lefts_before = scan[k] + __popc(bits & ((1u << lane) - 1u));
+                const uint32_t target = left ? lefts_before : total_left + (p - lefts_before);
+                rows_out[target] = rid[j];
+                gh_out[target] = gh[j];
+            }
         }
         __syncthreads();
         carry += round_total;

@@ -258,15 +258,19 @@ __device__ FeatureCandidate scan_feature(const int2* hist, const DevFeature& f, 
     return o;
 }
 
-// Reads a candidate another CTA wrote, past this SM's L1 (the last CTA of a launch reads every CTA's results).
-__device__ FeatureCandidate load_candidate(const FeatureCandidate* p) {
-    FeatureCandidate c;
+// Reads a record another CTA of the same launch may have written, past this SM's L1 (which is not coherent with
+// other SMs' writes): a candidate, a leaf record.
+template <class T>
+__device__ __forceinline__ T load_cg(const T* p) {
+    static_assert(sizeof(T) % 8 == 0 && alignof(T) >= 8, "read as 64-bit words");
+    T c;
     const unsigned long long* s = reinterpret_cast<const unsigned long long*>(p);
     unsigned long long* d = reinterpret_cast<unsigned long long*>(&c);
 #pragma unroll
-    for (int i = 0; i < static_cast<int>(sizeof(FeatureCandidate) / 8); ++i) d[i] = __ldcg(s + i);
+    for (int i = 0; i < static_cast<int>(sizeof(T) / 8); ++i) d[i] = __ldcg(s + i);
     return c;
 }
+__device__ __forceinline__ FeatureCandidate load_candidate(const FeatureCandidate* p) { return load_cg(p); }
 
 // better (split.rs:866-873)
 __device__ __forceinline__ bool better(const FeatureCandidate& a, const FeatureCandidate& b) {
@@ -327,11 +331,16 @@ __device__ void root_units(const TrainArgs& a, double& ug, double& uh) {
 // Tree::split (tree.rs:143-177) for a numerical split; returns the new leaf.
 __device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_info& info, const DevFeature& f,
                               int64_t left_count, int64_t right_count, double hs, double min_gain_to_split) {
-    const int32_t nl = *t.num_leaves;
+    // Every load before the first store, so they are in flight together; through L2, since the CTA that split
+    // earlier leaves may have been another one.
+    const int32_t nl = __ldcg(t.num_leaves);
+    const int32_t parent = __ldcg(t.leaf_parent + leaf);
+    const double old_weight = __ldcg(t.leaf_weight + leaf), old_value = __ldcg(t.leaf_value + leaf);
+    const int32_t depth = __ldcg(t.leaf_depth + leaf) + 1;
+    const bool parent_left = parent >= 0 && __ldcg(t.left_child + parent) == ~leaf;
     const int32_t node = nl - 1;
-    const int32_t parent = t.leaf_parent[leaf];
     if (parent >= 0) {
-        if (t.left_child[parent] == ~leaf)
+        if (parent_left)
             t.left_child[parent] = node;
         else
             t.right_child[parent] = node;
@@ -344,8 +353,8 @@ __device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_in
     t.decision_type[node] = dt;
     t.left_child[node] = ~leaf;
     t.right_child[node] = ~nl;
-    t.internal_weight[node] = t.leaf_weight[leaf];
-    t.internal_value[node] = t.leaf_value[leaf];
+    t.internal_weight[node] = old_weight;
+    t.internal_value[node] = old_value;
     t.internal_count[node] = left_count + right_count;
     t.leaf_value[leaf] = nan_to_zero(info.left_output);
     t.leaf_weight[leaf] = dmul(info.left_hess, hs);
@@ -355,7 +364,6 @@ __device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_in
     t.leaf_count[nl] = right_count;
     t.leaf_parent[leaf] = node;
     t.leaf_parent[nl] = node;
-    const int32_t depth = t.leaf_depth[leaf] + 1;
     t.leaf_depth[leaf] = depth;
     t.leaf_depth[nl] = depth;
     *t.num_leaves = nl + 1;
@@ -412,192 +420,314 @@ __device__ void search_context_cta(const TrainArgs& a, const Step& st, SearchCtx
     __syncthreads();
 }
 
-// One warp, one feature: the built child's bins from staging, the other's as parent - built, written into both
-// leaves' slots (learner.rs:365-367), then each child's scan into `cands` ([child][feature]). `buf` is the warp's
-// 2 x kMaxBins int2 of shared memory.
-__device__ void search_feature(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t f, int2 (*buf)[kMaxBins]) {
+// Work items of a step's search: one per (child, feature), item = child * F + feature; the root has one child.
+__device__ __forceinline__ uint32_t search_items(const TrainArgs& a, const Step& st) {
+    return (st.root ? 1u : 2u) * a.num_features;
+}
+
+// One warp, one item (child `ch`, feature `f`): the child's bins into the warp's `buf` (kMaxBins int2 of shared
+// memory), its scan into `cands[ch * F + f]`. Child 0 is the built one, straight from staging; child 1 is the
+// sibling, parent - built (learner.rs:365-367), and its warp also writes both children's slots (it alone reads
+// the parent's slot, which the built child may take over), or, at the root, child 0's warp writes the root's slot.
+// Every lane loads its bins (lane, lane + 32, ...) before using any, so a warp waits on memory once.
+__device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t item, int2* buf) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t F = a.num_features;
+    const uint32_t f = item % F, ch = item / F;
     FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
     const DevFeature feat = a.d.features[f];
-    FeatureCandidate none{};
-    none.feature = static_cast<int32_t>(f);
     if (!__ldcg(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
         if (lane == 0) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
             cands[f] = none;
             cands[F + f] = none;
         }
         return;
     }
-    const int children = st.root ? 1 : 2;
     const size_t slot_len = 2 * static_cast<size_t>(a.total_bins);
     const size_t off = 2 * static_cast<size_t>(feat.hist_offset);
-    int* built_slot = a.slots + static_cast<size_t>(s.child[0]) * slot_len + off;
-    int* other_slot = children == 2 ? a.slots + static_cast<size_t>(s.child[1]) * slot_len + off : nullptr;
-    const int* parent_slot = a.slots + static_cast<size_t>(st.root ? 0 : st.leaf) * slot_len + off;
-    for (uint32_t b = lane; b < feat.num_bins; b += 32) {
-        const int sg = __ldcg(a.staging + off + 2 * b), shh = __ldcg(a.staging + off + 2 * b + 1);
-        buf[0][b] = make_int2(sg, shh);
-        if (children == 2) {
-            const int pg = __ldcg(parent_slot + 2 * b), ph = __ldcg(parent_slot + 2 * b + 1);
-            buf[1][b] = make_int2(pg - sg, ph - shh);
+    const int2* staged = reinterpret_cast<const int2*>(a.staging + off);
+    int2 built[kPerLane], other[kPerLane];
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+        const uint32_t b = lane + 32u * k;
+        built[k] = b < feat.num_bins ? __ldcg(staged + b) : make_int2(0, 0);
+    }
+    if (ch == 1) {
+        const int2* parent = reinterpret_cast<const int2*>(a.slots + static_cast<size_t>(st.leaf) * slot_len + off);
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const uint32_t b = lane + 32u * k;
+            other[k] = b < feat.num_bins ? __ldcg(parent + b) : make_int2(0, 0);
+        }
+        int2* built_slot = reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[0]) * slot_len + off);
+        int2* other_slot = reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[1]) * slot_len + off);
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const uint32_t b = lane + 32u * k;
+            other[k] = make_int2(other[k].x - built[k].x, other[k].y - built[k].y);
+            if (b < feat.num_bins) {
+                __stcg(built_slot + b, built[k]);
+                __stcg(other_slot + b, other[k]);
+                buf[b] = other[k];
+            }
+        }
+    } else {
+        int2* slot = st.root ? reinterpret_cast<int2*>(a.slots + off) : nullptr;
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const uint32_t b = lane + 32u * k;
+            if (b < feat.num_bins) {
+                if (slot) __stcg(slot + b, built[k]);
+                buf[b] = built[k];
+            }
         }
     }
     __syncwarp();
-    // Slot writes after every lane has read the parent (the built child may reuse the parent's slot).
-    for (uint32_t b = lane; b < feat.num_bins; b += 32) {
-        __stcg(reinterpret_cast<int2*>(built_slot) + b, buf[0][b]);
-        if (children == 2) __stcg(reinterpret_cast<int2*>(other_slot) + b, buf[1][b]);
+    const FeatureCandidate c = scan_feature(buf, feat, static_cast<int>(f), s.ctx[ch], a.cfg);
+    if (lane == 0) {
+        cands[static_cast<size_t>(ch) * F + f] = c;
+        if (st.root) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
+            cands[F + f] = none;
+        }
     }
-    for (int ch = 0; ch < children; ++ch) {
-        const FeatureCandidate c = scan_feature(buf[ch], feat, static_cast<int>(f), s.ctx[ch], a.cfg);
-        if (lane == 0) cands[static_cast<size_t>(ch) * F + f] = c;
-    }
-    if (children == 1 && lane == 0) cands[F + f] = none;
     __syncwarp();
 }
 
-// After every feature's candidates are written: the split applied to the tree and the leaves, each child's best
-// split, and the next step (learner.rs:158-163, 249-352, 418-429). One CTA of at least 64 threads.
+// The best candidate of child `ch` over every feature (one warp; `better` is a total order, so the reduction order
+// does not matter), with the child's splittable flags written on the way.
+__device__ FeatureCandidate best_candidate(const TrainArgs& a, const SearchCtx& s, int ch) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t F = a.num_features;
+    const FeatureCandidate* cands = static_cast<const FeatureCandidate*>(a.candidates) + static_cast<size_t>(ch) * F;
+    uint8_t* splittable = a.splittable + static_cast<size_t>(s.child[ch]) * F;
+    FeatureCandidate best{};
+    best.found = 0;
+    // Four candidates per lane in flight at a time.
+    for (uint32_t f0 = 0; f0 < F; f0 += 128) {
+        FeatureCandidate c[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t f = f0 + 32u * j + lane;
+            if (f < F) c[j] = load_candidate(cands + f);
+            else c[j].found = 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t f = f0 + 32u * j + lane;
+            if (f < F) {
+                splittable[f] = static_cast<uint8_t>(c[j].splittable);
+                if (better(c[j], best)) best = c[j];
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        FeatureCandidate other;
+        const int src = lane ^ o;
+        other.found = __shfl_sync(0xffffffffu, best.found, src);
+        other.splittable = 0;
+        other.feature = __shfl_sync(0xffffffffu, best.feature, src);
+        other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
+        other.gain = __shfl_sync(0xffffffffu, best.gain, src);
+        other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
+        other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
+        other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
+        other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
+        other.left_count = shfl_i64(best.left_count, src);
+        other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
+        other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
+        if (better(other, best)) best = other;
+    }
+    return best;
+}
+
+// (gain, leaf) of the better of two leaves in best_leaf's order (learner.rs:418-429): the higher gain, on equal
+// gains the lower index; -1 is no leaf.
+__device__ __forceinline__ void prefer_leaf(double& gain, int32_t& leaf, double og, int32_t ol) {
+    if (ol >= 0 && (leaf < 0 || og > gain || (og == gain && ol < leaf))) {
+        leaf = ol;
+        gain = og;
+    }
+}
+
+// bin_split (learner.rs:432-452): bins 0..=threshold go left, and the NaN bin when missing values go left.
+__device__ __forceinline__ void left_bins_of(const sb2_split_info& info, const DevFeature& f, uint32_t (&bins)[8]) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const int64_t first = 32 * w, t = static_cast<int64_t>(info.threshold);
+        bins[w] = t >= first + 31 ? 0xFFFFFFFFu : t >= first ? (0xFFFFFFFFu >> (31 - (t - first))) : 0u;
+    }
+    if (info.default_left && f.nan_bin) bins[(f.num_bins - 1) >> 5] |= 1u << ((f.num_bins - 1) & 31);
+}
+
+// After every item's candidate is written: the split applied to the tree and the leaves, each child's best split,
+// and the next step (learner.rs:158-163, 249-352, 418-429). One CTA of at least 128 threads. The independent parts
+// run side by side so the CTA waits on memory about twice: warp 0 applies the split, warps 1-2 reduce the
+// children's candidates, warp 3 finds the best of the other leaves; then warp 0 joins them and writes the step.
 __device__ void search_finish(const TrainArgs& a, const Step& st, const SearchCtx& s) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t F = a.num_features;
     const IterState& it = *a.iter;
-    const double hs = it.spec.hess_scale;
-    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
     DevLeaf* leaves = a.leaves;
-    if (threadIdx.x == 0) {
-        if (st.root) {
-            DevLeaf& l = leaves[0];
-            l.units_grad = s.ctx[0].units_grad;
-            l.units_hess = s.ctx[0].units_hess;
-            l.count_global = it.root_count;
-            l.has_hist = s.searched;
-            l.has_best = 0;
-        } else {
-            if (s.left_global <= 0 || s.right_global <= 0) {
-                a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
-                a.iter->error_info = st.leaf;
-            }
-            const DevLeaf parent = leaves[st.leaf];
-            const DevFeature f = a.d.features[st.info.feature];
-            const int32_t nl =
-                tree_split(a.tree, st.leaf, st.info, f, s.left_global, s.right_global, hs, a.cfg.min_gain_to_split);
-            if (nl != st.new_leaf) {
-                a.iter->error = 2;
-                a.iter->error_info = nl;
-            }
-            DevLeaf l{}, r{};
-            l.begin = parent.begin;
-            l.count = st.local_left;
-            r.begin = parent.begin + st.local_left;
-            r.count = parent.count - st.local_left;
-            l.which = r.which = parent.which ^ 1u;
-            l.depth = r.depth = parent.depth + 1;
-            l.units_grad = st.info.left_grad;
-            l.units_hess = st.info.left_hess;
-            l.count_global = s.left_global;
-            r.units_grad = st.info.right_grad;
-            r.units_hess = st.info.right_hess;
-            r.count_global = s.right_global;
-            l.has_hist = r.has_hist = s.searched;
-            leaves[st.leaf] = l;
-            leaves[nl] = r;
-        }
-    }
-    __syncthreads();
-    if (s.searched && warp < (st.root ? 1u : 2u)) {
-        // Best candidate of child `warp` over every feature.
-        FeatureCandidate best{};
-        best.found = 0;
-        for (uint32_t f = lane; f < F; f += 32) {
-            const FeatureCandidate c = load_candidate(cands + static_cast<size_t>(warp) * F + f);
-            a.splittable[static_cast<size_t>(s.child[warp]) * F + f] = static_cast<uint8_t>(c.splittable);
-            if (better(c, best)) best = c;
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            FeatureCandidate other;
-            const int src = lane ^ o;
-            other.found = __shfl_sync(0xffffffffu, best.found, src);
-            other.splittable = 0;
-            other.feature = __shfl_sync(0xffffffffu, best.feature, src);
-            other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
-            other.gain = __shfl_sync(0xffffffffu, best.gain, src);
-            other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
-            other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
-            other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
-            other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
-            other.left_count = shfl_i64(best.left_count, src);
-            other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
-            other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
-            if (better(other, best)) best = other;
-        }
-        if (lane == 0) {
-            DevLeaf& l = leaves[s.child[warp]];
-            if (best.found && s.ctx[warp].valid) {
-                l.best = finish(s.ctx[warp], best, a.cfg);
-                l.has_best = 1;
-            } else {
-                l.has_best = 0;
-            }
-        }
-    }
-    __syncthreads();
+    const int children = st.root ? 1 : 2;
+    __shared__ DevLeaf s_child[2];           // the children's new leaf records (warp 0)
+    __shared__ sb2_split_info s_best[2];     // their best splits (warps 1-2)
+    __shared__ int32_t s_has_best[2];
+    __shared__ double s_other_gain;          // best of the leaves that are not children (warp 3)
+    __shared__ int32_t s_other_leaf;
     if (warp == 0) {
-        // best_leaf (learner.rs:418-429): the first maximum gain over leaves with a split; continue when positive.
-        const int32_t num_leaves = *a.tree.num_leaves;
-        double best_gain = -INFINITY;
-        int32_t best_leaf = -1;
-        for (int32_t l = lane; l < num_leaves; l += 32) {
-            if (leaves[l].has_best) {
-                const double g = leaves[l].best.gain;
-                if (best_leaf < 0 || g > best_gain) {
-                    best_leaf = l;
-                    best_gain = g;
+        if (lane == 0) {
+            const double hs = it.spec.hess_scale;
+            if (st.root) {
+                DevLeaf l = load_cg(leaves);
+                l.units_grad = s.ctx[0].units_grad;
+                l.units_hess = s.ctx[0].units_hess;
+                l.count_global = it.root_count;
+                l.has_hist = s.searched;
+                l.has_best = 0;
+                s_child[0] = l;
+            } else {
+                if (s.left_global <= 0 || s.right_global <= 0) {
+                    a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
+                    a.iter->error_info = st.leaf;
                 }
+                const DevLeaf parent = load_cg(leaves + st.leaf);
+                const DevFeature f = a.d.features[st.info.feature];
+                const int32_t nl = tree_split(a.tree, st.leaf, st.info, f, s.left_global, s.right_global, hs,
+                                              a.cfg.min_gain_to_split);
+                if (nl != st.new_leaf) {
+                    a.iter->error = 2;
+                    a.iter->error_info = nl;
+                }
+                DevLeaf l{}, r{};
+                l.begin = parent.begin;
+                l.count = st.local_left;
+                r.begin = parent.begin + st.local_left;
+                r.count = parent.count - st.local_left;
+                l.which = r.which = parent.which ^ 1u;
+                l.depth = r.depth = parent.depth + 1;
+                l.units_grad = st.info.left_grad;
+                l.units_hess = st.info.left_hess;
+                l.count_global = s.left_global;
+                r.units_grad = st.info.right_grad;
+                r.units_hess = st.info.right_hess;
+                r.count_global = s.right_global;
+                l.has_hist = r.has_hist = s.searched;
+                // child 0 is the built child: the left one (index st.leaf) when built_left
+                s_child[st.built_left ? 0 : 1] = l;
+                s_child[st.built_left ? 1 : 0] = r;
             }
         }
-        for (int o = 16; o > 0; o >>= 1) {
-            const double og = __shfl_xor_sync(0xffffffffu, best_gain, o);
-            const int32_t ol = __shfl_xor_sync(0xffffffffu, best_leaf, o);
-            if (ol >= 0 && (best_leaf < 0 || og > best_gain || (og == best_gain && ol < best_leaf))) {
-                best_leaf = ol;
-                best_gain = og;
-            }
-        }
-        Step* next = a.step;
-        if (best_leaf < 0 || !(best_gain > 0.0) || num_leaves >= a.max_leaves) {
-            if (lane == 0) next->active = 0;
-        } else {
-            const DevLeaf leaf = leaves[best_leaf];
-            const sb2_split_info info = leaf.best;
-            const DevFeature f = a.d.features[info.feature];
-            // Features the children evaluate: the tree's mask and the parent's splittable ones (learner.rs:278-284).
-            const uint8_t* mask = a.masks + static_cast<size_t>(it.iteration) * F;
-            for (uint32_t k = lane; k < F; k += 32)
-                a.evaluate[k] = static_cast<uint8_t>(mask[k] && a.splittable[static_cast<size_t>(best_leaf) * F + k]);
+    } else if (warp <= 2) {
+        const int ch = static_cast<int>(warp) - 1;
+        if (ch < children) {
+            FeatureCandidate best{};
+            best.found = 0;
+            if (s.searched) best = best_candidate(a, s, ch);
             if (lane == 0) {
-                leaves[best_leaf].has_best = 0;
-                Step n{};
-                n.active = 1;
-                n.root = 0;
-                n.leaf = best_leaf;
-                n.new_leaf = num_leaves;
-                n.may_search = leaf.has_hist && num_leaves + 1 < a.max_leaves && depth_allows(a, leaf.depth + 1);
-                n.built_left = info.left_count <= info.right_count;
-                n.begin = leaf.begin;
-                n.count = leaf.count;
-                n.which = leaf.which;
-                n.split_tile = static_cast<uint32_t>(f.tile);
-                n.split_lane = static_cast<uint32_t>(f.lane);
-                // bin_split (learner.rs:432-452)
-                for (uint32_t b = 0; b <= info.threshold && b < 256; ++b) n.left_bins[b >> 5] |= 1u << (b & 31);
-                if (info.default_left && f.nan_bin) n.left_bins[(f.num_bins - 1) >> 5] |= 1u << ((f.num_bins - 1) & 31);
-                n.parent_count = leaf.count_global;
-                n.info = info;
-                *next = n;
+                const bool has = best.found && s.ctx[ch].valid;
+                s_has_best[ch] = has;
+                s_best[ch] = has ? finish(s.ctx[ch], best, a.cfg) : sb2_split_info{};
             }
         }
+    } else if (warp == 3) {
+        // Leaves that existed before this step, other than the one being split.
+        const int32_t before = st.root ? 0 : st.new_leaf;
+        double gain = -INFINITY;
+        int32_t leaf = -1;
+        for (int32_t l0 = 0; l0 < before; l0 += 128) {
+            int32_t has[4];
+            double g[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int32_t l = l0 + 32 * j + static_cast<int32_t>(lane);
+                has[j] = l < before && l != st.leaf ? __ldcg(&leaves[l].has_best) : 0;
+                g[j] = has[j] ? __ldcg(&leaves[l].best.gain) : 0.0;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (has[j]) prefer_leaf(gain, leaf, g[j], l0 + 32 * j + static_cast<int32_t>(lane));
+        }
+        for (int o = 16; o > 0; o >>= 1)
+            prefer_leaf(gain, leaf, __shfl_xor_sync(0xffffffffu, gain, o), __shfl_xor_sync(0xffffffffu, leaf, o));
+        if (lane == 0) {
+            s_other_gain = gain;
+            s_other_leaf = leaf;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    // Join: the children's records get their best splits and go out, then the best leaf over children and others.
+    if (lane < static_cast<uint32_t>(children)) {
+        s_child[lane].has_best = s_has_best[lane];
+        if (s_has_best[lane]) s_child[lane].best = s_best[lane];
+    }
+    __syncwarp();
+    double gain = s_other_gain;
+    int32_t best_leaf = s_other_leaf;
+    for (int ch = 0; ch < children; ++ch) {
+        const DevLeaf& c = s_child[ch];
+        if (c.has_best) prefer_leaf(gain, best_leaf, c.best.gain, s.child[ch]);
+    }
+    const int32_t num_leaves = st.root ? 1 : st.new_leaf + 1;
+    const bool go = best_leaf >= 0 && gain > 0.0 && num_leaves < a.max_leaves;
+    const int chosen = !go ? -1 : best_leaf == s.child[0] ? 0 : (children == 2 && best_leaf == s.child[1]) ? 1 : -1;
+    if (lane < static_cast<uint32_t>(children)) {
+        DevLeaf c = s_child[lane];
+        if (static_cast<int>(lane) == chosen) c.has_best = 0;  // it is split next
+        leaves[s.child[lane]] = c;
+    }
+    Step* next = a.step;
+    if (!go) {
+        if (lane == 0) next->active = 0;
+        return;
+    }
+    DevLeaf leaf;
+    if (chosen >= 0) {
+        leaf = s_child[chosen];
+    } else {
+        leaf = load_cg(leaves + best_leaf);
+        if (lane == 0) leaves[best_leaf].has_best = 0;
+    }
+    const sb2_split_info info = leaf.best;
+    const DevFeature f = a.d.features[info.feature];
+    // Features the children evaluate: the tree's mask and the parent's splittable ones (learner.rs:278-284).
+    const uint8_t* mask = a.masks + static_cast<size_t>(it.iteration) * F;
+    const uint8_t* split_ok = a.splittable + static_cast<size_t>(best_leaf) * F;
+    for (uint32_t k0 = 0; k0 < F; k0 += 128) {
+        uint8_t m[4], o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t k = k0 + 32u * j + lane;
+            m[j] = k < F ? mask[k] : 0;
+            o[j] = k < F ? __ldcg(split_ok + k) : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t k = k0 + 32u * j + lane;
+            if (k < F) a.evaluate[k] = static_cast<uint8_t>(m[j] && o[j]);
+        }
+    }
+    if (lane == 0) {
+        Step n{};
+        n.active = 1;
+        n.root = 0;
+        n.leaf = best_leaf;
+        n.new_leaf = num_leaves;
+        n.may_search = leaf.has_hist && num_leaves + 1 < a.max_leaves && depth_allows(a, leaf.depth + 1);
+        n.built_left = info.left_count <= info.right_count;
+        n.begin = leaf.begin;
+        n.count = leaf.count;
+        n.which = leaf.which;
+        n.split_tile = static_cast<uint32_t>(f.tile);
+        n.split_lane = static_cast<uint32_t>(f.lane);
+        left_bins_of(info, f, n.left_bins);
+        n.parent_count = leaf.count_global;
+        n.info = info;
+        *next = n;
     }
 }
 

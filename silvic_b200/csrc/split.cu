@@ -10,7 +10,7 @@ namespace {
 
 // Every feature of the step's children, a warp each; the last CTA to finish applies the split and chooses the next.
 __global__ void __launch_bounds__(kSearchThreads) search_kernel(TrainArgs a) {
-    __shared__ int2 sh_hist[kSearchThreads / 32][2][kMaxBins];
+    __shared__ int2 sh_hist[kSearchThreads / 32][kMaxBins];
     __shared__ bool s_last;
     const Step st = *a.step;
     if (!st.active) return;
@@ -18,9 +18,9 @@ __global__ void __launch_bounds__(kSearchThreads) search_kernel(TrainArgs a) {
     __shared__ SearchCtx s;
     search_context_cta(a, st, &s);
     if (s.searched)
-        for (uint32_t f = blockIdx.x * (kSearchThreads / 32) + warp; f < a.num_features;
-             f += gridDim.x * (kSearchThreads / 32))
-            search_feature(a, st, s, f, sh_hist[warp]);
+        for (uint32_t item = blockIdx.x * (kSearchThreads / 32) + warp; item < search_items(a, st);
+             item += gridDim.x * (kSearchThreads / 32))
+            search_item(a, st, s, item, sh_hist[warp]);
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) s_last = atomicAdd(a.done_counter, 1u) == gridDim.x - 1;

@@ -136,10 +136,15 @@ constexpr int kSearchThreads = 256;   // 8 warps, one feature each
 int grow_threads();
 cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: partition flags,
-// scatter, histogram, slab reduction, search, the barrier that runs the finish, the other barriers.
+// scatter, histogram, slab reduction, search, the barrier that runs the finish, the other barriers. With
+// `trace_steps` > 0 it is followed by one row of kStepTrace values per step (up to trace_steps): the same phase
+// times of that step, then the rows of its histogram job, whether the job went straight to the output (1) or
+// through the shared histograms (0), and the rows of the leaf it split.
 constexpr int kGrowPhases = 7;
+constexpr int kStepTrace = kGrowPhases + 3;
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
-                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns);
+                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns,
+                             int trace_steps);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

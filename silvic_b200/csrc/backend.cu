@@ -95,7 +95,9 @@ struct sb2_backend {
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, counter, maxima, misc;
     DeviceBuffer slabs;        // histogram scratch: one slab per histogram CTA
     uint32_t slab_ints = 0;    // ints per slab
-    uint32_t hist_slots = 0;   // gradient slots over every unit
+    DeviceBuffer d_quads;      // the slab reduction's QuadMeta table
+    uint32_t num_quads = 0;
+    uint32_t quad_split = 1;   // threads per quad
     std::vector<uint8_t> api_used;
     bool api_used_all = true;
 
@@ -183,13 +185,16 @@ struct sb2_backend {
         h.out = out;
         h.slabs = slabs.as<int>();
         h.slab_ints = slab_ints;
+        h.num_quads = num_quads;
+        h.quads = d_quads.as<QuadMeta>();
+        h.quad_split = quad_split;
         return h;
     }
 
     // The histogram operation: per-CTA histograms into the slabs, then their sum into `h.out`.
     void run_hist(const HistArgs& h, cudaStream_t s) const {
         launch_histogram(h, hist_grid, hist_smem, s);
-        launch_histogram_reduce(h, hist_slots, s);
+        launch_histogram_reduce(h, s);
     }
 
     int row_grid() const { return sms * 8; }
@@ -585,11 +590,42 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * kMaxPartitionCtas));
     SB2_CUDA(b, b->staging.alloc(sizeof(int) * (2ull * b->total_bins + 2)));
     b->slab_ints = 0;
-    b->hist_slots = 0;
-    for (const Unit& u : b->units) {
-        b->slab_ints = std::max(b->slab_ints, 2 * u.slots);
-        b->hist_slots += u.slots;
+    for (const Unit& u : b->units) b->slab_ints = std::max(b->slab_ints, 2 * u.slots);
+    // The reduction's quads: per unit, per tile, four consecutive slots (one bin, lanes l .. l + 3).
+    std::vector<QuadMeta> quads;
+    for (uint32_t ui = 0; ui < b->units.size(); ++ui) {
+        const Unit& u = b->units[ui];
+        uint32_t off = 0;
+        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
+            const Tile& tile = b->tiles[t];
+            const uint32_t n = tile.smem_bins * tile.stride;
+            for (uint32_t s = 0; s < n; s += 4) {
+                QuadMeta m{};
+                m.unit = ui;
+                m.g_off = off + s;
+                m.h_off = off + n + s;
+                const uint32_t bin = s / tile.stride, lane0 = s % tile.stride;
+                for (uint32_t i = 0; i < 4; ++i) {
+                    const int32_t f = lane_feature[t * kTileLanes + lane0 + i];
+                    m.out[i] = f >= 0 && bin < b->dev_features[f].num_bins
+                                   ? static_cast<int32_t>(b->dev_features[f].hist_offset + bin)
+                                   : -1;
+                }
+                quads.push_back(m);
+            }
+            off += 2 * n;
+        }
     }
+    b->num_quads = static_cast<uint32_t>(quads.size());
+    // Threads per quad: as many as keep every thread of one histogram grid busy, up to a warp.
+    const uint64_t grid_threads = static_cast<uint64_t>(b->hist_grid) * histogram_threads();
+    b->quad_split = 1;
+    while (b->quad_split < 32 && static_cast<uint64_t>(b->quad_split) * 2 * b->num_quads <= grid_threads)
+        b->quad_split *= 2;
+    SB2_CUDA(b, b->d_quads.alloc(sizeof(QuadMeta) * std::max<size_t>(quads.size(), 1)));
+    if (!quads.empty())
+        SB2_CUDA(b, cudaMemcpyAsync(b->d_quads.ptr, quads.data(), sizeof(QuadMeta) * quads.size(),
+                                    cudaMemcpyHostToDevice, b->stream));
     SB2_CUDA(b, b->slabs.alloc(sizeof(int) * static_cast<size_t>(b->hist_grid) * std::max<uint32_t>(b->slab_ints, 4)));
     SB2_CUDA(b, b->hist_job.alloc(sizeof(HistJob)));
     SB2_CUDA(b, b->step.alloc(sizeof(Step)));
@@ -1095,7 +1131,7 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
     if (b->persistent()) {
         // One launch grows the whole tree (grow.cu).
         SB2_TRY(op(kOpTree, [&] {
-            return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_slots, b->hist_grid,
+            return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
                                             b->grow_smem, s,
                                             timer ? b->phase_ns.as<unsigned long long>() : nullptr,
                                             timer ? max_leaves : 0),

@@ -28,9 +28,7 @@ constexpr int kGrowThreads = kHistThreads;                // 512: the histogram 
 struct GrowArgs {
     TrainArgs t;
     HistArgs h;
-    unsigned int* barrier;        // [arrived, generation]
-    uint32_t hist_slots;
-    uint32_t pad_;
+    unsigned int* barrier;        // arrivals at grid barriers so far (zeroed before the launch)
     unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
     int pad2_;
@@ -89,48 +87,62 @@ __device__ __forceinline__ void broadcast_cg(const T* p, T* shared_copy) {
 
 __device__ __forceinline__ bool failed(const GrowArgs& g) { return __ldcg(&g.t.iter->error) != 0; }
 
-// Grid barrier; the last CTA to arrive runs `tail(...)` (whole CTA) before releasing the others. Returns false
-// once any CTA has recorded an error.
-template <class Tail>
-__device__ bool grid_barrier(const GrowArgs& g, Tail tail) {
-    __shared__ unsigned int s_last, s_gen;
-    __threadfence();
-    __syncthreads();
+// Grid barriers count arrivals on one word that only grows during the launch (the host zeroes it before): barrier
+// k of the launch is passed once the word reaches the running target, which every CTA advances identically (by
+// the grid size, plus one for a barrier with a tail). A plain barrier is released by its last arrival itself, so
+// it costs one atomic and the poll that sees it. In a barrier with a tail, the last CTA to arrive runs `tail()`
+// (whole CTA) and then adds the one that releases the others. Returns false once any CTA has recorded an error.
+template <bool kHasTail, class Tail>
+__device__ bool grid_barrier(const GrowArgs& g, unsigned int& target, Tail tail) {
+    __shared__ unsigned int s_last;
+    __shared__ int s_failed;
+    const unsigned int arrived_all = target + gridDim.x;
+    target = arrived_all + (kHasTail ? 1u : 0u);
+    __syncthreads();  // the CTA's work (and its writes) are done
     if (threadIdx.x == 0) {
-        volatile unsigned int* gen = g.barrier + 1;
-        s_gen = *gen;
         __threadfence();
-        s_last = atomicAdd(g.barrier, 1u) == gridDim.x - 1;
+        const unsigned int before = atomicAdd(g.barrier, 1u);
+        s_last = kHasTail && before == arrived_all - 1;
     }
     __syncthreads();
-    if (s_last) {
+    if (kHasTail && s_last) {
         __threadfence();
         tail();
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) {
-            g.barrier[0] = 0;
-            __threadfence();
-            atomicAdd(g.barrier + 1, 1u);
+            atomicAdd(g.barrier, 1u);
+            s_failed = failed(g);
         }
     } else if (threadIdx.x == 0) {
-        volatile unsigned int* gen = g.barrier + 1;
+        volatile unsigned int* count = g.barrier;
+        volatile int* error = &g.t.iter->error;
         unsigned long long spins = 0;
-        while (*gen == s_gen) {
+        int failed_now = 0;
+        // `count - target` as a signed difference: the count never runs more than one barrier ahead of a waiter.
+        // The error word is polled alongside: a CTA that gave up waiting stops the others without their timing out.
+        while (true) {
+            const unsigned int c = *count;
+            failed_now = *error;
+            if (failed_now != 0 || static_cast<int>(c - target) >= 0) break;
             if (++spins > kBarrierSpins) {
                 atomicCAS(&g.t.iter->error, 0, 3);  // a CTA never arrived
+                failed_now = 3;
                 break;
             }
-            __nanosleep(40);
+            __nanosleep(32);
         }
         __threadfence();
+        // An error the tail recorded before releasing is visible once the release is.
+        if (kHasTail && failed_now == 0) failed_now = failed(g);
+        s_failed = failed_now;
     }
     __syncthreads();
-    return !failed(g);
+    return !s_failed;
 }
 
-__device__ __forceinline__ bool grid_barrier(const GrowArgs& g) {
-    return grid_barrier(g, [] {});
+__device__ __forceinline__ bool grid_barrier(const GrowArgs& g, unsigned int& target) {
+    return grid_barrier<false>(g, target, [] {});
 }
 
 __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) {
@@ -144,6 +156,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     __shared__ SearchCtx s;
     __shared__ PhaseClock clock;
     if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
+    unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
+    __shared__ HistCta hist_cta;
+    histogram_prepare_cta(g.h, cta, smem, &hist_cta);
 
     for (int step = -1; step + 1 < a.max_leaves; ++step) {
         clock_step(g, clock, step);
@@ -156,12 +171,12 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
                 reinterpret_cast<int2*>(a.staging)[i] = make_int2(0, 0);
             partition_flags_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
             clock_mark(g, clock, 0);
-            if (!grid_barrier(g)) return;
+            if (!grid_barrier(g, target)) return;
             clock_mark(g, clock, 6);
             const uint32_t total_left = partition_scatter_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
             if (cta == 0 && threadIdx.x == 0) partition_publish(a, *a.step, total_left);
             clock_mark(g, clock, 1);
-            if (!grid_barrier(g)) return;
+            if (!grid_barrier(g, target)) return;
             clock_mark(g, clock, 6);
             broadcast_cg(a.step, &st);
         }
@@ -173,15 +188,14 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         if (direct)
             histogram_direct_cta(g.h, job, cta, ctas);
         else
-            histogram_cta(g.h, job, cta, smem);
+            histogram_cta(g.h, job, cta, smem, hist_cta);
         clock_mark(g, clock, 2);
-        if (!grid_barrier(g)) return;
+        if (!grid_barrier(g, target)) return;
         clock_mark(g, clock, 6);
         if (!direct) {
-            for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < g.hist_slots; i += ctas * kGrowThreads)
-                histogram_reduce_slot(g.h, job, i);
+            histogram_reduce_quads(g.h, job, cta * kGrowThreads + threadIdx.x, ctas * kGrowThreads);
             clock_mark(g, clock, 3);
-            if (!grid_barrier(g)) return;
+            if (!grid_barrier(g, target)) return;
             clock_mark(g, clock, 6);
         }
         search_context_cta(a, st, &s);
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             for (uint32_t item = gwarp; item < search_items(a, st); item += gwarps)
                 search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
         clock_mark(g, clock, 4);
-        if (!grid_barrier(g, [&] { search_finish(a, st, s); })) return;
+        if (!grid_barrier<true>(g, target, [&] { search_finish(a, st, s); })) return;
         clock_mark(g, clock, 5);  // the barrier with the finish in it
     }
 }
@@ -204,14 +218,12 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, grow_tree_kernel, kGrowThreads, smem_bytes);
 }
 
-cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
-                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns,
-                             int trace_steps) {
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
+                             cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
     GrowArgs g{};
     g.t = t;
     g.h = h;
     g.barrier = barrier;
-    g.hist_slots = hist_slots;
     g.phase_ns = phase_ns;
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet

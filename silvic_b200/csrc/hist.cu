@@ -10,13 +10,15 @@ namespace {
 
 __global__ void __launch_bounds__(kHistThreads) histogram_kernel(HistArgs a) {
     extern __shared__ __align__(16) int sh[];
+    __shared__ HistCta c;
     const HistJob job = *a.job;
-    histogram_cta(a, job, blockIdx.x, sh);
+    histogram_prepare_cta(a, blockIdx.x, sh, &c);
+    histogram_cta(a, job, blockIdx.x, sh, c);
 }
 
 __global__ void __launch_bounds__(256) histogram_reduce_kernel(HistArgs a) {
     const HistJob job = *a.job;
-    histogram_reduce_slot(a, job, blockIdx.x * 256 + threadIdx.x);
+    histogram_reduce_quads(a, job, blockIdx.x * 256 + threadIdx.x, gridDim.x * 256);
 }
 
 }  // namespace
@@ -27,8 +29,9 @@ void launch_histogram(const HistArgs& a, int grid, int smem_bytes, cudaStream_t 
     histogram_kernel<<<grid, kHistThreads, smem_bytes, stream>>>(a);
 }
 
-void launch_histogram_reduce(const HistArgs& a, uint32_t total_slots, cudaStream_t stream) {
-    histogram_reduce_kernel<<<static_cast<unsigned>(ceil_div(total_slots, 256)), 256, 0, stream>>>(a);
+void launch_histogram_reduce(const HistArgs& a, cudaStream_t stream) {
+    const uint64_t threads = static_cast<uint64_t>(a.num_quads) * a.quad_split;
+    histogram_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, stream>>>(a);
 }
 
 cudaError_t histogram_configure(int smem_bytes) {

@@ -41,6 +41,17 @@ struct HistJob {
     uint32_t pad_;
 };
 
+// Four consecutive gradient slots of one tile (one bin, four feature lanes) as the reduction sums them: their
+// offsets in a slab of the unit, and the output pair index of each lane (hist_offset + bin), -1 for a lane without
+// a feature or a bin past the feature's bins. Built at load.
+struct QuadMeta {
+    uint32_t unit;
+    uint32_t g_off;   // ints from the slab's start to the gradient slot
+    uint32_t h_off;   // ... to the hessian slot
+    int32_t out[4];
+    uint32_t pad_;
+};
+
 struct HistArgs {
     DevData d;
     const Unit* units;
@@ -54,6 +65,9 @@ struct HistArgs {
     int* out;                     // 2 * total_bins int32: the wanted features' bins are overwritten
     int* slabs;                   // scratch: one slab of slab_ints per CTA of the launch
     uint32_t slab_ints;           // 2 * the largest unit's slots
+    uint32_t num_quads;           // every unit's slots in fours
+    const QuadMeta* quads;
+    uint32_t quad_split;          // threads per quad in the reduction (a power of two <= 32)
     uint32_t pad_;
 };
 
@@ -66,7 +80,7 @@ __host__ __device__ __forceinline__ uint32_t unit_chunks(const Unit& u, uint32_t
 
 // The histogram: each CTA's private histogram into its scratch slab, then the slabs summed into `out`.
 void launch_histogram(const HistArgs& a, int grid, int smem_bytes, cudaStream_t stream);
-void launch_histogram_reduce(const HistArgs& a, uint32_t total_slots, cudaStream_t stream);
+void launch_histogram_reduce(const HistArgs& a, cudaStream_t stream);
 cudaError_t histogram_configure(int smem_bytes);
 cudaError_t histogram_occupancy(int smem_bytes, int* blocks_per_sm);
 int histogram_threads();

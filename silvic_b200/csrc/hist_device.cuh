@@ -118,37 +118,30 @@ __device__ __forceinline__ uint32_t unit_of_cta(const HistArgs& a, uint32_t cta)
     return ui;
 }
 
-// CTA `cta`'s share of `job`: its unit's rows of its chunk into shared memory, then into its slab. Needs
-// kHistThreads threads; returns without touching the slab when the CTA has no chunk.
-inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint32_t cta, int* sh) {
-    if (!job.active || job.count == 0) return;
-    const Unit unit = a.units[unit_of_cta(a, cta)];
-    const uint32_t chunk = cta - unit.cta_begin;
-    const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
-    if (chunk >= chunks) return;
-    const uint32_t lo = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * chunk / chunks);
-    const uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * (chunk + 1) / chunks);
+// The first 128-byte boundary of the dynamic shared memory `sh`: where the histogram starts (the callers reserve
+// kHistAlign more bytes).
+__device__ __forceinline__ uint32_t hist_shared_base(const int* sh) {
+    const uint32_t raw = static_cast<uint32_t>(__cvta_generic_to_shared(sh));
+    return (raw + kHistAlign - 1) & ~(kHistAlign - 1);
+}
 
-    // The histogram starts at the first 128-byte boundary of `sh` (the callers reserve kHistAlign more bytes).
-    const uint32_t sh_raw = static_cast<uint32_t>(__cvta_generic_to_shared(sh));
-    const uint32_t sh_addr = (sh_raw + kHistAlign - 1) & ~(kHistAlign - 1);
-    sh += (sh_addr - sh_raw) / 4;
-    {
-        int4* z = reinterpret_cast<int4*>(sh);
-        for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) z[i] = make_int4(0, 0, 0, 0);
-    }
+// What a histogram CTA does not relearn per job: its unit, the unit's tiles as the lanes use them (`active` 0;
+// the job sets its own bits), and each tile lane's feature. Kept in shared memory; the persistent tree kernel
+// fills it once per launch.
+struct HistCta {
+    Unit unit;
+    LaneTile tiles[kMaxUnitTiles];
+    int32_t lane_feature[kMaxUnitTiles][kTileLanes];
+};
 
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t warp = threadIdx.x >> 5;
-    constexpr uint32_t kWarps = kHistThreads / 32;
-    // The unit's tiles as the lanes use them, in shared memory (read per tile per batch, broadcast), with the
-    // features the histogram wants as one bit per lane (warp t fills tile t).
-    __shared__ LaneTile s_lt[kMaxUnitTiles];
-    const uint32_t num_tiles = unit.num_tiles;
-    if (warp < num_tiles) {
-        const int32_t f = a.d.lane_feature[(unit.first_tile + warp) * kTileLanes + lane];
-        const bool on = f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0);
-        const uint32_t bits = __ballot_sync(0xffffffffu, on);
+// Fills `c` for CTA `cta` (whole CTA; `sh` is the dynamic shared memory the histogram will use).
+inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, const int* sh, HistCta* c) {
+    if (threadIdx.x == 0) c->unit = a.units[unit_of_cta(a, cta)];
+    __syncthreads();
+    const Unit unit = c->unit;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp < unit.num_tiles) {
+        c->lane_feature[warp][lane] = a.d.lane_feature[(unit.first_tile + warp) * kTileLanes + lane];
         if (lane == 0) {
             // words before tile `warp`: every tile's arrays are 2 B S words (B >= 64, so 512-word multiples)
             uint32_t slot = 0;
@@ -161,7 +154,45 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
             lt.base = a.d.bins + tile.base;
             lt.stride = tile.stride;
             lt.bins = tile.smem_bins;
-            lt.g_addr = sh_addr + 4 * slot;
+            lt.g_addr = hist_shared_base(sh) + 4 * slot;
+            lt.active = 0;
+            c->tiles[warp] = lt;
+        }
+    }
+    __syncthreads();
+}
+
+// CTA `cta`'s share of `job`: its unit's rows of its chunk into shared memory, then into its slab. Needs
+// kHistThreads threads and the CTA's prepared `c`; returns without touching the slab when the CTA has no chunk.
+inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint32_t cta, int* sh, const HistCta& c) {
+    if (!job.active || job.count == 0) return;
+    const Unit unit = c.unit;
+    const uint32_t chunk = cta - unit.cta_begin;
+    const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
+    if (chunk >= chunks) return;
+    const uint32_t lo = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * chunk / chunks);
+    const uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * (chunk + 1) / chunks);
+
+    const uint32_t sh_addr = hist_shared_base(sh);
+    sh += (sh_addr - static_cast<uint32_t>(__cvta_generic_to_shared(sh))) / 4;
+    {
+        int4* z = reinterpret_cast<int4*>(sh);
+        for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) z[i] = make_int4(0, 0, 0, 0);
+    }
+
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t warp = threadIdx.x >> 5;
+    constexpr uint32_t kWarps = kHistThreads / 32;
+    // The unit's tiles with this job's wanted features (one bit per lane; warp t reads tile t's), in shared memory:
+    // read per tile per batch, broadcast.
+    __shared__ LaneTile s_lt[kMaxUnitTiles];
+    const uint32_t num_tiles = unit.num_tiles;
+    if (warp < num_tiles) {
+        const int32_t f = c.lane_feature[warp][lane];
+        const bool on = f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0);
+        const uint32_t bits = __ballot_sync(0xffffffffu, on);
+        if (lane == 0) {
+            LaneTile lt = c.tiles[warp];
             lt.active = bits;
             s_lt[warp] = lt;
         }
@@ -331,41 +362,62 @@ inline __device__ void histogram_direct_cta(const HistArgs& a, const HistJob& jo
     }
 }
 
-// Gradient slot `i` over every unit: the sum of the slabs of the unit's CTAs that took part, written into the flat
-// [g, h] output when its feature is wanted.
-inline __device__ void histogram_reduce_slot(const HistArgs& a, const HistJob& job, uint32_t i) {
+__device__ __forceinline__ int4 add4(int4 x, int4 y) { return make_int4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w); }
+
+__device__ __forceinline__ int4 shfl_xor4(int4 v, int o) {
+    return make_int4(__shfl_xor_sync(0xffffffffu, v.x, o), __shfl_xor_sync(0xffffffffu, v.y, o),
+                     __shfl_xor_sync(0xffffffffu, v.z, o), __shfl_xor_sync(0xffffffffu, v.w, o));
+}
+
+// The slab reduction, thread `thread` of `threads` (a multiple of 32): quad q's sums over the chunks of its unit
+// that took part are split over a.quad_split consecutive lanes (lane j of the group adds chunks j, j + split, ...,
+// with 128-bit loads, four chunks in flight), combined by shuffles, and the group's first lane writes the quad's
+// four [g, h] pairs. Every feature's bins are written, wanted or not (bins of unwanted features may hold anything).
+inline __device__ void histogram_reduce_quads(const HistArgs& a, const HistJob& job, uint32_t thread,
+                                              uint32_t threads) {
     if (!job.active || job.count == 0) return;
-    for (uint32_t u = 0; u < a.num_units; ++u) {
-        const Unit unit = a.units[u];
-        if (i >= unit.slots) {
-            i -= unit.slots;
-            continue;
+    const uint32_t split = a.quad_split;
+    const uint32_t j = thread & (split - 1);
+    const uint32_t groups = threads / split;
+    // every lane of a warp runs the same number of iterations: the shuffles need the whole warp
+    const uint32_t rounds = static_cast<uint32_t>(ceil_div(a.num_quads, groups));
+    for (uint32_t r = 0; r < rounds; ++r) {
+        const uint32_t q = r * groups + thread / split;
+        int4 g = make_int4(0, 0, 0, 0), h = g;
+        QuadMeta m{};
+        const bool mine = q < a.num_quads;
+        if (mine) {
+            m = a.quads[q];
+            const Unit unit = a.units[m.unit];
+            const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
+            const int* slab0 = a.slabs + static_cast<size_t>(unit.cta_begin) * a.slab_ints;
+            for (uint32_t c0 = j; c0 < chunks; c0 += 4 * split) {
+                int4 vg[4], vh[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t c = c0 + k * split;
+                    const int* slab = slab0 + static_cast<size_t>(c) * a.slab_ints;
+                    vg[k] = c < chunks ? __ldcg(reinterpret_cast<const int4*>(slab + m.g_off)) : make_int4(0, 0, 0, 0);
+                    vh[k] = c < chunks ? __ldcg(reinterpret_cast<const int4*>(slab + m.h_off)) : make_int4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    g = add4(g, vg[k]);
+                    h = add4(h, vh[k]);
+                }
+            }
         }
-        // The tile holding slot i of the unit, and the slot's offsets in the slab.
-        uint32_t off = 0, local = i, ti = unit.first_tile;
-        Tile tile = a.d.tiles[ti];
-        while (local >= tile.smem_bins * tile.stride) {
-            const uint32_t n = tile.smem_bins * tile.stride;
-            local -= n;
-            off += 2 * n;
-            tile = a.d.tiles[++ti];
+        for (uint32_t o = split >> 1; o > 0; o >>= 1) {
+            g = add4(g, shfl_xor4(g, static_cast<int>(o)));
+            h = add4(h, shfl_xor4(h, static_cast<int>(o)));
         }
-        const uint32_t n = tile.smem_bins * tile.stride;
-        const uint32_t bin = local / tile.stride, lane = local % tile.stride;
-        const int32_t f = a.d.lane_feature[ti * kTileLanes + lane];
-        if (f < 0 || (a.active != nullptr && __ldcg(a.active + f) == 0)) return;
-        const DevFeature feat = a.d.features[f];
-        if (bin >= feat.num_bins) return;
-        const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
-        const int* slab = a.slabs + static_cast<size_t>(unit.cta_begin) * a.slab_ints + off + local;
-        int g = 0, h = 0;
-#pragma unroll 4
-        for (uint32_t c = 0; c < chunks; ++c) {
-            g += __ldcg(slab + static_cast<size_t>(c) * a.slab_ints);
-            h += __ldcg(slab + static_cast<size_t>(c) * a.slab_ints + n);
+        if (mine && j == 0) {
+            int2* out = reinterpret_cast<int2*>(a.out);
+            if (m.out[0] >= 0) __stcg(out + m.out[0], make_int2(g.x, h.x));
+            if (m.out[1] >= 0) __stcg(out + m.out[1], make_int2(g.y, h.y));
+            if (m.out[2] >= 0) __stcg(out + m.out[2], make_int2(g.z, h.z));
+            if (m.out[3] >= 0) __stcg(out + m.out[3], make_int2(g.w, h.w));
         }
-        __stcg(reinterpret_cast<int2*>(a.out) + feat.hist_offset + bin, make_int2(g, h));
-        return;
     }
 }
 

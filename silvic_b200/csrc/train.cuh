@@ -142,9 +142,8 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // through the shared histograms (0), and the rows of the leaf it split.
 constexpr int kGrowPhases = 7;
 constexpr int kStepTrace = kGrowPhases + 3;
-cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, uint32_t hist_slots,
-                             int grid, int smem_bytes, cudaStream_t s, unsigned long long* phase_ns,
-                             int trace_steps);
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
+                             cudaStream_t s, unsigned long long* phase_ns, int trace_steps);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

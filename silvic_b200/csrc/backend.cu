@@ -93,6 +93,9 @@ struct sb2_backend {
     DeviceBuffer label, weight, scores, grad, hess, packed;
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, counter, maxima, misc;
+    DeviceBuffer api_spec;                    // the QuantSpec of the last sb2_quantize
+    sb2_quant_spec api_spec_host{};
+    const sb2_quant_spec* packed_spec = nullptr;  // the quantization the packed gradients now hold
     DeviceBuffer slabs;        // histogram scratch: one slab per histogram CTA
     uint32_t slab_ints = 0;    // ints per slab
     DeviceBuffer d_quads;      // the slab reduction's QuadMeta table
@@ -182,6 +185,7 @@ struct sb2_backend {
         }
         h.packed = packed.as<int32_t>();
         h.active = active;
+        h.spec = packed_spec;
         h.out = out;
         h.slabs = slabs.as<int>();
         h.slab_ints = slab_ints;
@@ -298,6 +302,15 @@ int run_histogram(sb2_backend* b, sb2_leaf_range leaf, double* out, size_t len) 
     if (len != 2ull * b->total_bins)
         return b->fail(SB2_EDEVICE, "histogram buffer of " + std::to_string(len) + " values, expected " +
                                         std::to_string(2ull * b->total_bins));
+    if (b->packed_spec == nullptr) return b->fail(SB2_EDEVICE, "histogram before any quantization");
+    if (b->packed_spec == b->api_spec.as<sb2_quant_spec>()) {
+        // The device sums in int32: every bin's sums must fit.
+        const sb2_quant_spec& q = b->api_spec_host;
+        const uint64_t max_q = static_cast<uint64_t>(std::max({q.grad_max_q, q.constant_hessian ? 1 : q.hess_max_q, 1}));
+        if (static_cast<uint64_t>(leaf.count) * max_q > 2147483647ull)
+            return b->fail(SB2_EUNSUPPORTED, "histogram sums of " + std::to_string(leaf.count) + " rows at " +
+                                                 std::to_string(max_q) + " units per row could pass int32");
+    }
     SB2_CUDA(b, cudaMemsetAsync(b->staging.ptr, 0, sizeof(int) * (2ull * b->total_bins + 2), b->stream));
     HistJob job{};
     job.active = 1;
@@ -482,8 +495,8 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         base += (n * t.stride + 127) / 128 * 128;
         b->tiles.push_back(t);
     }
-    // Histogram units: consecutive tiles, up to kMaxUnitTiles within a shared-memory budget (two int32 arrays of
-    // smem_bins * stride slots per tile).
+    // Histogram units: consecutive tiles, up to kMaxUnitTiles within a shared-memory budget (one packed int32 array
+    // of smem_bins * stride slots per tile).
 #ifndef SB2_UNIT_BUDGET_KB
 #define SB2_UNIT_BUDGET_KB 220  // of the 227 KB a CTA may hold, leaving room for the kernels' static shared memory
 #endif
@@ -497,7 +510,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         size_t bytes = 0;
         uint32_t feats = 0;
         while (i < b->tiles.size() && u.num_tiles < static_cast<uint32_t>(kMaxUnitTiles)) {
-            size_t tb = 8ull * b->tiles[i].smem_bins * b->tiles[i].stride;
+            size_t tb = 4ull * b->tiles[i].smem_bins * b->tiles[i].stride;
             if (u.num_tiles > 0 && bytes + tb > kUnitBudget) break;
             bytes += tb;
             u.slots += b->tiles[i].smem_bins * b->tiles[i].stride;
@@ -631,6 +644,10 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, b->step.alloc(sizeof(Step)));
     SB2_CUDA(b, b->iter.alloc(sizeof(IterState)));
     SB2_CUDA(b, b->api_active.alloc(std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->api_spec.alloc(sizeof(sb2_quant_spec)));
+    SB2_CUDA(b, cudaMemsetAsync(b->api_spec.ptr, 0, sizeof(sb2_quant_spec), b->stream));
+    b->api_spec_host = sb2_quant_spec{};
+    b->packed_spec = b->api_spec.as<sb2_quant_spec>();  // the packed gradients start as zeros
     SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * std::max<size_t>(F, 1)));
     SB2_CUDA(b, b->maxima.alloc(2 * sizeof(unsigned long long)));
     SB2_CUDA(b, b->grid_barrier.alloc(2 * sizeof(unsigned int)));
@@ -678,6 +695,11 @@ int sb2_compute_gradients(sb2_backend* b, sb2_gradient_stats* out) {
 
 int sb2_quantize(sb2_backend* b, const sb2_quant_spec* spec) {
     SB2_TRY(b->check_loaded());
+    if (!spec) return b->fail(SB2_EDEVICE, "null quantization spec");
+    // The histograms bound their packed sums by the spec the packed gradients came from.
+    b->api_spec_host = *spec;
+    SB2_CUDA(b, cudaMemcpyAsync(b->api_spec.ptr, spec, sizeof(sb2_quant_spec), cudaMemcpyHostToDevice, b->stream));
+    b->packed_spec = b->api_spec.as<sb2_quant_spec>();
     launch_api_quantize(b->row_args(), *spec, b->row_grid(), b->stream);
     SB2_CUDA(b, cudaGetLastError());
     return b->sync();
@@ -1199,6 +1221,8 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
         return b->fail(SB2_EUNSUPPORTED, "int32 histograms would overflow: rows * quant bins >= 2^31");
     tr.L = L;
     tr.iters = iters;
+    // Each iteration quantizes into the iteration state's spec; the histograms bound their sums by it.
+    b->packed_spec = &b->iter.as<IterState>()->spec;
     TrainBuffers& tb = tr.tb;
     SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));

@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
     __shared__ HistCta hist_cta;
     histogram_prepare_cta(g.h, cta, smem, &hist_cta);
+    const uint32_t round_rows = packed_round_rows(*g.h.spec);  // the iteration's quantization, set before the launch
 
     for (int step = -1; step + 1 < a.max_leaves; ++step) {
         clock_step(g, clock, step);
@@ -183,12 +184,12 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // The new histogram (the root, or the smaller child): straight into staging for a small job, else per-CTA
         // shared histograms and their slab reduction. Then the search.
         broadcast_cg(a.hist_job, &job);
-        const bool direct = job.count <= kDirectRows;
+        const bool direct = histogram_goes_direct(job.count, round_rows);
         clock_describe(g, clock, job.active ? job.count : 0u, direct, st.count);
         if (direct)
             histogram_direct_cta(g.h, job, cta, ctas);
         else
-            histogram_cta(g.h, job, cta, smem, hist_cta);
+            histogram_cta(g.h, job, cta, smem, hist_cta, round_rows);
         clock_mark(g, clock, 2);
         if (!grid_barrier(g, target)) return;
         clock_mark(g, clock, 6);

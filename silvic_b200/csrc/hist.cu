@@ -12,12 +12,18 @@ __global__ void __launch_bounds__(kHistThreads) histogram_kernel(HistArgs a) {
     extern __shared__ __align__(16) int sh[];
     __shared__ HistCta c;
     const HistJob job = *a.job;
+    const uint32_t round_rows = packed_round_rows(*a.spec);
+    if (histogram_goes_direct(job.count, round_rows)) {
+        histogram_direct_cta(a, job, blockIdx.x, gridDim.x);
+        return;
+    }
     histogram_prepare_cta(a, blockIdx.x, sh, &c);
-    histogram_cta(a, job, blockIdx.x, sh, c);
+    histogram_cta(a, job, blockIdx.x, sh, c, round_rows);
 }
 
 __global__ void __launch_bounds__(256) histogram_reduce_kernel(HistArgs a) {
     const HistJob job = *a.job;
+    if (histogram_goes_direct(job.count, packed_round_rows(*a.spec))) return;  // already in the output
     histogram_reduce_quads(a, job, blockIdx.x * 256 + threadIdx.x, gridDim.x * 256);
 }
 

@@ -62,6 +62,7 @@ struct HistArgs {
     const int32_t* ordered[2];    // ordered packed gradients, by partition position
     const int32_t* packed;        // packed gradients by row (identity jobs)
     const uint8_t* active;        // per feature: its bins are wanted; nullptr for all
+    const sb2_quant_spec* spec;   // the quantization of the packed gradients (bounds their per-bin sums)
     int* out;                     // 2 * total_bins int32: the wanted features' bins are overwritten
     int* slabs;                   // scratch: one slab of slab_ints per CTA of the launch
     uint32_t slab_ints;           // 2 * the largest unit's slots

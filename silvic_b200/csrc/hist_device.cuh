@@ -1,17 +1,19 @@
 // hist_device.cuh — the histogram's CTA-level device functions (see hist.cuh), shared by the standalone kernels
 // (hist.cu) and the persistent tree kernel (grow.cu).
 //
-// Shared memory of a CTA: for each tile of its unit, an int32 gradient array and an int32 hessian array of
-// smem_bins * stride slots, slot = bin * stride + feature lane. Native 32-bit shared atomics run 4-6x faster than
-// 64-bit ones on sm_100, so g and h are added separately rather than as one packed 64-bit value.
+// Shared memory of a CTA: for each tile of its unit, one int32 array of smem_bins * stride slots, slot = bin *
+// stride + feature lane, that accumulates the rows' packed gradients h * 65536 + g as they are (quantize.rs:103-107):
+// one 32-bit shared reduction per element, the shared-atomic unit's fastest operation on sm_100 (the kernel is bound
+// by it). The packed sums stay exact while every bin's |sum g| <= 32767 and sum h <= 65535, so a CTA adds at most
+// `round_rows` rows (packed_round_rows) before it flushes: it unpacks the slots into its slab of separate int32 g and
+// h arrays (stored the first time, added afterwards) and clears them.
 //
 // Work per warp: 32 consecutive positions of the leaf, lane k owning position k's row. A lane loads its row's tile
 // bytes with 128-bit loads (a 32-byte row is one sector; a warp's 32 rows are in flight together), permutes them by
-// its lane index, and walks them: at step i lane k adds its row's (g, h) at feature i XOR (k mod stride), so in a
-// full tile the 32 lanes of every atomic hit 32 different features, i.e. 32 different banks. The arrays are
-// aligned and sized (64, 128 or 256 bins per lane) so that an element costs one multiply-add for its address and
-// two shared reductions, the hessian's at a compile-time offset. Rows whose packed gradient is zero add nothing and
-// skip their atomics.
+// its lane index, and walks them: at step i lane k adds its row's packed gradient at feature i XOR (k mod stride), so
+// in a full tile the 32 lanes of every atomic hit 32 different features, i.e. 32 different banks. The arrays are
+// aligned so that an element costs one multiply-add for its address and one shared reduction. Rows whose packed
+// gradient is zero add nothing and skip their atomics.
 #pragma once
 
 #include "hist.cuh"
@@ -24,9 +26,33 @@ struct LaneTile {
     const uint8_t* base;  // the tile's row 0
     uint32_t stride;      // 4, 8, 16 or 32 bytes
     uint32_t bins;        // 64, 128 or 256: bin slots per feature lane
-    uint32_t g_addr;      // shared address of the tile's gradient array (aligned to 4 * stride bytes)
+    uint32_t addr;        // shared address of the tile's packed array (aligned to 4 * stride bytes)
     uint32_t active;      // bit f: feature lane f is wanted (0: the tile is skipped)
 };
+
+// Rows whose packed gradients one packed histogram can sum exactly: every bin's |sum g| <= 32767 and sum h <=
+// 65535 (h is 1 per row with a constant hessian).
+__host__ __device__ __forceinline__ uint32_t packed_round_rows(const sb2_quant_spec& s) {
+    const uint32_t gq = s.grad_max_q > 1 ? static_cast<uint32_t>(s.grad_max_q) : 1u;
+    const uint32_t hq = s.constant_hessian ? 1u : (s.hess_max_q > 1 ? static_cast<uint32_t>(s.hess_max_q) : 1u);
+    const uint32_t r = 32767u / gq < 65535u / hq ? 32767u / gq : 65535u / hq;
+    return r;
+}
+
+// A packed round shorter than a batch per warp is not worth the flushes: such quantizations (more than 64
+// gradient bins) histogram straight into the output instead (histogram_direct_cta).
+constexpr uint32_t kMinRoundRows = kHistThreads;
+
+// Jobs of at most kDirectRows rows skip the shared histograms too: every (row, feature) adds straight into the
+// output with global reductions, so there is nothing to clear, flush or reduce, which for a small leaf costs more
+// than its few atomics.
+constexpr uint32_t kDirectRows = 4096;
+
+// Whether a histogram of `count` rows goes straight into the output (histogram_direct_cta) rather than through the
+// shared histograms and their slab reduction.
+__host__ __device__ __forceinline__ bool histogram_goes_direct(uint32_t count, uint32_t round_rows) {
+    return count <= kDirectRows || round_rows < kMinRoundRows;
+}
 
 // Permutes the `W` words of a row so that byte i becomes the row's byte i ^ k (k < 4 W): byte bits within each word
 // by one byte_perm, word bits by conditional swaps.
@@ -50,65 +76,51 @@ __device__ __forceinline__ void xor_bytes(uint32_t (&w)[W], uint32_t k) {
     }
 }
 
-// Adds (g, h) at shared address `addr` (the gradient slot) and addr + kHessianOffset (the hessian slot), with
-// red.shared: no return value, never the generic path. No "memory" clobber: the compiler may move global loads
-// across these (the histogram is only read after a barrier).
-template <uint32_t kHessianOffset>
-__device__ __forceinline__ void shared_add_pair(uint32_t addr, int32_t g, int32_t h) {
-    asm volatile(
-        "red.shared.add.s32 [%0], %1;\n\t"
-        "red.shared.add.s32 [%0+%3], %2;" ::"r"(addr),
-        "r"(g), "r"(h), "n"(kHessianOffset));
+// Adds `v` at shared address `addr` with red.shared: no return value, never the generic path. No "memory" clobber:
+// the compiler may move global loads across these (the histogram is only read after a barrier).
+__device__ __forceinline__ void shared_add(uint32_t addr, uint32_t v) {
+    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v));
 }
 
-// Issues the loads of one row of a tile (stride 4, 8, 16 or 32 bytes) into w[0 .. stride / 4).
+// Issues the loads of one row of a tile (stride 4, 8, 16 or 32 bytes) into w[0 .. stride / 4). Streaming loads
+// (evict first): a histogram reads its rows' bins once, and the leaf histograms, partition buffers and metadata the
+// next phases read should stay in L2 instead.
 __device__ __forceinline__ void load_row(const LaneTile& t, uint32_t row, uint32_t (&w)[8]) {
     const uint8_t* p = t.base + static_cast<uint64_t>(row) * t.stride;
     if (t.stride == 32) {
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+        const uint4 b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
         w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w, w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
     } else if (t.stride == 16) {
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
         w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w;
     } else if (t.stride == 8) {
-        const uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+        const uint2 a = __ldcs(reinterpret_cast<const uint2*>(p));
         w[0] = a.x, w[1] = a.y;
     } else {
-        w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+        w[0] = __ldcs(reinterpret_cast<const uint32_t*>(p));
     }
 }
 
-// Adds one loaded row of one tile of `W` words (stride S = 4 W bytes) and `B` bins per lane: the lane's row's
-// (g, h) at feature i ^ k for i = 0 .. S-1, k = lane mod S. Slot (bin, f) of the gradient array is word
-// bin * S + f, so the S lanes of every step hit S different features, i.e. S different banks; with the array
-// aligned to 4 S bytes the slot's address is bin * 4S + (base | 4k) ^ 4i, one multiply-add per element. Every
-// feature of the tile is added, wanted or not: only wanted features' bins are ever read back.
-template <int W, int B>
-__device__ __forceinline__ void add_row(const LaneTile& t, uint32_t (&wrow)[8], int32_t g, int32_t h, uint32_t lane) {
+// Adds one loaded row of one tile of `W` words (stride S = 4 W bytes): the lane's row's packed gradient at feature
+// i ^ k for i = 0 .. S-1, k = lane mod S. Slot (bin, f) is word bin * S + f, so the S lanes of every step hit S
+// different features, i.e. S different banks; with the array aligned to 4 S bytes the slot's address is
+// bin * 4S + (base | 4k) ^ 4i, one multiply-add per element. Every feature of the tile is added, wanted or not:
+// only wanted features' bins are ever read back.
+template <int W>
+__device__ __forceinline__ void add_row(const LaneTile& t, const uint32_t (&wrow)[8], uint32_t packed, uint32_t lane) {
     constexpr uint32_t kStride = 4 * W;
     uint32_t w[W];
 #pragma unroll
     for (int j = 0; j < W; ++j) w[j] = wrow[j];
     const uint32_t k = lane & (kStride - 1);
     xor_bytes<W>(w, k);
-    const uint32_t base = t.g_addr | (4 * k);
+    const uint32_t base = t.addr | (4 * k);
 #pragma unroll
     for (int i = 0; i < static_cast<int>(kStride); ++i) {
         const uint32_t bin = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-        shared_add_pair<4 * B * kStride>(bin * (4 * kStride) + (base ^ (4u * i)), g, h);
+        shared_add(bin * (4 * kStride) + (base ^ (4u * i)), packed);
     }
-}
-
-template <int W>
-__device__ __forceinline__ void add_row_bins(const LaneTile& t, uint32_t (&wrow)[8], int32_t g, int32_t h,
-                                             uint32_t lane) {
-    if (t.bins == 256)
-        add_row<W, 256>(t, wrow, g, h, lane);
-    else if (t.bins == 128)
-        add_row<W, 128>(t, wrow, g, h, lane);
-    else
-        add_row<W, 64>(t, wrow, g, h, lane);
 }
 
 // The unit of histogram CTA `cta`.
@@ -143,18 +155,18 @@ inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, co
     if (warp < unit.num_tiles) {
         c->lane_feature[warp][lane] = a.d.lane_feature[(unit.first_tile + warp) * kTileLanes + lane];
         if (lane == 0) {
-            // words before tile `warp`: every tile's arrays are 2 B S words (B >= 64, so 512-word multiples)
+            // words before tile `warp`: every tile's array is B S words (B >= 64, so 256-word multiples)
             uint32_t slot = 0;
             for (uint32_t t = 0; t < warp; ++t) {
                 const Tile prev = a.d.tiles[unit.first_tile + t];
-                slot += 2 * prev.smem_bins * prev.stride;
+                slot += prev.smem_bins * prev.stride;
             }
             const Tile tile = a.d.tiles[unit.first_tile + warp];
             LaneTile lt;
             lt.base = a.d.bins + tile.base;
             lt.stride = tile.stride;
             lt.bins = tile.smem_bins;
-            lt.g_addr = hist_shared_base(sh) + 4 * slot;
+            lt.addr = hist_shared_base(sh) + 4 * slot;
             lt.active = 0;
             c->tiles[warp] = lt;
         }
@@ -162,23 +174,63 @@ inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, co
     __syncthreads();
 }
 
-// CTA `cta`'s share of `job`: its unit's rows of its chunk into shared memory, then into its slab. Needs
-// kHistThreads threads and the CTA's prepared `c`; returns without touching the slab when the CTA has no chunk.
-inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint32_t cta, int* sh, const HistCta& c) {
+// Unpacks the packed shared histogram `sh` of the unit into the CTA's slab: per tile, its slots' g into the slab's
+// gradient array and h into its hessian array (at twice the packed offset; see QuadMeta), stored when `first`, added
+// otherwise; the shared slots are cleared for the next round when `clear`. Four slots per thread and step.
+__device__ __forceinline__ void flush_packed(const HistCta& c, int4* sh, uint32_t sh_addr, int* slab, bool first,
+                                             bool clear) {
+    const uint32_t quads = c.unit.slots / 4;
+    for (uint32_t i = threadIdx.x; i < quads; i += kHistThreads) {
+        // the tile of quad i, and its place in the slab
+        uint32_t t = 0, s = 4 * i;
+        uint32_t p = (c.tiles[0].addr - sh_addr) / 4, n = c.tiles[0].bins * c.tiles[0].stride;
+        while (s >= p + n) {
+            ++t;
+            p = (c.tiles[t].addr - sh_addr) / 4;
+            n = c.tiles[t].bins * c.tiles[t].stride;
+        }
+        const int4 v = sh[i];
+        // unpack (quantize.rs:140-143): g is the low half sign-extended, h what remains above it
+        const int4 g = make_int4(static_cast<int16_t>(v.x & 0xFFFF), static_cast<int16_t>(v.y & 0xFFFF),
+                                 static_cast<int16_t>(v.z & 0xFFFF), static_cast<int16_t>(v.w & 0xFFFF));
+        const int4 h = make_int4(static_cast<int>(static_cast<uint32_t>(v.x - g.x) >> 16),
+                                 static_cast<int>(static_cast<uint32_t>(v.y - g.y) >> 16),
+                                 static_cast<int>(static_cast<uint32_t>(v.z - g.z) >> 16),
+                                 static_cast<int>(static_cast<uint32_t>(v.w - g.w) >> 16));
+        int4* gs = reinterpret_cast<int4*>(slab + p + s);  // 2 p + (s - p): the tile's gradient array
+        int4* hs = reinterpret_cast<int4*>(slab + p + n + s);
+        if (first) {
+            __stcg(gs, g);
+            __stcg(hs, h);
+        } else {
+            const int4 og = __ldcg(gs), oh = __ldcg(hs);
+            __stcg(gs, make_int4(og.x + g.x, og.y + g.y, og.z + g.z, og.w + g.w));
+            __stcg(hs, make_int4(oh.x + h.x, oh.y + h.y, oh.z + h.z, oh.w + h.w));
+        }
+        if (clear) sh[i] = make_int4(0, 0, 0, 0);
+    }
+}
+
+// CTA `cta`'s share of `job`: its unit's rows of its chunk into shared memory, then into its slab, in rounds of at
+// most `round_rows` rows (packed_round_rows of the job's quantization; at least kMinRoundRows). Needs kHistThreads
+// threads and the CTA's prepared `c`; returns without touching the slab when the CTA has no chunk.
+inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint32_t cta, int* sh, const HistCta& c,
+                                     uint32_t round_rows) {
     if (!job.active || job.count == 0) return;
     const Unit unit = c.unit;
     const uint32_t chunk = cta - unit.cta_begin;
     const uint32_t chunks = unit_chunks(unit, job.count, a.min_rows_per_cta);
     if (chunk >= chunks) return;
     const uint32_t lo = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * chunk / chunks);
-    const uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * (chunk + 1) / chunks);
+    uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(job.count) * (chunk + 1) / chunks);
 
     const uint32_t sh_addr = hist_shared_base(sh);
     sh += (sh_addr - static_cast<uint32_t>(__cvta_generic_to_shared(sh))) / 4;
     {
         int4* z = reinterpret_cast<int4*>(sh);
-        for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) z[i] = make_int4(0, 0, 0, 0);
+        for (uint32_t i = threadIdx.x; i < unit.slots / 4; i += kHistThreads) z[i] = make_int4(0, 0, 0, 0);
     }
+    int* slab = a.slabs + static_cast<size_t>(cta) * a.slab_ints;
 
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t warp = threadIdx.x >> 5;
@@ -200,82 +252,80 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
     __syncthreads();
     uint32_t any = 0;
     for (uint32_t t = 0; t < num_tiles; ++t) any |= s_lt[t].active;
+    if (any == 0) hi = lo;  // nothing wanted: one flush of zeros
 
-    const uint32_t span = hi - lo;
-    const uint32_t per_warp = static_cast<uint32_t>(ceil_div(ceil_div(span, kWarps), 32) * 32);
-    const uint32_t w_lo = lo + min(span, per_warp * warp);
-    const uint32_t w_hi = lo + min(span, per_warp * (warp + 1));
     const uint32_t* rows = a.rows[job.which & 1];
     const int32_t* ordered = a.ordered[job.which & 1];
-    // The row and packed gradient of position p (0 past the warp's range).
-    auto position = [&](uint32_t p, uint32_t& row, int32_t& packed) {
-        row = 0;
-        packed = 0;
-        if (p < w_hi) {
-            const uint32_t pos = job.begin + p;
-            if (job.identity) {
-                row = pos;
-                packed = __ldg(a.packed + pos);
-            } else {
-                row = __ldcg(rows + pos);  // written by this step's partition: not through the read-only path
-                packed = __ldcg(ordered + pos);
-            }
-        }
-    };
-    if (any != 0 && w_lo < w_hi) {
-        uint32_t next_row;
-        int32_t next_packed;
-        position(w_lo + lane, next_row, next_packed);
-        for (uint32_t p0 = w_lo; p0 < w_hi; p0 += 32) {
-            const uint32_t row = next_row;
-            const int32_t packed = next_packed;
-            // One tile ahead: tile t + 1's bytes are in flight while tile t's atomics issue (the first tile's
-            // together with the next batch's positions).
-            uint32_t cur[8] = {}, nxt[8] = {};
-            if (s_lt[0].active != 0) load_row(s_lt[0], row, cur);
-            position(p0 + 32 + lane, next_row, next_packed);
-            // unpack (quantize.rs:140-143); a zero row adds nothing.
-            const int32_t g = static_cast<int16_t>(static_cast<uint16_t>(static_cast<uint32_t>(packed)));
-            const int32_t h = (packed - g) >> 16;
-#pragma unroll
-            for (int t = 0; t < kMaxUnitTiles; ++t) {
-                if (t >= static_cast<int>(num_tiles)) break;
-                if (t + 1 < static_cast<int>(num_tiles) && s_lt[t + 1].active != 0) load_row(s_lt[t + 1], row, nxt);
-                const LaneTile lt = s_lt[t];
-                if (packed != 0 && lt.active != 0) {
-                    switch (lt.stride) {
-                        case 32:
-                            add_row_bins<8>(lt, cur, g, h, lane);
-                            break;
-                        case 16:
-                            add_row_bins<4>(lt, cur, g, h, lane);
-                            break;
-                        case 8:
-                            add_row_bins<2>(lt, cur, g, h, lane);
-                            break;
-                        default:
-                            add_row_bins<1>(lt, cur, g, h, lane);
-                            break;
-                    }
+    int4* sh4 = reinterpret_cast<int4*>(sh);
+    uint32_t r0 = lo;
+    do {
+        const uint32_t r1 = min(hi, r0 + round_rows);
+        const uint32_t span = r1 - r0;
+        const uint32_t per_warp = static_cast<uint32_t>(ceil_div(ceil_div(span, kWarps), 32) * 32);
+        const uint32_t w_lo = r0 + min(span, per_warp * warp);
+        const uint32_t w_hi = r0 + min(span, per_warp * (warp + 1));
+        // The row and packed gradient of position p (0 past the warp's range).
+        auto position = [&](uint32_t p, uint32_t& row, int32_t& packed) {
+            row = 0;
+            packed = 0;
+            if (p < w_hi) {
+                const uint32_t pos = job.begin + p;
+                if (job.identity) {
+                    row = pos;
+                    packed = __ldcs(a.packed + pos);
+                } else {
+                    row = __ldcg(rows + pos);  // written by this step's partition: not through the read-only path
+                    packed = __ldcg(ordered + pos);
                 }
+            }
+        };
+        if (w_lo < w_hi) {
+            uint32_t next_row;
+            int32_t next_packed;
+            position(w_lo + lane, next_row, next_packed);
+            for (uint32_t p0 = w_lo; p0 < w_hi; p0 += 32) {
+                const uint32_t row = next_row;
+                const uint32_t packed = static_cast<uint32_t>(next_packed);
+                // One tile ahead: tile t + 1's bytes are in flight while tile t's atomics issue (the first tile's
+                // together with the next batch's positions).
+                uint32_t cur[8] = {}, nxt[8] = {};
+                if (s_lt[0].active != 0) load_row(s_lt[0], row, cur);
+                position(p0 + 32 + lane, next_row, next_packed);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+                for (int t = 0; t < kMaxUnitTiles; ++t) {
+                    if (t >= static_cast<int>(num_tiles)) break;
+                    if (t + 1 < static_cast<int>(num_tiles) && s_lt[t + 1].active != 0)
+                        load_row(s_lt[t + 1], row, nxt);
+                    const LaneTile lt = s_lt[t];
+                    if (packed != 0 && lt.active != 0) {  // a zero row adds nothing
+                        switch (lt.stride) {
+                            case 32:
+                                add_row<8>(lt, cur, packed, lane);
+                                break;
+                            case 16:
+                                add_row<4>(lt, cur, packed, lane);
+                                break;
+                            case 8:
+                                add_row<2>(lt, cur, packed, lane);
+                                break;
+                            default:
+                                add_row<1>(lt, cur, packed, lane);
+                                break;
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+                }
             }
         }
-    }
-    __syncthreads();
-
-    // Flush: the shared histogram, as laid out, to this CTA's slab (2 * unit.slots ints, a multiple of 4).
-    int4* slab = reinterpret_cast<int4*>(a.slabs + static_cast<size_t>(cta) * a.slab_ints);
-    const int4* src = reinterpret_cast<const int4*>(sh);
-    for (uint32_t i = threadIdx.x; i < (2 * unit.slots) / 4; i += kHistThreads) __stcg(slab + i, src[i]);
-    __syncthreads();
+        __syncthreads();
+        flush_packed(c, sh4, sh_addr, slab, r0 == lo, r1 < hi);
+        __syncthreads();
+        r0 = r1;
+    } while (r0 < hi);
 }
 
-// Jobs of at most kDirectRows rows skip the shared histograms: every (row, feature) adds straight into the output
-// with global reductions, so there is nothing to clear, flush or reduce, which for a small leaf costs more than
-// its few atomics. The output must hold zeros in the wanted features' bins.
-constexpr uint32_t kDirectRows = 4096;
+// The output must hold zeros in the wanted features' bins before a direct histogram (histogram_goes_direct).
 
 __device__ __forceinline__ void global_add_pair(int* p, int32_t g, int32_t h) {
     asm volatile(

@@ -68,6 +68,28 @@ def test_histogram_matches_oracle(device, bins, rows, quant_bins):
     b.close()
 
 
+@pytest.mark.parametrize("quant_bins,rows", [(64, 400_000), (512, 60_000)],
+                         ids=["packed_rounds", "wide_quantization"])
+def test_histogram_packing_limits(device, quant_bins, rows):
+    """Histograms whose packed per-bin sums would pass 16 bits within one CTA: 64 quant bins over 400k rows make
+    every CTA flush its packed shared histogram several times (sums exact while |g| <= 32767, h <= 65535 per
+    round); 512 quant bins are too wide for packed rounds and go straight to the output."""
+    data = random_binned(rows, [255] * 6 + [16] * 3, seed=quant_bins)
+    b = loaded(data)
+    grad, hess = set_gradients(b, data, seed=4)
+    spec = orc.quant_spec(1.5, 0.75, None, quant_bins, True, 9, 3)
+    b.quantize(spec)
+    packed = b.read_packed()
+    assert np.array_equal(packed, orc.quantize(spec, grad, hess)), "quantize"
+    n = b.reset_partition(_abi.BagSpec(1, 4, 1, 0, 0.9))
+    part = b.read_partition(n)
+    for begin, count in [(0, n), (n // 3, n // 2)]:
+        got = b.histogram(begin, count)
+        want = orc.histogram(data, packed, part[begin:begin + count], max_quant=quant_bins)
+        assert np.array_equal(got, want), f"leaf {begin}+{count}"
+    b.close()
+
+
 def test_identity_root_histogram(device):
     data = random_binned(100_003, [255] * 33, seed=5)
     b = loaded(data)

@@ -86,6 +86,7 @@ struct sb2_backend {
     int hist_smem = 0;
     int hist_grid = 0;
     int grow_smem = 0;      // dynamic shared memory of the persistent tree kernel
+    uint32_t grow_flags_offset = 0;  // where in it the kernel's per-feature flags start
     bool grow_ok = false;   // it fits one CTA per SM
     DeviceBuffer grid_barrier;
     DeviceBuffer phase_ns;  // per-phase nanoseconds of the persistent kernel (profiling runs)
@@ -530,7 +531,14 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
     // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
-    b->grow_smem = std::max<int>(b->hist_smem, (grow_threads() / 32) * kMaxBins * 8);
+    // Then its per-feature flags (4 F bytes) after everything the phases share.
+    {
+        const size_t phases = std::max<size_t>({static_cast<size_t>(b->hist_smem),
+                                                static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8,
+                                                (2ull * grow_threads() + 64) * 4});
+        b->grow_flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
+        b->grow_smem = static_cast<int>(b->grow_flags_offset + (4ull * F + 15) / 16 * 16);
+    }
     int grow_per_sm = 0;
     SB2_CUDA(b, grow_configure(b->grow_smem, &grow_per_sm));
     b->grow_ok = grow_per_sm >= 1;
@@ -1050,7 +1058,8 @@ int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int wor
 namespace {
 
 struct TrainBuffers {
-    DeviceBuffer leaves, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records, record_bufs;
+    DeviceBuffer leaves, leaf_gain, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records,
+        record_bufs;
 };
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
@@ -1154,7 +1163,7 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
         // One launch grows the whole tree (grow.cu).
         SB2_TRY(op(kOpTree, [&] {
             return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
-                                            b->grow_smem, s,
+                                            b->grow_smem, b->grow_flags_offset, s,
                                             timer ? b->phase_ns.as<unsigned long long>() : nullptr,
                                             timer ? max_leaves : 0),
                            "cudaLaunchCooperativeKernel(grow_tree)");
@@ -1225,6 +1234,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     b->packed_spec = &b->iter.as<IterState>()->spec;
     TrainBuffers& tb = tr.tb;
     SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
+    SB2_CUDA(b, tb.leaf_gain.alloc(sizeof(double) * L));
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.masks.alloc(static_cast<size_t>(std::max(iters, 1)) * std::max<uint32_t>(F, 1)));
@@ -1276,6 +1286,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
         }
     t.num_iterations = iters;
     t.leaves = tb.leaves.as<DevLeaf>();
+    t.leaf_gain = tb.leaf_gain.as<double>();
     t.splittable = tb.splittable.as<uint8_t>();
     t.evaluate = tb.evaluate.as<uint8_t>();
     t.masks = tb.masks.as<uint8_t>();

@@ -3,11 +3,14 @@
 // A split step as separate launches costs a launch and a reload of the dataset's metadata per kernel, about 40 us
 // of fixed time per split on small leaves, which dominates a 255-leaf tree. Here one cooperative launch (every CTA
 // resident, one per SM) runs every step of the tree; its phases are separated by grid barriers:
-//   root:   histogram -> slab reduction -> search -> finish
-//   split:  partition flags -> scatter -> histogram of the smaller child -> slab reduction -> search -> finish
-// `finish` (apply the split, pick each child's best split, choose the next leaf) runs in the last CTA to arrive at
-// the search barrier before it releases the others. The phases are the device functions of partition.cuh,
-// hist_device.cuh and search.cuh, the same code the standalone kernels of the multi-GPU path run.
+//   root:   histogram -> [slab reduction] -> search -> finish
+//   split:  partition flags -> scatter -> histogram of the smaller child -> [slab reduction] -> search -> finish
+// (the slab reduction only for histograms through shared memory). Every CTA runs `finish` (apply the split, pick
+// each child's best split, choose the next leaf) on the same inputs and reaches the same next step in its own
+// shared memory; four CTAs write its results for later steps and kernels (search_finish_prepare). Work a CTA can do
+// before the others reach a barrier (the next search's context, the finish's parts without candidates) runs between
+// its arrival and its wait. The phases are the device functions of partition.cuh, hist_device.cuh and search.cuh,
+// which the standalone kernels of the multi-GPU path also run.
 //
 // Every barrier wait is bounded: a CTA that waits longer than kBarrierSpins polls records an error in the
 // iteration state and leaves the kernel, and every other CTA then leaves at its next barrier; the host reports the
@@ -31,8 +34,10 @@ struct GrowArgs {
     unsigned int* barrier;        // arrivals at grid barriers so far (zeroed before the launch)
     unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
-    int pad2_;
+    uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (4 F bytes)
 };
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -85,42 +90,29 @@ __device__ __forceinline__ void broadcast_cg(const T* p, T* shared_copy) {
     __syncthreads();
 }
 
-__device__ __forceinline__ bool failed(const GrowArgs& g) { return __ldcg(&g.t.iter->error) != 0; }
-
-// Grid barriers count arrivals on one word that only grows during the launch (the host zeroes it before): barrier
-// k of the launch is passed once the word reaches the running target, which every CTA advances identically (by
-// the grid size, plus one for a barrier with a tail). A plain barrier is released by its last arrival itself, so
-// it costs one atomic and the poll that sees it. In a barrier with a tail, the last CTA to arrive runs `tail()`
-// (whole CTA) and then adds the one that releases the others. Returns false once any CTA has recorded an error.
-template <bool kHasTail, class Tail>
-__device__ bool grid_barrier(const GrowArgs& g, unsigned int& target, Tail tail) {
-    __shared__ unsigned int s_last;
-    __shared__ int s_failed;
-    const unsigned int arrived_all = target + gridDim.x;
-    target = arrived_all + (kHasTail ? 1u : 0u);
+// Grid barriers count arrivals on one word that only grows during the launch (the host zeroes it before): a
+// barrier is passed once the word reaches the running target, which every CTA advances identically by the grid
+// size, so the last arrival itself releases the others and a barrier costs one atomic and the poll that sees it.
+// The error word is polled alongside. Returns false once any CTA has recorded an error (or this one gave up).
+// A barrier can be split: barrier_arrive, then CTA-local work that needs no other CTA's results (it overlaps the
+// wait), then barrier_wait.
+__device__ __forceinline__ void barrier_arrive(const GrowArgs& g, unsigned int& target) {
+    target += gridDim.x;
     __syncthreads();  // the CTA's work (and its writes) are done
     if (threadIdx.x == 0) {
         __threadfence();
-        const unsigned int before = atomicAdd(g.barrier, 1u);
-        s_last = kHasTail && before == arrived_all - 1;
+        atomicAdd(g.barrier, 1u);
     }
-    __syncthreads();
-    if (kHasTail && s_last) {
-        __threadfence();
-        tail();
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            atomicAdd(g.barrier, 1u);
-            s_failed = failed(g);
-        }
-    } else if (threadIdx.x == 0) {
+}
+
+__device__ bool barrier_wait(const GrowArgs& g, unsigned int target) {
+    __shared__ int s_failed;
+    if (threadIdx.x == 0) {
         volatile unsigned int* count = g.barrier;
         volatile int* error = &g.t.iter->error;
         unsigned long long spins = 0;
         int failed_now = 0;
         // `count - target` as a signed difference: the count never runs more than one barrier ahead of a waiter.
-        // The error word is polled alongside: a CTA that gave up waiting stops the others without their timing out.
         while (true) {
             const unsigned int c = *count;
             failed_now = *error;
@@ -133,8 +125,6 @@ __device__ bool grid_barrier(const GrowArgs& g, unsigned int& target, Tail tail)
             __nanosleep(32);
         }
         __threadfence();
-        // An error the tail recorded before releasing is visible once the release is.
-        if (kHasTail && failed_now == 0) failed_now = failed(g);
         s_failed = failed_now;
     }
     __syncthreads();
@@ -142,7 +132,8 @@ __device__ bool grid_barrier(const GrowArgs& g, unsigned int& target, Tail tail)
 }
 
 __device__ __forceinline__ bool grid_barrier(const GrowArgs& g, unsigned int& target) {
-    return grid_barrier<false>(g, target, [] {});
+    barrier_arrive(g, target);
+    return barrier_wait(g, target);
 }
 
 __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) {
@@ -151,39 +142,71 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     const uint32_t cta = blockIdx.x, ctas = gridDim.x;
     const uint32_t warp = threadIdx.x >> 5, warps = kGrowThreads / 32;
     const uint32_t gwarp = cta * warps + warp, gwarps = ctas * warps;
+    const uint32_t F = a.num_features;
+    // Every CTA keeps the learner's control state itself: the step, the histogram job, the evaluated features. The
+    // finish runs in every CTA on the same inputs, so no CTA waits for another to publish the next step.
     __shared__ Step st;
     __shared__ HistJob job;
     __shared__ SearchCtx s;
+    __shared__ FinishShared fs;
     __shared__ PhaseClock clock;
+    __shared__ uint32_t s_left;
+    uint8_t* eval = reinterpret_cast<uint8_t*>(smem) + g.flags_offset;  // F: features this step searches
+    uint8_t* mask = eval + F;                                            // F: the iteration's feature mask
+    uint8_t* csplit = mask + F;                                          // 2 F: the children's splittable flags
     if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
     unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
     __shared__ HistCta hist_cta;
     histogram_prepare_cta(g.h, cta, smem, &hist_cta);
     const uint32_t round_rows = packed_round_rows(*g.h.spec);  // the iteration's quantization, set before the launch
+    // The root step, its job and features, as the iteration's start left them.
+    broadcast_cg(a.step, &st);
+    broadcast_cg(a.hist_job, &job);
+    {
+        const uint8_t* iter_mask = a.masks + static_cast<size_t>(a.iter->iteration) * F;
+        for (uint32_t f = threadIdx.x; f < F; f += kGrowThreads) {
+            eval[f] = a.evaluate[f];
+            mask[f] = iter_mask[f];
+        }
+    }
+    __syncthreads();
 
     for (int step = -1; step + 1 < a.max_leaves; ++step) {
         clock_step(g, clock, step);
-        broadcast_cg(a.step, &st);
         if (!st.active) break;
         if (!st.root) {
             // Zeros in the staging histogram (its previous contents were read before the last barrier): the
-            // direct histogram adds into it. The left count slot is written by the scatter.
+            // direct histogram adds into it.
             for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < a.total_bins + 1; i += ctas * kGrowThreads)
                 reinterpret_cast<int2*>(a.staging)[i] = make_int2(0, 0);
             partition_flags_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
             clock_mark(g, clock, 0);
             if (!grid_barrier(g, target)) return;
             clock_mark(g, clock, 6);
-            const uint32_t total_left = partition_scatter_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
-            if (cta == 0 && threadIdx.x == 0) partition_publish(a, *a.step, total_left);
+            const uint32_t left = partition_scatter_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
+            // The built child's job (partition_publish's), in every CTA.
+            if (threadIdx.x == 0) {
+                s_left = left;
+                HistJob j{};
+                j.active = st.may_search;
+                j.identity = 0;
+                j.which = (st.which & 1) ^ 1u;
+                j.begin = st.built_left ? st.begin : st.begin + left;
+                j.count = st.built_left ? left : st.count - left;
+                job = j;
+            }
             clock_mark(g, clock, 1);
-            if (!grid_barrier(g, target)) return;
+            barrier_arrive(g, target);
+            // While the other CTAs finish their scatter: the children's search context (it needs only the counts).
+            if (warp == 1) {
+                const SearchCtx c = search_context(a, st, static_cast<int64_t>(s_left), eval, mask);
+                if (lane_id() == 0) s = c;
+            }
+            if (!barrier_wait(g, target)) return;
             clock_mark(g, clock, 6);
-            broadcast_cg(a.step, &st);
         }
         // The new histogram (the root, or the smaller child): straight into staging for a small job, else per-CTA
         // shared histograms and their slab reduction. Then the search.
-        broadcast_cg(a.hist_job, &job);
         const bool direct = histogram_goes_direct(job.count, round_rows);
         clock_describe(g, clock, job.active ? job.count : 0u, direct, st.count);
         if (direct)
@@ -199,13 +222,24 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             if (!grid_barrier(g, target)) return;
             clock_mark(g, clock, 6);
         }
-        search_context_cta(a, st, &s);
+        if (st.root) {  // the root's sums come from its histogram
+            if (warp == 0) {
+                const SearchCtx c = search_context(a, st, 0, eval, mask);
+                if (threadIdx.x == 0) s = c;
+            }
+            __syncthreads();
+        }
         if (s.searched)
             for (uint32_t item = gwarp; item < search_items(a, st); item += gwarps)
                 search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
         clock_mark(g, clock, 4);
-        if (!grid_barrier<true>(g, target, [&] { search_finish(a, st, s); })) return;
-        clock_mark(g, clock, 5);  // the barrier with the finish in it
+        barrier_arrive(g, target);
+        // While the other CTAs finish their search: the parts of the finish that need no candidates.
+        search_finish_prepare(a, st, s, st.root ? 0u : s_left, cta, fs);
+        if (!barrier_wait(g, target)) return;
+        clock_mark(g, clock, 6);
+        search_finish_replicated(a, st, s, eval, mask, csplit, cta, fs);
+        clock_mark(g, clock, 5);
     }
 }
 
@@ -220,11 +254,12 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
 }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
+                             uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
     GrowArgs g{};
     g.t = t;
     g.h = h;
     g.barrier = barrier;
+    g.flags_offset = flags_offset;
     g.phase_ns = phase_ns;
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet

@@ -380,8 +380,10 @@ struct SearchCtx {
 };
 
 // LeafCtx of the step's children (learner.rs:285-336), computed by a whole warp (the root's sums are a warp
-// reduction); every lane gets the same values.
-__device__ SearchCtx search_context(const TrainArgs& a, const Step& st) {
+// reduction); every lane gets the same values. `left_global` is the left child's rows over every rank; `evaluate`
+// and `root_mask` the features the children and the root search (global or shared memory).
+__device__ SearchCtx search_context(const TrainArgs& a, const Step& st, int64_t left_global, const uint8_t* evaluate,
+                                    const uint8_t* root_mask) {
     const IterState& it = *a.iter;
     const double gs = it.spec.grad_scale, hs = it.spec.hess_scale;
     SearchCtx s{};
@@ -392,11 +394,11 @@ __device__ SearchCtx search_context(const TrainArgs& a, const Step& st) {
         s.ctx[0] = make_ctx(a.cfg, gs, hs, ug, uh, it.root_count);
         s.child[0] = 0;
         s.child[1] = -1;
-        s.evaluate = a.masks + static_cast<size_t>(it.iteration) * a.num_features;
+        s.evaluate = root_mask;
     } else {
-        s.left_global = static_cast<int64_t>(static_cast<uint32_t>(__ldcg(a.staging + 2 * a.total_bins)));
+        s.left_global = left_global;
         s.right_global = st.parent_count - s.left_global;
-        const int depth = __ldcg(&a.leaves[st.leaf].depth) + 1;
+        const int depth = st.depth + 1;
         s.searched = st.may_search && s.left_global > 0 && s.right_global > 0 &&
                      may_split(a, depth, s.left_global, s.right_global);
         const Ctx lc = make_ctx(a.cfg, gs, hs, st.info.left_grad, st.info.left_hess, s.left_global);
@@ -405,20 +407,28 @@ __device__ SearchCtx search_context(const TrainArgs& a, const Step& st) {
         s.child[1] = st.built_left ? st.new_leaf : st.leaf;
         s.ctx[0] = st.built_left ? lc : rc;
         s.ctx[1] = st.built_left ? rc : lc;
-        s.evaluate = a.evaluate;
+        s.evaluate = evaluate;
     }
     return s;
 }
 
-// search_context computed once per CTA (warp 0) into shared memory `out`; every thread then reads `*out`.
+// search_context computed once per CTA (warp 0) into shared memory `out`, with the left count and the features from
+// global memory (the standalone search: the count rides after the staging histogram, reduced over ranks); every
+// thread then reads `*out`.
 __device__ void search_context_cta(const TrainArgs& a, const Step& st, SearchCtx* out) {
     __syncthreads();  // every thread is done with the previous context
     if ((threadIdx.x >> 5) == 0) {
-        const SearchCtx s = search_context(a, st);
+        const int64_t left = st.root ? 0 : static_cast<int64_t>(static_cast<uint32_t>(__ldcg(a.staging + 2 * a.total_bins)));
+        const SearchCtx s = search_context(a, st, left, a.evaluate,
+                                           a.masks + static_cast<size_t>(a.iter->iteration) * a.num_features);
         if (threadIdx.x == 0) *out = s;
     }
     __syncthreads();
 }
+
+// A feature flag that may sit in shared memory (the persistent kernel's copies) or in global memory written earlier
+// in the same launch.
+__device__ __forceinline__ uint8_t load_flag(const uint8_t* p) { return __isShared(p) ? *p : __ldcg(p); }
 
 // Work items of a step's search: one per (child, feature), item = child * F + feature; the root has one child.
 __device__ __forceinline__ uint32_t search_items(const TrainArgs& a, const Step& st) {
@@ -436,7 +446,7 @@ __device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx&
     const uint32_t f = item % F, ch = item / F;
     FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
     const DevFeature feat = a.d.features[f];
-    if (!__ldcg(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
+    if (!load_flag(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
         if (lane == 0) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
@@ -561,6 +571,30 @@ __device__ __forceinline__ void left_bins_of(const sb2_split_info& info, const D
         bins[w] = t >= first + 31 ? 0xFFFFFFFFu : t >= first ? (0xFFFFFFFFu >> (31 - (t - first))) : 0u;
     }
     if (info.default_left && f.nan_bin) bins[(f.num_bins - 1) >> 5] |= 1u << ((f.num_bins - 1) & 31);
+}
+
+// The step that splits `leaf` (index `index`, its best split chosen; `f` the split's feature) into `index` and
+// `num_leaves`: Learner::split_leaf's inputs (learner.rs:249-275).
+__device__ Step next_step(const TrainArgs& a, const DevLeaf& leaf, int32_t index, int32_t num_leaves,
+                          const DevFeature& f) {
+    const sb2_split_info& info = leaf.best;
+    Step n{};
+    n.active = 1;
+    n.root = 0;
+    n.leaf = index;
+    n.new_leaf = num_leaves;
+    n.may_search = leaf.has_hist && num_leaves + 1 < a.max_leaves && depth_allows(a, leaf.depth + 1);
+    n.built_left = info.left_count <= info.right_count;
+    n.begin = leaf.begin;
+    n.count = leaf.count;
+    n.which = leaf.which;
+    n.depth = leaf.depth;
+    n.split_tile = static_cast<uint32_t>(f.tile);
+    n.split_lane = static_cast<uint32_t>(f.lane);
+    left_bins_of(info, f, n.left_bins);
+    n.parent_count = leaf.count_global;
+    n.info = info;
+    return n;
 }
 
 // After every item's candidate is written: the split applied to the tree and the leaves, each child's best split,
@@ -711,24 +745,219 @@ __device__ void search_finish(const TrainArgs& a, const Step& st, const SearchCt
             if (k < F) a.evaluate[k] = static_cast<uint8_t>(m[j] && o[j]);
         }
     }
-    if (lane == 0) {
-        Step n{};
-        n.active = 1;
-        n.root = 0;
-        n.leaf = best_leaf;
-        n.new_leaf = num_leaves;
-        n.may_search = leaf.has_hist && num_leaves + 1 < a.max_leaves && depth_allows(a, leaf.depth + 1);
-        n.built_left = info.left_count <= info.right_count;
-        n.begin = leaf.begin;
-        n.count = leaf.count;
-        n.which = leaf.which;
-        n.split_tile = static_cast<uint32_t>(f.tile);
-        n.split_lane = static_cast<uint32_t>(f.lane);
-        left_bins_of(info, f, n.left_bins);
-        n.parent_count = leaf.count_global;
-        n.info = info;
-        *next = n;
+    if (lane == 0) *next = next_step(a, leaf, best_leaf, num_leaves, f);
+}
+
+// The children's records and best splits as the persistent kernel's CTAs share them during a finish.
+struct FinishShared {
+    DevLeaf child[2];
+    sb2_split_info best[2];
+    int32_t has_best[2];
+    double other_gain;
+    int32_t other_leaf;
+};
+
+// Whether CTA `cta` writes part `part` of a finish (CTA `part`, or CTA 0 in a grid of fewer than four).
+__device__ __forceinline__ bool writes_part(uint32_t cta, uint32_t part) { return cta == (part < gridDim.x ? part : 0u); }
+
+// search_finish for the persistent kernel, run by every CTA: each reads the same candidates and records and reaches
+// the same next step, in its own shared memory. The part that does not need this step's candidates,
+// search_finish_prepare, runs while the CTA waits at the search barrier; search_finish_replicated runs after it.
+// `st` (in: this step; out: the next), `left` the left child's rows, `eval` (shared, F bytes) the next step's
+// evaluated features, from the iteration's `mask` (shared, F bytes), `csplit` (shared, 2 F bytes) the children's
+// splittable flags. Four CTAs also write what later steps and kernels read, one part each so that no CTA's finish
+// is much longer than the others': CTA 0 the tree (Tree::split), CTA 1 the leaf records and their gains
+// (TrainArgs::leaf_gain), CTA 2 the children's splittable rows, CTA 3 the evaluated features. Every CTA reads only
+// entries no CTA writes in the same step (leaves chosen before this step, and the candidates). One CTA of at least
+// 128 threads.
+__device__ void search_finish_prepare(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t left,
+                                      uint32_t cta, FinishShared& fs) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const IterState& it = *a.iter;
+    if (warp == 0) {
+        if (lane == 0) {
+            if (st.root) {
+                DevLeaf l = load_cg(a.leaves);  // begin, count, which, depth: set before the launch
+                l.units_grad = s.ctx[0].units_grad;
+                l.units_hess = s.ctx[0].units_hess;
+                l.count_global = it.root_count;
+                l.has_hist = s.searched;
+                l.has_best = 0;
+                fs.child[0] = l;
+            } else {
+                DevLeaf l{}, r{};
+                l.begin = st.begin;
+                l.count = left;
+                r.begin = st.begin + left;
+                r.count = st.count - left;
+                l.which = r.which = st.which ^ 1u;
+                l.depth = r.depth = st.depth + 1;
+                l.units_grad = st.info.left_grad;
+                l.units_hess = st.info.left_hess;
+                l.count_global = s.left_global;
+                r.units_grad = st.info.right_grad;
+                r.units_hess = st.info.right_hess;
+                r.count_global = s.right_global;
+                l.has_hist = r.has_hist = s.searched;
+                // child 0 is the built child: the left one (index st.leaf) when built_left
+                fs.child[st.built_left ? 0 : 1] = l;
+                fs.child[st.built_left ? 1 : 0] = r;
+                if (writes_part(cta, 0)) {
+                    if (s.left_global <= 0 || s.right_global <= 0) {
+                        a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
+                        a.iter->error_info = st.leaf;
+                    }
+                    const DevFeature f = a.d.features[st.info.feature];
+                    const int32_t nl = tree_split(a.tree, st.leaf, st.info, f, s.left_global, s.right_global,
+                                                  it.spec.hess_scale, a.cfg.min_gain_to_split);
+                    if (nl != st.new_leaf) {
+                        a.iter->error = 2;
+                        a.iter->error_info = nl;
+                    }
+                }
+            }
+        }
+    } else if (warp == 3) {
+        // Leaves that existed before this step, other than the one being split: their gains, as CTA 1 left them
+        // in earlier steps.
+        const int32_t before = st.root ? 0 : st.new_leaf;
+        double gain = -INFINITY;
+        int32_t leaf = -1;
+        for (int32_t l0 = 0; l0 < before; l0 += 128) {
+            double g[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int32_t l = l0 + 32 * j + static_cast<int32_t>(lane);
+                g[j] = l < before && l != st.leaf ? __ldcg(a.leaf_gain + l) : -INFINITY;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (g[j] != -INFINITY) prefer_leaf(gain, leaf, g[j], l0 + 32 * j + static_cast<int32_t>(lane));
+        }
+        for (int o = 16; o > 0; o >>= 1)
+            prefer_leaf(gain, leaf, __shfl_xor_sync(0xffffffffu, gain, o), __shfl_xor_sync(0xffffffffu, leaf, o));
+        if (lane == 0) {
+            fs.other_gain = gain;
+            fs.other_leaf = leaf;
+        }
     }
+    __syncthreads();
+}
+
+__device__ void search_finish_replicated(const TrainArgs& a, Step& st, const SearchCtx& s, uint8_t* eval,
+                                         const uint8_t* mask, uint8_t* csplit, uint32_t cta, FinishShared& fs) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t F = a.num_features;
+    const int children = st.root ? 1 : 2;
+    if (warp >= 1 && warp <= 2) {
+        const int ch = static_cast<int>(warp) - 1;
+        if (ch < children) {
+            // best_candidate's reduction, with the splittable flags kept in shared memory (and written to the
+            // child's row by CTA 2)
+            FeatureCandidate best{};
+            best.found = 0;
+            if (s.searched) {
+                const FeatureCandidate* cands = static_cast<const FeatureCandidate*>(a.candidates) +
+                                                static_cast<size_t>(ch) * F;
+                uint8_t* row = a.splittable + static_cast<size_t>(s.child[ch]) * F;
+                for (uint32_t f0 = 0; f0 < F; f0 += 128) {
+                    FeatureCandidate c[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t f = f0 + 32u * j + lane;
+                        if (f < F) c[j] = load_candidate(cands + f);
+                        else c[j].found = 0;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t f = f0 + 32u * j + lane;
+                        if (f < F) {
+                            const uint8_t ok = static_cast<uint8_t>(c[j].splittable);
+                            csplit[static_cast<size_t>(ch) * F + f] = ok;
+                            if (writes_part(cta, 2)) row[f] = ok;
+                            if (better(c[j], best)) best = c[j];
+                        }
+                    }
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                    FeatureCandidate other;
+                    const int src = lane ^ o;
+                    other.found = __shfl_sync(0xffffffffu, best.found, src);
+                    other.splittable = 0;
+                    other.feature = __shfl_sync(0xffffffffu, best.feature, src);
+                    other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
+                    other.gain = __shfl_sync(0xffffffffu, best.gain, src);
+                    other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
+                    other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
+                    other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
+                    other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
+                    other.left_count = shfl_i64(best.left_count, src);
+                    other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
+                    other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
+                    if (better(other, best)) best = other;
+                }
+            }
+            if (lane == 0) {
+                const bool has = best.found && s.ctx[ch].valid;
+                fs.has_best[ch] = has;
+                fs.best[ch] = has ? finish(s.ctx[ch], best, a.cfg) : sb2_split_info{};
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // Join: the children's best splits, then the best leaf over children and others.
+        if (lane < static_cast<uint32_t>(children)) {
+            fs.child[lane].has_best = fs.has_best[lane];
+            if (fs.has_best[lane]) fs.child[lane].best = fs.best[lane];
+        }
+        __syncwarp();
+        double gain = fs.other_gain;
+        int32_t best_leaf = fs.other_leaf;
+        for (int ch = 0; ch < children; ++ch)
+            if (fs.child[ch].has_best) prefer_leaf(gain, best_leaf, fs.child[ch].best.gain, s.child[ch]);
+        const int32_t num_leaves = st.root ? 1 : st.new_leaf + 1;
+        const bool go = best_leaf >= 0 && gain > 0.0 && num_leaves < a.max_leaves;
+        const int chosen = !go ? -1 : best_leaf == s.child[0] ? 0 : (children == 2 && best_leaf == s.child[1]) ? 1 : -1;
+        if (writes_part(cta, 1) && lane < static_cast<uint32_t>(children)) {
+            DevLeaf c = fs.child[lane];
+            if (static_cast<int>(lane) == chosen) c.has_best = 0;  // it is split next
+            a.leaves[s.child[lane]] = c;
+            a.leaf_gain[s.child[lane]] = c.has_best ? c.best.gain : -INFINITY;
+        }
+        if (go) {
+            DevLeaf leaf;
+            if (chosen >= 0) leaf = fs.child[chosen];
+            else leaf = load_cg(a.leaves + best_leaf);  // recorded by CTA 1 in an earlier step
+            const DevFeature f = a.d.features[leaf.best.feature];
+            // Features the children evaluate: the tree's mask and the parent's splittable ones (learner.rs:278-284).
+            // CTA 3 also leaves them in global memory, where the histograms read them (after two barriers).
+            const uint8_t* split_ok = chosen >= 0 ? csplit + static_cast<size_t>(chosen) * F
+                                                  : a.splittable + static_cast<size_t>(best_leaf) * F;
+            for (uint32_t k0 = 0; k0 < F; k0 += 128) {
+                uint8_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = k0 + 32u * j + lane;
+                    o[j] = k < F ? load_flag(split_ok + k) : 0;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = k0 + 32u * j + lane;
+                    if (k < F) {
+                        const uint8_t e = static_cast<uint8_t>(mask[k] && o[j]);
+                        eval[k] = e;
+                        if (writes_part(cta, 3)) a.evaluate[k] = e;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) st = next_step(a, leaf, best_leaf, num_leaves, f);
+        } else if (lane == 0) {
+            st.active = 0;
+        }
+    }
+    __syncthreads();
 }
 
 }  // namespace

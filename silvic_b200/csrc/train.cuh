@@ -36,6 +36,7 @@ struct Step {
     int32_t may_search;  // the children's histograms are built (learner.rs:266-268)
     int32_t built_left;  // the histogram is built for the left child (learner.rs:271-275)
     uint32_t begin, count, which;  // the parent's rows
+    int32_t depth;                 // the parent's depth
     uint32_t split_tile, split_lane;
     uint32_t left_bins[8];
     int64_t parent_count;
@@ -92,6 +93,7 @@ struct TrainArgs {
     uint32_t num_features;
     // learner state
     DevLeaf* leaves;            // [max_leaves]
+    double* leaf_gain;          // [max_leaves]: the persistent kernel's copy of each leaf's best gain (-inf: none)
     uint8_t* splittable;        // [max_leaves * num_features]
     Step* step;
     uint8_t* evaluate;          // [num_features]: the current step's evaluated features
@@ -142,8 +144,10 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // through the shared histograms (0), and the rows of the leaf it split.
 constexpr int kGrowPhases = 7;
 constexpr int kStepTrace = kGrowPhases + 3;
+// `flags_offset`: where in its dynamic shared memory (`smem_bytes`, at least flags_offset + 4 F) the kernel keeps
+// its per-feature flags.
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             cudaStream_t s, unsigned long long* phase_ns, int trace_steps);
+                             uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns, int trace_steps);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

@@ -297,6 +297,11 @@ int sb2_find_best_split_noalloc(sb2_backend* b, const int32_t* hist, size_t len,
                                 double hess_scale, const sb2_split_config* cfg, sb2_split_info* out,
                                 uint8_t* splittable);
 
+/* No counterpart in the reference: test access to the device split search's division (a correctly rounded FMA
+ * division that pipelines, where the library's runs its calls one after another). Compares it with CUDA's correctly
+ * rounded division on `count` operand pairs hashed from `seed` and returns the pairs where they differ. */
+int sb2_check_division(sb2_backend* b, uint64_t count, uint32_t seed, uint64_t* mismatches);
+
 /* ---- measurement -------------------------------------------------------------------------------------------- */
 
 /* Times `repeats` histograms of rows 0 .. rows - 1 (all rows when `rows` is 0) with every feature, as the trainer

@@ -93,7 +93,7 @@ struct sb2_backend {
     DeviceBuffer bins, d_tiles, d_features, d_lane_feature, d_units;
     DeviceBuffer label, weight, scores, grad, hess, packed;
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
-    DeviceBuffer staging, hist_job, step, iter, api_active, candidates, counter, maxima, misc;
+    DeviceBuffer staging, hist_job, step, iter, api_active, candidates, cand_flags, cand_gain, counter, maxima, misc;
     DeviceBuffer api_spec;                    // the QuantSpec of the last sb2_quantize
     sb2_quant_spec api_spec_host{};
     const sb2_quant_spec* packed_spec = nullptr;  // the quantization the packed gradients now hold
@@ -169,6 +169,8 @@ struct sb2_backend {
         a.flags = flags.as<uint32_t>();
         a.tile_left = tile_left.as<uint32_t>();
         a.candidates = candidates.ptr;
+        a.cand_flags = cand_flags.as<uint8_t>();
+        a.cand_gain = cand_gain.as<double>();
         a.done_counter = counter.as<unsigned int>();
         return a;
     }
@@ -531,13 +533,13 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
     // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
-    // Then its per-feature flags (4 F bytes) after everything the phases share.
+    // Then its per-feature flags (5 F bytes) after everything the phases share.
     {
         const size_t phases = std::max<size_t>({static_cast<size_t>(b->hist_smem),
                                                 static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8,
                                                 (2ull * grow_threads() + 64) * 4});
         b->grow_flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
-        b->grow_smem = static_cast<int>(b->grow_flags_offset + (4ull * F + 15) / 16 * 16);
+        b->grow_smem = static_cast<int>(b->grow_flags_offset + (5ull * F + 15) / 16 * 16);
     }
     int grow_per_sm = 0;
     SB2_CUDA(b, grow_configure(b->grow_smem, &grow_per_sm));
@@ -657,6 +659,8 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     b->api_spec_host = sb2_quant_spec{};
     b->packed_spec = b->api_spec.as<sb2_quant_spec>();  // the packed gradients start as zeros
     SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->cand_flags.alloc(2 * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->cand_gain.alloc(sizeof(double) * 2 * std::max<size_t>(F, 1)));
     SB2_CUDA(b, b->maxima.alloc(2 * sizeof(unsigned long long)));
     SB2_CUDA(b, b->grid_barrier.alloc(2 * sizeof(unsigned int)));
     SB2_CUDA(b, cudaMemsetAsync(b->grid_barrier.ptr, 0, 2 * sizeof(unsigned int), b->stream));
@@ -980,6 +984,21 @@ int sb2_find_best_split_noalloc(sb2_backend* b, const int32_t* hist, size_t len,
                           scratch + kNoAllocCounterBytes, counter, out, splittable, b->search_grid(), b->stream);
     SB2_CUDA(b, cudaGetLastError());
     return b->sync();
+}
+
+int sb2_check_division(sb2_backend* b, uint64_t count, uint32_t seed, uint64_t* mismatches) {
+    if (!b || !mismatches) return SB2_EDEVICE;
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    DeviceBuffer d;
+    SB2_CUDA(b, d.alloc(sizeof(unsigned long long)));
+    SB2_CUDA(b, cudaMemsetAsync(d.ptr, 0, sizeof(unsigned long long), b->stream));
+    launch_division_check(count, seed, d.as<unsigned long long>(), b->sms * 8, b->stream);
+    SB2_CUDA(b, cudaGetLastError());
+    unsigned long long n = 0;
+    SB2_CUDA(b, cudaMemcpyAsync(&n, d.ptr, sizeof(n), cudaMemcpyDeviceToHost, b->stream));
+    SB2_TRY(b->sync());
+    *mismatches = n;
+    return SB2_OK;
 }
 
 int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* seconds) {

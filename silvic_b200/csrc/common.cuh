@@ -116,6 +116,70 @@ __device__ __forceinline__ long long packed_to_wide(int32_t packed) {
     return (static_cast<long long>(h) << 32) + static_cast<long long>(g);
 }
 
+// ---- correctly rounded division in pipelined FMA operations -------------------------------------------------
+//
+// a / b rounded to nearest even, as IEEE 754 division. The split scan divides 16 times per lane per feature; the
+// library division runs those one after another at a few hundred cycles each, which made the scan a 10k-cycle
+// chain. This one is straight-line FMA code, so a lane's divisions overlap. Method (Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; Cornea, Harrison, Tang,
+// "Scientific Computing on Itanium-based Systems", 2002, ch. 8): a single-precision reciprocal seed refined by two
+// Newton-Raphson steps y <- y + y (1 - b y); the quotient q = a y, one correction q <- q + y (a - b q), which leaves
+// q within one ulp of a / b; then, since a - b q is exactly representable for such q (no underflow in the range
+// below) and one FMA computes it exactly, the correctly rounded quotient is whichever of q and its neighbour toward
+// a / b leaves the smaller |a - b q|, the even one on a tie. Operands outside the range where no step can overflow
+// or underflow, and NaN, infinities and zero divisors, take __ddiv_rn.
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Whether div_fast is exact for a / b: no step can overflow or underflow.
+__device__ __forceinline__ bool div_in_range(double a, double b) {
+    const double aa = fabs(a), ab = fabs(b);
+    return ab > 0x1p-120 && ab < 0x1p120 && aa < 0x1p500 && (aa > 0x1p-500 || aa == 0.0);
+}
+
+// The branch-free part of div_rn: a / b correctly rounded when div_in_range(a, b).
+__device__ __forceinline__ double div_fast(double a, double b) {
+    double y = static_cast<double>(rcp_approx(static_cast<float>(b)));
+    double e = __fma_rn(-b, y, 1.0);
+    y = __fma_rn(y, e, y);
+    e = __fma_rn(-b, y, 1.0);
+    y = __fma_rn(y, e, y);
+    double q = __dmul_rn(a, y);
+    q = __fma_rn(__fma_rn(-b, q, a), y, q);
+    const double r = __fma_rn(-b, q, a);  // exact
+    // a / b - q = r / b: the neighbour toward a / b is above q when r and b have the same sign; adjacent doubles of
+    // one sign are adjacent bit patterns (larger magnitude, larger pattern)
+    const bool up = (r > 0.0) == (b > 0.0);
+    const long long qb = __double_as_longlong(q);
+    const long long nb = q == 0.0 ? (up ? 1ll : static_cast<long long>(0x8000000000000001ull))
+                                  : ((q > 0.0) == up ? qb + 1 : qb - 1);
+    const double q2 = __longlong_as_double(nb);
+    const double r2 = __fma_rn(-b, q2, a);  // exact
+    const double m = fabs(r), m2 = fabs(r2);
+    return m2 < m || (m2 == m && (__double_as_longlong(q2) & 1) == 0) ? q2 : q;
+}
+
+__device__ __forceinline__ double div_rn(double a, double b) { return div_in_range(a, b) ? div_fast(a, b) : __ddiv_rn(a, b); }
+
+// N divisions issued together (their fast paths overlap), then the library division for any pair outside the range.
+template <int N>
+__device__ __forceinline__ void div_rn_batch(const double (&a)[N], const double (&b)[N], double (&q)[N]) {
+    bool slow = false;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        slow |= !div_in_range(a[j], b[j]);
+        q[j] = div_fast(a[j], b[j]);
+    }
+    if (slow) {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (!div_in_range(a[j], b[j])) q[j] = __ddiv_rn(a[j], b[j]);
+    }
+}
+
 // ---- launch helpers ------------------------------------------------------------------------------------------
 
 __host__ __device__ __forceinline__ uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }

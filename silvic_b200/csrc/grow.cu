@@ -34,7 +34,7 @@ struct GrowArgs {
     unsigned int* barrier;        // arrivals at grid barriers so far (zeroed before the launch)
     unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
-    uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (4 F bytes)
+    uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (5 F bytes)
 };
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
@@ -99,10 +99,9 @@ __device__ __forceinline__ void broadcast_cg(const T* p, T* shared_copy) {
 __device__ __forceinline__ void barrier_arrive(const GrowArgs& g, unsigned int& target) {
     target += gridDim.x;
     __syncthreads();  // the CTA's work (and its writes) are done
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(g.barrier, 1u);
-    }
+    // A release reduction: the CTA's writes are visible GPU-wide before its arrival is, and nothing waits for a
+    // return value.
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(g.barrier) : "memory");
 }
 
 __device__ bool barrier_wait(const GrowArgs& g, unsigned int target) {
@@ -141,7 +140,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     const TrainArgs& a = g.t;
     const uint32_t cta = blockIdx.x, ctas = gridDim.x;
     const uint32_t warp = threadIdx.x >> 5, warps = kGrowThreads / 32;
-    const uint32_t gwarp = cta * warps + warp, gwarps = ctas * warps;
+    // Search items go round the CTAs first (item i to warp i / ctas of CTA i mod ctas), so a step's few hundred
+    // scans spread over every SM instead of filling a dozen.
+    const uint32_t item0 = warp * ctas + cta, items_stride = ctas * warps;
     const uint32_t F = a.num_features;
     // Every CTA keeps the learner's control state itself: the step, the histogram job, the evaluated features. The
     // finish runs in every CTA on the same inputs, so no CTA waits for another to publish the next step.
@@ -154,6 +155,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     uint8_t* eval = reinterpret_cast<uint8_t*>(smem) + g.flags_offset;  // F: features this step searches
     uint8_t* mask = eval + F;                                            // F: the iteration's feature mask
     uint8_t* csplit = mask + F;                                          // 2 F: the children's splittable flags
+    uint8_t* osplit = csplit + 2 * F;                                    // F: the best other leaf's
     if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
     unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
     __shared__ HistCta hist_cta;
@@ -230,15 +232,15 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             __syncthreads();
         }
         if (s.searched)
-            for (uint32_t item = gwarp; item < search_items(a, st); item += gwarps)
+            for (uint32_t item = item0; item < search_items(a, st); item += items_stride)
                 search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
         clock_mark(g, clock, 4);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.
-        search_finish_prepare(a, st, s, st.root ? 0u : s_left, cta, fs);
+        search_finish_prepare(a, st, s, st.root ? 0u : s_left, cta, osplit, fs);
         if (!barrier_wait(g, target)) return;
         clock_mark(g, clock, 6);
-        search_finish_replicated(a, st, s, eval, mask, csplit, cta, fs);
+        search_finish_replicated(a, st, s, eval, mask, csplit, osplit, cta, fs);
         clock_mark(g, clock, 5);
     }
 }

@@ -483,6 +483,41 @@ __global__ void fill_kernel(float* out, uint64_t n, float value) {
         out[i] = value;
 }
 
+// A double from hashed bits: sign, an exponent in [-span, span] around 0 (biased), and a mantissa that is random or
+// one of the awkward patterns (all zeros, all ones, a single bit).
+__device__ double division_operand(uint32_t h0, uint32_t h1, uint32_t h2, int span) {
+    uint64_t mant = (static_cast<uint64_t>(h1) << 32 | h2) & ((1ull << 52) - 1);
+    switch (h0 & 15) {
+        case 0: mant = 0; break;
+        case 1: mant = (1ull << 52) - 1; break;
+        case 2: mant = 1ull << (h1 % 52); break;
+        default: break;
+    }
+    const int exp = static_cast<int>((h0 >> 8) % static_cast<uint32_t>(2 * span + 1)) - span;
+    const uint64_t bits = (static_cast<uint64_t>(h0 >> 4 & 1) << 63) | (static_cast<uint64_t>(exp + 1023) << 52) | mant;
+    return __longlong_as_double(static_cast<long long>(bits));
+}
+
+// div_rn against the library's correctly rounded division on `n` hashed operand pairs: most in the range the
+// split scan divides in, some wide of it (they take the library path), exact quotients and zero numerators.
+__global__ void division_check_kernel(uint64_t n, uint32_t seed, unsigned long long* mismatches) {
+    unsigned long long bad = 0;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t k = mix32(seed ^ mix32(static_cast<uint32_t>(i) ^ mix32(static_cast<uint32_t>(i >> 32))));
+        const uint32_t h[6] = {mix32(k ^ 1u), mix32(k ^ 2u), mix32(k ^ 3u), mix32(k ^ 4u), mix32(k ^ 5u), mix32(k ^ 6u)};
+        const int span_a = (k & 7) == 0 ? 700 : 80, span_b = (k & 7) == 1 ? 200 : 60;
+        double b = division_operand(h[0], h[1], h[2], span_b);
+        double a = division_operand(h[3], h[4], h[5], span_a);
+        if ((k >> 3 & 31) == 0) a = __dmul_rn(b, static_cast<double>(h[4] & 0xFFFFF));  // exact quotients
+        if ((k >> 3 & 31) == 1) a = 0.0;
+        const double q = div_rn(a, b), want = __ddiv_rn(a, b);
+        const bool same = __double_as_longlong(q) == __double_as_longlong(want) || (q != q && want != want);
+        bad += same ? 0 : 1;
+    }
+    if (bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace
 
 void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) { gradients_kernel<<<grid, kRowThreads, 0, s>>>(a); }
@@ -520,6 +555,10 @@ void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint3
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s) {
     const int grid = static_cast<int>(n / 256 + 1 < 65535 ? n / 256 + 1 : 65535);
     fill_kernel<<<grid, 256, 0, s>>>(out, n, value);
+}
+
+void launch_division_check(uint64_t n, uint32_t seed, unsigned long long* mismatches, int grid, cudaStream_t s) {
+    division_check_kernel<<<grid, 256, 0, s>>>(n, seed, mismatches);
 }
 
 }  // namespace sb2

@@ -24,7 +24,7 @@ constexpr int kPerLane = kMaxBins / 32;
 __device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ double dsub(double a, double b) { return __dsub_rn(a, b); }
 __device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
-__device__ __forceinline__ double ddiv(double a, double b) { return __ddiv_rn(a, b); }
+__device__ __forceinline__ double ddiv(double a, double b) { return div_rn(a, b); }
 
 __device__ __forceinline__ int64_t sat_f64_i64(double q) {
     if (q != q) return 0;
@@ -143,23 +143,36 @@ __device__ Grown warp_scan(const int2* hist, int top, bool reverse, int m, const
         }
     }
     for (int o = 16; o > 0; o >>= 1) first_break = min(first_break, __shfl_xor_sync(0xffffffffu, first_break, o));
-    // Gains of the candidates before the break (ScanBuffer::evaluate).
+    // Gains of the candidates before the break (ScanBuffer::evaluate): leaf_gain(sum - left) + leaf_gain(left), each
+    // r^2 / (h + l2) with r = max(|g| - l1, 0), computed for every bin without branches so that the divisions of
+    // four bins issue together; bins past the break or skipped keep -inf.
     double gain[kPerLane];
     double mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) {
-        const int k = lane * kPerLane + i;
-        gain[i] = -INFINITY;
-        if (k < first_break) {
+    for (int i0 = 0; i0 < kPerLane; i0 += 4) {
+        double num[8], den[8], q[8];
+        bool use[4], window[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j, k = lane * kPerLane + i;
             const double uh = static_cast<double>(H[i]);
             const double hh = dadd(kEpsilon, dmul(uh, x.hs));
             const bool skip = C[i] < min_count || hh < c.min_sum_hessian_in_leaf || uh <= 0.0;
-            if (!skip) {
-                const double g = dmul(static_cast<double>(G[i]), x.gs);
-                gain[i] = dadd(leaf_gain(dsub(x.sum_grad, g), dsub(x.sum_hess, hh), c.lambda_l1, c.lambda_l2),
-                               leaf_gain(g, hh, c.lambda_l1, c.lambda_l2));
-            }
-            mx = fmax(mx, gain[i]);
+            window[j] = k < first_break;
+            use[j] = window[j] && !skip;
+            const double g = dmul(static_cast<double>(G[i]), x.gs);
+            const double rl = fmax(dsub(fabs(dsub(x.sum_grad, g)), c.lambda_l1), 0.0);
+            const double rr = fmax(dsub(fabs(g), c.lambda_l1), 0.0);
+            num[2 * j] = dmul(rl, rl);
+            den[2 * j] = dadd(dsub(x.sum_hess, hh), c.lambda_l2);
+            num[2 * j + 1] = dmul(rr, rr);
+            den[2 * j + 1] = dadd(hh, c.lambda_l2);
+        }
+        div_rn_batch(num, den, q);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            gain[i0 + j] = use[j] ? dadd(q[2 * j], q[2 * j + 1]) : -INFINITY;
+            if (window[j]) mx = fmax(mx, gain[i0 + j]);
         }
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -452,6 +465,10 @@ __device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx&
             none.feature = static_cast<int32_t>(f);
             cands[f] = none;
             cands[F + f] = none;
+            if (a.cand_flags) {
+                a.cand_flags[f] = 0;
+                a.cand_flags[F + f] = 0;
+            }
         }
         return;
     }
@@ -498,10 +515,15 @@ __device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx&
     const FeatureCandidate c = scan_feature(buf, feat, static_cast<int>(f), s.ctx[ch], a.cfg);
     if (lane == 0) {
         cands[static_cast<size_t>(ch) * F + f] = c;
+        if (a.cand_flags) {  // what the persistent kernel's finish compares, apart from the full candidate
+            a.cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
+            a.cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
+        }
         if (st.root) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
             cands[F + f] = none;
+            if (a.cand_flags) a.cand_flags[F + f] = 0;
         }
     }
     __syncwarp();
@@ -755,6 +777,7 @@ struct FinishShared {
     int32_t has_best[2];
     double other_gain;
     int32_t other_leaf;
+    DevLeaf other;  // the record of other_leaf (when there is one)
 };
 
 // Whether CTA `cta` writes part `part` of a finish (CTA `part`, or CTA 0 in a grid of fewer than four).
@@ -771,7 +794,7 @@ __device__ __forceinline__ bool writes_part(uint32_t cta, uint32_t part) { retur
 // entries no CTA writes in the same step (leaves chosen before this step, and the candidates). One CTA of at least
 // 128 threads.
 __device__ void search_finish_prepare(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t left,
-                                      uint32_t cta, FinishShared& fs) {
+                                      uint32_t cta, uint8_t* osplit, FinishShared& fs) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const IterState& it = *a.iter;
     if (warp == 0) {
@@ -840,62 +863,88 @@ __device__ void search_finish_prepare(const TrainArgs& a, const Step& st, const 
             fs.other_gain = gain;
             fs.other_leaf = leaf;
         }
+        // Its record and splittable row, in case it is split next (CTA 1 and CTA 2 wrote them in earlier steps).
+        if (leaf >= 0) {
+            if (lane == 0) fs.other = load_cg(a.leaves + leaf);
+            const uint32_t F = a.num_features;
+            const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
+            for (uint32_t k0 = 0; k0 < F; k0 += 128) {
+                uint8_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = k0 + 32u * j + lane;
+                    o[j] = k < F ? __ldcg(row + k) : 0;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = k0 + 32u * j + lane;
+                    if (k < F) osplit[k] = o[j];
+                }
+            }
+        }
     }
     __syncthreads();
 }
 
 __device__ void search_finish_replicated(const TrainArgs& a, Step& st, const SearchCtx& s, uint8_t* eval,
-                                         const uint8_t* mask, uint8_t* csplit, uint32_t cta, FinishShared& fs) {
+                                         const uint8_t* mask, uint8_t* csplit, const uint8_t* osplit, uint32_t cta,
+                                         FinishShared& fs) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t F = a.num_features;
     const int children = st.root ? 1 : 2;
     if (warp >= 1 && warp <= 2) {
         const int ch = static_cast<int>(warp) - 1;
         if (ch < children) {
-            // best_candidate's reduction, with the splittable flags kept in shared memory (and written to the
-            // child's row by CTA 2)
+            // The best candidate of the child over every feature by `better` (found, then the higher gain, then the
+            // lower feature), from the compact gains and flags; then the winner's full candidate. The splittable
+            // flags go to shared memory (and to the child's row, by CTA 2).
             FeatureCandidate best{};
             best.found = 0;
             if (s.searched) {
-                const FeatureCandidate* cands = static_cast<const FeatureCandidate*>(a.candidates) +
-                                                static_cast<size_t>(ch) * F;
+                const uint8_t* flags = a.cand_flags + static_cast<size_t>(ch) * F;
+                const double* gains = a.cand_gain + static_cast<size_t>(ch) * F;
                 uint8_t* row = a.splittable + static_cast<size_t>(s.child[ch]) * F;
+                int found = 0;
+                double bg = -INFINITY;
+                int32_t bf = -1;
                 for (uint32_t f0 = 0; f0 < F; f0 += 128) {
-                    FeatureCandidate c[4];
+                    uint8_t fl[4];
+                    double gn[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint32_t f = f0 + 32u * j + lane;
-                        if (f < F) c[j] = load_candidate(cands + f);
-                        else c[j].found = 0;
+                        fl[j] = f < F ? __ldcg(flags + f) : 0;
+                        gn[j] = f < F ? __ldcg(gains + f) : 0.0;
                     }
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint32_t f = f0 + 32u * j + lane;
-                        if (f < F) {
-                            const uint8_t ok = static_cast<uint8_t>(c[j].splittable);
-                            csplit[static_cast<size_t>(ch) * F + f] = ok;
-                            if (writes_part(cta, 2)) row[f] = ok;
-                            if (better(c[j], best)) best = c[j];
+                        if (f >= F) continue;
+                        const uint8_t ok = static_cast<uint8_t>((fl[j] >> 1) & 1);
+                        csplit[static_cast<size_t>(ch) * F + f] = ok;
+                        if (writes_part(cta, 2)) row[f] = ok;
+                        if (fl[j] & 1) {
+                            const double g = gn[j] != gn[j] ? -INFINITY : gn[j];  // `better` reads NaN as -inf
+                            if (!found || g > bg) {  // features rise with f: on equal gains the earlier stays
+                                found = 1;
+                                bg = g;
+                                bf = static_cast<int32_t>(f);
+                            }
                         }
                     }
                 }
                 for (int o = 16; o > 0; o >>= 1) {
-                    FeatureCandidate other;
-                    const int src = lane ^ o;
-                    other.found = __shfl_sync(0xffffffffu, best.found, src);
-                    other.splittable = 0;
-                    other.feature = __shfl_sync(0xffffffffu, best.feature, src);
-                    other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
-                    other.gain = __shfl_sync(0xffffffffu, best.gain, src);
-                    other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
-                    other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
-                    other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
-                    other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
-                    other.left_count = shfl_i64(best.left_count, src);
-                    other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
-                    other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
-                    if (better(other, best)) best = other;
+                    const int of = __shfl_xor_sync(0xffffffffu, found, o);
+                    const double og = __shfl_xor_sync(0xffffffffu, bg, o);
+                    const int32_t obf = __shfl_xor_sync(0xffffffffu, bf, o);
+                    if (of && (!found || og > bg || (og == bg && obf < bf))) {
+                        found = 1;
+                        bg = og;
+                        bf = obf;
+                    }
                 }
+                if (found) best = load_candidate(static_cast<const FeatureCandidate*>(a.candidates) +
+                                                 static_cast<size_t>(ch) * F + bf);
             }
             if (lane == 0) {
                 const bool has = best.found && s.ctx[ch].valid;
@@ -926,20 +975,18 @@ __device__ void search_finish_replicated(const TrainArgs& a, Step& st, const Sea
             a.leaf_gain[s.child[lane]] = c.has_best ? c.best.gain : -INFINITY;
         }
         if (go) {
-            DevLeaf leaf;
-            if (chosen >= 0) leaf = fs.child[chosen];
-            else leaf = load_cg(a.leaves + best_leaf);  // recorded by CTA 1 in an earlier step
+            // the chosen leaf: a child, or the best other leaf (prefetched by search_finish_prepare)
+            const DevLeaf leaf = chosen >= 0 ? fs.child[chosen] : fs.other;
             const DevFeature f = a.d.features[leaf.best.feature];
             // Features the children evaluate: the tree's mask and the parent's splittable ones (learner.rs:278-284).
             // CTA 3 also leaves them in global memory, where the histograms read them (after two barriers).
-            const uint8_t* split_ok = chosen >= 0 ? csplit + static_cast<size_t>(chosen) * F
-                                                  : a.splittable + static_cast<size_t>(best_leaf) * F;
+            const uint8_t* split_ok = chosen >= 0 ? csplit + static_cast<size_t>(chosen) * F : osplit;
             for (uint32_t k0 = 0; k0 < F; k0 += 128) {
                 uint8_t o[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t k = k0 + 32u * j + lane;
-                    o[j] = k < F ? load_flag(split_ok + k) : 0;
+                    o[j] = k < F ? split_ok[k] : 0;
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {

@@ -110,6 +110,8 @@ struct TrainArgs {
     uint32_t* tile_left;        // left count per partition tile
     // per-(child, feature) scan results and the search kernel's completion counter
     void* candidates;
+    uint8_t* cand_flags;        // [2 F]: bit 0 the candidate was found, bit 1 its feature stays splittable
+    double* cand_gain;          // [2 F]: its gain (what `better` compares)
     unsigned int* done_counter;
 };
 
@@ -144,7 +146,7 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // through the shared histograms (0), and the rows of the leaf it split.
 constexpr int kGrowPhases = 7;
 constexpr int kStepTrace = kGrowPhases + 3;
-// `flags_offset`: where in its dynamic shared memory (`smem_bytes`, at least flags_offset + 4 F) the kernel keeps
+// `flags_offset`: where in its dynamic shared memory (`smem_bytes`, at least flags_offset + 5 F) the kernel keeps
 // its per-feature flags.
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
                              uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns, int trace_steps);

@@ -199,6 +199,22 @@ def test_split_search_matches_oracle(device, case):
     b.close()
 
 
+def test_split_division_is_correctly_rounded(device):
+    """The split scan's FMA division equals CUDA's correctly rounded division bit for bit (so the gains equal the
+    CPU's IEEE divisions) on 2^27 hashed operand pairs: random and awkward mantissas, exact quotients, zero
+    numerators, and operands outside its fast range."""
+    import ctypes as C
+
+    b = B200Backend(0)
+    try:
+        for seed in (1, 20261107):
+            bad = C.c_uint64()
+            b._check(b._lib.sb2_check_division(b._h, 1 << 27, seed, C.byref(bad)))
+            assert bad.value == 0, f"seed {seed}: {bad.value} mismatches"
+    finally:
+        b.close()
+
+
 TRAIN_CASES = [
     ("l2_small", [255] * 10 + [17, 2], 20_000, dict(objective=_abi.REGRESSION, num_leaves=31, num_iterations=8)),
     ("l2_depth", [63] * 12, 15_000, dict(objective=_abi.REGRESSION, num_leaves=63, max_depth=4, num_iterations=5)),

@@ -86,6 +86,7 @@ struct sb2_backend {
     int hist_smem = 0;
     int hist_grid = 0;
     int grow_smem = 0;      // dynamic shared memory of the persistent tree kernel
+    uint32_t grow_scan_offset = 0;   // where in it the partition's scan words start
     uint32_t grow_flags_offset = 0;  // where in it the kernel's per-feature flags start
     bool grow_ok = false;   // it fits one CTA per SM
     DeviceBuffer grid_barrier;
@@ -533,11 +534,12 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
     // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
-    // Then its per-feature flags (5 F bytes) after everything the phases share.
+    // Layout: the histogram's arrays, the partition's scan words after them (both used in the same phase), then the
+    // per-feature flags (5 F bytes); the search's per-warp bins reuse the start.
     {
-        const size_t phases = std::max<size_t>({static_cast<size_t>(b->hist_smem),
-                                                static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8,
-                                                (2ull * grow_threads() + 64) * 4});
+        b->grow_scan_offset = static_cast<uint32_t>((b->hist_smem + 15) / 16 * 16);
+        const size_t phases = std::max<size_t>(b->grow_scan_offset + (2ull * grow_threads() + 64) * 4,
+                                               static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8);
         b->grow_flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
         b->grow_smem = static_cast<int>(b->grow_flags_offset + (5ull * F + 15) / 16 * 16);
     }
@@ -612,13 +614,16 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * (n / 32 + 2)));
     SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * kMaxPartitionCtas));
     SB2_CUDA(b, b->staging.alloc(sizeof(int) * (2ull * b->total_bins + 2)));
+    // A slab holds one unit's histogram (the standalone kernels, one unit per CTA) or every unit's (the persistent
+    // tree kernel, where a CTA histograms every unit of its rows).
     b->slab_ints = 0;
-    for (const Unit& u : b->units) b->slab_ints = std::max(b->slab_ints, 2 * u.slots);
+    for (const Unit& u : b->units) b->slab_ints += 2 * u.slots;
     // The reduction's quads: per unit, per tile, four consecutive slots (one bin, lanes l .. l + 3).
     std::vector<QuadMeta> quads;
+    uint32_t units_before = 0;  // slots of the earlier units
     for (uint32_t ui = 0; ui < b->units.size(); ++ui) {
         const Unit& u = b->units[ui];
-        uint32_t off = 0;
+        uint32_t off = 0, poff = 0;
         for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
             const Tile& tile = b->tiles[t];
             const uint32_t n = tile.smem_bins * tile.stride;
@@ -627,6 +632,9 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 m.unit = ui;
                 m.g_off = off + s;
                 m.h_off = off + n + s;
+                m.p_off = poff + s;
+                m.unit_off = 2 * units_before;
+                m.unit_off_packed = units_before;
                 const uint32_t bin = s / tile.stride, lane0 = s % tile.stride;
                 for (uint32_t i = 0; i < 4; ++i) {
                     const int32_t f = lane_feature[t * kTileLanes + lane0 + i];
@@ -637,7 +645,9 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 quads.push_back(m);
             }
             off += 2 * n;
+            poff += n;
         }
+        units_before += u.slots;
     }
     b->num_quads = static_cast<uint32_t>(quads.size());
     // Threads per quad: as many as keep every thread of one histogram grid busy, up to a warp.
@@ -1078,7 +1088,7 @@ namespace {
 
 struct TrainBuffers {
     DeviceBuffer leaves, leaf_gain, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records,
-        record_bufs;
+        record_bufs, cursors;
 };
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
@@ -1182,7 +1192,7 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
         // One launch grows the whole tree (grow.cu).
         SB2_TRY(op(kOpTree, [&] {
             return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
-                                            b->grow_smem, b->grow_flags_offset, s,
+                                            b->grow_smem, b->grow_scan_offset, b->grow_flags_offset, s,
                                             timer ? b->phase_ns.as<unsigned long long>() : nullptr,
                                             timer ? max_leaves : 0),
                            "cudaLaunchCooperativeKernel(grow_tree)");
@@ -1254,6 +1264,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     TrainBuffers& tb = tr.tb;
     SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
     SB2_CUDA(b, tb.leaf_gain.alloc(sizeof(double) * L));
+    SB2_CUDA(b, tb.cursors.alloc(sizeof(unsigned int) * 2 * L));
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.masks.alloc(static_cast<size_t>(std::max(iters, 1)) * std::max<uint32_t>(F, 1)));
@@ -1306,6 +1317,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     t.num_iterations = iters;
     t.leaves = tb.leaves.as<DevLeaf>();
     t.leaf_gain = tb.leaf_gain.as<double>();
+    t.cursors = tb.cursors.as<unsigned int>();
     t.splittable = tb.splittable.as<uint8_t>();
     t.evaluate = tb.evaluate.as<uint8_t>();
     t.masks = tb.masks.as<uint8_t>();

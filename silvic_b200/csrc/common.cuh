@@ -116,6 +116,10 @@ __device__ __forceinline__ long long packed_to_wide(int32_t packed) {
     return (static_cast<long long>(h) << 32) + static_cast<long long>(g);
 }
 
+// A feature flag that may sit in shared memory (the persistent kernel's copies) or in global memory written earlier
+// in the same launch (read past the SM's L1).
+__device__ __forceinline__ uint8_t load_flag(const uint8_t* p) { return __isShared(p) ? *p : __ldcg(p); }
+
 // ---- correctly rounded division in pipelined FMA operations -------------------------------------------------
 //
 // a / b rounded to nearest even, as IEEE 754 division. The split scan divides 16 times per lane per feature; the

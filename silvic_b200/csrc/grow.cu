@@ -17,8 +17,7 @@
 // error. Data another CTA wrote in the same launch is read with ld.global.cg (past the SM's L1).
 #include <cuda_runtime.h>
 
-#include "hist_device.cuh"
-#include "partition.cuh"
+#include "fused.cuh"
 #include "search.cuh"
 
 namespace sb2 {
@@ -35,6 +34,8 @@ struct GrowArgs {
     unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
     uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (5 F bytes)
+    uint32_t scan_offset;         // ... of the partition's scan words (2 kHistThreads + 64), past the histogram
+    uint32_t pad_;
 };
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
@@ -70,11 +71,11 @@ __device__ __forceinline__ void clock_step(const GrowArgs& g, PhaseClock& c, int
     c.row = step + 1 < g.trace_steps ? g.phase_ns + kGrowPhases + static_cast<size_t>(step + 1) * kStepTrace : nullptr;
 }
 
-__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, bool direct,
+__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, bool packed,
                                                uint32_t leaf_rows) {
     if (!clock_owner(g) || c.row == nullptr) return;
     c.row[kGrowPhases] = job_rows;
-    c.row[kGrowPhases + 1] = direct;
+    c.row[kGrowPhases + 1] = packed;
     c.row[kGrowPhases + 2] = leaf_rows;
 }
 
@@ -144,26 +145,31 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     // scans spread over every SM instead of filling a dozen.
     const uint32_t item0 = warp * ctas + cta, items_stride = ctas * warps;
     const uint32_t F = a.num_features;
-    // Every CTA keeps the learner's control state itself: the step, the histogram job, the evaluated features. The
-    // finish runs in every CTA on the same inputs, so no CTA waits for another to publish the next step.
+    // Every CTA keeps the learner's control state itself: the step, the evaluated features. The finish runs in
+    // every CTA on the same inputs, so no CTA waits for another to publish the next step.
     __shared__ Step st;
-    __shared__ HistJob job;
+    __shared__ HistJob root_job;
     __shared__ SearchCtx s;
     __shared__ FinishShared fs;
     __shared__ PhaseClock clock;
     __shared__ uint32_t s_left;
+    uint32_t* scan = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(smem) + g.scan_offset);
     uint8_t* eval = reinterpret_cast<uint8_t*>(smem) + g.flags_offset;  // F: features this step searches
     uint8_t* mask = eval + F;                                            // F: the iteration's feature mask
     uint8_t* csplit = mask + F;                                          // 2 F: the children's splittable flags
     uint8_t* osplit = csplit + 2 * F;                                    // F: the best other leaf's
     if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
     unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
-    __shared__ HistCta hist_cta;
-    histogram_prepare_cta(g.h, cta, smem, &hist_cta);
+    // The first units' descriptions, kept for the launch; later units are described per use.
+    constexpr uint32_t kUnitCache = 2;
+    __shared__ HistCta units[kUnitCache];
+    __shared__ HistCta spare;
+    const uint32_t cached = g.h.num_units < kUnitCache ? g.h.num_units : kUnitCache;
+    for (uint32_t u = 0; u < cached; ++u) histogram_prepare_unit(g.h, u, smem, units + u);
     const uint32_t round_rows = packed_round_rows(*g.h.spec);  // the iteration's quantization, set before the launch
     // The root step, its job and features, as the iteration's start left them.
     broadcast_cg(a.step, &st);
-    broadcast_cg(a.hist_job, &job);
+    broadcast_cg(a.hist_job, &root_job);
     {
         const uint8_t* iter_mask = a.masks + static_cast<size_t>(a.iter->iteration) * F;
         for (uint32_t f = threadIdx.x; f < F; f += kGrowThreads) {
@@ -176,72 +182,59 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     for (int step = -1; step + 1 < a.max_leaves; ++step) {
         clock_step(g, clock, step);
         if (!st.active) break;
-        if (!st.root) {
-            // Zeros in the staging histogram (its previous contents were read before the last barrier): the
-            // direct histogram adds into it.
-            for (uint32_t i = cta * kGrowThreads + threadIdx.x; i < a.total_bins + 1; i += ctas * kGrowThreads)
-                reinterpret_cast<int2*>(a.staging)[i] = make_int2(0, 0);
-            partition_flags_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
-            clock_mark(g, clock, 0);
-            if (!grid_barrier(g, target)) return;
-            clock_mark(g, clock, 6);
-            const uint32_t left = partition_scatter_cta(a, st, cta, ctas, reinterpret_cast<uint32_t*>(smem));
-            // The built child's job (partition_publish's), in every CTA.
-            if (threadIdx.x == 0) {
-                s_left = left;
-                HistJob j{};
-                j.active = st.may_search;
-                j.identity = 0;
-                j.which = (st.which & 1) ^ 1u;
-                j.begin = st.built_left ? st.begin : st.begin + left;
-                j.count = st.built_left ? left : st.count - left;
-                job = j;
-            }
+        // Phase A: the parent's partition and the built child's histogram into the slabs (the root: its histogram).
+        FusedStep f{};
+        f.root = st.root;
+        f.count = st.root ? root_job.count : st.count;
+        f.begin = st.root ? 0u : st.begin;
+        f.src = st.which & 1;
+        f.dst = f.src ^ 1u;
+        f.built_left = st.built_left;
+        f.histogram = st.root ? root_job.active != 0 : st.may_search != 0;
+        f.chunks = fused_chunks(f.count, ctas);
+        f.round_rows = round_rows;
+        f.packed = fused_packed(f.count, f.chunks, round_rows);
+        unsigned int* cursor = a.cursors + 2 * (st.root ? 0 : st.new_leaf);
+        clock_describe(g, clock, f.histogram ? f.count : 0u, f.packed, st.count);
+        fused_step_cta(a, g.h, st, f, cta, smem, scan, cursor, eval, units, cached, &spare);
+        clock_mark(g, clock, 0);
+        if (!grid_barrier(g, target)) return;
+        clock_mark(g, clock, 4);
+        // The left count, then the slab reduction into staging; the children's search context meanwhile.
+        if (!st.root && threadIdx.x == 0) s_left = __ldcg(cursor);
+        __syncthreads();
+        if (f.histogram) {
+            fused_reduce(g.h, f.chunks, f.packed, cta * kGrowThreads + threadIdx.x, ctas * kGrowThreads);
             clock_mark(g, clock, 1);
             barrier_arrive(g, target);
-            // While the other CTAs finish their scatter: the children's search context (it needs only the counts).
-            if (warp == 1) {
+            if (!st.root && warp == 1) {
                 const SearchCtx c = search_context(a, st, static_cast<int64_t>(s_left), eval, mask);
                 if (lane_id() == 0) s = c;
             }
             if (!barrier_wait(g, target)) return;
-            clock_mark(g, clock, 6);
-        }
-        // The new histogram (the root, or the smaller child): straight into staging for a small job, else per-CTA
-        // shared histograms and their slab reduction. Then the search.
-        const bool direct = histogram_goes_direct(job.count, round_rows);
-        clock_describe(g, clock, job.active ? job.count : 0u, direct, st.count);
-        if (direct)
-            histogram_direct_cta(g.h, job, cta, ctas);
-        else
-            histogram_cta(g.h, job, cta, smem, hist_cta, round_rows);
-        clock_mark(g, clock, 2);
-        if (!grid_barrier(g, target)) return;
-        clock_mark(g, clock, 6);
-        if (!direct) {
-            histogram_reduce_quads(g.h, job, cta * kGrowThreads + threadIdx.x, ctas * kGrowThreads);
-            clock_mark(g, clock, 3);
-            if (!grid_barrier(g, target)) return;
-            clock_mark(g, clock, 6);
+            clock_mark(g, clock, 4);
+        } else if (!st.root && warp == 1) {
+            const SearchCtx c = search_context(a, st, static_cast<int64_t>(s_left), eval, mask);
+            if (lane_id() == 0) s = c;
         }
         if (st.root) {  // the root's sums come from its histogram
             if (warp == 0) {
                 const SearchCtx c = search_context(a, st, 0, eval, mask);
                 if (threadIdx.x == 0) s = c;
             }
-            __syncthreads();
         }
+        __syncthreads();
         if (s.searched)
             for (uint32_t item = item0; item < search_items(a, st); item += items_stride)
                 search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
-        clock_mark(g, clock, 4);
+        clock_mark(g, clock, 2);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.
         search_finish_prepare(a, st, s, st.root ? 0u : s_left, cta, osplit, fs);
         if (!barrier_wait(g, target)) return;
-        clock_mark(g, clock, 6);
+        clock_mark(g, clock, 4);
         search_finish_replicated(a, st, s, eval, mask, csplit, osplit, cta, fs);
-        clock_mark(g, clock, 5);
+        clock_mark(g, clock, 3);
     }
 }
 
@@ -256,15 +249,20 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
 }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
+                             uint32_t scan_offset, uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns,
+                             int trace_steps) {
     GrowArgs g{};
     g.t = t;
     g.h = h;
     g.barrier = barrier;
+    g.scan_offset = scan_offset;
     g.flags_offset = flags_offset;
     g.phase_ns = phase_ns;
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet
+    if (e != cudaSuccess) return e;
+    // every step's placement cursors start at zero
+    e = cudaMemsetAsync(t.cursors, 0, sizeof(unsigned int) * 2 * static_cast<size_t>(t.max_leaves), s);
     if (e != cudaSuccess) return e;
     void* args[] = {&g};
     return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(grow_tree_kernel), dim3(grid), dim3(kGrowThreads),

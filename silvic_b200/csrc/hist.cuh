@@ -41,15 +41,19 @@ struct HistJob {
     uint32_t pad_;
 };
 
-// Four consecutive gradient slots of one tile (one bin, four feature lanes) as the reduction sums them: their
-// offsets in a slab of the unit, and the output pair index of each lane (hist_offset + bin), -1 for a lane without
-// a feature or a bin past the feature's bins. Built at load.
+// Four consecutive gradient slots of one tile (one bin, four feature lanes) as the reductions sum them: their
+// offsets in a unit's slab region (unpacked: per tile a gradient array then a hessian array; packed: the tiles'
+// packed arrays in a row, as in shared memory), where the unit's region starts when one slab holds every unit, and
+// the output pair index of each lane (hist_offset + bin), -1 for a lane without a feature or a bin past the
+// feature's bins. Built at load.
 struct QuadMeta {
     uint32_t unit;
-    uint32_t g_off;   // ints from the slab's start to the gradient slot
+    uint32_t g_off;   // ints from the unit's slab region to the gradient slot
     uint32_t h_off;   // ... to the hessian slot
+    uint32_t p_off;   // ... to the packed slot, in a region that holds packed sums (one int per slot)
     int32_t out[4];
-    uint32_t pad_;
+    uint32_t unit_off;         // where the unit's region starts in a slab holding every unit: 2 * earlier slots
+    uint32_t unit_off_packed;  // ... in a packed slab holding every unit: earlier slots
 };
 
 struct HistArgs {
@@ -65,7 +69,7 @@ struct HistArgs {
     const sb2_quant_spec* spec;   // the quantization of the packed gradients (bounds their per-bin sums)
     int* out;                     // 2 * total_bins int32: the wanted features' bins are overwritten
     int* slabs;                   // scratch: one slab of slab_ints per CTA of the launch
-    uint32_t slab_ints;           // 2 * the largest unit's slots
+    uint32_t slab_ints;           // 2 * every unit's slots
     uint32_t num_quads;           // every unit's slots in fours
     const QuadMeta* quads;
     uint32_t quad_split;          // threads per quad in the reduction (a power of two <= 32)

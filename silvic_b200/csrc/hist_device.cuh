@@ -146,9 +146,10 @@ struct HistCta {
     int32_t lane_feature[kMaxUnitTiles][kTileLanes];
 };
 
-// Fills `c` for CTA `cta` (whole CTA; `sh` is the dynamic shared memory the histogram will use).
-inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, const int* sh, HistCta* c) {
-    if (threadIdx.x == 0) c->unit = a.units[unit_of_cta(a, cta)];
+// Fills `c` for unit `u` (whole CTA; `sh` is the dynamic shared memory the histogram will use).
+inline __device__ void histogram_prepare_unit(const HistArgs& a, uint32_t u, const int* sh, HistCta* c) {
+    __syncthreads();  // every thread is done with the previous contents
+    if (threadIdx.x == 0) c->unit = a.units[u];
     __syncthreads();
     const Unit unit = c->unit;
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -172,6 +173,11 @@ inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, co
         }
     }
     __syncthreads();
+}
+
+// Fills `c` for the unit of histogram CTA `cta` (the standalone kernels: one unit per CTA).
+inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, const int* sh, HistCta* c) {
+    histogram_prepare_unit(a, unit_of_cta(a, cta), sh, c);
 }
 
 // Unpacks the packed shared histogram `sh` of the unit into the CTA's slab: per tile, its slots' g into the slab's

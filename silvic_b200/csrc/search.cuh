@@ -439,9 +439,6 @@ __device__ void search_context_cta(const TrainArgs& a, const Step& st, SearchCtx
     __syncthreads();
 }
 
-// A feature flag that may sit in shared memory (the persistent kernel's copies) or in global memory written earlier
-// in the same launch.
-__device__ __forceinline__ uint8_t load_flag(const uint8_t* p) { return __isShared(p) ? *p : __ldcg(p); }
 
 // Work items of a step's search: one per (child, feature), item = child * F + feature; the root has one child.
 __device__ __forceinline__ uint32_t search_items(const TrainArgs& a, const Step& st) {

@@ -108,6 +108,7 @@ struct TrainArgs {
     int32_t* ordered[2];
     uint32_t* flags;            // one bit per partition position
     uint32_t* tile_left;        // left count per partition tile
+    unsigned int* cursors;      // [2 * max_leaves]: the persistent kernel's placement counters per step
     // per-(child, feature) scan results and the search kernel's completion counter
     void* candidates;
     uint8_t* cand_flags;        // [2 F]: bit 0 the candidate was found, bit 1 its feature stays splittable
@@ -139,17 +140,18 @@ constexpr int kSearchThreads = 256;   // 8 warps, one feature each
 // The persistent tree kernel (grow.cu): every step of one tree in one cooperative launch.
 int grow_threads();
 cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
-// `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: partition flags,
-// scatter, histogram, slab reduction, search, the barrier that runs the finish, the other barriers. With
-// `trace_steps` > 0 it is followed by one row of kStepTrace values per step (up to trace_steps): the same phase
-// times of that step, then the rows of its histogram job, whether the job went straight to the output (1) or
-// through the shared histograms (0), and the rows of the leaf it split.
-constexpr int kGrowPhases = 7;
+// `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: the partition with
+// the built child's histogram, the slab reduction, the search, the finish, the grid barriers. With `trace_steps` > 0
+// it is followed by one row of kStepTrace values per step (up to trace_steps): the same phase times of that step,
+// then the rows of its histogram, whether the slabs held packed sums (1) or unpacked ones (0), and the rows of the
+// leaf it split.
+constexpr int kGrowPhases = 5;
 constexpr int kStepTrace = kGrowPhases + 3;
-// `flags_offset`: where in its dynamic shared memory (`smem_bytes`, at least flags_offset + 5 F) the kernel keeps
-// its per-feature flags.
+// Its dynamic shared memory (`smem_bytes`): the histogram's arrays first, the partition's scan words (2 * 512 + 64)
+// at `scan_offset`, its per-feature flags (5 F bytes) at `flags_offset`.
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns, int trace_steps);
+                             uint32_t scan_offset, uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns,
+                             int trace_steps);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

@@ -48,6 +48,9 @@ MAX_BIN = 255
 SAMPLE_ROWS = 200_000
 PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
 METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
+# DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
+# case of the same workload (the traffic grows with the rows): profiles/grow_tree_kernel_2m.md. None until measured.
+TREE_TRAFFIC_PER_ROW = None
 
 
 # ---- synthetic data (torch on the GPU as plumbing) ------------------------------------------------------------
@@ -232,6 +235,28 @@ def measured_peak_hbm() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, max_leaves: int) -> int:
+    """Bytes one tree's growth must move at the least (one GPU, `n_rows` rows of `row_bytes` bin bytes).
+
+    The root histogram reads every row's bins and packed gradient (its rows are in row order: no row ids) and writes
+    a histogram of `total_bins` [g, h] int32 pairs. Split k of a parent of P rows reads each row's id (not for the
+    root's rows), packed gradient and byte of the split feature, and writes id and gradient to the other partition
+    buffer; while more splits may follow (k + 2 < max_leaves) it also histograms the smaller child's B rows: their ids,
+    gradients and bins, and the histogram out. Split k is internal node k (nodes are numbered in split order).
+    """
+    def count(c: int) -> int:
+        return int(tree.internal_count[c]) if c >= 0 else int(tree.leaf_count[~c])
+
+    total = n_rows * (row_bytes + 4) + 8 * total_bins
+    for k in range(len(tree.internal_count)):
+        parent = int(tree.internal_count[k])
+        total += parent * ((0 if k == 0 else 4) + 4 + 1) + parent * 8
+        if k + 2 < max_leaves:
+            built = min(count(int(tree.left_child[k])), count(int(tree.right_child[k])))
+            total += built * (row_bytes + 8) + 8 * total_bins
+    return total
+
+
 def oracle_rate(data, iterations: int, params) -> tuple[float, list[float], int]:
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_lib as orc
@@ -318,7 +343,11 @@ def run_b200(args, rank: int, world: int):
     secs = model.iteration_seconds
     timed = float(sum(secs[args.warmup:args.warmup + args.steps]))
     trees = len(model.trees)
-    # Roofline of the dominant kernel: the root histogram (every row, every feature).
+    # The tree kernel's own launches in the timed region (one GPU: one cooperative launch per tree, CUDA events on
+    # the backend's stream around each).
+    tree_s = model.tree_seconds[args.warmup:args.warmup + args.steps]
+    timed_trees = model.trees[args.warmup:args.warmup + args.steps]
+    # The standalone root histogram (every row, every feature), the kernel the multi-GPU path runs per split.
     hist_s = backend.time_histogram(10)
     backend.close()
     launches_persistent = world == 1  # one GPU grows each tree in one cooperative launch
@@ -353,9 +382,28 @@ def run_b200(args, rank: int, world: int):
     n_local = end - begin
     S = sum(g.row_stride for g in data.groups)
     T = data.total_bins
-    bytes_root = n_local * (S + 4 + 4) + 8 * T  # algorithmic bytes of one root histogram launch
+    bytes_root = n_local * (S + 4) + 8 * T  # algorithmic bytes of one root histogram launch (rows in row order)
     peak, peak_kind = measured_peak_hbm()
-    achieved = bytes_root / hist_s / 1e9
+    hist_roofline = {"kernel": "histogram_kernel + slab reduction (root: every row, every feature)",
+                     "achieved": bytes_root / hist_s / 1e9, "launch_ms": hist_s * 1000.0,
+                     "algorithmic_bytes": bytes_root}
+    hist_roofline["frac"] = hist_roofline["achieved"] / peak
+    if tree_s and len(tree_s) == len(timed_trees):
+        # The dominant kernel: the persistent tree kernel, one launch per tree.
+        tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, PARAMS["num_leaves"]) for tr in timed_trees]
+        launch_s = sum(tree_s) / len(tree_s)
+        per_launch = sum(tree_bytes) / len(tree_bytes)
+        roofline = {"bound": "hbm", "achieved": per_launch / launch_s / 1e9, "peak": peak, "unit": "GB/s",
+                    "peak_kind": peak_kind,
+                    "traffic": None if TREE_TRAFFIC_PER_ROW is None else TREE_TRAFFIC_PER_ROW * n_local,
+                    "kernel": "grow_tree_kernel (one cooperative launch grows one tree)",
+                    "launch_ms": launch_s * 1000.0, "algorithmic_bytes": per_launch,
+                    "share_of_step": sum(tree_s) / timed, "root_histogram": hist_roofline}
+    else:
+        roofline = {"bound": "hbm", "achieved": hist_roofline["achieved"], "peak": peak, "unit": "GB/s",
+                    "peak_kind": peak_kind, "traffic": None, "kernel": hist_roofline["kernel"],
+                    "launch_ms": hist_roofline["launch_ms"], "algorithmic_bytes": bytes_root}
+    roofline["frac"] = roofline["achieved"] / peak
     line = {
         "metric": METRIC,
         "value": args.steps / timed,
@@ -374,10 +422,7 @@ def run_b200(args, rank: int, world: int):
                    "l2": "inputs (1 GB binned) larger than L2; no flush"},
         "trees": trees,
         "hist_rows_feats_per_s": n_local * FEATURES / hist_s * world,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                     "kernel": "histogram_kernel (root: every row, every feature)",
-                     "launch_ms": hist_s * 1000.0, "algorithmic_bytes": bytes_root},
+        "roofline": roofline,
         "clocks": clocks.summary(),
         "e2e": {"value": args.steps / e2e_s, "unit": "iters/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},

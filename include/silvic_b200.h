@@ -350,6 +350,10 @@ int sb2_model_num_trees(const sb2_model* m);
 int sb2_model_tree(const sb2_model* m, int index, sb2_tree_view* out);
 /* Seconds the device spent in each of the last sb2_train's iterations (CUDA events), and split steps taken. */
 int sb2_model_iteration_seconds(const sb2_model* m, double* out, size_t len);
+/* Seconds of each iteration's persistent tree kernel launch alone (CUDA events on the backend's stream around the
+ * launch; single GPU, 0 entries otherwise); returns how many there are. No counterpart in the reference: the
+ * roofline of the kernel that grows the trees. */
+int sb2_model_tree_seconds(const sb2_model* m, double* out, size_t len);
 
 #ifdef __cplusplus
 }

@@ -234,6 +234,7 @@ SIGNATURES = {
     "sb2_model_num_trees": (C.c_int, [VP]),
     "sb2_model_tree": (C.c_int, [VP, C.c_int, P(TreeView)]),
     "sb2_model_iteration_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
+    "sb2_model_tree_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
 }
 
 _lib = None

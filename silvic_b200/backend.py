@@ -9,7 +9,7 @@ running every boosting iteration on the device (`sb2_train`).
 from __future__ import annotations
 
 import ctypes as C
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 
@@ -334,6 +334,7 @@ class Model:
     trees: list[Tree]
     init_score: float
     iteration_seconds: list[float]
+    tree_seconds: list[float] = field(default_factory=list)  # the tree kernel's own time per iteration (1 GPU)
 
     @staticmethod
     def from_handle(lib, handle, init_score: float) -> "Model":
@@ -344,7 +345,9 @@ class Model:
             trees.append(Tree.from_view(v))
         secs = (C.c_double * 100000)()
         k = lib.sb2_model_iteration_seconds(handle, secs, 100000)
-        return Model(trees, init_score, list(secs[: min(k, 100000)]))
+        tsecs = (C.c_double * 100000)()
+        kt = lib.sb2_model_tree_seconds(handle, tsecs, 100000)
+        return Model(trees, init_score, list(secs[: min(k, 100000)]), list(tsecs[: min(kt, 100000)]))
 
     def predict_raw_row(self, row: np.ndarray) -> float:
         """Model::predict_raw_row (crates/silvic-core/src/model/predict.rs:19-23): f64 sum of leaf values."""

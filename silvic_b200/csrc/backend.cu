@@ -62,11 +62,13 @@ struct HostTree {
 struct sb2_model {
     std::vector<HostTree> trees;
     std::vector<double> seconds;
+    std::vector<double> tree_seconds;  // the persistent tree kernel's own time per iteration (single GPU)
 };
 
 struct sb2_backend {
     int device = 0;
     int sms = 148;
+    int smem_optin = 232448;  // shared memory a CTA may hold (static and dynamic)
     cudaStream_t stream = nullptr;
     std::string error;
     std::string name;
@@ -85,9 +87,7 @@ struct sb2_backend {
     std::vector<std::vector<int32_t>> group_column_feature;  // [group][column] -> feature
     int hist_smem = 0;
     int hist_grid = 0;
-    int grow_smem = 0;      // dynamic shared memory of the persistent tree kernel
-    uint32_t grow_scan_offset = 0;   // where in it the partition's scan words start
-    uint32_t grow_flags_offset = 0;  // where in it the kernel's per-feature flags start
+    GrowSmem grow_smem{};   // the persistent tree kernel's dynamic shared memory
     bool grow_ok = false;   // it fits one CTA per SM
     DeviceBuffer grid_barrier;
     DeviceBuffer phase_ns;  // per-phase nanoseconds of the persistent kernel (profiling runs)
@@ -398,6 +398,7 @@ int sb2_create(int device, sb2_backend** out) {
         return SB2_EUNSUPPORTED;
     }
     b->sms = prop.multiProcessorCount;
+    b->smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
     b->name = std::string(prop.name) + " (cuda sm_" + std::to_string(prop.major) + std::to_string(prop.minor) + ")";
     *out = b.release();
     return SB2_OK;
@@ -534,17 +535,34 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
     // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
-    // Layout: the histogram's arrays, the partition's scan words after them (both used in the same phase), then the
-    // per-feature flags (5 F bytes); the search's per-warp bins reuse the start.
+    // Layout (GrowSmem): the histogram's arrays, the partition's scan words, the histogram's staging slots (all three
+    // used in the same phase), then the per-feature flags (5 F bytes); the search's per-warp bins reuse the start.
+    // Staging gets what is left of the CTA's shared memory, up to kMaxStageDepth slots per warp.
     {
-        b->grow_scan_offset = static_cast<uint32_t>((b->hist_smem + 15) / 16 * 16);
-        const size_t phases = std::max<size_t>(b->grow_scan_offset + (2ull * grow_threads() + 64) * 4,
+        GrowSmem& m = b->grow_smem;
+        m.scan_offset = static_cast<uint32_t>((b->hist_smem + 15) / 16 * 16);
+        m.stage_offset = static_cast<uint32_t>((m.scan_offset + (2ull * grow_threads() + 64) * 4 + 127) / 128 * 128);
+        uint32_t slot = 0;
+        for (const Unit& u : b->units) {
+            uint32_t rows = 0;
+            for (uint32_t t = 0; t < u.num_tiles; ++t) rows += 32 * b->tiles[u.first_tile + t].stride;
+            slot = std::max(slot, rows);
+        }
+        m.slot_bytes = (slot + 128 + 127) / 128 * 128;  // the rows, then 32 packed gradients
+        const size_t flags = (5ull * F + 15) / 16 * 16;
+        const int stat = grow_static_smem();
+        if (stat < 0) return b->fail(SB2_EDEVICE, "cudaFuncGetAttributes(grow_tree)");
+        const size_t limit = static_cast<size_t>(b->smem_optin) - static_cast<size_t>(stat);
+        const size_t per_depth = static_cast<size_t>(grow_threads() / 32) * m.slot_bytes;
+        const size_t used = m.stage_offset + flags;
+        m.stage_depth = used < limit ? static_cast<uint32_t>(std::min<size_t>((limit - used) / per_depth, kMaxStageDepth)) : 0;
+        const size_t phases = std::max<size_t>(m.stage_offset + m.stage_depth * per_depth,
                                                static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8);
-        b->grow_flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
-        b->grow_smem = static_cast<int>(b->grow_flags_offset + (5ull * F + 15) / 16 * 16);
+        m.flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
+        m.bytes = static_cast<int>(m.flags_offset + flags);
     }
     int grow_per_sm = 0;
-    SB2_CUDA(b, grow_configure(b->grow_smem, &grow_per_sm));
+    SB2_CUDA(b, grow_configure(b->grow_smem.bytes, &grow_per_sm));
     b->grow_ok = grow_per_sm >= 1;
     if (b->grow_ok) per_sm = std::min(per_sm, grow_per_sm);  // one grid for both paths: the units' CTA ranges
     // CTAs in proportion to each unit's features (its share of the atomics), at least one each.
@@ -1159,8 +1177,10 @@ struct OpTimer {
     }
 };
 
-// One boosting iteration's launches (the body the CUDA graph captures); `timer` brackets each operation.
-int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTimer* timer) {
+// One boosting iteration's launches (the body the CUDA graph captures); `timer` brackets each operation, and
+// `tree_marks` (optional) the persistent tree kernel.
+int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTimer* timer,
+                      const cudaEvent_t* tree_marks = nullptr) {
     cudaStream_t s = b->stream;
     const TrainArgs& t = ia.t;
     const int row_grid = b->row_grid();
@@ -1191,11 +1211,14 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
     if (b->persistent()) {
         // One launch grows the whole tree (grow.cu).
         SB2_TRY(op(kOpTree, [&] {
-            return b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
-                                            b->grow_smem, b->grow_scan_offset, b->grow_flags_offset, s,
-                                            timer ? b->phase_ns.as<unsigned long long>() : nullptr,
-                                            timer ? max_leaves : 0),
-                           "cudaLaunchCooperativeKernel(grow_tree)");
+            if (tree_marks) cudaEventRecord(tree_marks[0], s);
+            const int st = b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
+                                                    b->grow_smem, s,
+                                                    timer ? b->phase_ns.as<unsigned long long>() : nullptr,
+                                                    timer ? max_leaves : 0),
+                                   "cudaLaunchCooperativeKernel(grow_tree)");
+            if (tree_marks) cudaEventRecord(tree_marks[1], s);
+            return st;
         }));
         max_leaves = 1;  // no separate split steps
     } else {
@@ -1428,7 +1451,8 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
         cudaGraphDestroy(graph);
         SB2_CUDA(b, ce);
     }
-    std::vector<cudaEvent_t> events(iters + 1);
+    // events[0 .. iters]: iteration boundaries; then, single GPU, a pair per iteration around the tree kernel
+    std::vector<cudaEvent_t> events(iters + 1 + (exec ? 0 : 2 * iters));
     for (auto& e : events) cudaEventCreate(&e);
     cudaEventRecord(events[0], b->stream);
     int launch_status = SB2_OK;
@@ -1437,7 +1461,7 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
             ce = cudaGraphLaunch(exec, b->stream);
             if (ce != cudaSuccess) break;
         } else {
-            launch_status = enqueue_iteration(b, tr.ia, L, nullptr);
+            launch_status = enqueue_iteration(b, tr.ia, L, nullptr, &events[iters + 1 + 2 * i]);
             if (launch_status != SB2_OK) break;
         }
         cudaEventRecord(events[i + 1], b->stream);
@@ -1454,6 +1478,10 @@ int sb2_train(sb2_backend* b, const sb2_params* p, double init_score, sb2_model*
             float ms = 0.0f;
             cudaEventElapsedTime(&ms, events[i], events[i + 1]);
             model->seconds.push_back(ms / 1000.0);
+            if (!exec) {
+                cudaEventElapsedTime(&ms, events[iters + 1 + 2 * i], events[iters + 2 + 2 * i]);
+                model->tree_seconds.push_back(ms / 1000.0);
+            }
         }
     }
     for (auto& e : events) cudaEventDestroy(e);
@@ -1608,6 +1636,12 @@ int sb2_model_iteration_seconds(const sb2_model* m, double* out, size_t len) {
     size_t k = std::min(len, m->seconds.size());
     std::copy(m->seconds.begin(), m->seconds.begin() + k, out);
     return static_cast<int>(m->seconds.size());
+}
+
+int sb2_model_tree_seconds(const sb2_model* m, double* out, size_t len) {
+    size_t k = std::min(len, m->tree_seconds.size());
+    std::copy(m->tree_seconds.begin(), m->tree_seconds.begin() + k, out);
+    return static_cast<int>(m->tree_seconds.size());
 }
 
 }  // extern "C"

@@ -7,9 +7,13 @@
 // reference's stable order: partition.cuh.) The kernel therefore places rows without a grid-wide prefix. Each CTA
 // of the step takes a range of the parent's positions, counts its lefts and rights, reserves room for them with one
 // atomic per side on the step's cursors (lefts fill the parent's range from its start, rights from its end) and
-// scatters its rows into the other partition buffer; in the same pass it adds its rows that go to the built child
-// into its shared histogram, unit by unit, and flushes that to its slab. The grid meets once, after which the slabs
-// are reduced and the children searched.
+// scatters its rows into the other partition buffer. Its rows of the built child are then one contiguous range of
+// that buffer, which the CTA histograms itself, every lane busy, and flushes to its slab. The grid meets once, after
+// which the slabs are reduced and the children searched.
+//
+// The histogram streams its rows' bins into shared memory with cp.async: each warp keeps `depth` batches of 32 rows
+// in flight in its own staging slots while it adds an earlier batch, so the gathers of a leaf's scattered rows
+// overlap the shared atomics instead of waiting for them.
 //
 // A CTA's packed shared sums are exact for at most `round_rows` rows (packed_round_rows); when its range is that
 // short it flushes the packed sums as they are (half the bytes) and the reduction unpacks them, else it flushes
@@ -18,10 +22,11 @@
 
 #include "hist_device.cuh"
 #include "partition.cuh"
+#include "train.cuh"
 
 namespace sb2 {
 
-constexpr uint32_t kFusedMinRows = 1024;  // parent positions per CTA at the least: small leaves use fewer CTAs
+constexpr uint32_t kFusedMinRows = 512;   // parent positions per CTA at the least: small leaves use fewer CTAs
 constexpr uint32_t kFusedScanWords = kHistThreads;  // words per scatter round: one per thread of the CTA scan
 
 // CTAs that take part in a phase over `count` positions, and CTA `cta`'s range [lo, hi) of them (whole words of
@@ -90,6 +95,8 @@ __device__ __forceinline__ bool fused_unit_begin(const HistCta& c, const uint8_t
         if (lane == 0) {
             LaneTile l = c.tiles[warp];
             l.active = bits;
+            l.stage_off = 0;  // the tile's rows in a staging slot: after the earlier tiles' 32 rows each
+            for (uint32_t t = 0; t < warp; ++t) l.stage_off += 32 * c.tiles[t].stride;
             lt[warp] = l;
         }
     }
@@ -113,6 +120,204 @@ __device__ __forceinline__ void fused_unit_flush(const HistCta& c, int4* sh4, ui
     __syncthreads();
 }
 
+// ---- staged histogram rows ---------------------------------------------------------------------------------
+
+// An L2 policy that evicts a histogram's bin rows first: they are read once, and the partition buffers, leaf
+// histograms and metadata the next phases read should stay.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint64_t pol) {
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint64_t pol) {
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Waits until at most `pending` of the thread's newest copy groups are outstanding (pending < kMaxStageDepth).
+__device__ __forceinline__ void cp_async_wait(uint32_t pending) {
+    switch (pending) {
+        case 0:
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            break;
+        case 1:
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            break;
+        case 2:
+            asm volatile("cp.async.wait_group 2;" ::: "memory");
+            break;
+        default:
+            asm volatile("cp.async.wait_group 3;" ::: "memory");
+            break;
+    }
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v)); }
+
+// Staging slot of a batch: per tile, 32 rows of `stride` bytes (lane k's row at k * stride), then the batch's 32
+// packed gradients. A 32-byte row's two halves are swapped on lanes with bit 2 set, so that the eight lanes of a
+// 128-bit shared load hit 32 different banks.
+__device__ __forceinline__ uint32_t stage_swap(uint32_t lane) { return (lane >> 2) & 1u; }
+
+// Lane's copies of row `row`'s bytes of every wanted tile into slot `slot`.
+__device__ __forceinline__ void stage_row(const LaneTile* lt, uint32_t nt, uint32_t slot, uint32_t row,
+                                          uint32_t lane, uint64_t pol) {
+#pragma unroll
+    for (int t = 0; t < kMaxUnitTiles; ++t) {
+        if (t >= static_cast<int>(nt)) break;
+        const LaneTile l = lt[t];
+        if (l.active == 0) continue;
+        const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.stride;
+        const uint32_t dst = slot + l.stage_off + lane * l.stride;
+        switch (l.stride) {
+            case 32: {
+                const uint32_t sw = stage_swap(lane);
+                cp_async16(dst + 16 * sw, src, pol);
+                cp_async16(dst + 16 * (sw ^ 1u), src + 16, pol);
+                break;
+            }
+            case 16:
+                cp_async16(dst, src, pol);
+                break;
+            case 8:
+                cp_async8(dst, src, pol);
+                break;
+            default:
+                cp_async4(dst, src, pol);
+                break;
+        }
+    }
+}
+
+// Adds the lane's staged row of slot `slot` (packed gradient `packed`, nonzero) at every wanted tile.
+__device__ __forceinline__ void add_staged(const LaneTile* lt, uint32_t nt, uint32_t slot, uint32_t packed,
+                                           uint32_t lane) {
+#pragma unroll
+    for (int t = 0; t < kMaxUnitTiles; ++t) {
+        if (t >= static_cast<int>(nt)) break;
+        const LaneTile l = lt[t];
+        if (l.active == 0) continue;
+        const uint32_t a = slot + l.stage_off + lane * l.stride;
+        uint32_t w[8];
+        switch (l.stride) {
+            case 32: {
+                const uint32_t sw = stage_swap(lane);
+                const uint4 x = lds128(a + 16 * sw), y = lds128(a + 16 * (sw ^ 1u));
+                w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w, w[4] = y.x, w[5] = y.y, w[6] = y.z, w[7] = y.w;
+                add_row<8>(l, w, packed, lane);
+                break;
+            }
+            case 16: {
+                const uint4 x = lds128(a);
+                w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w;
+                add_row<4>(l, w, packed, lane);
+                break;
+            }
+            case 8: {
+                const uint2 x = lds64(a);
+                w[0] = x.x, w[1] = x.y;
+                add_row<2>(l, w, packed, lane);
+                break;
+            }
+            default:
+                w[0] = lds32(a);
+                add_row<1>(l, w, packed, lane);
+                break;
+        }
+    }
+}
+
+// Where a warp's histogram rows come from: positions [b0, b1) of a partition buffer (`rows`, packed gradients `gh`),
+// or, with `identity`, rows b0 .. b1 themselves (gh indexed by row).
+struct RowSource {
+    const uint32_t* rows;
+    const int32_t* gh;
+    bool identity;
+};
+
+// Whole CTA: positions [b0, b1) of `src` into the unit's packed shared arrays (`lt`, `nt` tiles). Warp w takes
+// batches w, w + 16, ... of 32 positions; it keeps `depth` of them (<= kMaxStageDepth) in flight in its slots
+// (`stage`: the CTA's staging area, `slot_bytes` per slot) and adds the oldest as it lands. With `depth` 0 (no room
+// for staging) the lanes load their rows' bytes themselves.
+__device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, const RowSource& src, uint32_t b0,
+                                            uint32_t b1, uint32_t stage, uint32_t slot_bytes, uint32_t depth,
+                                            uint64_t pol) {
+    constexpr uint32_t kWarps = kHistThreads / 32;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t nb = b1 > b0 ? static_cast<uint32_t>(ceil_div(b1 - b0, 32)) : 0u;
+    const uint32_t n = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0u;  // this warp's batches
+    // The row and packed gradient of lane's position in the warp's batch i (packed 0 past the range).
+    auto position = [&](uint32_t i, uint32_t& row, uint32_t& packed) {
+        const uint32_t p = b0 + 32 * (warp + kWarps * i) + lane;
+        row = 0;
+        packed = 0;
+        if (p < b1) {
+            if (src.identity) {
+                row = p;
+                packed = static_cast<uint32_t>(__ldcs(src.gh + p));
+            } else {
+                row = __ldcg(src.rows + p);  // written by this step's scatter: not through the read-only path
+                packed = static_cast<uint32_t>(__ldcg(src.gh + p));
+            }
+        }
+    };
+    if (n == 0) return;
+    if (depth == 0) {
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t row, packed;
+            position(i, row, packed);
+            add_batch(lt, nt, row, packed, lane);
+        }
+        return;
+    }
+    const uint32_t mine = stage + warp * depth * slot_bytes;
+    const uint32_t gh_off = slot_bytes - 128;  // the slot's packed gradients
+    uint32_t next_row, next_packed;  // the position of batch `issued`, loaded one issue ahead
+    position(0, next_row, next_packed);
+    uint32_t issued = 0, issue_slot = 0, use_slot = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        while (issued < n && issued < i + depth) {
+            const uint32_t slot = mine + issue_slot * slot_bytes;
+            sts32(slot + gh_off + 4 * lane, next_packed);
+            if (next_packed != 0) stage_row(lt, nt, slot, next_row, lane, pol);  // a zero gradient adds nothing
+            cp_async_commit();
+            ++issued;
+            issue_slot = issue_slot + 1 == depth ? 0 : issue_slot + 1;
+            if (issued < n) position(issued, next_row, next_packed);
+        }
+        cp_async_wait(issued - i - 1);  // batch i's copies (this lane's) have landed
+        const uint32_t slot = mine + use_slot * slot_bytes;
+        use_slot = use_slot + 1 == depth ? 0 : use_slot + 1;
+        const uint32_t packed = lds32(slot + gh_off + 4 * lane);
+        if (packed != 0) add_staged(lt, nt, slot, packed, lane);
+    }
+}
+
 // What a step's phase needs besides the kernel arguments.
 struct FusedStep {
     uint32_t count;       // the parent's positions (the root: every row)
@@ -120,14 +325,18 @@ struct FusedStep {
     uint32_t src, dst;    // partition buffers read and written
     uint32_t chunks;      // CTAs taking part
     bool root;            // identity rows, no partition: every row is built
+    bool identity;        // the parent's rows are its positions (the root leaf's own split)
     bool built_left;      // the histogram is of the left child
     bool histogram;       // the built child's histogram is wanted (else only the partition runs)
     bool packed;          // slabs hold packed sums
     uint32_t round_rows;  // rows per packed round
+    uint32_t stage;       // shared address of the CTA's staging slots
+    uint32_t slot_bytes;  // bytes per staging slot
+    uint32_t depth;       // staging slots per warp (0: no staging)
 };
 
 // CTA `cta`'s part of a step (kHistThreads threads): for a split, the partition of its range of the parent into
-// the other buffer and, for every unit, its built-child rows into the unit's slab region. `scan` is 2 kHistThreads
+// the other buffer; then, for every unit, its built-child rows into the unit's slab region. `scan` is 2 kHistThreads
 // + 64 words of shared memory apart from the histogram's; `cursor` the step's two placement counters (zero before
 // the step); `units` the prepared unit descriptions (`cached` of them; later units are prepared into `spare`).
 inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, const Step& st, const FusedStep& fs,
@@ -138,21 +347,21 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     fused_range(fs.count, fs.chunks, cta, lo, hi);
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr uint32_t kWarps = kHistThreads / 32;
+    constexpr int kBatch = 4;  // words a warp has in flight
     const uint32_t* rows_in = a.rows[fs.src] + fs.begin;
     const int32_t* gh_in = a.ordered[fs.src] + fs.begin;
     uint32_t* rows_out = a.rows[fs.dst] + fs.begin;
     int32_t* gh_out = a.ordered[fs.dst] + fs.begin;
     uint32_t* words = scan + kHistThreads;       // a round's flag words
     uint32_t* sums = scan + 2 * kHistThreads;    // per-warp sums, then the round total
-    __shared__ uint32_t s_base[2];
+    __shared__ uint32_t s_base[3];               // the CTA's first left, first right (from the end), left count
 
-    // Pass 1 (splits): the flags of the CTA's words, kept in the flag buffer, and its left count.
     const uint32_t w_lo = lo / 32, w_hi = static_cast<uint32_t>(ceil_div(hi, 32));
     if (!fs.root) {
+        // Pass 1: the flags of the CTA's words, kept in the flag buffer, and its left count.
         const Tile tile = a.d.tiles[st.split_tile];
         const uint8_t* column = a.d.bins + tile.base + st.split_lane;
         uint32_t mine = 0;
-        constexpr int kBatch = 4;
         for (uint32_t w0 = w_lo + warp; w0 < w_hi; w0 += kBatch * kWarps) {
             uint32_t row[kBatch];
             bool valid[kBatch];
@@ -160,7 +369,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             for (int j = 0; j < kBatch; ++j) {
                 const uint32_t w = w0 + j * kWarps, p = w * 32 + lane;
                 valid[j] = w < w_hi && p < hi;
-                row[j] = valid[j] ? __ldcg(rows_in + p) : 0u;
+                row[j] = !valid[j] ? 0u : fs.identity ? fs.begin + p : __ldcg(rows_in + p);
             }
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) {
@@ -181,95 +390,106 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             // start and to the `right` positions ending `base_r` before the parent's end.
             s_base[0] = atomicAdd(cursor, left);
             s_base[1] = atomicAdd(cursor + 1, (hi - lo) - left);
+            s_base[2] = left;
         }
         __syncthreads();
-    }
 
-    // Pass 2, per unit: the histogram of the built rows (and, with the first unit, the scatter), in rounds.
+        // Pass 2: the scatter, in rounds of one word per thread: the round's word counts scanned over the CTA, then
+        // a warp per word (kBatch words in flight) places its 32 positions.
+        uint32_t carry = 0;  // lefts of the CTA's earlier rounds
+        for (uint32_t r0 = w_lo; r0 < w_hi; r0 += kFusedScanWords) {
+            const uint32_t nw = min(w_hi - r0, kFusedScanWords);
+            const uint32_t word = threadIdx.x < nw ? __ldcg(a.flags + r0 + threadIdx.x) : 0u;
+            words[threadIdx.x] = word;
+            const uint32_t cnt = __popc(word);
+            uint32_t incl = cnt;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t up = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += up;
+            }
+            if (lane == 31) sums[warp] = incl;
+            __syncthreads();
+            if (warp == 0) {
+                const uint32_t v = lane < kWarps ? sums[lane] : 0u;
+                uint32_t vi = v;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t up = __shfl_up_sync(0xffffffffu, vi, o);
+                    if (lane >= static_cast<uint32_t>(o)) vi += up;
+                }
+                if (lane < kWarps) sums[lane] = vi - v;
+                if (lane == 31) sums[32] = vi;
+            }
+            __syncthreads();
+            scan[threadIdx.x] = carry + sums[warp] + incl - cnt;  // the CTA's lefts before this word
+            __syncthreads();
+            for (uint32_t k0 = warp; k0 < nw; k0 += kBatch * kWarps) {
+                uint32_t row[kBatch];
+                int32_t gh[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const uint32_t k = k0 + j * kWarps, p = (r0 + k) * 32 + lane;
+                    const bool valid = k < nw && p < hi;
+                    row[j] = !valid ? 0u : fs.identity ? fs.begin + p : __ldcg(rows_in + p);
+                    gh[j] = valid ? __ldcg(gh_in + p) : 0;
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const uint32_t k = k0 + j * kWarps, p = (r0 + k) * 32 + lane;
+                    if (k >= nw) break;  // warp-uniform
+                    if (p >= hi) continue;
+                    const uint32_t bits = words[k];
+                    const bool left = (bits >> lane) & 1u;
+                    const uint32_t lefts = scan[k] + __popc(bits & ((1u << lane) - 1u));
+                    const uint32_t rights = (p - lo) - lefts;
+                    const uint32_t target = left ? s_base[0] + lefts : fs.count - 1 - (s_base[1] + rights);
+                    rows_out[target] = row[j];
+                    gh_out[target] = gh[j];
+                }
+            }
+            carry += sums[32];
+            __syncthreads();  // the round's scan and words are read
+        }
+    }
+    if (!fs.histogram) return;
+
+    // Pass 3, per unit: the built child's rows of this CTA, one contiguous range, into the unit's slab region.
+    RowSource src;
+    uint32_t b0, b1;
+    if (fs.root) {
+        src = RowSource{nullptr, h.packed, true};
+        b0 = lo;
+        b1 = hi;
+    } else {
+        src = RowSource{rows_out, gh_out, false};
+        const uint32_t left = s_base[2], right = (hi - lo) - left;
+        b0 = fs.built_left ? s_base[0] : fs.count - s_base[1] - right;
+        b1 = b0 + (fs.built_left ? left : right);
+    }
+    const uint64_t pol = evict_first_policy();
     const uint32_t sh_addr = hist_shared_base(sh);
     int4* sh4 = reinterpret_cast<int4*>(sh + (sh_addr - static_cast<uint32_t>(__cvta_generic_to_shared(sh))) / 4);
     __shared__ LaneTile s_lt[kMaxUnitTiles];
     int* slab = h.slabs + static_cast<size_t>(cta) * h.slab_ints;
     uint32_t region = 0;  // ints before this unit's slab region
-    const uint32_t round_words = min(kFusedScanWords, max(1u, fs.round_rows / 32));
+    // Rows per flush: all of them when the slabs hold packed sums (the range fits a packed round), else rounds of
+    // at most round_rows rows.
+    const uint32_t round = fs.packed ? 0xFFFFFFFFu : max(1u, fs.round_rows);
     for (uint32_t u = 0; u < h.num_units; ++u) {
-        if (!fs.histogram && (fs.root || u > 0)) break;  // nothing more to do without the histogram
         HistCta* c = u < cached ? units + u : spare;
         if (u >= cached) histogram_prepare_unit(h, u, sh, spare);
-        const bool want = fs.histogram && fused_unit_begin(*c, active, sh4, s_lt);
-        const bool scatter = !fs.root && u == 0;
+        const bool want = fused_unit_begin(*c, active, sh4, s_lt);
         const uint32_t nt = c->unit.num_tiles;
-        uint32_t carry = 0;  // lefts of the CTA's earlier rounds
-        for (uint32_t r0 = w_lo; r0 < w_hi || r0 == w_lo; r0 += round_words) {
-            const uint32_t r1 = min(w_hi, r0 + round_words);
-            const uint32_t nw = r1 > r0 ? r1 - r0 : 0;
-            if (scatter) {
-                // The round's word counts, scanned over the CTA (one word per thread).
-                const uint32_t word = threadIdx.x < nw ? __ldcg(a.flags + r0 + threadIdx.x) : 0u;
-                words[threadIdx.x] = word;
-                const uint32_t cnt = __popc(word);
-                uint32_t incl = cnt;
-                for (int o = 1; o < 32; o <<= 1) {
-                    const uint32_t up = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= static_cast<uint32_t>(o)) incl += up;
-                }
-                if (lane == 31) sums[warp] = incl;
-                __syncthreads();
-                if (warp == 0) {
-                    const uint32_t v = lane < kWarps ? sums[lane] : 0u;
-                    uint32_t vi = v;
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const uint32_t up = __shfl_up_sync(0xffffffffu, vi, o);
-                        if (lane >= static_cast<uint32_t>(o)) vi += up;
-                    }
-                    if (lane < kWarps) sums[lane] = vi - v;
-                    if (lane == 31) sums[32] = vi;
-                }
-                __syncthreads();
-                scan[threadIdx.x] = carry + sums[warp] + incl - cnt;  // the CTA's lefts before this word
-                __syncthreads();
-            }
-            if (want || scatter) {
-                // A warp per word: its 32 positions' rows, targets and the built child's histogram.
-                for (uint32_t k = warp; k < nw; k += kWarps) {
-                    const uint32_t w = r0 + k, p = w * 32 + lane;
-                    const bool valid = p < hi;
-                    uint32_t row;
-                    int32_t gh;
-                    if (fs.root) {
-                        row = fs.begin + p;
-                        gh = valid ? __ldcs(h.packed + row) : 0;
-                    } else {
-                        row = valid ? __ldcg(rows_in + p) : 0u;
-                        gh = valid ? __ldcg(gh_in + p) : 0;
-                    }
-                    bool built = fs.root;
-                    if (!fs.root) {
-                        const uint32_t bits = scatter ? words[k] : __ldcg(a.flags + w);
-                        const bool left = (bits >> lane) & 1u;
-                        built = left == fs.built_left;
-                        if (scatter && valid) {
-                            const uint32_t lefts = scan[k] + __popc(bits & ((1u << lane) - 1u));
-                            const uint32_t rights = (p - lo) - lefts;
-                            const uint32_t target = left ? s_base[0] + lefts : fs.count - 1 - (s_base[1] + rights);
-                            rows_out[target] = row;
-                            gh_out[target] = gh;
-                        }
-                    }
-                    if (want) add_batch(s_lt, nt, row, valid && built ? static_cast<uint32_t>(gh) : 0u, lane);
-                }
-            }
-            if (scatter) {
-                carry += sums[32];
-                __syncthreads();  // the round's scan and words are read
-            }
-            // Packed slabs: the whole range fits the packing, one flush at the end. Unpacked: a flush per round
-            // (rounds hold at most round_rows positions), stored the first time and added after.
-            const bool last = r1 >= w_hi;
-            if (fs.histogram && (last || !fs.packed))
-                fused_unit_flush(*c, sh4, sh_addr, slab + (fs.packed ? region / 2 : region), fs.packed, r0 == w_lo,
+        uint32_t r0 = b0;
+        while (true) {
+            const uint32_t r1 = want ? (b1 - r0 > round ? r0 + round : b1) : b1;
+            if (want) hist_stream(s_lt, nt, src, r0, r1, fs.stage, fs.slot_bytes, fs.depth, pol);
+            const bool last = r1 >= b1;
+            // Packed slabs: one flush at the end. Unpacked: a flush per round, stored the first time, added after.
+            if (last || !fs.packed)
+                fused_unit_flush(*c, sh4, sh_addr, slab + (fs.packed ? region / 2 : region), fs.packed, r0 == b0,
                                  !last);
             if (last) break;
+            r0 = r1;
         }
         region += 2 * c->unit.slots;
     }

@@ -35,6 +35,9 @@ struct GrowArgs {
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
     uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (5 F bytes)
     uint32_t scan_offset;         // ... of the partition's scan words (2 kHistThreads + 64), past the histogram
+    uint32_t stage_offset;        // ... of the histogram's staging slots (16 warps x stage_depth x slot_bytes)
+    uint32_t slot_bytes;
+    uint32_t stage_depth;         // 0: no staging
     uint32_t pad_;
 };
 
@@ -194,6 +197,10 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         f.chunks = fused_chunks(f.count, ctas);
         f.round_rows = round_rows;
         f.packed = fused_packed(f.count, f.chunks, round_rows);
+        f.identity = !st.root && st.depth == 0;  // the root leaf's rows are still in row order
+        f.stage = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + g.stage_offset;
+        f.slot_bytes = g.slot_bytes;
+        f.depth = g.stage_depth;
         unsigned int* cursor = a.cursors + 2 * (st.root ? 0 : st.new_leaf);
         clock_describe(g, clock, f.histogram ? f.count : 0u, f.packed, st.count);
         fused_step_cta(a, g.h, st, f, cta, smem, scan, cursor, eval, units, cached, &spare);
@@ -248,15 +255,23 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, grow_tree_kernel, kGrowThreads, smem_bytes);
 }
 
-cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             uint32_t scan_offset, uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns,
-                             int trace_steps) {
+int grow_static_smem() {
+    cudaFuncAttributes attr{};
+    if (cudaFuncGetAttributes(&attr, grow_tree_kernel) != cudaSuccess) return -1;
+    return static_cast<int>(attr.sharedSizeBytes);
+}
+
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,
+                             const GrowSmem& smem, cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
     GrowArgs g{};
     g.t = t;
     g.h = h;
     g.barrier = barrier;
-    g.scan_offset = scan_offset;
-    g.flags_offset = flags_offset;
+    g.scan_offset = smem.scan_offset;
+    g.stage_offset = smem.stage_offset;
+    g.slot_bytes = smem.slot_bytes;
+    g.stage_depth = smem.stage_depth;
+    g.flags_offset = smem.flags_offset;
     g.phase_ns = phase_ns;
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet
@@ -266,7 +281,7 @@ cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int
     if (e != cudaSuccess) return e;
     void* args[] = {&g};
     return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(grow_tree_kernel), dim3(grid), dim3(kGrowThreads),
-                                       args, static_cast<size_t>(smem_bytes), s);
+                                       args, static_cast<size_t>(smem.bytes), s);
 }
 
 }  // namespace sb2

@@ -28,6 +28,8 @@ struct LaneTile {
     uint32_t bins;        // 64, 128 or 256: bin slots per feature lane
     uint32_t addr;        // shared address of the tile's packed array (aligned to 4 * stride bytes)
     uint32_t active;      // bit f: feature lane f is wanted (0: the tile is skipped)
+    uint32_t stage_off;   // where a batch's rows of this tile start in a staging slot (the tree kernel's histogram)
+    uint32_t pad_;
 };
 
 // Rows whose packed gradients one packed histogram can sum exactly: every bin's |sum g| <= 32767 and sum h <=
@@ -169,6 +171,8 @@ inline __device__ void histogram_prepare_unit(const HistArgs& a, uint32_t u, con
             lt.bins = tile.smem_bins;
             lt.addr = hist_shared_base(sh) + 4 * slot;
             lt.active = 0;
+            lt.stage_off = 0;
+            lt.pad_ = 0;
             c->tiles[warp] = lt;
         }
     }
@@ -186,34 +190,55 @@ inline __device__ void histogram_prepare_cta(const HistArgs& a, uint32_t cta, co
 __device__ __forceinline__ void flush_packed(const HistCta& c, int4* sh, uint32_t sh_addr, int* slab, bool first,
                                              bool clear) {
     const uint32_t quads = c.unit.slots / 4;
-    for (uint32_t i = threadIdx.x; i < quads; i += kHistThreads) {
-        // the tile of quad i, and its place in the slab
-        uint32_t t = 0, s = 4 * i;
-        uint32_t p = (c.tiles[0].addr - sh_addr) / 4, n = c.tiles[0].bins * c.tiles[0].stride;
-        while (s >= p + n) {
-            ++t;
-            p = (c.tiles[t].addr - sh_addr) / 4;
-            n = c.tiles[t].bins * c.tiles[t].stride;
+    constexpr int kQuads = 4;  // quads per thread in flight: their slab reads overlap
+    for (uint32_t i0 = threadIdx.x; i0 < quads; i0 += kQuads * kHistThreads) {
+        int4 g[kQuads], h[kQuads];
+        int4* gs[kQuads];
+        int4* hs[kQuads];
+#pragma unroll
+        for (int j = 0; j < kQuads; ++j) {
+            const uint32_t i = i0 + j * kHistThreads;
+            gs[j] = hs[j] = nullptr;
+            if (i >= quads) continue;
+            // the tile of quad i, and its place in the slab
+            uint32_t t = 0, s = 4 * i;
+            uint32_t p = (c.tiles[0].addr - sh_addr) / 4, n = c.tiles[0].bins * c.tiles[0].stride;
+            while (s >= p + n) {
+                ++t;
+                p = (c.tiles[t].addr - sh_addr) / 4;
+                n = c.tiles[t].bins * c.tiles[t].stride;
+            }
+            const int4 v = sh[i];
+            // unpack (quantize.rs:140-143): g is the low half sign-extended, h what remains above it
+            g[j] = make_int4(static_cast<int16_t>(v.x & 0xFFFF), static_cast<int16_t>(v.y & 0xFFFF),
+                             static_cast<int16_t>(v.z & 0xFFFF), static_cast<int16_t>(v.w & 0xFFFF));
+            h[j] = make_int4(static_cast<int>(static_cast<uint32_t>(v.x - g[j].x) >> 16),
+                             static_cast<int>(static_cast<uint32_t>(v.y - g[j].y) >> 16),
+                             static_cast<int>(static_cast<uint32_t>(v.z - g[j].z) >> 16),
+                             static_cast<int>(static_cast<uint32_t>(v.w - g[j].w) >> 16));
+            gs[j] = reinterpret_cast<int4*>(slab + p + s);  // 2 p + (s - p): the tile's gradient array
+            hs[j] = reinterpret_cast<int4*>(slab + p + n + s);
+            if (clear) sh[i] = make_int4(0, 0, 0, 0);
         }
-        const int4 v = sh[i];
-        // unpack (quantize.rs:140-143): g is the low half sign-extended, h what remains above it
-        const int4 g = make_int4(static_cast<int16_t>(v.x & 0xFFFF), static_cast<int16_t>(v.y & 0xFFFF),
-                                 static_cast<int16_t>(v.z & 0xFFFF), static_cast<int16_t>(v.w & 0xFFFF));
-        const int4 h = make_int4(static_cast<int>(static_cast<uint32_t>(v.x - g.x) >> 16),
-                                 static_cast<int>(static_cast<uint32_t>(v.y - g.y) >> 16),
-                                 static_cast<int>(static_cast<uint32_t>(v.z - g.z) >> 16),
-                                 static_cast<int>(static_cast<uint32_t>(v.w - g.w) >> 16));
-        int4* gs = reinterpret_cast<int4*>(slab + p + s);  // 2 p + (s - p): the tile's gradient array
-        int4* hs = reinterpret_cast<int4*>(slab + p + n + s);
-        if (first) {
-            __stcg(gs, g);
-            __stcg(hs, h);
-        } else {
-            const int4 og = __ldcg(gs), oh = __ldcg(hs);
-            __stcg(gs, make_int4(og.x + g.x, og.y + g.y, og.z + g.z, og.w + g.w));
-            __stcg(hs, make_int4(oh.x + h.x, oh.y + h.y, oh.z + h.z, oh.w + h.w));
+        if (!first) {
+            int4 og[kQuads], oh[kQuads];
+#pragma unroll
+            for (int j = 0; j < kQuads; ++j) {
+                og[j] = gs[j] ? __ldcg(gs[j]) : make_int4(0, 0, 0, 0);
+                oh[j] = hs[j] ? __ldcg(hs[j]) : make_int4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int j = 0; j < kQuads; ++j) {
+                g[j] = make_int4(g[j].x + og[j].x, g[j].y + og[j].y, g[j].z + og[j].z, g[j].w + og[j].w);
+                h[j] = make_int4(h[j].x + oh[j].x, h[j].y + oh[j].y, h[j].z + oh[j].z, h[j].w + oh[j].w);
+            }
         }
-        if (clear) sh[i] = make_int4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < kQuads; ++j) {
+            if (gs[j] == nullptr) continue;
+            __stcg(gs[j], g[j]);
+            __stcg(hs[j], h[j]);
+        }
     }
 }
 

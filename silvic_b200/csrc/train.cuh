@@ -147,11 +147,23 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // leaf it split.
 constexpr int kGrowPhases = 5;
 constexpr int kStepTrace = kGrowPhases + 3;
-// Its dynamic shared memory (`smem_bytes`): the histogram's arrays first, the partition's scan words (2 * 512 + 64)
-// at `scan_offset`, its per-feature flags (5 F bytes) at `flags_offset`.
-cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid, int smem_bytes,
-                             uint32_t scan_offset, uint32_t flags_offset, cudaStream_t s, unsigned long long* phase_ns,
-                             int trace_steps);
+// The layout of its dynamic shared memory (`bytes` in all): the histogram's arrays first, the partition's scan
+// words (2 * 512 + 64) at `scan_offset`, the histogram's staging slots (16 warps x `stage_depth` slots of
+// `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags (5 F bytes) at `flags_offset`; the
+// search's per-warp bins reuse the start.
+constexpr uint32_t kMaxStageDepth = 4;  // staging slots per warp at most
+struct GrowSmem {
+    int bytes;
+    uint32_t scan_offset;
+    uint32_t stage_offset;
+    uint32_t slot_bytes;
+    uint32_t stage_depth;
+    uint32_t flags_offset;
+};
+// The kernel's static shared memory (bytes; -1 on error): the dynamic part has what is left of the CTA's limit.
+int grow_static_smem();
+cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,
+                             const GrowSmem& smem, cudaStream_t s, unsigned long long* phase_ns, int trace_steps);
 
 void launch_partition_flags(const TrainArgs& a, int grid, cudaStream_t s);
 void launch_partition_scatter(const TrainArgs& a, int grid, cudaStream_t s);

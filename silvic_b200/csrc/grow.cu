@@ -143,10 +143,13 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     extern __shared__ __align__(16) int smem[];
     const TrainArgs& a = g.t;
     const uint32_t cta = blockIdx.x, ctas = gridDim.x;
-    const uint32_t warp = threadIdx.x >> 5, warps = kGrowThreads / 32;
-    // Search items go round the CTAs first (item i to warp i / ctas of CTA i mod ctas), so a step's few hundred
-    // scans spread over every SM instead of filling a dozen.
-    const uint32_t item0 = warp * ctas + cta, items_stride = ctas * warps;
+    const uint32_t warp = threadIdx.x >> 5;
+    // Search items go to groups of kScanWarps warps, round the CTAs first (item i to group i / ctas of CTA i mod
+    // ctas), so a step's few hundred scans spread over every SM instead of filling a dozen.
+    constexpr uint32_t kGroups = kGrowThreads / kScanThreads;
+    const uint32_t group = threadIdx.x / kScanThreads;
+    const uint32_t item0 = group * ctas + cta, items_stride = ctas * kGroups;
+    __shared__ ScanShared scan_shared[kGroups];
     const uint32_t F = a.num_features;
     // Every CTA keeps the learner's control state itself: the step, the evaluated features. The finish runs in
     // every CTA on the same inputs, so no CTA waits for another to publish the next step.
@@ -233,7 +236,8 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         __syncthreads();
         if (s.searched)
             for (uint32_t item = item0; item < search_items(a, st); item += items_stride)
-                search_item(a, st, s, item, reinterpret_cast<int2*>(smem) + warp * kMaxBins);
+                search_item_group(a, st, s, item, reinterpret_cast<int2*>(smem) + group * kMaxBins,
+                                  scan_shared[group], 1 + static_cast<int>(group));
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.

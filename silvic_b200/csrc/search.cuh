@@ -271,6 +271,170 @@ __device__ FeatureCandidate scan_feature(const int2* hist, const DevFeature& f, 
     return o;
 }
 
+// ---- the scan over a group of warps (the persistent tree kernel) ------------------------------------------
+//
+// The same FindBestThresholdSequentially as warp_scan, one candidate per thread: a group of kScanWarps warps
+// (kScanThreads threads) scans a feature of up to kMaxBins bins, so every thread evaluates one bin's gain (two
+// divisions) instead of a lane's eight in a row, and the group meets at a named barrier for each cross-warp
+// reduction (prefix totals, the first break, the best gain, its first bin). Every value is the same integer or
+// IEEE operation on the same operands as warp_scan's: the results are identical.
+constexpr int kScanWarps = 8;
+constexpr int kScanThreads = kScanWarps * 32;
+
+// A group's shared scratch.
+struct ScanShared {
+    int64_t tot[3][kScanWarps];  // warp totals of g, h and count
+    int32_t imin[kScanWarps];    // warp minima: the first break, then the best candidate
+    double dmax[kScanWarps];     // warp maxima of the gains
+    Grown best;
+};
+
+__device__ __forceinline__ void group_sync(int bar) {
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(kScanThreads) : "memory");
+}
+
+__device__ __forceinline__ int32_t warp_min_i32(int32_t v) {
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// warp_scan over the group: thread t (threadIdx.x mod kScanThreads) owns candidate t. `bar` is the group's named
+// barrier (not 0); every thread of the group gets the result.
+__device__ Grown group_scan(const int2* hist, int top, bool reverse, int m, const Ctx& x, const sb2_split_config& c,
+                            ScanShared& sh, int bar) {
+    const int t = static_cast<int>(threadIdx.x) % kScanThreads, lane = t & 31, w = t >> 5;
+    const int64_t min_count = c.min_data_in_leaf > 1 ? c.min_data_in_leaf : 1;
+    int64_t g = 0, h = 0, cnt = 0;
+    if (t < m) {
+        const int2 v = hist[reverse ? top - t : t];
+        g = v.x;
+        h = v.y;
+        cnt = round_int(dmul(dmul(static_cast<double>(h), x.hs), x.cnt_factor));
+    }
+    // Inclusive prefix over the group: within the warp, then the earlier warps' totals.
+    int64_t G = g, H = h, C = cnt;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int64_t ug = shfl_up_i64(G, o), uh = shfl_up_i64(H, o), uc = shfl_up_i64(C, o);
+        if (lane >= o) {
+            G += ug;
+            H += uh;
+            C += uc;
+        }
+    }
+    if (lane == 31) {
+        sh.tot[0][w] = G;
+        sh.tot[1][w] = H;
+        sh.tot[2][w] = C;
+    }
+    group_sync(bar);
+    for (int j = 0; j < w; ++j) {
+        G += sh.tot[0][j];
+        H += sh.tot[1][j];
+        C += sh.tot[2][j];
+    }
+    // Flags and the first break.
+    bool skip = true;
+    double hh = 0.0;
+    int32_t first_break = m;
+    if (t < m) {
+        const double uh = static_cast<double>(H);
+        hh = dadd(kEpsilon, dmul(uh, x.hs));
+        skip = C < min_count || hh < c.min_sum_hessian_in_leaf || uh <= 0.0;
+        const bool other_small = x.num_data - C < min_count || dsub(x.sum_hess, hh) < c.min_sum_hessian_in_leaf ||
+                                 dsub(x.units_hess, uh) <= 0.0;
+        if (other_small && !skip) first_break = t;
+    }
+    first_break = warp_min_i32(first_break);
+    if (lane == 0) sh.imin[w] = first_break;
+    group_sync(bar);
+    first_break = sh.imin[0];
+    for (int j = 1; j < kScanWarps; ++j) first_break = min(first_break, sh.imin[j]);
+    // The gain of candidate t before the break (ScanBuffer::evaluate): leaf_gain(sum - left) + leaf_gain(left).
+    const bool window = t < first_break;
+    double gain = -INFINITY;
+    if (window && !skip) {
+        const double gd = dmul(static_cast<double>(G), x.gs);
+        const double rl = fmax(dsub(fabs(dsub(x.sum_grad, gd)), c.lambda_l1), 0.0);
+        const double rr = fmax(dsub(fabs(gd), c.lambda_l1), 0.0);
+        double num[2] = {dmul(rl, rl), dmul(rr, rr)};
+        double den[2] = {dadd(dsub(x.sum_hess, hh), c.lambda_l2), dadd(hh, c.lambda_l2)};
+        double q[2];
+        div_rn_batch(num, den, q);
+        gain = dadd(q[0], q[1]);
+    }
+    double mx = window ? gain : -INFINITY;
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) sh.dmax[w] = mx;
+    group_sync(bar);
+    mx = sh.dmax[0];
+    for (int j = 1; j < kScanWarps; ++j) mx = fmax(mx, sh.dmax[j]);
+    Grown out{};
+    out.found = false;
+    if (!(mx > x.min_gain_shift)) return out;
+    int32_t best = window && gain == mx ? t : (1 << 30);
+    best = warp_min_i32(best);
+    if (lane == 0) sh.imin[w] = best;
+    group_sync(bar);
+    best = sh.imin[0];
+    for (int j = 1; j < kScanWarps; ++j) best = min(best, sh.imin[j]);
+    if (t == best) {
+        Grown b{};
+        b.found = true;
+        b.bin = static_cast<uint32_t>(reverse ? top - t : t);
+        b.ug = static_cast<double>(G);
+        b.uh = static_cast<double>(H);
+        b.count = C;
+        b.gain = gain;
+        sh.best = b;
+    }
+    group_sync(bar);
+    return sh.best;
+}
+
+// scan_feature over the group (the same find_numerical, split.rs:584-620).
+__device__ FeatureCandidate scan_feature_group(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
+                                               const sb2_split_config& c, ScanShared& sh, int bar) {
+    FeatureCandidate o{};
+    o.feature = feature;
+    o.found = 0;
+    o.splittable = 0;
+    if (!x.valid) return o;
+    const int nb = static_cast<int>(f.num_bins);
+    if (f.nan_bin && nb > 2) {
+        const int last = nb - 2;
+        const Grown r = group_scan(hist, last, true, last, x, c, sh, bar);
+        const Grown fw = group_scan(hist, 0, false, last + 1, x, c, sh, bar);
+        double output_gain = -INFINITY;
+        if (r.found) {
+            reverse_best(x, r, o);
+            output_gain = dsub(o.best_gain, x.min_gain_shift);
+            o.default_left = 1;
+            o.found = 1;
+            o.splittable = 1;
+        }
+        if (fw.found) {
+            o.splittable = 1;
+            FeatureCandidate b = o;
+            forward_best(x, fw, b);
+            if (b.best_gain > dadd(output_gain, x.min_gain_shift)) {
+                o = b;
+                o.default_left = 0;
+                o.found = 1;
+            }
+        }
+    } else if (nb >= 2) {
+        const Grown r = group_scan(hist, nb - 1, true, nb - 1, x, c, sh, bar);
+        if (r.found) {
+            reverse_best(x, r, o);
+            o.default_left = f.nan_bin ? 0 : 1;
+            o.found = 1;
+            o.splittable = 1;
+        }
+    }
+    o.gain = dsub(o.best_gain, x.min_gain_shift);
+    return o;
+}
+
 // Reads a record another CTA of the same launch may have written, past this SM's L1 (which is not coherent with
 // other SMs' writes): a candidate, a leaf record.
 template <class T>
@@ -524,6 +688,64 @@ __device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx&
         }
     }
     __syncwarp();
+}
+
+// search_item for a group of kScanWarps warps (named barrier `bar`): thread t loads bin t, and the group scans the
+// child's bins in `buf` (kMaxBins int2 of the group's shared memory) with scan_feature_group. The same loads, slot
+// writes and candidate as search_item.
+__device__ void search_item_group(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t item, int2* buf,
+                                  ScanShared& sh, int bar) {
+    const uint32_t t = threadIdx.x % kScanThreads;
+    const uint32_t F = a.num_features;
+    const uint32_t f = item % F, ch = item / F;
+    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
+    const DevFeature feat = a.d.features[f];
+    if (!load_flag(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
+        if (t == 0) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
+            cands[f] = none;
+            cands[F + f] = none;
+            if (a.cand_flags) {
+                a.cand_flags[f] = 0;
+                a.cand_flags[F + f] = 0;
+            }
+        }
+        return;
+    }
+    const size_t slot_len = 2 * static_cast<size_t>(a.total_bins);
+    const size_t off = 2 * static_cast<size_t>(feat.hist_offset);
+    const bool mine = t < feat.num_bins;
+    const int2 built = mine ? __ldcg(reinterpret_cast<const int2*>(a.staging + off) + t) : make_int2(0, 0);
+    if (ch == 1) {
+        const int2* parent = reinterpret_cast<const int2*>(a.slots + static_cast<size_t>(st.leaf) * slot_len + off);
+        const int2 p = mine ? __ldcg(parent + t) : make_int2(0, 0);
+        if (mine) {
+            const int2 other = make_int2(p.x - built.x, p.y - built.y);
+            __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[0]) * slot_len + off) + t, built);
+            __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[1]) * slot_len + off) + t, other);
+            buf[t] = other;
+        }
+    } else if (mine) {
+        if (st.root) __stcg(reinterpret_cast<int2*>(a.slots + off) + t, built);
+        buf[t] = built;
+    }
+    group_sync(bar);
+    const FeatureCandidate c = scan_feature_group(buf, feat, static_cast<int>(f), s.ctx[ch], a.cfg, sh, bar);
+    if (t == 0) {
+        cands[static_cast<size_t>(ch) * F + f] = c;
+        if (a.cand_flags) {  // what the persistent kernel's finish compares, apart from the full candidate
+            a.cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
+            a.cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
+        }
+        if (st.root) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
+            cands[F + f] = none;
+            if (a.cand_flags) a.cand_flags[F + f] = 0;
+        }
+    }
+    group_sync(bar);  // buf and the scratch are free for the group's next item
 }
 
 // The best candidate of child `ch` over every feature (one warp; `better` is a total order, so the reduction order

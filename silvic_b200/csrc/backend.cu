@@ -76,6 +76,7 @@ struct sb2_backend {
 
     // dataset
     uint64_t num_rows = 0, row_offset = 0;
+    uint64_t column_stride = 0;  // bytes per feature-major column
     uint32_t num_features = 0, total_bins = 0;
     sb2_objective objective{};
     bool weighted = false;
@@ -91,7 +92,7 @@ struct sb2_backend {
     bool grow_ok = false;   // it fits one CTA per SM
     DeviceBuffer grid_barrier;
     DeviceBuffer phase_ns;  // per-phase nanoseconds of the persistent kernel (profiling runs)
-    DeviceBuffer bins, d_tiles, d_features, d_lane_feature, d_units;
+    DeviceBuffer bins, d_tiles, d_features, d_lane_feature, d_units, columns;
     DeviceBuffer label, weight, scores, grad, hess, packed;
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, cand_flags, cand_gain, counter, maxima, misc;
@@ -135,6 +136,8 @@ struct sb2_backend {
         d.total_bins = total_bins;
         d.num_rows = num_rows;
         d.row_offset = row_offset;
+        d.columns = columns.as<uint8_t>();
+        d.column_stride = column_stride;
         return d;
     }
 
@@ -533,11 +536,12 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     int per_sm = 1;
     SB2_CUDA(b, histogram_occupancy(b->hist_smem, &per_sm));
     per_sm = std::max(per_sm, 1);
-    // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the search's
-    // per-warp bins (256 [g, h] pairs per warp) and the partition's scan.
+    // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the partition's
+    // scan and the search's bins.
     // Layout (GrowSmem): the histogram's arrays, the partition's scan words, the histogram's staging slots (all three
-    // used in the same phase), then the per-feature flags (5 F bytes); the search's per-warp bins reuse the start.
-    // Staging gets what is left of the CTA's shared memory, up to kMaxStageDepth slots per warp.
+    // used in the same phase), then the per-feature flags (5 F bytes); the search's bins (kMaxBins [g, h] pairs per
+    // group of warps, 4 KB in all) reuse the scan words. Staging gets what is left of the CTA's shared memory, up to
+    // kMaxStageDepth slots per warp.
     {
         GrowSmem& m = b->grow_smem;
         m.scan_offset = static_cast<uint32_t>((b->hist_smem + 15) / 16 * 16);
@@ -556,9 +560,8 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         const size_t per_depth = static_cast<size_t>(grow_threads() / 32) * m.slot_bytes;
         const size_t used = m.stage_offset + flags;
         m.stage_depth = used < limit ? static_cast<uint32_t>(std::min<size_t>((limit - used) / per_depth, kMaxStageDepth)) : 0;
-        const size_t phases = std::max<size_t>(m.stage_offset + m.stage_depth * per_depth,
-                                               static_cast<size_t>(grow_threads() / 32) * kMaxBins * 8);
-        m.flags_offset = static_cast<uint32_t>((phases + 15) / 16 * 16);
+        static_assert((2 * 512 + 64) * 4 >= 2 * kMaxBins * 8, "the search's bins fit the scan words");
+        m.flags_offset = static_cast<uint32_t>((m.stage_offset + m.stage_depth * per_depth + 15) / 16 * 16);
         m.bytes = static_cast<int>(m.flags_offset + flags);
     }
     int grow_per_sm = 0;
@@ -618,6 +621,11 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         SB2_CUDA(b, cudaGetLastError());
         SB2_TRY(b->sync());  // the group buffer is reused
     }
+    // The feature-major copy the tree kernel's partition reads.
+    b->column_stride = (n + 127) / 128 * 128;
+    SB2_CUDA(b, b->columns.alloc(std::max<uint64_t>(static_cast<uint64_t>(F) * b->column_stride, 128)));
+    launch_columns(b->dev_data(), b->columns.as<uint8_t>(), b->stream);
+    SB2_CUDA(b, cudaGetLastError());
     // Rows.
     SB2_CUDA(b, b->label.alloc(sizeof(float) * n));
     SB2_CUDA(b, b->weight.alloc(sizeof(float) * (b->weighted ? n : 1)));

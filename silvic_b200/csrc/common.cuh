@@ -4,6 +4,9 @@
 //  - bins: the non-trivial features re-packed into tiles of at most 32 features. Tile t is row-major,
 //    `rows x stride_t` bytes (stride_t = its feature count rounded up to 4), so one row of a full tile is one 32-byte
 //    DRAM sector. Lane j of a warp owns the tile's feature j.
+//  - columns: every feature's bins again, feature-major (feature f's byte of row r at f * column_stride + r), for
+//    the partition, which reads one feature of a leaf's rows: rows of a leaf sit in runs of increasing row id, so a
+//    warp's 32 rows share a few sectors of a column instead of costing a 32-byte row sector each.
 //  - partition: two u32 row-id buffers and two packed-gradient buffers ("ordered gradients"). Every leaf's rows are a
 //    contiguous range of one of the two, recorded per leaf; a partition reads a leaf from one buffer and writes both
 //    children to the other at the same positions.
@@ -52,6 +55,8 @@ struct DevData {
     uint32_t pad_;
     uint64_t num_rows;
     uint64_t row_offset;
+    const uint8_t* columns;  // feature-major copy (null when not built)
+    uint64_t column_stride;  // bytes per column: num_rows rounded up to 128
 };
 
 // ---- quantize.rs, shared by host and device ------------------------------------------------------------------

@@ -83,11 +83,10 @@ __device__ __forceinline__ void add_batch(const LaneTile* lt, uint32_t num_tiles
     }
 }
 
-// The unit's tiles with the wanted features' bits into `lt` (shared), its packed arrays cleared. Whole CTA; returns
-// whether the unit has a wanted feature.
-__device__ __forceinline__ bool fused_unit_begin(const HistCta& c, const uint8_t* active, int4* sh4, LaneTile* lt) {
+// The unit's tiles with the wanted features' bits into `lt` (shared). Whole CTA; returns whether the unit has a
+// wanted feature. The packed arrays are zero already: cleared when the kernel starts and by every flush.
+__device__ __forceinline__ bool fused_unit_begin(const HistCta& c, const uint8_t* active, LaneTile* lt) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t i = threadIdx.x; i < c.unit.slots / 4; i += kHistThreads) sh4[i] = make_int4(0, 0, 0, 0);
     if (warp < c.unit.num_tiles) {
         const int32_t f = c.lane_feature[warp][lane];
         const bool on = f >= 0 && (active == nullptr || load_flag(active + f) != 0);
@@ -107,15 +106,18 @@ __device__ __forceinline__ bool fused_unit_begin(const HistCta& c, const uint8_t
 }
 
 // The unit's shared sums into the CTA's slab: packed as they are (`packed`: the slab region is one int per slot) or
-// unpacked (stored when `first`, added otherwise); cleared for another round when `clear`. Whole CTA.
+// unpacked (stored when `first`, added otherwise); the shared sums are left cleared. Whole CTA.
 __device__ __forceinline__ void fused_unit_flush(const HistCta& c, int4* sh4, uint32_t sh_addr, int* slab_unit,
-                                                 bool packed, bool first, bool clear) {
+                                                 bool packed, bool first) {
     __syncthreads();
     if (packed) {
         int4* dst = reinterpret_cast<int4*>(slab_unit);
-        for (uint32_t i = threadIdx.x; i < c.unit.slots / 4; i += kHistThreads) __stcg(dst + i, sh4[i]);
+        for (uint32_t i = threadIdx.x; i < c.unit.slots / 4; i += kHistThreads) {
+            __stcg(dst + i, sh4[i]);
+            sh4[i] = make_int4(0, 0, 0, 0);
+        }
     } else {
-        flush_packed(c, sh4, sh_addr, slab_unit, first, clear);
+        flush_packed(c, sh4, sh_addr, slab_unit, first, true);
     }
     __syncthreads();
 }
@@ -335,10 +337,10 @@ struct FusedStep {
     uint32_t depth;       // staging slots per warp (0: no staging)
 };
 
-// CTA `cta`'s part of a step (kHistThreads threads): for a split, the partition of its range of the parent into
+// CTA `cta`'s part of a step (kHistThreads threads; the unit histograms' shared arrays zero on entry and on return): for a split, the partition of its range of the parent into
 // the other buffer; then, for every unit, its built-child rows into the unit's slab region. `scan` is 2 kHistThreads
-// + 64 words of shared memory apart from the histogram's; `cursor` the step's two placement counters (zero before
-// the step); `units` the prepared unit descriptions (`cached` of them; later units are prepared into `spare`).
+// + 64 words of shared memory apart from the histogram's; `cursor` the step's two placement counters (8-byte aligned,
+// zero before the step); `units` the prepared unit descriptions (`cached` of them; later units are prepared into `spare`).
 inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, const Step& st, const FusedStep& fs,
                                       uint32_t cta, int* sh, uint32_t* scan, unsigned int* cursor,
                                       const uint8_t* active, HistCta* units, uint32_t cached, HistCta* spare) {
@@ -358,44 +360,48 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
 
     const uint32_t w_lo = lo / 32, w_hi = static_cast<uint32_t>(ceil_div(hi, 32));
     if (!fs.root) {
-        // Pass 1: the flags of the CTA's words, kept in the flag buffer, and its left count.
-        const Tile tile = a.d.tiles[st.split_tile];
-        const uint8_t* column = a.d.bins + tile.base + st.split_lane;
+        // Pass 1: the flags of the CTA's words, kept in the flag buffer, and its left count. The split feature's
+        // bins come from its feature-major column. Warp w takes kBatch consecutive words at a time, and its lanes
+        // 0 .. kBatch-1 store their flag words with one instruction.
+        const uint8_t* column = a.d.columns + static_cast<uint64_t>(st.info.feature) * a.d.column_stride;
         uint32_t mine = 0;
-        for (uint32_t w0 = w_lo + warp; w0 < w_hi; w0 += kBatch * kWarps) {
+        for (uint32_t w0 = w_lo + warp * kBatch; w0 < w_hi; w0 += kBatch * kWarps) {
             uint32_t row[kBatch];
             bool valid[kBatch];
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) {
-                const uint32_t w = w0 + j * kWarps, p = w * 32 + lane;
+                const uint32_t w = w0 + j, p = w * 32 + lane;
                 valid[j] = w < w_hi && p < hi;
                 row[j] = !valid[j] ? 0u : fs.identity ? fs.begin + p : __ldcg(rows_in + p);
             }
+            uint32_t flag_word = 0;
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) {
-                const uint32_t w = w0 + j * kWarps;
-                if (w >= w_hi) break;  // warp-uniform
-                const bool left = valid[j] && bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row[j]) * tile.stride));
+                const bool left = valid[j] && bin_goes_left(st.left_bins, __ldg(column + row[j]));
                 const uint32_t word = __ballot_sync(0xffffffffu, left);
-                if (lane == 0) a.flags[w] = word;
+                if (lane == static_cast<uint32_t>(j)) flag_word = word;
                 mine += __popc(word);
             }
+            if (lane < static_cast<uint32_t>(kBatch) && w0 + lane < w_hi) a.flags[w0 + lane] = flag_word;
         }
         if (lane == 0) sums[warp] = mine;
         __syncthreads();
         if (threadIdx.x == 0) {
             uint32_t left = 0;
             for (uint32_t k = 0; k < kWarps; ++k) left += sums[k];
-            // One atomic per side: this CTA's lefts and rights go to [base_l, base_l + left) from the parent's
-            // start and to the `right` positions ending `base_r` before the parent's end.
-            s_base[0] = atomicAdd(cursor, left);
-            s_base[1] = atomicAdd(cursor + 1, (hi - lo) - left);
+            // One 64-bit atomic for both sides (lefts in the low word, rights in the high; neither passes 2^32):
+            // this CTA's lefts go to [base_l, base_l + left) from the parent's start and its rights to the `right`
+            // positions ending `base_r` before the parent's end.
+            const unsigned long long add = (static_cast<unsigned long long>((hi - lo) - left) << 32) | left;
+            const unsigned long long old = atomicAdd(reinterpret_cast<unsigned long long*>(cursor), add);
+            s_base[0] = static_cast<uint32_t>(old);
+            s_base[1] = static_cast<uint32_t>(old >> 32);
             s_base[2] = left;
         }
         __syncthreads();
 
         // Pass 2: the scatter, in rounds of one word per thread: the round's word counts scanned over the CTA, then
-        // a warp per word (kBatch words in flight) places its 32 positions.
+        // each warp places kBatch consecutive words' positions at a time.
         uint32_t carry = 0;  // lefts of the CTA's earlier rounds
         for (uint32_t r0 = w_lo; r0 < w_hi; r0 += kFusedScanWords) {
             const uint32_t nw = min(w_hi - r0, kFusedScanWords);
@@ -422,19 +428,19 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             __syncthreads();
             scan[threadIdx.x] = carry + sums[warp] + incl - cnt;  // the CTA's lefts before this word
             __syncthreads();
-            for (uint32_t k0 = warp; k0 < nw; k0 += kBatch * kWarps) {
+            for (uint32_t k0 = warp * kBatch; k0 < nw; k0 += kBatch * kWarps) {
                 uint32_t row[kBatch];
                 int32_t gh[kBatch];
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const uint32_t k = k0 + j * kWarps, p = (r0 + k) * 32 + lane;
+                    const uint32_t k = k0 + j, p = (r0 + k) * 32 + lane;
                     const bool valid = k < nw && p < hi;
                     row[j] = !valid ? 0u : fs.identity ? fs.begin + p : __ldcg(rows_in + p);
                     gh[j] = valid ? __ldcg(gh_in + p) : 0;
                 }
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const uint32_t k = k0 + j * kWarps, p = (r0 + k) * 32 + lane;
+                    const uint32_t k = k0 + j, p = (r0 + k) * 32 + lane;
                     if (k >= nw) break;  // warp-uniform
                     if (p >= hi) continue;
                     const uint32_t bits = words[k];
@@ -477,7 +483,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     for (uint32_t u = 0; u < h.num_units; ++u) {
         HistCta* c = u < cached ? units + u : spare;
         if (u >= cached) histogram_prepare_unit(h, u, sh, spare);
-        const bool want = fused_unit_begin(*c, active, sh4, s_lt);
+        const bool want = fused_unit_begin(*c, active, s_lt);
         const uint32_t nt = c->unit.num_tiles;
         uint32_t r0 = b0;
         while (true) {
@@ -486,8 +492,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             const bool last = r1 >= b1;
             // Packed slabs: one flush at the end. Unpacked: a flush per round, stored the first time, added after.
             if (last || !fs.packed)
-                fused_unit_flush(*c, sh4, sh_addr, slab + (fs.packed ? region / 2 : region), fs.packed, r0 == b0,
-                                 !last);
+                fused_unit_flush(*c, sh4, sh_addr, slab + (fs.packed ? region / 2 : region), fs.packed, r0 == b0);
             if (last) break;
             r0 = r1;
         }

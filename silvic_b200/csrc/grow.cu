@@ -172,6 +172,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     __shared__ HistCta spare;
     const uint32_t cached = g.h.num_units < kUnitCache ? g.h.num_units : kUnitCache;
     for (uint32_t u = 0; u < cached; ++u) histogram_prepare_unit(g.h, u, smem, units + u);
+    // The histogram's shared arrays start at zero; every flush leaves them so.
+    for (uint32_t i = threadIdx.x; i < g.scan_offset / 16; i += kGrowThreads)
+        reinterpret_cast<int4*>(smem)[i] = make_int4(0, 0, 0, 0);
     const uint32_t round_rows = packed_round_rows(*g.h.spec);  // the iteration's quantization, set before the launch
     // The root step, its job and features, as the iteration's start left them.
     broadcast_cg(a.step, &st);
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         __syncthreads();
         if (s.searched)
             for (uint32_t item = item0; item < search_items(a, st); item += items_stride)
-                search_item_group(a, st, s, item, reinterpret_cast<int2*>(smem) + group * kMaxBins,
+                search_item_group(a, st, s, item, reinterpret_cast<int2*>(scan) + group * kMaxBins,
                                   scan_shared[group], 1 + static_cast<int>(group));
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);

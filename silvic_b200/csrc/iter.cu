@@ -552,6 +552,40 @@ void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint3
     repack_kernel<<<grid, 256, 0, s>>>(src, rows, src_stride, src_column, dst, dst_stride, dst_lane, num_bins, bad);
 }
 
+// One CTA per 128 rows of one tile: the rows into shared memory at a pitch of stride + 1 bytes, then warp w writes
+// the 128 bytes of tile lanes w, w + 8, ... as one 128-byte store each (lane j: rows 4j .. 4j + 3). With the odd
+// pitch both the byte stores of the first step and the column reads of the second hit 32 different banks.
+__global__ void columns_kernel(DevData d, uint8_t* columns) {
+    constexpr uint32_t kRows = 128;
+    __shared__ uint8_t sh[kRows * (kTileLanes + 1)];
+    const Tile tile = d.tiles[blockIdx.y];
+    const uint32_t pitch = tile.stride + 1;
+    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kRows;
+    const uint32_t words = kRows * tile.stride / 4;
+    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
+        const uint32_t row = i / (tile.stride / 4), wb = i % (tile.stride / 4);
+        uint32_t v = 0;
+        if (r0 + row < d.num_rows)
+            v = *reinterpret_cast<const uint32_t*>(d.bins + tile.base + (r0 + row) * tile.stride + 4 * wb);
+        for (int q = 0; q < 4; ++q) sh[row * pitch + 4 * wb + q] = static_cast<uint8_t>(v >> (8 * q));
+    }
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    for (uint32_t l = warp; l < tile.nfeat; l += warps) {
+        const int32_t f = d.lane_feature[blockIdx.y * kTileLanes + l];
+        if (f < 0) continue;
+        uint32_t v = 0;
+        for (int q = 0; q < 4; ++q) v |= static_cast<uint32_t>(sh[(4 * lane + q) * pitch + l]) << (8 * q);
+        *reinterpret_cast<uint32_t*>(columns + static_cast<uint64_t>(f) * d.column_stride + r0 + 4 * lane) = v;
+    }
+}
+
+void launch_columns(const DevData& d, uint8_t* columns, cudaStream_t s) {
+    if (d.num_tiles == 0 || d.num_rows == 0) return;
+    const dim3 grid(static_cast<unsigned>(ceil_div(d.num_rows, 128)), d.num_tiles);
+    columns_kernel<<<grid, 256, 0, s>>>(d, columns);
+}
+
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s) {
     const int grid = static_cast<int>(n / 256 + 1 < 65535 ? n / 256 + 1 : 65535);
     fill_kernel<<<grid, 256, 0, s>>>(out, n, value);

@@ -76,6 +76,8 @@ void launch_api_add_tree(const DevData& d, const RowArgs& r, const TileNode* nod
 void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
                    uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad, cudaStream_t s);
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s);
+// The feature-major copy of the tiles (DevData::columns, which must be allocated: num_features * column_stride).
+void launch_columns(const DevData& d, uint8_t* columns, cudaStream_t s);
 // Counts the operand pairs where the split scan's division (div_rn) differs from CUDA's correctly rounded one.
 void launch_division_check(uint64_t n, uint32_t seed, unsigned long long* mismatches, int grid, cudaStream_t s);
 void launch_api_find_split(const DevData& d, const int* hist, const uint8_t* evaluate, double ug, double uh,

@@ -149,8 +149,9 @@ constexpr int kGrowPhases = 5;
 constexpr int kStepTrace = kGrowPhases + 3;
 // The layout of its dynamic shared memory (`bytes` in all): the histogram's arrays first, the partition's scan
 // words (2 * 512 + 64) at `scan_offset`, the histogram's staging slots (16 warps x `stage_depth` slots of
-// `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags (5 F bytes) at `flags_offset`; the
-// search's per-warp bins reuse the start.
+// `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags (5 F bytes) at `flags_offset`. The
+// search's bins (kMaxBins [g, h] pairs per group of kScanWarps warps) reuse the scan words; the histogram's arrays
+// stay zero between steps.
 constexpr uint32_t kMaxStageDepth = 4;  // staging slots per warp at most
 struct GrowSmem {
     int bytes;

@@ -501,40 +501,39 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
 }
 
 // The step's slab reduction (thread `thread` of `threads`): histogram_reduce_quads over slabs that hold every unit,
-// packed or not.
-inline __device__ void fused_reduce(const HistArgs& a, uint32_t chunks, bool packed, uint32_t thread,
-                                    uint32_t threads) {
-    const uint32_t split = a.quad_split;
+// packed or not. Each quad takes as many threads as the grid has to spare (a power of two up to a warp), each
+// thread up to kLoads of its chunks' loads in flight at once.
+template <bool kPacked>
+__device__ __forceinline__ void fused_reduce_quads(const HistArgs& a, uint32_t chunks, uint32_t thread,
+                                                   uint32_t threads) {
+    constexpr int kLoads = kPacked ? 8 : 4;  // chunks per thread and batch (an int4 each, two when unpacked)
+    uint32_t split = 1;
+    while (split < 32 && 2 * split * a.num_quads <= threads) split *= 2;
     const uint32_t j = thread & (split - 1);
     const uint32_t groups = threads / split;
     const uint32_t rounds = static_cast<uint32_t>(ceil_div(a.num_quads, groups));
-    for (uint32_t r = 0; r < rounds; ++r) {
+    for (uint32_t r = 0; r < rounds; ++r) {  // the same count on every lane: the shuffles need the whole warp
         const uint32_t q = r * groups + thread / split;
         int4 g = make_int4(0, 0, 0, 0), hs = g;
         QuadMeta m{};
         const bool mine = q < a.num_quads;
         if (mine) {
             m = a.quads[q];
-            for (uint32_t c0 = j; c0 < chunks; c0 += 4 * split) {
-                int4 v[4], w[4];
+            const uint32_t off = kPacked ? m.unit_off_packed + m.p_off : m.unit_off + m.g_off;
+            const uint32_t off_h = m.unit_off + m.h_off;
+            for (uint32_t c0 = j; c0 < chunks; c0 += kLoads * split) {
+                int4 v[kLoads], w[kLoads];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < kLoads; ++k) {
                     const uint32_t c = c0 + k * split;
                     const int* slab = a.slabs + static_cast<size_t>(c) * a.slab_ints;
                     const bool in = c < chunks;
-                    if (packed) {
-                        v[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + m.unit_off_packed + m.p_off))
-                                  : make_int4(0, 0, 0, 0);
-                    } else {
-                        v[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + m.unit_off + m.g_off))
-                                  : make_int4(0, 0, 0, 0);
-                        w[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + m.unit_off + m.h_off))
-                                  : make_int4(0, 0, 0, 0);
-                    }
+                    v[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + off)) : make_int4(0, 0, 0, 0);
+                    if (!kPacked) w[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + off_h)) : make_int4(0, 0, 0, 0);
                 }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if (packed) {
+                for (int k = 0; k < kLoads; ++k) {
+                    if (kPacked) {
                         // unpack (quantize.rs:140-143)
                         const int4 x = v[k];
                         const int4 gx = make_int4(static_cast<int16_t>(x.x & 0xFFFF), static_cast<int16_t>(x.y & 0xFFFF),
@@ -563,6 +562,14 @@ inline __device__ void fused_reduce(const HistArgs& a, uint32_t chunks, bool pac
             if (m.out[3] >= 0) __stcg(out + m.out[3], make_int2(g.w, hs.w));
         }
     }
+}
+
+inline __device__ void fused_reduce(const HistArgs& a, uint32_t chunks, bool packed, uint32_t thread,
+                                    uint32_t threads) {
+    if (packed)
+        fused_reduce_quads<true>(a, chunks, thread, threads);
+    else
+        fused_reduce_quads<false>(a, chunks, thread, threads);
 }
 
 }  // namespace sb2

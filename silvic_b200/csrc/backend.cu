@@ -599,33 +599,48 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, cudaMemcpyAsync(b->d_features.ptr, b->dev_features.data(), sizeof(DevFeature) * F, cudaMemcpyHostToDevice, b->stream));
     SB2_CUDA(b, cudaMemcpyAsync(b->d_lane_feature.ptr, lane_feature.data(), sizeof(int32_t) * lane_feature.size(), cudaMemcpyHostToDevice, b->stream));
     SB2_CUDA(b, cudaMemcpyAsync(b->d_units.ptr, b->units.data(), sizeof(Unit) * b->units.size(), cudaMemcpyHostToDevice, b->stream));
-    SB2_CUDA(b, cudaMemsetAsync(b->bins.ptr, 0, b->bins.bytes, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->bins.ptr, 0, b->bins.bytes, b->stream));  // tile padding past the last row
     SB2_CUDA(b, b->counter.alloc(sizeof(unsigned int)));
     SB2_CUDA(b, cudaMemsetAsync(b->counter.ptr, 0, sizeof(unsigned int), b->stream));
-    // Bins: each group uploaded once, its columns scattered into the tiles; every bin checked against its feature.
-    DeviceBuffer group_buf;
-    for (uint32_t g = 0; g < train->num_groups; ++g) {
-        const sb2_group& grp = train->groups[g];
-        if (n == 0) break;
-        SB2_CUDA(b, group_buf.alloc(n * grp.row_stride));
-        SB2_CUDA(b, cudaMemcpyAsync(group_buf.ptr, grp.data, n * grp.row_stride, cudaMemcpyHostToDevice, b->stream));
-        for (uint32_t k = 0; k < grp.num_features; ++k) {
-            uint32_t f = grp.features[k];
-            const DevFeature& d = b->dev_features[f];
-            if (d.tile < 0) continue;
-            const Tile& t = b->tiles[d.tile];
-            launch_repack(group_buf.as<uint8_t>(), n, grp.row_stride, train->features[f].column,
-                          b->bins.as<uint8_t>() + t.base, t.stride, static_cast<uint32_t>(d.lane), d.num_bins,
-                          b->counter.as<unsigned int>(), b->stream);
-        }
-        SB2_CUDA(b, cudaGetLastError());
-        SB2_TRY(b->sync());  // the group buffer is reused
-    }
-    // The feature-major copy the tree kernel's partition reads.
+    // Bins: each group uploaded once (one staging buffer, in stream order) and transposed into the feature-major
+    // copy the tree kernel's partition reads, every bin checked against its feature; then the tiles from the copy.
     b->column_stride = (n + 127) / 128 * 128;
     SB2_CUDA(b, b->columns.alloc(std::max<uint64_t>(static_cast<uint64_t>(F) * b->column_stride, 128)));
-    launch_columns(b->dev_data(), b->columns.as<uint8_t>(), b->stream);
-    SB2_CUDA(b, cudaGetLastError());
+    {
+        uint64_t max_group = 0;
+        uint32_t max_stride = 1;
+        for (uint32_t g = 0; g < train->num_groups; ++g) {
+            max_group = std::max<uint64_t>(max_group, n * train->groups[g].row_stride);
+            max_stride = std::max(max_stride, train->groups[g].row_stride);
+        }
+        DeviceBuffer group_buf, group_meta;
+        SB2_CUDA(b, group_buf.alloc(std::max<uint64_t>(max_group, 16)));
+        SB2_CUDA(b, group_meta.alloc(8ull * max_stride));
+        std::vector<std::vector<int32_t>> metas(train->num_groups);  // alive until the copies are done
+        for (uint32_t g = 0; g < train->num_groups && n > 0; ++g) {
+            const sb2_group& grp = train->groups[g];
+            std::vector<int32_t>& meta = metas[g];  // [row_stride] column -> feature, then [row_stride] bins
+            meta.assign(2ull * grp.row_stride, -1);
+            for (uint32_t k = 0; k < grp.num_features; ++k) {
+                const uint32_t f = grp.features[k];
+                const uint32_t col = train->features[f].column;
+                if (col >= grp.row_stride) return b->fail(SB2_EDEVICE, "a feature's column lies outside its group's rows");
+                if (b->dev_features[f].tile < 0) continue;
+                meta[col] = static_cast<int32_t>(f);
+                meta[grp.row_stride + col] = static_cast<int32_t>(b->dev_features[f].num_bins);
+            }
+            SB2_CUDA(b, cudaMemcpyAsync(group_buf.ptr, grp.data, n * grp.row_stride, cudaMemcpyHostToDevice, b->stream));
+            SB2_CUDA(b, cudaMemcpyAsync(group_meta.ptr, meta.data(), sizeof(int32_t) * meta.size(), cudaMemcpyHostToDevice,
+                                        b->stream));
+            launch_group_columns(group_buf.as<uint8_t>(), n, grp.row_stride, group_meta.as<int32_t>(),
+                                 reinterpret_cast<const uint32_t*>(group_meta.as<int32_t>() + grp.row_stride),
+                                 b->columns.as<uint8_t>(), b->column_stride, b->counter.as<unsigned int>(), b->stream);
+            SB2_CUDA(b, cudaGetLastError());
+        }
+        launch_tiles(b->dev_data(), b->bins.as<uint8_t>(), b->stream);
+        SB2_CUDA(b, cudaGetLastError());
+        SB2_TRY(b->sync());  // the staging buffers go out of scope
+    }
     // Rows.
     SB2_CUDA(b, b->label.alloc(sizeof(float) * n));
     SB2_CUDA(b, b->weight.alloc(sizeof(float) * (b->weighted ? n : 1)));

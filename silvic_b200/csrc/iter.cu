@@ -463,18 +463,63 @@ __global__ void __launch_bounds__(kRowThreads) api_add_tree_kernel(DevData d, Ro
     }
 }
 
-// One feature's column of a group moved into its tile lane; a bin past the feature's bins sets `bad` (the
-// histogram's shared slots hold exactly each feature's bins).
-__global__ void repack_kernel(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
-                              uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad) {
-    bool out_of_range = false;
-    for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; row < rows;
-         row += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        const uint8_t bin = src[row * src_stride + src_column];
-        out_of_range |= bin >= num_bins;
-        dst[row * dst_stride + dst_lane] = bin;
+// A group's columns (rows of `row_stride` bytes) into the feature-major copy: one CTA per 128 rows and 64-column
+// strip. The strip's bytes go to shared memory at a pitch of 65 (coalesced byte loads), then warp w writes columns
+// w, w + 8, ... of the strip, lane j rows 4j .. 4j + 3 as one 32-bit store (128 bytes per warp; with the odd pitch
+// the reads hit 32 different banks). `col_feature[c]` is column c's feature (-1: none or trivial), `col_bins[c]` its
+// bin count: a bin past it sets `bad` (the histogram's shared slots hold exactly each feature's bins).
+__global__ void group_columns_kernel(const uint8_t* src, uint64_t rows, uint32_t row_stride, const int32_t* col_feature,
+                                     const uint32_t* col_bins, uint8_t* columns, uint64_t column_stride,
+                                     unsigned int* bad) {
+    constexpr uint32_t kRows = 128, kStrip = 64, kPitch = kStrip + 1;
+    __shared__ uint8_t sh[kRows * kPitch];
+    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kRows;
+    const uint32_t c0 = blockIdx.y * kStrip;
+    for (uint32_t i = threadIdx.x; i < kRows * kStrip; i += blockDim.x) {
+        const uint32_t row = i / kStrip, c = i % kStrip;
+        sh[row * kPitch + c] = r0 + row < rows && c0 + c < row_stride ? src[(r0 + row) * row_stride + c0 + c] : 0;
     }
-    if (__any_sync(0xffffffffu, out_of_range) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    bool out_of_range = false;
+    for (uint32_t c = warp; c < kStrip && c0 + c < row_stride; c += warps) {
+        const int32_t f = col_feature[c0 + c];
+        if (f < 0) continue;
+        const uint32_t nb = col_bins[c0 + c];
+        uint32_t v = 0;
+        for (int q = 0; q < 4; ++q) {
+            const uint8_t bin = sh[(4 * lane + q) * kPitch + c];
+            out_of_range |= r0 + 4 * lane + q < rows && bin >= nb;
+            v |= static_cast<uint32_t>(bin) << (8 * q);
+        }
+        *reinterpret_cast<uint32_t*>(columns + static_cast<uint64_t>(f) * column_stride + r0 + 4 * lane) = v;
+    }
+    if (__any_sync(0xffffffffu, out_of_range) && lane == 0) atomicOr(bad, 1u);
+}
+
+// The tiles from the feature-major copy: one CTA per 128 rows of one tile. Warp w reads the columns of tile lanes
+// w, w + 8, ... (128 bytes each, coalesced) into shared memory at a pitch of 132, then the CTA writes the tile's 128
+// rows as 32-bit words (padding lanes 0).
+__global__ void tiles_kernel(DevData d, uint8_t* bins) {
+    constexpr uint32_t kRows = 128, kPitch = kRows + 4;
+    __shared__ __align__(4) uint8_t sh[kTileLanes * kPitch];
+    const Tile tile = d.tiles[blockIdx.y];
+    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kRows;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    for (uint32_t l = warp; l < tile.stride; l += warps) {
+        const int32_t f = l < tile.nfeat ? d.lane_feature[blockIdx.y * kTileLanes + l] : -1;
+        const uint32_t v = f >= 0 ? *reinterpret_cast<const uint32_t*>(d.columns + static_cast<uint64_t>(f) * d.column_stride + r0 + 4 * lane) : 0u;
+        *reinterpret_cast<uint32_t*>(sh + l * kPitch + 4 * lane) = v;
+    }
+    __syncthreads();
+    const uint32_t words = tile.stride / 4;
+    for (uint32_t i = threadIdx.x; i < kRows * words; i += blockDim.x) {
+        const uint32_t row = i / words, wb = i % words;
+        if (r0 + row >= d.num_rows) continue;
+        uint32_t v = 0;
+        for (int q = 0; q < 4; ++q) v |= static_cast<uint32_t>(sh[(4 * wb + q) * kPitch + row]) << (8 * q);
+        *reinterpret_cast<uint32_t*>(bins + tile.base + (r0 + row) * tile.stride + 4 * wb) = v;
+    }
 }
 
 __global__ void fill_kernel(float* out, uint64_t n, float value) {
@@ -546,44 +591,18 @@ void launch_api_add_tree(const DevData& d, const RowArgs& r, const TileNode* nod
                          const float* leaf_values, int grid, cudaStream_t s) {
     api_add_tree_kernel<<<grid, kRowThreads, 0, s>>>(d, r, nodes, num_nodes, leaf_values);
 }
-void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
-                   uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad, cudaStream_t s) {
-    const int grid = static_cast<int>(rows / 256 + 1 < 65535 ? rows / 256 + 1 : 65535);
-    repack_kernel<<<grid, 256, 0, s>>>(src, rows, src_stride, src_column, dst, dst_stride, dst_lane, num_bins, bad);
+void launch_group_columns(const uint8_t* src, uint64_t rows, uint32_t row_stride, const int32_t* col_feature,
+                          const uint32_t* col_bins, uint8_t* columns, uint64_t column_stride, unsigned int* bad,
+                          cudaStream_t s) {
+    if (rows == 0 || row_stride == 0) return;
+    const dim3 grid(static_cast<unsigned>(ceil_div(rows, 128)), static_cast<unsigned>(ceil_div(row_stride, 64)));
+    group_columns_kernel<<<grid, 256, 0, s>>>(src, rows, row_stride, col_feature, col_bins, columns, column_stride, bad);
 }
 
-// One CTA per 128 rows of one tile: the rows into shared memory at a pitch of stride + 1 bytes, then warp w writes
-// the 128 bytes of tile lanes w, w + 8, ... as one 128-byte store each (lane j: rows 4j .. 4j + 3). With the odd
-// pitch both the byte stores of the first step and the column reads of the second hit 32 different banks.
-__global__ void columns_kernel(DevData d, uint8_t* columns) {
-    constexpr uint32_t kRows = 128;
-    __shared__ uint8_t sh[kRows * (kTileLanes + 1)];
-    const Tile tile = d.tiles[blockIdx.y];
-    const uint32_t pitch = tile.stride + 1;
-    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kRows;
-    const uint32_t words = kRows * tile.stride / 4;
-    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
-        const uint32_t row = i / (tile.stride / 4), wb = i % (tile.stride / 4);
-        uint32_t v = 0;
-        if (r0 + row < d.num_rows)
-            v = *reinterpret_cast<const uint32_t*>(d.bins + tile.base + (r0 + row) * tile.stride + 4 * wb);
-        for (int q = 0; q < 4; ++q) sh[row * pitch + 4 * wb + q] = static_cast<uint8_t>(v >> (8 * q));
-    }
-    __syncthreads();
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    for (uint32_t l = warp; l < tile.nfeat; l += warps) {
-        const int32_t f = d.lane_feature[blockIdx.y * kTileLanes + l];
-        if (f < 0) continue;
-        uint32_t v = 0;
-        for (int q = 0; q < 4; ++q) v |= static_cast<uint32_t>(sh[(4 * lane + q) * pitch + l]) << (8 * q);
-        *reinterpret_cast<uint32_t*>(columns + static_cast<uint64_t>(f) * d.column_stride + r0 + 4 * lane) = v;
-    }
-}
-
-void launch_columns(const DevData& d, uint8_t* columns, cudaStream_t s) {
+void launch_tiles(const DevData& d, uint8_t* bins, cudaStream_t s) {
     if (d.num_tiles == 0 || d.num_rows == 0) return;
     const dim3 grid(static_cast<unsigned>(ceil_div(d.num_rows, 128)), d.num_tiles);
-    columns_kernel<<<grid, 256, 0, s>>>(d, columns);
+    tiles_kernel<<<grid, 256, 0, s>>>(d, bins);
 }
 
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s) {

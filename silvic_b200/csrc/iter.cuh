@@ -73,11 +73,14 @@ void launch_api_leaf_sums(const RowArgs& r, const uint32_t* partition, const sb2
                           float gs, float hs, int64_t* out, int grid, cudaStream_t s);
 void launch_api_add_tree(const DevData& d, const RowArgs& r, const TileNode* nodes, uint32_t num_nodes,
                          const float* leaf_values, int grid, cudaStream_t s);
-void launch_repack(const uint8_t* src, uint64_t rows, uint32_t src_stride, uint32_t src_column, uint8_t* dst,
-                   uint32_t dst_stride, uint32_t dst_lane, uint32_t num_bins, unsigned int* bad, cudaStream_t s);
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s);
-// The feature-major copy of the tiles (DevData::columns, which must be allocated: num_features * column_stride).
-void launch_columns(const DevData& d, uint8_t* columns, cudaStream_t s);
+// Load: a group's columns into the feature-major copy (`col_feature`/`col_bins` per group column; a bin out of its
+// feature's range sets `bad`), then, once every group is in, the tiles from the copy (whole 128-row blocks of each
+// column: column_stride is the row count rounded up to 128).
+void launch_group_columns(const uint8_t* src, uint64_t rows, uint32_t row_stride, const int32_t* col_feature,
+                          const uint32_t* col_bins, uint8_t* columns, uint64_t column_stride, unsigned int* bad,
+                          cudaStream_t s);
+void launch_tiles(const DevData& d, uint8_t* bins, cudaStream_t s);
 // Counts the operand pairs where the split scan's division (div_rn) differs from CUDA's correctly rounded one.
 void launch_division_check(uint64_t n, uint32_t seed, unsigned long long* mismatches, int grid, cudaStream_t s);
 void launch_api_find_split(const DevData& d, const int* hist, const uint8_t* evaluate, double ug, double uh,

@@ -315,13 +315,14 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
  * histogram, partition, split search, leaf sums, finalize (renewal and the tree record), score update, NCCL
  * collectives, and the whole tree when one persistent kernel grows it (single GPU; the histogram, partition and
  * search entries are then 0); then that kernel's phases summed over the tree's steps (device clock of its first
- * CTA): the partition with the built child's histogram, slab reduction, search, finish, and the time spent in grid
- * barriers (num_ops <= 15; fewer fills a prefix). The per-operation breakdown of the reference's `Timed` test backend
+ * CTA): the partition with the built child's histogram, the children's search context, the slab reduction with the
+ * search, finish, and the time spent in grid barriers (num_ops <= 15; fewer fills a prefix). The per-operation breakdown of the reference's `Timed` test backend
  * (crates/silvic-core/tests/train_cpu.rs:434-484). `out` (may be NULL) receives the model. */
 int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_score, double* seconds_by_op,
                       size_t num_ops, sb2_model** out);
 /* The same run; `rows` (max_steps rows of 8 doubles) receives one row per split step of the last tree (row 0 the
- * root): seconds in the partition with the built child's histogram, slab reduction, search, finish, grid barriers
+ * root): seconds in the partition with the built child's histogram, search context, slab reduction with the search,
+ * finish, grid barriers
  * (device clock of the tree kernel's first CTA), then the rows of the step's histogram, 1 when the slabs held packed
  * sums (0: unpacked), and the rows of the leaf that was split.
  * *num_steps gets the rows written. Single GPU only (SB2_EUNSUPPORTED otherwise). */

@@ -227,8 +227,8 @@ class B200Backend:
         return secs.value
 
     PROFILE_OPS = ("gradients", "quantize", "histogram", "partition", "search", "leaf_sums", "finalize",
-                   "add_tree", "collectives", "tree", "tree.partition_histogram", "tree.slab_reduce", "tree.search",
-                   "tree.finish", "tree.barriers")
+                   "add_tree", "collectives", "tree", "tree.partition_histogram", "tree.search_context",
+                   "tree.reduce_search", "tree.finish", "tree.barriers")
 
     def profile_train(self, params: _abi.Params, init_score: float) -> tuple[dict, "Model"]:
         """Device seconds per operation of the last iteration (graph-free, CUDA events), and the model."""
@@ -240,8 +240,8 @@ class B200Backend:
         finally:
             self._lib.sb2_model_free(m)
 
-    STEP_FIELDS = ("partition_histogram", "slab_reduce", "search", "finish", "barriers", "hist_rows", "packed",
-                   "leaf_rows")
+    STEP_FIELDS = ("partition_histogram", "search_context", "reduce_search", "finish", "barriers", "hist_rows",
+                   "packed", "leaf_rows")
 
     def profile_steps(self, params: _abi.Params, init_score: float, max_steps: int = 1 << 17) -> np.ndarray:
         """Per split step of the last tree (row 0 the root): the tree kernel's phase seconds and the step's sizes,

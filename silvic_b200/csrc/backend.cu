@@ -472,6 +472,8 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         d.num_bins = m.num_bins;
         d.nan_bin = m.nan_bin;
         d.kind = m.kind;
+        d.slab_off = 0;
+        d.pad_ = 0;
         if (m.num_bins > 0 && m.kind != SB2_TRIVIAL) {
             if (m.group >= train->num_groups) return b->fail(SB2_EDATA, "feature in a missing group");
             used.push_back(f);
@@ -529,6 +531,23 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         max_unit_bytes = std::max(max_unit_bytes, bytes);
         b->units.push_back(u);
         unit_features.push_back(feats);
+    }
+    // Where each feature's bins sit in the tree kernel's slabs: feature-major inside each unit's region (the unit's
+    // tiles in order, each tile's lanes in order, smem_bins slots per lane), so a feature's bins are contiguous.
+    {
+        uint32_t before = 0;  // slots of the earlier units
+        for (const Unit& u : b->units) {
+            uint32_t p = 0;  // slots of the unit's earlier tiles
+            for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
+                const Tile& tile = b->tiles[t];
+                for (uint32_t l = 0; l < tile.nfeat; ++l) {
+                    const int32_t f = lane_feature[t * kTileLanes + l];
+                    if (f >= 0) b->dev_features[f].slab_off = before + p + l * tile.smem_bins;
+                }
+                p += tile.smem_bins * tile.stride;
+            }
+            before += u.slots;
+        }
     }
     // The kernel aligns its histogram to kHistAlign bytes inside the dynamic shared memory.
     b->hist_smem = static_cast<int>(std::max<size_t>(max_unit_bytes, 16) + kHistAlign);
@@ -661,10 +680,9 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     for (const Unit& u : b->units) b->slab_ints += 2 * u.slots;
     // The reduction's quads: per unit, per tile, four consecutive slots (one bin, lanes l .. l + 3).
     std::vector<QuadMeta> quads;
-    uint32_t units_before = 0;  // slots of the earlier units
     for (uint32_t ui = 0; ui < b->units.size(); ++ui) {
         const Unit& u = b->units[ui];
-        uint32_t off = 0, poff = 0;
+        uint32_t off = 0;
         for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
             const Tile& tile = b->tiles[t];
             const uint32_t n = tile.smem_bins * tile.stride;
@@ -673,9 +691,6 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 m.unit = ui;
                 m.g_off = off + s;
                 m.h_off = off + n + s;
-                m.p_off = poff + s;
-                m.unit_off = 2 * units_before;
-                m.unit_off_packed = units_before;
                 const uint32_t bin = s / tile.stride, lane0 = s % tile.stride;
                 for (uint32_t i = 0; i < 4; ++i) {
                     const int32_t f = lane_feature[t * kTileLanes + lane0 + i];
@@ -686,9 +701,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 quads.push_back(m);
             }
             off += 2 * n;
-            poff += n;
         }
-        units_before += u.slots;
     }
     b->num_quads = static_cast<uint32_t>(quads.size());
     // Threads per quad: as many as keep every thread of one histogram grid busy, up to a warp.
@@ -1360,6 +1373,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
             t.sums_feature = static_cast<int32_t>(f);
             break;
         }
+    t.root_from_rows = b->persistent() ? 1 : 0;  // one GPU: the root's sums straight from the rows
     t.num_iterations = iters;
     t.leaves = tb.leaves.as<DevLeaf>();
     t.leaf_gain = tb.leaf_gain.as<double>();

@@ -41,6 +41,8 @@ struct DevFeature {
     uint32_t num_bins;
     uint32_t nan_bin;
     uint32_t kind;
+    uint32_t slab_off;    // the tree kernel's slabs: this feature's packed bins start here ([g, h] pairs at twice it)
+    uint32_t pad_;
 };
 
 // The loaded training shard, passed to kernels by value.

@@ -22,6 +22,7 @@
 
 #include "hist_device.cuh"
 #include "partition.cuh"
+#include "search.cuh"
 #include "train.cuh"
 
 namespace sb2 {
@@ -45,6 +46,24 @@ __device__ __forceinline__ void fused_range(uint32_t count, uint32_t chunks, uin
     lo = static_cast<uint32_t>(min(static_cast<uint64_t>(count), 32 * (words * cta / chunks)));
     hi = static_cast<uint32_t>(min(static_cast<uint64_t>(count), 32 * (words * (cta + 1) / chunks)));
 }
+
+// Shared-memory accesses by 32-bit shared address.
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v)); }
 
 // Whether the slabs of a phase over `count` positions hold packed sums: every CTA's range fits one packed round.
 __host__ __device__ __forceinline__ bool fused_packed(uint32_t count, uint32_t chunks, uint32_t round_rows) {
@@ -105,19 +124,71 @@ __device__ __forceinline__ bool fused_unit_begin(const HistCta& c, const uint8_t
     return any != 0;
 }
 
-// The unit's shared sums into the CTA's slab: packed as they are (`packed`: the slab region is one int per slot) or
-// unpacked (stored when `first`, added otherwise); the shared sums are left cleared. Whole CTA.
-__device__ __forceinline__ void fused_unit_flush(const HistCta& c, int4* sh4, uint32_t sh_addr, int* slab_unit,
-                                                 bool packed, bool first) {
+// The unit's shared sums into the CTA's slab, feature-major: per tile, per lane (feature), the lane's bin slots in a
+// row (DevFeature::slab_off), so the reduction reads a feature's bins contiguously. Packed (`packed`): one int per
+// bin as it is; unpacked: a [g, h] pair per bin, stored when `first`, added otherwise. The shared sums are left
+// cleared. Whole CTA. Per tile, through `stage` (shared, at least 32 (smem_bins + 4) words; 0 when absent): thread i
+// reads bins 4q .. 4q+3 of lane i mod S (S = the tile's stride; the lanes of a warp read different banks) and
+// stores them lane-major at a pitch of smem_bins + 4 words (eight lanes of a 128-bit store hit 32 banks); then the
+// tile's lanes are copied out row by row with coalesced 16-byte stores. Without staging room the quads are stored
+// from the first step directly.
+__device__ __forceinline__ void fused_unit_flush(const HistCta& c, int* slab_packed, int* slab_pairs, bool packed,
+                                                 bool first, uint32_t stage) {
     __syncthreads();
-    if (packed) {
-        int4* dst = reinterpret_cast<int4*>(slab_unit);
-        for (uint32_t i = threadIdx.x; i < c.unit.slots / 4; i += kHistThreads) {
-            __stcg(dst + i, sh4[i]);
-            sh4[i] = make_int4(0, 0, 0, 0);
+    uint32_t p = 0;  // slots of the unit's earlier tiles
+    for (uint32_t t = 0; t < c.unit.num_tiles; ++t) {
+        const LaneTile& tile = c.tiles[t];
+        const uint32_t S = tile.stride, quads = tile.bins / 4, pitch = tile.bins + 4;
+        // Stores the 4 bins of quad q of lane l (packed values v) into the slab.
+        auto put = [&](uint32_t l, uint32_t q, const uint4& v) {
+            const uint32_t at = p + l * tile.bins + 4 * q;  // the 4 bins' first slot in the feature-major region
+            if (packed) {
+                __stcg(reinterpret_cast<uint4*>(slab_packed + at), v);
+                return;
+            }
+            // unpack (quantize.rs:140-143): g is the low half sign-extended, h what remains above it
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            int g[4], h[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                g[k] = static_cast<int16_t>(w[k] & 0xFFFFu);
+                h[k] = static_cast<int>((w[k] - static_cast<uint32_t>(g[k])) >> 16);
+            }
+            int4* dst = reinterpret_cast<int4*>(slab_pairs + 2 * at);
+            int4 x = make_int4(g[0], h[0], g[1], h[1]), y = make_int4(g[2], h[2], g[3], h[3]);
+            if (!first) {
+                const int4 ox = __ldcg(dst), oy = __ldcg(dst + 1);
+                x = make_int4(x.x + ox.x, x.y + ox.y, x.z + ox.z, x.w + ox.w);
+                y = make_int4(y.x + oy.x, y.y + oy.y, y.z + oy.z, y.w + oy.w);
+            }
+            __stcg(dst, x);
+            __stcg(dst + 1, y);
+        };
+        for (uint32_t i = threadIdx.x; i < quads * S; i += kHistThreads) {
+            const uint32_t l = i % S, q = i / S;
+            const uint32_t a0 = tile.addr + 4 * (4 * q * S + l);  // bin 4q of lane l
+            uint4 v;
+            v.x = lds32(a0);
+            v.y = lds32(a0 + 4 * S);
+            v.z = lds32(a0 + 8 * S);
+            v.w = lds32(a0 + 12 * S);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sts32(a0 + 4 * k * S, 0u);
+            if (stage != 0)
+                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(stage + 4 * (l * pitch + 4 * q)), "r"(v.x),
+                             "r"(v.y), "r"(v.z), "r"(v.w));
+            else
+                put(l, q, v);
         }
-    } else {
-        flush_packed(c, sh4, sh_addr, slab_unit, first, true);
+        if (stage != 0) {
+            __syncthreads();
+            for (uint32_t i = threadIdx.x; i < quads * S; i += kHistThreads) {
+                const uint32_t l = i / quads, q = i % quads;
+                put(l, q, lds128(stage + 4 * (l * pitch + 4 * q)));
+            }
+            __syncthreads();  // the staging words are free for the next tile
+        }
+        p += tile.bins * S;
     }
     __syncthreads();
 }
@@ -164,22 +235,6 @@ __device__ __forceinline__ void cp_async_wait(uint32_t pending) {
     }
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v)); }
 
 // Staging slot of a batch: per tile, 32 rows of `stride` bytes (lane k's row at k * stride), then the batch's 32
 // packed gradients. A 32-byte row's two halves are swapped on lanes with bit 2 set, so that the eight lanes of a
@@ -472,8 +527,6 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
         b1 = b0 + (fs.built_left ? left : right);
     }
     const uint64_t pol = evict_first_policy();
-    const uint32_t sh_addr = hist_shared_base(sh);
-    int4* sh4 = reinterpret_cast<int4*>(sh + (sh_addr - static_cast<uint32_t>(__cvta_generic_to_shared(sh))) / 4);
     __shared__ LaneTile s_lt[kMaxUnitTiles];
     int* slab = h.slabs + static_cast<size_t>(cta) * h.slab_ints;
     uint32_t region = 0;  // ints before this unit's slab region
@@ -492,7 +545,8 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             const bool last = r1 >= b1;
             // Packed slabs: one flush at the end. Unpacked: a flush per round, stored the first time, added after.
             if (last || !fs.packed)
-                fused_unit_flush(*c, sh4, sh_addr, slab + (fs.packed ? region / 2 : region), fs.packed, r0 == b0);
+                fused_unit_flush(*c, slab + region / 2, slab + region, fs.packed, r0 == b0,
+                                 fs.depth > 0 && fs.depth * kWarps * fs.slot_bytes >= 4 * 32 * (256 + 4) ? fs.stage : 0u);
             if (last) break;
             r0 = r1;
         }
@@ -500,76 +554,115 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     }
 }
 
-// The step's slab reduction (thread `thread` of `threads`): histogram_reduce_quads over slabs that hold every unit,
-// packed or not. Each quad takes as many threads as the grid has to spare (a power of two up to a warp), each
-// thread up to kLoads of its chunks' loads in flight at once.
+// ---- the built child's histogram and the search, one feature per CTA ---------------------------------------
+
+// Feature `f`'s bins of the built child summed over the step's `chunks` slabs into `out` (shared, [g, h] per bin):
+// thread t of the CTA takes bin t mod 256 over the chunks c = t / 256, t / 256 + 2, ... (a warp reads 32
+// consecutive bins of a chunk: 128 or 256 bytes), with kLoads chunks in flight; the odd chunks' sums meet the even
+// ones' through `part` (shared). Whole CTA (kHistThreads threads).
 template <bool kPacked>
-__device__ __forceinline__ void fused_reduce_quads(const HistArgs& a, uint32_t chunks, uint32_t thread,
-                                                   uint32_t threads) {
-    constexpr int kLoads = kPacked ? 8 : 4;  // chunks per thread and batch (an int4 each, two when unpacked)
-    uint32_t split = 1;
-    while (split < 32 && 2 * split * a.num_quads <= threads) split *= 2;
-    const uint32_t j = thread & (split - 1);
-    const uint32_t groups = threads / split;
-    const uint32_t rounds = static_cast<uint32_t>(ceil_div(a.num_quads, groups));
-    for (uint32_t r = 0; r < rounds; ++r) {  // the same count on every lane: the shuffles need the whole warp
-        const uint32_t q = r * groups + thread / split;
-        int4 g = make_int4(0, 0, 0, 0), hs = g;
-        QuadMeta m{};
-        const bool mine = q < a.num_quads;
-        if (mine) {
-            m = a.quads[q];
-            const uint32_t off = kPacked ? m.unit_off_packed + m.p_off : m.unit_off + m.g_off;
-            const uint32_t off_h = m.unit_off + m.h_off;
-            for (uint32_t c0 = j; c0 < chunks; c0 += kLoads * split) {
-                int4 v[kLoads], w[kLoads];
+__device__ __forceinline__ void reduce_feature_bins(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
+                                                    int2* part, int2* out) {
+    constexpr int kLoads = 16;
+    const uint32_t b = threadIdx.x & 255, half = threadIdx.x >> 8;
+    int sg = 0, sh = 0;
+    if (b < feat.num_bins) {
+        const int* base = h.slabs + (kPacked ? feat.slab_off + b : 2 * (feat.slab_off + b));
+        for (uint32_t c0 = half; c0 < chunks; c0 += 2 * kLoads) {
+            uint32_t v[kLoads];
+            int2 w[kLoads];
 #pragma unroll
-                for (int k = 0; k < kLoads; ++k) {
-                    const uint32_t c = c0 + k * split;
-                    const int* slab = a.slabs + static_cast<size_t>(c) * a.slab_ints;
-                    const bool in = c < chunks;
-                    v[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + off)) : make_int4(0, 0, 0, 0);
-                    if (!kPacked) w[k] = in ? __ldcg(reinterpret_cast<const int4*>(slab + off_h)) : make_int4(0, 0, 0, 0);
-                }
+            for (int k = 0; k < kLoads; ++k) {
+                const uint32_t c = c0 + 2 * k;
+                const int* at = base + static_cast<size_t>(c) * h.slab_ints;
+                if (kPacked)
+                    v[k] = c < chunks ? static_cast<uint32_t>(__ldcg(at)) : 0u;
+                else
+                    w[k] = c < chunks ? __ldcg(reinterpret_cast<const int2*>(at)) : make_int2(0, 0);
+            }
 #pragma unroll
-                for (int k = 0; k < kLoads; ++k) {
-                    if (kPacked) {
-                        // unpack (quantize.rs:140-143)
-                        const int4 x = v[k];
-                        const int4 gx = make_int4(static_cast<int16_t>(x.x & 0xFFFF), static_cast<int16_t>(x.y & 0xFFFF),
-                                                  static_cast<int16_t>(x.z & 0xFFFF), static_cast<int16_t>(x.w & 0xFFFF));
-                        g = add4(g, gx);
-                        hs = add4(hs, make_int4(static_cast<int>(static_cast<uint32_t>(x.x - gx.x) >> 16),
-                                                static_cast<int>(static_cast<uint32_t>(x.y - gx.y) >> 16),
-                                                static_cast<int>(static_cast<uint32_t>(x.z - gx.z) >> 16),
-                                                static_cast<int>(static_cast<uint32_t>(x.w - gx.w) >> 16)));
-                    } else {
-                        g = add4(g, v[k]);
-                        hs = add4(hs, w[k]);
-                    }
+            for (int k = 0; k < kLoads; ++k) {
+                if (kPacked) {
+                    const int g = static_cast<int16_t>(v[k] & 0xFFFFu);  // quantize.rs:140-143
+                    sg += g;
+                    sh += static_cast<int>((v[k] - static_cast<uint32_t>(g)) >> 16);
+                } else {
+                    sg += w[k].x;
+                    sh += w[k].y;
                 }
             }
         }
-        for (uint32_t o = split >> 1; o > 0; o >>= 1) {
-            g = add4(g, shfl_xor4(g, static_cast<int>(o)));
-            hs = add4(hs, shfl_xor4(hs, static_cast<int>(o)));
-        }
-        if (mine && j == 0) {
-            int2* out = reinterpret_cast<int2*>(a.out);
-            if (m.out[0] >= 0) __stcg(out + m.out[0], make_int2(g.x, hs.x));
-            if (m.out[1] >= 0) __stcg(out + m.out[1], make_int2(g.y, hs.y));
-            if (m.out[2] >= 0) __stcg(out + m.out[2], make_int2(g.z, hs.z));
-            if (m.out[3] >= 0) __stcg(out + m.out[3], make_int2(g.w, hs.w));
-        }
+        if (half == 1) part[b] = make_int2(sg, sh);
     }
+    __syncthreads();
+    if (half == 0 && b < feat.num_bins) out[b] = make_int2(sg + part[b].x, sh + part[b].y);
+    __syncthreads();
 }
 
-inline __device__ void fused_reduce(const HistArgs& a, uint32_t chunks, bool packed, uint32_t thread,
-                                    uint32_t threads) {
+// The step's search for feature `f` in one CTA, both children at once: the built child's bins reduced from the
+// slabs, then group 0 scans the built child and group 1 the sibling (parent - built, learner.rs:365-367), each with
+// scan_feature_group, as search_item_group does for one item. `bufs` is 2 kMaxBins int2 of shared memory.
+__device__ void search_feature_cta(const TrainArgs& a, const HistArgs& h, const Step& st, const SearchCtx& s,
+                                   uint32_t f, uint32_t chunks, bool packed, int2* bufs, ScanShared* scan_sh) {
+    const uint32_t F = a.num_features;
+    const uint32_t group = threadIdx.x / kScanThreads, t = threadIdx.x % kScanThreads;
+    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
+    const DevFeature feat = a.d.features[f];
+    if (!load_flag(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
+        if (threadIdx.x == 0) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
+            cands[f] = none;
+            cands[F + f] = none;
+            if (a.cand_flags) {
+                a.cand_flags[f] = 0;
+                a.cand_flags[F + f] = 0;
+            }
+        }
+        return;
+    }
+    int2* built = bufs;
+    int2* other = bufs + kMaxBins;
     if (packed)
-        fused_reduce_quads<true>(a, chunks, thread, threads);
+        reduce_feature_bins<true>(h, feat, chunks, other, built);
     else
-        fused_reduce_quads<false>(a, chunks, thread, threads);
+        reduce_feature_bins<false>(h, feat, chunks, other, built);
+    const size_t slot_len = 2 * static_cast<size_t>(a.total_bins);
+    const size_t off = 2 * static_cast<size_t>(feat.hist_offset);
+    const bool mine = t < feat.num_bins;
+    const int ch = static_cast<int>(group);
+    if (st.root) {
+        if (group == 0 && mine) __stcg(reinterpret_cast<int2*>(a.slots + off) + t, built[t]);
+    } else if (group == 1 && mine) {
+        const int2 p = __ldcg(reinterpret_cast<const int2*>(a.slots + static_cast<size_t>(st.leaf) * slot_len + off) + t);
+        const int2 bt = built[t];
+        const int2 o = make_int2(p.x - bt.x, p.y - bt.y);
+        other[t] = o;
+        // group 1 alone reads the parent's slot, which the built child may take over: it writes both children's
+        __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[0]) * slot_len + off) + t, bt);
+        __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[1]) * slot_len + off) + t, o);
+    }
+    const int bar = 1 + ch;
+    if (st.root && group == 1) {
+        if (t == 0) {
+            FeatureCandidate none{};
+            none.feature = static_cast<int32_t>(f);
+            cands[F + f] = none;
+            if (a.cand_flags) a.cand_flags[F + f] = 0;
+        }
+    } else {
+        group_sync(bar);  // the group's bins are in place
+        const FeatureCandidate c = scan_feature_group(ch == 0 ? built : other, feat, static_cast<int>(f), s.ctx[ch],
+                                                      a.cfg, scan_sh[group], bar);
+        if (t == 0) {
+            cands[static_cast<size_t>(ch) * F + f] = c;
+            if (a.cand_flags) {
+                a.cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
+                a.cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
+            }
+        }
+    }
+    __syncthreads();  // the buffers and the scratch are free for the CTA's next feature
 }
 
 }  // namespace sb2

@@ -144,11 +144,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     const TrainArgs& a = g.t;
     const uint32_t cta = blockIdx.x, ctas = gridDim.x;
     const uint32_t warp = threadIdx.x >> 5;
-    // Search items go to groups of kScanWarps warps, round the CTAs first (item i to group i / ctas of CTA i mod
-    // ctas), so a step's few hundred scans spread over every SM instead of filling a dozen.
+    // The search's two groups of kScanWarps warps (one per child) and their scratch.
     constexpr uint32_t kGroups = kGrowThreads / kScanThreads;
-    const uint32_t group = threadIdx.x / kScanThreads;
-    const uint32_t item0 = group * ctas + cta, items_stride = ctas * kGroups;
+    static_assert(kGroups == 2, "one scan group per child");
     __shared__ ScanShared scan_shared[kGroups];
     const uint32_t F = a.num_features;
     // Every CTA keeps the learner's control state itself: the step, the evaluated features. The finish runs in
@@ -213,34 +211,20 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         clock_mark(g, clock, 0);
         if (!grid_barrier(g, target)) return;
         clock_mark(g, clock, 4);
-        // The left count, then the slab reduction into staging; the children's search context meanwhile.
+        // The left count and the children's search context (every CTA: the finish is replicated), then the
+        // search: one feature per CTA, its built child's bins reduced from the slabs and both children scanned.
         if (!st.root && threadIdx.x == 0) s_left = __ldcg(cursor);
         __syncthreads();
-        if (f.histogram) {
-            fused_reduce(g.h, f.chunks, f.packed, cta * kGrowThreads + threadIdx.x, ctas * kGrowThreads);
-            clock_mark(g, clock, 1);
-            barrier_arrive(g, target);
-            if (!st.root && warp == 1) {
-                const SearchCtx c = search_context(a, st, static_cast<int64_t>(s_left), eval, mask);
-                if (lane_id() == 0) s = c;
-            }
-            if (!barrier_wait(g, target)) return;
-            clock_mark(g, clock, 4);
-        } else if (!st.root && warp == 1) {
-            const SearchCtx c = search_context(a, st, static_cast<int64_t>(s_left), eval, mask);
+        if (warp == 0) {
+            const SearchCtx c = search_context(a, st, st.root ? 0 : static_cast<int64_t>(s_left), eval, mask);
             if (lane_id() == 0) s = c;
         }
-        if (st.root) {  // the root's sums come from its histogram
-            if (warp == 0) {
-                const SearchCtx c = search_context(a, st, 0, eval, mask);
-                if (threadIdx.x == 0) s = c;
-            }
-        }
         __syncthreads();
+        clock_mark(g, clock, 1);
         if (s.searched)
-            for (uint32_t item = item0; item < search_items(a, st); item += items_stride)
-                search_item_group(a, st, s, item, reinterpret_cast<int2*>(scan) + group * kMaxBins,
-                                  scan_shared[group], 1 + static_cast<int>(group));
+            for (uint32_t feature = cta; feature < F; feature += ctas)
+                search_feature_cta(a, g.h, st, s, feature, f.chunks, f.packed, reinterpret_cast<int2*>(scan),
+                                   scan_shared);
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.

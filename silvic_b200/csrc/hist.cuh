@@ -42,18 +42,14 @@ struct HistJob {
 };
 
 // Four consecutive gradient slots of one tile (one bin, four feature lanes) as the reductions sum them: their
-// offsets in a unit's slab region (unpacked: per tile a gradient array then a hessian array; packed: the tiles'
-// packed arrays in a row, as in shared memory), where the unit's region starts when one slab holds every unit, and
-// the output pair index of each lane (hist_offset + bin), -1 for a lane without a feature or a bin past the
-// feature's bins. Built at load.
+// offsets in a unit's slab region (per tile a gradient array then a hessian array) and the output pair index of
+// each lane (hist_offset + bin), -1 for a lane without a feature or a bin past the feature's bins. Built at load.
 struct QuadMeta {
     uint32_t unit;
     uint32_t g_off;   // ints from the unit's slab region to the gradient slot
     uint32_t h_off;   // ... to the hessian slot
-    uint32_t p_off;   // ... to the packed slot, in a region that holds packed sums (one int per slot)
+    uint32_t pad_;
     int32_t out[4];
-    uint32_t unit_off;         // where the unit's region starts in a slab holding every unit: 2 * earlier slots
-    uint32_t unit_off_packed;  // ... in a packed slab holding every unit: earlier slots
 };
 
 struct HistArgs {

@@ -158,12 +158,35 @@ __global__ void __launch_bounds__(kRowThreads) iteration_start_kernel(IterArgs a
         return;
     }
     const sb2_quant_spec spec = s_spec;
+    long long sum_g = 0, sum_h = 0;
     for (uint64_t row = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; row < a.r.num_rows;
          row += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
         const int32_t p = quantize_row(spec, a.r.grad[row], a.r.hess[row], a.r.row_offset + row);
         a.r.packed[row] = p;
         a.t.rows[0][row] = static_cast<uint32_t>(row);
         a.t.ordered[0][row] = p;
+        const int32_t g = static_cast<int16_t>(static_cast<uint16_t>(static_cast<uint32_t>(p)));  // quantize.rs:140-143
+        sum_g += g;
+        sum_h += (p - g) >> 16;
+    }
+    // The root's units: this block's sums, then one 64-bit atomic per value (two's complement adds exactly).
+    for (int o = 16; o > 0; o >>= 1) {
+        sum_g += __shfl_xor_sync(0xffffffffu, sum_g, o);
+        sum_h += __shfl_xor_sync(0xffffffffu, sum_h, o);
+    }
+    __shared__ long long s_sums[2][kRowThreads / 32];
+    if ((threadIdx.x & 31) == 0) {
+        s_sums[0][threadIdx.x >> 5] = sum_g;
+        s_sums[1][threadIdx.x >> 5] = sum_h;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < kRowThreads / 32; ++k) {
+            sum_g += s_sums[0][k];
+            sum_h += s_sums[1][k];
+        }
+        atomicAdd(&it->root_units[0], static_cast<unsigned long long>(sum_g));
+        atomicAdd(&it->root_units[1], static_cast<unsigned long long>(sum_h));
     }
     if (blockIdx.x != 0) return;
     const uint32_t F = a.t.num_features;
@@ -368,6 +391,7 @@ __global__ void __launch_bounds__(kRowThreads) finalize_kernel(IterArgs a) {
         it->iteration = iteration + 1;
         it->max_abs_grad_bits = 0ull;
         it->max_hess_bits = 0ull;
+        it->root_units[0] = it->root_units[1] = 0ull;
     }
 }
 

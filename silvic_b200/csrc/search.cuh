@@ -490,6 +490,11 @@ __device__ __forceinline__ double nan_to_zero(double v) { return v != v ? 0.0 : 
 
 // The root's LeafSums units from the bins of the sums feature (LeafSums::from_feature_hist, split.rs:101-108).
 __device__ void root_units(const TrainArgs& a, double& ug, double& uh) {
+    if (a.root_from_rows) {
+        ug = static_cast<double>(static_cast<int64_t>(__ldcg(&a.iter->root_units[0])));
+        uh = static_cast<double>(static_cast<int64_t>(__ldcg(&a.iter->root_units[1])));
+        return;
+    }
     const int lane = threadIdx.x & 31;
     const DevFeature f = a.d.features[a.sums_feature];
     int64_t g = 0, h = 0;

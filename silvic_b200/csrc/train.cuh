@@ -79,6 +79,9 @@ struct IterState {
     unsigned long long max_hess_bits;
     sb2_quant_spec spec;
     int64_t root_count;    // bagged rows over every rank
+    // This rank's sums of every row's quantized g and h (iteration start): the root's units when one GPU grows the
+    // tree (every row falls in one bin of every feature, so they equal the sums over any feature's histogram).
+    unsigned long long root_units[2];
 };
 
 // Everything the training kernels read, by value.
@@ -88,6 +91,7 @@ struct TrainArgs {
     int32_t max_leaves;      // params.num_leaves
     int32_t max_depth;
     int32_t sums_feature;    // first non-trivial feature (learner.rs:115), -1 when none
+    int32_t root_from_rows;  // 1: the root's units come from IterState::root_units instead of the histogram
     int32_t num_iterations;
     uint32_t total_bins;
     uint32_t num_features;
@@ -141,7 +145,8 @@ constexpr int kSearchThreads = 256;   // 8 warps, one feature each
 int grow_threads();
 cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: the partition with
-// the built child's histogram, the slab reduction, the search, the finish, the grid barriers. With `trace_steps` > 0
+// the built child's histogram, the children's search context, the slab reduction with the search, the finish, the
+// grid barriers. With `trace_steps` > 0
 // it is followed by one row of kStepTrace values per step (up to trace_steps): the same phase times of that step,
 // then the rows of its histogram, whether the slabs held packed sums (1) or unpacked ones (0), and the rows of the
 // leaf it split.

@@ -134,8 +134,9 @@ def build_dataset(begin: int, end: int, device, chunk: int = 2_000_000):
     group_feats = [list(range(s, min(s + per_group, FEATURES))) for s in range(0, FEATURES, per_group)]
     strides = [(len(g) + 3) // 4 * 4 for g in group_feats]
     # Page-locked host arrays: the load's host-to-device copies run at DMA speed (and count in the e2e time).
-    pinned = [torch.empty((n, s), dtype=torch.uint8, pin_memory=True) for s in strides]
-    pinned.append(torch.empty(n, dtype=torch.float32, pin_memory=True))
+    pin = torch.cuda.is_available()
+    pinned = [torch.empty((n, s), dtype=torch.uint8, pin_memory=pin) for s in strides]
+    pinned.append(torch.empty(n, dtype=torch.float32, pin_memory=pin))
     host = [t.numpy() for t in pinned[:-1]]
     label = pinned[-1].numpy()
     b32 = bounds.to(torch.float32)
@@ -240,8 +241,9 @@ def measured_peak_hbm() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, max_leaves: int) -> int:
-    """Bytes one tree's growth must move at the least (one GPU, `n_rows` rows of `row_bytes` bin bytes).
+def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, max_leaves: int, world: int = 1) -> int:
+    """Bytes one GPU's tree kernel must move at the least to grow `tree` (`n_rows` rows of `row_bytes` bin bytes on
+    this GPU; with `world` ranks the tree's node counts are global, and each rank holds 1/world of every leaf).
 
     The root histogram reads every row's bins and packed gradient (its rows are in row order: no row ids) and writes
     a histogram of `total_bins` [g, h] int32 pairs. Split k of a parent of P rows reads each row's id (not for the
@@ -250,11 +252,11 @@ def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, m
     gradients and bins, and the histogram out. Split k is internal node k (nodes are numbered in split order).
     """
     def count(c: int) -> int:
-        return int(tree.internal_count[c]) if c >= 0 else int(tree.leaf_count[~c])
+        return (int(tree.internal_count[c]) if c >= 0 else int(tree.leaf_count[~c])) // world
 
     total = n_rows * (row_bytes + 4) + 8 * total_bins
     for k in range(len(tree.internal_count)):
-        parent = int(tree.internal_count[k])
+        parent = int(tree.internal_count[k]) // world
         total += parent * ((0 if k == 0 else 4) + 4 + 1) + parent * 8
         if k + 2 < max_leaves:
             built = min(count(int(tree.left_child[k])), count(int(tree.right_child[k])))
@@ -355,7 +357,7 @@ def run_b200(args, rank: int, world: int):
     # The standalone root histogram (every row, every feature), the kernel the multi-GPU path runs per split.
     hist_s = backend.time_histogram(10)
     backend.close()
-    launches_persistent = world == 1  # one GPU grows each tree in one cooperative launch
+    launches_persistent = bool(model.tree_seconds)  # each tree in one cooperative launch (per GPU)
     t = torch.tensor([timed, hist_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -395,7 +397,7 @@ def run_b200(args, rank: int, world: int):
     hist_roofline["frac"] = hist_roofline["achieved"] / peak
     if tree_s and len(tree_s) == len(timed_trees):
         # The dominant kernel: the persistent tree kernel, one launch per tree.
-        tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, PARAMS["num_leaves"]) for tr in timed_trees]
+        tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, PARAMS["num_leaves"], world) for tr in timed_trees]
         launch_s = sum(tree_s) / len(tree_s)
         per_launch = sum(tree_bytes) / len(tree_bytes)
         roofline = {"bound": "hbm", "achieved": per_launch / launch_s / 1e9, "peak": peak, "unit": "GB/s",

@@ -110,8 +110,24 @@ struct sb2_backend {
     // multi-GPU
     ncclComm_t comm = nullptr;
     int world = 1, rank = 0;
+    // The tree kernel's exchange with the other ranks (GrowExchange): this rank's buffer and every rank's mapped
+    // here through CUDA IPC; set up by the first training run after the ranks joined.
+    DeviceBuffer xbuf;
+    void* xpeers[kMaxRanks] = {};
+    size_t xbytes = 0;
+    bool xready = false;
+    uint32_t xepoch = 0;  // the last epoch a launch used
+
+    void close_exchange() {
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (r != rank && xpeers[r]) cudaIpcCloseMemHandle(xpeers[r]);
+        for (auto& p : xpeers) p = nullptr;
+        xready = false;
+        xbytes = 0;
+    }
 
     ~sb2_backend() {
+        close_exchange();
         if (comm) ncclCommDestroy(comm);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -228,7 +244,8 @@ struct sb2_backend {
     }
     int sync() { return cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize"); }
     // Single-GPU training grows each tree in one persistent launch; with NCCL ranks, per-step launches.
-    bool persistent() const { return grow_ok && comm == nullptr; }
+    // One launch per tree: one GPU, or ranks whose exchange is set up.
+    bool persistent() const { return grow_ok && (comm == nullptr || xready); }
 };
 
 namespace {
@@ -1126,6 +1143,7 @@ int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int wor
         ncclCommDestroy(b->comm);
         b->comm = nullptr;
     }
+    b->close_exchange();
     b->world = world;
     b->rank = rank;
     if (world == 1) return SB2_OK;
@@ -1245,11 +1263,24 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
         }));
     SB2_TRY(op(kOpQuantize, [&] { launch_iteration_start(ia, row_grid, s); return SB2_OK; }));
     if (b->persistent()) {
-        // One launch grows the whole tree (grow.cu).
+        // One launch grows the whole tree (grow.cu); ranks sum the root's units first and exchange the rest inside.
+        GrowExchange x{};
+        x.world = b->comm ? b->world : 1;
+        x.rank = b->comm ? b->rank : 0;
+        if (b->comm) {
+            for (int r = 0; r < b->world; ++r) x.peers[r] = static_cast<uint8_t*>(b->xpeers[r]);
+            x.epoch0 = b->xepoch;
+            b->xepoch += static_cast<uint32_t>(max_leaves) + 2;
+            SB2_TRY(op(kOpCollective, [&] {
+                return nccl_status(b, ncclAllReduce(t.iter->root_units, t.iter->root_units, 2, ncclUint64, ncclSum,
+                                                    b->comm, s),
+                                   "ncclAllReduce(root units)");
+            }));
+        }
         SB2_TRY(op(kOpTree, [&] {
             if (tree_marks) cudaEventRecord(tree_marks[0], s);
             const int st = b->cuda(launch_grow_tree(t, h, b->grid_barrier.as<unsigned int>(), b->hist_grid,
-                                                    b->grow_smem, s,
+                                                    b->grow_smem, x, s,
                                                     timer ? b->phase_ns.as<unsigned long long>() : nullptr,
                                                     timer ? max_leaves : 0),
                                    "cudaLaunchCooperativeKernel(grow_tree)");
@@ -1297,9 +1328,60 @@ struct Training {
     int iters = 0;
 };
 
+// The tree kernel's exchange with the other ranks (GrowExchange). Collective: every rank calls it, with the same
+// dataset shape. A rank that cannot take part (no cooperative tree kernel, more than kMaxRanks ranks, an IPC
+// mapping refused) makes every rank keep the per-step launches with NCCL.
+int setup_exchange(sb2_backend* b) {
+    if (!b->comm || b->world <= 1) return SB2_OK;
+    const size_t need = exchange_bytes(b->num_features);
+    if (b->xready && b->xbytes == need) return SB2_OK;
+    b->close_exchange();
+    int ok = b->grow_ok && b->world <= kMaxRanks ? 1 : 0;
+    cudaIpcMemHandle_t mine{};
+    if (ok)
+        ok = b->xbuf.alloc(need) == cudaSuccess && cudaMemset(b->xbuf.ptr, 0, need) == cudaSuccess &&
+             cudaIpcGetMemHandle(&mine, b->xbuf.ptr) == cudaSuccess;
+    cudaGetLastError();
+    // Every rank's handle (in-place all-gather), then whether every rank mapped every other rank's buffer.
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    DeviceBuffer hs;
+    SB2_CUDA(b, hs.alloc(hb * b->world + sizeof(int)));
+    SB2_CUDA(b, cudaMemcpyAsync(hs.as<char>() + hb * b->rank, &mine, hb, cudaMemcpyHostToDevice, b->stream));
+    SB2_TRY(nccl_status(b, ncclAllGather(hs.as<char>() + hb * b->rank, hs.ptr, hb, ncclUint8, b->comm, b->stream),
+                        "ncclAllGather(exchange handles)"));
+    std::vector<cudaIpcMemHandle_t> handles(b->world);
+    SB2_CUDA(b, cudaMemcpyAsync(handles.data(), hs.ptr, hb * b->world, cudaMemcpyDeviceToHost, b->stream));
+    SB2_TRY(b->sync());
+    for (int r = 0; r < b->world && ok; ++r) {
+        if (r == b->rank) continue;
+        if (cudaIpcOpenMemHandle(&b->xpeers[r], handles[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            b->xpeers[r] = nullptr;
+            ok = 0;
+            cudaGetLastError();
+        }
+    }
+    int* agree = reinterpret_cast<int*>(hs.as<char>() + hb * b->world);
+    SB2_CUDA(b, cudaMemcpyAsync(agree, &ok, sizeof(int), cudaMemcpyHostToDevice, b->stream));
+    SB2_TRY(nccl_status(b, ncclAllReduce(agree, agree, 1, ncclInt32, ncclMin, b->comm, b->stream),
+                        "ncclAllReduce(exchange ready)"));
+    int all = 0;
+    SB2_CUDA(b, cudaMemcpyAsync(&all, agree, sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+    SB2_TRY(b->sync());
+    if (!all) {
+        b->close_exchange();
+        return SB2_OK;
+    }
+    b->xpeers[b->rank] = b->xbuf.ptr;
+    b->xready = true;
+    b->xbytes = need;
+    b->xepoch = 0;
+    return SB2_OK;
+}
+
 int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Training& tr) {
     SB2_TRY(b->check_loaded());
     SB2_CUDA(b, cudaSetDevice(b->device));
+    SB2_TRY(setup_exchange(b));
     if (p->objective != b->objective.kind) return b->fail(SB2_ECONFIG, "params objective differs from the loaded one");
     if (!p->use_quantized_grad) return b->fail(SB2_EUNSUPPORTED, "the device trainer is quantized only");
     if (p->bagging_fraction < 1.0 && p->bagging_freq > 0)
@@ -1406,6 +1488,8 @@ int collect_model(sb2_backend* b, Training& tr, std::unique_ptr<sb2_model>& mode
     TrainBuffers& tb = tr.tb;
     IterState it{};
     SB2_CUDA(b, cudaMemcpy(&it, b->iter.ptr, sizeof(it), cudaMemcpyDeviceToHost));
+    if (it.error == 4) return b->fail(SB2_ECOLLECTIVE, "a rank did not reach a split step's exchange in time");
+    if (it.error == 3) return b->fail(SB2_EINTERNAL, "a CTA of the tree kernel did not reach a grid barrier in time");
     if (it.error) return b->fail(SB2_EINTERNAL, "internal error " + std::to_string(it.error) + " at leaf " +
                                                     std::to_string(it.error_info));
     std::vector<TreeRecordHeader> heads;

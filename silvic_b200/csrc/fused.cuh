@@ -554,6 +554,103 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     }
 }
 
+// ---- ranks: flags and sums over NVLink ------------------------------------------------------------------------
+
+constexpr unsigned long long kPeerSpins = 1ull << 22;  // polls of a peer's flag (a few seconds) before error 4
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread: waits until a rank's `flag` reaches `epoch`, at most kPeerSpins polls; false (error 4 recorded, or
+// another CTA's error seen) when it gives up.
+__device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, int* error) {
+    for (unsigned long long i = 0;; ++i) {
+        if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+        if (*reinterpret_cast<volatile int*>(error) != 0) return false;
+        if (i > kPeerSpins) {
+            atomicCAS(error, 0, 4);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+// One warp: waits, lane r for rank r (r < world, r != skip), until every rank's flag at byte `off` of its exchange
+// buffer reaches `epoch`; true when all did.
+__device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int skip, int* error) {
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    bool ok = true;
+    if (lane < x.world && lane != skip)
+        ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[lane] + off), epoch, error);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// CTA 0, one thread: this rank's left count of the step into its exchange buffer. The release store orders the
+// value before the flag for every rank that acquires the flag.
+__device__ __forceinline__ void publish_left(const GrowExchange& x, uint32_t epoch, uint32_t left) {
+    uint32_t* own = reinterpret_cast<uint32_t*>(x.peers[x.rank]);
+    own[2 + (epoch & 1)] = left;
+    st_release_sys(own, epoch);
+}
+
+// Whole CTA: every rank's left count of the step, summed into *total; false when a rank did not answer.
+__device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoch, int* error, int64_t* total) {
+    __shared__ int64_t s_total;
+    __shared__ int s_ok;
+    if (threadIdx.x < 32) {
+        const bool ok = wait_ranks(x, 0, epoch, -1, error);
+        const int lane = static_cast<int>(threadIdx.x);
+        int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcv(reinterpret_cast<const uint32_t*>(x.peers[lane]) + 2 + (epoch & 1))) : 0;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) {
+            s_total = v;
+            s_ok = ok;
+        }
+    }
+    __syncthreads();
+    *total = s_total;
+    const bool ok = s_ok != 0;
+    __syncthreads();
+    return ok;
+}
+
+// Whole CTA: feature `f`'s built-child bins of this rank (`built`, shared) published, then replaced by every rank's
+// sum; false when a rank did not answer.
+__device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t epoch, uint32_t F, uint32_t f,
+                                              uint32_t nb, int2* built, int* error) {
+    __shared__ int s_ok;
+    const size_t at = exchange_bins_offset(F) + ((static_cast<size_t>(epoch & 1) * F + f) * kMaxBins) * sizeof(int2);
+    const size_t flag = 128 + 4ull * f;
+    if (threadIdx.x < nb) reinterpret_cast<int2*>(x.peers[x.rank] + at)[threadIdx.x] = built[threadIdx.x];
+    __syncthreads();  // the CTA's bins are written: the release below orders them before the flag
+    if (threadIdx.x == 0) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[x.rank] + flag), epoch);
+    if (threadIdx.x < 32) {
+        const bool ok = wait_ranks(x, flag, epoch, x.rank, error);
+        if (threadIdx.x == 0) s_ok = ok;
+    }
+    __syncthreads();
+    const bool ok = s_ok != 0;
+    if (ok && threadIdx.x < nb) {
+        int2 v[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+            v[r] = r < x.world && r != x.rank ? __ldcv(reinterpret_cast<const int2*>(x.peers[r] + at) + threadIdx.x)
+                                              : make_int2(0, 0);
+        int2 sum = built[threadIdx.x];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) sum = make_int2(sum.x + v[r].x, sum.y + v[r].y);
+        built[threadIdx.x] = sum;
+    }
+    __syncthreads();
+    return ok;
+}
+
 // ---- the built child's histogram and the search, one feature per CTA ---------------------------------------
 
 // Feature `f`'s bins of the built child summed over the step's `chunks` slabs into `out` (shared, [g, h] per bin):
@@ -599,16 +696,32 @@ __device__ __forceinline__ void reduce_feature_bins(const HistArgs& h, const Dev
     __syncthreads();
 }
 
-// The step's search for feature `f` in one CTA, both children at once: the built child's bins reduced from the
-// slabs, then group 0 scans the built child and group 1 the sibling (parent - built, learner.rs:365-367), each with
-// scan_feature_group, as search_item_group does for one item. `bufs` is 2 kMaxBins int2 of shared memory.
-__device__ void search_feature_cta(const TrainArgs& a, const HistArgs& h, const Step& st, const SearchCtx& s,
-                                   uint32_t f, uint32_t chunks, bool packed, int2* bufs, ScanShared* scan_sh) {
+// The step's search for feature `f` in one CTA, both children at once, in two parts. feature_bins_cta: the built
+// child's bins reduced from the slabs (and, with ranks, summed over every rank's: exchange_bins) into `bufs`
+// (2 kMaxBins int2 of shared memory); *evaluated says whether the feature is searched at all (`evaluate`: the
+// step's features). False when a rank did not answer (error recorded).
+__device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, uint32_t f, uint32_t chunks, bool packed,
+                                 const uint8_t* evaluate, int2* bufs, const GrowExchange& x, uint32_t epoch,
+                                 bool* evaluated) {
+    const DevFeature feat = a.d.features[f];
+    *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
+    if (!*evaluated) return true;
+    if (packed)
+        reduce_feature_bins<true>(h, feat, chunks, bufs + kMaxBins, bufs);
+    else
+        reduce_feature_bins<false>(h, feat, chunks, bufs + kMaxBins, bufs);
+    return x.world == 1 || exchange_bins(x, epoch, a.num_features, f, feat.num_bins, bufs, &a.iter->error);
+}
+
+// feature_scan_cta: with the built child's bins in `bufs`, group 0 scans the built child and group 1 the sibling
+// (parent - built, learner.rs:365-367; group 1 alone reads the parent's slot, which the built child may take over,
+// and writes both children's), each with scan_feature_group, as search_item_group does for one item.
+__device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t f, bool evaluated,
+                                 int2* bufs, ScanShared* scan_sh) {
     const uint32_t F = a.num_features;
     const uint32_t group = threadIdx.x / kScanThreads, t = threadIdx.x % kScanThreads;
     FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
-    const DevFeature feat = a.d.features[f];
-    if (!load_flag(s.evaluate + f) || feat.tile < 0 || feat.num_bins == 0) {
+    if (!evaluated) {
         if (threadIdx.x == 0) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
@@ -621,12 +734,9 @@ __device__ void search_feature_cta(const TrainArgs& a, const HistArgs& h, const 
         }
         return;
     }
+    const DevFeature feat = a.d.features[f];
     int2* built = bufs;
     int2* other = bufs + kMaxBins;
-    if (packed)
-        reduce_feature_bins<true>(h, feat, chunks, other, built);
-    else
-        reduce_feature_bins<false>(h, feat, chunks, other, built);
     const size_t slot_len = 2 * static_cast<size_t>(a.total_bins);
     const size_t off = 2 * static_cast<size_t>(feat.hist_offset);
     const bool mine = t < feat.num_bins;
@@ -638,7 +748,6 @@ __device__ void search_feature_cta(const TrainArgs& a, const HistArgs& h, const 
         const int2 bt = built[t];
         const int2 o = make_int2(p.x - bt.x, p.y - bt.y);
         other[t] = o;
-        // group 1 alone reads the parent's slot, which the built child may take over: it writes both children's
         __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[0]) * slot_len + off) + t, bt);
         __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[1]) * slot_len + off) + t, o);
     }

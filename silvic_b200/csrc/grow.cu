@@ -39,6 +39,7 @@ struct GrowArgs {
     uint32_t slot_bytes;
     uint32_t stage_depth;         // 0: no staging
     uint32_t pad_;
+    GrowExchange x;               // the other ranks (world 1: none)
 };
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
@@ -215,16 +216,36 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // search: one feature per CTA, its built child's bins reduced from the slabs and both children scanned.
         if (!st.root && threadIdx.x == 0) s_left = __ldcg(cursor);
         __syncthreads();
+        const uint32_t epoch = g.x.epoch0 + static_cast<uint32_t>(step + 2);  // this step's, on every rank
+        const bool ranks = g.x.world > 1;
+        const uint8_t* evaluate = st.root ? mask : eval;  // the features this step searches (search_context's)
+        int2* bufs = reinterpret_cast<int2*>(scan);
+        if (ranks && !st.root && cta == 0 && threadIdx.x == 0) publish_left(g.x, epoch, s_left);
+        // With at most one feature per CTA, its bins (and their exchange) come first, so that the left counts'
+        // exchange has arrived by the time the search context needs it.
+        const bool early = f.histogram && F <= ctas;
+        bool evaluated = false;
+        if (early && cta < F && !feature_bins_cta(a, g.h, cta, f.chunks, f.packed, evaluate, bufs, g.x, epoch, &evaluated))
+            return;
+        int64_t left_global = s_left;
+        if (ranks && !st.root && !gather_left(g.x, epoch, &a.iter->error, &left_global)) return;
         if (warp == 0) {
-            const SearchCtx c = search_context(a, st, st.root ? 0 : static_cast<int64_t>(s_left), eval, mask);
+            const SearchCtx c = search_context(a, st, st.root ? 0 : left_global, eval, mask);
             if (lane_id() == 0) s = c;
         }
         __syncthreads();
         clock_mark(g, clock, 1);
-        if (s.searched)
-            for (uint32_t feature = cta; feature < F; feature += ctas)
-                search_feature_cta(a, g.h, st, s, feature, f.chunks, f.packed, reinterpret_cast<int2*>(scan),
-                                   scan_shared);
+        if (s.searched) {
+            if (early) {
+                if (cta < F) feature_scan_cta(a, st, s, cta, evaluated, bufs, scan_shared);
+            } else {
+                for (uint32_t feature = cta; feature < F; feature += ctas) {
+                    if (!feature_bins_cta(a, g.h, feature, f.chunks, f.packed, evaluate, bufs, g.x, epoch, &evaluated))
+                        return;
+                    feature_scan_cta(a, st, s, feature, evaluated, bufs, scan_shared);
+                }
+            }
+        }
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.
@@ -253,8 +274,10 @@ int grow_static_smem() {
 }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,
-                             const GrowSmem& smem, cudaStream_t s, unsigned long long* phase_ns, int trace_steps) {
+                             const GrowSmem& smem, const GrowExchange& x, cudaStream_t s,
+                             unsigned long long* phase_ns, int trace_steps) {
     GrowArgs g{};
+    g.x = x;
     g.t = t;
     g.h = h;
     g.barrier = barrier;

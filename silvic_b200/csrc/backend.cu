@@ -1333,7 +1333,7 @@ struct Training {
 // mapping refused) makes every rank keep the per-step launches with NCCL.
 int setup_exchange(sb2_backend* b) {
     if (!b->comm || b->world <= 1) return SB2_OK;
-    const size_t need = exchange_bytes(b->num_features);
+    const size_t need = exchange_bytes(b->num_features, static_cast<uint32_t>(b->world));
     if (b->xready && b->xbytes == need) return SB2_OK;
     b->close_exchange();
     int ok = b->grow_ok && b->world <= kMaxRanks ? 1 : 0;

@@ -581,22 +581,24 @@ __device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, 
     }
 }
 
-// One warp: waits, lane r for rank r (r < world, r != skip), until every rank's flag at byte `off` of its exchange
-// buffer reaches `epoch`; true when all did.
-__device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int skip, int* error) {
+// One warp: waits, lane s for source rank s (s < world), until the flag at byte `off + 4 s` of this rank's own
+// exchange buffer reaches `epoch`; true when every rank's did.
+__device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int* error) {
     const int lane = static_cast<int>(threadIdx.x & 31);
     bool ok = true;
-    if (lane < x.world && lane != skip)
-        ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[lane] + off), epoch, error);
+    if (lane < x.world) ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[x.rank] + off) + lane, epoch, error);
     return __all_sync(0xffffffffu, ok);
 }
 
-// CTA 0, one thread: this rank's left count of the step into its exchange buffer. The release store orders the
-// value before the flag for every rank that acquires the flag.
+// CTA 0, warp 0: this rank's left count of the step into every rank's buffer (lane q writes rank q's), each
+// followed by its flag; the release store orders the count before the flag.
 __device__ __forceinline__ void publish_left(const GrowExchange& x, uint32_t epoch, uint32_t left) {
-    uint32_t* own = reinterpret_cast<uint32_t*>(x.peers[x.rank]);
-    own[2 + (epoch & 1)] = left;
-    st_release_sys(own, epoch);
+    const int q = static_cast<int>(threadIdx.x & 31);
+    if (q < x.world) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(x.peers[q]);
+        dst[16 + (epoch & 1) * kMaxRanks + x.rank] = left;
+        st_release_sys(dst + x.rank, epoch);
+    }
 }
 
 // Whole CTA: every rank's left count of the step, summed into *total; false when a rank did not answer.
@@ -604,9 +606,10 @@ __device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoc
     __shared__ int64_t s_total;
     __shared__ int s_ok;
     if (threadIdx.x < 32) {
-        const bool ok = wait_ranks(x, 0, epoch, -1, error);
+        const bool ok = wait_ranks(x, 0, epoch, error);
         const int lane = static_cast<int>(threadIdx.x);
-        int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcv(reinterpret_cast<const uint32_t*>(x.peers[lane]) + 2 + (epoch & 1))) : 0;
+        const uint32_t* own = reinterpret_cast<const uint32_t*>(x.peers[x.rank]);
+        int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcg(own + 16 + (epoch & 1) * kMaxRanks + lane)) : 0;
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         if (lane == 0) {
             s_total = v;
@@ -620,31 +623,38 @@ __device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoc
     return ok;
 }
 
-// Whole CTA: feature `f`'s built-child bins of this rank (`built`, shared) published, then replaced by every rank's
-// sum; false when a rank did not answer.
+// Whole CTA: feature `f`'s built-child bins of this rank (`built`, shared) written into every rank's buffer, then
+// replaced by the sum of every rank's copies in this rank's buffer; false when a rank did not answer.
 __device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t epoch, uint32_t F, uint32_t f,
                                               uint32_t nb, int2* built, int* error) {
     __shared__ int s_ok;
-    const size_t at = exchange_bins_offset(F) + ((static_cast<size_t>(epoch & 1) * F + f) * kMaxBins) * sizeof(int2);
-    const size_t flag = 128 + 4ull * f;
-    if (threadIdx.x < nb) reinterpret_cast<int2*>(x.peers[x.rank] + at)[threadIdx.x] = built[threadIdx.x];
-    __syncthreads();  // the CTA's bins are written: the release below orders them before the flag
-    if (threadIdx.x == 0) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[x.rank] + flag), epoch);
+    const size_t base = exchange_bins_offset(F);
+    const size_t per_src = static_cast<size_t>(F) * kMaxBins;
+    const size_t parity = static_cast<size_t>(epoch & 1) * x.world * per_src;
+    // slot of source rank s: base + (parity + s * per_src + f * kMaxBins) int2
+    if (threadIdx.x < nb) {
+        const int2 v = built[threadIdx.x];
+        const size_t at = parity + static_cast<size_t>(x.rank) * per_src + static_cast<size_t>(f) * kMaxBins + threadIdx.x;
+        for (int q = 0; q < x.world; ++q) reinterpret_cast<int2*>(x.peers[q] + base)[at] = v;
+    }
+    __syncthreads();  // the CTA's stores are issued: each release below orders them before its flag
+    const size_t flags = exchange_flags_offset() + 4ull * kMaxRanks * f;  // this feature's flags, one per source
     if (threadIdx.x < 32) {
-        const bool ok = wait_ranks(x, flag, epoch, x.rank, error);
+        const int q = static_cast<int>(threadIdx.x);
+        if (q < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[q] + flags) + x.rank, epoch);
+        const bool ok = wait_ranks(x, flags, epoch, error);
         if (threadIdx.x == 0) s_ok = ok;
     }
     __syncthreads();
     const bool ok = s_ok != 0;
     if (ok && threadIdx.x < nb) {
+        const int2* own = reinterpret_cast<const int2*>(x.peers[x.rank] + base) + parity + static_cast<size_t>(f) * kMaxBins + threadIdx.x;
         int2 v[kMaxRanks];
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r)
-            v[r] = r < x.world && r != x.rank ? __ldcv(reinterpret_cast<const int2*>(x.peers[r] + at) + threadIdx.x)
-                                              : make_int2(0, 0);
-        int2 sum = built[threadIdx.x];
+        for (int s = 0; s < kMaxRanks; ++s) v[s] = s < x.world ? __ldcg(own + s * per_src) : make_int2(0, 0);
+        int2 sum = make_int2(0, 0);
 #pragma unroll
-        for (int r = 0; r < kMaxRanks; ++r) sum = make_int2(sum.x + v[r].x, sum.y + v[r].y);
+        for (int s = 0; s < kMaxRanks; ++s) sum = make_int2(sum.x + v[s].x, sum.y + v[s].y);
         built[threadIdx.x] = sum;
     }
     __syncthreads();

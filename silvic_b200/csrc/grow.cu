@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         const bool ranks = g.x.world > 1;
         const uint8_t* evaluate = st.root ? mask : eval;  // the features this step searches (search_context's)
         int2* bufs = reinterpret_cast<int2*>(scan);
-        if (ranks && !st.root && cta == 0 && threadIdx.x == 0) publish_left(g.x, epoch, s_left);
+        if (ranks && !st.root && cta == 0 && threadIdx.x < 32) publish_left(g.x, epoch, s_left);
         // With at most one feature per CTA, its bins (and their exchange) come first, so that the left counts'
         // exchange has arrived by the time the search context needs it.
         const bool early = f.histogram && F <= ctas;

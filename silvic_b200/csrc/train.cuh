@@ -170,9 +170,10 @@ struct GrowSmem {
 int grow_static_smem();
 
 // Ranks of one training run, one GPU each, every rank running the tree kernel at once: per split step each rank
-// publishes its left count and, per searched feature, its built child's bins in its own exchange buffer, raises a
-// flag with the step's epoch, and sums every rank's copies, read over NVLink through CUDA IPC mappings. Every rank
-// then runs the same search and finish on the same sums and grows the same tree.
+// writes its left count and, per searched feature, its built child's bins into every rank's exchange buffer (NVLink
+// stores through CUDA IPC mappings), then raises its flag there with the step's epoch; each rank waits on the flags
+// in its own buffer and sums the copies from its own memory. Every rank then runs the same search and finish on the
+// same sums and grows the same tree.
 constexpr int kMaxRanks = 8;
 struct GrowExchange {
     uint8_t* peers[kMaxRanks];  // every rank's exchange buffer (this rank's own at [rank]); unused with one rank
@@ -180,10 +181,15 @@ struct GrowExchange {
     uint32_t epoch0;            // the launch's epochs are epoch0 + 1 (the root) .. (they rise across launches)
     uint32_t pad_;
 };
-// An exchange buffer: [0] the left count's flag, [2 + parity] the left count (u32 words); from byte 128 a flag per
-// feature (u32); then the built child's bins, int2 [2 parities][F][kMaxBins].
-__host__ __device__ inline size_t exchange_bins_offset(uint32_t F) { return 128 + (4ull * F + 127) / 128 * 128; }
-__host__ __device__ inline size_t exchange_bytes(uint32_t F) { return exchange_bins_offset(F) + 2ull * F * kMaxBins * 8; }
+// An exchange buffer, per source rank s: u32 left-count flags [s] at byte 0, left counts [parity][s] at byte 64,
+// feature flags [s][F] from byte 128; then the built child's bins, int2 [parity][s][F][kMaxBins].
+__host__ __device__ inline size_t exchange_flags_offset() { return 128; }
+__host__ __device__ inline size_t exchange_bins_offset(uint32_t F) {
+    return 128 + (4ull * kMaxRanks * F + 127) / 128 * 128;
+}
+__host__ __device__ inline size_t exchange_bytes(uint32_t F, uint32_t world) {
+    return exchange_bins_offset(F) + 2ull * world * F * kMaxBins * 8;
+}
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,
                              const GrowSmem& smem, const GrowExchange& x, cudaStream_t s,

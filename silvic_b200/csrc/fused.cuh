@@ -668,8 +668,8 @@ __device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t ep
 // consecutive bins of a chunk: 128 or 256 bytes), with kLoads chunks in flight; the odd chunks' sums meet the even
 // ones' through `part` (shared). Whole CTA (kHistThreads threads).
 template <bool kPacked>
-__device__ __forceinline__ void reduce_feature_bins(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
-                                                    int2* part, int2* out) {
+__device__ __forceinline__ void reduce_feature_bins_halves(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
+                                                           int2* part, int2* out) {
     constexpr int kLoads = 16;
     const uint32_t b = threadIdx.x & 255, half = threadIdx.x >> 8;
     int sg = 0, sh = 0;
@@ -706,20 +706,85 @@ __device__ __forceinline__ void reduce_feature_bins(const HistArgs& h, const Dev
     __syncthreads();
 }
 
+// The same sum with 16-byte loads: thread (g, q) of the CTA takes bins 4q .. 4q+3 over the chunks g, g + 8, ...
+// (64 threads cover a feature's 256 bins of one chunk; 8 such groups split the chunks, all of a group's loads in
+// flight together), and the 8 groups' sums meet in `scratch` (shared, 8 x 64 x 32 bytes).
+template <bool kPacked>
+__device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
+                                                          int4* scratch, int2* out) {
+    constexpr uint32_t kGroups = kHistThreads / 64, kLoads = 8;
+    const uint32_t q = threadIdx.x & 63, g = threadIdx.x >> 6;
+    int4 sg = make_int4(0, 0, 0, 0), sh = sg;  // bins 4q .. 4q+3: g and h sums
+    if (4 * q < feat.num_bins) {
+        const int* base = h.slabs + (kPacked ? feat.slab_off + 4 * q : 2 * (feat.slab_off + 4 * q));
+        for (uint32_t c0 = g; c0 < chunks; c0 += kGroups * kLoads) {
+            int4 v[kLoads], w[kLoads];
+#pragma unroll
+            for (uint32_t k = 0; k < kLoads; ++k) {
+                const uint32_t c = c0 + kGroups * k;
+                const int4* at = reinterpret_cast<const int4*>(base + static_cast<size_t>(c) * h.slab_ints);
+                v[k] = c < chunks ? __ldcg(at) : make_int4(0, 0, 0, 0);
+                if (!kPacked) w[k] = c < chunks ? __ldcg(at + 1) : make_int4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < kLoads; ++k) {
+                if (kPacked) {
+                    // unpack (quantize.rs:140-143)
+                    const uint32_t x[4] = {static_cast<uint32_t>(v[k].x), static_cast<uint32_t>(v[k].y),
+                                           static_cast<uint32_t>(v[k].z), static_cast<uint32_t>(v[k].w)};
+                    int gx[4], hx[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        gx[j] = static_cast<int16_t>(x[j] & 0xFFFFu);
+                        hx[j] = static_cast<int>((x[j] - static_cast<uint32_t>(gx[j])) >> 16);
+                    }
+                    sg = make_int4(sg.x + gx[0], sg.y + gx[1], sg.z + gx[2], sg.w + gx[3]);
+                    sh = make_int4(sh.x + hx[0], sh.y + hx[1], sh.z + hx[2], sh.w + hx[3]);
+                } else {  // [g, h] pairs: v = bins 4q, 4q+1; w = 4q+2, 4q+3
+                    sg = make_int4(sg.x + v[k].x, sg.y + v[k].z, sg.z + w[k].x, sg.w + w[k].z);
+                    sh = make_int4(sh.x + v[k].y, sh.y + v[k].w, sh.z + w[k].y, sh.w + w[k].w);
+                }
+            }
+        }
+    }
+    scratch[2 * (g * 64 + q)] = sg;
+    scratch[2 * (g * 64 + q) + 1] = sh;
+    __syncthreads();
+    const uint32_t b = threadIdx.x;
+    if (b < feat.num_bins) {
+        const int* sc = reinterpret_cast<const int*>(scratch);
+        int tg = 0, th = 0;
+#pragma unroll
+        for (uint32_t k = 0; k < kGroups; ++k) {
+            tg += sc[8 * (k * 64 + b / 4) + (b & 3)];
+            th += sc[8 * (k * 64 + b / 4) + 4 + (b & 3)];
+        }
+        out[b] = make_int2(tg, th);
+    }
+    __syncthreads();
+}
+
 // The step's search for feature `f` in one CTA, both children at once, in two parts. feature_bins_cta: the built
 // child's bins reduced from the slabs (and, with ranks, summed over every rank's: exchange_bins) into `bufs`
-// (2 kMaxBins int2 of shared memory); *evaluated says whether the feature is searched at all (`evaluate`: the
-// step's features). False when a rank did not answer (error recorded).
+// (2 kMaxBins int2 of shared memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction);
+// *evaluated says whether the feature is searched at all (`evaluate`: the step's features). False when a rank did
+// not answer (error recorded).
 __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, uint32_t f, uint32_t chunks, bool packed,
-                                 const uint8_t* evaluate, int2* bufs, const GrowExchange& x, uint32_t epoch,
-                                 bool* evaluated) {
+                                 const uint8_t* evaluate, int2* bufs, int4* scratch, const GrowExchange& x,
+                                 uint32_t epoch, bool* evaluated) {
     const DevFeature feat = a.d.features[f];
     *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
     if (!*evaluated) return true;
-    if (packed)
-        reduce_feature_bins<true>(h, feat, chunks, bufs + kMaxBins, bufs);
-    else
-        reduce_feature_bins<false>(h, feat, chunks, bufs + kMaxBins, bufs);
+    if (scratch != nullptr) {
+        if (packed)
+            reduce_feature_bins_quads<true>(h, feat, chunks, scratch, bufs);
+        else
+            reduce_feature_bins_quads<false>(h, feat, chunks, scratch, bufs);
+    } else if (packed) {
+        reduce_feature_bins_halves<true>(h, feat, chunks, bufs + kMaxBins, bufs);
+    } else {
+        reduce_feature_bins_halves<false>(h, feat, chunks, bufs + kMaxBins, bufs);
+    }
     return x.world == 1 || exchange_bins(x, epoch, a.num_features, f, feat.num_bins, bufs, &a.iter->error);
 }
 

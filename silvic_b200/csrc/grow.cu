@@ -220,12 +220,17 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         const bool ranks = g.x.world > 1;
         const uint8_t* evaluate = st.root ? mask : eval;  // the features this step searches (search_context's)
         int2* bufs = reinterpret_cast<int2*>(scan);
+        // the reduction's scratch: the histogram's staging slots, free in this phase
+        int4* scratch = g.stage_depth * (kGrowThreads / 32) * g.slot_bytes >= 16384
+                            ? reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(smem) + g.stage_offset)
+                            : nullptr;
         if (ranks && !st.root && cta == 0 && threadIdx.x < 32) publish_left(g.x, epoch, s_left);
         // With at most one feature per CTA, its bins (and their exchange) come first, so that the left counts'
         // exchange has arrived by the time the search context needs it.
         const bool early = f.histogram && F <= ctas;
         bool evaluated = false;
-        if (early && cta < F && !feature_bins_cta(a, g.h, cta, f.chunks, f.packed, evaluate, bufs, g.x, epoch, &evaluated))
+        if (early && cta < F &&
+            !feature_bins_cta(a, g.h, cta, f.chunks, f.packed, evaluate, bufs, scratch, g.x, epoch, &evaluated))
             return;
         int64_t left_global = s_left;
         if (ranks && !st.root && !gather_left(g.x, epoch, &a.iter->error, &left_global)) return;
@@ -240,7 +245,8 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
                 if (cta < F) feature_scan_cta(a, st, s, cta, evaluated, bufs, scan_shared);
             } else {
                 for (uint32_t feature = cta; feature < F; feature += ctas) {
-                    if (!feature_bins_cta(a, g.h, feature, f.chunks, f.packed, evaluate, bufs, g.x, epoch, &evaluated))
+                    if (!feature_bins_cta(a, g.h, feature, f.chunks, f.packed, evaluate, bufs, scratch, g.x, epoch,
+                                          &evaluated))
                         return;
                     feature_scan_cta(a, st, s, feature, evaluated, bufs, scan_shared);
                 }

@@ -50,7 +50,7 @@ PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_qu
 METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
 # DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
 # case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md.
-TREE_TRAFFIC_PER_ROW = 1266
+TREE_TRAFFIC_PER_ROW = 1261
 
 
 # ---- synthetic data (torch on the GPU as plumbing) ------------------------------------------------------------

@@ -349,6 +349,14 @@ class Model:
         kt = lib.sb2_model_tree_seconds(handle, tsecs, 100000)
         return Model(trees, init_score, list(secs[: min(k, 100000)]), list(tsecs[: min(kt, 100000)]))
 
+    def to_lightgbm_string(self, dataset, params: _abi.Params) -> str:
+        """The model file silvic writes for this training run (`Model::to_lightgbm_string`,
+        crates/silvic-core/src/model/text.rs:48-70): feature names and infos from `dataset`, parameters from
+        `params` (silvic_b200.model_text)."""
+        from . import model_text
+
+        return model_text.from_trained(self, dataset, params).to_string()
+
     def predict_raw_row(self, row: np.ndarray) -> float:
         """Model::predict_raw_row (crates/silvic-core/src/model/predict.rs:19-23): f64 sum of leaf values."""
         score = 0.0

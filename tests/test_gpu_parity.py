@@ -239,3 +239,8 @@ def test_training_matches_oracle(device, name, bins, rows, params):
     assert len(model.trees) == len(ref.trees)
     for k, (t, r) in enumerate(zip(model.trees, ref.trees)):
         assert orc.trees_equal(t, r) == [], f"tree {k}"
+    # the emitted model file is the oracle model's, byte for byte (silvic_b200.model_text, pinned on LightGBM's
+    # files in test_model_text.py)
+    from silvic_b200.backend import Model
+
+    assert model.to_lightgbm_string(data, p) == Model(ref.trees, ref.init_score, []).to_lightgbm_string(data, p)

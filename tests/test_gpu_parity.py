@@ -223,6 +223,8 @@ TRAIN_CASES = [
                                         min_data_in_leaf=50, num_iterations=6, feature_fraction=0.6,
                                         num_grad_quant_bins=16)),
     ("l2_nan", [40] * 8, 10_000, dict(objective=_abi.REGRESSION, num_leaves=20, num_iterations=4)),
+    # more features than CTAs (several per CTA in the search) and several histogram units
+    ("wide", [255] * 60 + [15] * 140, 6_000, dict(objective=_abi.REGRESSION, num_leaves=31, num_iterations=3)),
 ]
 
 

@@ -41,12 +41,28 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 SEED = 20261107
+CONFIG = "c2"
 ROWS = 10_000_000
 GAUSSIAN, UNIFORM = 70, 30
 FEATURES = GAUSSIAN + UNIFORM
 MAX_BIN = 255
 SAMPLE_ROWS = 200_000
 PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
+
+
+def set_config(name: str):
+    """c2 (the default) or c4 (configs[3], the multi-GPU scaling config: 100,000,000 rows
+    x 256 N(0,1) features, target = a random 32-feature linear function + N(0,1) noise, L2 regression, 255 bins,
+    255 leaves)."""
+    global CONFIG, ROWS, GAUSSIAN, UNIFORM, FEATURES, PARAMS
+    CONFIG = name
+    if name == "c4":
+        ROWS, GAUSSIAN, UNIFORM = 100_000_000, 256, 0
+        PARAMS = dict(objective="regression", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
+    else:
+        ROWS, GAUSSIAN, UNIFORM = 10_000_000, 70, 30
+        PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
+    FEATURES = GAUSSIAN + UNIFORM
 METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
 # DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
 # case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md.
@@ -92,10 +108,20 @@ def features_of(rows, device):
 
 
 def labels_of(rows, x):
-    """Bernoulli(sigmoid(sparse linear in 12 features + 3 pairwise interactions))."""
+    """c2: Bernoulli(sigmoid(sparse linear in 12 features + 3 pairwise interactions)); c4: a linear function of 32
+    random features + N(0,1) noise."""
     import torch
 
     g = np.random.default_rng(SEED)
+    if CONFIG == "c4":
+        picked = g.choice(FEATURES, size=32, replace=False)
+        weights = g.normal(0.0, 1.0, size=32)
+        y = torch.zeros(rows.numel(), dtype=torch.float64, device=x.device)
+        for f, w in zip(picked, weights):
+            y += float(w) * x[:, int(f)].double()
+        u1, u2 = 1.0 - _unit(6000, rows), _unit(6001, rows)
+        y += torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2.0 * torch.pi * u2)
+        return y.to(torch.float32)
     picked = g.choice(FEATURES, size=12, replace=False)
     weights = g.normal(0.0, 1.0, size=12)
     pairs = g.choice(FEATURES, size=(3, 2), replace=False)
@@ -278,7 +304,8 @@ def oracle_rate(data, iterations: int, params) -> tuple[float, list[float], int]
 def oracle_params():
     from silvic_b200 import _abi
 
-    return dict(objective=_abi.BINARY, num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
+    objective = _abi.REGRESSION if PARAMS["objective"] == "regression" else _abi.BINARY
+    return dict(objective=objective, num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
 
 
 def set_rows(rows: int):
@@ -287,6 +314,9 @@ def set_rows(rows: int):
 
 
 def workload() -> str:
+    if CONFIG == "c4":
+        size = "100M" if ROWS == 100_000_000 else f"{ROWS:,} rows (reduced)"
+        return f"configs[3]: L2 regression {size} x 256, 255 bins, 255 leaves"
     size = "10M" if ROWS == 10_000_000 else f"{ROWS:,} rows (reduced)"
     return f"configs[1]: binary {size} x 100, 255 bins, 255 leaves"
 
@@ -426,7 +456,7 @@ def run_b200(args, rank: int, world: int):
         "data": "synthetic",
         "config": {"workload": workload(), "rows": ROWS,
                    "features": FEATURES, "num_leaves": 255, "parallelism": f"rows sharded over {world} GPU(s)",
-                   "l2": "inputs (1 GB binned) larger than L2; no flush"},
+                   "l2": f"inputs ({n_local * S / 1e9:.1f} GB binned per GPU) larger than L2; no flush"},
         "trees": trees,
         "hist_rows_feats_per_s": n_local * FEATURES / hist_s * world,
         "roofline": roofline,
@@ -441,7 +471,7 @@ def run_b200(args, rank: int, world: int):
     if world == 1 and not args.no_cpu_baseline:
         rate, secs, cores = oracle_rate(data, 2, oracle_params())
         line["cpu_baseline"] = {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port",
-                                "sample": f"2 boosting iterations of the same {ROWS:,} x 100 dataset, "
+                                "sample": f"2 boosting iterations of the same {ROWS:,} x {FEATURES} dataset, "
                                           f"{sum(secs):.1f} s on {cores} threads"}
     print(json.dumps(line), flush=True)
 
@@ -453,10 +483,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--rows", type=int, default=ROWS,
-                    help="rows of the synthetic set (a smaller case for profiling; the benchmark is 10,000,000)")
+    ap.add_argument("--config", default="c2", choices=["c2", "c4"],
+                    help="c2 (default): BASELINE configs[1]; c4: configs[3], the 100M-row scaling config")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows of the synthetic set (a smaller case for profiling; default: the config's)")
     args = ap.parse_args()
-    set_rows(args.rows)
+    set_config(args.config)
+    if args.rows:
+        set_rows(args.rows)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1:

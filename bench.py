@@ -65,8 +65,9 @@ def set_config(name: str):
     FEATURES = GAUSSIAN + UNIFORM
 METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
 # DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
-# case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md.
-TREE_TRAFFIC_PER_ROW = 1261
+# case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md. Per config;
+# none captured for c4.
+TREE_TRAFFIC_PER_ROW = {"c2": 1261, "c4": None}
 
 
 # ---- synthetic data (torch on the GPU as plumbing) ------------------------------------------------------------
@@ -432,7 +433,7 @@ def run_b200(args, rank: int, world: int):
         per_launch = sum(tree_bytes) / len(tree_bytes)
         roofline = {"bound": "hbm", "achieved": per_launch / launch_s / 1e9, "peak": peak, "unit": "GB/s",
                     "peak_kind": peak_kind,
-                    "traffic": None if TREE_TRAFFIC_PER_ROW is None else TREE_TRAFFIC_PER_ROW * n_local,
+                    "traffic": None if TREE_TRAFFIC_PER_ROW[CONFIG] is None else TREE_TRAFFIC_PER_ROW[CONFIG] * n_local,
                     "kernel": "grow_tree_kernel (one cooperative launch grows one tree)",
                     "launch_ms": launch_s * 1000.0, "algorithmic_bytes": per_launch,
                     "share_of_step": sum(tree_s) / timed, "root_histogram": hist_roofline}

@@ -575,7 +575,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the partition's
     // scan and the search's bins.
     // Layout (GrowSmem): the histogram's arrays, the partition's scan words, the histogram's staging slots (all three
-    // used in the same phase), then the per-feature flags (5 F bytes); the search's bins (kMaxBins [g, h] pairs per
+    // used in the same phase), then the per-feature flags ((5 kSplits + 1) F bytes); the search's bins (kMaxBins [g, h] pairs per
     // group of warps, 4 KB in all) reuse the scan words. Staging gets what is left of the CTA's shared memory, up to
     // kMaxStageDepth slots per warp.
     {
@@ -589,7 +589,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
             slot = std::max(slot, rows);
         }
         m.slot_bytes = (slot + 128 + 127) / 128 * 128;  // the rows, then 32 packed gradients
-        const size_t flags = (5ull * F + 15) / 16 * 16;
+        const size_t flags = ((5ull * kSplits + 1) * F + 15) / 16 * 16;
         const int stat = grow_static_smem();
         if (stat < 0) return b->fail(SB2_EDEVICE, "cudaFuncGetAttributes(grow_tree)");
         const size_t limit = static_cast<size_t>(b->smem_optin) - static_cast<size_t>(stat);
@@ -688,7 +688,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         SB2_CUDA(b, b->rows[k].alloc(sizeof(uint32_t) * n));
         SB2_CUDA(b, b->ordered[k].alloc(sizeof(int32_t) * n));
     }
-    SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * (n / 32 + 2)));
+    SB2_CUDA(b, b->flags.alloc(sizeof(uint32_t) * kSplits * (n / 32 + 2)));  // the tree kernel's splits
     SB2_CUDA(b, b->tile_left.alloc(sizeof(uint32_t) * kMaxPartitionCtas));
     SB2_CUDA(b, b->staging.alloc(sizeof(int) * (2ull * b->total_bins + 2)));
     // A slab holds one unit's histogram (the standalone kernels, one unit per CTA) or every unit's (the persistent
@@ -739,9 +739,9 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     SB2_CUDA(b, cudaMemsetAsync(b->api_spec.ptr, 0, sizeof(sb2_quant_spec), b->stream));
     b->api_spec_host = sb2_quant_spec{};
     b->packed_spec = b->api_spec.as<sb2_quant_spec>();  // the packed gradients start as zeros
-    SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * std::max<size_t>(F, 1)));
-    SB2_CUDA(b, b->cand_flags.alloc(2 * std::max<size_t>(F, 1)));
-    SB2_CUDA(b, b->cand_gain.alloc(sizeof(double) * 2 * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->candidates.alloc(sizeof(FeatureCandidate) * 2 * kSplits * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->cand_flags.alloc(2 * kSplits * std::max<size_t>(F, 1)));
+    SB2_CUDA(b, b->cand_gain.alloc(sizeof(double) * 2 * kSplits * std::max<size_t>(F, 1)));
     SB2_CUDA(b, b->maxima.alloc(2 * sizeof(unsigned long long)));
     SB2_CUDA(b, b->grid_barrier.alloc(2 * sizeof(unsigned int)));
     SB2_CUDA(b, cudaMemsetAsync(b->grid_barrier.ptr, 0, 2 * sizeof(unsigned int), b->stream));
@@ -1405,11 +1405,12 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     TrainBuffers& tb = tr.tb;
     SB2_CUDA(b, tb.leaves.alloc(sizeof(DevLeaf) * L));
     SB2_CUDA(b, tb.leaf_gain.alloc(sizeof(double) * L));
-    SB2_CUDA(b, tb.cursors.alloc(sizeof(unsigned int) * 2 * L));
+    SB2_CUDA(b, tb.cursors.alloc(sizeof(unsigned int) * 2 * kSplits * (static_cast<size_t>(L) + 1)));
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.masks.alloc(static_cast<size_t>(std::max(iters, 1)) * std::max<uint32_t>(F, 1)));
-    SB2_CUDA(b, tb.slots.alloc(sizeof(int) * static_cast<size_t>(L) * 2 * b->total_bins));
+    // one slot per leaf, then the tree kernel's spare slots
+    SB2_CUDA(b, tb.slots.alloc(sizeof(int) * (static_cast<size_t>(L) + kSplits - 1) * 2 * b->total_bins));
     SB2_CUDA(b, tb.leaf_sums.alloc(sizeof(int64_t) * 2 * L));
     SB2_CUDA(b, tb.leaf_values.alloc(sizeof(float) * L));
     SB2_CUDA(b, tb.records.alloc(sizeof(TreeRecordHeader) * std::max(iters, 1)));
@@ -1714,8 +1715,8 @@ int sb2_profile_steps(sb2_backend* b, const sb2_params* p, double init_score, do
     std::unique_ptr<sb2_model> model;
     SB2_TRY(profile_run(b, p, init_score, last, trace, model));
     if (trace.empty()) return b->fail(SB2_EUNSUPPORTED, "step traces come from the single-GPU tree kernel only");
-    const size_t leaves = model->trees.empty() ? 0 : static_cast<size_t>(model->trees.back().num_leaves);
-    const size_t steps = std::min<size_t>(leaves, trace.size() / kStepTrace);
+    size_t steps = 0;  // the grid steps that ran: each ran at least one split
+    while (steps < trace.size() / kStepTrace && trace[steps * kStepTrace + kGrowPhases + 1] > 0) ++steps;
     *num_steps = std::min(steps, max_steps);
     for (size_t s = 0; s < *num_steps; ++s)
         for (int k = 0; k < kStepTrace; ++k) {

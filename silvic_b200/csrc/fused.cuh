@@ -392,13 +392,16 @@ struct FusedStep {
     uint32_t depth;       // staging slots per warp (0: no staging)
 };
 
-// CTA `cta`'s part of a step (kHistThreads threads; the unit histograms' shared arrays zero on entry and on return): for a split, the partition of its range of the parent into
-// the other buffer; then, for every unit, its built-child rows into the unit's slab region. `scan` is 2 kHistThreads
-// + 64 words of shared memory apart from the histogram's; `cursor` the step's two placement counters (8-byte aligned,
-// zero before the step); `units` the prepared unit descriptions (`cached` of them; later units are prepared into `spare`).
+// Part `cta` (of fs.chunks) of a split (kHistThreads threads; the unit histograms' shared arrays zero on entry and
+// on return): for a split, the partition of its range of the parent into the other buffer (`flags`: the split's
+// flag words, one per 32 positions); then, for every unit, its built-child rows into the unit's region of slab
+// `slab_index`. `scan` is 2 kHistThreads + 64 words of shared memory apart from the histogram's; `cursor` the
+// split's two placement counters (8-byte aligned, zero before the step); `units` the prepared unit descriptions
+// (`cached` of them; later units are prepared into `spare`).
 inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, const Step& st, const FusedStep& fs,
-                                      uint32_t cta, int* sh, uint32_t* scan, unsigned int* cursor,
-                                      const uint8_t* active, HistCta* units, uint32_t cached, HistCta* spare) {
+                                      uint32_t cta, uint32_t slab_index, uint32_t* flags, int* sh, uint32_t* scan,
+                                      unsigned int* cursor, const uint8_t* active, HistCta* units, uint32_t cached,
+                                      HistCta* spare) {
     if (cta >= fs.chunks) return;
     uint32_t lo, hi;
     fused_range(fs.count, fs.chunks, cta, lo, hi);
@@ -437,7 +440,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
                 if (lane == static_cast<uint32_t>(j)) flag_word = word;
                 mine += __popc(word);
             }
-            if (lane < static_cast<uint32_t>(kBatch) && w0 + lane < w_hi) a.flags[w0 + lane] = flag_word;
+            if (lane < static_cast<uint32_t>(kBatch) && w0 + lane < w_hi) flags[w0 + lane] = flag_word;
         }
         if (lane == 0) sums[warp] = mine;
         __syncthreads();
@@ -460,7 +463,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
         uint32_t carry = 0;  // lefts of the CTA's earlier rounds
         for (uint32_t r0 = w_lo; r0 < w_hi; r0 += kFusedScanWords) {
             const uint32_t nw = min(w_hi - r0, kFusedScanWords);
-            const uint32_t word = threadIdx.x < nw ? __ldcg(a.flags + r0 + threadIdx.x) : 0u;
+            const uint32_t word = threadIdx.x < nw ? __ldcg(flags + r0 + threadIdx.x) : 0u;
             words[threadIdx.x] = word;
             const uint32_t cnt = __popc(word);
             uint32_t incl = cnt;
@@ -528,7 +531,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     }
     const uint64_t pol = evict_first_policy();
     __shared__ LaneTile s_lt[kMaxUnitTiles];
-    int* slab = h.slabs + static_cast<size_t>(cta) * h.slab_ints;
+    int* slab = h.slabs + static_cast<size_t>(slab_index) * h.slab_ints;
     uint32_t region = 0;  // ints before this unit's slab region
     // Rows per flush: all of them when the slabs hold packed sums (the range fits a packed round), else rounds of
     // at most round_rows rows.
@@ -590,55 +593,60 @@ __device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, ui
     return __all_sync(0xffffffffu, ok);
 }
 
-// CTA 0, warp 0: this rank's left count of the step into every rank's buffer (lane q writes rank q's), each
-// followed by its flag; the release store orders the count before the flag.
-__device__ __forceinline__ void publish_left(const GrowExchange& x, uint32_t epoch, uint32_t left) {
+// Left count of split j from source rank s, in the exchange buffer's words (the step's parity).
+__device__ __forceinline__ size_t exchange_left_word(uint32_t epoch, int j, int s) {
+    return kXLeftValues / 4 + ((epoch & 1) * kSplits + static_cast<size_t>(j)) * kMaxRanks + s;
+}
+
+// CTA 0, warp 0: this rank's left counts of the step's `n` splits into every rank's buffer (lane q writes rank
+// q's), each rank's followed by this rank's flag; the release store orders the counts before the flag.
+__device__ __forceinline__ void publish_left(const GrowExchange& x, uint32_t epoch, const uint32_t* left, int n) {
     const int q = static_cast<int>(threadIdx.x & 31);
     if (q < x.world) {
         uint32_t* dst = reinterpret_cast<uint32_t*>(x.peers[q]);
-        dst[16 + (epoch & 1) * kMaxRanks + x.rank] = left;
-        st_release_sys(dst + x.rank, epoch);
+        for (int j = 0; j < n; ++j) dst[exchange_left_word(epoch, j, x.rank)] = left[j];
+        st_release_sys(dst + kXLeftFlags / 4 + x.rank, epoch);
     }
 }
 
-// Whole CTA: every rank's left count of the step, summed into *total; false when a rank did not answer.
-__device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoch, int* error, int64_t* total) {
-    __shared__ int64_t s_total;
+// Whole CTA: every rank's left counts of the step's `n` splits, summed into total[j] (shared); false when a rank
+// did not answer.
+__device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoch, int n, int* error, int64_t* total) {
     __shared__ int s_ok;
     if (threadIdx.x < 32) {
-        const bool ok = wait_ranks(x, 0, epoch, error);
+        const bool ok = wait_ranks(x, kXLeftFlags, epoch, error);
         const int lane = static_cast<int>(threadIdx.x);
         const uint32_t* own = reinterpret_cast<const uint32_t*>(x.peers[x.rank]);
-        int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcg(own + 16 + (epoch & 1) * kMaxRanks + lane)) : 0;
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) {
-            s_total = v;
-            s_ok = ok;
+        for (int j = 0; j < n; ++j) {
+            int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcg(own + exchange_left_word(epoch, j, lane))) : 0;
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) total[j] = v;
         }
+        if (lane == 0) s_ok = ok;
     }
     __syncthreads();
-    *total = s_total;
     const bool ok = s_ok != 0;
     __syncthreads();
     return ok;
 }
 
-// Whole CTA: feature `f`'s built-child bins of this rank (`built`, shared) written into every rank's buffer, then
-// replaced by the sum of every rank's copies in this rank's buffer; false when a rank did not answer.
-__device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t epoch, uint32_t F, uint32_t f,
+// Whole CTA: split j's feature `f`'s built-child bins of this rank (`built`, shared) written into every rank's
+// buffer, then replaced by the sum of every rank's copies in this rank's buffer; false when a rank did not answer.
+__device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t epoch, uint32_t F, uint32_t j, uint32_t f,
                                               uint32_t nb, int2* built, int* error) {
     __shared__ int s_ok;
     const size_t base = exchange_bins_offset(F);
-    const size_t per_src = static_cast<size_t>(F) * kMaxBins;
+    const size_t per_src = static_cast<size_t>(kSplits) * F * kMaxBins;
     const size_t parity = static_cast<size_t>(epoch & 1) * x.world * per_src;
-    // slot of source rank s: base + (parity + s * per_src + f * kMaxBins) int2
+    const size_t item = static_cast<size_t>(j) * F + f;
+    // slot of source rank s: base + (parity + s * per_src + item * kMaxBins) int2
     if (threadIdx.x < nb) {
         const int2 v = built[threadIdx.x];
-        const size_t at = parity + static_cast<size_t>(x.rank) * per_src + static_cast<size_t>(f) * kMaxBins + threadIdx.x;
+        const size_t at = parity + static_cast<size_t>(x.rank) * per_src + item * kMaxBins + threadIdx.x;
         for (int q = 0; q < x.world; ++q) reinterpret_cast<int2*>(x.peers[q] + base)[at] = v;
     }
     __syncthreads();  // the CTA's stores are issued: each release below orders them before its flag
-    const size_t flags = exchange_flags_offset() + 4ull * kMaxRanks * f;  // this feature's flags, one per source
+    const size_t flags = kXFeatureFlags + 4ull * kMaxRanks * item;  // this item's flags, one per source
     if (threadIdx.x < 32) {
         const int q = static_cast<int>(threadIdx.x);
         if (q < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[q] + flags) + x.rank, epoch);
@@ -648,7 +656,7 @@ __device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t ep
     __syncthreads();
     const bool ok = s_ok != 0;
     if (ok && threadIdx.x < nb) {
-        const int2* own = reinterpret_cast<const int2*>(x.peers[x.rank] + base) + parity + static_cast<size_t>(f) * kMaxBins + threadIdx.x;
+        const int2* own = reinterpret_cast<const int2*>(x.peers[x.rank] + base) + parity + item * kMaxBins + threadIdx.x;
         int2 v[kMaxRanks];
 #pragma unroll
         for (int s = 0; s < kMaxRanks; ++s) v[s] = s < x.world ? __ldcg(own + s * per_src) : make_int2(0, 0);
@@ -663,18 +671,18 @@ __device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t ep
 
 // ---- the built child's histogram and the search, one feature per CTA ---------------------------------------
 
-// Feature `f`'s bins of the built child summed over the step's `chunks` slabs into `out` (shared, [g, h] per bin):
+// Feature `f`'s bins of the built child summed over `chunks` slabs from slab `first` into `out` (shared, [g, h] per bin):
 // thread t of the CTA takes bin t mod 256 over the chunks c = t / 256, t / 256 + 2, ... (a warp reads 32
 // consecutive bins of a chunk: 128 or 256 bytes), with kLoads chunks in flight; the odd chunks' sums meet the even
 // ones' through `part` (shared). Whole CTA (kHistThreads threads).
 template <bool kPacked>
-__device__ __forceinline__ void reduce_feature_bins_halves(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
-                                                           int2* part, int2* out) {
+__device__ __forceinline__ void reduce_feature_bins_halves(const HistArgs& h, const DevFeature& feat, uint32_t first,
+                                                           uint32_t chunks, int2* part, int2* out) {
     constexpr int kLoads = 16;
     const uint32_t b = threadIdx.x & 255, half = threadIdx.x >> 8;
     int sg = 0, sh = 0;
     if (b < feat.num_bins) {
-        const int* base = h.slabs + (kPacked ? feat.slab_off + b : 2 * (feat.slab_off + b));
+        const int* base = h.slabs + static_cast<size_t>(first) * h.slab_ints + (kPacked ? feat.slab_off + b : 2 * (feat.slab_off + b));
         for (uint32_t c0 = half; c0 < chunks; c0 += 2 * kLoads) {
             uint32_t v[kLoads];
             int2 w[kLoads];
@@ -710,13 +718,13 @@ __device__ __forceinline__ void reduce_feature_bins_halves(const HistArgs& h, co
 // (64 threads cover a feature's 256 bins of one chunk; 8 such groups split the chunks, all of a group's loads in
 // flight together), and the 8 groups' sums meet in `scratch` (shared, 8 x 64 x 32 bytes).
 template <bool kPacked>
-__device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, const DevFeature& feat, uint32_t chunks,
-                                                          int4* scratch, int2* out) {
+__device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, const DevFeature& feat, uint32_t first,
+                                                          uint32_t chunks, int4* scratch, int2* out) {
     constexpr uint32_t kGroups = kHistThreads / 64, kLoads = 8;
     const uint32_t q = threadIdx.x & 63, g = threadIdx.x >> 6;
     int4 sg = make_int4(0, 0, 0, 0), sh = sg;  // bins 4q .. 4q+3: g and h sums
     if (4 * q < feat.num_bins) {
-        const int* base = h.slabs + (kPacked ? feat.slab_off + 4 * q : 2 * (feat.slab_off + 4 * q));
+        const int* base = h.slabs + static_cast<size_t>(first) * h.slab_ints + (kPacked ? feat.slab_off + 4 * q : 2 * (feat.slab_off + 4 * q));
         for (uint32_t c0 = g; c0 < chunks; c0 += kGroups * kLoads) {
             int4 v[kLoads], w[kLoads];
 #pragma unroll
@@ -764,48 +772,56 @@ __device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, con
     __syncthreads();
 }
 
-// The step's search for feature `f` in one CTA, both children at once, in two parts. feature_bins_cta: the built
-// child's bins reduced from the slabs (and, with ranks, summed over every rank's: exchange_bins) into `bufs`
-// (2 kMaxBins int2 of shared memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction);
-// *evaluated says whether the feature is searched at all (`evaluate`: the step's features). False when a rank did
-// not answer (error recorded).
-__device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, uint32_t f, uint32_t chunks, bool packed,
-                                 const uint8_t* evaluate, int2* bufs, int4* scratch, const GrowExchange& x,
-                                 uint32_t epoch, bool* evaluated) {
+// The search of split j of a step for feature `f` in one CTA, both children at once, in two parts.
+// feature_bins_cta: the built child's bins reduced from the split's slabs (`chunks` of them from slab `first`,
+// packed or not) and, with ranks, summed over every rank's (exchange_bins), into `bufs` (2 kMaxBins int2 of shared
+// memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction); *evaluated says whether the
+// feature is searched at all (`evaluate`: the split's features). False when a rank did not answer (error recorded).
+__device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, uint32_t j, uint32_t f, uint32_t first,
+                                 uint32_t chunks, bool packed, const uint8_t* evaluate, int2* bufs, int4* scratch,
+                                 const GrowExchange& x, uint32_t epoch, bool* evaluated) {
     const DevFeature feat = a.d.features[f];
     *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
     if (!*evaluated) return true;
     if (scratch != nullptr) {
         if (packed)
-            reduce_feature_bins_quads<true>(h, feat, chunks, scratch, bufs);
+            reduce_feature_bins_quads<true>(h, feat, first, chunks, scratch, bufs);
         else
-            reduce_feature_bins_quads<false>(h, feat, chunks, scratch, bufs);
+            reduce_feature_bins_quads<false>(h, feat, first, chunks, scratch, bufs);
     } else if (packed) {
-        reduce_feature_bins_halves<true>(h, feat, chunks, bufs + kMaxBins, bufs);
+        reduce_feature_bins_halves<true>(h, feat, first, chunks, bufs + kMaxBins, bufs);
     } else {
-        reduce_feature_bins_halves<false>(h, feat, chunks, bufs + kMaxBins, bufs);
+        reduce_feature_bins_halves<false>(h, feat, first, chunks, bufs + kMaxBins, bufs);
     }
-    return x.world == 1 || exchange_bins(x, epoch, a.num_features, f, feat.num_bins, bufs, &a.iter->error);
+    return x.world == 1 || exchange_bins(x, epoch, a.num_features, j, f, feat.num_bins, bufs, &a.iter->error);
+}
+
+// The histogram slot split j of a step writes child `c`'s bins to: the child's own (learner.rs:365-367), except
+// that the child which keeps the parent's index takes a spare slot (max_leaves + j - 1) when the split is
+// speculative (j >= 1), so that the parent's bins survive a dropped split; the finish copies it over on commit.
+__device__ __forceinline__ size_t child_slot(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t j, int c) {
+    return j > 0 && s.child[c] == st.leaf ? static_cast<size_t>(a.max_leaves) + j - 1 : static_cast<size_t>(s.child[c]);
 }
 
 // feature_scan_cta: with the built child's bins in `bufs`, group 0 scans the built child and group 1 the sibling
 // (parent - built, learner.rs:365-367; group 1 alone reads the parent's slot, which the built child may take over,
-// and writes both children's), each with scan_feature_group, as search_item_group does for one item.
-__device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t f, bool evaluated,
-                                 int2* bufs, ScanShared* scan_sh) {
+// and writes both children's), each with scan_feature_group, as search_item_group does for one item. The
+// candidates go to rows 2 j (built) and 2 j + 1 (sibling) of F.
+__device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t j, uint32_t f,
+                                 bool evaluated, int2* bufs, ScanShared* scan_sh) {
     const uint32_t F = a.num_features;
     const uint32_t group = threadIdx.x / kScanThreads, t = threadIdx.x % kScanThreads;
-    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates);
+    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates) + static_cast<size_t>(2 * j) * F;
+    uint8_t* cand_flags = a.cand_flags + static_cast<size_t>(2 * j) * F;
+    double* cand_gain = a.cand_gain + static_cast<size_t>(2 * j) * F;
     if (!evaluated) {
         if (threadIdx.x == 0) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
             cands[f] = none;
             cands[F + f] = none;
-            if (a.cand_flags) {
-                a.cand_flags[f] = 0;
-                a.cand_flags[F + f] = 0;
-            }
+            cand_flags[f] = 0;
+            cand_flags[F + f] = 0;
         }
         return;
     }
@@ -823,8 +839,8 @@ __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const Searc
         const int2 bt = built[t];
         const int2 o = make_int2(p.x - bt.x, p.y - bt.y);
         other[t] = o;
-        __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[0]) * slot_len + off) + t, bt);
-        __stcg(reinterpret_cast<int2*>(a.slots + static_cast<size_t>(s.child[1]) * slot_len + off) + t, o);
+        __stcg(reinterpret_cast<int2*>(a.slots + child_slot(a, st, s, j, 0) * slot_len + off) + t, bt);
+        __stcg(reinterpret_cast<int2*>(a.slots + child_slot(a, st, s, j, 1) * slot_len + off) + t, o);
     }
     const int bar = 1 + ch;
     if (st.root && group == 1) {
@@ -832,7 +848,7 @@ __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const Searc
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
             cands[F + f] = none;
-            if (a.cand_flags) a.cand_flags[F + f] = 0;
+            cand_flags[F + f] = 0;
         }
     } else {
         group_sync(bar);  // the group's bins are in place
@@ -840,10 +856,8 @@ __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const Searc
                                                       a.cfg, scan_sh[group], bar);
         if (t == 0) {
             cands[static_cast<size_t>(ch) * F + f] = c;
-            if (a.cand_flags) {
-                a.cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
-                a.cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
-            }
+            cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
+            cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
         }
     }
     __syncthreads();  // the buffers and the scratch are free for the CTA's next feature

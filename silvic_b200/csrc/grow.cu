@@ -2,15 +2,16 @@
 //
 // A split step as separate launches costs a launch and a reload of the dataset's metadata per kernel, about 40 us
 // of fixed time per split on small leaves, which dominates a 255-leaf tree. Here one cooperative launch (every CTA
-// resident, one per SM) runs every step of the tree; its phases are separated by grid barriers:
-//   root:   histogram -> [slab reduction] -> search -> finish
-//   split:  partition flags -> scatter -> histogram of the smaller child -> [slab reduction] -> search -> finish
-// (the slab reduction only for histograms through shared memory). Every CTA runs `finish` (apply the split, pick
-// each child's best split, choose the next leaf) on the same inputs and reaches the same next step in its own
-// shared memory; four CTAs write its results for later steps and kernels (search_finish_prepare). Work a CTA can do
-// before the others reach a barrier (the next search's context, the finish's parts without candidates) runs between
-// its arrival and its wait. The phases are the device functions of partition.cuh, hist_device.cuh and search.cuh,
-// which the standalone kernels of the multi-GPU path also run.
+// resident, one per SM) runs every step of the tree, in grid steps of up to kSplits splits (the best leaf's and,
+// speculatively, the next ones', steps.cuh); a grid step's phases are separated by two grid barriers:
+//   each split: partition of the parent -> histogram of the smaller child (fused.cuh), the splits side by side on
+//               shares of the grid  |  the slab reductions and searches, one (split, feature) per CTA at a time
+//               |  finish
+// (the root: its histogram, its reduction and search, its finish). Every CTA runs the finish (commit the splits that
+// hold, pick each child's best split, choose the next splits) on the same inputs and reaches the same next grid
+// step in its own shared memory; three CTAs write its results for later steps and kernels. Work a CTA can do before
+// the others reach a barrier (the first search item's reduction, the finish's parts without candidates) runs
+// between its arrival and its wait.
 //
 // Every barrier wait is bounded: a CTA that waits longer than kBarrierSpins polls records an error in the
 // iteration state and leaves the kernel, and every other CTA then leaves at its next barrier; the host reports the
@@ -19,6 +20,7 @@
 
 #include "fused.cuh"
 #include "search.cuh"
+#include "steps.cuh"
 
 namespace sb2 {
 
@@ -33,7 +35,7 @@ struct GrowArgs {
     unsigned int* barrier;        // arrivals at grid barriers so far (zeroed before the launch)
     unsigned long long* phase_ns; // optional: nanoseconds spent per phase (kGrowPhases), summed over steps,
     int trace_steps;              // then per-step rows (kStepTrace) for this many steps
-    uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags (5 F bytes)
+    uint32_t flags_offset;        // bytes into the dynamic shared memory of the per-feature flags ((5 kSplits + 1) F)
     uint32_t scan_offset;         // ... of the partition's scan words (2 kHistThreads + 64), past the histogram
     uint32_t stage_offset;        // ... of the histogram's staging slots (16 warps x stage_depth x slot_bytes)
     uint32_t slot_bytes;
@@ -41,8 +43,6 @@ struct GrowArgs {
     uint32_t pad_;
     GrowExchange x;               // the other ranks (world 1: none)
 };
-
-__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -75,12 +75,12 @@ __device__ __forceinline__ void clock_step(const GrowArgs& g, PhaseClock& c, int
     c.row = step + 1 < g.trace_steps ? g.phase_ns + kGrowPhases + static_cast<size_t>(step + 1) * kStepTrace : nullptr;
 }
 
-__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, bool packed,
-                                               uint32_t leaf_rows) {
+// The grid step's sizes in its trace row: the rows of its histograms and its splits (the committed ones are added
+// at its finish).
+__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, uint32_t splits) {
     if (!clock_owner(g) || c.row == nullptr) return;
     c.row[kGrowPhases] = job_rows;
-    c.row[kGrowPhases + 1] = packed;
-    c.row[kGrowPhases + 2] = leaf_rows;
+    c.row[kGrowPhases + 1] = splits;
 }
 
 // `*p`, which another CTA may have written in this launch, copied into shared memory once per CTA (one 32-bit word
@@ -140,6 +140,13 @@ __device__ __forceinline__ bool grid_barrier(const GrowArgs& g, unsigned int& ta
     return barrier_wait(g, target);
 }
 
+// How a grid step's splits share the grid in its first phase: split j takes `budget` CTAs from `base` (in
+// proportion to its rows, at least one), of which `chunks` take part; its slabs hold packed sums when `packed`.
+struct SplitPlan {
+    uint32_t base, chunks, count;
+    uint32_t packed;
+};
+
 __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) {
     extern __shared__ __align__(16) int smem[];
     const TrainArgs& a = g.t;
@@ -150,19 +157,23 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     static_assert(kGroups == 2, "one scan group per child");
     __shared__ ScanShared scan_shared[kGroups];
     const uint32_t F = a.num_features;
-    // Every CTA keeps the learner's control state itself: the step, the evaluated features. The finish runs in
-    // every CTA on the same inputs, so no CTA waits for another to publish the next step.
-    __shared__ Step st;
+    // Every CTA keeps the learner's control state itself: the grid step's splits and their features. The finish
+    // runs in every CTA on the same inputs, so no CTA waits for another to publish the next step.
+    __shared__ Step st[kSplits];
+    __shared__ int s_n;  // splits of the grid step (0: the tree is done)
     __shared__ HistJob root_job;
-    __shared__ SearchCtx s;
-    __shared__ FinishShared fs;
+    __shared__ SearchCtx sc[kSplits];
+    __shared__ StepsFinish fs;
+    __shared__ SplitPlan plan[kSplits];
     __shared__ PhaseClock clock;
-    __shared__ uint32_t s_left;
+    __shared__ uint32_t s_left[kSplits];          // this rank's left counts
+    __shared__ int64_t s_left_global[kSplits];    // every rank's
     uint32_t* scan = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(smem) + g.scan_offset);
-    uint8_t* eval = reinterpret_cast<uint8_t*>(smem) + g.flags_offset;  // F: features this step searches
-    uint8_t* mask = eval + F;                                            // F: the iteration's feature mask
-    uint8_t* csplit = mask + F;                                          // 2 F: the children's splittable flags
-    uint8_t* osplit = csplit + 2 * F;                                    // F: the best other leaf's
+    uint8_t* eval = reinterpret_cast<uint8_t*>(smem) + g.flags_offset;  // kSplits rows of F: each split's features
+    uint8_t* mask = eval + kSplits * F;                                  // F: the iteration's feature mask
+    uint8_t* csplit = mask + F;                                          // 2 kSplits rows: the children's splittable
+    uint8_t* osplit = csplit + 2 * kSplits * F;                          // kSplits rows: the best other leaves'
+    uint8_t* psplit = osplit + kSplits * F;                              // kSplits rows: the split leaves'
     if (clock_owner(g)) clock = PhaseClock{nullptr, global_ns()};
     unsigned int target = 0;  // the barrier count that releases the next barrier (see grid_barrier)
     // The first units' descriptions, kept for the launch; later units are described per use.
@@ -175,8 +186,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
     for (uint32_t i = threadIdx.x; i < g.scan_offset / 16; i += kGrowThreads)
         reinterpret_cast<int4*>(smem)[i] = make_int4(0, 0, 0, 0);
     const uint32_t round_rows = packed_round_rows(*g.h.spec);  // the iteration's quantization, set before the launch
+    const size_t flag_words = a.d.num_rows / 32 + 2;             // per split
     // The root step, its job and features, as the iteration's start left them.
-    broadcast_cg(a.step, &st);
+    broadcast_cg(a.step, &st[0]);
     broadcast_cg(a.hist_job, &root_job);
     {
         const uint8_t* iter_mask = a.masks + static_cast<size_t>(a.iter->iteration) * F;
@@ -185,80 +197,119 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             mask[f] = iter_mask[f];
         }
     }
+    if (threadIdx.x == 0) s_n = st[0].active ? 1 : 0;
     __syncthreads();
 
-    for (int step = -1; step + 1 < a.max_leaves; ++step) {
-        clock_step(g, clock, step);
-        if (!st.active) break;
-        // Phase A: the parent's partition and the built child's histogram into the slabs (the root: its histogram).
-        FusedStep f{};
-        f.root = st.root;
-        f.count = st.root ? root_job.count : st.count;
-        f.begin = st.root ? 0u : st.begin;
-        f.src = st.which & 1;
-        f.dst = f.src ^ 1u;
-        f.built_left = st.built_left;
-        f.histogram = st.root ? root_job.active != 0 : st.may_search != 0;
-        f.chunks = fused_chunks(f.count, ctas);
-        f.round_rows = round_rows;
-        f.packed = fused_packed(f.count, f.chunks, round_rows);
-        f.identity = !st.root && st.depth == 0;  // the root leaf's rows are still in row order
-        f.stage = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + g.stage_offset;
-        f.slot_bytes = g.slot_bytes;
-        f.depth = g.stage_depth;
-        unsigned int* cursor = a.cursors + 2 * (st.root ? 0 : st.new_leaf);
-        clock_describe(g, clock, f.histogram ? f.count : 0u, f.packed, st.count);
-        fused_step_cta(a, g.h, st, f, cta, smem, scan, cursor, eval, units, cached, &spare);
+    // Grid step gs (-1: the root) runs the splits st[0 .. n).
+    for (int gs = -1; gs < a.max_leaves; ++gs) {
+        clock_step(g, clock, gs);
+        const int n = s_n;
+        if (n == 0) break;
+        // Phase A: each split's partition and built child's histogram into its slabs (the root: its histogram),
+        // every CTA working on one split.
+        if (threadIdx.x == 0) {
+            uint64_t total = 0;
+            for (int j = 0; j < n; ++j) total += st[j].root ? root_job.count : st[j].count;
+            uint32_t base = 0, hist_rows = 0;
+            for (int j = 0; j < n; ++j) {
+                const uint32_t count = st[j].root ? root_job.count : st[j].count;
+                const uint32_t budget =
+                    1u + static_cast<uint32_t>(total ? static_cast<uint64_t>(ctas - n) * count / total : 0);
+                const uint32_t chunks = fused_chunks(count, budget);
+                plan[j] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
+                base += budget;
+                if (st[j].root ? root_job.active != 0 : st[j].may_search != 0) hist_rows += count;
+            }
+            clock_describe(g, clock, hist_rows, static_cast<uint32_t>(n));
+        }
+        __syncthreads();
+        int mine = -1;
+        for (int j = 0; j < n; ++j)
+            if (cta >= plan[j].base && cta < plan[j].base + plan[j].chunks) mine = j;
+        if (mine >= 0) {
+            const Step& sj = st[mine];
+            FusedStep f{};
+            f.root = sj.root;
+            f.count = plan[mine].count;
+            f.begin = sj.root ? 0u : sj.begin;
+            f.src = sj.which & 1;
+            f.dst = f.src ^ 1u;
+            f.built_left = sj.built_left;
+            f.histogram = sj.root ? root_job.active != 0 : sj.may_search != 0;
+            f.chunks = plan[mine].chunks;
+            f.round_rows = round_rows;
+            f.packed = plan[mine].packed != 0;
+            f.identity = !sj.root && sj.depth == 0;  // the root leaf's rows are still in row order
+            f.stage = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + g.stage_offset;
+            f.slot_bytes = g.slot_bytes;
+            f.depth = g.stage_depth;
+            unsigned int* cursor = a.cursors + 2 * (static_cast<size_t>(gs + 1) * kSplits + mine);
+            fused_step_cta(a, g.h, sj, f, cta - plan[mine].base, cta, a.flags + mine * flag_words, smem, scan, cursor,
+                           eval + static_cast<size_t>(mine) * F, units, cached, &spare);
+        }
         clock_mark(g, clock, 0);
         if (!grid_barrier(g, target)) return;
         clock_mark(g, clock, 4);
-        // The left count and the children's search context (every CTA: the finish is replicated), then the
-        // search: one feature per CTA, its built child's bins reduced from the slabs and both children scanned.
-        if (!st.root && threadIdx.x == 0) s_left = __ldcg(cursor);
+        // The left counts and the splits' search contexts (every CTA: the finish is replicated), then the search:
+        // items (split j, feature f) = j F + f, CTA c taking items c, c + ctas, ...: the built child's bins reduced
+        // from the split's slabs and both children scanned.
+        if (threadIdx.x < static_cast<uint32_t>(n))
+            s_left[threadIdx.x] = st[threadIdx.x].root ? 0u : __ldcg(a.cursors + 2 * (static_cast<size_t>(gs + 1) * kSplits + threadIdx.x));
         __syncthreads();
-        const uint32_t epoch = g.x.epoch0 + static_cast<uint32_t>(step + 2);  // this step's, on every rank
+        const uint32_t epoch = g.x.epoch0 + static_cast<uint32_t>(gs + 2);  // this grid step's, on every rank
         const bool ranks = g.x.world > 1;
-        const uint8_t* evaluate = st.root ? mask : eval;  // the features this step searches (search_context's)
         int2* bufs = reinterpret_cast<int2*>(scan);
         // the reduction's scratch: the histogram's staging slots, free in this phase
         int4* scratch = g.stage_depth * (kGrowThreads / 32) * g.slot_bytes >= 16384
                             ? reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(smem) + g.stage_offset)
                             : nullptr;
-        if (ranks && !st.root && cta == 0 && threadIdx.x < 32) publish_left(g.x, epoch, s_left);
-        // With at most one feature per CTA, its bins (and their exchange) come first, so that the left counts'
-        // exchange has arrived by the time the search context needs it.
-        const bool early = f.histogram && F <= ctas;
-        bool evaluated = false;
-        if (early && cta < F &&
-            !feature_bins_cta(a, g.h, cta, f.chunks, f.packed, evaluate, bufs, scratch, g.x, epoch, &evaluated))
-            return;
-        int64_t left_global = s_left;
-        if (ranks && !st.root && !gather_left(g.x, epoch, &a.iter->error, &left_global)) return;
-        if (warp == 0) {
-            const SearchCtx c = search_context(a, st, st.root ? 0 : left_global, eval, mask);
-            if (lane_id() == 0) s = c;
+        if (ranks && !st[0].root && cta == 0 && threadIdx.x < 32) publish_left(g.x, epoch, s_left, n);
+        const uint32_t items = static_cast<uint32_t>(n) * F;
+        // The CTA's first item's bins (and their exchange) come before the contexts, so that the left counts'
+        // exchange has arrived by the time the contexts need it.
+        bool have = false, evaluated = false;
+        if (cta < items) {
+            const uint32_t j = cta / F, f = cta % F;
+            if (st[j].root ? root_job.active != 0 : st[j].may_search != 0) {
+                const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
+                if (!feature_bins_cta(a, g.h, j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate, bufs,
+                                      scratch, g.x, epoch, &evaluated))
+                    return;
+                have = true;
+            }
+        }
+        if (ranks && !st[0].root) {
+            if (!gather_left(g.x, epoch, n, &a.iter->error, s_left_global)) return;
+        } else if (threadIdx.x < static_cast<uint32_t>(n)) {
+            s_left_global[threadIdx.x] = s_left[threadIdx.x];
+        }
+        __syncthreads();
+        if (warp < static_cast<uint32_t>(n)) {
+            const SearchCtx c = search_context(a, st[warp], st[warp].root ? 0 : s_left_global[warp],
+                                               eval + static_cast<size_t>(warp) * F, mask);
+            if ((threadIdx.x & 31) == 0) sc[warp] = c;
         }
         __syncthreads();
         clock_mark(g, clock, 1);
-        if (s.searched) {
-            if (early) {
-                if (cta < F) feature_scan_cta(a, st, s, cta, evaluated, bufs, scan_shared);
-            } else {
-                for (uint32_t feature = cta; feature < F; feature += ctas) {
-                    if (!feature_bins_cta(a, g.h, feature, f.chunks, f.packed, evaluate, bufs, scratch, g.x, epoch,
-                                          &evaluated))
-                        return;
-                    feature_scan_cta(a, st, s, feature, evaluated, bufs, scan_shared);
-                }
+        for (uint32_t i = cta; i < items; i += ctas) {
+            const uint32_t j = i / F, f = i % F;
+            if (!sc[j].searched) continue;
+            if (i != cta || !have) {
+                const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
+                if (!feature_bins_cta(a, g.h, j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate, bufs,
+                                      scratch, g.x, epoch, &evaluated))
+                    return;
             }
+            feature_scan_cta(a, st[j], sc[j], j, f, evaluated, bufs, scan_shared);
         }
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.
-        search_finish_prepare(a, st, s, st.root ? 0u : s_left, cta, osplit, fs);
+        steps_finish_prepare(a, st, n, sc, s_left, osplit, psplit, fs);
         if (!barrier_wait(g, target)) return;
         clock_mark(g, clock, 4);
-        search_finish_replicated(a, st, s, eval, mask, csplit, osplit, cta, fs);
+        steps_finish(a, st, s_n, sc, eval, mask, csplit, osplit, psplit, cta, fs);
+        if (clock_owner(g) && clock.row) clock.row[kGrowPhases + 2] = static_cast<unsigned long long>(fs.committed);
         clock_mark(g, clock, 3);
     }
 }
@@ -296,8 +347,8 @@ cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet
     if (e != cudaSuccess) return e;
-    // every step's placement cursors start at zero
-    e = cudaMemsetAsync(t.cursors, 0, sizeof(unsigned int) * 2 * static_cast<size_t>(t.max_leaves), s);
+    // every split's placement cursors start at zero
+    e = cudaMemsetAsync(t.cursors, 0, sizeof(unsigned int) * 2 * kSplits * (static_cast<size_t>(t.max_leaves) + 1), s);
     if (e != cudaSuccess) return e;
     void* args[] = {&g};
     return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(grow_tree_kernel), dim3(grid), dim3(kGrowThreads),

@@ -510,12 +510,15 @@ __device__ void root_units(const TrainArgs& a, double& ug, double& uh) {
     uh = static_cast<double>(h);
 }
 
-// Tree::split (tree.rs:143-177) for a numerical split; returns the new leaf.
-__device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_info& info, const DevFeature& f,
-                              int64_t left_count, int64_t right_count, double hs, double min_gain_to_split) {
+// Tree::split (tree.rs:143-177) for a numerical split of `leaf` into `leaf` and the new leaf `nl` (node nl - 1),
+// without the leaf count. Splits of different leaves into different new leaves may run at once: each writes only its
+// own node, leaves and child pointer (a parent's left pointer is read only by the split of its left child's leaf,
+// the one that may write it).
+__device__ void tree_split_at(const DevTree& t, int32_t leaf, int32_t nl, const sb2_split_info& info,
+                              const DevFeature& f, int64_t left_count, int64_t right_count, double hs,
+                              double min_gain_to_split) {
     // Every load before the first store, so they are in flight together; through L2, since the CTA that split
     // earlier leaves may have been another one.
-    const int32_t nl = __ldcg(t.num_leaves);
     const int32_t parent = __ldcg(t.leaf_parent + leaf);
     const double old_weight = __ldcg(t.leaf_weight + leaf), old_value = __ldcg(t.leaf_value + leaf);
     const int32_t depth = __ldcg(t.leaf_depth + leaf) + 1;
@@ -548,6 +551,13 @@ __device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_in
     t.leaf_parent[nl] = node;
     t.leaf_depth[leaf] = depth;
     t.leaf_depth[nl] = depth;
+}
+
+// Tree::split as one step: the new leaf is the tree's next; returns it.
+__device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_info& info, const DevFeature& f,
+                              int64_t left_count, int64_t right_count, double hs, double min_gain_to_split) {
+    const int32_t nl = __ldcg(t.num_leaves);
+    tree_split_at(t, leaf, nl, info, f, left_count, right_count, hs, min_gain_to_split);
     *t.num_leaves = nl + 1;
     return nl;
 }
@@ -994,242 +1004,8 @@ __device__ void search_finish(const TrainArgs& a, const Step& st, const SearchCt
     if (lane == 0) *next = next_step(a, leaf, best_leaf, num_leaves, f);
 }
 
-// The children's records and best splits as the persistent kernel's CTAs share them during a finish.
-struct FinishShared {
-    DevLeaf child[2];
-    sb2_split_info best[2];
-    int32_t has_best[2];
-    double other_gain;
-    int32_t other_leaf;
-    DevLeaf other;  // the record of other_leaf (when there is one)
-};
-
 // Whether CTA `cta` writes part `part` of a finish (CTA `part`, or CTA 0 in a grid of fewer than four).
 __device__ __forceinline__ bool writes_part(uint32_t cta, uint32_t part) { return cta == (part < gridDim.x ? part : 0u); }
-
-// search_finish for the persistent kernel, run by every CTA: each reads the same candidates and records and reaches
-// the same next step, in its own shared memory. The part that does not need this step's candidates,
-// search_finish_prepare, runs while the CTA waits at the search barrier; search_finish_replicated runs after it.
-// `st` (in: this step; out: the next), `left` the left child's rows, `eval` (shared, F bytes) the next step's
-// evaluated features, from the iteration's `mask` (shared, F bytes), `csplit` (shared, 2 F bytes) the children's
-// splittable flags. Four CTAs also write what later steps and kernels read, one part each so that no CTA's finish
-// is much longer than the others': CTA 0 the tree (Tree::split), CTA 1 the leaf records and their gains
-// (TrainArgs::leaf_gain), CTA 2 the children's splittable rows, CTA 3 the evaluated features. Every CTA reads only
-// entries no CTA writes in the same step (leaves chosen before this step, and the candidates). One CTA of at least
-// 128 threads.
-__device__ void search_finish_prepare(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t left,
-                                      uint32_t cta, uint8_t* osplit, FinishShared& fs) {
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const IterState& it = *a.iter;
-    if (warp == 0) {
-        if (lane == 0) {
-            if (st.root) {
-                DevLeaf l = load_cg(a.leaves);  // begin, count, which, depth: set before the launch
-                l.units_grad = s.ctx[0].units_grad;
-                l.units_hess = s.ctx[0].units_hess;
-                l.count_global = it.root_count;
-                l.has_hist = s.searched;
-                l.has_best = 0;
-                fs.child[0] = l;
-            } else {
-                DevLeaf l{}, r{};
-                l.begin = st.begin;
-                l.count = left;
-                r.begin = st.begin + left;
-                r.count = st.count - left;
-                l.which = r.which = st.which ^ 1u;
-                l.depth = r.depth = st.depth + 1;
-                l.units_grad = st.info.left_grad;
-                l.units_hess = st.info.left_hess;
-                l.count_global = s.left_global;
-                r.units_grad = st.info.right_grad;
-                r.units_hess = st.info.right_hess;
-                r.count_global = s.right_global;
-                l.has_hist = r.has_hist = s.searched;
-                // child 0 is the built child: the left one (index st.leaf) when built_left
-                fs.child[st.built_left ? 0 : 1] = l;
-                fs.child[st.built_left ? 1 : 0] = r;
-                if (writes_part(cta, 0)) {
-                    if (s.left_global <= 0 || s.right_global <= 0) {
-                        a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
-                        a.iter->error_info = st.leaf;
-                    }
-                    const DevFeature f = a.d.features[st.info.feature];
-                    const int32_t nl = tree_split(a.tree, st.leaf, st.info, f, s.left_global, s.right_global,
-                                                  it.spec.hess_scale, a.cfg.min_gain_to_split);
-                    if (nl != st.new_leaf) {
-                        a.iter->error = 2;
-                        a.iter->error_info = nl;
-                    }
-                }
-            }
-        }
-    } else if (warp == 3) {
-        // Leaves that existed before this step, other than the one being split: their gains, as CTA 1 left them
-        // in earlier steps.
-        const int32_t before = st.root ? 0 : st.new_leaf;
-        double gain = -INFINITY;
-        int32_t leaf = -1;
-        for (int32_t l0 = 0; l0 < before; l0 += 128) {
-            double g[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int32_t l = l0 + 32 * j + static_cast<int32_t>(lane);
-                g[j] = l < before && l != st.leaf ? __ldcg(a.leaf_gain + l) : -INFINITY;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (g[j] != -INFINITY) prefer_leaf(gain, leaf, g[j], l0 + 32 * j + static_cast<int32_t>(lane));
-        }
-        for (int o = 16; o > 0; o >>= 1)
-            prefer_leaf(gain, leaf, __shfl_xor_sync(0xffffffffu, gain, o), __shfl_xor_sync(0xffffffffu, leaf, o));
-        if (lane == 0) {
-            fs.other_gain = gain;
-            fs.other_leaf = leaf;
-        }
-        // Its record and splittable row, in case it is split next (CTA 1 and CTA 2 wrote them in earlier steps).
-        if (leaf >= 0) {
-            if (lane == 0) fs.other = load_cg(a.leaves + leaf);
-            const uint32_t F = a.num_features;
-            const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
-            for (uint32_t k0 = 0; k0 < F; k0 += 128) {
-                uint8_t o[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t k = k0 + 32u * j + lane;
-                    o[j] = k < F ? __ldcg(row + k) : 0;
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t k = k0 + 32u * j + lane;
-                    if (k < F) osplit[k] = o[j];
-                }
-            }
-        }
-    }
-    __syncthreads();
-}
-
-__device__ void search_finish_replicated(const TrainArgs& a, Step& st, const SearchCtx& s, uint8_t* eval,
-                                         const uint8_t* mask, uint8_t* csplit, const uint8_t* osplit, uint32_t cta,
-                                         FinishShared& fs) {
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t F = a.num_features;
-    const int children = st.root ? 1 : 2;
-    if (warp >= 1 && warp <= 2) {
-        const int ch = static_cast<int>(warp) - 1;
-        if (ch < children) {
-            // The best candidate of the child over every feature by `better` (found, then the higher gain, then the
-            // lower feature), from the compact gains and flags; then the winner's full candidate. The splittable
-            // flags go to shared memory (and to the child's row, by CTA 2).
-            FeatureCandidate best{};
-            best.found = 0;
-            if (s.searched) {
-                const uint8_t* flags = a.cand_flags + static_cast<size_t>(ch) * F;
-                const double* gains = a.cand_gain + static_cast<size_t>(ch) * F;
-                uint8_t* row = a.splittable + static_cast<size_t>(s.child[ch]) * F;
-                int found = 0;
-                double bg = -INFINITY;
-                int32_t bf = -1;
-                for (uint32_t f0 = 0; f0 < F; f0 += 128) {
-                    uint8_t fl[4];
-                    double gn[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t f = f0 + 32u * j + lane;
-                        fl[j] = f < F ? __ldcg(flags + f) : 0;
-                        gn[j] = f < F ? __ldcg(gains + f) : 0.0;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t f = f0 + 32u * j + lane;
-                        if (f >= F) continue;
-                        const uint8_t ok = static_cast<uint8_t>((fl[j] >> 1) & 1);
-                        csplit[static_cast<size_t>(ch) * F + f] = ok;
-                        if (writes_part(cta, 2)) row[f] = ok;
-                        if (fl[j] & 1) {
-                            const double g = gn[j] != gn[j] ? -INFINITY : gn[j];  // `better` reads NaN as -inf
-                            if (!found || g > bg) {  // features rise with f: on equal gains the earlier stays
-                                found = 1;
-                                bg = g;
-                                bf = static_cast<int32_t>(f);
-                            }
-                        }
-                    }
-                }
-                for (int o = 16; o > 0; o >>= 1) {
-                    const int of = __shfl_xor_sync(0xffffffffu, found, o);
-                    const double og = __shfl_xor_sync(0xffffffffu, bg, o);
-                    const int32_t obf = __shfl_xor_sync(0xffffffffu, bf, o);
-                    if (of && (!found || og > bg || (og == bg && obf < bf))) {
-                        found = 1;
-                        bg = og;
-                        bf = obf;
-                    }
-                }
-                if (found) best = load_candidate(static_cast<const FeatureCandidate*>(a.candidates) +
-                                                 static_cast<size_t>(ch) * F + bf);
-            }
-            if (lane == 0) {
-                const bool has = best.found && s.ctx[ch].valid;
-                fs.has_best[ch] = has;
-                fs.best[ch] = has ? finish(s.ctx[ch], best, a.cfg) : sb2_split_info{};
-            }
-        }
-    }
-    __syncthreads();
-    if (warp == 0) {
-        // Join: the children's best splits, then the best leaf over children and others.
-        if (lane < static_cast<uint32_t>(children)) {
-            fs.child[lane].has_best = fs.has_best[lane];
-            if (fs.has_best[lane]) fs.child[lane].best = fs.best[lane];
-        }
-        __syncwarp();
-        double gain = fs.other_gain;
-        int32_t best_leaf = fs.other_leaf;
-        for (int ch = 0; ch < children; ++ch)
-            if (fs.child[ch].has_best) prefer_leaf(gain, best_leaf, fs.child[ch].best.gain, s.child[ch]);
-        const int32_t num_leaves = st.root ? 1 : st.new_leaf + 1;
-        const bool go = best_leaf >= 0 && gain > 0.0 && num_leaves < a.max_leaves;
-        const int chosen = !go ? -1 : best_leaf == s.child[0] ? 0 : (children == 2 && best_leaf == s.child[1]) ? 1 : -1;
-        if (writes_part(cta, 1) && lane < static_cast<uint32_t>(children)) {
-            DevLeaf c = fs.child[lane];
-            if (static_cast<int>(lane) == chosen) c.has_best = 0;  // it is split next
-            a.leaves[s.child[lane]] = c;
-            a.leaf_gain[s.child[lane]] = c.has_best ? c.best.gain : -INFINITY;
-        }
-        if (go) {
-            // the chosen leaf: a child, or the best other leaf (prefetched by search_finish_prepare)
-            const DevLeaf leaf = chosen >= 0 ? fs.child[chosen] : fs.other;
-            const DevFeature f = a.d.features[leaf.best.feature];
-            // Features the children evaluate: the tree's mask and the parent's splittable ones (learner.rs:278-284).
-            // CTA 3 also leaves them in global memory, where the histograms read them (after two barriers).
-            const uint8_t* split_ok = chosen >= 0 ? csplit + static_cast<size_t>(chosen) * F : osplit;
-            for (uint32_t k0 = 0; k0 < F; k0 += 128) {
-                uint8_t o[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t k = k0 + 32u * j + lane;
-                    o[j] = k < F ? split_ok[k] : 0;
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t k = k0 + 32u * j + lane;
-                    if (k < F) {
-                        const uint8_t e = static_cast<uint8_t>(mask[k] && o[j]);
-                        eval[k] = e;
-                        if (writes_part(cta, 3)) a.evaluate[k] = e;
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) st = next_step(a, leaf, best_leaf, num_leaves, f);
-        } else if (lane == 0) {
-            st.active = 0;
-        }
-    }
-    __syncthreads();
-}
 
 }  // namespace
 

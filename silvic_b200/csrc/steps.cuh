@@ -1,0 +1,429 @@
+// steps.cuh — the persistent tree kernel's grid steps: the best leaf's split and, run beside it, the splits of the
+// next kSplits - 1 leaves in the order the learner would take them, committed only as far as that order holds.
+//
+// The learner splits one leaf at a time, always the leaf with the best split (Learner::grow, learner.rs:158-163,
+// with the ties of `prefer_leaf`). Ranked at the end of a step, the leaves X1, X2, ... by their best gains, X1 is
+// split next; X2 is split after it exactly when neither child of X1 prefers over X2; X3 after that when no child of
+// X1 or X2 prefers over it; and so on: every other leaf already ranks below them, and a leaf's split (its rows, its
+// histogram, its children's searches) does not depend on the splits before it. A grid step therefore runs the
+// splits of X1 .. Xn together (n <= kSplits, each a whole partition, histogram and search) and, at its finish,
+// commits X1 and then each next Xj while the rule holds; the first Xj that a new child outranks, and all after it,
+// are dropped: their leaves stay leaves, as they were, and are ranked again. The committed sequence is the
+// learner's own, so the tree is identical. On trees of config 2 the next split is a child of the previous one for
+// about 1.5% of splits, so a step commits nearly all of its splits.
+//
+// A dropped split leaves no trace: its partition wrote only the other buffer's copy of its own positions (its leaf
+// record still names the buffer that holds its rows), its children's histograms went to spare slots (copied to the
+// children's slots only when committed), and its candidates and records are overwritten by later steps.
+#pragma once
+
+#include "search.cuh"
+#include "train.cuh"
+
+namespace sb2 {
+
+// The finish's scratch (shared memory of every CTA).
+struct StepsFinish {
+    DevLeaf child[kSplits][2];           // the children of every split (child 0 the built one)
+    sb2_split_info best[kSplits][2];
+    int32_t has_best[kSplits][2];
+    double other_gain[kSplits];          // the best leaves that no split of the step touches
+    int32_t other_leaf[kSplits];
+    DevLeaf other[kSplits];              // their records
+    DevLeaf pending[kSplits];            // the records of the step's own leaves (split j >= 1), kept if dropped
+    int32_t committed;                   // splits committed by this step
+    int32_t next_n;                      // splits of the next step
+    Step next[kSplits];
+    int32_t next_from[kSplits];          // where each next split's leaf comes from (kPool* codes)
+};
+
+// The leaves a finish ranks, one per lane of a warp: the untouched best leaves (code k), the committed splits'
+// children (kPoolChild + 2 i + c) and the dropped splits' own leaves (kPoolPending + j).
+constexpr int kPoolChild = kSplits, kPoolPending = 3 * kSplits;
+static_assert(4 * kSplits <= 32, "the finish ranks one leaf per lane");
+
+// The leaf indices of split `st`'s children: [built, other] (the left child keeps the parent's index).
+__device__ __forceinline__ void child_indices(const Step& st, int32_t (&idx)[2]) {
+    idx[0] = st.built_left ? st.leaf : st.new_leaf;
+    idx[1] = st.built_left ? st.new_leaf : st.leaf;
+}
+
+// Whether (og, ol) comes first in the learner's order over (g, l): the higher gain, then the lower index.
+__device__ __forceinline__ bool ranks_before(double og, int32_t ol, double g, int32_t l) {
+    return og > g || (og == g && ol < l);
+}
+
+// Before the step's last grid barrier completes (no candidate needed): every split's children records (warp 0);
+// the kSplits best leaves no split touches, and their records and splittable rows (warp 3); the records and rows
+// of the step's own speculative leaves (warp 4). `left[j]`: split j's left count on this rank.
+__device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, const SearchCtx* sc,
+                                     const uint32_t* left, uint8_t* osplit, uint8_t* psplit, StepsFinish& fs) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t F = a.num_features;
+    const IterState& it = *a.iter;
+    if (warp == 0 && lane < static_cast<uint32_t>(n)) {
+        const int j = static_cast<int>(lane);
+        const Step& s = st[j];
+        if (s.root) {
+            DevLeaf l = load_cg(a.leaves);  // begin, count, which, depth: set before the launch
+            l.units_grad = sc[j].ctx[0].units_grad;
+            l.units_hess = sc[j].ctx[0].units_hess;
+            l.count_global = it.root_count;
+            l.has_hist = sc[j].searched;
+            l.has_best = 0;
+            fs.child[j][0] = l;
+        } else {
+            DevLeaf l{}, r{};
+            l.begin = s.begin;
+            l.count = left[j];
+            r.begin = s.begin + left[j];
+            r.count = s.count - left[j];
+            l.which = r.which = s.which ^ 1u;
+            l.depth = r.depth = s.depth + 1;
+            l.units_grad = s.info.left_grad;
+            l.units_hess = s.info.left_hess;
+            l.count_global = sc[j].left_global;
+            r.units_grad = s.info.right_grad;
+            r.units_hess = s.info.right_hess;
+            r.count_global = sc[j].right_global;
+            l.has_hist = r.has_hist = sc[j].searched;
+            fs.child[j][s.built_left ? 0 : 1] = l;
+            fs.child[j][s.built_left ? 1 : 0] = r;
+        }
+    } else if (warp == 3) {
+        // The leaves that existed before this step, other than the step's own: the kSplits best by their gains (as
+        // the writer CTA left them in earlier steps). Each lane keeps its own best kSplits in order; the warp then
+        // takes the best head kSplits times.
+        const int32_t before = st[0].root ? 0 : st[0].new_leaf;
+        double tg[kSplits];
+        int32_t tl[kSplits];
+#pragma unroll
+        for (int k = 0; k < kSplits; ++k) {
+            tg[k] = -INFINITY;
+            tl[k] = -1;
+        }
+        for (int32_t l0 = 0; l0 < before; l0 += 32 * 4) {
+            double g[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int32_t l = l0 + 32 * q + static_cast<int32_t>(lane);
+                g[q] = l < before ? __ldcg(a.leaf_gain + l) : -INFINITY;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                int32_t l = l0 + 32 * q + static_cast<int32_t>(lane);
+                bool skip = l >= before || g[q] == -INFINITY;
+                for (int j = 0; j < n; ++j) skip |= l == st[j].leaf;
+                if (skip) continue;
+                double gv = g[q];
+#pragma unroll
+                for (int k = 0; k < kSplits; ++k)  // insertion: the entry carried down swaps with worse ones
+                    if (tl[k] < 0 || ranks_before(gv, l, tg[k], tl[k])) {
+                        const double sg = tg[k];
+                        const int32_t sl = tl[k];
+                        tg[k] = gv;
+                        tl[k] = l;
+                        gv = sg;
+                        l = sl;
+                        if (l < 0) break;
+                    }
+            }
+        }
+        int32_t taken[kSplits];
+#pragma unroll
+        for (int k = 0; k < kSplits; ++k) {
+            double bg = tg[0];
+            int32_t bl = tl[0];
+            for (int o = 16; o > 0; o >>= 1)
+                prefer_leaf(bg, bl, __shfl_xor_sync(0xffffffffu, bg, o), __shfl_xor_sync(0xffffffffu, bl, o));
+            taken[k] = bl;
+            if (bl >= 0 && tl[0] == bl) {  // the owner pops its head
+#pragma unroll
+                for (int q = 0; q + 1 < kSplits; ++q) {
+                    tg[q] = tg[q + 1];
+                    tl[q] = tl[q + 1];
+                }
+                tg[kSplits - 1] = -INFINITY;
+                tl[kSplits - 1] = -1;
+            }
+            if (lane == 0) {
+                fs.other_gain[k] = bg;
+                fs.other_leaf[k] = bl;
+            }
+        }
+        // their records and splittable rows, in case they are split next
+        for (int k = 0; k < kSplits; ++k) {
+            const int32_t leaf = taken[k];
+            if (leaf < 0) continue;
+            if (lane == 0) fs.other[k] = load_cg(a.leaves + leaf);
+            const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
+            for (uint32_t f = lane; f < F; f += 32) osplit[static_cast<size_t>(k) * F + f] = __ldcg(row + f);
+        }
+    } else if (warp == 4) {
+        for (int j = 1; j < n; ++j) {
+            if (lane == 0) fs.pending[j] = load_cg(a.leaves + st[j].leaf);
+            const uint8_t* row = a.splittable + static_cast<size_t>(st[j].leaf) * F;
+            for (uint32_t f = lane; f < F; f += 32) psplit[static_cast<size_t>(j) * F + f] = __ldcg(row + f);
+        }
+    }
+    __syncthreads();
+}
+
+// The step's finish, in every CTA on the same inputs: each child's best split from the compact candidates (warps
+// 1 .. 2n), the splits committed, the tree, records and slots of the committed splits (writer CTAs), and the next
+// step's splits into `st` (and their features into `eval`, kSplits rows of F). `csplit` holds 2 kSplits rows of F
+// (the children's splittable flags), `mask` the iteration's feature mask.
+__device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchCtx* sc, uint8_t* eval,
+                             const uint8_t* mask, uint8_t* csplit, const uint8_t* osplit, const uint8_t* psplit,
+                             uint32_t cta, StepsFinish& fs) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t F = a.num_features;
+    const IterState& it = *a.iter;
+    const int children = st[0].root ? 1 : 2;
+    if (warp >= 1 && warp <= static_cast<uint32_t>(2 * n)) {
+        const int j = static_cast<int>(warp - 1) / 2, ch = static_cast<int>(warp - 1) % 2;
+        if (ch < children) {
+            // The best candidate of the child over every feature by `better` (found, then the higher gain, then the
+            // lower feature), from the compact gains and flags; then the winner's full candidate.
+            FeatureCandidate best{};
+            best.found = 0;
+            uint8_t* rowc = csplit + static_cast<size_t>(2 * j + ch) * F;
+            if (sc[j].searched) {
+                const uint8_t* flags = a.cand_flags + static_cast<size_t>(2 * j + ch) * F;
+                const double* gains = a.cand_gain + static_cast<size_t>(2 * j + ch) * F;
+                int found = 0;
+                double bg = -INFINITY;
+                int32_t bf = -1;
+                for (uint32_t f0 = 0; f0 < F; f0 += 128) {
+                    uint8_t fl[4];
+                    double gn[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t f = f0 + 32u * q + lane;
+                        fl[q] = f < F ? __ldcg(flags + f) : 0;
+                        gn[q] = f < F ? __ldcg(gains + f) : 0.0;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t f = f0 + 32u * q + lane;
+                        if (f >= F) continue;
+                        rowc[f] = static_cast<uint8_t>((fl[q] >> 1) & 1);
+                        if (fl[q] & 1) {
+                            const double g = gn[q] != gn[q] ? -INFINITY : gn[q];  // `better` reads NaN as -inf
+                            if (!found || g > bg) {  // features rise with f: on equal gains the earlier stays
+                                found = 1;
+                                bg = g;
+                                bf = static_cast<int32_t>(f);
+                            }
+                        }
+                    }
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                    const int of = __shfl_xor_sync(0xffffffffu, found, o);
+                    const double og = __shfl_xor_sync(0xffffffffu, bg, o);
+                    const int32_t obf = __shfl_xor_sync(0xffffffffu, bf, o);
+                    if (of && (!found || og > bg || (og == bg && obf < bf))) {
+                        found = 1;
+                        bg = og;
+                        bf = obf;
+                    }
+                }
+                if (found)
+                    best = load_candidate(static_cast<const FeatureCandidate*>(a.candidates) +
+                                          static_cast<size_t>(2 * j + ch) * F + bf);
+            } else {
+                for (uint32_t f = lane; f < F; f += 32) rowc[f] = 0;
+            }
+            if (lane == 0) {
+                const bool has = best.found && sc[j].ctx[ch].valid;
+                fs.has_best[j][ch] = has;
+                fs.best[j][ch] = has ? finish(sc[j].ctx[ch], best, a.cfg) : sb2_split_info{};
+            }
+        }
+    }
+    __syncthreads();
+
+    // The commit rule and the next step's splits (warp 0; every CTA takes the same decisions).
+    const int32_t N = st[0].root ? 0 : st[0].new_leaf;  // leaves before the step
+    if (warp == 0) {
+        if (lane < static_cast<uint32_t>(2 * n)) {
+            const int j = static_cast<int>(lane) / 2, c = static_cast<int>(lane) % 2;
+            if (c < children) {
+                fs.child[j][c].has_best = fs.has_best[j][c];
+                if (fs.has_best[j][c]) fs.child[j][c].best = fs.best[j][c];
+            }
+        }
+        // Split j commits when the ones before it did and none of their children comes before its leaf.
+        int committed = 1;
+        if (!st[0].root) {
+            for (int j = 1; j < n; ++j) {
+                const double gj = st[j].info.gain;
+                bool ok = gj > 0.0 && N + j < a.max_leaves;
+                for (int i = 0; i < j && ok; ++i) {
+                    int32_t idx[2];
+                    child_indices(st[i], idx);
+                    for (int c = 0; c < 2; ++c)
+                        if (fs.has_best[i][c] && ranks_before(fs.best[i][c].gain, idx[c], gj, st[j].leaf)) ok = false;
+                }
+                if (!ok) break;
+                ++committed;
+            }
+        }
+        // The leaves after the committed splits, one per lane (kPool* codes), ranked kSplits times.
+        const int32_t leaves_after = st[0].root ? 1 : N + committed;
+        double pg = -INFINITY;
+        int32_t pl = -1;
+        if (lane < static_cast<uint32_t>(kSplits)) {
+            pg = fs.other_gain[lane];
+            pl = fs.other_leaf[lane];
+        } else if (lane < static_cast<uint32_t>(kPoolPending)) {
+            const int i = static_cast<int>(lane - kPoolChild) / 2, c = static_cast<int>(lane - kPoolChild) % 2;
+            if (i < committed && c < children && fs.has_best[i][c]) {
+                int32_t idx[2];
+                if (st[i].root) {
+                    idx[0] = 0;
+                    idx[1] = -1;
+                } else {
+                    child_indices(st[i], idx);
+                }
+                pg = fs.best[i][c].gain;
+                pl = idx[c];
+            }
+        } else if (lane < static_cast<uint32_t>(kPoolPending + kSplits)) {
+            const int j = static_cast<int>(lane) - kPoolPending;
+            if (j >= committed && j < n) {
+                pg = st[j].info.gain;
+                pl = st[j].leaf;
+            }
+        }
+        int next_n = 0;
+        for (int k = 0; k < kSplits; ++k) {
+            double bg = pg;
+            int32_t bl = pl;
+            for (int o = 16; o > 0; o >>= 1)
+                prefer_leaf(bg, bl, __shfl_xor_sync(0xffffffffu, bg, o), __shfl_xor_sync(0xffffffffu, bl, o));
+            // (a step never runs more splits than the grid has CTAs: each takes at least one)
+            if (bl < 0 || !(bg > 0.0) || leaves_after + k >= a.max_leaves || k >= static_cast<int>(gridDim.x)) break;
+            if (pl == bl) {  // the leaf's lane (leaves are distinct)
+                fs.next_from[k] = static_cast<int32_t>(lane);
+                fs.next[k].leaf = bl;  // the rest is filled below
+                pl = -1;
+            }
+            ++next_n;
+        }
+        if (lane == 0) {
+            fs.committed = committed;
+            fs.next_n = next_n;
+        }
+    }
+    __syncthreads();
+    const int committed = fs.committed;
+    const int32_t leaves_after = st[0].root ? 1 : N + committed;
+
+    // Writer CTAs: the tree (a lane per committed split), the committed children's records and rows; every CTA a
+    // share of the spare slots of committed speculative splits, copied into their children's slots.
+    if (writes_part(cta, 0) && warp == 0 && !st[0].root) {
+        if (lane < static_cast<uint32_t>(committed)) {
+            const int i = static_cast<int>(lane);
+            const Step& s = st[i];
+            if (sc[i].left_global <= 0 || sc[i].right_global <= 0) {
+                a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
+                a.iter->error_info = s.leaf;
+            }
+            const DevFeature f = a.d.features[s.info.feature];
+            tree_split_at(a.tree, s.leaf, N + i, s.info, f, sc[i].left_global, sc[i].right_global, it.spec.hess_scale,
+                          a.cfg.min_gain_to_split);
+        }
+        if (lane == 0) {
+            const int32_t before = __ldcg(a.tree.num_leaves);
+            if (before != N) {
+                a.iter->error = 2;
+                a.iter->error_info = before;
+            }
+            *a.tree.num_leaves = N + committed;
+        }
+    }
+    if (writes_part(cta, 1) && warp == 0 && lane < static_cast<uint32_t>(2 * committed)) {
+        const int i = static_cast<int>(lane) / 2, c = static_cast<int>(lane) % 2;
+        if (c < children) {
+            int32_t idx[2];
+            if (st[i].root) {
+                idx[0] = 0;
+                idx[1] = -1;
+            } else {
+                child_indices(st[i], idx);
+            }
+            const DevLeaf r = fs.child[i][c];
+            a.leaves[idx[c]] = r;
+            a.leaf_gain[idx[c]] = r.has_best ? r.best.gain : -INFINITY;
+        }
+    }
+    if (writes_part(cta, 2) && warp < static_cast<uint32_t>(2 * committed)) {
+        const int i = static_cast<int>(warp) / 2, c = static_cast<int>(warp) % 2;
+        if (c < children) {
+            int32_t idx[2];
+            if (st[i].root) {
+                idx[0] = 0;
+                idx[1] = -1;
+            } else {
+                child_indices(st[i], idx);
+            }
+            uint8_t* row = a.splittable + static_cast<size_t>(idx[c]) * F;
+            const uint8_t* src = csplit + static_cast<size_t>(2 * i + c) * F;
+            for (uint32_t f = lane; f < F; f += 32) row[f] = src[f];
+        }
+    }
+    if (committed > 1) {
+        // the spare slot of each committed speculative split's child that keeps the parent's index (child_slot)
+        const size_t slot_len = a.total_bins;  // [g, h] pairs
+        const size_t total = static_cast<size_t>(committed - 1) * slot_len;
+        for (size_t q = static_cast<size_t>(cta) * blockDim.x + threadIdx.x; q < total;
+             q += static_cast<size_t>(gridDim.x) * blockDim.x) {
+            const int i = 1 + static_cast<int>(q / slot_len);
+            if (!sc[i].searched) continue;
+            const size_t e = q % slot_len;
+            const int2* src = reinterpret_cast<const int2*>(a.slots) + (static_cast<size_t>(a.max_leaves) + i - 1) * slot_len;
+            int2* dst = reinterpret_cast<int2*>(a.slots) + static_cast<size_t>(st[i].leaf) * slot_len;
+            __stcg(dst + e, __ldcg(src + e));
+        }
+    }
+
+    // The next step's splits: their records, steps and features (learner.rs:249-286).
+    const int next_n = fs.next_n;
+    if (warp < static_cast<uint32_t>(next_n)) {
+        const int k = static_cast<int>(warp);
+        const int src = fs.next_from[k];
+        const int32_t leaf_index = fs.next[k].leaf;
+        const DevLeaf* rec;
+        const uint8_t* split_ok;
+        if (src < kPoolChild) {
+            rec = &fs.other[src];
+            split_ok = osplit + static_cast<size_t>(src) * F;
+        } else if (src < kPoolPending) {
+            rec = &fs.child[(src - kPoolChild) / 2][(src - kPoolChild) % 2];
+            split_ok = csplit + static_cast<size_t>(src - kPoolChild) * F;
+        } else {
+            rec = &fs.pending[src - kPoolPending];
+            split_ok = psplit + static_cast<size_t>(src - kPoolPending) * F;
+        }
+        uint8_t* ev = eval + static_cast<size_t>(k) * F;
+        for (uint32_t f = lane; f < F; f += 32) ev[f] = static_cast<uint8_t>(mask[f] && split_ok[f]);
+        if (lane == 0) {
+            const DevFeature feat = a.d.features[rec->best.feature];
+            fs.next[k] = next_step(a, *rec, leaf_index, leaves_after + k, feat);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < static_cast<uint32_t>(kSplits)) {
+        const int k = static_cast<int>(threadIdx.x);
+        if (k < next_n) {
+            st[k] = fs.next[k];
+        } else {
+            st[k].active = 0;
+        }
+    }
+    if (threadIdx.x == 0) n = next_n;
+    __syncthreads();
+}
+
+}  // namespace sb2

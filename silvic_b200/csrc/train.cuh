@@ -103,20 +103,23 @@ struct TrainArgs {
     uint8_t* evaluate;          // [num_features]: the current step's evaluated features
     const uint8_t* masks;       // [num_iterations * num_features]: per-iteration feature_mask
     int* staging;               // [2 * total_bins + 2]: the step's new histogram and, after it, the left count
-    int* slots;                 // [max_leaves * 2 * total_bins]: one histogram per leaf
+    int* slots;                 // [(max_leaves + kSplits - 1) * 2 * total_bins]: one histogram per leaf, then the
+                                // tree kernel's spare slots
     HistJob* hist_job;
     IterState* iter;
     DevTree tree;               // the tree being grown
     // partition
     uint32_t* rows[2];
     int32_t* ordered[2];
-    uint32_t* flags;            // one bit per partition position
+    uint32_t* flags;            // one bit per partition position; the tree kernel: kSplits regions of
+                                // num_rows / 32 + 2 words
     uint32_t* tile_left;        // left count per partition tile
-    unsigned int* cursors;      // [2 * max_leaves]: the persistent kernel's placement counters per step
-    // per-(child, feature) scan results and the search kernel's completion counter
+    unsigned int* cursors;      // [2 kSplits (max_leaves + 1)]: the tree kernel's placement counters per split
+    // per-(child, feature) scan results (the tree kernel: per split of a step, 2 kSplits rows of F) and the search
+    // kernel's completion counter
     void* candidates;
-    uint8_t* cand_flags;        // [2 F]: bit 0 the candidate was found, bit 1 its feature stays splittable
-    double* cand_gain;          // [2 F]: its gain (what `better` compares)
+    uint8_t* cand_flags;        // [2 kSplits F]: bit 0 the candidate was found, bit 1 its feature stays splittable
+    double* cand_gain;          // [2 kSplits F]: its gain (what `better` compares)
     unsigned int* done_counter;
 };
 
@@ -154,7 +157,8 @@ constexpr int kGrowPhases = 5;
 constexpr int kStepTrace = kGrowPhases + 3;
 // The layout of its dynamic shared memory (`bytes` in all): the histogram's arrays first, the partition's scan
 // words (2 * 512 + 64) at `scan_offset`, the histogram's staging slots (16 warps x `stage_depth` slots of
-// `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags (5 F bytes) at `flags_offset`. The
+// `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags ((5 kSplits + 1) F bytes) at
+// `flags_offset`. The
 // search's bins (kMaxBins [g, h] pairs per group of kScanWarps warps) reuse the scan words; the histogram's arrays
 // stay zero between steps.
 constexpr uint32_t kMaxStageDepth = 4;  // staging slots per warp at most
@@ -181,14 +185,17 @@ struct GrowExchange {
     uint32_t epoch0;            // the launch's epochs are epoch0 + 1 (the root) .. (they rise across launches)
     uint32_t pad_;
 };
-// An exchange buffer, per source rank s: u32 left-count flags [s] at byte 0, left counts [parity][s] at byte 64,
-// feature flags [s][F] from byte 128; then the built child's bins, int2 [parity][s][F][kMaxBins].
-__host__ __device__ inline size_t exchange_flags_offset() { return 128; }
+// Splits a grid step of the tree kernel runs at most (steps.cuh).
+constexpr int kSplits = 4;
+// An exchange buffer (u32 words unless noted), for split j of a step and source rank s: the left counts' flags [s]
+// at byte 0, the left counts [parity][j][s] at byte 128, the bins' flags [j][F][s] from byte 512; then the built
+// child's bins, int2 [parity][s][j][F][kMaxBins].
+constexpr size_t kXLeftFlags = 0, kXLeftValues = 128, kXFeatureFlags = 512;
 __host__ __device__ inline size_t exchange_bins_offset(uint32_t F) {
-    return 128 + (4ull * kMaxRanks * F + 127) / 128 * 128;
+    return kXFeatureFlags + (4ull * kSplits * kMaxRanks * F + 127) / 128 * 128;
 }
 __host__ __device__ inline size_t exchange_bytes(uint32_t F, uint32_t world) {
-    return exchange_bins_offset(F) + 2ull * world * F * kMaxBins * 8;
+    return exchange_bins_offset(F) + 2ull * world * kSplits * F * kMaxBins * 8;
 }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,

@@ -53,3 +53,20 @@ def random_binned(rows: int, bins_per_feature: list[int], nan_bins: list[bool] |
         label = (signal + 0.3 * noise).astype(np.float32)
     mappers = [numerical_mapper(f"f{f}", nb, nb > 2 and nan_bins[f]) for f, nb in enumerate(bins_per_feature)]
     return BinnedDataset.from_bins(bins, mappers, label)
+
+
+def nested_binned(rows: int, seed: int = 7) -> BinnedDataset:
+    """Three binary features whose conjunction carries most of the label (8 when all three are set) beside six
+    63-bin features with small effects: each split on the conjunction's path leaves a child with a larger gain than
+    any other leaf, so the learner's next leaf is often a child of its last split."""
+    r = np.arange(rows, dtype=np.uint64)
+    widths = [2, 2, 2] + [63] * 6
+    bins = np.empty((rows, len(widths)), dtype=np.uint8)
+    for f, nb in enumerate(widths):
+        bins[:, f] = np.minimum((unit(seed * 1000 + f, r) * nb).astype(np.int64), nb - 1).astype(np.uint8)
+    label = 8.0 * (bins[:, 0] & bins[:, 1] & bins[:, 2])
+    for f in range(3, len(widths)):
+        label = label + 0.3 * (f - 2) * bins[:, f].astype(np.float64) / 62.0
+    label = (label + 0.2 * (unit(seed * 1000 + 999, r) - 0.5)).astype(np.float32)
+    mappers = [numerical_mapper(f"f{f}", nb, False) for f, nb in enumerate(widths)]
+    return BinnedDataset.from_bins(bins, mappers, label)

@@ -10,7 +10,7 @@ import pytest
 from silvic_b200 import _abi
 from silvic_b200.backend import B200Backend, init_score
 import oracle_lib as orc
-from synth import random_binned
+from synth import nested_binned, random_binned
 
 pytestmark = pytest.mark.gpu
 
@@ -246,3 +246,25 @@ def test_training_matches_oracle(device, name, bins, rows, params):
     from silvic_b200.backend import Model
 
     assert model.to_lightgbm_string(data, p) == Model(ref.trees, ref.init_score, []).to_lightgbm_string(data, p)
+
+
+def test_speculative_splits_drop_and_match_oracle(device):
+    """The tree kernel runs the next leaves' splits beside the best one's and drops those a fresh child outranks.
+    On data where the best leaf is often a child of the last split, some grid steps drop splits; the trees stay the
+    oracle's, and the last tree's committed splits are its leaves (the root counts one)."""
+    data = nested_binned(20_000)
+    p = orc.default_params(objective=_abi.REGRESSION, num_leaves=31, num_iterations=3)
+    ref = orc.train([data], p)
+    b = loaded(data, p.objective, p.sigmoid)
+    s0 = init_score(p, data.label)
+    model = b.train(p, s0)
+    steps = b.profile_steps(p, s0)
+    b.close()
+    assert len(model.trees) == len(ref.trees)
+    for k, (t, r) in enumerate(zip(model.trees, ref.trees)):
+        assert orc.trees_equal(t, r) == [], f"tree {k}"
+    fields = B200Backend.STEP_FIELDS
+    splits = int(steps[:, fields.index("splits")].sum())
+    committed = int(steps[:, fields.index("committed")].sum())
+    assert committed == ref.trees[-1].num_leaves
+    assert splits > committed, "no speculative split was dropped"

@@ -407,7 +407,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     fused_range(fs.count, fs.chunks, cta, lo, hi);
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr uint32_t kWarps = kHistThreads / 32;
-    constexpr int kBatch = 4;  // words a warp has in flight
+    constexpr int kBatch = 8;  // words a warp has in flight
     const uint32_t* rows_in = a.rows[fs.src] + fs.begin;
     const int32_t* gh_in = a.ordered[fs.src] + fs.begin;
     uint32_t* rows_out = a.rows[fs.dst] + fs.begin;
@@ -423,6 +423,28 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
         // 0 .. kBatch-1 store their flag words with one instruction.
         const uint8_t* column = a.d.columns + static_cast<uint64_t>(st.info.feature) * a.d.column_stride;
         uint32_t mine = 0;
+        if (fs.identity && fs.begin % 16 == 0) {
+            // The parent's rows are its positions: lane k reads the bins of 16 consecutive rows with one 16-byte
+            // load (a warp covers 16 words), and lanes 2i, 2i + 1 make word i's two halves. The column's stride
+            // (a multiple of 128 bytes) covers the 16 bytes past any row.
+            constexpr uint32_t kWords = 16;
+            for (uint32_t w0 = w_lo + warp * kWords; w0 < w_hi; w0 += kWords * kWarps) {
+                const uint32_t p0 = w0 * 32 + 16 * lane;
+                uint32_t m = 0;
+                if (p0 < hi) {
+                    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(column + fs.begin + p0));
+                    const uint32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (bin_goes_left(st.left_bins, (x[k / 4] >> (8 * (k % 4))) & 0xFFu)) m |= 1u << k;
+                    if (hi - p0 < 16) m &= (1u << (hi - p0)) - 1u;
+                }
+                mine += __reduce_add_sync(0xffffffffu, __popc(m));  // every lane keeps the warp's count
+                const uint32_t upper = __shfl_down_sync(0xffffffffu, m, 1);
+                const uint32_t w = w0 + lane / 2;
+                if ((lane & 1) == 0 && w < w_hi) flags[w] = m | (upper << 16);
+            }
+        } else {
         for (uint32_t w0 = w_lo + warp * kBatch; w0 < w_hi; w0 += kBatch * kWarps) {
             uint32_t row[kBatch];
             bool valid[kBatch];
@@ -441,6 +463,7 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
                 mine += __popc(word);
             }
             if (lane < static_cast<uint32_t>(kBatch) && w0 + lane < w_hi) flags[w0 + lane] = flag_word;
+        }
         }
         if (lane == 0) sums[warp] = mine;
         __syncthreads();

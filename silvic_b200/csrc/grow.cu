@@ -208,13 +208,25 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // Phase A: each split's partition and built child's histogram into its slabs (the root: its histogram),
         // every CTA working on one split.
         if (threadIdx.x == 0) {
-            uint64_t total = 0;
-            for (int j = 0; j < n; ++j) total += st[j].root ? root_job.count : st[j].count;
+            // A split's work: its partition, about one unit per parent row, and its histogram, about three per
+            // built row (the built side's share of the split's rows, as the split's counts estimate it).
+            uint64_t weight[kSplits], total = 0;
+            for (int j = 0; j < n; ++j) {
+                const Step& sj = st[j];
+                const uint64_t count = sj.root ? root_job.count : sj.count;
+                uint64_t w = count;
+                const int64_t l = sj.info.left_count > 0 ? sj.info.left_count : 0;
+                const int64_t r = sj.info.right_count > 0 ? sj.info.right_count : 0;
+                if (!sj.root && sj.may_search && l + r > 0)
+                    w += 3 * count * static_cast<uint64_t>(sj.built_left ? l : r) / static_cast<uint64_t>(l + r);
+                weight[j] = w;
+                total += w;
+            }
             uint32_t base = 0, hist_rows = 0;
             for (int j = 0; j < n; ++j) {
                 const uint32_t count = st[j].root ? root_job.count : st[j].count;
                 const uint32_t budget =
-                    1u + static_cast<uint32_t>(total ? static_cast<uint64_t>(ctas - n) * count / total : 0);
+                    1u + static_cast<uint32_t>(total ? static_cast<uint64_t>(ctas - n) * weight[j] / total : 0);
                 const uint32_t chunks = fused_chunks(count, budget);
                 plan[j] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
                 base += budget;

@@ -169,8 +169,8 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
     __syncthreads();
 }
 
-// The step's finish, in every CTA on the same inputs: each child's best split from the compact candidates (warps
-// 1 .. 2n), the splits committed, the tree, records and slots of the committed splits (writer CTAs), and the next
+// The step's finish, in every CTA on the same inputs: each child's best split from the compact candidates (warp
+// 2 j + c for child c of split j), the splits committed, the tree, records and slots of the committed splits (writer CTAs), and the next
 // step's splits into `st` (and their features into `eval`, kSplits rows of F). `csplit` holds 2 kSplits rows of F
 // (the children's splittable flags), `mask` the iteration's feature mask.
 __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchCtx* sc, uint8_t* eval,
@@ -180,8 +180,9 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
     const uint32_t F = a.num_features;
     const IterState& it = *a.iter;
     const int children = st[0].root ? 1 : 2;
-    if (warp >= 1 && warp <= static_cast<uint32_t>(2 * n)) {
-        const int j = static_cast<int>(warp - 1) / 2, ch = static_cast<int>(warp - 1) % 2;
+    static_assert(2 * kSplits <= kHistThreads / 32, "a warp per child");
+    if (warp < static_cast<uint32_t>(2 * n)) {
+        const int j = static_cast<int>(warp) / 2, ch = static_cast<int>(warp) % 2;
         if (ch < children) {
             // The best candidate of the child over every feature by `better` (found, then the higher gain, then the
             // lower feature), from the compact gains and flags; then the winner's full candidate.

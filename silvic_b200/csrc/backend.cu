@@ -499,14 +499,14 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     const uint64_t n = train->num_rows;
     b->tiles.clear();
     std::vector<int32_t> lane_feature;
-    uint64_t base = 0;
     for (size_t i = 0; i < used.size(); i += kTileLanes) {
         Tile t{};
         t.nfeat = static_cast<uint32_t>(std::min<size_t>(kTileLanes, used.size() - i));
         // Row bytes: 4, 8, 16 or 32, so a row is one aligned vector load.
         t.stride = 4;
         while (t.stride < t.nfeat) t.stride *= 2;
-        t.base = base;
+        t.base = 0;  // placed with its unit below
+        t.pitch = t.stride;
         t.smem_bins = 0;
         for (uint32_t l = 0; l < kTileLanes; ++l) {
             int32_t f = l < t.nfeat ? static_cast<int32_t>(used[i + l]) : -1;
@@ -519,7 +519,6 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         }
         // 64, 128 or 256 bin slots per lane: the histogram kernel's shared addressing is specialised on these.
         t.smem_bins = t.smem_bins <= 64 ? 64 : t.smem_bins <= 128 ? 128 : 256;
-        base += (n * t.stride + 127) / 128 * 128;
         b->tiles.push_back(t);
     }
     // Histogram units: consecutive tiles, up to kMaxUnitTiles within a shared-memory budget (one packed int32 array
@@ -548,6 +547,23 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         max_unit_bytes = std::max(max_unit_bytes, bytes);
         b->units.push_back(u);
         unit_features.push_back(feats);
+    }
+    // The bins in device memory: per unit, each row's bytes of the unit's tiles side by side (the tiles at their
+    // own alignment, the row padded to whole 32-byte sectors), so that a histogram reading a leaf's scattered rows
+    // reads one run of sectors per row and unit instead of one sector in each tile's region.
+    uint64_t base = 0;
+    for (const Unit& u : b->units) {
+        uint32_t off = 0;
+        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
+            Tile& tile = b->tiles[t];
+            const uint32_t align = std::min<uint32_t>(tile.stride, 16);
+            off = (off + align - 1) / align * align;
+            tile.base = base + off;
+            off += tile.stride;
+        }
+        const uint32_t pitch = off <= 16 ? off : (off + 31) / 32 * 32;
+        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) b->tiles[t].pitch = pitch;
+        base += (n * pitch + 127) / 128 * 128;
     }
     // Where each feature's bins sit in the tree kernel's slabs: feature-major inside each unit's region (the unit's
     // tiles in order, each tile's lanes in order, smem_bins slots per lane), so a feature's bins are contiguous.

@@ -27,10 +27,10 @@ constexpr int kWarp = 32;
 // One tile of up to 32 features.
 struct Tile {
     uint64_t base;       // byte offset of the tile's row 0 in the bins buffer
-    uint32_t stride;     // bytes per row (feature count rounded up to 4)
+    uint32_t stride;     // the tile's bytes per row (feature count rounded up to 4)
     uint32_t nfeat;      // features in the tile
     uint32_t smem_bins;  // bins per lane kept in the histogram's shared slots (max num_bins in the tile)
-    uint32_t pad_;
+    uint32_t pitch;      // bytes from one row to the next: the tiles of a histogram unit share their rows
 };
 
 // A feature as the kernels see it.

@@ -249,7 +249,7 @@ __device__ __forceinline__ void stage_row(const LaneTile* lt, uint32_t nt, uint3
         if (t >= static_cast<int>(nt)) break;
         const LaneTile l = lt[t];
         if (l.active == 0) continue;
-        const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.stride;
+        const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.pitch;
         const uint32_t dst = slot + l.stage_off + lane * l.stride;
         switch (l.stride) {
             case 32: {

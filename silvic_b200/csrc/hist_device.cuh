@@ -24,12 +24,12 @@ constexpr int kHistThreads = 512;
 
 struct LaneTile {
     const uint8_t* base;  // the tile's row 0
-    uint32_t stride;      // 4, 8, 16 or 32 bytes
+    uint32_t stride;      // 4, 8, 16 or 32 bytes of a row
     uint32_t bins;        // 64, 128 or 256: bin slots per feature lane
     uint32_t addr;        // shared address of the tile's packed array (aligned to 4 * stride bytes)
     uint32_t active;      // bit f: feature lane f is wanted (0: the tile is skipped)
     uint32_t stage_off;   // where a batch's rows of this tile start in a staging slot (the tree kernel's histogram)
-    uint32_t pad_;
+    uint32_t pitch;       // bytes from one row to the next (Tile::pitch)
 };
 
 // Rows whose packed gradients one packed histogram can sum exactly: every bin's |sum g| <= 32767 and sum h <=
@@ -88,7 +88,7 @@ __device__ __forceinline__ void shared_add(uint32_t addr, uint32_t v) {
 // (evict first): a histogram reads its rows' bins once, and the leaf histograms, partition buffers and metadata the
 // next phases read should stay in L2 instead.
 __device__ __forceinline__ void load_row(const LaneTile& t, uint32_t row, uint32_t (&w)[8]) {
-    const uint8_t* p = t.base + static_cast<uint64_t>(row) * t.stride;
+    const uint8_t* p = t.base + static_cast<uint64_t>(row) * t.pitch;
     if (t.stride == 32) {
         const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
         const uint4 b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
@@ -172,7 +172,7 @@ inline __device__ void histogram_prepare_unit(const HistArgs& a, uint32_t u, con
             lt.addr = hist_shared_base(sh) + 4 * slot;
             lt.active = 0;
             lt.stage_off = 0;
-            lt.pad_ = 0;
+            lt.pitch = tile.pitch;
             c->tiles[warp] = lt;
         }
     }
@@ -420,6 +420,7 @@ inline __device__ void histogram_direct_cta(const HistArgs& a, const HistJob& jo
         LaneTile lt;
         lt.base = a.d.bins + tile.base;
         lt.stride = tile.stride;
+        lt.pitch = tile.pitch;
         uint32_t wd[8];
         load_row(lt, row, wd);  // row 0 for positions past the job: in bounds, and adds nothing
         // unpack (quantize.rs:140-143)

@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kRowThreads) api_add_tree_kernel(DevData d, Ro
         while (node >= 0) {
             const TileNode& nd = nodes[node];
             const Tile tile = d.tiles[nd.tile];
-            const uint32_t bin = d.bins[tile.base + row * tile.stride + nd.lane];
+            const uint32_t bin = d.bins[tile.base + row * tile.pitch + nd.lane];
             node = ((nd.left_bins[bin >> 5] >> (bin & 31)) & 1u) ? nd.left : nd.right;
         }
         r.scores[row] = __fadd_rn(r.scores[row], leaf_values[~node]);
@@ -542,7 +542,7 @@ __global__ void tiles_kernel(DevData d, uint8_t* bins) {
         if (r0 + row >= d.num_rows) continue;
         uint32_t v = 0;
         for (int q = 0; q < 4; ++q) v |= static_cast<uint32_t>(sh[(4 * wb + q) * kPitch + row]) << (8 * q);
-        *reinterpret_cast<uint32_t*>(bins + tile.base + (r0 + row) * tile.stride + 4 * wb) = v;
+        *reinterpret_cast<uint32_t*>(bins + tile.base + (r0 + row) * tile.pitch + 4 * wb) = v;
     }
 }
 

@@ -54,7 +54,7 @@ inline __device__ void partition_flags_cta(const TrainArgs& a, const Step& st, u
                 left[j] = static_cast<double>(uniform01(st.bag_seed, 2u, st.bag_round, st.row_offset + row[j])) <
                           st.bag_fraction;
             else
-                left[j] = bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row[j]) * tile.stride));
+                left[j] = bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row[j]) * tile.pitch));
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {

@@ -321,7 +321,7 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
 int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_score, double* seconds_by_op,
                       size_t num_ops, sb2_model** out);
 /* The same run; `rows` (max_steps rows of 8 doubles) receives one row per grid step of the last tree's kernel (row
- * 0 the root; a grid step runs up to four splits side by side): seconds in the partitions with the built children's
+ * 0 the root; a grid step runs up to eight splits side by side): seconds in the partitions with the built children's
  * histograms, search contexts, slab reductions with the searches, finish, grid barriers (device clock of the tree
  * kernel's first CTA), then the rows of the step's histograms, the splits it ran and the splits it committed.
  * *num_steps gets the rows written. Single GPU only (SB2_EUNSUPPORTED otherwise). */

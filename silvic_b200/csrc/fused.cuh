@@ -799,13 +799,21 @@ __device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, con
 // feature_bins_cta: the built child's bins reduced from the split's slabs (`chunks` of them from slab `first`,
 // packed or not) and, with ranks, summed over every rank's (exchange_bins), into `bufs` (2 kMaxBins int2 of shared
 // memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction); *evaluated says whether the
-// feature is searched at all (`evaluate`: the split's features). False when a rank did not answer (error recorded).
-__device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, uint32_t j, uint32_t f, uint32_t first,
-                                 uint32_t chunks, bool packed, const uint8_t* evaluate, int2* bufs, int4* scratch,
-                                 const GrowExchange& x, uint32_t epoch, bool* evaluated) {
+// feature is searched at all (`evaluate`: the split's features). For a split (not the root), the threads of the
+// sibling's scan group (feature_scan_cta) also load their bin of the parent's histogram into `parent`, so that the
+// load overlaps the reduction. False when a rank did not answer (error recorded).
+__device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const Step& st, uint32_t j, uint32_t f,
+                                 uint32_t first, uint32_t chunks, bool packed, const uint8_t* evaluate, int2* bufs,
+                                 int4* scratch, const GrowExchange& x, uint32_t epoch, bool* evaluated, int2& parent) {
     const DevFeature feat = a.d.features[f];
     *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
     if (!*evaluated) return true;
+    {
+        const uint32_t t = threadIdx.x % kScanThreads;
+        if (!st.root && threadIdx.x / kScanThreads == 1 && t < feat.num_bins)
+            parent = __ldcg(reinterpret_cast<const int2*>(a.slots) +
+                            static_cast<size_t>(st.leaf) * a.total_bins + feat.hist_offset + t);
+    }
     if (scratch != nullptr) {
         if (packed)
             reduce_feature_bins_quads<true>(h, feat, first, chunks, scratch, bufs);
@@ -831,7 +839,7 @@ __device__ __forceinline__ size_t child_slot(const TrainArgs& a, const Step& st,
 // and writes both children's), each with scan_feature_group, as search_item_group does for one item. The
 // candidates go to rows 2 j (built) and 2 j + 1 (sibling) of F.
 __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t j, uint32_t f,
-                                 bool evaluated, int2* bufs, ScanShared* scan_sh) {
+                                 bool evaluated, const int2& parent, int2* bufs, ScanShared* scan_sh) {
     const uint32_t F = a.num_features;
     const uint32_t group = threadIdx.x / kScanThreads, t = threadIdx.x % kScanThreads;
     FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates) + static_cast<size_t>(2 * j) * F;
@@ -858,9 +866,8 @@ __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const Searc
     if (st.root) {
         if (group == 0 && mine) __stcg(reinterpret_cast<int2*>(a.slots + off) + t, built[t]);
     } else if (group == 1 && mine) {
-        const int2 p = __ldcg(reinterpret_cast<const int2*>(a.slots + static_cast<size_t>(st.leaf) * slot_len + off) + t);
         const int2 bt = built[t];
-        const int2 o = make_int2(p.x - bt.x, p.y - bt.y);
+        const int2 o = make_int2(parent.x - bt.x, parent.y - bt.y);
         other[t] = o;
         __stcg(reinterpret_cast<int2*>(a.slots + child_slot(a, st, s, j, 0) * slot_len + off) + t, bt);
         __stcg(reinterpret_cast<int2*>(a.slots + child_slot(a, st, s, j, 1) * slot_len + off) + t, o);

@@ -209,24 +209,24 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // every CTA working on one split.
         if (threadIdx.x == 0) {
             // A split's work: its partition, about one unit per parent row, and its histogram, about three per
-            // built row (the built side's share of the split's rows, as the split's counts estimate it).
-            uint64_t weight[kSplits], total = 0;
+            // built row (the built side's share of the split's rows, as the split's counts estimate it). In floats:
+            // every CTA computes the same shares from the same steps.
+            float weight[kSplits], total = 0.0f;
             for (int j = 0; j < n; ++j) {
                 const Step& sj = st[j];
-                const uint64_t count = sj.root ? root_job.count : sj.count;
-                uint64_t w = count;
-                const int64_t l = sj.info.left_count > 0 ? sj.info.left_count : 0;
-                const int64_t r = sj.info.right_count > 0 ? sj.info.right_count : 0;
-                if (!sj.root && sj.may_search && l + r > 0)
-                    w += 3 * count * static_cast<uint64_t>(sj.built_left ? l : r) / static_cast<uint64_t>(l + r);
+                const float count = static_cast<float>(sj.root ? root_job.count : sj.count);
+                float w = count;
+                const float l = sj.info.left_count > 0 ? static_cast<float>(sj.info.left_count) : 0.0f;
+                const float r = sj.info.right_count > 0 ? static_cast<float>(sj.info.right_count) : 0.0f;
+                if (!sj.root && sj.may_search && l + r > 0.0f) w += 3.0f * count * (sj.built_left ? l : r) / (l + r);
                 weight[j] = w;
                 total += w;
             }
             uint32_t base = 0, hist_rows = 0;
             for (int j = 0; j < n; ++j) {
                 const uint32_t count = st[j].root ? root_job.count : st[j].count;
-                const uint32_t budget =
-                    1u + static_cast<uint32_t>(total ? static_cast<uint64_t>(ctas - n) * weight[j] / total : 0);
+                const float share = total > 0.0f ? static_cast<float>(ctas - n) * (weight[j] / total) : 0.0f;
+                const uint32_t budget = 1u + min(static_cast<uint32_t>(share), ctas - n);
                 const uint32_t chunks = fused_chunks(count, budget);
                 plan[j] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
                 base += budget;
@@ -280,12 +280,13 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // The CTA's first item's bins (and their exchange) come before the contexts, so that the left counts'
         // exchange has arrived by the time the contexts need it.
         bool have = false, evaluated = false;
+        int2 parent = make_int2(0, 0);  // this thread's bin of the split's parent histogram (feature_bins_cta)
         if (cta < items) {
             const uint32_t j = cta / F, f = cta % F;
             if (st[j].root ? root_job.active != 0 : st[j].may_search != 0) {
                 const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
-                if (!feature_bins_cta(a, g.h, j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate, bufs,
-                                      scratch, g.x, epoch, &evaluated))
+                if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate,
+                                      bufs, scratch, g.x, epoch, &evaluated, parent))
                     return;
                 have = true;
             }
@@ -308,11 +309,11 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             if (!sc[j].searched) continue;
             if (i != cta || !have) {
                 const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
-                if (!feature_bins_cta(a, g.h, j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate, bufs,
-                                      scratch, g.x, epoch, &evaluated))
+                if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate,
+                                      bufs, scratch, g.x, epoch, &evaluated, parent))
                     return;
             }
-            feature_scan_cta(a, st[j], sc[j], j, f, evaluated, bufs, scan_shared);
+            feature_scan_cta(a, st[j], sc[j], j, f, evaluated, parent, bufs, scan_shared);
         }
         clock_mark(g, clock, 2);
         barrier_arrive(g, target);

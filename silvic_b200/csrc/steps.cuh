@@ -25,8 +25,6 @@ namespace sb2 {
 // The finish's scratch (shared memory of every CTA).
 struct StepsFinish {
     DevLeaf child[kSplits][2];           // the children of every split (child 0 the built one)
-    sb2_split_info best[kSplits][2];
-    int32_t has_best[kSplits][2];
     double other_gain[kSplits];          // the best leaves that no split of the step touches
     int32_t other_leaf[kSplits];
     DevLeaf other[kSplits];              // their records
@@ -35,6 +33,11 @@ struct StepsFinish {
     int32_t next_n;                      // splits of the next step
     Step next[kSplits];
     int32_t next_from[kSplits];          // where each next split's leaf comes from (kPool* codes)
+    // The features of the best splits above, loaded ahead: the step's splits (also the pending leaves'), the
+    // children's, the other leaves'.
+    DevFeature split_feat[kSplits];
+    DevFeature child_feat[kSplits][2];
+    DevFeature other_feat[kSplits];
 };
 
 // The leaves a finish ranks, one per lane of a warp: the untouched best leaves (code k), the committed splits'
@@ -64,6 +67,7 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
     if (warp == 0 && lane < static_cast<uint32_t>(n)) {
         const int j = static_cast<int>(lane);
         const Step& s = st[j];
+        if (!s.root) fs.split_feat[j] = a.d.features[s.info.feature];
         if (s.root) {
             DevLeaf l = load_cg(a.leaves);  // begin, count, which, depth: set before the launch
             l.units_grad = sc[j].ctx[0].units_grad;
@@ -155,7 +159,10 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
         for (int k = 0; k < kSplits; ++k) {
             const int32_t leaf = taken[k];
             if (leaf < 0) continue;
-            if (lane == 0) fs.other[k] = load_cg(a.leaves + leaf);
+            if (lane == 0) {
+                fs.other[k] = load_cg(a.leaves + leaf);
+                fs.other_feat[k] = a.d.features[fs.other[k].best.feature];
+            }
             const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
             for (uint32_t f = lane; f < F; f += 32) osplit[static_cast<size_t>(k) * F + f] = __ldcg(row + f);
         }
@@ -229,16 +236,18 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                         bf = obf;
                     }
                 }
-                if (found)
+                if (found && lane == 0) {
                     best = load_candidate(static_cast<const FeatureCandidate*>(a.candidates) +
                                           static_cast<size_t>(2 * j + ch) * F + bf);
+                    fs.child_feat[j][ch] = a.d.features[bf];
+                }
             } else {
                 for (uint32_t f = lane; f < F; f += 32) rowc[f] = 0;
             }
             if (lane == 0) {
                 const bool has = best.found && sc[j].ctx[ch].valid;
-                fs.has_best[j][ch] = has;
-                fs.best[j][ch] = has ? finish(sc[j].ctx[ch], best, a.cfg) : sb2_split_info{};
+                fs.child[j][ch].has_best = has;
+                if (has) fs.child[j][ch].best = finish(sc[j].ctx[ch], best, a.cfg);
             }
         }
     }
@@ -247,13 +256,6 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
     // The commit rule and the next step's splits (warp 0; every CTA takes the same decisions).
     const int32_t N = st[0].root ? 0 : st[0].new_leaf;  // leaves before the step
     if (warp == 0) {
-        if (lane < static_cast<uint32_t>(2 * n)) {
-            const int j = static_cast<int>(lane) / 2, c = static_cast<int>(lane) % 2;
-            if (c < children) {
-                fs.child[j][c].has_best = fs.has_best[j][c];
-                if (fs.has_best[j][c]) fs.child[j][c].best = fs.best[j][c];
-            }
-        }
         // Split j commits when the ones before it did and none of their children comes before its leaf.
         int committed = 1;
         if (!st[0].root) {
@@ -264,7 +266,8 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                     int32_t idx[2];
                     child_indices(st[i], idx);
                     for (int c = 0; c < 2; ++c)
-                        if (fs.has_best[i][c] && ranks_before(fs.best[i][c].gain, idx[c], gj, st[j].leaf)) ok = false;
+                        if (fs.child[i][c].has_best && ranks_before(fs.child[i][c].best.gain, idx[c], gj, st[j].leaf))
+                            ok = false;
                 }
                 if (!ok) break;
                 ++committed;
@@ -279,7 +282,7 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
             pl = fs.other_leaf[lane];
         } else if (lane < static_cast<uint32_t>(kPoolPending)) {
             const int i = static_cast<int>(lane - kPoolChild) / 2, c = static_cast<int>(lane - kPoolChild) % 2;
-            if (i < committed && c < children && fs.has_best[i][c]) {
+            if (i < committed && c < children && fs.child[i][c].has_best) {
                 int32_t idx[2];
                 if (st[i].root) {
                     idx[0] = 0;
@@ -287,7 +290,7 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                 } else {
                     child_indices(st[i], idx);
                 }
-                pg = fs.best[i][c].gain;
+                pg = fs.child[i][c].best.gain;
                 pl = idx[c];
             }
         } else if (lane < static_cast<uint32_t>(kPoolPending + kSplits)) {
@@ -331,9 +334,8 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                 a.iter->error = 1;  // split sends every row to one side (learner.rs:295-300)
                 a.iter->error_info = s.leaf;
             }
-            const DevFeature f = a.d.features[s.info.feature];
-            tree_split_at(a.tree, s.leaf, N + i, s.info, f, sc[i].left_global, sc[i].right_global, it.spec.hess_scale,
-                          a.cfg.min_gain_to_split);
+            tree_split_at(a.tree, s.leaf, N + i, s.info, fs.split_feat[i], sc[i].left_global, sc[i].right_global,
+                          it.spec.hess_scale, a.cfg.min_gain_to_split);
         }
         if (lane == 0) {
             const int32_t before = __ldcg(a.tree.num_leaves);
@@ -396,23 +398,24 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
         const int src = fs.next_from[k];
         const int32_t leaf_index = fs.next[k].leaf;
         const DevLeaf* rec;
+        const DevFeature* feat;
         const uint8_t* split_ok;
         if (src < kPoolChild) {
             rec = &fs.other[src];
+            feat = &fs.other_feat[src];
             split_ok = osplit + static_cast<size_t>(src) * F;
         } else if (src < kPoolPending) {
             rec = &fs.child[(src - kPoolChild) / 2][(src - kPoolChild) % 2];
+            feat = &fs.child_feat[(src - kPoolChild) / 2][(src - kPoolChild) % 2];
             split_ok = csplit + static_cast<size_t>(src - kPoolChild) * F;
         } else {
             rec = &fs.pending[src - kPoolPending];
+            feat = &fs.split_feat[src - kPoolPending];  // a pending leaf's best split is the step's split
             split_ok = psplit + static_cast<size_t>(src - kPoolPending) * F;
         }
         uint8_t* ev = eval + static_cast<size_t>(k) * F;
         for (uint32_t f = lane; f < F; f += 32) ev[f] = static_cast<uint8_t>(mask[f] && split_ok[f]);
-        if (lane == 0) {
-            const DevFeature feat = a.d.features[rec->best.feature];
-            fs.next[k] = next_step(a, *rec, leaf_index, leaves_after + k, feat);
-        }
+        if (lane == 0) fs.next[k] = next_step(a, *rec, leaf_index, leaves_after + k, *feat);
     }
     __syncthreads();
     if (threadIdx.x < static_cast<uint32_t>(kSplits)) {

@@ -186,7 +186,7 @@ struct GrowExchange {
     uint32_t pad_;
 };
 // Splits a grid step of the tree kernel runs at most (steps.cuh).
-constexpr int kSplits = 4;
+constexpr int kSplits = 8;
 // An exchange buffer (u32 words unless noted), for split j of a step and source rank s: the left counts' flags [s]
 // at byte 0, the left counts [parity][j][s] at byte 128, the bins' flags [j][F][s] from byte 512; then the built
 // child's bins, int2 [parity][s][j][F][kMaxBins].

@@ -67,7 +67,8 @@ __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) { asm volatile("st
 
 // Whether the slabs of a phase over `count` positions hold packed sums: every CTA's range fits one packed round.
 __host__ __device__ __forceinline__ bool fused_packed(uint32_t count, uint32_t chunks, uint32_t round_rows) {
-    return 32 * ceil_div(ceil_div(count, 32), chunks) <= round_rows;
+    const uint32_t words = (count >> 5) + ((count & 31u) != 0);  // 32-bit: a divide per split per step
+    return (words + chunks - 1) / chunks <= round_rows / 32;
 }
 
 // One 32-row batch of a warp into the unit's packed shared arrays (`lt`: its tiles with the wanted bits): lane k's

@@ -207,32 +207,41 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         if (n == 0) break;
         // Phase A: each split's partition and built child's histogram into its slabs (the root: its histogram),
         // every CTA working on one split.
-        if (threadIdx.x == 0) {
-            // A split's work: its partition, about one unit per parent row, and its histogram, about three per
-            // built row (the built side's share of the split's rows, as the split's counts estimate it). In floats:
-            // every CTA computes the same shares from the same steps.
-            float weight[kSplits], total = 0.0f;
-            for (int j = 0; j < n; ++j) {
-                const Step& sj = st[j];
-                const float count = static_cast<float>(sj.root ? root_job.count : sj.count);
-                float w = count;
+        if (warp == 0) {
+            // Lane j plans split j. Its work: its partition, about one unit per parent row, and its histogram, about
+            // three per built row (the built side's share of the split's rows, as the split's counts estimate it).
+            // In floats, summed in a fixed order: every CTA computes the same shares from the same steps.
+            const uint32_t lane = threadIdx.x & 31;
+            const bool on = lane < static_cast<uint32_t>(n);
+            uint32_t count = 0;
+            float w = 0.0f;
+            bool hist = false;
+            if (on) {
+                const Step& sj = st[lane];
+                count = sj.root ? root_job.count : sj.count;
+                hist = sj.root ? root_job.active != 0 : sj.may_search != 0;
+                const float c = static_cast<float>(count);
                 const float l = sj.info.left_count > 0 ? static_cast<float>(sj.info.left_count) : 0.0f;
                 const float r = sj.info.right_count > 0 ? static_cast<float>(sj.info.right_count) : 0.0f;
-                if (!sj.root && sj.may_search && l + r > 0.0f) w += 3.0f * count * (sj.built_left ? l : r) / (l + r);
-                weight[j] = w;
-                total += w;
+                w = !sj.root && sj.may_search && l + r > 0.0f ? c + 3.0f * c * (sj.built_left ? l : r) / (l + r) : c;
             }
-            uint32_t base = 0, hist_rows = 0;
-            for (int j = 0; j < n; ++j) {
-                const uint32_t count = st[j].root ? root_job.count : st[j].count;
-                const float share = total > 0.0f ? static_cast<float>(ctas - n) * (weight[j] / total) : 0.0f;
-                const uint32_t budget = 1u + min(static_cast<uint32_t>(share), ctas - n);
+            float total = w;
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xffffffffu, total, o);
+            total = __shfl_sync(0xffffffffu, total, 0);
+            const float share = on && total > 0.0f ? static_cast<float>(ctas - n) * (w / total) : 0.0f;
+            const uint32_t budget = on ? 1u + min(static_cast<uint32_t>(share), ctas - n) : 0u;
+            uint32_t base = budget;  // inclusive prefix, then exclusive
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t up = __shfl_up_sync(0xffffffffu, base, o);
+                if (lane >= static_cast<uint32_t>(o)) base += up;
+            }
+            base -= budget;
+            if (on) {
                 const uint32_t chunks = fused_chunks(count, budget);
-                plan[j] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
-                base += budget;
-                if (st[j].root ? root_job.active != 0 : st[j].may_search != 0) hist_rows += count;
+                plan[lane] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
             }
-            clock_describe(g, clock, hist_rows, static_cast<uint32_t>(n));
+            const uint32_t hist_rows = __reduce_add_sync(0xffffffffu, hist ? count : 0u);
+            if (lane == 0) clock_describe(g, clock, hist_rows, static_cast<uint32_t>(n));
         }
         __syncthreads();
         int mine = -1;

@@ -29,6 +29,7 @@ struct StepsFinish {
     int32_t other_leaf[kSplits];
     DevLeaf other[kSplits];              // their records
     DevLeaf pending[kSplits];            // the records of the step's own leaves (split j >= 1), kept if dropped
+    int32_t pending_leaf[kSplits];       // their indices (-1: split 0)
     int32_t committed;                   // splits committed by this step
     int32_t next_n;                      // splits of the next step
     Step next[kSplits];
@@ -45,15 +46,37 @@ struct StepsFinish {
 constexpr int kPoolChild = kSplits, kPoolPending = 3 * kSplits;
 static_assert(4 * kSplits <= 32, "the finish ranks one leaf per lane");
 
-// The leaf indices of split `st`'s children: [built, other] (the left child keeps the parent's index).
-__device__ __forceinline__ void child_indices(const Step& st, int32_t (&idx)[2]) {
-    idx[0] = st.built_left ? st.leaf : st.new_leaf;
-    idx[1] = st.built_left ? st.new_leaf : st.leaf;
+// The leaf index of split `st`'s child c (0: the built one; the left child keeps the parent's index; the root's
+// only child is leaf 0).
+__device__ __forceinline__ int32_t child_index(const Step& st, int c) {
+    if (st.root) return 0;
+    return (c == 0) == (st.built_left != 0) ? st.leaf : st.new_leaf;
 }
 
 // Whether (og, ol) comes first in the learner's order over (g, l): the higher gain, then the lower index.
 __device__ __forceinline__ bool ranks_before(double og, int32_t ol, double g, int32_t l) {
     return og > g || (og == g && ol < l);
+}
+
+// Warp: the splittable rows of `rows` leaves (leaf[k], k < rows; negative: none) into `dst` (shared, rows of F),
+// eight bytes a lane in flight.
+__device__ __forceinline__ void load_split_rows(const TrainArgs& a, const int32_t* leaf, int rows, uint8_t* dst) {
+    constexpr int kLoads = 8;
+    const uint32_t lane = threadIdx.x & 31, F = a.num_features;
+    const uint32_t total = static_cast<uint32_t>(rows) * F;
+    for (uint32_t e0 = lane; e0 < total; e0 += 32 * kLoads) {
+        uint8_t v[kLoads];
+#pragma unroll
+        for (int q = 0; q < kLoads; ++q) {
+            const uint32_t e = e0 + 32 * q, k = e / F;
+            v[q] = e < total && leaf[k] >= 0 ? __ldcg(a.splittable + static_cast<size_t>(leaf[k]) * F + (e - k * F)) : 0;
+        }
+#pragma unroll
+        for (int q = 0; q < kLoads; ++q) {
+            const uint32_t e = e0 + 32 * q;
+            if (e < total) dst[e] = v[q];
+        }
+    }
 }
 
 // Before the step's last grid barrier completes (no candidate needed): every split's children records (warp 0);
@@ -62,7 +85,6 @@ __device__ __forceinline__ bool ranks_before(double og, int32_t ol, double g, in
 __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, const SearchCtx* sc,
                                      const uint32_t* left, uint8_t* osplit, uint8_t* psplit, StepsFinish& fs) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t F = a.num_features;
     const IterState& it = *a.iter;
     if (warp == 0 && lane < static_cast<uint32_t>(n)) {
         const int j = static_cast<int>(lane);
@@ -133,14 +155,12 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
                     }
             }
         }
-        int32_t taken[kSplits];
 #pragma unroll
         for (int k = 0; k < kSplits; ++k) {
             double bg = tg[0];
             int32_t bl = tl[0];
             for (int o = 16; o > 0; o >>= 1)
                 prefer_leaf(bg, bl, __shfl_xor_sync(0xffffffffu, bg, o), __shfl_xor_sync(0xffffffffu, bl, o));
-            taken[k] = bl;
             if (bl >= 0 && tl[0] == bl) {  // the owner pops its head
 #pragma unroll
                 for (int q = 0; q + 1 < kSplits; ++q) {
@@ -155,23 +175,19 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
                 fs.other_leaf[k] = bl;
             }
         }
-        // their records and splittable rows, in case they are split next
-        for (int k = 0; k < kSplits; ++k) {
-            const int32_t leaf = taken[k];
-            if (leaf < 0) continue;
-            if (lane == 0) {
-                fs.other[k] = load_cg(a.leaves + leaf);
-                fs.other_feat[k] = a.d.features[fs.other[k].best.feature];
-            }
-            const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
-            for (uint32_t f = lane; f < F; f += 32) osplit[static_cast<size_t>(k) * F + f] = __ldcg(row + f);
+        __syncwarp();
+        // their records (lane k: leaf k's) and splittable rows, in case they are split next
+        if (lane < static_cast<uint32_t>(kSplits) && fs.other_leaf[lane] >= 0) {
+            const DevLeaf r = load_cg(a.leaves + fs.other_leaf[lane]);
+            fs.other[lane] = r;
+            fs.other_feat[lane] = a.d.features[r.best.feature];
         }
+        load_split_rows(a, fs.other_leaf, kSplits, osplit);
     } else if (warp == 4) {
-        for (int j = 1; j < n; ++j) {
-            if (lane == 0) fs.pending[j] = load_cg(a.leaves + st[j].leaf);
-            const uint8_t* row = a.splittable + static_cast<size_t>(st[j].leaf) * F;
-            for (uint32_t f = lane; f < F; f += 32) psplit[static_cast<size_t>(j) * F + f] = __ldcg(row + f);
-        }
+        if (lane >= 1 && lane < static_cast<uint32_t>(n)) fs.pending[lane] = load_cg(a.leaves + st[lane].leaf);
+        if (lane < static_cast<uint32_t>(kSplits)) fs.pending_leaf[lane] = lane >= 1 && lane < static_cast<uint32_t>(n) ? st[lane].leaf : -1;
+        __syncwarp();
+        load_split_rows(a, fs.pending_leaf, n, psplit);
     }
     __syncthreads();
 }
@@ -256,20 +272,23 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
     // The commit rule and the next step's splits (warp 0; every CTA takes the same decisions).
     const int32_t N = st[0].root ? 0 : st[0].new_leaf;  // leaves before the step
     if (warp == 0) {
-        // Split j commits when the ones before it did and none of their children comes before its leaf.
+        // Split j commits when the ones before it did and none of their children comes before its leaf: lane
+        // 2 i + c tests child c of split i against every later split.
         int committed = 1;
         if (!st[0].root) {
-            for (int j = 1; j < n; ++j) {
-                const double gj = st[j].info.gain;
-                bool ok = gj > 0.0 && N + j < a.max_leaves;
-                for (int i = 0; i < j && ok; ++i) {
-                    int32_t idx[2];
-                    child_indices(st[i], idx);
-                    for (int c = 0; c < 2; ++c)
-                        if (fs.child[i][c].has_best && ranks_before(fs.child[i][c].best.gain, idx[c], gj, st[j].leaf))
-                            ok = false;
+            uint32_t beaten = 0;  // bit j: a child of an earlier split comes before split j's leaf
+            if (lane < static_cast<uint32_t>(2 * n)) {
+                const int i = static_cast<int>(lane) / 2, c = static_cast<int>(lane) % 2;
+                if (fs.child[i][c].has_best) {
+                    const double cg = fs.child[i][c].best.gain;
+                    const int32_t ci = child_index(st[i], c);
+                    for (int j = i + 1; j < n; ++j)
+                        if (ranks_before(cg, ci, st[j].info.gain, st[j].leaf)) beaten |= 1u << j;
                 }
-                if (!ok) break;
+            }
+            beaten = __reduce_or_sync(0xffffffffu, beaten);
+            for (int j = 1; j < n; ++j) {
+                if (((beaten >> j) & 1u) || !(st[j].info.gain > 0.0) || N + j >= a.max_leaves) break;
                 ++committed;
             }
         }
@@ -283,15 +302,8 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
         } else if (lane < static_cast<uint32_t>(kPoolPending)) {
             const int i = static_cast<int>(lane - kPoolChild) / 2, c = static_cast<int>(lane - kPoolChild) % 2;
             if (i < committed && c < children && fs.child[i][c].has_best) {
-                int32_t idx[2];
-                if (st[i].root) {
-                    idx[0] = 0;
-                    idx[1] = -1;
-                } else {
-                    child_indices(st[i], idx);
-                }
                 pg = fs.child[i][c].best.gain;
-                pl = idx[c];
+                pl = child_index(st[i], c);
             }
         } else if (lane < static_cast<uint32_t>(kPoolPending + kSplits)) {
             const int j = static_cast<int>(lane) - kPoolPending;
@@ -300,20 +312,22 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                 pl = st[j].leaf;
             }
         }
-        int next_n = 0;
-        for (int k = 0; k < kSplits; ++k) {
-            double bg = pg;
-            int32_t bl = pl;
-            for (int o = 16; o > 0; o >>= 1)
-                prefer_leaf(bg, bl, __shfl_xor_sync(0xffffffffu, bg, o), __shfl_xor_sync(0xffffffffu, bl, o));
-            // (a step never runs more splits than the grid has CTAs: each takes at least one)
-            if (bl < 0 || !(bg > 0.0) || leaves_after + k >= a.max_leaves || k >= static_cast<int>(gridDim.x)) break;
-            if (pl == bl) {  // the leaf's lane (leaves are distinct)
-                fs.next_from[k] = static_cast<int32_t>(lane);
-                fs.next[k].leaf = bl;  // the rest is filled below
-                pl = -1;
-            }
-            ++next_n;
+        // Each leaf's rank: the leaves that come before it (a strict order: gains are numbers or -inf, indices
+        // distinct). The next step takes the first ranks while their gains are positive and leaves may be added
+        // (and never more splits than the grid has CTAs: each takes at least one).
+        int rank = 0;
+        for (int q = 0; q < 32; ++q) {
+            const double og = __shfl_sync(0xffffffffu, pg, q);
+            const int32_t ol = __shfl_sync(0xffffffffu, pl, q);
+            rank += ol >= 0 && ranks_before(og, ol, pg, pl);
+        }
+        const int positive = __popc(__ballot_sync(0xffffffffu, pl >= 0 && pg > 0.0));
+        const int room = a.max_leaves - leaves_after;
+        int next_n = min(min(positive, kSplits), min(room, static_cast<int>(gridDim.x)));
+        next_n = max(next_n, 0);
+        if (pl >= 0 && rank < next_n) {
+            fs.next_from[rank] = static_cast<int32_t>(lane);
+            fs.next[rank].leaf = pl;  // the rest is filled below
         }
         if (lane == 0) {
             fs.committed = committed;
@@ -349,29 +363,16 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
     if (writes_part(cta, 1) && warp == 0 && lane < static_cast<uint32_t>(2 * committed)) {
         const int i = static_cast<int>(lane) / 2, c = static_cast<int>(lane) % 2;
         if (c < children) {
-            int32_t idx[2];
-            if (st[i].root) {
-                idx[0] = 0;
-                idx[1] = -1;
-            } else {
-                child_indices(st[i], idx);
-            }
+            const int32_t leaf = child_index(st[i], c);
             const DevLeaf r = fs.child[i][c];
-            a.leaves[idx[c]] = r;
-            a.leaf_gain[idx[c]] = r.has_best ? r.best.gain : -INFINITY;
+            a.leaves[leaf] = r;
+            a.leaf_gain[leaf] = r.has_best ? r.best.gain : -INFINITY;
         }
     }
     if (writes_part(cta, 2) && warp < static_cast<uint32_t>(2 * committed)) {
         const int i = static_cast<int>(warp) / 2, c = static_cast<int>(warp) % 2;
         if (c < children) {
-            int32_t idx[2];
-            if (st[i].root) {
-                idx[0] = 0;
-                idx[1] = -1;
-            } else {
-                child_indices(st[i], idx);
-            }
-            uint8_t* row = a.splittable + static_cast<size_t>(idx[c]) * F;
+            uint8_t* row = a.splittable + static_cast<size_t>(child_index(st[i], c)) * F;
             const uint8_t* src = csplit + static_cast<size_t>(2 * i + c) * F;
             for (uint32_t f = lane; f < F; f += 32) row[f] = src[f];
         }

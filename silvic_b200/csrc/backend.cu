@@ -548,22 +548,29 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         b->units.push_back(u);
         unit_features.push_back(feats);
     }
-    // The bins in device memory: per unit, each row's bytes of the unit's tiles side by side (the tiles at their
-    // own alignment, the row padded to whole 32-byte sectors), so that a histogram reading a leaf's scattered rows
-    // reads one run of sectors per row and unit instead of one sector in each tile's region.
+    // The bins in device memory: per unit, each row's bytes of the unit's full tiles (32 features: one 32-byte
+    // sector a row) side by side, so that a histogram reading a leaf's scattered rows reads one run of sectors per
+    // row and unit instead of one sector in each tile's region; a partial tile (the last one) keeps its own region,
+    // where its narrow rows pack whole sectors.
     uint64_t base = 0;
     for (const Unit& u : b->units) {
-        uint32_t off = 0;
+        uint32_t full = 0;
+        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) full += b->tiles[t].stride == 32;
+        uint32_t k = 0;
         for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
             Tile& tile = b->tiles[t];
-            const uint32_t align = std::min<uint32_t>(tile.stride, 16);
-            off = (off + align - 1) / align * align;
-            tile.base = base + off;
-            off += tile.stride;
+            if (tile.stride != 32) continue;
+            tile.base = base + 32 * k++;
+            tile.pitch = 32 * full;
         }
-        const uint32_t pitch = off <= 16 ? off : (off + 31) / 32 * 32;
-        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) b->tiles[t].pitch = pitch;
-        base += (n * pitch + 127) / 128 * 128;
+        base += (n * 32 * full + 127) / 128 * 128;
+        for (uint32_t t = u.first_tile; t < u.first_tile + u.num_tiles; ++t) {
+            Tile& tile = b->tiles[t];
+            if (tile.stride == 32) continue;
+            tile.base = base;
+            tile.pitch = tile.stride;
+            base += (n * tile.stride + 127) / 128 * 128;
+        }
     }
     // Where each feature's bins sit in the tree kernel's slabs: feature-major inside each unit's region (the unit's
     // tiles in order, each tile's lanes in order, smem_bins slots per lane), so a feature's bins are contiguous.

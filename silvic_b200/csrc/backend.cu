@@ -1183,7 +1183,7 @@ namespace {
 
 struct TrainBuffers {
     DeviceBuffer leaves, leaf_gain, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records,
-        record_bufs, cursors;
+        record_bufs, cursors, leaf_of_row;
 };
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
@@ -1436,6 +1436,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     SB2_CUDA(b, tb.slots.alloc(sizeof(int) * (static_cast<size_t>(L) + kSplits - 1) * 2 * b->total_bins));
     SB2_CUDA(b, tb.leaf_sums.alloc(sizeof(int64_t) * 2 * L));
     SB2_CUDA(b, tb.leaf_values.alloc(sizeof(float) * L));
+    SB2_CUDA(b, tb.leaf_of_row.alloc(sizeof(uint16_t) * std::max<uint64_t>(b->num_rows, 1)));
     SB2_CUDA(b, tb.records.alloc(sizeof(TreeRecordHeader) * std::max(iters, 1)));
     DevTree work{};
     DevTree& rec = tr.rec;
@@ -1500,6 +1501,7 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     ia.k.total_rows = global_rows;
     ia.leaf_sums = tb.leaf_sums.as<int64_t>();
     ia.leaf_values_f32 = tb.leaf_values.as<float>();
+    ia.leaf_of_row = tb.leaf_of_row.as<uint16_t>();
     ia.records = tb.records.as<TreeRecordHeader>();
     ia.record_tree = rec;
     return SB2_OK;

@@ -225,30 +225,72 @@ __global__ void __launch_bounds__(kRowThreads) iteration_start_kernel(IterArgs a
     }
 }
 
-// The leaves of the current tree sorted by first position, for position -> leaf lookups.
+// The leaves of the current tree (those with rows on this rank) sorted by first position, for position -> leaf
+// lookups: first position, leaf index, partition buffer.
+constexpr int kIndexLeaves = 1024;
 struct LeafIndex {
-    uint32_t begin[1024];
-    uint16_t leaf[1024];
+    uint32_t begin[kIndexLeaves];
+    uint16_t leaf[kIndexLeaves];
+    uint8_t which[kIndexLeaves];
     int n;
 };
 
+// Whole CTA of kRowThreads threads: every leaf's record is read once (kIndexLeaves / kRowThreads leaves a thread,
+// all loads in flight together), then ranked by its first position against the others in shared memory (the
+// first positions of non-empty leaves are distinct).
 __device__ void build_leaf_index(const TrainArgs& t, LeafIndex& li) {
-    const int32_t L = *t.tree.num_leaves;
-    if (threadIdx.x == 0) li.n = 0;
-    __syncthreads();
-    for (int32_t l = threadIdx.x; l < L; l += blockDim.x) {
-        const DevLeaf lf = t.leaves[l];
-        if (lf.count == 0) continue;
-        int rank = 0;
-        for (int32_t m = 0; m < L; ++m) {
-            const DevLeaf o = t.leaves[m];
-            if (o.count != 0 && o.begin < lf.begin) ++rank;
+    constexpr int kPer = kIndexLeaves / kRowThreads;
+    const int32_t L = min(*t.tree.num_leaves, kIndexLeaves);
+    uint32_t b[kPer], w[kPer];
+    bool live[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        const int32_t l = static_cast<int32_t>(threadIdx.x) + q * kRowThreads;
+        live[q] = false;
+        b[q] = 0xFFFFFFFFu;
+        w[q] = 0;
+        if (l < L) {
+            const DevLeaf& lf = t.leaves[l];
+            const uint32_t count = lf.count;
+            live[q] = count != 0;
+            b[q] = live[q] ? lf.begin : 0xFFFFFFFFu;
+            w[q] = lf.which & 1u;
         }
-        li.begin[rank] = lf.begin;
-        li.leaf[rank] = static_cast<uint16_t>(l);
-        atomicAdd(&li.n, 1);
+    }
+    if (threadIdx.x == 0) li.n = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        const int32_t l = static_cast<int32_t>(threadIdx.x) + q * kRowThreads;
+        if (l < L) li.begin[l] = b[q];  // scratch: every leaf's first position (empty: never before another)
     }
     __syncthreads();
+    int rank[kPer];
+    int live_here = 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        rank[q] = 0;
+        if (!live[q]) continue;
+        ++live_here;
+        for (int32_t m = 0; m < L; ++m) rank[q] += li.begin[m] < b[q];
+    }
+    if (live_here) atomicAdd(&li.n, live_here);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        if (!live[q]) continue;
+        li.begin[rank[q]] = b[q];
+        li.leaf[rank[q]] = static_cast<uint16_t>(threadIdx.x + q * kRowThreads);
+        li.which[rank[q]] = static_cast<uint8_t>(w[q]);
+    }
+    __syncthreads();
+}
+
+constexpr int kRowUnroll = 4;  // positions a thread has in flight in the row passes over a tree's leaves
+
+// The index entry of position p: a binary search, or, from the entry `k` of an earlier position, a walk forward.
+__device__ __forceinline__ int leaf_after(const LeafIndex& li, int k, uint32_t p) {
+    while (k + 1 < li.n && li.begin[k + 1] <= p) ++k;
+    return k;
 }
 
 __device__ __forceinline__ int leaf_of(const LeafIndex& li, uint32_t p) {
@@ -263,44 +305,65 @@ __device__ __forceinline__ int leaf_of(const LeafIndex& li, uint32_t p) {
     return lo;
 }
 
-__global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
+// Each row's leaf in the current tree (IterArgs::leaf_of_row), from the partition: the CTA's range of positions,
+// kRowUnroll a thread at a time (their row ids in flight together), each thread walking the leaf index forward.
+__global__ void __launch_bounds__(kRowThreads) leaf_map_kernel(IterArgs a) {
     __shared__ LeafIndex li;
-    __shared__ long long sums[2 * 1024];
     if (a.t.iter->stopped) return;
     build_leaf_index(a.t, li);
-    const int32_t L = *a.t.tree.num_leaves;
+    const uint64_t n = a.r.num_rows;
+    const uint64_t lo = n * blockIdx.x / gridDim.x, hi = n * (blockIdx.x + 1) / gridDim.x;
+    int walk = lo < hi ? leaf_of(li, static_cast<uint32_t>(lo)) : 0;
+    for (uint64_t p0 = lo + threadIdx.x; p0 < hi; p0 += kRowUnroll * kRowThreads) {
+        int kq[kRowUnroll];
+#pragma unroll
+        for (int q = 0; q < kRowUnroll; ++q) {
+            const uint64_t p = p0 + static_cast<uint64_t>(q) * kRowThreads;
+            kq[q] = -1;
+            if (p < hi) {
+                walk = leaf_after(li, walk, static_cast<uint32_t>(p));
+                kq[q] = walk;
+            }
+        }
+        uint32_t rq[kRowUnroll];
+#pragma unroll
+        for (int q = 0; q < kRowUnroll; ++q)
+            rq[q] = kq[q] >= 0 ? a.t.rows[li.which[kq[q]]][p0 + static_cast<uint64_t>(q) * kRowThreads] : 0u;
+#pragma unroll
+        for (int q = 0; q < kRowUnroll; ++q)
+            if (kq[q] >= 0) a.leaf_of_row[rq[q]] = li.leaf[kq[q]];
+    }
+}
+
+// Backend::leaf_sums for every leaf of the tree (backend/cpu.rs:886-905: the fixed-point sums of the leaf's rows'
+// gradients and hessians): the rows in order, four a thread at a time, each row's pair added to its leaf's sums in
+// shared memory (64-bit atomics; integer sums, so the order is free), then the CTA's sums added to the output.
+__global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
+    __shared__ long long sums[2 * kIndexLeaves];
+    if (a.t.iter->stopped) return;
+    const int32_t L = min(*a.t.tree.num_leaves, kIndexLeaves);
     for (int i = threadIdx.x; i < 2 * L; i += kRowThreads) sums[i] = 0;
     __syncthreads();
     const double mg = __longlong_as_double(static_cast<long long>(a.t.iter->max_abs_grad_bits));
     const double mh = __longlong_as_double(static_cast<long long>(a.t.iter->max_hess_bits));
     const float gs = fixed_point_scale(mg), hs = fixed_point_scale(mh);
     const uint64_t n = a.r.num_rows;
-    const uint64_t lo = n * blockIdx.x / gridDim.x, hi = n * (blockIdx.x + 1) / gridDim.x;
-    const int lane = threadIdx.x & 31;
-    for (uint64_t base = lo + (threadIdx.x & ~31u); base < hi; base += kRowThreads) {
-        const uint64_t p = base + lane;
-        int k = -1;
-        long long g = 0, h = 0;
-        if (p < hi) {
-            k = leaf_of(li, static_cast<uint32_t>(p));
-            const DevLeaf& lf = a.t.leaves[li.leaf[k]];
-            const uint32_t row = a.t.rows[lf.which & 1][p];
-            g = to_fixed(a.r.grad[row], gs);
-            h = to_fixed(a.r.hess[row], hs);
-        }
-        const int k0 = __shfl_sync(0xffffffffu, k, 0);
-        if (__all_sync(0xffffffffu, k == k0 || k < 0) && k0 >= 0) {
-            for (int o = 16; o > 0; o >>= 1) {
-                g += __shfl_xor_sync(0xffffffffu, g, o);
-                h += __shfl_xor_sync(0xffffffffu, h, o);
-            }
-            if (lane == 0) {
-                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k0]]), static_cast<unsigned long long>(g));
-                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k0] + 1]), static_cast<unsigned long long>(h));
-            }
-        } else if (k >= 0) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k]]), static_cast<unsigned long long>(g));
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * li.leaf[k] + 1]), static_cast<unsigned long long>(h));
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kRowThreads;
+    auto add = [&](uint32_t leaf, float g, float h) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * leaf]), static_cast<unsigned long long>(to_fixed(g, gs)));
+        atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * leaf + 1]), static_cast<unsigned long long>(to_fixed(h, hs)));
+    };
+    for (uint64_t r0 = (static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x) * 4; r0 < n; r0 += 4 * stride) {
+        if (r0 + 4 <= n) {
+            const ushort4 k = *reinterpret_cast<const ushort4*>(a.leaf_of_row + r0);
+            const float4 g = *reinterpret_cast<const float4*>(a.r.grad + r0);
+            const float4 h = *reinterpret_cast<const float4*>(a.r.hess + r0);
+            add(k.x, g.x, h.x);
+            add(k.y, g.y, h.y);
+            add(k.z, g.z, h.z);
+            add(k.w, g.w, h.w);
+        } else {
+            for (uint64_t row = r0; row < n; ++row) add(a.leaf_of_row[row], a.r.grad[row], a.r.hess[row]);
         }
     }
     __syncthreads();
@@ -396,20 +459,30 @@ __global__ void __launch_bounds__(kRowThreads) finalize_kernel(IterArgs a) {
 }
 
 __global__ void __launch_bounds__(kRowThreads) add_tree_partition_kernel(IterArgs a) {
-    __shared__ LeafIndex li;
+    __shared__ float values[kIndexLeaves];
     IterState* it = a.t.iter;
     // finalize has recorded the tree; a stopped run adds nothing. The iteration advances here, after every kernel
     // of this iteration has read it.
     const bool stopped = it->stopped;
     if (!stopped) {
-        build_leaf_index(a.t, li);
+        // Every row's leaf, as leaf_sums left it: the rows in order, four a thread at a time.
+        const int32_t L = min(*a.t.tree.num_leaves, kIndexLeaves);
+        for (int32_t l = threadIdx.x; l < L; l += kRowThreads) values[l] = a.leaf_values_f32[l];
+        __syncthreads();
         const uint64_t n = a.r.num_rows;
-        for (uint64_t p = static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x; p < n;
-             p += static_cast<uint64_t>(gridDim.x) * kRowThreads) {
-            const int k = leaf_of(li, static_cast<uint32_t>(p));
-            const int l = li.leaf[k];
-            const uint32_t row = a.t.rows[a.t.leaves[l].which & 1][p];
-            a.r.scores[row] = __fadd_rn(a.r.scores[row], a.leaf_values_f32[l]);
+        const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kRowThreads;
+        for (uint64_t r0 = (static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x) * 4; r0 < n; r0 += 4 * stride) {
+            if (r0 + 4 <= n) {
+                const ushort4 k = *reinterpret_cast<const ushort4*>(a.leaf_of_row + r0);
+                float4 s = *reinterpret_cast<const float4*>(a.r.scores + r0);
+                s.x = __fadd_rn(s.x, values[k.x]);
+                s.y = __fadd_rn(s.y, values[k.y]);
+                s.z = __fadd_rn(s.z, values[k.z]);
+                s.w = __fadd_rn(s.w, values[k.w]);
+                *reinterpret_cast<float4*>(a.r.scores + r0) = s;
+            } else {
+                for (uint64_t row = r0; row < n; ++row) a.r.scores[row] = __fadd_rn(a.r.scores[row], values[a.leaf_of_row[row]]);
+            }
         }
     }
 }
@@ -593,7 +666,10 @@ void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) { gradients_k
 void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s) {
     iteration_start_kernel<<<grid, kRowThreads, 0, s>>>(a);
 }
-void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s) { leaf_sums_kernel<<<grid, kRowThreads, 0, s>>>(a); }
+void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s) {
+    leaf_map_kernel<<<grid, kRowThreads, 0, s>>>(a);
+    leaf_sums_kernel<<<std::max(grid / 4, 1), kRowThreads, 0, s>>>(a);  // fewer CTAs: fewer output atomics
+}
 void launch_finalize(const IterArgs& a, cudaStream_t s) { finalize_kernel<<<1, kRowThreads, 0, s>>>(a); }
 void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s) {
     add_tree_partition_kernel<<<grid, kRowThreads, 0, s>>>(a);

@@ -46,6 +46,7 @@ struct IterArgs {
     IterConsts k;
     int64_t* leaf_sums;          // [2 * max_leaves], reduced over ranks between leaf_sums and finalize
     float* leaf_values_f32;      // [max_leaves]: what add_tree adds
+    uint16_t* leaf_of_row;       // [num_rows]: each row's leaf in the current tree (leaf_sums writes, add_tree reads)
     TreeRecordHeader* records;   // [num_iterations]
     DevTree record_tree;         // arrays [num_iterations * max_leaves]
 };

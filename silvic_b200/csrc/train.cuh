@@ -188,9 +188,11 @@ struct GrowExchange {
 // Splits a grid step of the tree kernel runs at most (steps.cuh).
 constexpr int kSplits = 8;
 // An exchange buffer (u32 words unless noted), for split j of a step and source rank s: the left counts' flags [s]
-// at byte 0, the left counts [parity][j][s] at byte 128, the bins' flags [j][F][s] from byte 512; then the built
-// child's bins, int2 [parity][s][j][F][kMaxBins].
-constexpr size_t kXLeftFlags = 0, kXLeftValues = 128, kXFeatureFlags = 512;
+// at byte 0, the left counts [parity][j][s] at byte 128, the bins' flags [j][F][s] after them (128-byte aligned);
+// then the built child's bins, int2 [parity][s][j][F][kMaxBins].
+constexpr size_t kXLeftFlags = 0, kXLeftValues = 128;
+constexpr size_t kXFeatureFlags = (kXLeftValues + 4 * 2 * kSplits * kMaxRanks + 127) / 128 * 128;
+static_assert(kXLeftFlags + 4 * kMaxRanks <= kXLeftValues, "the left counts' flags fit before the counts");
 __host__ __device__ inline size_t exchange_bins_offset(uint32_t F) {
     return kXFeatureFlags + (4ull * kSplits * kMaxRanks * F + 127) / 128 * 128;
 }

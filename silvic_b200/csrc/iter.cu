@@ -339,10 +339,11 @@ __global__ void __launch_bounds__(kRowThreads) leaf_map_kernel(IterArgs a) {
 // gradients and hessians): the rows in order, four a thread at a time, each row's pair added to its leaf's sums in
 // shared memory (64-bit atomics; integer sums, so the order is free), then the CTA's sums added to the output.
 __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
-    __shared__ long long sums[2 * kIndexLeaves];
+    // g and h sums in separate arrays: a warp's 64-bit atomics on random leaves spread over every bank
+    __shared__ long long sum_g[kIndexLeaves], sum_h[kIndexLeaves];
     if (a.t.iter->stopped) return;
     const int32_t L = min(*a.t.tree.num_leaves, kIndexLeaves);
-    for (int i = threadIdx.x; i < 2 * L; i += kRowThreads) sums[i] = 0;
+    for (int i = threadIdx.x; i < L; i += kRowThreads) sum_g[i] = sum_h[i] = 0;
     __syncthreads();
     const double mg = __longlong_as_double(static_cast<long long>(a.t.iter->max_abs_grad_bits));
     const double mh = __longlong_as_double(static_cast<long long>(a.t.iter->max_hess_bits));
@@ -350,8 +351,8 @@ __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
     const uint64_t n = a.r.num_rows;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kRowThreads;
     auto add = [&](uint32_t leaf, float g, float h) {
-        atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * leaf]), static_cast<unsigned long long>(to_fixed(g, gs)));
-        atomicAdd(reinterpret_cast<unsigned long long*>(&sums[2 * leaf + 1]), static_cast<unsigned long long>(to_fixed(h, hs)));
+        atomicAdd(reinterpret_cast<unsigned long long*>(&sum_g[leaf]), static_cast<unsigned long long>(to_fixed(g, gs)));
+        atomicAdd(reinterpret_cast<unsigned long long*>(&sum_h[leaf]), static_cast<unsigned long long>(to_fixed(h, hs)));
     };
     for (uint64_t r0 = (static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x) * 4; r0 < n; r0 += 4 * stride) {
         if (r0 + 4 <= n) {
@@ -367,9 +368,10 @@ __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
         }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 2 * L; i += kRowThreads)
-        if (sums[i] != 0)
-            atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[i]), static_cast<unsigned long long>(sums[i]));
+    for (int i = threadIdx.x; i < L; i += kRowThreads) {
+        if (sum_g[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i]), static_cast<unsigned long long>(sum_g[i]));
+        if (sum_h[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i + 1]), static_cast<unsigned long long>(sum_h[i]));
+    }
 }
 
 // split::leaf_output (split.rs:190-192)

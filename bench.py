@@ -466,8 +466,8 @@ def run_b200(args, rank: int, world: int):
                 "d2h_bytes_per_step": d2h // args.steps},
         # Our kernels per iteration: gradients, iteration start (quantize), the tree (one persistent launch, or
         # histogram + reduction + search for the root and partition flags + scatter + histogram + reduction + search
-        # per split with NCCL ranks), leaf sums, finalize, score update.
-        "gpu_launches": args.steps * (6 if launches_persistent else 3 + 3 + 5 * (PARAMS["num_leaves"] - 1) + 3),
+        # per split with NCCL ranks), leaf map + leaf sums, finalize, score update.
+        "gpu_launches": args.steps * (7 if launches_persistent else 3 + 3 + 5 * (PARAMS["num_leaves"] - 1) + 4),
     }
     if world == 1 and not args.no_cpu_baseline:
         rate, secs, cores = oracle_rate(data, 2, oracle_params())

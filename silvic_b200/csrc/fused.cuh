@@ -796,16 +796,89 @@ __device__ __forceinline__ void reduce_feature_bins_quads(const HistArgs& h, con
     __syncthreads();
 }
 
+// A search item's slab bins copied ahead into shared memory while the CTA scans its previous item: chunk c's
+// quads (int4: four packed bins, or two [g, h] pairs) at `pbuf` + 16 (c * quads + k). Whole CTA; false (nothing
+// issued) when they do not fit in `cap` bytes.
+__device__ __forceinline__ uint32_t slab_quads(uint32_t num_bins, bool packed) {
+    return packed ? (num_bins + 3) / 4 : (num_bins + 1) / 2;
+}
+
+__device__ __forceinline__ bool prefetch_feature_bins(const HistArgs& h, const DevFeature& feat, uint32_t first,
+                                                      uint32_t chunks, bool packed, uint32_t pbuf, uint32_t cap) {
+    const uint32_t per = slab_quads(feat.num_bins, packed);
+    if (static_cast<uint64_t>(chunks) * per * 16 > cap) return false;
+    // the bins past num_bins that a quad covers lie inside the feature's smem_bins slots of the slab
+    const int* base = h.slabs + static_cast<size_t>(first) * h.slab_ints + (packed ? feat.slab_off : 2 * feat.slab_off);
+    const uint64_t pol = evict_first_policy();
+    for (uint32_t e = threadIdx.x; e < chunks * per; e += kHistThreads) {
+        const uint32_t c = e / per, k = e - c * per;
+        cp_async16(pbuf + 16 * e, base + static_cast<size_t>(c) * h.slab_ints + 4 * k, pol);
+    }
+    cp_async_commit();
+    return true;
+}
+
+// reduce_feature_bins_quads over the prefetched copy (`pbuf`, as prefetch_feature_bins laid it out).
+template <bool kPacked>
+__device__ __forceinline__ void reduce_feature_bins_staged(const DevFeature& feat, uint32_t chunks, uint32_t pbuf,
+                                                           int4* scratch, int2* out) {
+    constexpr uint32_t kGroups = kHistThreads / 64;
+    const uint32_t q = threadIdx.x & 63, g = threadIdx.x >> 6;
+    const uint32_t per = slab_quads(feat.num_bins, kPacked);
+    int4 sg = make_int4(0, 0, 0, 0), sh = sg;
+    if (4 * q < feat.num_bins) {
+        for (uint32_t c = g; c < chunks; c += kGroups) {
+            const uint32_t at = pbuf + 16 * (c * per + (kPacked ? q : 2 * q));
+            const uint4 v = lds128(at);
+            if (kPacked) {
+                const uint32_t x[4] = {v.x, v.y, v.z, v.w};
+                int gx[4], hx[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    gx[j] = static_cast<int16_t>(x[j] & 0xFFFFu);  // quantize.rs:140-143
+                    hx[j] = static_cast<int>((x[j] - static_cast<uint32_t>(gx[j])) >> 16);
+                }
+                sg = make_int4(sg.x + gx[0], sg.y + gx[1], sg.z + gx[2], sg.w + gx[3]);
+                sh = make_int4(sh.x + hx[0], sh.y + hx[1], sh.z + hx[2], sh.w + hx[3]);
+            } else {
+                const uint4 w = lds128(at + 16);
+                sg = make_int4(sg.x + static_cast<int>(v.x), sg.y + static_cast<int>(v.z), sg.z + static_cast<int>(w.x),
+                               sg.w + static_cast<int>(w.z));
+                sh = make_int4(sh.x + static_cast<int>(v.y), sh.y + static_cast<int>(v.w), sh.z + static_cast<int>(w.y),
+                               sh.w + static_cast<int>(w.w));
+            }
+        }
+    }
+    scratch[2 * (g * 64 + q)] = sg;
+    scratch[2 * (g * 64 + q) + 1] = sh;
+    __syncthreads();
+    const uint32_t b = threadIdx.x;
+    if (b < feat.num_bins) {
+        const int* sc = reinterpret_cast<const int*>(scratch);
+        int tg = 0, th = 0;
+#pragma unroll
+        for (uint32_t k = 0; k < kGroups; ++k) {
+            tg += sc[8 * (k * 64 + b / 4) + (b & 3)];
+            th += sc[8 * (k * 64 + b / 4) + 4 + (b & 3)];
+        }
+        out[b] = make_int2(tg, th);
+    }
+    __syncthreads();
+}
+
 // The search of split j of a step for feature `f` in one CTA, both children at once, in two parts.
 // feature_bins_cta: the built child's bins reduced from the split's slabs (`chunks` of them from slab `first`,
 // packed or not) and, with ranks, summed over every rank's (exchange_bins), into `bufs` (2 kMaxBins int2 of shared
 // memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction); *evaluated says whether the
 // feature is searched at all (`evaluate`: the split's features). For a split (not the root), the threads of the
 // sibling's scan group (feature_scan_cta) also load their bin of the parent's histogram into `parent`, so that the
-// load overlaps the reduction. False when a rank did not answer (error recorded).
+// load overlaps the reduction. With `pbuf` (not 0) the slab bins were prefetched there (prefetch_feature_bins):
+// the reduction waits for the copies and reads them from shared memory. False when a rank did not answer (error
+// recorded).
 __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const Step& st, uint32_t j, uint32_t f,
                                  uint32_t first, uint32_t chunks, bool packed, const uint8_t* evaluate, int2* bufs,
-                                 int4* scratch, const GrowExchange& x, uint32_t epoch, bool* evaluated, int2& parent) {
+                                 int4* scratch, const GrowExchange& x, uint32_t epoch, bool* evaluated, int2& parent,
+                                 uint32_t pbuf = 0) {
     const DevFeature feat = a.d.features[f];
     *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
     if (!*evaluated) return true;
@@ -815,7 +888,14 @@ __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const St
             parent = __ldcg(reinterpret_cast<const int2*>(a.slots) +
                             static_cast<size_t>(st.leaf) * a.total_bins + feat.hist_offset + t);
     }
-    if (scratch != nullptr) {
+    if (pbuf != 0) {
+        cp_async_wait(0);
+        __syncthreads();  // every thread's copies have landed
+        if (packed)
+            reduce_feature_bins_staged<true>(feat, chunks, pbuf, scratch, bufs);
+        else
+            reduce_feature_bins_staged<false>(feat, chunks, pbuf, scratch, bufs);
+    } else if (scratch != nullptr) {
         if (packed)
             reduce_feature_bins_quads<true>(h, feat, first, chunks, scratch, bufs);
         else

@@ -313,14 +313,30 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         }
         __syncthreads();
         clock_mark(g, clock, 1);
+        // While a CTA scans an item, the slab bins of its next searched item are copied into the staging slots past
+        // the reduction's scratch (when they fit).
+        const uint32_t pbuf = scratch != nullptr ? static_cast<uint32_t>(__cvta_generic_to_shared(scratch)) + 16384u : 0u;
+        const uint32_t pcap = scratch != nullptr ? g.stage_depth * (kGrowThreads / 32) * g.slot_bytes - 16384u : 0u;
+        uint32_t prefetched = 0xFFFFFFFFu;  // the item whose bins are in pbuf
         for (uint32_t i = cta; i < items; i += ctas) {
             const uint32_t j = i / F, f = i % F;
             if (!sc[j].searched) continue;
             if (i != cta || !have) {
                 const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
                 if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate,
-                                      bufs, scratch, g.x, epoch, &evaluated, parent))
+                                      bufs, scratch, g.x, epoch, &evaluated, parent, prefetched == i ? pbuf : 0u))
                     return;
+            }
+            prefetched = 0xFFFFFFFFu;
+            uint32_t next = i + ctas;
+            while (next < items && !sc[next / F].searched) next += ctas;
+            if (pbuf != 0 && next < items) {
+                const uint32_t jn = next / F, fn = next % F;
+                const DevFeature feat = a.d.features[fn];
+                const uint8_t* ev = st[jn].root ? mask : eval + static_cast<size_t>(jn) * F;
+                if (ev[fn] && feat.tile >= 0 && feat.num_bins != 0 &&
+                    prefetch_feature_bins(g.h, feat, plan[jn].base, plan[jn].chunks, plan[jn].packed != 0, pbuf, pcap))
+                    prefetched = next;
             }
             feature_scan_cta(a, st[j], sc[j], j, f, evaluated, parent, bufs, scan_shared);
         }

@@ -328,6 +328,20 @@ int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_scor
 int sb2_profile_steps(sb2_backend* b, const sb2_params* params, double init_score, double* rows, size_t max_steps,
                       size_t* num_steps);
 
+/* ---- dataset construction -------------------------------------------------------------------------------- */
+
+/* data::binning::bin_rows (crates/silvic-core/src/data/binning.rs:71-135) on the handle's device: the values of a
+ * rows × cols matrix (`row_major`: values[row * cols + feature], else values[feature * rows + row]), f32
+ * (`value_bytes` 4) or f64 (8), in host or device memory, are binned with each numerical feature's upper bounds
+ * (BinMapper::value_to_bin, data/bin_mapper.rs:343-360: the number of bounds below the value; NaN to the NaN bin,
+ * or to 0.0's bin) into the groups' rows. The matrix column of feature f is f. `group_data[g]` is a host buffer of
+ * rows × groups[g].row_stride bytes that receives group g's rows (padding columns 0); `features` and `groups` are
+ * as in sb2_dataset (each group's features, columns and row stride; `data` unused). A categorical feature in a
+ * group returns SB2_EUNSUPPORTED; a group whose bounds exceed 200 KiB, SB2_EUNSUPPORTED. Returns when done. */
+int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
+                  const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
+                  uint8_t* const* group_data);
+
 /* ---- multi-GPU --------------------------------------------------------------------------------------------- */
 
 /* An NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */

@@ -1330,6 +1330,60 @@ int orc_add_tree(const sb2_dataset* data, const sb2_device_node* nodes, size_t n
                  size_t num_leaves, float* scores) {
     return add_tree(*data, nodes, num_nodes, leaf_values, num_leaves, scores) ? SB2_OK : SB2_EDEVICE;
 }
+// BinMapper::value_to_bin for a numerical mapper (data/bin_mapper.rs:343-360): the number of upper bounds below
+// the value (`partition_point(bound < value)`); NaN goes to the NaN bin, or to 0.0's bin without one.
+uint32_t orc_value_to_bin(const double* ub, uint32_t n, int nan_bin, double value) {
+    if (value != value) {
+        if (nan_bin) return n;
+        value = 0.0;
+    }
+    uint32_t k = 0;
+    while (k < n && ub[k] < value) ++k;
+    return k;
+}
+
+namespace {
+
+// data/binning.rs:51-61: the branch-free search over the bounds padded to 256 with +inf.
+uint8_t padded_numerical_bin(const double (&bounds)[256], uint8_t nan, double value) {
+    if (value != value) return nan;
+    size_t pos = 0;
+    for (size_t step : {128, 64, 32, 16, 8, 4, 2, 1}) pos += step * static_cast<size_t>(bounds[(pos + step - 1) & 255] < value);
+    return static_cast<uint8_t>(pos);
+}
+
+}  // namespace
+
+// data/binning.rs:71-135 (bin_rows / bin_column / fill), one row chunk after another.
+int orc_bin_rows(const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
+                 const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
+                 uint8_t* const* group_data) {
+    if (value_bytes != 4 && value_bytes != 8) return SB2_EDATA;
+    for (uint32_t g = 0; g < num_groups; ++g) {
+        const sb2_group& grp = groups[g];
+        std::memset(group_data[g], 0, rows * grp.row_stride);
+        for (uint32_t k = 0; k < grp.num_features; ++k) {
+            const uint32_t f = grp.features[k];
+            if (f >= num_features || f >= cols) return SB2_EDATA;
+            const sb2_feature& m = features[f];
+            if (m.kind != SB2_NUMERICAL) return SB2_EUNSUPPORTED;
+            if (m.num_upper_bounds == 0 || m.num_upper_bounds > 256) return SB2_EDATA;
+            double bounds[256];
+            for (size_t i = 0; i < 256; ++i)
+                bounds[i] = i < m.num_upper_bounds ? m.upper_bounds[i] : std::numeric_limits<double>::infinity();
+            const uint8_t nan = static_cast<uint8_t>(orc_value_to_bin(m.upper_bounds, m.num_upper_bounds, m.nan_bin,
+                                                                      std::numeric_limits<double>::quiet_NaN()));
+            for (uint64_t r = 0; r < rows; ++r) {
+                const uint64_t at = row_major ? r * cols + f : static_cast<uint64_t>(f) * rows + r;
+                const double v = value_bytes == 8 ? static_cast<const double*>(values)[at]
+                                                  : static_cast<double>(static_cast<const float*>(values)[at]);
+                group_data[g][r * grp.row_stride + m.column] = padded_numerical_bin(bounds, nan, v);
+            }
+        }
+    }
+    return SB2_OK;
+}
+
 uint32_t orc_reset_partition(const sb2_bag_spec* bag, uint64_t num_rows, uint64_t row_offset, uint32_t* out) {
     uint32_t k = 0;
     for (uint64_t r = 0; r < num_rows; ++r)

@@ -49,6 +49,14 @@ int orc_add_tree(const sb2_dataset* data, const sb2_device_node* nodes, size_t n
                  size_t num_leaves, float* scores);
 uint32_t orc_reset_partition(const sb2_bag_spec* bag, uint64_t num_rows, uint64_t row_offset, uint32_t* out);
 
+/* data/binning.rs: bin_rows over a dense f32 (value_bytes 4) or f64 (8) matrix into the groups' rows
+ * (group_data[g]: rows x row_stride bytes); numerical features only (else SB2_EUNSUPPORTED). value_to_bin of one
+ * value with one feature's bounds (data/bin_mapper.rs:343-360), for the tests. */
+int orc_bin_rows(const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
+                 const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
+                 uint8_t* const* group_data);
+uint32_t orc_value_to_bin(const double* upper_bounds, uint32_t num_upper_bounds, int nan_bin, double value);
+
 /* split.rs */
 int orc_find_best_split(const sb2_dataset* data, const double* hist, const uint8_t* evaluate, double sum_grad,
                         double sum_hess, int64_t count, double grad_scale, double hess_scale,

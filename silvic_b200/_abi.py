@@ -235,6 +235,8 @@ SIGNATURES = {
     "sb2_model_tree": (C.c_int, [VP, C.c_int, P(TreeView)]),
     "sb2_model_iteration_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
     "sb2_model_tree_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
+    "sb2_bin_dense": (C.c_int, [VP, VP, C.c_int, C.c_uint64, C.c_uint32, C.c_int, P(Feature), C.c_uint32, P(Group),
+                                C.c_uint32, P(P(C.c_uint8))]),
 }
 
 _lib = None

@@ -79,6 +79,28 @@ def params_from_dict(params: dict) -> _abi.Params:
     return p
 
 
+def _matrix_view(values):
+    """(pointer, rows, cols, value bytes, row-major, keep-alive) of a 2-D float32/float64 matrix: a numpy array
+    (C- or Fortran-ordered) or a CUDA torch tensor (contiguous or its transpose)."""
+    if hasattr(values, "data_ptr") and getattr(values, "is_cuda", False):
+        if values.dim() != 2 or values.element_size() not in (4, 8) or not values.is_floating_point():
+            raise ValueError("a 2-D float32 or float64 tensor")
+        rows, cols = values.shape
+        if values.is_contiguous():
+            return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), True, values
+        if values.t().is_contiguous():
+            return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), False, values
+        values = values.contiguous()
+        return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), True, values
+    a = np.asarray(values)
+    if a.ndim != 2 or a.dtype not in (np.float32, np.float64):
+        raise ValueError("a 2-D float32 or float64 array")
+    if not (a.flags.c_contiguous or a.flags.f_contiguous):
+        a = np.ascontiguousarray(a)
+    rows, cols = a.shape
+    return C.c_void_p(a.ctypes.data), rows, cols, a.itemsize, bool(a.flags.c_contiguous), a
+
+
 class B200Backend:
     """One GPU's backend handle (`trait Backend`). Not thread-safe; handles are independent."""
 
@@ -122,6 +144,24 @@ class B200Backend:
         d = train.c_struct()
         self._check(self._lib.sb2_load(self._h, C.byref(d), C.byref(obj)))
         self._data = train
+
+    def bin_dense(self, values, features, groups) -> list[np.ndarray]:
+        """data::binning::bin_rows on the device (`sb2_bin_dense`): `values` (rows × features, float32 or float64,
+        C- or Fortran-ordered numpy array, or a CUDA torch tensor) binned with `features`' upper bounds into each of
+        `groups`' rows; returns one uint8 array of rows × row_stride per group."""
+        from .dataset import BinnedDataset
+
+        ptr, rows, cols, vbytes, row_major, keep = _matrix_view(values)
+        shell = BinnedDataset(rows, 0, list(features), [g.__class__(g.features, g.row_stride, g.hist_offset,
+                                                                      g.total_bins, np.zeros((0, g.row_stride), np.uint8))
+                                                        for g in groups], 0, np.zeros(0, np.float32))
+        d = shell.c_struct()
+        outs = [np.zeros((rows, g.row_stride), dtype=np.uint8) for g in groups]
+        ptrs = (C.POINTER(C.c_uint8) * max(len(outs), 1))(*[o.ctypes.data_as(C.POINTER(C.c_uint8)) for o in outs])
+        self._check(self._lib.sb2_bin_dense(self._h, ptr, vbytes, rows, cols, int(row_major), d.features,
+                                            len(features), d.groups, len(groups), ptrs))
+        del keep
+        return outs
 
     def init_scores(self, dataset: int, value: float):
         self._check(self._lib.sb2_init_scores(self._h, dataset, value))

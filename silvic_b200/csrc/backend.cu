@@ -16,6 +16,7 @@
 #include <string>
 #include <vector>
 
+#include "binning.cuh"
 #include "iter.cuh"
 
 using namespace sb2;
@@ -1749,6 +1750,124 @@ int sb2_profile_steps(sb2_backend* b, const sb2_params* p, double init_score, do
             rows[s * kStepTrace + k] = k < kGrowPhases ? v * 1e-9 : v;
         }
     return SB2_OK;
+}
+
+// data::binning::bin_rows on the device: see the header. Per chunk of rows (at most ~256 MB of values), the values
+// (copied from the host when they live there) are binned group by group into a device buffer of the chunk's group
+// rows, which is copied into the caller's group buffer.
+int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
+                  const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
+                  uint8_t* const* group_data) {
+    if (!b) return SB2_EDEVICE;
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    if (value_bytes != 4 && value_bytes != 8) return b->fail(SB2_EDATA, "values must be f32 (4 bytes) or f64 (8)");
+    if (rows == 0 || num_groups == 0) return SB2_OK;
+    if (!values || !features || !groups || !group_data) return b->fail(SB2_EDATA, "a null buffer");
+    // Per group: its features' matrix columns, byte columns, bounds and NaN bins, uploaded once.
+    struct GroupPlan {
+        DeviceBuffer meta, bounds, out;
+        uint32_t nf = 0, total = 0;
+    };
+    std::vector<GroupPlan> plans(num_groups);
+    for (uint32_t g = 0; g < num_groups; ++g) {
+        const sb2_group& grp = groups[g];
+        if (!group_data[g]) return b->fail(SB2_EDATA, "group " + std::to_string(g) + " has no output buffer");
+        std::vector<uint32_t> feat, column, off{0};
+        std::vector<uint8_t> nan;
+        std::vector<double> bounds;
+        for (uint32_t k = 0; k < grp.num_features; ++k) {
+            const uint32_t f = grp.features[k];
+            if (f >= num_features || f >= cols)
+                return b->fail(SB2_EDATA, "group " + std::to_string(g) + " names feature " + std::to_string(f) +
+                                              " beyond the matrix's columns");
+            const sb2_feature& m = features[f];
+            if (m.kind == SB2_CATEGORICAL)
+                return b->fail(SB2_EUNSUPPORTED, "categorical feature " + std::to_string(f) + ": the device binning is numerical only");
+            if (m.kind != SB2_NUMERICAL || !m.upper_bounds || m.num_upper_bounds == 0 || m.num_upper_bounds > 256)
+                return b->fail(SB2_EDATA, "grouped feature " + std::to_string(f) + " without 1..256 upper bounds");
+            if (m.column >= grp.row_stride)
+                return b->fail(SB2_EDATA, "feature " + std::to_string(f) + "'s column lies outside its group's rows");
+            feat.push_back(f);
+            column.push_back(m.column);
+            bounds.insert(bounds.end(), m.upper_bounds, m.upper_bounds + m.num_upper_bounds);
+            off.push_back(static_cast<uint32_t>(bounds.size()));
+            // value_to_bin(NaN) (bin_mapper.rs:347-352): the NaN bin, or the bin of 0.0
+            uint32_t zero = 0;
+            while (zero < m.num_upper_bounds && m.upper_bounds[zero] < 0.0) ++zero;
+            nan.push_back(static_cast<uint8_t>(m.nan_bin ? m.num_upper_bounds : zero));
+        }
+        GroupPlan& p = plans[g];
+        p.nf = static_cast<uint32_t>(feat.size());
+        p.total = static_cast<uint32_t>(bounds.size());
+        if (sizeof(double) * p.total > 200 * 1024)
+            return b->fail(SB2_EUNSUPPORTED, "group " + std::to_string(g) + " has more bounds than shared memory holds");
+        // meta: feature [nf], column [nf], bound_off [nf + 1], nan [nf] (bytes)
+        std::vector<uint8_t> meta(4 * (3 * p.nf + 1) + p.nf);
+        std::memcpy(meta.data(), feat.data(), 4 * p.nf);
+        std::memcpy(meta.data() + 4 * p.nf, column.data(), 4 * p.nf);
+        std::memcpy(meta.data() + 8 * p.nf, off.data(), 4 * (p.nf + 1));
+        std::memcpy(meta.data() + 4 * (3 * p.nf + 1), nan.data(), p.nf);
+        SB2_CUDA(b, p.meta.alloc(meta.size()));
+        SB2_CUDA(b, p.bounds.alloc(sizeof(double) * std::max<uint32_t>(p.total, 1)));
+        SB2_CUDA(b, cudaMemcpyAsync(p.meta.ptr, meta.data(), meta.size(), cudaMemcpyHostToDevice, b->stream));
+        if (p.total)
+            SB2_CUDA(b, cudaMemcpyAsync(p.bounds.ptr, bounds.data(), sizeof(double) * p.total, cudaMemcpyHostToDevice,
+                                        b->stream));
+        SB2_TRY(b->sync());  // the host vectors go out of scope
+    }
+    cudaPointerAttributes attr{};
+    const bool on_device = cudaPointerGetAttributes(&attr, values) == cudaSuccess &&
+                           (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
+    cudaGetLastError();  // a host pointer may leave an error from the query
+    const uint64_t row_bytes = static_cast<uint64_t>(cols) * value_bytes;
+    uint64_t chunk = std::max<uint64_t>((256ull << 20) / std::max<uint64_t>(row_bytes, 1), 128) / 128 * 128;
+    chunk = std::min(chunk, rows);
+    DeviceBuffer staged;
+    if (!on_device) SB2_CUDA(b, staged.alloc(chunk * row_bytes));
+    for (uint32_t g = 0; g < num_groups; ++g) SB2_CUDA(b, plans[g].out.alloc(chunk * std::max<uint32_t>(groups[g].row_stride, 1)));
+    for (uint64_t r0 = 0; r0 < rows; r0 += chunk) {
+        const uint64_t n = std::min(chunk, rows - r0);
+        BinGroupArgs a{};
+        a.f64 = value_bytes == 8;
+        a.row_major = row_major != 0;
+        a.cols = cols;
+        a.chunk_rows = n;
+        if (on_device) {
+            a.values = values;
+            a.rows = rows;
+            a.row0 = r0;
+        } else {
+            const uint8_t* src = static_cast<const uint8_t*>(values);
+            if (row_major)
+                SB2_CUDA(b, cudaMemcpyAsync(staged.ptr, src + r0 * row_bytes, n * row_bytes, cudaMemcpyHostToDevice, b->stream));
+            else
+                SB2_CUDA(b, cudaMemcpy2DAsync(staged.ptr, n * value_bytes, src + r0 * value_bytes, rows * value_bytes,
+                                              n * value_bytes, cols, cudaMemcpyHostToDevice, b->stream));
+            a.values = staged.ptr;
+            a.rows = n;  // the staged column-major chunk's pitch
+            a.row0 = 0;
+        }
+        for (uint32_t g = 0; g < num_groups; ++g) {
+            GroupPlan& p = plans[g];
+            const uint32_t stride = groups[g].row_stride;
+            if (stride == 0) continue;
+            const uint8_t* meta = p.meta.as<uint8_t>();
+            a.num_features = p.nf;
+            a.feature = reinterpret_cast<const uint32_t*>(meta);
+            a.column = reinterpret_cast<const uint32_t*>(meta + 4 * p.nf);
+            a.bound_off = reinterpret_cast<const uint32_t*>(meta + 8 * p.nf);
+            a.nan_bin = meta + 4 * (3 * p.nf + 1);
+            a.bounds = p.bounds.as<double>();
+            a.total_bounds = p.total;
+            a.stride = stride;
+            a.out = p.out.as<uint8_t>();
+            SB2_CUDA(b, cudaMemsetAsync(p.out.ptr, 0, n * stride, b->stream));  // padding columns are 0
+            SB2_CUDA(b, launch_bin_group(a, b->stream));
+            SB2_CUDA(b, cudaMemcpyAsync(group_data[g] + r0 * stride, p.out.ptr, n * stride, cudaMemcpyDeviceToHost,
+                                        b->stream));
+        }
+    }
+    return b->sync();
 }
 
 int sb2_model_free(sb2_model* m) {

@@ -42,6 +42,9 @@ _SIGS = {
     "orc_add_tree": (C.c_int, [P(_abi.Dataset), P(_abi.DeviceNode), C.c_size_t, P(C.c_float), C.c_size_t,
                                P(C.c_float)]),
     "orc_reset_partition": (C.c_uint32, [P(_abi.BagSpec), C.c_uint64, C.c_uint64, P(C.c_uint32)]),
+    "orc_bin_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_uint32, C.c_int, P(_abi.Feature), C.c_uint32,
+                               P(_abi.Group), C.c_uint32, P(P(C.c_uint8))]),
+    "orc_value_to_bin": (C.c_uint32, [P(C.c_double), C.c_uint32, C.c_int, C.c_double]),
     "orc_find_best_split": (C.c_int, [P(_abi.Dataset), P(C.c_double), P(C.c_uint8), C.c_double, C.c_double,
                                       C.c_int64, C.c_double, C.c_double, P(_abi.SplitConfig), P(_abi.SplitInfo),
                                       P(C.c_uint8)]),
@@ -153,6 +156,31 @@ def add_tree(data, nodes, leaf_values, scores) -> np.ndarray:
     code = lib().orc_add_tree(C.byref(d), arr, len(nodes), _p(lv, C.c_float), len(lv), _p(s, C.c_float))
     assert code == 0, lib().orc_last_error()
     return s
+
+
+def value_to_bin(upper_bounds, nan_bin, value) -> int:
+    ub = np.ascontiguousarray(upper_bounds, dtype=np.float64)
+    return int(lib().orc_value_to_bin(_p(ub, C.c_double), len(ub), int(nan_bin), float(value)))
+
+
+def bin_rows(values: np.ndarray, features, groups) -> list[np.ndarray]:
+    """data/binning.rs bin_rows of a C- or Fortran-ordered f32/f64 matrix into each group's rows."""
+    from silvic_b200.dataset import BinnedDataset
+
+    a = np.asarray(values)
+    if not (a.flags.c_contiguous or a.flags.f_contiguous):
+        a = np.ascontiguousarray(a)
+    rows, cols = a.shape
+    shell = BinnedDataset(rows, 0, list(features), [g.__class__(g.features, g.row_stride, g.hist_offset, g.total_bins,
+                                                                np.zeros((0, g.row_stride), np.uint8)) for g in groups],
+                          0, np.zeros(0, np.float32))
+    d = shell.c_struct()
+    outs = [np.zeros((rows, g.row_stride), dtype=np.uint8) for g in groups]
+    ptrs = (P(C.c_uint8) * max(len(outs), 1))(*[_p(o, C.c_uint8) for o in outs])
+    code = lib().orc_bin_rows(C.c_void_p(a.ctypes.data), a.itemsize, rows, cols, int(a.flags.c_contiguous),
+                              d.features, len(features), d.groups, len(groups), ptrs)
+    assert code == 0, code
+    return outs
 
 
 def reset_partition(bag, num_rows, row_offset=0) -> np.ndarray:

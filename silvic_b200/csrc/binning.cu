@@ -2,15 +2,17 @@
 // (data::binning::bin_rows, crates/silvic-core/src/data/binning.rs:71-135, with BinMapper::value_to_bin,
 // data/bin_mapper.rs:343-360).
 //
-// Per group, one CTA takes 128 rows: the group's upper bounds sit in shared memory (a group holds at most 8192
-// bins, data/mod.rs:22, so its bounds fit), every thread bins values of the tile and writes the bytes into the
-// group's rows. Row-major input: consecutive threads take consecutive features of a row (the row's values of the
-// group are contiguous when its features are); column-major: consecutive rows of a feature. A value's bin is the
-// number of upper bounds below it (`partition_point(bound < value)`; the last bound is +inf), NaN goes to the NaN
-// bin, or to zero's bin when the feature has none. The byte-wide binary search over the feature's bounds is the
-// same count as the reference's branch-free search over bounds padded to 256 with +inf (binning.rs:51-61).
+// Per group, each CTA copies the group's upper bounds into shared memory once (a group holds at most 8192 bins,
+// data/mod.rs:22, so its bounds fit) and bins tiles of 128 rows in turn, every thread four rows of one feature at a
+// time (four searches in flight), writing the bytes into the group's rows. Row-major input: consecutive threads
+// take consecutive features of the same rows (the rows' values of the group are contiguous when its features are);
+// column-major: consecutive row quads of a feature. A value's bin is the number of upper bounds below it
+// (`partition_point(bound < value)`; the last bound is +inf), found by binary lifting over the feature's own
+// bounds: the same count as the reference's branch-free search over bounds padded to 256 with +inf
+// (binning.rs:51-61). NaN goes to the NaN bin, or to zero's bin when the feature has none.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "binning.cuh"
@@ -22,36 +24,53 @@ namespace {
 constexpr uint32_t kTileRows = 128;
 constexpr int kBinThreads = 256;
 
-__device__ __forceinline__ uint32_t count_below(const double* bounds, uint32_t n, double v) {
-    uint32_t lo = 0, hi = n;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (bounds[mid] < v)
-            lo = mid + 1;
-        else
-            hi = mid;
-    }
-    return lo;
-}
+constexpr uint32_t kQuad = 4;  // rows of one feature a thread bins at once: four searches in flight
 
 __global__ void __launch_bounds__(kBinThreads) bin_group_kernel(BinGroupArgs a) {
     extern __shared__ double bounds[];  // the group's features' bounds, back to back (a.bound_off)
     for (uint32_t i = threadIdx.x; i < a.total_bounds; i += kBinThreads) bounds[i] = a.bounds[i];
     __syncthreads();
-    const uint64_t tile0 = static_cast<uint64_t>(blockIdx.x) * kTileRows;
-    const uint32_t nf = a.num_features;
-    for (uint32_t e = threadIdx.x; e < kTileRows * nf; e += kBinThreads) {
-        const uint32_t r = a.row_major ? e / nf : e % kTileRows;
-        const uint32_t k = a.row_major ? e % nf : e / kTileRows;
-        const uint64_t row = tile0 + r;  // in the chunk
-        if (row >= a.chunk_rows) continue;
-        const uint64_t at = a.row_major ? (a.row0 + row) * a.cols + a.feature[k]
-                                        : static_cast<uint64_t>(a.feature[k]) * a.rows + a.row0 + row;
-        const double v = a.f64 ? static_cast<const double*>(a.values)[at]
-                               : static_cast<double>(static_cast<const float*>(a.values)[at]);
-        const uint32_t off = a.bound_off[k];
-        const uint32_t bin = v != v ? a.nan_bin[k] : count_below(bounds + off, a.bound_off[k + 1] - off, v);
-        a.out[row * a.stride + a.column[k]] = static_cast<uint8_t>(bin);
+    const uint32_t nf = a.num_features, quads = kTileRows / kQuad;
+    const uint64_t tiles = (a.chunk_rows + kTileRows - 1) / kTileRows;
+    // a CTA loads its group's bounds once and bins tile after tile
+    for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const uint64_t tile0 = tile * kTileRows;
+        for (uint32_t e = threadIdx.x; e < quads * nf; e += kBinThreads) {
+            // row-major: consecutive threads take consecutive features of the same rows; column-major:
+            // consecutive row quads of the same feature
+            const uint32_t k = a.row_major ? e % nf : e / quads;
+            const uint32_t q = a.row_major ? e / nf : e % quads;
+            const uint64_t row0 = tile0 + kQuad * q;  // in the chunk
+            double v[kQuad];
+#pragma unroll
+            for (uint32_t i = 0; i < kQuad; ++i) {
+                const uint64_t row = row0 + i;
+                v[i] = 0.0;
+                if (row < a.chunk_rows) {
+                    const uint64_t at = a.row_major ? (a.row0 + row) * a.cols + a.feature[k]
+                                                    : static_cast<uint64_t>(a.feature[k]) * a.rows + a.row0 + row;
+                    v[i] = a.f64 ? static_cast<const double*>(a.values)[at]
+                                 : static_cast<double>(static_cast<const float*>(a.values)[at]);
+                }
+            }
+            // The number of bounds below each value, by binary lifting over the feature's n bounds (the count is
+            // built from the powers of two at or below n, largest first).
+            const uint32_t off = a.bound_off[k], n = a.bound_off[k + 1] - off;
+            const double* b = bounds + off;
+            uint32_t pos[kQuad] = {0, 0, 0, 0};
+            for (uint32_t step = n ? 1u << (31 - __clz(n)) : 0u; step; step >>= 1) {
+#pragma unroll
+                for (uint32_t i = 0; i < kQuad; ++i)
+                    if (pos[i] + step <= n && b[pos[i] + step - 1] < v[i]) pos[i] += step;
+            }
+#pragma unroll
+            for (uint32_t i = 0; i < kQuad; ++i) {
+                const uint64_t row = row0 + i;
+                if (row >= a.chunk_rows) break;
+                const uint32_t bin = v[i] != v[i] ? a.nan_bin[k] : pos[i];
+                a.out[row * a.stride + a.column[k]] = static_cast<uint8_t>(bin);
+            }
+        }
     }
 }
 
@@ -63,7 +82,15 @@ cudaError_t launch_bin_group(const BinGroupArgs& a, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(bin_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const unsigned grid = static_cast<unsigned>((a.chunk_rows + kTileRows - 1) / kTileRows);
+    // enough CTAs to fill the GPU, each over many tiles (its copy of the bounds then serves many rows)
+    int device = 0, sms = 0, per_sm = 0;
+    e = cudaGetDevice(&device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bin_group_kernel, kBinThreads, smem);
+    if (e != cudaSuccess) return e;
+    const uint64_t tiles = (a.chunk_rows + kTileRows - 1) / kTileRows;
+    const uint64_t want = static_cast<uint64_t>(std::max(sms, 1)) * std::max(per_sm, 1);
+    const unsigned grid = static_cast<unsigned>(std::min(tiles, want));
     bin_group_kernel<<<grid, kBinThreads, smem, s>>>(a);
     return cudaGetLastError();
 }

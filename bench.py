@@ -477,6 +477,41 @@ def run_b200(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_binning(args):
+    """The device binning of a dense matrix (`sb2_bin_dense`, data/binning.rs bin_rows) on the config's raw
+    features: a device-resident f32 matrix into the dataset's groups of 32 features, timed from the call until the
+    group rows are in host memory (wall clock: the copy of the rows back is part of the job). One line of JSON."""
+    import torch
+
+    from silvic_b200.backend import B200Backend
+    from silvic_b200.dataset import FeatureGroup, FeatureMeta
+
+    dev = torch.device("cuda", 0)
+    bounds = bin_bounds(dev).cpu().numpy()
+    x = features_of(torch.arange(ROWS, dtype=torch.int64, device=dev), dev)
+    per_group = 8192 // MAX_BIN
+    feats, groups = [], []
+    for gi, start in enumerate(range(0, FEATURES, per_group)):
+        members = list(range(start, min(FEATURES, start + per_group)))
+        groups.append(FeatureGroup(members, (len(members) + 3) // 4 * 4, 0, 0, np.zeros((0, 4), np.uint8)))
+        for col, f in enumerate(members):
+            feats.append(FeatureMeta(name=f"Column_{f}", num_bins=MAX_BIN, upper_bounds=bounds[f].copy(), group=gi,
+                                     column=col))
+    b = B200Backend(0)
+    times = []
+    for it in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        b.bin_dense(x, feats, groups)
+        if it >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    b.close()
+    s = sum(times) / len(times)
+    print(json.dumps({"binning": {"rows": ROWS, "features": FEATURES, "ms": s * 1e3,
+                                  "values_per_s": ROWS * FEATURES / s, "input": "device f32 row-major",
+                                  "output": "host group rows", "steps": args.steps, "warmup": args.warmup}}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -488,10 +523,15 @@ def main():
                     help="c2 (default): BASELINE configs[1]; c4: configs[3], the 100M-row scaling config")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows of the synthetic set (a smaller case for profiling; default: the config's)")
+    ap.add_argument("--binning", action="store_true",
+                    help="time the device binning of the config's raw features instead of training (one GPU)")
     args = ap.parse_args()
     set_config(args.config)
     if args.rows:
         set_rows(args.rows)
+    if args.binning:
+        run_binning(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1:

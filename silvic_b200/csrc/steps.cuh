@@ -58,23 +58,21 @@ __device__ __forceinline__ bool ranks_before(double og, int32_t ol, double g, in
     return og > g || (og == g && ol < l);
 }
 
-// Warp: the splittable rows of `rows` leaves (leaf[k], k < rows; negative: none) into `dst` (shared, rows of F),
-// eight bytes a lane in flight.
-__device__ __forceinline__ void load_split_rows(const TrainArgs& a, const int32_t* leaf, int rows, uint8_t* dst) {
-    constexpr int kLoads = 8;
+// Warp: leaf `leaf`'s splittable row (F bytes) into `dst`, eight bytes a lane in flight.
+__device__ __forceinline__ void copy_split_row(const TrainArgs& a, int32_t leaf, uint8_t* dst) {
     const uint32_t lane = threadIdx.x & 31, F = a.num_features;
-    const uint32_t total = static_cast<uint32_t>(rows) * F;
-    for (uint32_t e0 = lane; e0 < total; e0 += 32 * kLoads) {
-        uint8_t v[kLoads];
+    const uint8_t* row = a.splittable + static_cast<size_t>(leaf) * F;
+    for (uint32_t f0 = 0; f0 < F; f0 += 32 * 8) {
+        uint8_t v[8];
 #pragma unroll
-        for (int q = 0; q < kLoads; ++q) {
-            const uint32_t e = e0 + 32 * q, k = e / F;
-            v[q] = e < total && leaf[k] >= 0 ? __ldcg(a.splittable + static_cast<size_t>(leaf[k]) * F + (e - k * F)) : 0;
+        for (uint32_t q = 0; q < 8; ++q) {
+            const uint32_t f = f0 + 32 * q + lane;
+            v[q] = f < F ? __ldcg(row + f) : 0;
         }
 #pragma unroll
-        for (int q = 0; q < kLoads; ++q) {
-            const uint32_t e = e0 + 32 * q;
-            if (e < total) dst[e] = v[q];
+        for (uint32_t q = 0; q < 8; ++q) {
+            const uint32_t f = f0 + 32 * q + lane;
+            if (f < F) dst[f] = v[q];
         }
     }
 }
@@ -175,19 +173,31 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
                 fs.other_leaf[k] = bl;
             }
         }
-        __syncwarp();
-        // their records (lane k: leaf k's) and splittable rows, in case they are split next
-        if (lane < static_cast<uint32_t>(kSplits) && fs.other_leaf[lane] >= 0) {
-            const DevLeaf r = load_cg(a.leaves + fs.other_leaf[lane]);
-            fs.other[lane] = r;
-            fs.other_feat[lane] = a.d.features[r.best.feature];
-        }
-        load_split_rows(a, fs.other_leaf, kSplits, osplit);
     } else if (warp == 4) {
-        if (lane >= 1 && lane < static_cast<uint32_t>(n)) fs.pending[lane] = load_cg(a.leaves + st[lane].leaf);
         if (lane < static_cast<uint32_t>(kSplits)) fs.pending_leaf[lane] = lane >= 1 && lane < static_cast<uint32_t>(n) ? st[lane].leaf : -1;
-        __syncwarp();
-        load_split_rows(a, fs.pending_leaf, n, psplit);
+    }
+    __syncthreads();
+    // The records and splittable rows of those leaves, in case they are split next, and of the step's own
+    // speculative leaves, in case their splits are dropped: warp k < kSplits the k-th best other leaf's (lane 0 its
+    // record and split feature), warp kSplits + j split j's leaf's.
+    static_assert(2 * kSplits <= kHistThreads / 32, "a warp per prepared leaf");
+    if (warp < static_cast<uint32_t>(kSplits)) {
+        const int32_t leaf = fs.other_leaf[warp];
+        if (leaf >= 0) {
+            if (lane == 0) {
+                const DevLeaf r = load_cg(a.leaves + leaf);
+                fs.other[warp] = r;
+                fs.other_feat[warp] = a.d.features[r.best.feature];
+            }
+            copy_split_row(a, leaf, osplit + static_cast<size_t>(warp) * a.num_features);
+        }
+    } else if (warp < static_cast<uint32_t>(2 * kSplits)) {
+        const uint32_t j = warp - kSplits;
+        const int32_t leaf = fs.pending_leaf[j];
+        if (leaf >= 0) {
+            if (lane == 0) fs.pending[j] = load_cg(a.leaves + leaf);
+            copy_split_row(a, leaf, psplit + static_cast<size_t>(j) * a.num_features);
+        }
     }
     __syncthreads();
 }

@@ -67,7 +67,7 @@ METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8
 # DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
 # case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md. Per config;
 # none captured for c4.
-TREE_TRAFFIC_PER_ROW = {"c2": 880, "c4": None}
+TREE_TRAFFIC_PER_ROW = {"c2": 885, "c4": None}
 
 
 # ---- synthetic data (torch on the GPU as plumbing) ------------------------------------------------------------

@@ -338,21 +338,35 @@ __global__ void __launch_bounds__(kRowThreads) leaf_map_kernel(IterArgs a) {
 // Backend::leaf_sums for every leaf of the tree (backend/cpu.rs:886-905: the fixed-point sums of the leaf's rows'
 // gradients and hessians): the rows in order, four a thread at a time, each row's pair added to its leaf's sums in
 // shared memory (64-bit atomics; integer sums, so the order is free), then the CTA's sums added to the output.
+constexpr uint64_t kLeafSumRows = 60000;  // rows a leaf_sums CTA takes at most: its 32-bit halves cannot overflow
+
 __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
-    // g and h sums in separate arrays: a warp's 64-bit atomics on random leaves spread over every bank
-    __shared__ long long sum_g[kIndexLeaves], sum_h[kIndexLeaves];
+    // Each fixed-point value (|v| < 2^31) is added as two 32-bit halves, its low 16 bits (unsigned) and the rest
+    // (signed): over at most 65536 rows neither sum overflows, and 32-bit shared atomics run several times faster
+    // than 64-bit ones. A value outside that range (a gradient far beyond the scale's maximum) goes straight to the
+    // output with a 64-bit atomic.
+    __shared__ uint32_t g_lo[kIndexLeaves], h_lo[kIndexLeaves];
+    __shared__ int32_t g_hi[kIndexLeaves], h_hi[kIndexLeaves];
     if (a.t.iter->stopped) return;
     const int32_t L = min(*a.t.tree.num_leaves, kIndexLeaves);
-    for (int i = threadIdx.x; i < L; i += kRowThreads) sum_g[i] = sum_h[i] = 0;
+    for (int i = threadIdx.x; i < L; i += kRowThreads) g_lo[i] = h_lo[i] = 0, g_hi[i] = h_hi[i] = 0;
     __syncthreads();
     const double mg = __longlong_as_double(static_cast<long long>(a.t.iter->max_abs_grad_bits));
     const double mh = __longlong_as_double(static_cast<long long>(a.t.iter->max_hess_bits));
     const float gs = fixed_point_scale(mg), hs = fixed_point_scale(mh);
     const uint64_t n = a.r.num_rows;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kRowThreads;
+    auto add1 = [&](uint32_t leaf, int64_t v, uint32_t* lo, int32_t* hi, long long* out) {
+        if (static_cast<uint64_t>(v + (1ll << 31)) < (1ull << 32)) {
+            atomicAdd(lo + leaf, static_cast<uint32_t>(v) & 0xFFFFu);
+            atomicAdd(hi + leaf, static_cast<int32_t>(v >> 16));
+        } else {
+            atomicAdd(reinterpret_cast<unsigned long long*>(out), static_cast<unsigned long long>(v));
+        }
+    };
     auto add = [&](uint32_t leaf, float g, float h) {
-        atomicAdd(reinterpret_cast<unsigned long long*>(&sum_g[leaf]), static_cast<unsigned long long>(to_fixed(g, gs)));
-        atomicAdd(reinterpret_cast<unsigned long long*>(&sum_h[leaf]), static_cast<unsigned long long>(to_fixed(h, hs)));
+        add1(leaf, to_fixed(g, gs), g_lo, g_hi, reinterpret_cast<long long*>(a.leaf_sums) + 2 * leaf);
+        add1(leaf, to_fixed(h, hs), h_lo, h_hi, reinterpret_cast<long long*>(a.leaf_sums) + 2 * leaf + 1);
     };
     for (uint64_t r0 = (static_cast<uint64_t>(blockIdx.x) * kRowThreads + threadIdx.x) * 4; r0 < n; r0 += 4 * stride) {
         if (r0 + 4 <= n) {
@@ -369,8 +383,10 @@ __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
     }
     __syncthreads();
     for (int i = threadIdx.x; i < L; i += kRowThreads) {
-        if (sum_g[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i]), static_cast<unsigned long long>(sum_g[i]));
-        if (sum_h[i] != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i + 1]), static_cast<unsigned long long>(sum_h[i]));
+        const long long sg = static_cast<long long>(g_hi[i]) * 65536 + g_lo[i];
+        const long long sh = static_cast<long long>(h_hi[i]) * 65536 + h_lo[i];
+        if (sg != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i]), static_cast<unsigned long long>(sg));
+        if (sh != 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.leaf_sums[2 * i + 1]), static_cast<unsigned long long>(sh));
     }
 }
 
@@ -670,7 +686,9 @@ void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s) {
 }
 void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s) {
     leaf_map_kernel<<<grid, kRowThreads, 0, s>>>(a);
-    leaf_sums_kernel<<<std::max(grid / 4, 1), kRowThreads, 0, s>>>(a);  // fewer CTAs: fewer output atomics
+    // fewer CTAs than the row passes (fewer output atomics), but enough that none takes more than kLeafSumRows rows
+    const uint64_t need = (a.r.num_rows + kLeafSumRows - 1025) / (kLeafSumRows - 1024);
+    leaf_sums_kernel<<<static_cast<unsigned>(std::max<uint64_t>(std::max(grid / 4, 1), need)), kRowThreads, 0, s>>>(a);
 }
 void launch_finalize(const IterArgs& a, cudaStream_t s) { finalize_kernel<<<1, kRowThreads, 0, s>>>(a); }
 void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s) {

@@ -1,26 +1,32 @@
-"""Benchmark: boosting iterations/s of silvic's quantized-histogram training on B200, BASELINE config 2.
+"""Benchmark: boosting iterations/s of silvic's quantized-histogram training on B200 (BASELINE.json's metric).
 
-Workload: binary classification, 10,000,000 rows x 100 f32 features (70 N(0,1),
-30 U[0,1)), label ~ Bernoulli(sigmoid(sparse random linear + 3 pairwise interactions)), 255 bins, 255 leaves,
-quantized gradients (4 bins). A "step" is one boosting iteration: gradients, quantization, a 255-leaf tree grown
-split by split on the device (partition, smaller-child histogram, sibling subtraction, split scan), leaf renewal
-and the score update.
+Default workload: BASELINE.json configs[3] ("c4"), the largest configuration that fits one B200 and the one the
+scaling target names: L2 regression, 100,000,000 rows x 256 f32 features ~ N(0,1), target = a random 32-feature
+linear function + N(0,1) noise, 255 bins, 255 leaves, quantized gradients (4 bins), 200 trees in a full job.
+`--config` selects another configuration: c1 (configs[0]: 1M x 28 L2, 63 leaves, 100 trees) or c2 (configs[1]:
+10M x 100 binary, 255 leaves, 500 trees). A "step" is one boosting iteration: gradients, quantization, a tree grown
+split by split on the device (partition, smaller-child histogram, sibling subtraction, split scan, leaf choice),
+leaf renewal and the score update.
 
-Data are synthetic: every feature value is a pure function of (seed, global row, feature) from silvic's counter
-hash, generated on the GPU, so any rank regenerates its own rows. Bin bounds are equal-frequency cuts of the first
-200,000 rows (bin_construct_sample_cnt's default sample size), bins the rows with them, and pack the features into
-silvic's group layout (32 features of 255 bins per group). The binned matrix (1 GB) is larger than the 126 MB L2,
-so no L2 flush is needed between timed iterations.
+Data are synthetic (BASELINE names no public dataset): every feature value is a pure function of (seed, global row,
+feature) from silvic's counter hash, generated on the GPU, so any rank regenerates its own rows. Bin bounds are
+equal-frequency cuts of the first 200,000 rows (bin_construct_sample_cnt's default sample size); the rows are binned
+by the product's device binning (sb2_bin_dense, data::binning::bin_rows) into silvic's group layout (32 features of
+255 bins per group). The binned matrix (c4: 25.6 GB; c2: 1 GB) is larger than the 126 MB L2, so no L2 flush is
+needed between timed iterations.
 
 Arms:
-  default            the B200 backend; `value` = iterations/s from CUDA events around each iteration of the
-                     device-resident trainer (inputs resident in HBM), max over ranks; `e2e` = the same metric
-                     through the reference-facing C ABI with host buffers: sb2_load (host->device copy of the binned
-                     data) + sb2_train + the trees read back, wall clock.
+  default            the B200 backend. `value` = iterations/s from CUDA events around each iteration of the
+                     device-resident trainer (inputs resident in HBM), max over ranks. `e2e` = the same metric for a
+                     whole job through the reference-facing C ABI with host buffers: a fresh handle, sb2_load (the
+                     host->device copy of the binned data), sb2_join_ranks (N>1), sb2_train of the config's full tree
+                     count and the trees read back, wall clock, max over ranks; its one-time setup is reported apart.
+                     `parity`: the first trees of the timed run against the CPU oracle's trees of the same dataset
+                     (the whole dataset, on rank 0, at every N), field by field and as LightGBM model text.
   --impl reference   the CPU restatement of silvic-core's trainer (oracle/, "port") on this box's host cores.
 
-Multi-GPU: one process per GPU (torchrun). Rows are sharded contiguously (strong scaling: the 10M-row job is fixed)
-and every split's histogram is allreduced over NCCL inside the backend.
+Multi-GPU: one process per GPU (torchrun). Rows are sharded contiguously (strong scaling: the job is fixed); the
+split steps exchange histograms inside the tree kernel over NVLink.
 """
 
 from __future__ import annotations
@@ -33,6 +39,7 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass, field
 from pathlib import Path
 
 import numpy as np
@@ -41,33 +48,58 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 SEED = 20261107
-CONFIG = "c2"
-ROWS = 10_000_000
-GAUSSIAN, UNIFORM = 70, 30
-FEATURES = GAUSSIAN + UNIFORM
-MAX_BIN = 255
 SAMPLE_ROWS = 200_000
-PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
+METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
+PARITY_TREES = 2  # trees of the timed run checked against the oracle's
+
+
+@dataclass
+class Config:
+    name: str
+    index: int            # position in BASELINE.json's configs
+    rows: int
+    objective: str
+    max_bin: int
+    num_leaves: int
+    trees: int            # trees of the full job (the e2e run)
+    kinds: list = field(default_factory=list)  # per feature: "gauss" or "unif"
+    # DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a
+    # smaller case of the same workload (the traffic grows with the rows); None: not captured
+    traffic_per_row: float | None = None
+
+    @property
+    def features(self) -> int:
+        return len(self.kinds)
+
+    def describe(self, rows: int) -> str:
+        size = f"{rows:,} rows" + ("" if rows == self.rows else " (reduced)")
+        return (f"configs[{self.index}]: {self.objective} {size} x {self.features}, {self.max_bin} bins, "
+                f"{self.num_leaves} leaves")
+
+
+CONFIGS = {
+    "c1": Config("c1", 0, 1_000_000, "regression", 255, 63, 100, ["gauss"] * 28),
+    "c2": Config("c2", 1, 10_000_000, "binary", 255, 255, 500, ["gauss"] * 70 + ["unif"] * 30, 885.0),
+    "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256),
+}
+CFG = CONFIGS["c4"]
+ROWS = CFG.rows
 
 
 def set_config(name: str):
-    """c2 (the default) or c4 (configs[3], the multi-GPU scaling config: 100,000,000 rows
-    x 256 N(0,1) features, target = a random 32-feature linear function + N(0,1) noise, L2 regression, 255 bins,
-    255 leaves)."""
-    global CONFIG, ROWS, GAUSSIAN, UNIFORM, FEATURES, PARAMS
-    CONFIG = name
-    if name == "c4":
-        ROWS, GAUSSIAN, UNIFORM = 100_000_000, 256, 0
-        PARAMS = dict(objective="regression", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
-    else:
-        ROWS, GAUSSIAN, UNIFORM = 10_000_000, 70, 30
-        PARAMS = dict(objective="binary", num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
-    FEATURES = GAUSSIAN + UNIFORM
-METRIC = "boosting iters/sec + histogram rows·feats/sec (HBM % peak) at 1/2/4/8 B200"
-# DRAM bytes (read + write) the tree kernel moved per training row in one launch, from an ncu capture of a smaller
-# case of the same workload (2M rows; the traffic grows with the rows): profiles/grow_tree_kernel_2m.md. Per config;
-# none captured for c4.
-TREE_TRAFFIC_PER_ROW = {"c2": 885, "c4": None}
+    global CFG, ROWS
+    CFG = CONFIGS[name]
+    ROWS = CFG.rows
+
+
+def set_rows(rows: int):
+    global ROWS
+    ROWS = rows
+
+
+def params_dict(num_iterations: int) -> dict:
+    return dict(objective=CFG.objective, num_leaves=CFG.num_leaves, learning_rate=0.1, num_grad_quant_bins=4,
+                num_iterations=num_iterations)
 
 
 # ---- synthetic data (torch on the GPU as plumbing) ------------------------------------------------------------
@@ -94,104 +126,159 @@ def _unit(stream: int, rows):
     return (h >> 8).to(torch.float64) / 16777216.0
 
 
-def features_of(rows, device):
-    """[len(rows), 100] f32: features 0..69 ~ N(0,1) (Box-Muller), 70..99 ~ U[0,1)."""
+def _gauss(stream: int, rows):
+    """N(0, 1) by Box-Muller from two counter-hash uniforms (streams `stream`, `stream` + 1)."""
     import torch
 
-    out = torch.empty((rows.numel(), FEATURES), dtype=torch.float32, device=device)
-    for f in range(GAUSSIAN):
-        u1 = 1.0 - _unit(2 * f, rows)
-        u2 = _unit(2 * f + 1, rows)
-        out[:, f] = (torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2.0 * torch.pi * u2)).to(torch.float32)
-    for f in range(GAUSSIAN, FEATURES):
-        out[:, f] = _unit(1000 + f, rows).to(torch.float32)
+    u1 = 1.0 - _unit(stream, rows)
+    u2 = _unit(stream + 1, rows)
+    return torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2.0 * torch.pi * u2)
+
+
+def column(f: int, rows):
+    """Feature f of `rows` (f64): kind "gauss" ~ N(0,1) (streams 2f, 2f+1), "unif" ~ U[0,1) (stream 1000 + f)."""
+    kind = CFG.kinds[f]
+    if kind == "gauss":
+        return _gauss(2 * f, rows)
+    if kind == "unif":
+        return _unit(1000 + f, rows)
+    raise ValueError(kind)
+
+
+def features_of(rows, device):
+    """[len(rows), features] f32."""
+    import torch
+
+    out = torch.empty((rows.numel(), CFG.features), dtype=torch.float32, device=device)
+    for f in range(CFG.features):
+        out[:, f] = column(f, rows).to(torch.float32)
     return out
 
 
-def labels_of(rows, x):
-    """c2: Bernoulli(sigmoid(sparse linear in 12 features + 3 pairwise interactions)); c4: a linear function of 32
-    random features + N(0,1) noise."""
+def labels_of(rows):
+    """The config's label, computing only the features it depends on.
+    c1: 8 random-weight features + 0.5 x0 x1 + N(0, 0.1); c2: Bernoulli(sigmoid(sparse linear in 12 features + 3
+    pairwise interactions)); c4: a linear function of 32 random features + N(0, 1)."""
     import torch
 
-    g = np.random.default_rng(SEED)
-    if CONFIG == "c4":
-        picked = g.choice(FEATURES, size=32, replace=False)
-        weights = g.normal(0.0, 1.0, size=32)
-        y = torch.zeros(rows.numel(), dtype=torch.float64, device=x.device)
+    x = lambda f: column(int(f), rows).to(torch.float32).double()  # noqa: E731  (the f32 feature, as binned)
+    if CFG.name == "c1":
+        g = np.random.default_rng(SEED + 1)
+        picked = g.choice(CFG.features, size=8, replace=False)
+        weights = g.normal(0.0, 1.0, size=8)
+        y = torch.zeros(rows.numel(), dtype=torch.float64, device=rows.device)
         for f, w in zip(picked, weights):
-            y += float(w) * x[:, int(f)].double()
-        u1, u2 = 1.0 - _unit(6000, rows), _unit(6001, rows)
-        y += torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2.0 * torch.pi * u2)
+            y += float(w) * x(f)
+        y += 0.5 * x(0) * x(1) + 0.1 * _gauss(6000, rows)
         return y.to(torch.float32)
-    picked = g.choice(FEATURES, size=12, replace=False)
+    g = np.random.default_rng(SEED)
+    if CFG.name == "c4":
+        picked = g.choice(CFG.features, size=32, replace=False)
+        weights = g.normal(0.0, 1.0, size=32)
+        y = torch.zeros(rows.numel(), dtype=torch.float64, device=rows.device)
+        for f, w in zip(picked, weights):
+            y += float(w) * x(f)
+        y += _gauss(6000, rows)
+        return y.to(torch.float32)
+    picked = g.choice(CFG.features, size=12, replace=False)
     weights = g.normal(0.0, 1.0, size=12)
-    pairs = g.choice(FEATURES, size=(3, 2), replace=False)
-    logit = torch.zeros(rows.numel(), dtype=torch.float64, device=x.device)
+    pairs = g.choice(CFG.features, size=(3, 2), replace=False)
+    logit = torch.zeros(rows.numel(), dtype=torch.float64, device=rows.device)
     for f, w in zip(picked, weights):
-        logit += float(w) * x[:, int(f)].double()
+        logit += float(w) * x(f)
     for a, b in pairs:
-        logit += 0.8 * x[:, int(a)].double() * x[:, int(b)].double()
+        logit += 0.8 * x(a) * x(b)
     p = torch.sigmoid(logit)
     return (_unit(5000, rows) < p).to(torch.float32)
 
 
-def bin_bounds(device):
-    """Equal-frequency upper bounds per feature from the first SAMPLE_ROWS rows (ascending, last +inf)."""
+def bin_mappers(device):
+    """Per feature: equal-frequency upper bounds (ascending, duplicates dropped, the last +inf) from the first
+    SAMPLE_ROWS rows, and the sample's min and max."""
     import torch
 
-    rows = torch.arange(SAMPLE_ROWS, dtype=torch.int64, device=device)
-    x = features_of(rows, device).double()
-    srt, _ = torch.sort(x, dim=0)
-    k = torch.arange(1, MAX_BIN, device=device)
-    cut = (k * SAMPLE_ROWS) // MAX_BIN
-    bounds = (srt[cut - 1] + srt[cut]) / 2.0
-    bounds = torch.cat([bounds, torch.full((1, FEATURES), float("inf"), device=device, dtype=torch.float64)])
-    return bounds.T.contiguous()  # [FEATURES, MAX_BIN]
+    n = min(SAMPLE_ROWS, max(ROWS, 1))
+    rows = torch.arange(n, dtype=torch.int64, device=device)
+    k = torch.arange(1, CFG.max_bin, device=device)
+    cut = (k * n) // CFG.max_bin
+    out = []
+    for f in range(CFG.features):
+        srt, _ = torch.sort(column(f, rows).to(torch.float32).double())
+        bounds = ((srt[cut - 1] + srt[cut]) / 2.0).cpu().numpy()
+        bounds = np.unique(bounds[np.isfinite(bounds)])
+        out.append((np.append(bounds, np.inf), float(srt[0]), float(srt[-1])))
+    return out
+
+
+def dataset_layout(mappers):
+    """silvic's group layout of the config's features (data/build.rs:336-382): features in order, a new group
+    when the next feature's bins would take the group past 8192."""
+    from silvic_b200.dataset import FeatureGroup, FeatureMeta
+
+    features, groups, members, offset, group_bins = [], [], [], 0, 0
+    for f, (ub, lo, hi) in enumerate(mappers):
+        nb = len(ub)
+        if members and group_bins + nb > 8192:
+            groups.append(members)
+            members, group_bins = [], 0
+        features.append(FeatureMeta(name=f"Column_{f}", num_bins=nb, upper_bounds=ub, min_value=lo, max_value=hi,
+                                    group=len(groups), column=len(members), hist_offset=offset))
+        members.append(f)
+        group_bins += nb
+        offset += nb
+    if members:
+        groups.append(members)
+    out = []
+    for gi, feats in enumerate(groups):
+        hist_offset = features[feats[0]].hist_offset
+        total = sum(features[f].num_bins for f in feats)
+        out.append(FeatureGroup(feats, (len(feats) + 3) // 4 * 4, hist_offset, total, np.zeros((0, 4), np.uint8)))
+    return features, out, offset
 
 
 def build_dataset(begin: int, end: int, device, chunk: int = 2_000_000):
-    """Rows begin..end binned into silvic's group layout on the GPU, returned as host arrays."""
+    """Rows begin..end in silvic's group layout, in page-locked host memory (the load's host-to-device copies run at
+    DMA speed and count in the e2e time). On a GPU the rows are binned by the product (sb2_bin_dense); without one
+    (the CPU tests of the bench's sharding) by torch.bucketize, which counts the same bounds."""
     import torch
 
-    from silvic_b200.dataset import BinnedDataset, FeatureGroup, FeatureMeta
+    from silvic_b200.dataset import BinnedDataset, FeatureGroup
 
-    bounds = bin_bounds(device)
+    mappers = bin_mappers(device)
+    features, shells, total_bins = dataset_layout(mappers)
     n = end - begin
-    per_group = 8192 // MAX_BIN  # 32 features of 255 bins per group (data/build.rs:336-382)
-    group_feats = [list(range(s, min(s + per_group, FEATURES))) for s in range(0, FEATURES, per_group)]
-    strides = [(len(g) + 3) // 4 * 4 for g in group_feats]
-    # Page-locked host arrays: the load's host-to-device copies run at DMA speed (and count in the e2e time).
     pin = torch.cuda.is_available()
-    pinned = [torch.empty((n, s), dtype=torch.uint8, pin_memory=pin) for s in strides]
+    pinned = [torch.empty((n, g.row_stride), dtype=torch.uint8, pin_memory=pin) for g in shells]
     pinned.append(torch.empty(n, dtype=torch.float32, pin_memory=pin))
     host = [t.numpy() for t in pinned[:-1]]
     label = pinned[-1].numpy()
-    b32 = bounds.to(torch.float32)
-    for lo in range(0, n, chunk):
-        hi = min(n, lo + chunk)
-        rows = torch.arange(begin + lo, begin + hi, dtype=torch.int64, device=device)
-        x = features_of(rows, device)
-        label[lo:hi] = labels_of(rows, x).cpu().numpy()
-        xt = x.T.contiguous()
-        binned = torch.empty((FEATURES, hi - lo), dtype=torch.uint8, device=device)
-        for f in range(FEATURES):
-            # the first bin whose upper bound is >= value (BinMapper::value_to_bin, data/bin_mapper.rs:344-360)
-            binned[f] = torch.bucketize(xt[f], b32[f], right=False).to(torch.uint8)
-        for gi, feats in enumerate(group_feats):
-            blk = torch.zeros((hi - lo, strides[gi]), dtype=torch.uint8, device=device)
-            blk[:, : len(feats)] = binned[feats].T
-            host[gi][lo:hi] = blk.cpu().numpy()
-    features, groups, offset = [], [], 0
-    ub = bounds.cpu().numpy()
-    for gi, feats in enumerate(group_feats):
-        hist_offset = offset
-        for col, f in enumerate(feats):
-            features.append(FeatureMeta(name=f"Column_{f}", num_bins=MAX_BIN, upper_bounds=ub[f].copy(),
-                                        min_value=float(ub[f][0]), max_value=float(ub[f][-2]), group=gi,
-                                        column=col, hist_offset=offset))
-            offset += MAX_BIN
-        groups.append(FeatureGroup(feats, strides[gi], hist_offset, len(feats) * MAX_BIN, host[gi]))
-    data = BinnedDataset(n, begin, features, groups, offset, label)
+    binner = None
+    if device.type == "cuda":
+        from silvic_b200 import B200Backend
+
+        binner = B200Backend(device.index or 0)
+    try:
+        for lo in range(0, n, chunk):
+            hi = min(n, lo + chunk)
+            rows = torch.arange(begin + lo, begin + hi, dtype=torch.int64, device=device)
+            x = features_of(rows, device)
+            label[lo:hi] = labels_of(rows).cpu().numpy()
+            if binner is not None:
+                binner.bin_dense(x, features, shells, out=[h[lo:hi] for h in host])
+            else:
+                for gi, g in enumerate(shells):
+                    blk = torch.zeros((hi - lo, g.row_stride), dtype=torch.uint8)
+                    for col, f in enumerate(g.features):
+                        ub = torch.from_numpy(features[f].upper_bounds).to(torch.float64)
+                        blk[:, col] = torch.bucketize(x[:, f].double(), ub, right=False).to(torch.uint8)
+                    host[gi][lo:hi] = blk.numpy()
+            del x
+    finally:
+        if binner is not None:
+            binner.close()
+    groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, host[gi])
+              for gi, g in enumerate(shells)]
+    data = BinnedDataset(n, begin, features, groups, total_bins, label)
     data._keep.extend(pinned)
     return data
 
@@ -201,10 +288,9 @@ def all_labels(device):
     import torch
 
     out = np.empty(ROWS, dtype=np.float32)
-    for lo in range(0, ROWS, 2_000_000):
-        hi = min(ROWS, lo + 2_000_000)
-        rows = torch.arange(lo, hi, dtype=torch.int64, device=device)
-        out[lo:hi] = labels_of(rows, features_of(rows, device)).cpu().numpy()
+    for lo in range(0, ROWS, 4_000_000):
+        hi = min(ROWS, lo + 4_000_000)
+        out[lo:hi] = labels_of(torch.arange(lo, hi, dtype=torch.int64, device=device)).cpu().numpy()
     return out
 
 
@@ -275,8 +361,9 @@ def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, m
     The root histogram reads every row's bins and packed gradient (its rows are in row order: no row ids) and writes
     a histogram of `total_bins` [g, h] int32 pairs. Split k of a parent of P rows reads each row's id (not for the
     root's rows), packed gradient and byte of the split feature, and writes id and gradient to the other partition
-    buffer; while more splits may follow (k + 2 < max_leaves) it also histograms the smaller child's B rows: their ids,
-    gradients and bins, and the histogram out. Split k is internal node k (nodes are numbered in split order).
+    buffer (n·(4+1+4) read, 8 written); while more splits may follow (k + 2 < max_leaves) it also histograms the
+    smaller child's B rows: their ids, gradients and bins, and the histogram out. Split k is internal node k (nodes
+    are numbered in split order).
     """
     def count(c: int) -> int:
         return (int(tree.internal_count[c]) if c >= 0 else int(tree.leaf_count[~c])) // world
@@ -291,35 +378,43 @@ def tree_algorithmic_bytes(tree, n_rows: int, row_bytes: int, total_bins: int, m
     return total
 
 
-def oracle_rate(data, iterations: int, params) -> tuple[float, list[float], int]:
+def oracle_params(num_iterations: int):
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as orc
+    from silvic_b200 import _abi
+
+    objective = {"regression": _abi.REGRESSION, "binary": _abi.BINARY}[CFG.objective]
+    return orc.default_params(objective=objective, num_leaves=CFG.num_leaves, learning_rate=0.1,
+                              num_grad_quant_bins=4, num_iterations=num_iterations)
+
+
+def oracle_train(data, iterations: int):
+    """The CPU oracle's trainer on `data` (test infrastructure: the bench's CPU legs only)."""
     sys.path.insert(0, str(ROOT / "tests"))
     import oracle_lib as orc
 
-    p = orc.default_params(**params)
-    p.num_iterations = iterations
-    m = orc.train([data], p)
-    secs = m.iteration_seconds
-    return len(secs) / sum(secs), secs, orc.lib().orc_num_threads()
+    m = orc.train([data], oracle_params(iterations))
+    return m, orc.lib().orc_num_threads()
 
 
-def oracle_params():
-    from silvic_b200 import _abi
+def parity_of(model, ref, data) -> dict:
+    """The device model's first trees against the oracle's trees of the same dataset: every tree field bit for bit,
+    the initial score, and the LightGBM model text of those trees byte for byte."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle_lib as orc
+    from silvic_b200.backend import Model
 
-    objective = _abi.REGRESSION if PARAMS["objective"] == "regression" else _abi.BINARY
-    return dict(objective=objective, num_leaves=255, learning_rate=0.1, num_grad_quant_bins=4)
-
-
-def set_rows(rows: int):
-    global ROWS
-    ROWS = rows
-
-
-def workload() -> str:
-    if CONFIG == "c4":
-        size = "100M" if ROWS == 100_000_000 else f"{ROWS:,} rows (reduced)"
-        return f"configs[3]: L2 regression {size} x 256, 255 bins, 255 leaves"
-    size = "10M" if ROWS == 10_000_000 else f"{ROWS:,} rows (reduced)"
-    return f"configs[1]: binary {size} x 100, 255 bins, 255 leaves"
+    k = len(ref.trees)
+    mine = model.trees[:k]
+    differs = [f"tree {i}: {','.join(d)}" for i, (t, r) in enumerate(zip(mine, ref.trees))
+               if (d := orc.trees_equal(t, r))]
+    p = oracle_params(k)
+    text_dev = Model(mine, model.init_score, []).to_lightgbm_string(data, p)
+    text_ref = Model(ref.trees, ref.init_score, []).to_lightgbm_string(data, p)
+    return {"trees": k, "trees_identical": len(mine) == k and not differs,
+            "init_score_identical": model.init_score == ref.init_score,
+            "model_text_identical": text_dev == text_ref, "differences": differs[:5],
+            "against": "CPU oracle (oracle/oracle.cpp) on the whole dataset"}
 
 
 def run_reference(args, rank: int, world: int):
@@ -329,27 +424,56 @@ def run_reference(args, rank: int, world: int):
 
     data = build_dataset(0, ROWS, torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu"))
     # Warm-up iteration, then as many timed iterations (up to --steps) as fit a ~60 s CPU budget.
-    warm_rate, warm_secs, cores = oracle_rate(data, max(1, min(args.warmup, 1)), oracle_params())
-    per_iter = max(warm_secs)
+    warm, _ = oracle_train(data, 1)
+    per_iter = max(warm.iteration_seconds)
     k = int(max(1, min(args.steps, 60.0 // max(per_iter, 1e-3))))
-    rate, secs, cores = oracle_rate(data, k, oracle_params())
-    sample = f"{len(secs)} boosting iterations of the full {ROWS:,} x 100 set on {cores} threads"
+    m, cores = oracle_train(data, k)
+    secs = m.iteration_seconds
+    rate = len(secs) / sum(secs)
+    sample = f"{len(secs)} boosting iterations of the full {ROWS:,} x {CFG.features} set on {cores} threads"
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "iters/s", "n_gpus": world,
             "steps": args.steps, "timed_steps": len(secs), "warmup": args.warmup,
             "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int32 histograms / f64 split search", "data": "synthetic",
-            "config": {"workload": workload(), "rows": ROWS,
-                       "features": FEATURES, "num_leaves": 255},
+            "config": {"workload": CFG.describe(ROWS), "rows": ROWS, "features": CFG.features,
+                       "num_leaves": CFG.num_leaves},
             "cpu_baseline": {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": rate, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def _max_over_ranks(values: list[float], world: int, dev) -> list[float]:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def _joined_backend(local: int, data, params, rank: int, world: int) -> tuple[object, float, float]:
+    """A fresh handle with `data` loaded and, with ranks, joined: (backend, load seconds, join seconds)."""
+    import torch.distributed as dist
+
+    from silvic_b200 import B200Backend
+
+    t0 = time.perf_counter()
+    b = B200Backend(local)
+    b.load(data, params.objective, params.sigmoid)
+    t1 = time.perf_counter()
+    if world > 1:
+        uid = [B200Backend.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        b.join_ranks(uid[0], world, rank)
+    return b, t1 - t0, time.perf_counter() - t1
 
 
 def run_b200(args, rank: int, world: int):
     import torch
     import torch.distributed as dist
 
-    from silvic_b200 import B200Backend, init_score, params_from_dict
+    from silvic_b200 import init_score, params_from_dict
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -358,20 +482,11 @@ def run_b200(args, rank: int, world: int):
     data = build_dataset(begin, end, dev)
     labels = all_labels(dev) if world > 1 else data.label
     torch.cuda.synchronize()
-    params = params_from_dict(dict(PARAMS, num_iterations=args.warmup + args.steps))
+    params = params_from_dict(params_dict(args.warmup + args.steps))
     score0 = init_score(params, labels)
 
-    def make_backend():
-        b = B200Backend(local)
-        b.load(data, params.objective, params.sigmoid)
-        if world > 1:
-            uid = [B200Backend.nccl_unique_id() if rank == 0 else None]
-            dist.broadcast_object_list(uid, src=0)
-            b.join_ranks(uid[0], world, rank)
-        return b
-
     # Device-timed run: per-iteration CUDA events; the last `steps` iterations are the timed region.
-    backend = make_backend()
+    backend, _, _ = _joined_backend(local, data, params, rank, world)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -380,41 +495,33 @@ def run_b200(args, rank: int, world: int):
     torch.cuda.synchronize()
     secs = model.iteration_seconds
     timed = float(sum(secs[args.warmup:args.warmup + args.steps]))
-    trees = len(model.trees)
-    # The tree kernel's own launches in the timed region (one GPU: one cooperative launch per tree, CUDA events on
-    # the backend's stream around each).
+    # The tree kernel's own launches in the timed region (one cooperative launch per tree, CUDA events on the
+    # backend's stream around each).
     tree_s = model.tree_seconds[args.warmup:args.warmup + args.steps]
     timed_trees = model.trees[args.warmup:args.warmup + args.steps]
-    # The standalone root histogram (every row, every feature), the kernel the multi-GPU path runs per split.
+    # The standalone root histogram (every row, every feature).
     hist_s = backend.time_histogram(10)
     backend.close()
-    launches_persistent = bool(model.tree_seconds)  # each tree in one cooperative launch (per GPU)
-    t = torch.tensor([timed, hist_s], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    timed, hist_s = float(t[0]), float(t[1])
+    launches_persistent = bool(model.tree_seconds)
+    timed, hist_s = _max_over_ranks([timed, hist_s], world, dev)
 
-    # End to end through the C ABI with host buffers: load (host -> device) + train + trees back.
-    e2e_params = params_from_dict(dict(PARAMS, num_iterations=args.steps))
+    # End to end through the C ABI with host buffers: a whole job of the config's trees, setup included.
+    e2e_params = params_from_dict(params_dict(args.trees or CFG.trees))
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    b2 = B200Backend(local)
-    b2.load(data, e2e_params.objective, e2e_params.sigmoid)
-    if world > 1:
-        uid = [B200Backend.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        b2.join_ranks(uid[0], world, rank)
+    b2, load_s, join_s = _joined_backend(local, data, e2e_params, rank, world)
+    t1 = time.perf_counter()
     m2 = b2.train(e2e_params, score0)
     e2e_s = time.perf_counter() - t0
+    train_s = time.perf_counter() - t1
     b2.close()
-    e = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e, op=dist.ReduceOp.MAX)
-    e2e_s = float(e[0])
+    e2e_s, load_s, join_s, train_s = _max_over_ranks([e2e_s, load_s, join_s, train_s], world, dev)
+    e2e_trees = len(m2.trees)
     h2d = sum(g.data.nbytes for g in data.groups) + data.label.nbytes
     d2h = sum(sum(getattr(t_, f).nbytes for f in t_.FIELDS) for t_ in m2.trees)
-
+    del m2
+    # Every collective is done: the other ranks leave while rank 0 checks parity on the CPU.
     if rank != 0:
         return
     n_local = end - begin
@@ -428,15 +535,15 @@ def run_b200(args, rank: int, world: int):
     hist_roofline["frac"] = hist_roofline["achieved"] / peak
     if tree_s and len(tree_s) == len(timed_trees):
         # The dominant kernel: the persistent tree kernel, one launch per tree.
-        tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, PARAMS["num_leaves"], world) for tr in timed_trees]
+        tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, CFG.num_leaves, world) for tr in timed_trees]
         launch_s = sum(tree_s) / len(tree_s)
         per_launch = sum(tree_bytes) / len(tree_bytes)
         roofline = {"bound": "hbm", "achieved": per_launch / launch_s / 1e9, "peak": peak, "unit": "GB/s",
                     "peak_kind": peak_kind,
-                    "traffic": None if TREE_TRAFFIC_PER_ROW[CONFIG] is None else TREE_TRAFFIC_PER_ROW[CONFIG] * n_local,
+                    "traffic": None if CFG.traffic_per_row is None else CFG.traffic_per_row * n_local,
                     "kernel": "grow_tree_kernel (one cooperative launch grows one tree)",
                     "launch_ms": launch_s * 1000.0, "algorithmic_bytes": per_launch,
-                    "share_of_step": sum(tree_s) / timed, "root_histogram": hist_roofline}
+                    "share_of_step": sum(tree_s) / timed if world == 1 else None, "root_histogram": hist_roofline}
     else:
         roofline = {"bound": "hbm", "achieved": hist_roofline["achieved"], "peak": peak, "unit": "GB/s",
                     "peak_kind": peak_kind, "traffic": None, "kernel": hist_roofline["kernel"],
@@ -454,75 +561,78 @@ def run_b200(args, rank: int, world: int):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int32 histograms / f64 split search",
-        "data": "synthetic",
-        "config": {"workload": workload(), "rows": ROWS,
-                   "features": FEATURES, "num_leaves": 255, "parallelism": f"rows sharded over {world} GPU(s)",
+        "data": "synthetic (counter-hash features; equal-frequency bins of the first 200,000 rows)",
+        "config": {"workload": CFG.describe(ROWS), "rows": ROWS, "features": CFG.features,
+                   "num_leaves": CFG.num_leaves, "parallelism": f"rows sharded over {world} GPU(s)",
                    "l2": f"inputs ({n_local * S / 1e9:.1f} GB binned per GPU) larger than L2; no flush"},
-        "trees": trees,
-        "hist_rows_feats_per_s": n_local * FEATURES / hist_s * world,
+        "trees": len(model.trees),
+        "hist_rows_feats_per_s": n_local * CFG.features / hist_s * world,
         "roofline": roofline,
         "clocks": clocks.summary(),
-        "e2e": {"value": args.steps / e2e_s, "unit": "iters/s", "h2d_bytes_per_step": h2d // args.steps,
-                "d2h_bytes_per_step": d2h // args.steps},
+        "e2e": {"value": e2e_trees / e2e_s, "unit": "iters/s", "trees": e2e_trees, "seconds": e2e_s,
+                "h2d_bytes_per_step": h2d // e2e_trees, "d2h_bytes_per_step": d2h // e2e_trees,
+                "setup_seconds": {"load": load_s, "join_ranks": join_s}, "train_seconds": train_s},
         # Our kernels per iteration: gradients, iteration start (quantize), the tree (one persistent launch, or
         # histogram + reduction + search for the root and partition flags + scatter + histogram + reduction + search
         # per split with NCCL ranks), leaf map + leaf sums, finalize, score update.
-        "gpu_launches": args.steps * (7 if launches_persistent else 3 + 3 + 5 * (PARAMS["num_leaves"] - 1) + 4),
+        "gpu_launches": args.steps * (7 if launches_persistent else 3 + 3 + 5 * (CFG.num_leaves - 1) + 4),
     }
-    if world == 1 and not args.no_cpu_baseline:
-        rate, secs, cores = oracle_rate(data, 2, oracle_params())
-        line["cpu_baseline"] = {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port",
-                                "sample": f"2 boosting iterations of the same {ROWS:,} x {FEATURES} dataset, "
-                                          f"{sum(secs):.1f} s on {cores} threads"}
+    if not args.no_parity:
+        # The oracle trains the first trees of the same job on the whole dataset (on one rank: the same data; with
+        # ranks, rank 0 builds every rank's rows). Its time is also the CPU baseline at N = 1.
+        full = data if world == 1 else build_dataset(0, ROWS, dev)
+        ref, cores = oracle_train(full, PARITY_TREES)
+        line["parity"] = parity_of(model, ref, full)
+        if world == 1:
+            secs_ref = ref.iteration_seconds
+            line["cpu_baseline"] = {"value": len(secs_ref) / sum(secs_ref), "unit": "iters/s", "cores": cores,
+                                    "kind": "port",
+                                    "sample": f"{len(secs_ref)} boosting iterations of the same {ROWS:,} x "
+                                              f"{CFG.features} dataset, {sum(secs_ref):.1f} s on {cores} threads"}
     print(json.dumps(line), flush=True)
 
 
 def run_binning(args):
     """The device binning of a dense matrix (`sb2_bin_dense`, data/binning.rs bin_rows) on the config's raw
-    features: a device-resident f32 matrix into the dataset's groups of 32 features, timed from the call until the
-    group rows are in host memory (wall clock: the copy of the rows back is part of the job). One line of JSON."""
+    features: a device-resident f32 matrix into the dataset's groups, timed from the call until the group rows are
+    in host memory (wall clock: the copy of the rows back is part of the job). One line of JSON."""
     import torch
 
     from silvic_b200.backend import B200Backend
-    from silvic_b200.dataset import FeatureGroup, FeatureMeta
 
     dev = torch.device("cuda", 0)
-    bounds = bin_bounds(dev).cpu().numpy()
-    x = features_of(torch.arange(ROWS, dtype=torch.int64, device=dev), dev)
-    per_group = 8192 // MAX_BIN
-    feats, groups = [], []
-    for gi, start in enumerate(range(0, FEATURES, per_group)):
-        members = list(range(start, min(FEATURES, start + per_group)))
-        groups.append(FeatureGroup(members, (len(members) + 3) // 4 * 4, 0, 0, np.zeros((0, 4), np.uint8)))
-        for col, f in enumerate(members):
-            feats.append(FeatureMeta(name=f"Column_{f}", num_bins=MAX_BIN, upper_bounds=bounds[f].copy(), group=gi,
-                                     column=col))
+    rows = min(ROWS, 10_000_000)
+    features, groups, _ = dataset_layout(bin_mappers(dev))
+    x = features_of(torch.arange(rows, dtype=torch.int64, device=dev), dev)
     b = B200Backend(0)
     times = []
     for it in range(args.warmup + args.steps):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        b.bin_dense(x, feats, groups)
+        b.bin_dense(x, features, groups)
         if it >= args.warmup:
             times.append(time.perf_counter() - t0)
     b.close()
     s = sum(times) / len(times)
-    print(json.dumps({"binning": {"rows": ROWS, "features": FEATURES, "ms": s * 1e3,
-                                  "values_per_s": ROWS * FEATURES / s, "input": "device f32 row-major",
+    print(json.dumps({"binning": {"rows": rows, "features": CFG.features, "ms": s * 1e3,
+                                  "values_per_s": rows * CFG.features / s, "input": "device f32 row-major",
                                   "output": "host group rows", "steps": args.steps, "warmup": args.warmup}}))
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c2", choices=["c2", "c4"],
-                    help="c2 (default): BASELINE configs[1]; c4: configs[3], the 100M-row scaling config")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle's trees (parity and, at N = 1, the CPU baseline)")
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS),
+                    help="c4 (default): BASELINE configs[3], 100M rows; c1: configs[0]; c2: configs[1]")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows of the synthetic set (a smaller case for profiling; default: the config's)")
+    ap.add_argument("--trees", type=int, default=0,
+                    help="trees of the end-to-end job (default: the config's full count)")
     ap.add_argument("--binning", action="store_true",
                     help="time the device binning of the config's raw features instead of training (one GPU)")
     args = ap.parse_args()

@@ -287,8 +287,10 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
  *   out         one sb2_split_info, written
  *   splittable  num_features bytes, written
  * The call allocates nothing: its scratch is a fixed 320 KiB array in this library's device module, enough for
- * datasets of at most 4096 features; larger ones return SB2_EUNSUPPORTED. The first call on each device looks up
- * that array's address (cudaGetSymbolAddress, which may load the module), so make it before any stream capture.
+ * datasets of at most 4096 features; larger ones return SB2_EUNSUPPORTED. The first call on each handle looks up
+ * that array's address on the handle's device (cudaGetSymbolAddress, which may load the module) and keeps it for
+ * the handle's life, so make that first call before any stream capture. A cudaDeviceReset ends the handle with
+ * the rest of its device memory; a handle created afterwards looks the address up again.
  * The call runs on the handle's stream and returns once the results are written; the caller's writes to `hist`
  * and `evaluate` must be complete before it. All calls on one device share the one scratch array: calls that
  * overlap (from other threads, or other handles on the same device) race and give wrong results. */
@@ -301,6 +303,14 @@ int sb2_find_best_split_noalloc(sb2_backend* b, const int32_t* hist, size_t len,
  * division that pipelines, where the library's runs its calls one after another). Compares it with CUDA's correctly
  * rounded division on `count` operand pairs hashed from `seed` and returns the pairs where they differ. */
 int sb2_check_division(sb2_backend* b, uint64_t count, uint32_t seed, uint64_t* mismatches);
+
+/* No counterpart in the reference: test access to the tree kernel's failure detection, the analogue of the
+ * reference's hung-rank test (crates/silvic-net/tests/ring.rs:338). With `spin_limit` > 0, the single-rank handle
+ * trains as rank 0 of two ranks whose other rank never answers: its exchange buffer is local memory that nothing
+ * writes, so the first wait for its histogram bins gives up after `spin_limit` polls and sb2_train returns
+ * SB2_ECOLLECTIVE. No GPU fault is involved: every wait is bounded and the kernel returns. `spin_limit` 0 makes the
+ * handle one rank again. Not for a handle that joined ranks. */
+int sb2_test_unanswered_peer(sb2_backend* b, uint32_t spin_limit);
 
 /* ---- measurement -------------------------------------------------------------------------------------------- */
 
@@ -346,7 +356,15 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
 
 /* An NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */
 int sb2_nccl_unique_id(uint8_t* out, size_t len);
-/* Joins `world` ranks (one process per GPU) through an NCCL communicator; call after sb2_load on every rank. */
+/* How the tree kernel's ranks exchange their histograms (no counterpart in the reference, whose ranks allreduce each
+ * split's histogram over TCP, learner.rs:189-220): SB2_EXCHANGE_AUTO (the default) pushes each split's bins over
+ * NVLink inside the tree kernel when every rank can map every other rank's buffer (CUDA IPC), else falls back to
+ * SB2_EXCHANGE_NCCL: per-step launches with an ncclAllReduce of each split's histogram, in one CUDA graph per
+ * iteration. Both give the same trees. Call before sb2_join_ranks, with the same mode on every rank. */
+enum { SB2_EXCHANGE_AUTO = 0, SB2_EXCHANGE_NCCL = 1 };
+int sb2_set_rank_exchange(sb2_backend* b, int mode);
+/* Joins `world` ranks (one process per GPU) through an NCCL communicator; call after sb2_load on every rank. It also
+ * maps every rank's exchange buffer (CUDA IPC) for the tree kernel's histogram exchange over NVLink. Collective. */
 int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int world, int rank);
 
 /* ---- device-resident training: boosting::train (crates/silvic-core/src/boosting.rs:63-149) ------------------ */

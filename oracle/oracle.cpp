@@ -26,6 +26,9 @@
 #include <string>
 #include <vector>
 
+#include <condition_variable>
+#include <functional>
+#include <mutex>
 #include <thread>
 
 namespace {
@@ -36,6 +39,85 @@ thread_local std::string g_error;
 
 int g_threads = static_cast<int>(std::max(1u, std::thread::hardware_concurrency()));
 
+// A pool of worker threads kept for the process: a parallel call hands every worker one job and waits for all of
+// them, so a call costs two condition-variable round trips instead of creating and joining threads (the trainer makes
+// thousands of calls per tree, the reference's rayon pool none of that cost either). Calls come from one thread.
+class Pool {
+public:
+    // Runs job(k) for k in [0, t) on t threads (the caller's among them) and returns when all are done.
+    void run(size_t t, const std::function<void(size_t)>& job) {
+        if (t <= 1 || inside_) {  // a call from inside a job runs its parts on the calling thread
+            for (size_t k = 0; k < t; ++k) job(k);
+            return;
+        }
+        grow(t - 1);
+        {
+            std::lock_guard<std::mutex> g(lock_);
+            job_ = &job;
+            active_ = t - 1;
+            pending_ = t - 1;
+            ++generation_;
+        }
+        wake_.notify_all();
+        inside_ = true;
+        job(0);
+        inside_ = false;
+        std::unique_lock<std::mutex> g(lock_);
+        done_.wait(g, [&] { return pending_ == 0; });
+        job_ = nullptr;
+    }
+    ~Pool() {
+        {
+            std::lock_guard<std::mutex> g(lock_);
+            stop_ = true;
+        }
+        wake_.notify_all();
+        for (std::thread& th : workers_) th.join();
+    }
+
+private:
+    void grow(size_t n) {
+        while (workers_.size() < n) {
+            const size_t index = workers_.size() + 1;  // job index of the worker; 0 is the caller
+            workers_.emplace_back([this, index] { loop(index); });
+        }
+    }
+    void loop(size_t index) {
+        uint64_t seen = 0;
+        while (true) {
+            const std::function<void(size_t)>* job;
+            {
+                std::unique_lock<std::mutex> g(lock_);
+                wake_.wait(g, [&] { return stop_ || generation_ != seen; });
+                if (stop_) return;
+                seen = generation_;
+                if (index > active_) continue;  // this call needs fewer workers
+                job = job_;
+            }
+            inside_ = true;
+            (*job)(index);
+            inside_ = false;
+            std::lock_guard<std::mutex> g(lock_);
+            if (--pending_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex lock_;
+    std::condition_variable wake_, done_;
+    const std::function<void(size_t)>* job_ = nullptr;
+    size_t active_ = 0, pending_ = 0;
+    uint64_t generation_ = 0;
+    bool stop_ = false;
+    static thread_local bool inside_;
+};
+
+thread_local bool Pool::inside_ = false;
+
+Pool& pool() {
+    static Pool p;
+    return p;
+}
+
 // Runs body(i) for every i in [0, n), each thread over one contiguous range.
 template <class F>
 void parallel_for(size_t n, F&& body) {
@@ -44,13 +126,10 @@ void parallel_for(size_t n, F&& body) {
         for (size_t i = 0; i < n; ++i) body(i);
         return;
     }
-    std::vector<std::thread> pool;
-    for (size_t k = 0; k < t; ++k)
-        pool.emplace_back([&, k] {
-            size_t b = n * k / t, e = n * (k + 1) / t;
-            for (size_t i = b; i < e; ++i) body(i);
-        });
-    for (std::thread& th : pool) th.join();
+    pool().run(t, [&](size_t k) {
+        size_t b = n * k / t, e = n * (k + 1) / t;
+        for (size_t i = b; i < e; ++i) body(i);
+    });
 }
 
 // Runs body(i) for every i in [0, n), items claimed one at a time (uneven work).
@@ -62,12 +141,9 @@ void parallel_tasks(size_t n, F&& body) {
         return;
     }
     std::atomic<size_t> next{0};
-    std::vector<std::thread> pool;
-    for (size_t k = 0; k < t; ++k)
-        pool.emplace_back([&] {
-            for (size_t i = next.fetch_add(1); i < n; i = next.fetch_add(1)) body(i);
-        });
-    for (std::thread& th : pool) th.join();
+    pool().run(t, [&](size_t) {
+        for (size_t i = next.fetch_add(1); i < n; i = next.fetch_add(1)) body(i);
+    });
 }
 
 // Sums (or otherwise combines) per-thread partial results of body(i, partial) over [0, n).
@@ -75,13 +151,10 @@ template <class T, class F, class C>
 T parallel_reduce(size_t n, T init, F&& body, C&& combine) {
     size_t t = std::min<size_t>(static_cast<size_t>(g_threads), std::max<size_t>(1, n / 2048));
     std::vector<T> parts(t, init);
-    std::vector<std::thread> pool;
-    for (size_t k = 0; k < t; ++k)
-        pool.emplace_back([&, k] {
-            size_t b = n * k / t, e = n * (k + 1) / t;
-            for (size_t i = b; i < e; ++i) body(i, parts[k]);
-        });
-    for (std::thread& th : pool) th.join();
+    pool().run(t, [&](size_t k) {
+        size_t b = n * k / t, e = n * (k + 1) / t;
+        for (size_t i = b; i < e; ++i) body(i, parts[k]);
+    });
     T out = init;
     for (const T& p : parts) out = combine(out, p);
     return out;

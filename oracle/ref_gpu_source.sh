@@ -3,7 +3,11 @@
 # params.rs:30-53): its CUDA prelude, the shared capacities as #defines, common.h, kernels.kern. The reference's
 # files are read where they lie; the result goes to oracle/_ref/ only (not committed).
 set -e
-REF=${1:-/root/reference}
+if [ -z "$1" ]; then
+  echo "usage: ref_gpu_source.sh <reference checkout> [output]" >&2
+  exit 2
+fi
+REF=$1
 OUT=${2:-_ref/ref_kernels.cuh}
 K="$REF/crates/silvic-gpu/kernels"
 {

@@ -14,6 +14,7 @@ LIBRARY = Path(__file__).resolve().parent / "_lib" / "libsilvic_b200.so"
 OK, ECONFIG, EDATA, EINTERNAL, EDEVICE, ECOLLECTIVE, EMODEL, EUNSUPPORTED = range(8)
 NUMERICAL, CATEGORICAL, TRIVIAL = 0, 1, 2
 REGRESSION, BINARY, LAMBDARANK = 0, 1, 2
+EXCHANGE_AUTO, EXCHANGE_NCCL = 0, 1
 LEFT, RIGHT = 0, 1
 
 ERROR_KINDS = {
@@ -228,6 +229,8 @@ SIGNATURES = {
     "sb2_profile_steps": (C.c_int, [VP, P(Params), C.c_double, P(C.c_double), C.c_size_t, P(C.c_size_t)]),
     "sb2_nccl_unique_id": (C.c_int, [P(C.c_uint8), C.c_size_t]),
     "sb2_join_ranks": (C.c_int, [VP, P(C.c_uint8), C.c_size_t, C.c_int, C.c_int]),
+    "sb2_set_rank_exchange": (C.c_int, [VP, C.c_int]),
+    "sb2_test_unanswered_peer": (C.c_int, [VP, C.c_uint32]),
     "sb2_train": (C.c_int, [VP, P(Params), C.c_double, P(VP)]),
     "sb2_boost_from_average": (C.c_int, [P(Params), P(C.c_float), P(C.c_float), C.c_size_t, P(C.c_double)]),
     "sb2_model_free": (C.c_int, [VP]),

@@ -145,10 +145,11 @@ class B200Backend:
         self._check(self._lib.sb2_load(self._h, C.byref(d), C.byref(obj)))
         self._data = train
 
-    def bin_dense(self, values, features, groups) -> list[np.ndarray]:
+    def bin_dense(self, values, features, groups, out: list[np.ndarray] | None = None) -> list[np.ndarray]:
         """data::binning::bin_rows on the device (`sb2_bin_dense`): `values` (rows × features, float32 or float64,
         C- or Fortran-ordered numpy array, or a CUDA torch tensor) binned with `features`' upper bounds into each of
-        `groups`' rows; returns one uint8 array of rows × row_stride per group."""
+        `groups`' rows; returns one uint8 array of rows × row_stride per group (`out`, when given: C-contiguous
+        arrays of that shape, written in place)."""
         from .dataset import BinnedDataset
 
         ptr, rows, cols, vbytes, row_major, keep = _matrix_view(values)
@@ -156,7 +157,13 @@ class B200Backend:
                                                                       g.total_bins, np.zeros((0, g.row_stride), np.uint8))
                                                         for g in groups], 0, np.zeros(0, np.float32))
         d = shell.c_struct()
-        outs = [np.zeros((rows, g.row_stride), dtype=np.uint8) for g in groups]
+        if out is None:
+            outs = [np.zeros((rows, g.row_stride), dtype=np.uint8) for g in groups]
+        else:
+            outs = list(out)
+            for o, g in zip(outs, groups):
+                if o.shape != (rows, g.row_stride) or o.dtype != np.uint8 or not o.flags.c_contiguous:
+                    raise ValueError(f"output of shape {o.shape}, expected C-contiguous uint8 {(rows, g.row_stride)}")
         ptrs = (C.POINTER(C.c_uint8) * max(len(outs), 1))(*[o.ctypes.data_as(C.POINTER(C.c_uint8)) for o in outs])
         self._check(self._lib.sb2_bin_dense(self._h, ptr, vbytes, rows, cols, int(row_major), d.features,
                                             len(features), d.groups, len(groups), ptrs))
@@ -301,6 +308,14 @@ class B200Backend:
         if code != _abi.OK:
             raise _abi.SilvicError(code, _abi.global_error())
         return bytes(buf)
+
+    def set_rank_exchange(self, mode: int):
+        """sb2_set_rank_exchange: _abi.EXCHANGE_AUTO (NVLink inside the tree kernel) or _abi.EXCHANGE_NCCL."""
+        self._check(self._lib.sb2_set_rank_exchange(self._h, mode))
+
+    def test_unanswered_peer(self, spin_limit: int):
+        """sb2_test_unanswered_peer: train as rank 0 of two whose other rank never answers (0: one rank again)."""
+        self._check(self._lib.sb2_test_unanswered_peer(self._h, spin_limit))
 
     def join_ranks(self, unique_id: bytes, world: int, rank: int):
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)

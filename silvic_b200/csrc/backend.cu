@@ -118,13 +118,23 @@ struct sb2_backend {
     size_t xbytes = 0;
     bool xready = false;
     uint32_t xepoch = 0;  // the last epoch a launch used
+    int exchange_mode = SB2_EXCHANGE_AUTO;
+    uint32_t peer_spins = kPeerSpins;  // polls of a rank's flag before the tree kernel gives up (error 4)
+    // sb2_test_unanswered_peer: a second rank whose exchange buffer is local memory that nothing writes.
+    bool fake_peer = false;
+    DeviceBuffer fake_xbuf;
+
+    // sb2_find_best_split_noalloc's scratch array on this handle's device, looked up by the handle's first such call.
+    void* noalloc_scratch = nullptr;
 
     void close_exchange() {
         for (int r = 0; r < kMaxRanks; ++r)
-            if (r != rank && xpeers[r]) cudaIpcCloseMemHandle(xpeers[r]);
+            if (r != rank && xpeers[r] && !fake_peer) cudaIpcCloseMemHandle(xpeers[r]);
         for (auto& p : xpeers) p = nullptr;
         xready = false;
         xbytes = 0;
+        fake_peer = false;
+        peer_spins = kPeerSpins;
     }
 
     ~sb2_backend() {
@@ -1022,25 +1032,18 @@ namespace {
 constexpr uint32_t kNoAllocMaxFeatures = 4096;
 constexpr size_t kNoAllocCounterBytes = 256;  // the arrival counter, padded so the candidates stay 256-aligned
 constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + sizeof(FeatureCandidate) * kNoAllocMaxFeatures;
-constexpr int kNoAllocMaxDevices = 64;
-
 // [0, 4): the counter, which must be zero when a launch starts (each call clears it); then the candidates.
 static __device__ __align__(256) unsigned char g_noalloc_split_scratch[kNoAllocScratchBytes];
 
-// The scratch's device address on b's device, looked up once per device (with that device current) and kept.
+// The scratch's device address on b's device, looked up with that device current by the handle's first call and kept
+// in the handle: a handle made after a device reset (cudaDeviceReset ends every handle's memory) looks it up again.
 int noalloc_split_scratch(sb2_backend* b, unsigned char** out) {
-    static std::mutex lock;
-    static void* addresses[kNoAllocMaxDevices] = {};
-    if (b->device < 0 || b->device >= kNoAllocMaxDevices)
-        return b->fail(SB2_EUNSUPPORTED, "sb2_find_best_split_noalloc: device " + std::to_string(b->device) +
-                                             " beyond the " + std::to_string(kNoAllocMaxDevices) + " it keeps scratch for");
-    std::lock_guard<std::mutex> guard(lock);
-    if (addresses[b->device] == nullptr) {
+    if (b->noalloc_scratch == nullptr) {
         void* p = nullptr;
         SB2_CUDA(b, cudaGetSymbolAddress(&p, g_noalloc_split_scratch));
-        addresses[b->device] = p;
+        b->noalloc_scratch = p;
     }
-    *out = static_cast<unsigned char*>(addresses[b->device]);
+    *out = static_cast<unsigned char*>(b->noalloc_scratch);
     return SB2_OK;
 }
 
@@ -1144,6 +1147,14 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
     return SB2_OK;
 }
 
+}  // extern "C"
+
+namespace {
+int setup_exchange(sb2_backend* b);  // below, with the trainer
+}  // namespace
+
+extern "C" {
+
 int sb2_nccl_unique_id(uint8_t* out, size_t len) {
     if (len < sizeof(ncclUniqueId)) {
         g_global_error = "NCCL unique id buffer smaller than 128 bytes";
@@ -1156,6 +1167,41 @@ int sb2_nccl_unique_id(uint8_t* out, size_t len) {
         return SB2_ECOLLECTIVE;
     }
     std::memcpy(out, &id, sizeof(id));
+    return SB2_OK;
+}
+
+int sb2_set_rank_exchange(sb2_backend* b, int mode) {
+    if (!b) return SB2_EDEVICE;
+    if (mode != SB2_EXCHANGE_AUTO && mode != SB2_EXCHANGE_NCCL)
+        return b->fail(SB2_ECONFIG, "unknown rank exchange mode " + std::to_string(mode));
+    if (b->comm) return b->fail(SB2_ECONFIG, "the rank exchange is chosen before sb2_join_ranks");
+    b->exchange_mode = mode;
+    return SB2_OK;
+}
+
+int sb2_test_unanswered_peer(sb2_backend* b, uint32_t spin_limit) {
+    if (!b) return SB2_EDEVICE;
+    SB2_TRY(b->check_loaded());
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    SB2_TRY(b->sync());
+    if (b->comm) return b->fail(SB2_ECONFIG, "sb2_test_unanswered_peer on a handle that joined ranks");
+    b->close_exchange();
+    SB2_CUDA(b, b->fake_xbuf.alloc(0));
+    SB2_CUDA(b, b->xbuf.alloc(0));
+    if (spin_limit == 0) return SB2_OK;  // back to one rank
+    if (!b->grow_ok) return b->fail(SB2_EUNSUPPORTED, "the tree kernel does not fit this dataset");
+    const size_t need = exchange_bytes(b->num_features, 2);
+    SB2_CUDA(b, b->xbuf.alloc(need));
+    SB2_CUDA(b, b->fake_xbuf.alloc(need));
+    SB2_CUDA(b, cudaMemsetAsync(b->xbuf.ptr, 0, need, b->stream));
+    SB2_CUDA(b, cudaMemsetAsync(b->fake_xbuf.ptr, 0, need, b->stream));
+    SB2_TRY(b->sync());
+    b->xpeers[0] = b->xbuf.ptr;
+    b->xpeers[1] = b->fake_xbuf.ptr;
+    b->xbytes = need;
+    b->xepoch = 0;
+    b->fake_peer = true;
+    b->peer_spins = spin_limit;
     return SB2_OK;
 }
 
@@ -1173,7 +1219,10 @@ int sb2_join_ranks(sb2_backend* b, const uint8_t* unique_id, size_t len, int wor
     if (world == 1) return SB2_OK;
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
-    return nccl_status(b, ncclCommInitRank(&b->comm, world, id, rank), "ncclCommInitRank");
+    SB2_TRY(nccl_status(b, ncclCommInitRank(&b->comm, world, id, rank), "ncclCommInitRank"));
+    // With the training set loaded, the tree kernel's exchange (every rank's buffer mapped here) is set up now, as
+    // part of joining; otherwise the first training run does it.
+    return b->loaded ? setup_exchange(b) : SB2_OK;
 }
 
 }  // extern "C"
@@ -1289,12 +1338,15 @@ int enqueue_iteration(sb2_backend* b, const IterArgs& ia, int max_leaves, OpTime
     if (b->persistent()) {
         // One launch grows the whole tree (grow.cu); ranks sum the root's units first and exchange the rest inside.
         GrowExchange x{};
-        x.world = b->comm ? b->world : 1;
+        x.world = b->fake_peer ? 2 : b->comm ? b->world : 1;
         x.rank = b->comm ? b->rank : 0;
-        if (b->comm) {
-            for (int r = 0; r < b->world; ++r) x.peers[r] = static_cast<uint8_t*>(b->xpeers[r]);
+        x.spin_limit = b->peer_spins;
+        if (x.world > 1) {
+            for (int r = 0; r < x.world; ++r) x.peers[r] = static_cast<uint8_t*>(b->xpeers[r]);
             x.epoch0 = b->xepoch;
             b->xepoch += static_cast<uint32_t>(max_leaves) + 2;
+        }
+        if (b->comm) {
             SB2_TRY(op(kOpCollective, [&] {
                 return nccl_status(b, ncclAllReduce(t.iter->root_units, t.iter->root_units, 2, ncclUint64, ncclSum,
                                                     b->comm, s),
@@ -1360,7 +1412,7 @@ int setup_exchange(sb2_backend* b) {
     const size_t need = exchange_bytes(b->num_features, static_cast<uint32_t>(b->world));
     if (b->xready && b->xbytes == need) return SB2_OK;
     b->close_exchange();
-    int ok = b->grow_ok && b->world <= kMaxRanks ? 1 : 0;
+    int ok = b->grow_ok && b->world <= kMaxRanks && b->exchange_mode == SB2_EXCHANGE_AUTO ? 1 : 0;
     cudaIpcMemHandle_t mine{};
     if (ok)
         ok = b->xbuf.alloc(need) == cudaSuccess && cudaMemset(b->xbuf.ptr, 0, need) == cudaSuccess &&
@@ -1819,6 +1871,11 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
     const bool on_device = cudaPointerGetAttributes(&attr, values) == cudaSuccess &&
                            (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
     cudaGetLastError();  // a host pointer may leave an error from the query
+    // The kernels read device values in place, so they must live on the handle's own device: another GPU's memory
+    // is not reachable without peer access, and is rejected before anything is launched.
+    if (on_device && attr.device != b->device)
+        return b->fail(SB2_EDATA, "sb2_bin_dense: the values are memory of device " + std::to_string(attr.device) +
+                                      ", not of the handle's device " + std::to_string(b->device));
     const uint64_t row_bytes = static_cast<uint64_t>(cols) * value_bytes;
     uint64_t chunk = std::max<uint64_t>((256ull << 20) / std::max<uint64_t>(row_bytes, 1), 128) / 128 * 128;
     chunk = std::min(chunk, rows);

@@ -583,7 +583,6 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
 
 // ---- ranks: flags and sums over NVLink ------------------------------------------------------------------------
 
-constexpr unsigned long long kPeerSpins = 1ull << 22;  // polls of a peer's flag (a few seconds) before error 4
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -594,13 +593,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-// One thread: waits until a rank's `flag` reaches `epoch`, at most kPeerSpins polls; false (error 4 recorded, or
+// One thread: waits until a rank's `flag` reaches `epoch`, at most `limit` polls; false (error 4 recorded, or
 // another CTA's error seen) when it gives up.
-__device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, int* error) {
-    for (unsigned long long i = 0;; ++i) {
+__device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, uint32_t limit, int* error) {
+    for (uint32_t i = 0;; ++i) {
         if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
         if (*reinterpret_cast<volatile int*>(error) != 0) return false;
-        if (i > kPeerSpins) {
+        if (i >= limit) {
             atomicCAS(error, 0, 4);
             return false;
         }
@@ -613,7 +612,8 @@ __device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, 
 __device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int* error) {
     const int lane = static_cast<int>(threadIdx.x & 31);
     bool ok = true;
-    if (lane < x.world) ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[x.rank] + off) + lane, epoch, error);
+    if (lane < x.world)
+        ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[x.rank] + off) + lane, epoch, x.spin_limit, error);
     return __all_sync(0xffffffffu, ok);
 }
 

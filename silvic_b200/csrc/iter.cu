@@ -309,7 +309,7 @@ __device__ __forceinline__ int leaf_of(const LeafIndex& li, uint32_t p) {
 // kRowUnroll a thread at a time (their row ids in flight together), each thread walking the leaf index forward.
 __global__ void __launch_bounds__(kRowThreads) leaf_map_kernel(IterArgs a) {
     __shared__ LeafIndex li;
-    if (a.t.iter->stopped) return;
+    if (a.t.iter->stopped || a.t.iter->error != 0) return;  // an error ends training at this iteration's finalize
     build_leaf_index(a.t, li);
     const uint64_t n = a.r.num_rows;
     const uint64_t lo = n * blockIdx.x / gridDim.x, hi = n * (blockIdx.x + 1) / gridDim.x;
@@ -337,7 +337,9 @@ __global__ void __launch_bounds__(kRowThreads) leaf_map_kernel(IterArgs a) {
 
 // Backend::leaf_sums for every leaf of the tree (backend/cpu.rs:886-905: the fixed-point sums of the leaf's rows'
 // gradients and hessians): the rows in order, four a thread at a time, each row's pair added to its leaf's sums in
-// shared memory (64-bit atomics; integer sums, so the order is free), then the CTA's sums added to the output.
+// shared memory as two 32-bit halves per value (integer sums, so the order is free), then the CTA's sums added to the
+// output with 64-bit atomics. A CTA takes at most kLeafSumRows rows (launch_leaf_sums sizes the grid for it): 60,000
+// low halves of at most 65,535 stay below 2^32, and 60,000 high halves of magnitude below 2^15 below 2^31.
 constexpr uint64_t kLeafSumRows = 60000;  // rows a leaf_sums CTA takes at most: its 32-bit halves cannot overflow
 
 __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kRowThreads) leaf_sums_kernel(IterArgs a) {
     // output with a 64-bit atomic.
     __shared__ uint32_t g_lo[kIndexLeaves], h_lo[kIndexLeaves];
     __shared__ int32_t g_hi[kIndexLeaves], h_hi[kIndexLeaves];
-    if (a.t.iter->stopped) return;
+    if (a.t.iter->stopped || a.t.iter->error != 0) return;
     const int32_t L = min(*a.t.tree.num_leaves, kIndexLeaves);
     for (int i = threadIdx.x; i < L; i += kRowThreads) g_lo[i] = h_lo[i] = 0, g_hi[i] = h_hi[i] = 0;
     __syncthreads();
@@ -400,6 +402,12 @@ __device__ __forceinline__ double leaf_output(double g, double h, double l1, dou
 __global__ void __launch_bounds__(kRowThreads) finalize_kernel(IterArgs a) {
     IterState* it = a.t.iter;
     if (it->stopped) return;
+    if (it->error != 0) {
+        // The tree kernel gave up (a rank or a CTA did not answer in time): training stops here, this tree
+        // unrecorded; the host reports the error.
+        if (threadIdx.x == 0) it->stopped = 1;
+        return;
+    }
     const DevTree& t = a.t.tree;
     const int32_t L = *t.num_leaves;
     const int32_t iteration = it->iteration;

@@ -183,8 +183,9 @@ struct GrowExchange {
     uint8_t* peers[kMaxRanks];  // every rank's exchange buffer (this rank's own at [rank]); unused with one rank
     int32_t world, rank;
     uint32_t epoch0;            // the launch's epochs are epoch0 + 1 (the root) .. (they rise across launches)
-    uint32_t pad_;
+    uint32_t spin_limit;        // polls of a rank's flag before the wait gives up (error 4)
 };
+constexpr uint32_t kPeerSpins = 1u << 22;  // polls of a peer's flag (a few seconds) before error 4, by default
 // Splits a grid step of the tree kernel runs at most (steps.cuh).
 constexpr int kSplits = 8;
 // An exchange buffer (u32 words unless noted), for split j of a step and source rank s: the left counts' flags [s]

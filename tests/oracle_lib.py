@@ -233,6 +233,36 @@ def train(shards, params: _abi.Params) -> OracleModel:
         lib().orc_model_free(m)
 
 
+class OracleTrainer:
+    """An oracle training run whose model stays open for prediction (Model::predict_raw_row, model/predict.rs:19-23,
+    restated in oracle.cpp): `trees`, `init_score`, `predict_raw(row)` on raw f64 feature values."""
+
+    def __init__(self, shards, params: _abi.Params):
+        self._structs = [s.c_struct() for s in shards]
+        arr = (_abi.Dataset * len(self._structs))(*self._structs)
+        self._m = C.c_void_p()
+        code = lib().orc_train(arr, len(self._structs), C.byref(params), C.byref(self._m))
+        assert code == 0, lib().orc_last_error()
+        self.trees = []
+        for i in range(lib().orc_model_num_trees(self._m)):
+            v = _abi.TreeView()
+            lib().orc_model_tree(self._m, i, C.byref(v))
+            self.trees.append(Tree.from_view(v))
+        self.init_score = lib().orc_model_init_score(self._m)
+
+    def predict_raw(self, row) -> float:
+        r = np.ascontiguousarray(row, dtype=np.float64)
+        return lib().orc_model_predict_raw(self._m, C.byref(self._structs[0]), _p(r, C.c_double))
+
+    def close(self):
+        if self._m:
+            lib().orc_model_free(self._m)
+            self._m = None
+
+    def __del__(self):
+        self.close()
+
+
 def default_params(**overrides) -> _abi.Params:
     """sb2_default_params' defaults (crates/silvic-core/src/config.rs:123-165) without loading the CUDA library."""
     p = _abi.Params()

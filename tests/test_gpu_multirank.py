@@ -1,0 +1,46 @@
+"""Two ranks grow the trees of one GPU (the reference pins this as `two_ranks_grow_the_tree_of_one`,
+crates/silvic-core/src/learner.rs:709-722, and `two_ranks_train_the_model_of_one`,
+crates/silvic-core/tests/train_cpu.rs:270-286).
+
+Two processes (torchrun, one per GPU) each hold a contiguous row shard and join with sb2_join_ranks; their trees must
+equal, field by field, the trees one GPU grows on the whole dataset and the CPU oracle's. Both exchanges run: the
+tree kernel's own over NVLink (the default) and the NCCL fallback (per-step launches with an ncclAllReduce of each
+split's histogram). Skipped with fewer than two GPUs. NVLS is off (NCCL_NVLS_ENABLE=0): the exchange uses plain peer
+stores and NCCL only small reductions."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+WORKER = Path(__file__).resolve().parent / "multirank_worker.py"
+
+
+@pytest.mark.parametrize("mode", ["auto", "nccl"])
+def test_two_ranks_grow_the_trees_of_one_gpu(device, mode, tmp_path):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = tmp_path / "result.json"
+    port = 29500 + (os.getpid() + (0 if mode == "auto" else 7)) % 2000
+    # config c2's shape (100 features, binary) at 1M rows: 255-leaf trees run grid steps of eight splits
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", f"--master-port={port}", str(WORKER), str(out), mode,
+           "c2", "1000000", "3", "255"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT))
+    run = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
+    assert run.returncode == 0, (run.stdout[-4000:], run.stderr[-4000:])
+    res = json.loads(out.read_text())
+    assert res["world"] == 2 and res["trees"] == 3
+    assert res["tree_kernel_exchange"] == (mode == "auto"), res
+    assert res["identical_to_one_gpu"], res["differences"]
+    assert res["identical_to_oracle"], res["differences"]

@@ -1,7 +1,8 @@
 """sb2_find_best_split_noalloc, the split search for callers that cannot let a call allocate device memory: its
 results, taken through the C ABI from device buffers the test owns, equal sb2_find_best_split's on the same inputs,
-on two calls in a row (the second reuses the scratch the first left behind). It has no counterpart in the
-reference. Collected last so it also runs after every other test in one process."""
+on two calls in a row (the second reuses the scratch the first left behind), and the CPU oracle's find_best_split
+(a restatement of crates/silvic-core/src/split.rs:919-961 that shares no code with the device search). It has no
+counterpart in the reference. Collected last so it also runs after every other test in one process."""
 
 from __future__ import annotations
 
@@ -12,6 +13,7 @@ import pytest
 
 from silvic_b200 import _abi
 from silvic_b200.backend import B200Backend
+import oracle_lib as orc
 from synth import random_binned
 
 pytestmark = pytest.mark.gpu
@@ -76,6 +78,10 @@ def test_noalloc_split_matches_find_best_split(device):
             assert got.as_tuple() == want.as_tuple(), f"call {k}"
             assert np.array_equal(got_spl, want_spl), f"call {k}"
             assert want.found, f"call {k} should find a split"
+            # And the CPU oracle's search on the same histogram: the same split, bit for bit.
+            ref, ref_spl = orc.find_best_split(data, hist, evaluate, sums, scale, cfg)
+            assert got.as_tuple() == ref.as_tuple(), f"call {k} differs from the oracle"
+            assert np.array_equal(got_spl, ref_spl), f"call {k}: splittable differs from the oracle"
     finally:
         b.close()
 

@@ -3,8 +3,9 @@
 Default workload: BASELINE.json configs[3] ("c4"), the largest configuration that fits one B200 and the one the
 scaling target names: L2 regression, 100,000,000 rows x 256 f32 features ~ N(0,1), target = a random 32-feature
 linear function + N(0,1) noise, 255 bins, 255 leaves, quantized gradients (4 bins), 200 trees in a full job.
-`--config` selects another configuration: c1 (configs[0]: 1M x 28 L2, 63 leaves, 100 trees) or c2 (configs[1]:
-10M x 100 binary, 255 leaves, 500 trees). A "step" is one boosting iteration: gradients, quantization, a tree grown
+`--config` selects another configuration: c1 (configs[0]: 1M x 28 L2, 63 leaves, 100 trees), c2 (configs[1]:
+10M x 100 binary, 255 leaves, 500 trees) or c3 (configs[2]: 2M x 136 lambdarank over queries of Poisson(120) rows,
+127 leaves, 300 trees). A "step" is one boosting iteration: gradients, quantization, a tree grown
 split by split on the device (partition, smaller-child histogram, sibling subtraction, split scan, leaf choice),
 leaf renewal and the score update.
 
@@ -80,6 +81,8 @@ class Config:
 CONFIGS = {
     "c1": Config("c1", 0, 1_000_000, "regression", 255, 63, 100, ["gauss"] * 28),
     "c2": Config("c2", 1, 10_000_000, "binary", 255, 255, 500, ["gauss"] * 70 + ["unif"] * 30, 885.0),
+    "c3": Config("c3", 2, 2_000_000, "lambdarank", 255, 127, 300,
+                 ["gauss"] * 60 + ["lognormal"] * 40 + ["zeros30"] * 36),
     "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256),
 }
 CFG = CONFIGS["c4"]
@@ -136,13 +139,50 @@ def _gauss(stream: int, rows):
 
 
 def column(f: int, rows):
-    """Feature f of `rows` (f64): kind "gauss" ~ N(0,1) (streams 2f, 2f+1), "unif" ~ U[0,1) (stream 1000 + f)."""
+    """Feature f of `rows` (f64): kind "gauss" ~ N(0,1) (streams 2f, 2f+1), "unif" ~ U[0,1) (stream 1000 + f),
+    "lognormal" = exp(N(0,1)), "zeros30" = N(0,1) with 30% of the rows exactly 0 (stream 3000 + f)."""
     kind = CFG.kinds[f]
     if kind == "gauss":
         return _gauss(2 * f, rows)
     if kind == "unif":
         return _unit(1000 + f, rows)
+    if kind == "lognormal":
+        import torch
+
+        return torch.exp(_gauss(2 * f, rows))
+    if kind == "zeros30":
+        return _gauss(2 * f, rows) * (_unit(3000 + f, rows) >= 0.3)
     raise ValueError(kind)
+
+
+_QUERIES: dict = {}
+
+
+def query_boundaries() -> np.ndarray:
+    """c3's queries over rows 0..ROWS: sizes ~ Poisson(120) clipped to [1, 1000] from a seeded generator, in order,
+    the last one cut at the last row (num_queries + 1 boundaries)."""
+    if ROWS not in _QUERIES:
+        g = np.random.default_rng(SEED + 3)
+        sizes = np.clip(g.poisson(120.0, size=ROWS // 100 + 16), 1, 1000)
+        while sizes.sum() < ROWS:
+            sizes = np.concatenate([sizes, np.clip(g.poisson(120.0, size=1024), 1, 1000)])
+        bounds = np.concatenate([[0], np.cumsum(sizes)])
+        last = int(np.searchsorted(bounds, ROWS))
+        bounds = bounds[: last + 1]
+        bounds[-1] = ROWS
+        _QUERIES[ROWS] = bounds.astype(np.int64)
+    return _QUERIES[ROWS]
+
+
+def shard_rows(rank: int, world: int) -> tuple[int, int]:
+    """Rank's contiguous rows; with queries, cut at the query boundary nearest to an even split (a query stays on
+    one rank)."""
+    cut = lambda r: ROWS * r // world  # noqa: E731
+    if CFG.objective != "lambdarank":
+        return cut(rank), cut(rank + 1)
+    qb = query_boundaries()
+    snap = lambda r: 0 if r == 0 else ROWS if r == world else int(qb[np.abs(qb - cut(r)).argmin()])  # noqa: E731
+    return snap(rank), snap(rank + 1)
 
 
 def features_of(rows, device):
@@ -162,6 +202,8 @@ def labels_of(rows):
     import torch
 
     x = lambda f: column(int(f), rows).to(torch.float32).double()  # noqa: E731  (the f32 feature, as binned)
+    if CFG.name == "c3":
+        return _relevance(rows, x)
     if CFG.name == "c1":
         g = np.random.default_rng(SEED + 1)
         picked = g.choice(CFG.features, size=8, replace=False)
@@ -190,6 +232,33 @@ def labels_of(rows):
         logit += 0.8 * x(a) * x(b)
     p = torch.sigmoid(logit)
     return (_unit(5000, rows) < p).to(torch.float32)
+
+
+_RELEVANCE_CUTS: dict = {}
+
+
+def _relevance(rows, x):
+    """c3's integer relevance 0..4: a noisy linear score in 20 random features, cut at its 50/75/90/97th percentiles
+    over the first SAMPLE_ROWS rows (the same cuts on every rank)."""
+    import torch
+
+    g = np.random.default_rng(SEED + 2)
+    picked = g.choice(CFG.features, size=20, replace=False)
+    weights = g.normal(0.0, 1.0, size=20)
+
+    def score(r, xf):
+        y = torch.zeros(r.numel(), dtype=torch.float64, device=r.device)
+        for f, w in zip(picked, weights):
+            y += float(w) * torch.tanh(xf(f))
+        return y + 0.5 * _gauss(7000, r)
+
+    key = (ROWS, SAMPLE_ROWS)
+    if key not in _RELEVANCE_CUTS:
+        sample = torch.arange(min(SAMPLE_ROWS, ROWS), dtype=torch.int64, device=rows.device)
+        s = score(sample, lambda f: column(int(f), sample).to(torch.float32).double())
+        _RELEVANCE_CUTS[key] = torch.quantile(s.float(), torch.tensor([0.5, 0.75, 0.9, 0.97], device=s.device)).double()
+    cuts = _RELEVANCE_CUTS[key].to(rows.device)
+    return torch.bucketize(score(rows, x), cuts, right=True).to(torch.float32)
 
 
 def bin_mappers(device):
@@ -279,6 +348,11 @@ def build_dataset(begin: int, end: int, device, chunk: int = 2_000_000):
     groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, host[gi])
               for gi, g in enumerate(shells)]
     data = BinnedDataset(n, begin, features, groups, total_bins, label)
+    if CFG.objective == "lambdarank":
+        qb = query_boundaries()
+        lo, hi = np.searchsorted(qb, [begin, end])
+        assert qb[lo] == begin and qb[hi] == end, "a shard must hold whole queries"
+        data.query_boundaries = (qb[lo:hi + 1] - begin).astype(np.uint32)
     data._keep.extend(pinned)
     return data
 
@@ -383,7 +457,7 @@ def oracle_params(num_iterations: int):
     import oracle_lib as orc
     from silvic_b200 import _abi
 
-    objective = {"regression": _abi.REGRESSION, "binary": _abi.BINARY}[CFG.objective]
+    objective = {"regression": _abi.REGRESSION, "binary": _abi.BINARY, "lambdarank": _abi.LAMBDARANK}[CFG.objective]
     return orc.default_params(objective=objective, num_leaves=CFG.num_leaves, learning_rate=0.1,
                               num_grad_quant_bins=4, num_iterations=num_iterations)
 
@@ -460,7 +534,7 @@ def _joined_backend(local: int, data, params, rank: int, world: int) -> tuple[ob
 
     t0 = time.perf_counter()
     b = B200Backend(local)
-    b.load(data, params.objective, params.sigmoid)
+    b.load(data, params.objective, params.sigmoid, params)
     t1 = time.perf_counter()
     if world > 1:
         uid = [B200Backend.nccl_unique_id() if rank == 0 else None]
@@ -478,7 +552,7 @@ def run_b200(args, rank: int, world: int):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    begin, end = ROWS * rank // world, ROWS * (rank + 1) // world
+    begin, end = shard_rows(rank, world)
     data = build_dataset(begin, end, dev)
     labels = all_labels(dev) if world > 1 else data.label
     torch.cuda.synchronize()
@@ -628,7 +702,7 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the oracle's trees (parity and, at N = 1, the CPU baseline)")
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS),
-                    help="c4 (default): BASELINE configs[3], 100M rows; c1: configs[0]; c2: configs[1]")
+                    help="c4 (default): BASELINE configs[3], 100M rows; c1, c2, c3: configs[0], [1], [2]")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows of the synthetic set (a smaller case for profiling; default: the config's)")
     ap.add_argument("--trees", type=int, default=0,

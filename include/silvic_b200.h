@@ -84,12 +84,18 @@ typedef struct sb2_dataset {
     const uint32_t* query_boundaries; /* NULL, or num_queries + 1 row boundaries */
 } sb2_dataset;
 
-/* ObjectiveSetup (crates/silvic-core/src/backend/mod.rs:58-71), pointwise objectives. */
+/* ObjectiveSetup (crates/silvic-core/src/backend/mod.rs:58-71). Lambdarank (objective/lambdarank.rs) takes the
+ * dataset's query boundaries; its per-query inverse max DCGs are computed at load from the labels. */
 enum { SB2_REGRESSION = 0, SB2_BINARY = 1, SB2_LAMBDARANK = 2 };
 typedef struct sb2_objective {
     int32_t kind;
     int32_t pad_;
-    double sigmoid; /* binary */
+    double sigmoid;                      /* binary and lambdarank */
+    int32_t lambdarank_norm;             /* lambdarank: normalize the lambdas (LightGBM's lambdarank_norm) */
+    uint32_t lambdarank_truncation_level;
+    const double* label_gain;            /* lambdarank: gain per label; NULL: LightGBM's default 2^i - 1, i < 31 */
+    uint32_t num_label_gain;
+    uint32_t pad2_;
 } sb2_objective;
 
 /* LeafRange (crates/silvic-core/src/backend/mod.rs:17-22): partition[begin .. begin + count]. */
@@ -169,7 +175,7 @@ typedef struct sb2_split_info {
 /* Training parameters (crates/silvic-core/src/config.rs:73-116, defaults :123-165), the subset this backend
  * trains with. sb2_default_params() fills the reference defaults. */
 typedef struct sb2_params {
-    int32_t objective;            /* SB2_REGRESSION / SB2_BINARY */
+    int32_t objective;            /* SB2_REGRESSION / SB2_BINARY / SB2_LAMBDARANK */
     int32_t num_iterations;
     double learning_rate;
     int32_t num_leaves;
@@ -192,6 +198,11 @@ typedef struct sb2_params {
     int32_t quant_train_renew_leaf;
     int32_t stochastic_rounding;
     int32_t pad_;
+    int32_t lambdarank_norm;              /* lambdarank only: as in sb2_objective */
+    uint32_t lambdarank_truncation_level;
+    const double* label_gain;             /* NULL: the default gains */
+    uint32_t num_label_gain;
+    uint32_t pad2_;
 } sb2_params;
 
 /* One tree in LightGBM 3.3.5 array layout (crates/silvic-core/src/tree.rs:47-73). The arrays belong to the

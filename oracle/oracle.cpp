@@ -304,6 +304,181 @@ void gradients(const sb2_objective& o, const float* scores, const float* label, 
     }
 }
 
+// ---- objective/lambdarank.rs ----------------------------------------------------------------------------------
+
+constexpr size_t MAX_POSITION = 10000;             // lambdarank.rs:25
+constexpr double MIN_SIGMOID_INPUT = -50.0;        // lambdarank.rs:28
+constexpr size_t SIGMOID_BINS = 1024 * 1024;       // lambdarank.rs:31
+constexpr double SCORE_DISTANCE_EPSILON = static_cast<double>(0.01f);  // lambdarank.rs:34
+
+// lambdarank.rs:37-46: 1 / log2(2 + rank)
+double discount(size_t rank) { return 1.0 / std::log2(2.0 + static_cast<double>(rank)); }
+
+// config.rs:118-121
+std::vector<double> default_label_gain() {
+    std::vector<double> g;
+    for (uint32_t i = 0; i < 31; ++i) g.push_back(static_cast<double>((1u << i) - 1u));
+    return g;
+}
+
+// lambdarank.rs:122-139 (DCGCalculator::CalMaxDCGAtK)
+double max_dcg_at_k(size_t k, const float* labels, size_t n, const std::vector<double>& gain) {
+    std::vector<size_t> count(gain.size(), 0);
+    for (size_t i = 0; i < n; ++i) ++count[static_cast<size_t>(labels[i])];
+    size_t top = gain.size() - 1;
+    double dcg = 0.0;
+    for (size_t j = 0; j < std::min(k, n); ++j) {
+        while (top > 0 && count[top] == 0) --top;
+        dcg += discount(j) * gain[top];
+        --count[top];  // wraps at label 0, as the reference's wrapping_sub
+    }
+    return dcg;
+}
+
+// ObjectiveSetup::LambdaRank (objective/mod.rs:35-65) with the sigmoid table (lambdarank.rs:51-120) of one rank.
+struct LambdaRank {
+    double sigmoid = 1.0;
+    bool norm = true;
+    size_t truncation_level = 30;
+    std::vector<double> label_gain, inverse_max_dcg;
+    const std::vector<double>* table = nullptr;  // shared by the setups of one sigmoid
+    double min_input = 0.0, max_input = 0.0, idx_factor = 0.0;
+};
+
+bool lambdarank_setup(const sb2_params& p, const sb2_dataset& d, LambdaRank& out) {
+    if (!d.query_boundaries || d.num_queries == 0 || d.query_boundaries[0] != 0 ||
+        d.query_boundaries[d.num_queries] != d.num_rows) {
+        g_error = "ranking tasks require query information";
+        return false;
+    }
+    out.sigmoid = p.sigmoid;
+    out.norm = p.lambdarank_norm != 0;
+    out.truncation_level = p.lambdarank_truncation_level;
+    out.label_gain = p.label_gain && p.num_label_gain ? std::vector<double>(p.label_gain, p.label_gain + p.num_label_gain)
+                                                     : default_label_gain();
+    for (size_t i = 0; i < d.num_rows; ++i) {  // check_labels (lambdarank.rs:173-195)
+        const float l = d.label[i];
+        if (std::fabs(static_cast<double>(l) - static_cast<double>(static_cast<int32_t>(l))) > K_EPSILON || l < 0.0f ||
+            static_cast<size_t>(l) >= out.label_gain.size()) {
+            g_error = "lambdarank label " + std::to_string(l) + " is not an integer below the label gains";
+            return false;
+        }
+    }
+    out.inverse_max_dcg.resize(d.num_queries);
+    for (uint32_t q = 0; q < d.num_queries; ++q) {
+        const uint32_t b = d.query_boundaries[q], e = d.query_boundaries[q + 1];
+        const double m = max_dcg_at_k(out.truncation_level, d.label + b, e - b, out.label_gain);
+        out.inverse_max_dcg[q] = m > 0.0 ? 1.0 / m : 0.0;
+    }
+    out.min_input = MIN_SIGMOID_INPUT / out.sigmoid / 2.0;
+    out.max_input = -out.min_input;
+    out.idx_factor = static_cast<double>(SIGMOID_BINS) / (out.max_input - out.min_input);
+    // The table for this sigmoid, built once and kept while the sigmoid stays the same (SigmoidTable::shared).
+    static double cached_sigmoid = std::numeric_limits<double>::quiet_NaN();
+    static std::vector<double> cached;
+    if (!(cached_sigmoid == out.sigmoid)) {
+        cached.resize(SIGMOID_BINS);
+        for (size_t i = 0; i < SIGMOID_BINS; ++i) {
+            const double score = static_cast<double>(i) / out.idx_factor + out.min_input;
+            cached[i] = 1.0 / (1.0 + std::exp(score * out.sigmoid));
+        }
+        cached_sigmoid = out.sigmoid;
+    }
+    out.table = &cached;
+    return true;
+}
+
+// SigmoidTable::get (lambdarank.rs:110-119)
+double sigmoid_at(const LambdaRank& lr, double delta) {
+    const std::vector<double>& table = *lr.table;
+    if (delta <= lr.min_input) return table[0];
+    if (delta >= lr.max_input) return table[SIGMOID_BINS - 1];
+    return table[std::min(static_cast<size_t>((delta - lr.min_input) * lr.idx_factor), SIGMOID_BINS - 1)];
+}
+
+// descending_key (lambdarank.rs:162-168): ascending order of the key is descending order of the score.
+uint32_t descending_key(float score) {
+    float v = score + 0.0f;
+    uint32_t bits;
+    std::memcpy(&bits, &v, 4);
+    const uint32_t ascending = (bits >> 31) == 1 ? ~bits : (bits | (1u << 31));
+    return ~ascending;
+}
+
+// query_gradients (lambdarank.rs:264-321) with load_ranked (:324-341), worst_score (:344-351) and accumulate_pairs
+// (:353-396) for one query of n rows.
+void lambdarank_query(const LambdaRank& lr, size_t query, const float* scores, const float* label, const float* weight,
+                      size_t n, float* grad, float* hess) {
+    if (n == 0) return;
+    std::vector<uint64_t> keys(n);
+    for (size_t r = 0; r < n; ++r) keys[r] = (static_cast<uint64_t>(descending_key(scores[r])) << 32) | r;
+    std::sort(keys.begin(), keys.end());
+    std::vector<size_t> order(n);
+    std::vector<double> score(n), gain(n), disc(n), lambda(n, 0.0), hessian(n, 0.0);
+    std::vector<float> lab(n);
+    for (size_t k = 0; k < n; ++k) {
+        order[k] = static_cast<size_t>(keys[k] & 0xFFFFFFFFull);
+        score[k] = static_cast<double>(scores[order[k]]);
+        lab[k] = label[order[k]];
+        gain[k] = lr.label_gain[static_cast<size_t>(lab[k])];
+        disc[k] = discount(k);
+    }
+    size_t worst = n - 1;
+    if (worst > 0 && score[worst] == -std::numeric_limits<double>::infinity()) --worst;
+    const bool norm_by_distance = lr.norm && score[0] != score[worst];
+    const double inverse_max_dcg = lr.inverse_max_dcg[query];
+    size_t valid = n;
+    for (size_t k = 0; k < n; ++k)
+        if (score[k] == -std::numeric_limits<double>::infinity()) {
+            valid = k;
+            break;
+        }
+    const double sigmoid_squared = lr.sigmoid * lr.sigmoid;
+    double sum_lambdas = 0.0;
+    const size_t rows_i = std::min(lr.truncation_level, valid > 0 ? valid - 1 : 0);
+    for (size_t i = 0; i < rows_i; ++i) {
+        double lambda_i = lambda[i], hessian_i = hessian[i];
+        for (size_t j = i + 1; j < valid; ++j) {
+            if (lab[j] == lab[i]) continue;
+            const double sign = lab[i] > lab[j] ? 1.0 : -1.0;
+            const double delta_score = sign * (score[i] - score[j]);
+            const double dcg_gap = sign * (gain[i] - gain[j]);
+            const double paired_discount = std::fabs(disc[i] - disc[j]);
+            double delta_pair_ndcg = dcg_gap * paired_discount * inverse_max_dcg;
+            if (norm_by_distance) delta_pair_ndcg /= SCORE_DISTANCE_EPSILON + std::fabs(delta_score);
+            const double p = sigmoid_at(lr, delta_score);
+            const double p_lambda = p * (-lr.sigmoid * delta_pair_ndcg);
+            const double p_hessian = p * (1.0 - p) * (sigmoid_squared * delta_pair_ndcg);
+            lambda_i += sign * p_lambda;
+            lambda[j] -= sign * p_lambda;
+            hessian_i += p_hessian;
+            hessian[j] += p_hessian;
+            sum_lambdas -= 2.0 * p_lambda;
+        }
+        lambda[i] = lambda_i;
+        hessian[i] = hessian_i;
+    }
+    const double norm_factor = lr.norm && sum_lambdas > 0.0 ? std::log2(1.0 + sum_lambdas) / sum_lambdas : 1.0;
+    for (size_t k = 0; k < n; ++k) {
+        float g = static_cast<float>(lambda[k] * norm_factor);
+        float h = static_cast<float>(hessian[k] * norm_factor);
+        if (weight) {
+            g = g * weight[order[k]];
+            h = h * weight[order[k]];
+        }
+        grad[order[k]] = g;
+        hess[order[k]] = h;
+    }
+}
+
+// lambdarank::gradients (lambdarank.rs:197-240): every query of one rank, in parallel over queries.
+void lambdarank_gradients(const LambdaRank& lr, const sb2_dataset& d, const float* scores, float* grad, float* hess) {
+    parallel_tasks(d.num_queries, [&](size_t q) {
+        const uint32_t b = d.query_boundaries[q], e = d.query_boundaries[q + 1];
+        lambdarank_query(lr, q, scores + b, d.label + b, d.weight ? d.weight + b : nullptr, e - b, grad + b, hess + b);
+    });
+}
+
 // objective/regression.rs:8-17 and binary.rs:8-16: [sum label * weight, sum weight] in row order.
 void label_sums(int objective, const float* label, const float* weight, size_t n, double out[2]) {
     double l = 0.0, w = 0.0;
@@ -1227,7 +1402,12 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
     }
     for (uint32_t f = 0; f < shards[0].num_features; ++f)
         if (shards[0].features[f].kind == SB2_CATEGORICAL) throw std::runtime_error("categorical features");
-    sb2_objective obj{p.objective, 0, p.sigmoid};
+    sb2_objective obj{};
+    obj.kind = p.objective;
+    obj.sigmoid = p.sigmoid;
+    std::vector<LambdaRank> ranking(p.objective == SB2_LAMBDARANK ? num_shards : 0);
+    for (size_t r = 0; r < ranking.size(); ++r)
+        if (!lambdarank_setup(p, shards[r], ranking[r])) throw std::runtime_error(g_error);
     // init_score: per-rank label sums, allreduced in rank order.
     double sums[2] = {0.0, 0.0};
     for (int r = 0; r < num_shards; ++r) {
@@ -1248,7 +1428,11 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
         double maxima[2] = {0.0, 0.0};
         for (Rank& rk : w.ranks) {
             size_t n = rk.data->num_rows;
-            gradients(obj, rk.scores.data(), rk.data->label, rk.data->weight, n, rk.grad.data(), rk.hess.data());
+            if (p.objective == SB2_LAMBDARANK)
+                lambdarank_gradients(ranking[&rk - w.ranks.data()], *rk.data, rk.scores.data(), rk.grad.data(),
+                                     rk.hess.data());
+            else
+                gradients(obj, rk.scores.data(), rk.data->label, rk.data->weight, n, rk.grad.data(), rk.hess.data());
             using Pair = std::pair<double, double>;
             auto [mg, mh] = parallel_reduce(
                 n, Pair{0.0, 0.0},
@@ -1516,6 +1700,31 @@ int orc_model_iteration_seconds(const orc_model* m, double* out, size_t len) {
     std::copy(m->m.seconds.begin(), m->m.seconds.begin() + k, out);
     return static_cast<int>(m->m.seconds.size());
 }
+int orc_lambdarank_gradients(const sb2_params* params, const sb2_dataset* data, const float* scores, float* grad,
+                             float* hess) {
+    LambdaRank lr;
+    if (!lambdarank_setup(*params, *data, lr)) return SB2_EDATA;
+    lambdarank_gradients(lr, *data, scores, grad, hess);
+    return SB2_OK;
+}
+double orc_lambdarank_max_dcg(size_t k, const float* labels, size_t n, const double* gain, size_t num_gain) {
+    return max_dcg_at_k(k, labels, n, std::vector<double>(gain, gain + num_gain));
+}
+double orc_lambdarank_sigmoid(double sigmoid, double delta) {
+    sb2_params p{};
+    p.sigmoid = sigmoid;
+    const uint32_t qb[2] = {0, 1};
+    const float label = 0.0f;
+    sb2_dataset d{};
+    d.num_rows = 1;
+    d.num_queries = 1;
+    d.query_boundaries = qb;
+    d.label = &label;
+    LambdaRank lr;
+    if (!lambdarank_setup(p, d, lr)) return std::numeric_limits<double>::quiet_NaN();
+    return sigmoid_at(lr, delta);
+}
+
 // Model::predict_raw_row (model/predict.rs:19-23) with numerical_decision (:118-141).
 double orc_model_predict_raw(const orc_model* m, const sb2_dataset* data, const double* row) {
     (void)data;

@@ -38,6 +38,12 @@ int64_t orc_to_fixed(float value, float scale);
 void orc_gradients(const sb2_objective* objective, const float* scores, const float* label, const float* weight,
                    size_t n, float* grad, float* hess);
 double orc_init_score(const sb2_params* params, const float* label, const float* weight, size_t n);
+/* objective/lambdarank.rs: every query's gradients (data: num_rows, label, weight, query boundaries) at `scores`;
+ * max_dcg_at_k; the sigmoid table's entry for a score difference. SB2_EDATA for labels or queries it rejects. */
+int orc_lambdarank_gradients(const sb2_params* params, const sb2_dataset* data, const float* scores, float* grad,
+                             float* hess);
+double orc_lambdarank_max_dcg(size_t k, const float* labels, size_t n, const double* gain, size_t num_gain);
+double orc_lambdarank_sigmoid(double sigmoid, double delta);
 
 /* CpuBackend operations on a dataset */
 int orc_histogram(const sb2_dataset* data, const int32_t* packed, int32_t max_quant, const uint32_t* rows,

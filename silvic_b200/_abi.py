@@ -72,7 +72,9 @@ class Dataset(C.Structure):
 
 
 class Objective(C.Structure):
-    _fields_ = [("kind", C.c_int32), ("pad_", C.c_int32), ("sigmoid", C.c_double)]
+    _fields_ = [("kind", C.c_int32), ("pad_", C.c_int32), ("sigmoid", C.c_double), ("lambdarank_norm", C.c_int32),
+                ("lambdarank_truncation_level", C.c_uint32), ("label_gain", C.POINTER(C.c_double)),
+                ("num_label_gain", C.c_uint32), ("pad2_", C.c_uint32)]
 
 
 class LeafRange(C.Structure):
@@ -167,6 +169,11 @@ class Params(C.Structure):
         ("quant_train_renew_leaf", C.c_int32),
         ("stochastic_rounding", C.c_int32),
         ("pad_", C.c_int32),
+        ("lambdarank_norm", C.c_int32),
+        ("lambdarank_truncation_level", C.c_uint32),
+        ("label_gain", C.POINTER(C.c_double)),
+        ("num_label_gain", C.c_uint32),
+        ("pad2_", C.c_uint32),
     ]
 
 

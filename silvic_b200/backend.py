@@ -40,9 +40,13 @@ _PARAM_ALIASES = {
     "num_grad_quant_bins": [],
     "quant_train_renew_leaf": [],
     "stochastic_rounding": [],
+    "lambdarank_truncation_level": [],
+    "lambdarank_norm": [],
+    "label_gain": [],
 }
 _OBJECTIVES = {"regression": _abi.REGRESSION, "regression_l2": _abi.REGRESSION, "l2": _abi.REGRESSION,
-               "mean_squared_error": _abi.REGRESSION, "mse": _abi.REGRESSION, "binary": _abi.BINARY}
+               "mean_squared_error": _abi.REGRESSION, "mse": _abi.REGRESSION, "binary": _abi.BINARY,
+               "lambdarank": _abi.LAMBDARANK}
 # Accepted for LightGBM compatibility, no effect (crates/silvic-core/src/config.rs NO_EFFECT_KEYS), plus the ones
 # that select this backend or describe binning, which happens before training.
 _IGNORED = {"force_row_wise", "force_col_wise", "deterministic", "histogram_pool_size", "feature_pre_filter",
@@ -72,8 +76,15 @@ def params_from_dict(params: dict) -> _abi.Params:
             if value not in _OBJECTIVES:
                 raise _abi.SilvicError(_abi.EUNSUPPORTED, f"objective `{value}` on the B200 backend")
             p.objective = _OBJECTIVES[value]
-        elif name in ("boost_from_average", "use_quantized_grad", "quant_train_renew_leaf", "stochastic_rounding"):
+        elif name in ("boost_from_average", "use_quantized_grad", "quant_train_renew_leaf", "stochastic_rounding",
+                      "lambdarank_norm"):
             setattr(p, name, int(bool(value)))
+        elif name == "label_gain":
+            gains = [float(v) for v in (value.split(",") if isinstance(value, str) else value)]
+            arr = (C.c_double * max(len(gains), 1))(*gains)
+            p._label_gain = arr  # kept alive with the struct
+            p.label_gain = C.cast(arr, C.POINTER(C.c_double))
+            p.num_label_gain = len(gains)
         else:
             setattr(p, name, type(getattr(p, name))(value))
     return p
@@ -139,8 +150,16 @@ class B200Backend:
         self._lib.sb2_name(self._h, buf, len(buf))
         return buf.value.decode()
 
-    def load(self, train: BinnedDataset, objective: str = "regression", sigmoid: float = 1.0):
+    def load(self, train: BinnedDataset, objective: str = "regression", sigmoid: float = 1.0,
+             params: _abi.Params | None = None):
+        """Backend::load. Lambdarank takes its normalization, truncation level and label gains from `params`
+        (LightGBM's defaults without it)."""
         obj = _abi.Objective(_OBJECTIVES[objective] if isinstance(objective, str) else objective, 0, sigmoid)
+        obj.lambdarank_norm, obj.lambdarank_truncation_level = 1, 30
+        if params is not None:
+            obj.lambdarank_norm = params.lambdarank_norm
+            obj.lambdarank_truncation_level = params.lambdarank_truncation_level
+            obj.label_gain, obj.num_label_gain = params.label_gain, params.num_label_gain
         d = train.c_struct()
         self._check(self._lib.sb2_load(self._h, C.byref(d), C.byref(obj)))
         self._data = train
@@ -439,7 +458,7 @@ def train(params: dict, train_set: BinnedDataset, device: int = 0) -> Model:
     p = params_from_dict(params)
     backend = B200Backend(device)
     try:
-        backend.load(train_set, p.objective, p.sigmoid)
+        backend.load(train_set, p.objective, p.sigmoid, p)
         return backend.train(p, init_score(p, train_set.label, train_set.weight))
     finally:
         backend.close()

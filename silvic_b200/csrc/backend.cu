@@ -97,6 +97,10 @@ struct sb2_backend {
     DeviceBuffer label, weight, scores, grad, hess, packed;
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, cand_flags, cand_gain, counter, maxima, misc;
+    // lambdarank: the queries and the host-computed tables the gradient kernel reads (RankArgs)
+    DeviceBuffer rk_bounds, rk_imdcg, rk_gain, rk_discount, rk_table;
+    RankArgs ranking{};
+    std::vector<double> rank_gain;            // the loaded label gains, to check training parameters against
     DeviceBuffer api_spec;                    // the QuantSpec of the last sb2_quantize
     sb2_quant_spec api_spec_host{};
     const sb2_quant_spec* packed_spec = nullptr;  // the quantization the packed gradients now hold
@@ -180,6 +184,7 @@ struct sb2_backend {
         r.grad = grad.as<float>();
         r.hess = hess.as<float>();
         r.packed = packed.as<int32_t>();
+        r.rank = ranking;
         return r;
     }
 
@@ -398,6 +403,10 @@ void sb2_default_params(sb2_params* p) {
     p->num_grad_quant_bins = 4;
     p->quant_train_renew_leaf = 1;
     p->stochastic_rounding = 1;
+    p->lambdarank_norm = 1;                // config.rs:153-154
+    p->lambdarank_truncation_level = 30;
+    p->label_gain = nullptr;               // config.rs:118-121: 2^i - 1 for i < 31
+    p->num_label_gain = 0;
 }
 
 int sb2_create(int device, sb2_backend** out) {
@@ -452,14 +461,118 @@ int sb2_name(const sb2_backend* b, char* buf, size_t len) {
     return SB2_OK;
 }
 
+namespace {
+
+// LightGBM's default label gains (config.rs:118-121): 2^i - 1 for i < 31.
+std::vector<double> label_gains(const double* gain, uint32_t count) {
+    if (gain != nullptr && count > 0) return std::vector<double>(gain, gain + count);
+    std::vector<double> g;
+    for (uint32_t i = 0; i < 31; ++i) g.push_back(static_cast<double>((1u << i) - 1u));
+    return g;
+}
+
+// ObjectiveSetup::LambdaRank (objective/mod.rs:35-65) for the device: the queries checked and uploaded, and the
+// tables the gradient kernel reads, computed here once with the reference's own expressions and the same libm
+// (lambdarank.rs:37-46 discounts, :51-72 the sigmoid table, :122-139 max DCG, :173-195 the label checks).
+int load_ranking(sb2_backend* b, const sb2_dataset* d, const sb2_objective* o) {
+    const uint64_t n = d->num_rows;
+    const uint32_t nq = d->num_queries;
+    const uint32_t* qb = d->query_boundaries;
+    if (qb == nullptr || nq == 0) return b->fail(SB2_EDATA, "ranking tasks require query information");
+    if (qb[0] != 0 || qb[nq] != n) return b->fail(SB2_EDATA, "query boundaries must run from row 0 to the last row");
+    uint32_t longest = 0;
+    for (uint32_t q = 0; q < nq; ++q) {
+        if (qb[q + 1] < qb[q]) return b->fail(SB2_EDATA, "query boundaries must not decrease");
+        longest = std::max(longest, qb[q + 1] - qb[q]);
+    }
+    if (longest > kMaxQueryRows)
+        return b->fail(SB2_EUNSUPPORTED, "a query of " + std::to_string(longest) + " rows; the device takes " +
+                                             std::to_string(kMaxQueryRows) + " at most");
+    if (!(o->sigmoid > 0.0)) return b->fail(SB2_ECONFIG, "lambdarank needs a positive sigmoid");
+    const std::vector<double> gain = label_gains(o->label_gain, o->num_label_gain);
+    for (uint64_t i = 0; i < n; ++i) {
+        const float l = d->label[i];
+        if (std::fabs(static_cast<double>(l) - static_cast<double>(static_cast<int32_t>(l))) > static_cast<double>(1e-15f) ||
+            l < 0.0f || static_cast<size_t>(l) >= gain.size())
+            return b->fail(SB2_EDATA, "lambdarank label " + std::to_string(l) + " of row " + std::to_string(i) +
+                                          " is not a non-negative integer below the " + std::to_string(gain.size()) +
+                                          " label gains");
+    }
+    std::vector<double> discount(kMaxQueryRows);
+    for (uint32_t i = 0; i < kMaxQueryRows; ++i) discount[i] = 1.0 / std::log2(2.0 + static_cast<double>(i));
+    const size_t k = o->lambdarank_truncation_level;
+    std::vector<double> inverse_max_dcg(nq);
+    std::vector<size_t> count(gain.size());
+    for (uint32_t q = 0; q < nq; ++q) {
+        std::fill(count.begin(), count.end(), 0);
+        for (uint32_t r = qb[q]; r < qb[q + 1]; ++r) ++count[static_cast<size_t>(d->label[r])];
+        size_t top = gain.size() - 1;
+        double dcg = 0.0;
+        for (size_t j = 0; j < std::min<size_t>(k, qb[q + 1] - qb[q]); ++j) {
+            while (top > 0 && count[top] == 0) --top;
+            dcg += discount[j] * gain[top];
+            --count[top];  // wraps at label 0, as the reference's wrapping_sub
+        }
+        inverse_max_dcg[q] = dcg > 0.0 ? 1.0 / dcg : 0.0;
+    }
+    RankArgs& a = b->ranking;
+    a = RankArgs{};
+    a.sigmoid = o->sigmoid;
+    a.sigmoid_squared = o->sigmoid * o->sigmoid;
+    a.min_input = -50.0 / o->sigmoid / 2.0;
+    a.max_input = -a.min_input;
+    a.idx_factor = static_cast<double>(kSigmoidBins) / (a.max_input - a.min_input);
+    std::vector<double> table(kSigmoidBins);
+    for (uint32_t i = 0; i < kSigmoidBins; ++i) {
+        const double score = static_cast<double>(i) / a.idx_factor + a.min_input;
+        table[i] = 1.0 / (1.0 + std::exp(score * o->sigmoid));
+    }
+    SB2_CUDA(b, b->rk_bounds.alloc(sizeof(uint32_t) * (nq + 1ull)));
+    SB2_CUDA(b, b->rk_imdcg.alloc(sizeof(double) * nq));
+    SB2_CUDA(b, b->rk_gain.alloc(sizeof(double) * gain.size()));
+    SB2_CUDA(b, b->rk_discount.alloc(sizeof(double) * discount.size()));
+    SB2_CUDA(b, b->rk_table.alloc(sizeof(double) * table.size()));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_bounds.ptr, qb, sizeof(uint32_t) * (nq + 1ull), cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_imdcg.ptr, inverse_max_dcg.data(), sizeof(double) * nq, cudaMemcpyHostToDevice,
+                                b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_gain.ptr, gain.data(), sizeof(double) * gain.size(), cudaMemcpyHostToDevice,
+                                b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_discount.ptr, discount.data(), sizeof(double) * discount.size(),
+                                cudaMemcpyHostToDevice, b->stream));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_table.ptr, table.data(), sizeof(double) * table.size(), cudaMemcpyHostToDevice,
+                                b->stream));
+    SB2_TRY(b->sync());  // the host tables go out of scope
+    a.bounds = b->rk_bounds.as<uint32_t>();
+    a.inverse_max_dcg = b->rk_imdcg.as<double>();
+    a.label_gain = b->rk_gain.as<double>();
+    a.discount = b->rk_discount.as<double>();
+    a.table = b->rk_table.as<double>();
+    a.num_queries = nq;
+    a.cap = 2;
+    while (a.cap < longest) a.cap <<= 1;
+    a.truncation = static_cast<uint32_t>(std::min<size_t>(k, 0xFFFFFFFFu));
+    a.norm = o->lambdarank_norm != 0;
+    int per_sm = 0;
+    SB2_CUDA(b, lambdarank_configure(a.cap, &per_sm));
+    if (per_sm < 1) return b->fail(SB2_EUNSUPPORTED, "the lambdarank kernel does not fit this dataset's queries");
+    a.grid = static_cast<uint32_t>(std::max(1, std::min<int>(static_cast<int>(std::min<uint32_t>(nq, 1u << 30)),
+                                                            b->sms * per_sm)));
+    b->rank_gain = gain;
+    return SB2_OK;
+}
+
+}  // namespace
+
 // Backend::load
 int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* objective) {
     if (!b || !train || !objective) return SB2_EDEVICE;
     SB2_CUDA(b, cudaSetDevice(b->device));
     if (train->num_rows > 0xFFFFFFFFull)
         return b->fail(SB2_EUNSUPPORTED, std::to_string(train->num_rows) + " rows on one rank; the limit is 2^32 - 1");
-    if (objective->kind != SB2_REGRESSION && objective->kind != SB2_BINARY)
+    if (objective->kind != SB2_REGRESSION && objective->kind != SB2_BINARY && objective->kind != SB2_LAMBDARANK)
         return b->fail(SB2_EUNSUPPORTED, "objective " + std::to_string(objective->kind) + " has no device gradients");
+    b->ranking = RankArgs{};
+    if (objective->kind == SB2_LAMBDARANK) SB2_TRY(load_ranking(b, train, objective));
     const uint32_t F = train->num_features;
     b->features.assign(train->features, train->features + F);
     b->upper_bounds.assign(F, {});
@@ -657,6 +770,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     b->num_features = F;
     b->total_bins = train->total_bins;
     b->objective = *objective;
+    b->objective.label_gain = nullptr;  // the gains live in rank_gain; the caller's array is not kept
     b->weighted = train->weight != nullptr;
 
     // Device buffers.
@@ -1459,6 +1573,11 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     SB2_CUDA(b, cudaSetDevice(b->device));
     SB2_TRY(setup_exchange(b));
     if (p->objective != b->objective.kind) return b->fail(SB2_ECONFIG, "params objective differs from the loaded one");
+    if (p->objective == SB2_LAMBDARANK &&
+        (p->sigmoid != b->objective.sigmoid || (p->lambdarank_norm != 0) != (b->ranking.norm != 0) ||
+         p->lambdarank_truncation_level != b->objective.lambdarank_truncation_level ||
+         label_gains(p->label_gain, p->num_label_gain) != b->rank_gain))
+        return b->fail(SB2_ECONFIG, "lambdarank parameters differ from the loaded objective's");
     if (!p->use_quantized_grad) return b->fail(SB2_EUNSUPPORTED, "the device trainer is quantized only");
     if (p->bagging_fraction < 1.0 && p->bagging_freq > 0)
         return b->fail(SB2_EUNSUPPORTED, "bagging in the device trainer");

@@ -688,7 +688,13 @@ __global__ void division_check_kernel(uint64_t n, uint32_t seed, unsigned long l
 
 }  // namespace
 
-void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) { gradients_kernel<<<grid, kRowThreads, 0, s>>>(a); }
+void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) {
+    if (a.r.objective == SB2_LAMBDARANK)
+        launch_lambdarank(a.r, &a.t.iter->stopped, &a.t.iter->max_abs_grad_bits, &a.t.iter->max_hess_bits,
+                          static_cast<int>(a.r.rank.grid), s);
+    else
+        gradients_kernel<<<grid, kRowThreads, 0, s>>>(a);
+}
 void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s) {
     iteration_start_kernel<<<grid, kRowThreads, 0, s>>>(a);
 }
@@ -703,7 +709,10 @@ void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s) {
     add_tree_partition_kernel<<<grid, kRowThreads, 0, s>>>(a);
 }
 void launch_api_gradients(const RowArgs& r, unsigned long long* bits, int grid, cudaStream_t s) {
-    api_gradients_kernel<<<grid, kRowThreads, 0, s>>>(r, bits);
+    if (r.objective == SB2_LAMBDARANK)
+        launch_lambdarank(r, nullptr, bits, bits + 1, static_cast<int>(r.rank.grid), s);
+    else
+        api_gradients_kernel<<<grid, kRowThreads, 0, s>>>(r, bits);
 }
 void launch_api_quantize(const RowArgs& r, const sb2_quant_spec& spec, int grid, cudaStream_t s) {
     api_quantize_kernel<<<grid, kRowThreads, 0, s>>>(r, spec);

@@ -5,11 +5,31 @@
 
 namespace sb2 {
 
+// LambdaRank (objective/lambdarank.rs; ObjectiveSetup::LambdaRank, backend/mod.rs:58-71): the rank's queries and
+// the tables the host computes once at load with the same libm calls as the reference (the sigmoid table's exp,
+// the discounts' log2, the inverse max DCGs), so the device's pair arithmetic starts from the same values.
+constexpr uint32_t kSigmoidBins = 1u << 20;   // lambdarank.rs:31
+constexpr uint32_t kMaxQueryRows = 4096;      // longest query the device takes (its rows are sorted in shared memory)
+struct RankArgs {
+    const uint32_t* bounds;          // [num_queries + 1] row boundaries of the rank's queries
+    const double* inverse_max_dcg;   // [num_queries]
+    const double* label_gain;
+    const double* discount;          // [kMaxQueryRows]: 1 / log2(2 + rank)
+    const double* table;             // [kSigmoidBins]: LightGBM's sigmoid table
+    uint32_t num_queries;
+    uint32_t cap;                    // a power of two >= the longest query (and >= 2): rows a CTA sorts
+    uint32_t truncation;             // lambdarank_truncation_level
+    int32_t norm;                    // lambdarank_norm
+    uint32_t grid;                   // CTAs of the gradient launch
+    uint32_t pad_;
+    double sigmoid, sigmoid_squared, min_input, max_input, idx_factor;
+};
+
 // The objective and the rows the gradient and score kernels read.
 struct RowArgs {
     uint64_t num_rows;
     uint64_t row_offset;
-    int32_t objective;   // SB2_REGRESSION / SB2_BINARY
+    int32_t objective;   // SB2_REGRESSION / SB2_BINARY / SB2_LAMBDARANK
     int32_t pad_;
     double sigmoid;
     const float* label;
@@ -18,6 +38,7 @@ struct RowArgs {
     float* grad;
     float* hess;
     int32_t* packed;
+    RankArgs rank;        // lambdarank only
 };
 
 // Training constants of one run (Params subset) the iteration kernels need.
@@ -61,6 +82,12 @@ struct TileNode {
 constexpr int kRowThreads = 256;
 
 void launch_gradients(const IterArgs& a, int grid, cudaStream_t s);
+// LambdaRank gradients of every query (lambdarank.cu) and their maxima (atomicMax of the f64 bits of |grad|, |hess|);
+// nothing when `stopped` (may be null) is set. The kernel's dynamic shared memory is lambdarank_smem(cap) bytes.
+size_t lambdarank_smem(uint32_t cap);
+cudaError_t lambdarank_configure(uint32_t cap, int* blocks_per_sm);
+void launch_lambdarank(const RowArgs& r, const int32_t* stopped, unsigned long long* max_g, unsigned long long* max_h,
+                       int grid, cudaStream_t s);
 void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s);
 void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s);
 void launch_finalize(const IterArgs& a, cudaStream_t s);

@@ -57,11 +57,13 @@ class BinnedDataset:
     total_bins: int
     label: np.ndarray
     weight: np.ndarray | None = None
+    # lambdarank: num_queries + 1 row boundaries of the rank's queries (data/mod.rs:62-74), starting at 0
+    query_boundaries: np.ndarray | None = None
     _keep: list = field(default_factory=list, repr=False)
 
     @staticmethod
     def from_bins(bins: np.ndarray, mappers: list[FeatureMeta], label: np.ndarray, *, weight=None,
-                  row_offset: int = 0) -> "BinnedDataset":
+                  row_offset: int = 0, query_boundaries=None) -> "BinnedDataset":
         """Packs per-feature bins (uint8 [rows, features]) into groups: `layout` (data/build.rs:336-382), the
         non-trivial features in input order, a new group whenever the next feature's bins would take the current one
         over GROUP_BIN_BUDGET."""
@@ -96,7 +98,8 @@ class BinnedDataset:
             out_groups.append(FeatureGroup(g["features"], stride, g["hist_offset"], g["total_bins"], data))
         label = np.ascontiguousarray(label, dtype=np.float32)
         weight = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
-        return BinnedDataset(rows, row_offset, features, out_groups, offset, label, weight)
+        qb = None if query_boundaries is None else np.ascontiguousarray(query_boundaries, dtype=np.uint32)
+        return BinnedDataset(rows, row_offset, features, out_groups, offset, label, weight, qb)
 
     def bin(self, feature: int, row: int) -> int:
         m = self.features[feature]
@@ -107,12 +110,20 @@ class BinnedDataset:
         return self.groups[m.group].data[:, m.column]
 
     def shard(self, begin: int, end: int) -> "BinnedDataset":
-        """Rows begin..end as one rank holds them: `row_offset` moves by `begin` (data/mod.rs:64-65)."""
+        """Rows begin..end as one rank holds them: `row_offset` moves by `begin` (data/mod.rs:64-65). With queries,
+        begin and end must be query boundaries: a query's rows stay on one rank."""
         groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins,
                                np.ascontiguousarray(g.data[begin:end])) for g in self.groups]
+        qb = None
+        if self.query_boundaries is not None:
+            qb_all = self.query_boundaries.astype(np.int64)
+            lo, hi = np.searchsorted(qb_all, [begin, end])
+            if lo >= len(qb_all) or qb_all[lo] != begin or hi >= len(qb_all) or qb_all[hi] != end:
+                raise ValueError(f"rows {begin}..{end} cut a query")
+            qb = np.ascontiguousarray(qb_all[lo:hi + 1] - begin, dtype=np.uint32)
         return BinnedDataset(end - begin, self.row_offset + begin, self.features, groups, self.total_bins,
                              np.ascontiguousarray(self.label[begin:end]),
-                             None if self.weight is None else np.ascontiguousarray(self.weight[begin:end]))
+                             None if self.weight is None else np.ascontiguousarray(self.weight[begin:end]), qb)
 
     def c_struct(self) -> _abi.Dataset:
         """The dataset as `sb2_dataset`; the arrays it points to live as long as this object."""
@@ -149,6 +160,11 @@ class BinnedDataset:
             w = np.ascontiguousarray(self.weight, dtype=np.float32)
             keep.append(w)
             d.weight = w.ctypes.data_as(C.POINTER(C.c_float))
+        if self.query_boundaries is not None:
+            qb = np.ascontiguousarray(self.query_boundaries, dtype=np.uint32)
+            keep.append(qb)
+            d.num_queries = len(qb) - 1
+            d.query_boundaries = qb.ctypes.data_as(C.POINTER(C.c_uint32))
         d._keep = keep  # ctypes keeps Python attributes on the struct object alive with it
         return d
 

@@ -399,7 +399,8 @@ def _parse_tree(fields, num_features: int) -> TextTree:
 # ---- a trained model as a file ---------------------------------------------------------------------------
 
 def model_parameters(params: _abi.Params) -> list:
-    """`Params::model_parameters` (config.rs:444-498) for the parameters a device-trained model carries; the
+    """`Params::model_parameters` (config.rs:444-498) for the parameters a device-trained model carries (lambdarank's
+    three after the quantization ones, config.rs:486-493); the
     binning and categorical parameters the device trainer does not take keep the reference's defaults
     (config.rs:123-167)."""
     objective = {_abi.REGRESSION: "regression", _abi.BINARY: "binary"}.get(params.objective, "lambdarank")
@@ -419,6 +420,14 @@ def model_parameters(params: _abi.Params) -> list:
            ("num_grad_quant_bins", str(params.num_grad_quant_bins)),
            ("quant_train_renew_leaf", str(int(bool(params.quant_train_renew_leaf)))),
            ("stochastic_rounding", str(int(bool(params.stochastic_rounding))))]
+    if objective == "lambdarank":
+        if params.label_gain and params.num_label_gain:
+            gains = [params.label_gain[i] for i in range(params.num_label_gain)]
+        else:
+            gains = [float((1 << i) - 1) for i in range(31)]  # config.rs:118-121
+        out += [("lambdarank_truncation_level", str(params.lambdarank_truncation_level)),
+                ("lambdarank_norm", str(int(bool(params.lambdarank_norm)))),
+                ("label_gain", ",".join(g(v) for v in gains))]
     if objective != "regression":
         out.append(("sigmoid", g(params.sigmoid)))
     return out

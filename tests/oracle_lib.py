@@ -34,6 +34,10 @@ _SIGS = {
     "orc_gradients": (None, [P(_abi.Objective), P(C.c_float), P(C.c_float), P(C.c_float), C.c_size_t, P(C.c_float),
                              P(C.c_float)]),
     "orc_init_score": (C.c_double, [P(_abi.Params), P(C.c_float), P(C.c_float), C.c_size_t]),
+    "orc_lambdarank_gradients": (C.c_int, [P(_abi.Params), P(_abi.Dataset), P(C.c_float), P(C.c_float),
+                                           P(C.c_float)]),
+    "orc_lambdarank_max_dcg": (C.c_double, [C.c_size_t, P(C.c_float), C.c_size_t, P(C.c_double), C.c_size_t]),
+    "orc_lambdarank_sigmoid": (C.c_double, [C.c_double, C.c_double]),
     "orc_histogram": (C.c_int, [P(_abi.Dataset), P(C.c_int32), C.c_int32, P(C.c_uint32), C.c_size_t, P(C.c_uint8),
                                 P(C.c_double)]),
     "orc_partition": (C.c_uint32, [P(_abi.Dataset), P(_abi.BinSplit), P(C.c_uint32), C.c_size_t]),
@@ -135,6 +139,39 @@ def gradients(objective, scores, label, weight=None, sigmoid=1.0):
     lib().orc_gradients(C.byref(o), _p(s, C.c_float), _p(lb, C.c_float), None if w is None else _p(w, C.c_float),
                         len(s), _p(g, C.c_float), _p(h, C.c_float))
     return g, h
+
+
+def lambdarank_gradients(params: _abi.Params, label, scores, query_boundaries, weight=None):
+    """objective/lambdarank.rs gradients of every query at `scores`: (grad, hess) f32, or raises on rejected
+    labels or queries."""
+    label = np.ascontiguousarray(label, dtype=np.float32)
+    scores = np.ascontiguousarray(scores, dtype=np.float32)
+    qb = np.ascontiguousarray(query_boundaries, dtype=np.uint32)
+    d = _abi.Dataset()
+    d.num_rows, d.num_queries = len(label), len(qb) - 1
+    d.label = _p(label, C.c_float)
+    d.query_boundaries = _p(qb, C.c_uint32)
+    w = None
+    if weight is not None:
+        w = np.ascontiguousarray(weight, dtype=np.float32)
+        d.weight = _p(w, C.c_float)
+    grad = np.full(len(label), np.nan, dtype=np.float32)
+    hess = np.full(len(label), np.nan, dtype=np.float32)
+    code = lib().orc_lambdarank_gradients(C.byref(params), C.byref(d), _p(scores, C.c_float), _p(grad, C.c_float),
+                                          _p(hess, C.c_float))
+    if code != 0:
+        raise ValueError(lib().orc_last_error().decode())
+    return grad, hess
+
+
+def lambdarank_max_dcg(k, labels, gain) -> float:
+    labels = np.ascontiguousarray(labels, dtype=np.float32)
+    gain = np.ascontiguousarray(gain, dtype=np.float64)
+    return lib().orc_lambdarank_max_dcg(k, _p(labels, C.c_float), len(labels), _p(gain, C.c_double), len(gain))
+
+
+def lambdarank_sigmoid(sigmoid: float, delta: float) -> float:
+    return lib().orc_lambdarank_sigmoid(sigmoid, delta)
 
 
 def leaf_sums(grad, hess, partition_rows, leaves, gs, hs) -> np.ndarray:
@@ -271,7 +308,7 @@ def default_params(**overrides) -> _abi.Params:
                     min_gain_to_split=0.0, bagging_fraction=1.0, bagging_freq=0, bagging_seed=3,
                     feature_fraction=1.0, feature_fraction_seed=2, data_random_seed=1, boost_from_average=1,
                     use_quantized_grad=1, sigmoid=1.0, num_grad_quant_bins=4, quant_train_renew_leaf=1,
-                    stochastic_rounding=1)
+                    stochastic_rounding=1, lambdarank_norm=1, lambdarank_truncation_level=30)
     defaults.update(overrides)
     for k, v in defaults.items():
         setattr(p, k, v)

@@ -70,3 +70,23 @@ def nested_binned(rows: int, seed: int = 7) -> BinnedDataset:
     label = (label + 0.2 * (unit(seed * 1000 + 999, r) - 0.5)).astype(np.float32)
     mappers = [numerical_mapper(f"f{f}", nb, False) for f, nb in enumerate(widths)]
     return BinnedDataset.from_bins(bins, mappers, label)
+
+
+def ranking_binned(rows: int, bins_per_feature: list[int], seed: int = 1, mean_query: float = 40.0,
+                   long_query: int = 0) -> BinnedDataset:
+    """A lambdarank dataset: hash-drawn bins, queries of Poisson(mean_query) rows (at least 1; one query of
+    `long_query` rows first when given), labels 0..4: a noisy score of a few features cut into five levels."""
+    data = random_binned(rows, bins_per_feature, seed=seed)
+    rng = np.random.default_rng(seed)
+    sizes = [long_query] if long_query else []
+    while sum(sizes) < rows:
+        sizes.append(max(1, int(rng.poisson(mean_query))))
+    sizes[-1] -= sum(sizes) - rows
+    if sizes[-1] == 0:
+        sizes.pop()
+    qb = np.concatenate([[0], np.cumsum(sizes)]).astype(np.uint32)
+    score = data.label.astype(np.float64) + 0.3 * rng.normal(size=rows)
+    label = np.clip(np.floor((score - score.min()) / (np.ptp(score) + 1e-12) * 5.0), 0, 4).astype(np.float32)
+    data.label = label
+    data.query_boundaries = qb
+    return data

@@ -4,8 +4,9 @@ Default workload: BASELINE.json configs[3] ("c4"), the largest configuration tha
 scaling target names: L2 regression, 100,000,000 rows x 256 f32 features ~ N(0,1), target = a random 32-feature
 linear function + N(0,1) noise, 255 bins, 255 leaves, quantized gradients (4 bins), 200 trees in a full job.
 `--config` selects another configuration: c1 (configs[0]: 1M x 28 L2, 63 leaves, 100 trees), c2 (configs[1]:
-10M x 100 binary, 255 leaves, 500 trees) or c3 (configs[2]: 2M x 136 lambdarank over queries of Poisson(120) rows,
-127 leaves, 300 trees). A "step" is one boosting iteration: gradients, quantization, a tree grown
+10M x 100 binary, 255 leaves, 500 trees), c3 (configs[2]: 2M x 136 lambdarank over queries of Poisson(120) rows,
+127 leaves, 300 trees) or c5 (configs[4]: 5M x 2000 binary, 63 bins, 80% of the features 95% zeros, 31 leaves,
+200 trees). A "step" is one boosting iteration: gradients, quantization, a tree grown
 split by split on the device (partition, smaller-child histogram, sibling subtraction, split scan, leaf choice),
 leaf renewal and the score update.
 
@@ -84,6 +85,9 @@ CONFIGS = {
     "c3": Config("c3", 2, 2_000_000, "lambdarank", 255, 127, 300,
                  ["gauss"] * 60 + ["lognormal"] * 40 + ["zeros30"] * 36),
     "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256),
+    # 80% of the features zero-dominant (every fifth feature is N(0,1), the rest 95% zeros)
+    "c5": Config("c5", 4, 5_000_000, "binary", 63, 31, 200,
+                 ["gauss" if f % 5 == 0 else "sparse95" for f in range(2000)]),
 }
 CFG = CONFIGS["c4"]
 ROWS = CFG.rows
@@ -140,7 +144,8 @@ def _gauss(stream: int, rows):
 
 def column(f: int, rows):
     """Feature f of `rows` (f64): kind "gauss" ~ N(0,1) (streams 2f, 2f+1), "unif" ~ U[0,1) (stream 1000 + f),
-    "lognormal" = exp(N(0,1)), "zeros30" = N(0,1) with 30% of the rows exactly 0 (stream 3000 + f)."""
+    "lognormal" = exp(N(0,1)), "zeros30" / "sparse95" = N(0,1) with 30% / 95% of the rows exactly 0 (stream
+    3000 + f)."""
     kind = CFG.kinds[f]
     if kind == "gauss":
         return _gauss(2 * f, rows)
@@ -152,6 +157,8 @@ def column(f: int, rows):
         return torch.exp(_gauss(2 * f, rows))
     if kind == "zeros30":
         return _gauss(2 * f, rows) * (_unit(3000 + f, rows) >= 0.3)
+    if kind == "sparse95":
+        return _gauss(2 * f, rows) * (_unit(3000 + f, rows) >= 0.95)
     raise ValueError(kind)
 
 
@@ -198,12 +205,21 @@ def features_of(rows, device):
 def labels_of(rows):
     """The config's label, computing only the features it depends on.
     c1: 8 random-weight features + 0.5 x0 x1 + N(0, 0.1); c2: Bernoulli(sigmoid(sparse linear in 12 features + 3
-    pairwise interactions)); c4: a linear function of 32 random features + N(0, 1)."""
+    pairwise interactions)); c3: relevance 0..4 (_relevance); c4: a linear function of 32 random features + N(0, 1);
+    c5: Bernoulli(sigmoid(linear in 50 random features))."""
     import torch
 
     x = lambda f: column(int(f), rows).to(torch.float32).double()  # noqa: E731  (the f32 feature, as binned)
     if CFG.name == "c3":
         return _relevance(rows, x)
+    if CFG.name == "c5":
+        g = np.random.default_rng(SEED + 5)
+        picked = g.choice(CFG.features, size=50, replace=False)
+        weights = g.normal(0.0, 1.0, size=50)
+        logit = torch.zeros(rows.numel(), dtype=torch.float64, device=rows.device)
+        for f, w in zip(picked, weights):
+            logit += float(w) * x(f)
+        return (_unit(5000, rows) < torch.sigmoid(logit)).to(torch.float32)
     if CFG.name == "c1":
         g = np.random.default_rng(SEED + 1)
         picked = g.choice(CFG.features, size=8, replace=False)
@@ -702,7 +718,7 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the oracle's trees (parity and, at N = 1, the CPU baseline)")
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS),
-                    help="c4 (default): BASELINE configs[3], 100M rows; c1, c2, c3: configs[0], [1], [2]")
+                    help="c4 (default): BASELINE configs[3], 100M rows; c1, c2, c3, c5: configs[0], [1], [2], [4]")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows of the synthetic set (a smaller case for profiling; default: the config's)")
     ap.add_argument("--trees", type=int, default=0,

@@ -98,7 +98,7 @@ struct sb2_backend {
     DeviceBuffer rows[2], ordered[2], flags, tile_left;
     DeviceBuffer staging, hist_job, step, iter, api_active, candidates, cand_flags, cand_gain, counter, maxima, misc;
     // lambdarank: the queries and the host-computed tables the gradient kernel reads (RankArgs)
-    DeviceBuffer rk_bounds, rk_imdcg, rk_gain, rk_discount, rk_table;
+    DeviceBuffer rk_bounds, rk_queries, rk_imdcg, rk_gain, rk_discount, rk_table;
     RankArgs ranking{};
     std::vector<double> rank_gain;            // the loaded label gains, to check training parameters against
     DeviceBuffer api_spec;                    // the QuantSpec of the last sb2_quantize
@@ -527,6 +527,15 @@ int load_ranking(sb2_backend* b, const sb2_dataset* d, const sb2_objective* o) {
         const double score = static_cast<double>(i) / a.idx_factor + a.min_input;
         table[i] = 1.0 / (1.0 + std::exp(score * o->sigmoid));
     }
+    // The queries the warp kernel takes (at most lambdarank_warp_rows() rows), then the rest, each in row order.
+    std::vector<uint32_t> order;
+    for (uint32_t q = 0; q < nq; ++q)
+        if (qb[q + 1] - qb[q] <= lambdarank_warp_rows()) order.push_back(q);
+    const uint32_t num_short = static_cast<uint32_t>(order.size());
+    for (uint32_t q = 0; q < nq; ++q)
+        if (qb[q + 1] - qb[q] > lambdarank_warp_rows()) order.push_back(q);
+    SB2_CUDA(b, b->rk_queries.alloc(sizeof(uint32_t) * nq));
+    SB2_CUDA(b, cudaMemcpyAsync(b->rk_queries.ptr, order.data(), sizeof(uint32_t) * nq, cudaMemcpyHostToDevice, b->stream));
     SB2_CUDA(b, b->rk_bounds.alloc(sizeof(uint32_t) * (nq + 1ull)));
     SB2_CUDA(b, b->rk_imdcg.alloc(sizeof(double) * nq));
     SB2_CUDA(b, b->rk_gain.alloc(sizeof(double) * gain.size()));
@@ -543,6 +552,9 @@ int load_ranking(sb2_backend* b, const sb2_dataset* d, const sb2_objective* o) {
                                 b->stream));
     SB2_TRY(b->sync());  // the host tables go out of scope
     a.bounds = b->rk_bounds.as<uint32_t>();
+    a.queries = b->rk_queries.as<uint32_t>();
+    a.num_short = num_short;
+    a.num_gain = static_cast<uint32_t>(gain.size());
     a.inverse_max_dcg = b->rk_imdcg.as<double>();
     a.label_gain = b->rk_gain.as<double>();
     a.discount = b->rk_discount.as<double>();
@@ -552,11 +564,12 @@ int load_ranking(sb2_backend* b, const sb2_dataset* d, const sb2_objective* o) {
     while (a.cap < longest) a.cap <<= 1;
     a.truncation = static_cast<uint32_t>(std::min<size_t>(k, 0xFFFFFFFFu));
     a.norm = o->lambdarank_norm != 0;
-    int per_sm = 0;
-    SB2_CUDA(b, lambdarank_configure(a.cap, &per_sm));
-    if (per_sm < 1) return b->fail(SB2_EUNSUPPORTED, "the lambdarank kernel does not fit this dataset's queries");
-    a.grid = static_cast<uint32_t>(std::max(1, std::min<int>(static_cast<int>(std::min<uint32_t>(nq, 1u << 30)),
-                                                            b->sms * per_sm)));
+    int warp_per_sm = 0, cta_per_sm = 0;
+    SB2_CUDA(b, lambdarank_configure(a.cap, &warp_per_sm, &cta_per_sm));
+    if (warp_per_sm < 1 || (num_short < nq && cta_per_sm < 1))
+        return b->fail(SB2_EUNSUPPORTED, "the lambdarank kernels do not fit this dataset's queries");
+    a.warp_grid = static_cast<uint32_t>(std::max(1, b->sms * warp_per_sm));
+    a.cta_grid = static_cast<uint32_t>(std::max(1, std::min<int>(static_cast<int>(nq - num_short), b->sms * cta_per_sm)));
     b->rank_gain = gain;
     return SB2_OK;
 }

@@ -690,8 +690,7 @@ __global__ void division_check_kernel(uint64_t n, uint32_t seed, unsigned long l
 
 void launch_gradients(const IterArgs& a, int grid, cudaStream_t s) {
     if (a.r.objective == SB2_LAMBDARANK)
-        launch_lambdarank(a.r, &a.t.iter->stopped, &a.t.iter->max_abs_grad_bits, &a.t.iter->max_hess_bits,
-                          static_cast<int>(a.r.rank.grid), s);
+        launch_lambdarank(a.r, &a.t.iter->stopped, &a.t.iter->max_abs_grad_bits, &a.t.iter->max_hess_bits, s);
     else
         gradients_kernel<<<grid, kRowThreads, 0, s>>>(a);
 }
@@ -710,7 +709,7 @@ void launch_add_tree_partition(const IterArgs& a, int grid, cudaStream_t s) {
 }
 void launch_api_gradients(const RowArgs& r, unsigned long long* bits, int grid, cudaStream_t s) {
     if (r.objective == SB2_LAMBDARANK)
-        launch_lambdarank(r, nullptr, bits, bits + 1, static_cast<int>(r.rank.grid), s);
+        launch_lambdarank(r, nullptr, bits, bits + 1, s);
     else
         api_gradients_kernel<<<grid, kRowThreads, 0, s>>>(r, bits);
 }

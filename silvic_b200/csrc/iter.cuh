@@ -12,16 +12,18 @@ constexpr uint32_t kSigmoidBins = 1u << 20;   // lambdarank.rs:31
 constexpr uint32_t kMaxQueryRows = 4096;      // longest query the device takes (its rows are sorted in shared memory)
 struct RankArgs {
     const uint32_t* bounds;          // [num_queries + 1] row boundaries of the rank's queries
+    const uint32_t* queries;         // [num_queries]: the short queries (a warp each), then the long ones (a CTA each)
     const double* inverse_max_dcg;   // [num_queries]
-    const double* label_gain;
+    const double* label_gain;        // [num_gain]
     const double* discount;          // [kMaxQueryRows]: 1 / log2(2 + rank)
     const double* table;             // [kSigmoidBins]: LightGBM's sigmoid table
     uint32_t num_queries;
-    uint32_t cap;                    // a power of two >= the longest query (and >= 2): rows a CTA sorts
+    uint32_t num_short;              // queries of at most lambdarank_warp_rows() rows
+    uint32_t cap;                    // a power of two >= the longest query (and >= 2): the CTA kernel's rows
     uint32_t truncation;             // lambdarank_truncation_level
+    uint32_t num_gain;
     int32_t norm;                    // lambdarank_norm
-    uint32_t grid;                   // CTAs of the gradient launch
-    uint32_t pad_;
+    uint32_t warp_grid, cta_grid;    // CTAs of the two gradient launches
     double sigmoid, sigmoid_squared, min_input, max_input, idx_factor;
 };
 
@@ -83,11 +85,13 @@ constexpr int kRowThreads = 256;
 
 void launch_gradients(const IterArgs& a, int grid, cudaStream_t s);
 // LambdaRank gradients of every query (lambdarank.cu) and their maxima (atomicMax of the f64 bits of |grad|, |hess|);
-// nothing when `stopped` (may be null) is set. The kernel's dynamic shared memory is lambdarank_smem(cap) bytes.
+// nothing when `stopped` (may be null) is set. Queries of at most lambdarank_warp_rows() rows take a warp each, longer
+// ones (up to kMaxQueryRows) a CTA each with lambdarank_smem(cap) bytes of dynamic shared memory.
 size_t lambdarank_smem(uint32_t cap);
-cudaError_t lambdarank_configure(uint32_t cap, int* blocks_per_sm);
+uint32_t lambdarank_warp_rows();
+cudaError_t lambdarank_configure(uint32_t cap, int* warp_blocks_per_sm, int* cta_blocks_per_sm);
 void launch_lambdarank(const RowArgs& r, const int32_t* stopped, unsigned long long* max_g, unsigned long long* max_h,
-                       int grid, cudaStream_t s);
+                       cudaStream_t s);
 void launch_iteration_start(const IterArgs& a, int grid, cudaStream_t s);
 void launch_leaf_sums(const IterArgs& a, int grid, cudaStream_t s);
 void launch_finalize(const IterArgs& a, cudaStream_t s);

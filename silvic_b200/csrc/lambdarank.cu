@@ -167,8 +167,9 @@ __device__ __forceinline__ void store_row(const RowArgs& r, uint64_t at, double 
 
 // ---- a warp per query ------------------------------------------------------------------------------------------
 
-// Per warp: the keys (cap u64), then per rank slot the score (f64), the three term arrays (f64) and the label (f32).
-constexpr size_t kWarpSlotBytes = 8 + 8 + 3 * 8 + 4;
+// Per warp: the keys (cap u64), then per rank slot the three term arrays (f64), the score and the label (f32; the
+// f64 score is the f32 one converted, exactly).
+constexpr size_t kWarpSlotBytes = 8 + 3 * 8 + 4 + 4;
 
 __global__ void __launch_bounds__(kRankThreads) lambdarank_warp_kernel(RowArgs r, const uint32_t* queries,
                                                                         uint32_t num_queries, const int32_t* stopped,
@@ -184,11 +185,11 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_warp_kernel(RowArgs r
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = kRankThreads / 32;
     unsigned char* mine = smem + static_cast<size_t>(warp) * kWarpQueryRows * kWarpSlotBytes;
     unsigned long long* key = reinterpret_cast<unsigned long long*>(mine);
-    double* score = reinterpret_cast<double*>(key + kWarpQueryRows);
-    double* t_lambda = score + kWarpQueryRows;
+    double* t_lambda = reinterpret_cast<double*>(key + kWarpQueryRows);
     double* t_hessian = t_lambda + kWarpQueryRows;
     double* t_sum = t_hessian + kWarpQueryRows;
-    float* label = reinterpret_cast<float*>(t_sum + kWarpQueryRows);
+    float* score = reinterpret_cast<float*>(t_sum + kWarpQueryRows);
+    float* label = score + kWarpQueryRows;
     const auto sync = [] { __syncwarp(); };
     double mg = 0.0, mh = 0.0;
     for (uint32_t qi = blockIdx.x * warps + warp; qi < num_queries; qi += gridDim.x * warps) {
@@ -214,23 +215,23 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_warp_kernel(RowArgs r
             hes[m] = 0.0;
             if (i < n) {
                 row[m] = static_cast<uint32_t>(key[i]);
-                const double s = static_cast<double>(r.scores[b + row[m]]);
+                const float s = r.scores[b + row[m]];
                 score[i] = s;
                 label[i] = r.label[b + row[m]];
-                if (s == -CUDART_INF) valid = min(valid, i);
+                if (s == -CUDART_INF_F) valid = min(valid, i);
             }
         }
         for (int o = 16; o > 0; o >>= 1) valid = min(valid, __shfl_xor_sync(0xffffffffu, valid, o));
         __syncwarp();
         uint32_t worst = n - 1;  // worst_score (lambdarank.rs:344-351): one trailing -inf skipped
-        if (worst > 0 && score[worst] == -CUDART_INF) --worst;
+        if (worst > 0 && score[worst] == -CUDART_INF_F) --worst;
         PairCtx c{};
         c.by_distance = k.norm != 0 && score[0] != score[worst];
         c.inverse_max_dcg = k.inverse_max_dcg[q];
         const uint32_t rows_i = min(k.truncation, valid > 0 ? valid - 1 : 0u);
         double total = 0.0;  // lane 2: the sum of lambdas over the pairs so far
         for (uint32_t i = 0; i < rows_i; ++i) {
-            c.score_i = score[i];
+            c.score_i = static_cast<double>(score[i]);
             c.label_i = label[i];
             c.gain_i = gain_of(k, s_gain, c.label_i);
             c.discount_i = __ldg(k.discount + i);
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_warp_kernel(RowArgs r
                 const uint32_t j = lane + 32 * m;
                 if (j > i && j < valid) {
                     const float lj = label[j];
-                    const PairTerms t = pair_terms(k, c, score[j], gain_of(k, s_gain, lj), j, lj);
+                    const PairTerms t = pair_terms(k, c, static_cast<double>(score[j]), gain_of(k, s_gain, lj), j, lj);
                     if (t.counted) {
                         lam[m] = __dsub_rn(lam[m], t.lambda_j);
                         hes[m] = __dadd_rn(hes[m], t.hessian_j);
@@ -282,9 +283,9 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_warp_kernel(RowArgs r
 
 // ---- a CTA per query -------------------------------------------------------------------------------------------
 
-// Per rank slot: the key (u64; after the gather, the row in its low half), the score, lambda, hessian and the three
-// term arrays (f64), the label (f32).
-constexpr size_t kCtaSlotBytes = 8 + 6 * 8 + 4;
+// Per rank slot: the key (u64; after the gather, the row in its low half), lambda, hessian and the three term arrays
+// (f64), the score and the label (f32): 56 bytes, so a 4096-row query fits a CTA's shared memory.
+constexpr size_t kCtaSlotBytes = 8 + 5 * 8 + 4 + 4;
 
 __global__ void __launch_bounds__(kRankThreads) lambdarank_cta_kernel(RowArgs r, const uint32_t* queries,
                                                                        uint32_t num_queries, const int32_t* stopped,
@@ -298,13 +299,13 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_cta_kernel(RowArgs r,
     const RankArgs& k = r.rank;
     const uint32_t cap_max = k.cap;
     unsigned long long* key = reinterpret_cast<unsigned long long*>(smem);
-    double* score = reinterpret_cast<double*>(key + cap_max);
-    double* lam = score + cap_max;
+    double* lam = reinterpret_cast<double*>(key + cap_max);
     double* hes = lam + cap_max;
     double* t_lambda = hes + cap_max;
     double* t_hessian = t_lambda + cap_max;
     double* t_sum = t_hessian + cap_max;
-    float* label = reinterpret_cast<float*>(t_sum + cap_max);
+    float* score = reinterpret_cast<float*>(t_sum + cap_max);
+    float* label = score + cap_max;
     for (uint32_t i = threadIdx.x; i < kSharedGains; i += kRankThreads)
         s_gain[i] = i < k.num_gain ? k.label_gain[i] : 0.0;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -323,30 +324,30 @@ __global__ void __launch_bounds__(kRankThreads) lambdarank_cta_kernel(RowArgs r,
         bitonic_sort(key, cap, tid, static_cast<uint32_t>(kRankThreads), sync);
         for (uint32_t i = tid; i < n; i += kRankThreads) {
             const uint32_t row = static_cast<uint32_t>(key[i]);
-            const double s = static_cast<double>(r.scores[b + row]);
+            const float s = r.scores[b + row];
             score[i] = s;
             label[i] = r.label[b + row];
             lam[i] = 0.0;
             hes[i] = 0.0;
-            if (s == -CUDART_INF) atomicMin(&s_valid, i);
+            if (s == -CUDART_INF_F) atomicMin(&s_valid, i);
         }
         __syncthreads();
         const uint32_t valid = s_valid;
         uint32_t worst = n - 1;
-        if (worst > 0 && score[worst] == -CUDART_INF) --worst;
+        if (worst > 0 && score[worst] == -CUDART_INF_F) --worst;
         PairCtx c{};
         c.by_distance = k.norm != 0 && score[0] != score[worst];
         c.inverse_max_dcg = k.inverse_max_dcg[q];
         const uint32_t rows_i = min(k.truncation, valid > 0 ? valid - 1 : 0u);
         double total = 0.0;  // thread 2: the sum of lambdas over the pairs so far
         for (uint32_t i = 0; i < rows_i; ++i) {
-            c.score_i = score[i];
+            c.score_i = static_cast<double>(score[i]);
             c.label_i = label[i];
             c.gain_i = gain_of(k, s_gain, c.label_i);
             c.discount_i = __ldg(k.discount + i);
             for (uint32_t j = i + 1 + tid; j < valid; j += kRankThreads) {
                 const float lj = label[j];
-                const PairTerms t = pair_terms(k, c, score[j], gain_of(k, s_gain, lj), j, lj);
+                const PairTerms t = pair_terms(k, c, static_cast<double>(score[j]), gain_of(k, s_gain, lj), j, lj);
                 if (t.counted) {
                     lam[j] = __dsub_rn(lam[j], t.lambda_j);
                     hes[j] = __dadd_rn(hes[j], t.hessian_j);

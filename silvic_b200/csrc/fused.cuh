@@ -607,42 +607,45 @@ __device__ __forceinline__ bool wait_peer(const uint32_t* flag, uint32_t epoch, 
     }
 }
 
-// One warp: waits, lane s for source rank s (s < world), until the flag at byte `off + 4 s` of this rank's own
-// exchange buffer reaches `epoch`; true when every rank's did.
-__device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int* error) {
+// One warp: waits, lane s for source rank s (s < world, s != `skip`), until the flag at byte `off + 4 s` of this
+// rank's own exchange buffer reaches `epoch`; true when every rank's did.
+__device__ __forceinline__ bool wait_ranks(const GrowExchange& x, size_t off, uint32_t epoch, int* error,
+                                           int skip = -1) {
     const int lane = static_cast<int>(threadIdx.x & 31);
     bool ok = true;
-    if (lane < x.world)
+    if (lane < x.world && lane != skip)
         ok = wait_peer(reinterpret_cast<const uint32_t*>(x.peers[x.rank] + off) + lane, epoch, x.spin_limit, error);
     return __all_sync(0xffffffffu, ok);
 }
 
 // Left count of split j from source rank s, in the exchange buffer's words (the step's parity).
-__device__ __forceinline__ size_t exchange_left_word(uint32_t epoch, int j, int s) {
-    return kXLeftValues / 4 + ((epoch & 1) * kSplits + static_cast<size_t>(j)) * kMaxRanks + s;
+__device__ __forceinline__ size_t exchange_left_word(const ExchangeLayout& L, uint32_t epoch, int j, int s) {
+    return L.left_values / 4 + ((epoch & 1) * kSplits + static_cast<size_t>(j)) * kMaxRanks + s;
 }
 
 // CTA 0, warp 0: this rank's left counts of the step's `n` splits into every rank's buffer (lane q writes rank
 // q's), each rank's followed by this rank's flag; the release store orders the counts before the flag.
-__device__ __forceinline__ void publish_left(const GrowExchange& x, uint32_t epoch, const uint32_t* left, int n) {
+__device__ __forceinline__ void publish_left(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch,
+                                             const uint32_t* left, int n) {
     const int q = static_cast<int>(threadIdx.x & 31);
     if (q < x.world) {
         uint32_t* dst = reinterpret_cast<uint32_t*>(x.peers[q]);
-        for (int j = 0; j < n; ++j) dst[exchange_left_word(epoch, j, x.rank)] = left[j];
-        st_release_sys(dst + kXLeftFlags / 4 + x.rank, epoch);
+        for (int j = 0; j < n; ++j) dst[exchange_left_word(L, epoch, j, x.rank)] = left[j];
+        st_release_sys(dst + L.left_flags / 4 + x.rank, epoch);
     }
 }
 
 // Whole CTA: every rank's left counts of the step's `n` splits, summed into total[j] (shared); false when a rank
 // did not answer.
-__device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoch, int n, int* error, int64_t* total) {
+__device__ __forceinline__ bool gather_left(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch, int n,
+                                            int* error, int64_t* total) {
     __shared__ int s_ok;
     if (threadIdx.x < 32) {
-        const bool ok = wait_ranks(x, kXLeftFlags, epoch, error);
+        const bool ok = wait_ranks(x, L.left_flags, epoch, error);
         const int lane = static_cast<int>(threadIdx.x);
         const uint32_t* own = reinterpret_cast<const uint32_t*>(x.peers[x.rank]);
         for (int j = 0; j < n; ++j) {
-            int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcg(own + exchange_left_word(epoch, j, lane))) : 0;
+            int64_t v = ok && lane < x.world ? static_cast<int64_t>(__ldcg(own + exchange_left_word(L, epoch, j, lane))) : 0;
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (lane == 0) total[j] = v;
         }
@@ -654,41 +657,115 @@ __device__ __forceinline__ bool gather_left(const GrowExchange& x, uint32_t epoc
     return ok;
 }
 
-// Whole CTA: split j's feature `f`'s built-child bins of this rank (`built`, shared) written into every rank's
-// buffer, then replaced by the sum of every rank's copies in this rank's buffer; false when a rank did not answer.
-__device__ __forceinline__ bool exchange_bins(const GrowExchange& x, uint32_t epoch, uint32_t F, uint32_t j, uint32_t f,
-                                              uint32_t nb, int2* built, int* error) {
+__device__ __forceinline__ int owner_of(const GrowExchange& x, uint32_t f) { return static_cast<int>(f % x.world); }
+
+// Item (j, feature f)'s word in the owner's item flags, and its bins from source s in the owner's buffer.
+__device__ __forceinline__ size_t item_flags_at(const ExchangeLayout& L, const GrowExchange& x, uint32_t j, uint32_t f) {
+    return L.item_flags + 4ull * (static_cast<size_t>(j) * L.owned + f / x.world) * kMaxRanks;
+}
+__device__ __forceinline__ size_t item_bins_at(const ExchangeLayout& L, const GrowExchange& x, int s, uint32_t j,
+                                               uint32_t f) {
+    return L.bins + 8ull * ((static_cast<size_t>(s) * kSplits + j) * L.owned + f / x.world) * kMaxBins;
+}
+
+// Whole CTA, at a feature this rank does not own: its built-child bins of split j (`built`, shared) written into
+// the owner's buffer, then this rank's flag for the item raised there.
+__device__ __forceinline__ void push_bins(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch, uint32_t j,
+                                          uint32_t f, uint32_t nb, const int2* built) {
+    const int owner = owner_of(x, f);
+    int2* dst = reinterpret_cast<int2*>(x.peers[owner] + item_bins_at(L, x, x.rank, j, f));
+    for (uint32_t t = threadIdx.x; t < nb; t += blockDim.x) dst[t] = built[t];
+    __syncthreads();  // the CTA's stores are issued: the release below orders them before the flag
+    if (threadIdx.x == 0)
+        st_release_sys(reinterpret_cast<uint32_t*>(x.peers[owner] + item_flags_at(L, x, j, f)) + x.rank, epoch);
+}
+
+// Whole CTA, at a feature this rank owns: every other rank's built-child bins of split j added to this rank's own
+// (`built`, shared); false when a rank did not answer (error recorded).
+__device__ __forceinline__ bool gather_bins(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch,
+                                            uint32_t j, uint32_t f, uint32_t nb, int2* built, int* error) {
     __shared__ int s_ok;
-    const size_t base = exchange_bins_offset(F);
-    const size_t per_src = static_cast<size_t>(kSplits) * F * kMaxBins;
-    const size_t parity = static_cast<size_t>(epoch & 1) * x.world * per_src;
-    const size_t item = static_cast<size_t>(j) * F + f;
-    // slot of source rank s: base + (parity + s * per_src + item * kMaxBins) int2
-    if (threadIdx.x < nb) {
-        const int2 v = built[threadIdx.x];
-        const size_t at = parity + static_cast<size_t>(x.rank) * per_src + item * kMaxBins + threadIdx.x;
-        for (int q = 0; q < x.world; ++q) reinterpret_cast<int2*>(x.peers[q] + base)[at] = v;
-    }
-    __syncthreads();  // the CTA's stores are issued: each release below orders them before its flag
-    const size_t flags = kXFeatureFlags + 4ull * kMaxRanks * item;  // this item's flags, one per source
     if (threadIdx.x < 32) {
-        const int q = static_cast<int>(threadIdx.x);
-        if (q < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[q] + flags) + x.rank, epoch);
-        const bool ok = wait_ranks(x, flags, epoch, error);
+        const bool ok = wait_ranks(x, item_flags_at(L, x, j, f), epoch, error, x.rank);
         if (threadIdx.x == 0) s_ok = ok;
     }
     __syncthreads();
     const bool ok = s_ok != 0;
-    if (ok && threadIdx.x < nb) {
-        const int2* own = reinterpret_cast<const int2*>(x.peers[x.rank] + base) + parity + item * kMaxBins + threadIdx.x;
-        int2 v[kMaxRanks];
+    if (ok) {
+        for (uint32_t t = threadIdx.x; t < nb; t += blockDim.x) {
+            int2 v[kMaxRanks];
 #pragma unroll
-        for (int s = 0; s < kMaxRanks; ++s) v[s] = s < x.world ? __ldcg(own + s * per_src) : make_int2(0, 0);
-        int2 sum = make_int2(0, 0);
+            for (int q = 0; q < kMaxRanks; ++q)
+                v[q] = q < x.world && q != x.rank
+                           ? __ldcg(reinterpret_cast<const int2*>(x.peers[x.rank] + item_bins_at(L, x, q, j, f)) + t)
+                           : make_int2(0, 0);
+            int2 sum = built[t];
 #pragma unroll
-        for (int s = 0; s < kMaxRanks; ++s) sum = make_int2(sum.x + v[s].x, sum.y + v[s].y);
-        built[threadIdx.x] = sum;
+            for (int q = 0; q < kMaxRanks; ++q) sum = make_int2(sum.x + v[q].x, sum.y + v[q].y);
+            built[t] = sum;
+        }
     }
+    __syncthreads();
+    return ok;
+}
+
+// A search item's two candidates (rows 2 j and 2 j + 1 at feature f), written to every rank's candidate arrays (one
+// rank: the local ones, as `a` holds them).
+struct CandidateSink {
+    FeatureCandidate* cands[kMaxRanks];
+    uint8_t* flags[kMaxRanks];
+    double* gains[kMaxRanks];
+    int ranks;
+};
+
+// With ranks, the step's set (`parity`) of rank q's candidate arrays in its exchange buffer (ExchangeLayout).
+__device__ __forceinline__ size_t candidate_set(const ExchangeLayout& L, uint32_t parity) {
+    return static_cast<size_t>(parity & 1) * 2 * kSplits * L.features;
+}
+
+__device__ __forceinline__ CandidateSink candidate_sink(const TrainArgs& a, const GrowExchange& x,
+                                                        const ExchangeLayout& L, uint32_t parity) {
+    CandidateSink k{};
+    k.ranks = x.world > 1 ? x.world : 1;
+    const size_t set = candidate_set(L, parity);
+    for (int q = 0; q < k.ranks; ++q) {
+        if (x.world > 1) {
+            k.cands[q] = reinterpret_cast<FeatureCandidate*>(x.peers[q] + L.candidates) + set;
+            k.flags[q] = x.peers[q] + L.cand_flags + set;
+            k.gains[q] = reinterpret_cast<double*>(x.peers[q] + L.cand_gain) + set;
+        } else {
+            k.cands[q] = static_cast<FeatureCandidate*>(a.candidates);
+            k.flags[q] = a.cand_flags;
+            k.gains[q] = a.cand_gain;
+        }
+    }
+    return k;
+}
+
+__device__ __forceinline__ void sink_candidate(const CandidateSink& k, size_t at, const FeatureCandidate& c) {
+    const uint8_t flags = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
+    for (int q = 0; q < k.ranks; ++q) {
+        k.cands[q][at] = c;
+        k.flags[q][at] = flags;
+        k.gains[q][at] = c.gain;
+    }
+}
+
+// CTA 0, warp 0, after the grid barrier that follows the search: this rank's step flag in every rank's buffer (every
+// candidate this rank owns is written). Every CTA then waits for every rank's (wait_steps).
+__device__ __forceinline__ void publish_step(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch) {
+    const int q = static_cast<int>(threadIdx.x & 31);
+    if (q < x.world) st_release_sys(reinterpret_cast<uint32_t*>(x.peers[q] + L.step_flags) + x.rank, epoch);
+}
+
+__device__ __forceinline__ bool wait_steps(const GrowExchange& x, const ExchangeLayout& L, uint32_t epoch, int* error) {
+    __shared__ int s_ok;
+    if (threadIdx.x < 32) {
+        const bool ok = wait_ranks(x, L.step_flags, epoch, error);
+        if (threadIdx.x == 0) s_ok = ok;
+    }
+    __syncthreads();
+    const bool ok = s_ok != 0;
     __syncthreads();
     return ok;
 }
@@ -866,23 +943,27 @@ __device__ __forceinline__ void reduce_feature_bins_staged(const DevFeature& fea
     __syncthreads();
 }
 
+// What a rank does with an item's built-child bins: searches them alone (one rank), pushes them to the feature's
+// owner (another rank owns it), or adds every other rank's to them (it owns the feature).
+enum class BinsMode { kLocal, kPush, kGather };
+
 // The search of split j of a step for feature `f` in one CTA, both children at once, in two parts.
 // feature_bins_cta: the built child's bins reduced from the split's slabs (`chunks` of them from slab `first`,
-// packed or not) and, with ranks, summed over every rank's (exchange_bins), into `bufs` (2 kMaxBins int2 of shared
-// memory; `scratch`, 16 KB of shared memory or null, serves the 16-byte reduction); *evaluated says whether the
-// feature is searched at all (`evaluate`: the split's features). For a split (not the root), the threads of the
-// sibling's scan group (feature_scan_cta) also load their bin of the parent's histogram into `parent`, so that the
-// load overlaps the reduction. With `pbuf` (not 0) the slab bins were prefetched there (prefetch_feature_bins):
-// the reduction waits for the copies and reads them from shared memory. False when a rank did not answer (error
-// recorded).
+// packed or not) into `bufs` (2 kMaxBins int2 of shared memory; `scratch`, 16 KB of shared memory or null, serves
+// the 16-byte reduction), then, with ranks, pushed to the feature's owner or summed with every rank's (`mode`);
+// *evaluated says whether the feature is searched at all (`evaluate`: the split's features). For a split (not the
+// root) searched here, the threads of the sibling's scan group (feature_scan_cta) also load their bin of the
+// parent's histogram into `parent`, so that the load overlaps the reduction. With `pbuf` (not 0) the slab bins were
+// prefetched there (prefetch_feature_bins): the reduction waits for the copies and reads them from shared memory.
+// False when a rank did not answer (error recorded).
 __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const Step& st, uint32_t j, uint32_t f,
                                  uint32_t first, uint32_t chunks, bool packed, const uint8_t* evaluate, int2* bufs,
-                                 int4* scratch, const GrowExchange& x, uint32_t epoch, bool* evaluated, int2& parent,
-                                 uint32_t pbuf = 0) {
+                                 int4* scratch, BinsMode mode, const GrowExchange& x, const ExchangeLayout& L,
+                                 uint32_t epoch, bool* evaluated, int2& parent, uint32_t pbuf = 0) {
     const DevFeature feat = a.d.features[f];
     *evaluated = load_flag(evaluate + f) && feat.tile >= 0 && feat.num_bins != 0;
     if (!*evaluated) return true;
-    {
+    if (mode != BinsMode::kPush) {
         const uint32_t t = threadIdx.x % kScanThreads;
         if (!st.root && threadIdx.x / kScanThreads == 1 && t < feat.num_bins)
             parent = __ldcg(reinterpret_cast<const int2*>(a.slots) +
@@ -905,7 +986,12 @@ __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const St
     } else {
         reduce_feature_bins_halves<false>(h, feat, first, chunks, bufs + kMaxBins, bufs);
     }
-    return x.world == 1 || exchange_bins(x, epoch, a.num_features, j, f, feat.num_bins, bufs, &a.iter->error);
+    if (mode == BinsMode::kPush) {
+        push_bins(x, L, epoch, j, f, feat.num_bins, bufs);
+        return true;
+    }
+    if (mode == BinsMode::kGather) return gather_bins(x, L, epoch, j, f, feat.num_bins, bufs, &a.iter->error);
+    return true;
 }
 
 // The histogram slot split j of a step writes child `c`'s bins to: the child's own (learner.rs:365-367), except
@@ -920,20 +1006,17 @@ __device__ __forceinline__ size_t child_slot(const TrainArgs& a, const Step& st,
 // and writes both children's), each with scan_feature_group, as search_item_group does for one item. The
 // candidates go to rows 2 j (built) and 2 j + 1 (sibling) of F.
 __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t j, uint32_t f,
-                                 bool evaluated, const int2& parent, int2* bufs, ScanShared* scan_sh) {
+                                 bool evaluated, const int2& parent, int2* bufs, ScanShared* scan_sh,
+                                 const CandidateSink& sink) {
     const uint32_t F = a.num_features;
     const uint32_t group = threadIdx.x / kScanThreads, t = threadIdx.x % kScanThreads;
-    FeatureCandidate* cands = static_cast<FeatureCandidate*>(a.candidates) + static_cast<size_t>(2 * j) * F;
-    uint8_t* cand_flags = a.cand_flags + static_cast<size_t>(2 * j) * F;
-    double* cand_gain = a.cand_gain + static_cast<size_t>(2 * j) * F;
+    const size_t row = static_cast<size_t>(2 * j) * F;  // candidate rows 2 j and 2 j + 1
     if (!evaluated) {
         if (threadIdx.x == 0) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
-            cands[f] = none;
-            cands[F + f] = none;
-            cand_flags[f] = 0;
-            cand_flags[F + f] = 0;
+            sink_candidate(sink, row + f, none);
+            sink_candidate(sink, row + F + f, none);
         }
         return;
     }
@@ -958,18 +1041,13 @@ __device__ void feature_scan_cta(const TrainArgs& a, const Step& st, const Searc
         if (t == 0) {
             FeatureCandidate none{};
             none.feature = static_cast<int32_t>(f);
-            cands[F + f] = none;
-            cand_flags[F + f] = 0;
+            sink_candidate(sink, row + F + f, none);
         }
     } else {
         group_sync(bar);  // the group's bins are in place
         const FeatureCandidate c = scan_feature_group(ch == 0 ? built : other, feat, static_cast<int>(f), s.ctx[ch],
                                                       a.cfg, scan_sh[group], bar);
-        if (t == 0) {
-            cands[static_cast<size_t>(ch) * F + f] = c;
-            cand_flags[static_cast<size_t>(ch) * F + f] = static_cast<uint8_t>((c.found ? 1 : 0) | (c.splittable ? 2 : 0));
-            cand_gain[static_cast<size_t>(ch) * F + f] = c.gain;
-        }
+        if (t == 0) sink_candidate(sink, row + static_cast<size_t>(ch) * F + f, c);
     }
     __syncthreads();  // the buffers and the scratch are free for the CTA's next feature
 }

@@ -101,12 +101,16 @@ __device__ __forceinline__ void broadcast_cg(const T* p, T* shared_copy) {
 // The error word is polled alongside. Returns false once any CTA has recorded an error (or this one gave up).
 // A barrier can be split: barrier_arrive, then CTA-local work that needs no other CTA's results (it overlaps the
 // wait), then barrier_wait.
-__device__ __forceinline__ void barrier_arrive(const GrowArgs& g, unsigned int& target) {
+__device__ __forceinline__ void barrier_arrive(const GrowArgs& g, unsigned int& target, bool system = false) {
     target += gridDim.x;
     __syncthreads();  // the CTA's work (and its writes) are done
     // A release reduction: the CTA's writes are visible GPU-wide before its arrival is, and nothing waits for a
-    // return value.
-    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(g.barrier) : "memory");
+    // return value. `system`: the CTA also wrote other ranks' memory, which a system-scope fence orders first (the
+    // rank's step flag, raised after the barrier, then covers those writes too).
+    if (threadIdx.x == 0) {
+        if (system) __threadfence_system();
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(g.barrier) : "memory");
+    }
 }
 
 __device__ bool barrier_wait(const GrowArgs& g, unsigned int target) {
@@ -279,29 +283,60 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         __syncthreads();
         const uint32_t epoch = g.x.epoch0 + static_cast<uint32_t>(gs + 2);  // this grid step's, on every rank
         const bool ranks = g.x.world > 1;
+        const ExchangeLayout L = exchange_layout(F, ranks ? static_cast<uint32_t>(g.x.world) : 1u);
+        const CandidateSink sink = candidate_sink(a, g.x, L, epoch);
         int2* bufs = reinterpret_cast<int2*>(scan);
         // the reduction's scratch: the histogram's staging slots, free in this phase
         int4* scratch = g.stage_depth * (kGrowThreads / 32) * g.slot_bytes >= 16384
                             ? reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(smem) + g.stage_offset)
                             : nullptr;
-        if (ranks && !st[0].root && cta == 0 && threadIdx.x < 32) publish_left(g.x, epoch, s_left, n);
+        // While a CTA scans an item, the slab bins of its next item are copied into the staging slots past the
+        // reduction's scratch (when they fit).
+        const uint32_t pbuf = scratch != nullptr ? static_cast<uint32_t>(__cvta_generic_to_shared(scratch)) + 16384u : 0u;
+        const uint32_t pcap = scratch != nullptr ? g.stage_depth * (kGrowThreads / 32) * g.slot_bytes - 16384u : 0u;
+        if (ranks && !st[0].root && cta == 0 && threadIdx.x < 32) publish_left(g.x, L, epoch, s_left, n);
         const uint32_t items = static_cast<uint32_t>(n) * F;
-        // The CTA's first item's bins (and their exchange) come before the contexts, so that the left counts'
-        // exchange has arrived by the time the contexts need it.
+        // Split j's built-child histogram was made in phase A (else there is nothing to reduce or exchange).
+        auto built = [&](uint32_t j) { return st[j].root ? root_job.active != 0 : st[j].may_search != 0; };
+        auto features_of = [&](uint32_t j) -> const uint8_t* { return st[j].root ? mask : eval + static_cast<size_t>(j) * F; };
+        // Copies item i's slab bins ahead into pbuf (when they fit); true when it did.
+        auto prefetch = [&](uint32_t i) {
+            const uint32_t jn = i / F, fn = i % F;
+            const DevFeature feat = a.d.features[fn];
+            return pbuf != 0 && features_of(jn)[fn] && feat.tile >= 0 && feat.num_bins != 0 &&
+                   prefetch_feature_bins(g.h, feat, plan[jn].base, plan[jn].chunks, plan[jn].packed != 0, pbuf, pcap);
+        };
         bool have = false, evaluated = false;
         int2 parent = make_int2(0, 0);  // this thread's bin of the split's parent histogram (feature_bins_cta)
-        if (cta < items) {
+        if (ranks) {
+            // Items of features another rank owns: this rank's built-child bins, reduced from its slabs, pushed to
+            // the owner (they need no search context, so they run before the left counts are gathered).
+            auto pushed = [&](uint32_t i) { return built(i / F) && owner_of(g.x, i % F) != g.x.rank; };
+            uint32_t prefetched = 0xFFFFFFFFu;
+            for (uint32_t i = cta; i < items; i += ctas) {
+                if (!pushed(i)) continue;
+                const uint32_t j = i / F, f = i % F;
+                feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, features_of(j),
+                                 bufs, scratch, BinsMode::kPush, g.x, L, epoch, &evaluated, parent,
+                                 prefetched == i ? pbuf : 0u);
+                prefetched = 0xFFFFFFFFu;
+                uint32_t next = i + ctas;
+                while (next < items && !pushed(next)) next += ctas;
+                if (next < items && prefetch(next)) prefetched = next;
+            }
+            if (prefetched != 0xFFFFFFFFu) cp_async_wait(0);  // nothing is left in flight
+        } else if (cta < items) {
+            // One rank: the CTA's first item's bins come before the contexts.
             const uint32_t j = cta / F, f = cta % F;
-            if (st[j].root ? root_job.active != 0 : st[j].may_search != 0) {
-                const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
-                if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate,
-                                      bufs, scratch, g.x, epoch, &evaluated, parent))
-                    return;
+            if (built(j)) {
+                feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, features_of(j),
+                                 bufs, scratch, BinsMode::kLocal, g.x, L, epoch, &evaluated, parent);
                 have = true;
             }
         }
+        // The left counts and the splits' search contexts (every CTA: the finish is replicated).
         if (ranks && !st[0].root) {
-            if (!gather_left(g.x, epoch, n, &a.iter->error, s_left_global)) return;
+            if (!gather_left(g.x, L, epoch, n, &a.iter->error, s_left_global)) return;
         } else if (threadIdx.x < static_cast<uint32_t>(n)) {
             s_left_global[threadIdx.x] = s_left[threadIdx.x];
         }
@@ -313,40 +348,46 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         }
         __syncthreads();
         clock_mark(g, clock, 1);
-        // While a CTA scans an item, the slab bins of its next searched item are copied into the staging slots past
-        // the reduction's scratch (when they fit).
-        const uint32_t pbuf = scratch != nullptr ? static_cast<uint32_t>(__cvta_generic_to_shared(scratch)) + 16384u : 0u;
-        const uint32_t pcap = scratch != nullptr ? g.stage_depth * (kGrowThreads / 32) * g.slot_bytes - 16384u : 0u;
+        // The searches: every item (one rank) or the items of the features this rank owns, each with every rank's
+        // bins added; items (split j, feature f) = j F + f, CTA c taking items c, c + ctas, ...
+        auto searched = [&](uint32_t i) { return sc[i / F].searched && (!ranks || owner_of(g.x, i % F) == g.x.rank); };
+        const BinsMode mode = ranks ? BinsMode::kGather : BinsMode::kLocal;
         uint32_t prefetched = 0xFFFFFFFFu;  // the item whose bins are in pbuf
         for (uint32_t i = cta; i < items; i += ctas) {
+            if (!searched(i)) continue;
             const uint32_t j = i / F, f = i % F;
-            if (!sc[j].searched) continue;
             if (i != cta || !have) {
-                const uint8_t* evaluate = st[j].root ? mask : eval + static_cast<size_t>(j) * F;
-                if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0, evaluate,
-                                      bufs, scratch, g.x, epoch, &evaluated, parent, prefetched == i ? pbuf : 0u))
+                if (!feature_bins_cta(a, g.h, st[j], j, f, plan[j].base, plan[j].chunks, plan[j].packed != 0,
+                                      features_of(j), bufs, scratch, mode, g.x, L, epoch, &evaluated, parent,
+                                      prefetched == i ? pbuf : 0u))
                     return;
             }
             prefetched = 0xFFFFFFFFu;
             uint32_t next = i + ctas;
-            while (next < items && !sc[next / F].searched) next += ctas;
-            if (pbuf != 0 && next < items) {
-                const uint32_t jn = next / F, fn = next % F;
-                const DevFeature feat = a.d.features[fn];
-                const uint8_t* ev = st[jn].root ? mask : eval + static_cast<size_t>(jn) * F;
-                if (ev[fn] && feat.tile >= 0 && feat.num_bins != 0 &&
-                    prefetch_feature_bins(g.h, feat, plan[jn].base, plan[jn].chunks, plan[jn].packed != 0, pbuf, pcap))
-                    prefetched = next;
-            }
-            feature_scan_cta(a, st[j], sc[j], j, f, evaluated, parent, bufs, scan_shared);
+            while (next < items && !searched(next)) next += ctas;
+            if (next < items && prefetch(next)) prefetched = next;
+            feature_scan_cta(a, st[j], sc[j], j, f, evaluated, parent, bufs, scan_shared, sink);
         }
         clock_mark(g, clock, 2);
-        barrier_arrive(g, target);
+        barrier_arrive(g, target, ranks);
         // While the other CTAs finish their search: the parts of the finish that need no candidates.
         steps_finish_prepare(a, st, n, sc, s_left, osplit, psplit, fs);
         if (!barrier_wait(g, target)) return;
+        const FeatureCandidate* cands = static_cast<const FeatureCandidate*>(a.candidates);
+        const uint8_t* cand_flags = a.cand_flags;
+        const double* cand_gain = a.cand_gain;
+        if (ranks) {
+            // Every rank's candidates of the step are in this rank's arrays once every rank raised its step flag.
+            if (cta == 0 && threadIdx.x < 32) publish_step(g.x, L, epoch);
+            if (!wait_steps(g.x, L, epoch, &a.iter->error)) return;
+            const uint8_t* own = g.x.peers[g.x.rank];
+            const size_t set = candidate_set(L, epoch);
+            cands = reinterpret_cast<const FeatureCandidate*>(own + L.candidates) + set;
+            cand_flags = own + L.cand_flags + set;
+            cand_gain = reinterpret_cast<const double*>(own + L.cand_gain) + set;
+        }
         clock_mark(g, clock, 4);
-        steps_finish(a, st, s_n, sc, eval, mask, csplit, osplit, psplit, cta, fs);
+        steps_finish(a, st, s_n, sc, eval, mask, csplit, osplit, psplit, cta, fs, cands, cand_flags, cand_gain);
         if (clock_owner(g) && clock.row) clock.row[kGrowPhases + 2] = static_cast<unsigned long long>(fs.committed);
         clock_mark(g, clock, 3);
     }

@@ -202,13 +202,14 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
     __syncthreads();
 }
 
-// The step's finish, in every CTA on the same inputs: each child's best split from the compact candidates (warp
-// 2 j + c for child c of split j), the splits committed, the tree, records and slots of the committed splits (writer CTAs), and the next
+// The step's finish, in every CTA on the same inputs: each child's best split from the compact candidates
+// (`candidates`, `cand_flags`, `cand_gain`: rows 2 j + c of F; warp 2 j + c for child c of split j), the splits committed, the tree, records and slots of the committed splits (writer CTAs), and the next
 // step's splits into `st` (and their features into `eval`, kSplits rows of F). `csplit` holds 2 kSplits rows of F
 // (the children's splittable flags), `mask` the iteration's feature mask.
 __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchCtx* sc, uint8_t* eval,
                              const uint8_t* mask, uint8_t* csplit, const uint8_t* osplit, const uint8_t* psplit,
-                             uint32_t cta, StepsFinish& fs) {
+                             uint32_t cta, StepsFinish& fs, const FeatureCandidate* candidates,
+                             const uint8_t* cand_flags, const double* cand_gain) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t F = a.num_features;
     const IterState& it = *a.iter;
@@ -223,8 +224,8 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
             best.found = 0;
             uint8_t* rowc = csplit + static_cast<size_t>(2 * j + ch) * F;
             if (sc[j].searched) {
-                const uint8_t* flags = a.cand_flags + static_cast<size_t>(2 * j + ch) * F;
-                const double* gains = a.cand_gain + static_cast<size_t>(2 * j + ch) * F;
+                const uint8_t* flags = cand_flags + static_cast<size_t>(2 * j + ch) * F;
+                const double* gains = cand_gain + static_cast<size_t>(2 * j + ch) * F;
                 int found = 0;
                 double bg = -INFINITY;
                 int32_t bf = -1;
@@ -263,8 +264,7 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
                     }
                 }
                 if (found && lane == 0) {
-                    best = load_candidate(static_cast<const FeatureCandidate*>(a.candidates) +
-                                          static_cast<size_t>(2 * j + ch) * F + bf);
+                    best = load_candidate(candidates + static_cast<size_t>(2 * j + ch) * F + bf);
                     fs.child_feat[j][ch] = a.d.features[bf];
                 }
             } else {

@@ -173,11 +173,14 @@ struct GrowSmem {
 // The kernel's static shared memory (bytes; -1 on error): the dynamic part has what is left of the CTA's limit.
 int grow_static_smem();
 
-// Ranks of one training run, one GPU each, every rank running the tree kernel at once: per split step each rank
-// writes its left count and, per searched feature, its built child's bins into every rank's exchange buffer (NVLink
-// stores through CUDA IPC mappings), then raises its flag there with the step's epoch; each rank waits on the flags
-// in its own buffer and sums the copies from its own memory. Every rank then runs the same search and finish on the
-// same sums and grows the same tree.
+// Ranks of one training run, one GPU each, every rank running the tree kernel at once. Feature f belongs to rank
+// f mod world (its owner). Per grid step each rank writes its left counts into every rank's exchange buffer; per
+// searched (split, feature) item every other rank reduces its own slabs of the built child's bins and writes them
+// into the owner's buffer (NVLink stores through CUDA IPC mappings), raising its flag there with the step's epoch;
+// the owner waits on those flags in its own memory, sums the copies with its own, searches both children and writes
+// the two candidates into every rank's candidate arrays. Once every CTA of a rank has done so, the rank raises its
+// step flag in every buffer; each rank's finish waits for all of them and runs on the same candidates, so every
+// rank grows the same tree (split.rs:866-873 `better` is a total order: the choice does not depend on who searched).
 constexpr int kMaxRanks = 8;
 struct GrowExchange {
     uint8_t* peers[kMaxRanks];  // every rank's exchange buffer (this rank's own at [rank]); unused with one rank
@@ -188,18 +191,44 @@ struct GrowExchange {
 constexpr uint32_t kPeerSpins = 1u << 22;  // polls of a peer's flag (a few seconds) before error 4, by default
 // Splits a grid step of the tree kernel runs at most (steps.cuh).
 constexpr int kSplits = 8;
-// An exchange buffer (u32 words unless noted), for split j of a step and source rank s: the left counts' flags [s]
-// at byte 0, the left counts [parity][j][s] at byte 128, the bins' flags [j][F][s] after them (128-byte aligned);
-// then the built child's bins, int2 [parity][s][j][F][kMaxBins].
-constexpr size_t kXLeftFlags = 0, kXLeftValues = 128;
-constexpr size_t kXFeatureFlags = (kXLeftValues + 4 * 2 * kSplits * kMaxRanks + 127) / 128 * 128;
-static_assert(kXLeftFlags + 4 * kMaxRanks <= kXLeftValues, "the left counts' flags fit before the counts");
-__host__ __device__ inline size_t exchange_bins_offset(uint32_t F) {
-    return kXFeatureFlags + (4ull * kSplits * kMaxRanks * F + 127) / 128 * 128;
+
+// An exchange buffer, for split j of a step, source rank s and owned feature slot o = f / world (the owner's o-th
+// feature): u32 flags and counts, then the arrays, each 128-byte aligned.
+struct ExchangeLayout {
+    size_t left_flags;    // u32 [kMaxRanks]: source s's left counts are in (the step's epoch)
+    size_t left_values;   // u32 [2 parity][kSplits][kMaxRanks]
+    size_t step_flags;    // u32 [kMaxRanks]: source s wrote every candidate of the step it owns
+    size_t item_flags;    // u32 [kSplits][owned][kMaxRanks]: source s's bins of item (j, o) are in
+    size_t bins;          // int2 [kMaxRanks][kSplits][owned][kMaxBins]: source s's built-child bins
+    // The step's candidates, written by their owners, in two sets by the step's parity: an owner may write the next
+    // step's candidates (those it needs no other rank for) while a slower rank still reads this step's.
+    size_t candidates;    // FeatureCandidate [2 parity][2 kSplits][F]
+    size_t cand_flags;    // u8 [2 parity][2 kSplits][F]
+    size_t cand_gain;     // f64 [2 parity][2 kSplits][F]
+    size_t bytes;
+    uint32_t owned;       // feature slots a rank owns at most: ceil(F / world)
+    uint32_t features;
+};
+
+__host__ __device__ inline size_t align128(size_t v) { return (v + 127) / 128 * 128; }
+
+__host__ __device__ inline ExchangeLayout exchange_layout(uint32_t F, uint32_t world) {
+    ExchangeLayout x{};
+    const uint32_t w = world < 1 ? 1u : world;
+    x.owned = (F + w - 1) / w;
+    x.left_flags = 0;
+    x.left_values = 128;
+    x.step_flags = align128(x.left_values + 4ull * 2 * kSplits * kMaxRanks);
+    x.item_flags = x.step_flags + 128;
+    x.bins = align128(x.item_flags + 4ull * kSplits * x.owned * kMaxRanks);
+    x.features = F;
+    x.candidates = align128(x.bins + 8ull * kMaxRanks * kSplits * x.owned * kMaxBins);
+    x.cand_flags = align128(x.candidates + sizeof(FeatureCandidate) * 2ull * 2 * kSplits * F);
+    x.cand_gain = align128(x.cand_flags + 2ull * 2 * kSplits * F);
+    x.bytes = align128(x.cand_gain + 8ull * 2 * 2 * kSplits * F);
+    return x;
 }
-__host__ __device__ inline size_t exchange_bytes(uint32_t F, uint32_t world) {
-    return exchange_bins_offset(F) + 2ull * world * kSplits * F * kMaxBins * 8;
-}
+__host__ __device__ inline size_t exchange_bytes(uint32_t F, uint32_t world) { return exchange_layout(F, world).bytes; }
 
 cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int* barrier, int grid,
                              const GrowSmem& smem, const GrowExchange& x, cudaStream_t s,

@@ -521,13 +521,15 @@ def run_reference(args, rank: int, world: int):
     secs = m.iteration_seconds
     rate = len(secs) / sum(secs)
     sample = f"{len(secs)} boosting iterations of the full {ROWS:,} x {CFG.features} set on {cores} threads"
+    by_op = {k_: v / len(secs) for k_, v in m.op_seconds.items()}
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "iters/s", "n_gpus": world,
             "steps": args.steps, "timed_steps": len(secs), "warmup": args.warmup,
             "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int32 histograms / f64 split search", "data": "synthetic",
             "config": {"workload": CFG.describe(ROWS), "rows": ROWS, "features": CFG.features,
                        "num_leaves": CFG.num_leaves},
-            "cpu_baseline": {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": rate, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample,
+                             "seconds_by_op": by_op},
             "e2e": {"value": rate, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -678,7 +680,9 @@ def run_b200(args, rank: int, world: int):
             line["cpu_baseline"] = {"value": len(secs_ref) / sum(secs_ref), "unit": "iters/s", "cores": cores,
                                     "kind": "port",
                                     "sample": f"{len(secs_ref)} boosting iterations of the same {ROWS:,} x "
-                                              f"{CFG.features} dataset, {sum(secs_ref):.1f} s on {cores} threads"}
+                                              f"{CFG.features} dataset, {sum(secs_ref):.1f} s on {cores} threads",
+                                    # the reference's `Timed` split (tests/train_cpu.rs:434-484), seconds per iteration
+                                    "seconds_by_op": {k: v / len(secs_ref) for k, v in ref.op_seconds.items()}}
     print(json.dumps(line), flush=True)
 
 

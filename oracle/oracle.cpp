@@ -1172,6 +1172,21 @@ struct ModelOut {
     std::vector<Tree> trees;
     double init_score = 0.0;
     std::vector<double> seconds;
+    std::vector<double> op_seconds;  // per operation (OpTimer's order), summed over the run
+};
+
+// The per-operation split of the reference's `Timed` test backend (tests/train_cpu.rs:434-484): wall seconds spent in
+// gradients, quantize, histogram, split search, partition, leaf sums and add_tree, summed over a training run.
+enum { kOpGradients, kOpQuantize, kOpHistogram, kOpSearch, kOpPartition, kOpLeafSums, kOpAddTree, kOps };
+double g_op_seconds[kOps];
+
+struct OpTimer {
+    int op;
+    std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+    explicit OpTimer(int o) : op(o) {}
+    ~OpTimer() {
+        g_op_seconds[op] += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    }
 };
 
 struct Learner {
@@ -1210,6 +1225,7 @@ struct Learner {
         std::vector<double> total(2 * w.total_bins, 0.0), part(2 * w.total_bins);
         for (size_t r = 0; r < w.ranks.size(); ++r) {
             Rank& rk = w.ranks[r];
+            OpTimer timer(kOpHistogram);
             histogram_quantized(*rk.data, rk.layout, rk.packed.data(), rk.max_quant,
                                 rk.partition.data() + ranges[r].begin, ranges[r].count, part.data());
             for (size_t i = 0; i < total.size(); ++i) total[i] += part[i];
@@ -1220,6 +1236,7 @@ struct Learner {
     void find_split(Leaf& leaf, std::vector<double> hist, const std::vector<uint8_t>& evaluate, HistScale scale) {
         leaf.splittable.assign(d0.num_features, 0);
         sb2_split_info info;
+        OpTimer timer(kOpSearch);
         if (!find_best_split(d0, hist.data(), evaluate.data(), leaf.sums, scale, &cfg, info, leaf.splittable.data()))
             throw std::runtime_error(g_error);
         leaf.has_best = info.found != 0;
@@ -1300,6 +1317,7 @@ struct Learner {
         int64_t left_count = 0;
         for (size_t r = 0; r < w.ranks.size(); ++r) {
             Rank& rk = w.ranks[r];
+            OpTimer timer(kOpPartition);
             left_local[r] = stable_partition(*rk.data, split, rk.partition.data() + parent_range[r].begin,
                                              parent_range[r].count);
             left_count += left_local[r];
@@ -1364,6 +1382,7 @@ struct Learner {
             std::vector<sb2_leaf_range> lr(leaves.size());
             for (size_t i = 0; i < leaves.size(); ++i) lr[i] = {leaves[i][r].begin, leaves[i][r].count};
             std::vector<int64_t> part(2 * leaves.size());
+            OpTimer timer(kOpLeafSums);
             orc_leaf_sums(rk.grad.data(), rk.hess.data(), rk.partition.data(), lr.data(), lr.size(), gs, hs,
                           part.data());
             for (size_t i = 0; i < flat.size(); ++i) flat[i] += part[i];
@@ -1422,12 +1441,14 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
     Learner learner(p, w);
     ModelOut out;
     out.init_score = init_score;
+    std::fill(g_op_seconds, g_op_seconds + kOps, 0.0);
     const sb2_dataset& d0 = shards[0];
     for (int iteration = 0; iteration < p.num_iterations; ++iteration) {
         auto t0 = std::chrono::steady_clock::now();
         double maxima[2] = {0.0, 0.0};
         for (Rank& rk : w.ranks) {
             size_t n = rk.data->num_rows;
+            OpTimer timer(kOpGradients);
             if (p.objective == SB2_LAMBDARANK)
                 lambdarank_gradients(ranking[&rk - w.ranks.data()], *rk.data, rk.scores.data(), rk.grad.data(),
                                      rk.hess.data());
@@ -1452,6 +1473,7 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
         for (Rank& rk : w.ranks) {
             size_t n = rk.data->num_rows;
             uint64_t off = rk.data->row_offset;
+            OpTimer timer(kOpQuantize);
             parallel_for(n, [&](size_t i) { rk.packed[i] = quantize_row(spec, rk.grad[i], rk.hess[i], off + i); });
             rk.max_quant = std::max(spec.grad_max_q, spec.hess_max_q);
         }
@@ -1502,13 +1524,16 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
         }
         std::vector<sb2_device_node> nodes;
         device_nodes(tree, splits, nodes);
-        for (Rank& rk : w.ranks)
+        for (Rank& rk : w.ranks) {
+            OpTimer timer(kOpAddTree);
             if (!add_tree(*rk.data, nodes.data(), nodes.size(), leaf_values.data(), leaf_values.size(),
                           rk.scores.data()))
                 throw std::runtime_error(g_error);
+        }
         out.trees.push_back(std::move(tree));
         out.seconds.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
     }
+    out.op_seconds.assign(g_op_seconds, g_op_seconds + kOps);
     return out;
 }
 
@@ -1723,6 +1748,12 @@ double orc_lambdarank_sigmoid(double sigmoid, double delta) {
     LambdaRank lr;
     if (!lambdarank_setup(p, d, lr)) return std::numeric_limits<double>::quiet_NaN();
     return sigmoid_at(lr, delta);
+}
+
+int orc_model_op_seconds(const orc_model* m, double* out, size_t len) {
+    const size_t k = std::min(len, m->m.op_seconds.size());
+    std::copy(m->m.op_seconds.begin(), m->m.op_seconds.begin() + k, out);
+    return static_cast<int>(m->m.op_seconds.size());
 }
 
 // Model::predict_raw_row (model/predict.rs:19-23) with numerical_decision (:118-141).

@@ -78,6 +78,10 @@ int orc_model_tree(const orc_model* m, int index, sb2_tree_view* out);
 double orc_model_init_score(const orc_model* m);
 /* Wall seconds of each iteration of the last orc_train. */
 int orc_model_iteration_seconds(const orc_model* m, double* out, size_t len);
+/* Wall seconds per operation over the run, as the reference's `Timed` backend splits them
+ * (crates/silvic-core/tests/train_cpu.rs:434-484): gradients, quantize, histogram, split search, partition, leaf
+ * sums, add_tree. Returns how many there are (7). */
+int orc_model_op_seconds(const orc_model* m, double* out, size_t len);
 /* f64 prediction of one raw row (crates/silvic-core/src/model/predict.rs numerical decisions): sum of trees. */
 double orc_model_predict_raw(const orc_model* m, const sb2_dataset* data, const double* row);
 const char* orc_last_error(void);

@@ -59,6 +59,7 @@ _SIGS = {
     "orc_model_tree": (C.c_int, [VP, C.c_int, P(_abi.TreeView)]),
     "orc_model_init_score": (C.c_double, [VP]),
     "orc_model_iteration_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
+    "orc_model_op_seconds": (C.c_int, [VP, P(C.c_double), C.c_size_t]),
     "orc_model_predict_raw": (C.c_double, [VP, P(_abi.Dataset), P(C.c_double)]),
     "orc_last_error": (C.c_char_p, []),
 }
@@ -245,9 +246,13 @@ def feature_mask(data, fraction, seed, iteration) -> np.ndarray:
     return out
 
 
+OP_NAMES = ("gradients", "quantize", "histogram", "split_search", "partition", "leaf_sums", "add_tree")
+
+
 class OracleModel:
-    def __init__(self, trees, init_score, seconds, handle_predict=None):
+    def __init__(self, trees, init_score, seconds, op_seconds=None):
         self.trees, self.init_score, self.iteration_seconds = trees, init_score, seconds
+        self.op_seconds = dict(zip(OP_NAMES, op_seconds or []))
 
 
 def train(shards, params: _abi.Params) -> OracleModel:
@@ -265,7 +270,9 @@ def train(shards, params: _abi.Params) -> OracleModel:
             trees.append(Tree.from_view(v))
         secs = (C.c_double * 100000)()
         k = lib().orc_model_iteration_seconds(m, secs, 100000)
-        return OracleModel(trees, lib().orc_model_init_score(m), list(secs[:k]))
+        ops = (C.c_double * 16)()
+        kops = lib().orc_model_op_seconds(m, ops, 16)
+        return OracleModel(trees, lib().orc_model_init_score(m), list(secs[:k]), list(ops[:kops]))
     finally:
         lib().orc_model_free(m)
 

@@ -759,6 +759,11 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         static_assert((2 * 512 + 64) * 4 >= 2 * kMaxBins * 8, "the search's bins fit the scan words");
         m.flags_offset = static_cast<uint32_t>((m.stage_offset + m.stage_depth * per_depth + 15) / 16 * 16);
         m.bytes = static_cast<int>(m.flags_offset + flags);
+        // The histogram's cost per built row against the partition's per parent row: one shared atomic per bin byte
+        // of the row against ~17 bytes moved; 3 at 100 features, 8 at 256, at least 1.
+        uint32_t row_bytes = 0;
+        for (const Tile& t : b->tiles) row_bytes += t.stride;
+        m.hist_weight = std::max(1.0f, static_cast<float>(row_bytes) / 32.0f);
     }
     int grow_per_sm = 0;
     SB2_CUDA(b, grow_configure(b->grow_smem.bytes, &grow_per_sm));

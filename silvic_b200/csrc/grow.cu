@@ -40,7 +40,7 @@ struct GrowArgs {
     uint32_t stage_offset;        // ... of the histogram's staging slots (16 warps x stage_depth x slot_bytes)
     uint32_t slot_bytes;
     uint32_t stage_depth;         // 0: no staging
-    uint32_t pad_;
+    float hist_weight;            // GrowSmem::hist_weight
     GrowExchange x;               // the other ranks (world 1: none)
 };
 
@@ -212,8 +212,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // Phase A: each split's partition and built child's histogram into its slabs (the root: its histogram),
         // every CTA working on one split.
         if (warp == 0) {
-            // Lane j plans split j. Its work: its partition, about one unit per parent row, and its histogram, about
-            // three per built row (the built side's share of the split's rows, as the split's counts estimate it).
+            // Lane j plans split j. Its work: its partition, about one unit per parent row, and its histogram,
+            // `hist_weight` units per built row (the built side's share of the split's rows, as the split's counts
+            // estimate it).
             // In floats, summed in a fixed order: every CTA computes the same shares from the same steps.
             const uint32_t lane = threadIdx.x & 31;
             const bool on = lane < static_cast<uint32_t>(n);
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
                 const float c = static_cast<float>(count);
                 const float l = sj.info.left_count > 0 ? static_cast<float>(sj.info.left_count) : 0.0f;
                 const float r = sj.info.right_count > 0 ? static_cast<float>(sj.info.right_count) : 0.0f;
-                w = !sj.root && sj.may_search && l + r > 0.0f ? c + 3.0f * c * (sj.built_left ? l : r) / (l + r) : c;
+                w = !sj.root && sj.may_search && l + r > 0.0f ? c + g.hist_weight * c * (sj.built_left ? l : r) / (l + r) : c;
             }
             float total = w;
             for (int o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xffffffffu, total, o);
@@ -422,6 +423,7 @@ cudaError_t launch_grow_tree(const TrainArgs& t, const HistArgs& h, unsigned int
     g.slot_bytes = smem.slot_bytes;
     g.stage_depth = smem.stage_depth;
     g.flags_offset = smem.flags_offset;
+    g.hist_weight = smem.hist_weight;
     g.phase_ns = phase_ns;
     g.trace_steps = phase_ns ? trace_steps : 0;
     cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(unsigned int), s);  // nobody has arrived yet

@@ -169,6 +169,9 @@ struct GrowSmem {
     uint32_t slot_bytes;
     uint32_t stage_depth;
     uint32_t flags_offset;
+    // A built child's row costs a grid step's plan this many parent rows of partition: its histogram adds one
+    // shared atomic per bin byte of the row, the partition moves about 17 bytes per row.
+    float hist_weight;
 };
 // The kernel's static shared memory (bytes; -1 on error): the dynamic part has what is left of the CTA's limit.
 int grow_static_smem();

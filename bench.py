@@ -544,6 +544,9 @@ def _max_over_ranks(values: list[float], world: int, dev) -> list[float]:
     return [float(v) for v in t]
 
 
+DOMINANT_SHARE: float | None = None  # --dominant-share: sb2_set_dominant_share before every load (None: default)
+
+
 def _joined_backend(local: int, data, params, rank: int, world: int) -> tuple[object, float, float]:
     """A fresh handle with `data` loaded and, with ranks, joined: (backend, load seconds, join seconds)."""
     import torch.distributed as dist
@@ -552,6 +555,8 @@ def _joined_backend(local: int, data, params, rank: int, world: int) -> tuple[ob
 
     t0 = time.perf_counter()
     b = B200Backend(local)
+    if DOMINANT_SHARE is not None:
+        b.set_dominant_share(DOMINANT_SHARE)
     b.load(data, params.objective, params.sigmoid, params)
     t1 = time.perf_counter()
     if world > 1:
@@ -656,7 +661,8 @@ def run_b200(args, rank: int, world: int):
         "data": "synthetic (counter-hash features; equal-frequency bins of the first 200,000 rows)",
         "config": {"workload": CFG.describe(ROWS), "rows": ROWS, "features": CFG.features,
                    "num_leaves": CFG.num_leaves, "parallelism": f"rows sharded over {world} GPU(s)",
-                   "l2": f"inputs ({n_local * S / 1e9:.1f} GB binned per GPU) larger than L2; no flush"},
+                   "l2": f"inputs ({n_local * S / 1e9:.1f} GB binned per GPU) larger than L2; no flush",
+                   **({"dominant_share": DOMINANT_SHARE} if DOMINANT_SHARE is not None else {})},
         "trees": len(model.trees),
         "hist_rows_feats_per_s": n_local * CFG.features / hist_s * world,
         "roofline": roofline,
@@ -729,8 +735,14 @@ def main():
                     help="trees of the end-to-end job (default: the config's full count)")
     ap.add_argument("--binning", action="store_true",
                     help="time the device binning of the config's raw features instead of training (one GPU)")
+    ap.add_argument("--dominant-share", type=float, default=None,
+                    help="sb2_set_dominant_share before each load: tiles whose features hold this share of the rows "
+                         "in their most frequent bins skip them in the tree kernel's histogram (default: off)")
     args = ap.parse_args()
     set_config(args.config)
+    if args.dominant_share is not None:
+        global DOMINANT_SHARE
+        DOMINANT_SHARE = args.dominant_share
     if args.rows:
         set_rows(args.rows)
     if args.binning:

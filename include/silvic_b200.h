@@ -363,6 +363,15 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
                   const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
                   uint8_t* const* group_data);
 
+/* The most-frequent-bin skip of the tree kernel's histogram (LightGBM's most_freq_bin, which the reference's GPU
+ * backend keeps per column, crates/silvic-gpu/src/backend.rs:336-376 and kernels.kern:439-468): at sb2_load, a tile
+ * of up to 32 features whose features hold, on average, at least `share` of the rows in their most frequent bins
+ * skips those bins' shared-memory adds, and the kernel recovers them from the rows' totals. Results are identical
+ * either way. Off by default (a share above 1): the histogram gives each lane of a warp a different feature, so a
+ * dominant bin causes no bank conflict, and on B200 the per-element test costs more issue slots than the skipped
+ * atomics save. 0: every tile skips. Takes effect at the next sb2_load. */
+int sb2_set_dominant_share(sb2_backend* b, double share);
+
 /* ---- multi-GPU --------------------------------------------------------------------------------------------- */
 
 /* An NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */

@@ -237,6 +237,7 @@ SIGNATURES = {
     "sb2_nccl_unique_id": (C.c_int, [P(C.c_uint8), C.c_size_t]),
     "sb2_join_ranks": (C.c_int, [VP, P(C.c_uint8), C.c_size_t, C.c_int, C.c_int]),
     "sb2_set_rank_exchange": (C.c_int, [VP, C.c_int]),
+    "sb2_set_dominant_share": (C.c_int, [VP, C.c_double]),
     "sb2_test_unanswered_peer": (C.c_int, [VP, C.c_uint32]),
     "sb2_train": (C.c_int, [VP, P(Params), C.c_double, P(VP)]),
     "sb2_boost_from_average": (C.c_int, [P(Params), P(C.c_float), P(C.c_float), C.c_size_t, P(C.c_double)]),

@@ -328,6 +328,12 @@ class B200Backend:
             raise _abi.SilvicError(code, _abi.global_error())
         return bytes(buf)
 
+    def set_dominant_share(self, share: float):
+        """sb2_set_dominant_share: tiles whose features hold at least `share` of the rows in their most frequent bins
+        (on average) skip those bins in the tree kernel's histogram; 0: every tile, above 1 (the default): none.
+        Takes effect at the next load."""
+        self._check(self._lib.sb2_set_dominant_share(self._h, float(share)))
+
     def set_rank_exchange(self, mode: int):
         """sb2_set_rank_exchange: _abi.EXCHANGE_AUTO (NVLink inside the tree kernel) or _abi.EXCHANGE_NCCL."""
         self._check(self._lib.sb2_set_rank_exchange(self._h, mode))

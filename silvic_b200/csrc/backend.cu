@@ -106,6 +106,8 @@ struct sb2_backend {
     const sb2_quant_spec* packed_spec = nullptr;  // the quantization the packed gradients now hold
     DeviceBuffer slabs;        // histogram scratch: one slab per histogram CTA
     uint32_t slab_ints = 0;    // ints per slab
+    uint32_t slab_totals = 0;  // ints before a slab's rows' totals (0: none; no tile skips its dominant bins)
+    double dominant_share = 2.0;  // sb2_set_dominant_share (above 1: no tile skips)
     DeviceBuffer d_quads;      // the slab reduction's QuadMeta table
     uint32_t num_quads = 0;
     uint32_t quad_split = 1;   // threads per quad
@@ -228,6 +230,7 @@ struct sb2_backend {
         h.out = out;
         h.slabs = slabs.as<int>();
         h.slab_ints = slab_ints;
+        h.totals = slab_totals;
         h.num_quads = num_quads;
         h.quads = d_quads.as<QuadMeta>();
         h.quad_split = quad_split;
@@ -627,7 +630,7 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
         d.nan_bin = m.nan_bin;
         d.kind = m.kind;
         d.slab_off = 0;
-        d.pad_ = 0;
+        d.mfb = 0;
         if (m.num_bins > 0 && m.kind != SB2_TRIVIAL) {
             if (m.group >= train->num_groups) return b->fail(SB2_EDATA, "feature in a missing group");
             used.push_back(f);
@@ -839,6 +842,46 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                                  b->columns.as<uint8_t>(), b->column_stride, b->counter.as<unsigned int>(), b->stream);
             SB2_CUDA(b, cudaGetLastError());
         }
+        // Each feature's most frequent bin (LightGBM's most_freq_bin; the reference's GPU backend keeps it per
+        // column, crates/silvic-gpu/src/backend.rs:336-376): a tile whose features hold at least dominant_share of
+        // the rows in theirs, on average, stores each feature's bins 0 and mfb exchanged, and the tree kernel's
+        // histogram skips the stored 0s (recovered from the rows' totals).
+        DeviceBuffer d_used, d_counts;
+        std::vector<int32_t> used_ids(used.begin(), used.end());
+        std::vector<unsigned int> counts;
+        if (n > 0 && !used.empty() && b->dominant_share <= 1.0) {
+            SB2_CUDA(b, d_used.alloc(sizeof(int32_t) * used.size()));
+            SB2_CUDA(b, d_counts.alloc(sizeof(unsigned int) * 256 * used.size()));
+            SB2_CUDA(b, cudaMemcpyAsync(d_used.ptr, used_ids.data(), sizeof(int32_t) * used.size(), cudaMemcpyHostToDevice,
+                                        b->stream));
+            SB2_CUDA(b, cudaMemsetAsync(d_counts.ptr, 0, d_counts.bytes, b->stream));
+            launch_bin_counts(b->columns.as<uint8_t>(), b->column_stride, n, d_used.as<int32_t>(),
+                              static_cast<uint32_t>(used.size()), d_counts.as<unsigned int>(), b->stream);
+            SB2_CUDA(b, cudaGetLastError());
+            counts.resize(256 * used.size());
+            SB2_CUDA(b, cudaMemcpyAsync(counts.data(), d_counts.ptr, sizeof(unsigned int) * counts.size(),
+                                        cudaMemcpyDeviceToHost, b->stream));
+            SB2_TRY(b->sync());
+            for (size_t t = 0; t < b->tiles.size(); ++t) {
+                Tile& tile = b->tiles[t];
+                uint32_t mfb[kTileLanes] = {};
+                double held = 0;
+                for (uint32_t l = 0; l < tile.nfeat; ++l) {
+                    const size_t i = t * kTileLanes + l;  // the tiles hold the used features in order
+                    const unsigned int* c = counts.data() + 256 * i;
+                    for (uint32_t bin = 1; bin < b->dev_features[used[i]].num_bins; ++bin)
+                        if (c[bin] > c[mfb[l]]) mfb[l] = bin;
+                    held += c[mfb[l]];
+                }
+                if (held < b->dominant_share * static_cast<double>(n) * tile.nfeat) continue;
+                tile.skip = 1;
+                for (uint32_t l = 0; l < tile.nfeat; ++l) b->dev_features[used[t * kTileLanes + l]].mfb = mfb[l] | kDominantSkip;
+            }
+            SB2_CUDA(b, cudaMemcpyAsync(b->d_tiles.ptr, b->tiles.data(), sizeof(Tile) * b->tiles.size(),
+                                        cudaMemcpyHostToDevice, b->stream));
+            SB2_CUDA(b, cudaMemcpyAsync(b->d_features.ptr, b->dev_features.data(), sizeof(DevFeature) * F,
+                                        cudaMemcpyHostToDevice, b->stream));
+        }
         launch_tiles(b->dev_data(), b->bins.as<uint8_t>(), b->stream);
         SB2_CUDA(b, cudaGetLastError());
         SB2_TRY(b->sync());  // the staging buffers go out of scope
@@ -861,6 +904,12 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     // tree kernel, where a CTA histograms every unit of its rows).
     b->slab_ints = 0;
     for (const Unit& u : b->units) b->slab_ints += 2 * u.slots;
+    // The tree kernel's slabs end with the rows' totals [g, h] when a tile skips its dominant bins (4 ints: the
+    // slabs stay 16-byte aligned).
+    b->slab_totals = 0;
+    for (const Tile& t : b->tiles)
+        if (t.skip) b->slab_totals = b->slab_ints;
+    if (b->slab_totals != 0) b->slab_ints += 4;
     // The reduction's quads: per unit, per tile, four consecutive slots (one bin, lanes l .. l + 3).
     std::vector<QuadMeta> quads;
     for (uint32_t ui = 0; ui < b->units.size(); ++ui) {
@@ -877,8 +926,10 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
                 const uint32_t bin = s / tile.stride, lane0 = s % tile.stride;
                 for (uint32_t i = 0; i < 4; ++i) {
                     const int32_t f = lane_feature[t * kTileLanes + lane0 + i];
+                    // the tiles store bins 0 and mfb exchanged: slot `bin` holds bin swap_dominant(bin, mfb)
                     m.out[i] = f >= 0 && bin < b->dev_features[f].num_bins
-                                   ? static_cast<int32_t>(b->dev_features[f].hist_offset + bin)
+                                   ? static_cast<int32_t>(b->dev_features[f].hist_offset +
+                                                          swap_dominant(bin, b->dev_features[f].mfb & 0xFFu))
                                    : -1;
                 }
                 quads.push_back(m);
@@ -1069,6 +1120,13 @@ int sb2_add_tree(sb2_backend* b, const sb2_device_node* nodes, size_t num_nodes,
         tn[k].tile = static_cast<uint32_t>(b->dev_features[f].tile);
         tn[k].lane = static_cast<uint32_t>(b->dev_features[f].lane);
         std::memcpy(tn[k].left_bins, nodes[k].split.left_bins, sizeof(tn[k].left_bins));
+        // The tiles store the feature's bins 0 and mfb exchanged: so do the node's bits.
+        const uint32_t mfb = b->dev_features[f].mfb & 0xFFu;
+        if (mfb != 0) {
+            const uint32_t b0 = tn[k].left_bins[0] & 1u, bm = (tn[k].left_bins[mfb >> 5] >> (mfb & 31)) & 1u;
+            tn[k].left_bins[0] = (tn[k].left_bins[0] & ~1u) | bm;
+            tn[k].left_bins[mfb >> 5] = (tn[k].left_bins[mfb >> 5] & ~(1u << (mfb & 31))) | (b0 << (mfb & 31));
+        }
         tn[k].left = nodes[k].left;
         tn[k].right = nodes[k].right;
     }
@@ -1308,6 +1366,13 @@ int sb2_set_rank_exchange(sb2_backend* b, int mode) {
         return b->fail(SB2_ECONFIG, "unknown rank exchange mode " + std::to_string(mode));
     if (b->comm) return b->fail(SB2_ECONFIG, "the rank exchange is chosen before sb2_join_ranks");
     b->exchange_mode = mode;
+    return SB2_OK;
+}
+
+int sb2_set_dominant_share(sb2_backend* b, double share) {
+    if (!b) return SB2_EDEVICE;
+    if (!(share >= 0.0)) return b->fail(SB2_ECONFIG, "the dominant-bin share must be at least 0");
+    b->dominant_share = share;
     return SB2_OK;
 }
 

@@ -3,7 +3,12 @@
 // Device layout of a loaded training set (one GPU's row shard):
 //  - bins: the non-trivial features re-packed into tiles of at most 32 features. Tile t is row-major,
 //    `rows x stride_t` bytes (stride_t = its feature count rounded up to 4), so one row of a full tile is one 32-byte
-//    DRAM sector. Lane j of a warp owns the tile's feature j.
+//    DRAM sector. Lane j of a warp owns the tile's feature j. In a tile whose features are dominated by one bin
+//    each (Tile::skip, when sb2_set_dominant_share asks for it), every feature's bins 0 and mfb (its most frequent
+//    bin) trade places in the tile bytes, so
+//    the tree kernel's histogram skips the dominant bin with one compare against 0 and recovers it by subtraction
+//    from the rows' totals (LightGBM's most_freq_bin, which the reference's hist_quant keeps in a register,
+//    crates/silvic-gpu/kernels/kernels.kern:439-468). Only histograms read tile bytes; the columns stay as loaded.
 //  - columns: every feature's bins again, feature-major (feature f's byte of row r at f * column_stride + r), for
 //    the partition, which reads one feature of a leaf's rows: rows of a leaf sit in runs of increasing row id, so a
 //    warp's 32 rows share a few sectors of a column instead of costing a 32-byte row sector each.
@@ -31,7 +36,18 @@ struct Tile {
     uint32_t nfeat;      // features in the tile
     uint32_t smem_bins;  // bins per lane kept in the histogram's shared slots (max num_bins in the tile)
     uint32_t pitch;      // bytes from one row to the next: the tiles of a histogram unit share their rows
+    uint32_t skip;       // 1: the features' dominant bins are stored as 0 and the tree kernel skips stored 0s
+    uint32_t pad_;
 };
+
+// DevFeature::mfb: the bin stored as 0 in the tiles (bits 0-7) and kDominantSkip when the feature's tile skips.
+constexpr uint32_t kDominantSkip = 1u << 8;
+
+// A tile byte of a feature whose bins 0 and `mfb` trade places, to its bin (and a bin to its tile byte: the
+// exchange is its own inverse).
+__host__ __device__ __forceinline__ uint32_t swap_dominant(uint32_t bin, uint32_t mfb) {
+    return bin == 0 ? mfb : (bin == mfb ? 0u : bin);
+}
 
 // A feature as the kernels see it.
 struct DevFeature {
@@ -42,7 +58,7 @@ struct DevFeature {
     uint32_t nan_bin;
     uint32_t kind;
     uint32_t slab_off;    // the tree kernel's slabs: this feature's packed bins start here ([g, h] pairs at twice it)
-    uint32_t pad_;
+    uint32_t mfb;         // bits 0-7: the bin stored as 0 in the tiles (swap_dominant); kDominantSkip: tile skips
 };
 
 // The loaded training shard, passed to kernels by value.

@@ -71,6 +71,16 @@ __host__ __device__ __forceinline__ bool fused_packed(uint32_t count, uint32_t c
     return (words + chunks - 1) / chunks <= round_rows / 32;
 }
 
+// add_row for one tile of the tree kernel: a Tile::skip tile adds no stored bin 0 (the features' dominant bins,
+// recovered from the rows' totals by recover_dominant_bins).
+template <int W>
+__device__ __forceinline__ void add_row_tile(const LaneTile& l, const uint32_t (&w)[8], uint32_t packed, uint32_t lane) {
+    if (l.skip)
+        add_row<W, true>(l, w, packed, lane);
+    else
+        add_row<W, false>(l, w, packed, lane);
+}
+
 // One 32-row batch of a warp into the unit's packed shared arrays (`lt`: its tiles with the wanted bits): lane k's
 // row adds `packed` (0: nothing) at every tile, each tile's bytes loaded one tile ahead.
 __device__ __forceinline__ void add_batch(const LaneTile* lt, uint32_t num_tiles, uint32_t row, uint32_t packed,
@@ -85,16 +95,16 @@ __device__ __forceinline__ void add_batch(const LaneTile* lt, uint32_t num_tiles
         if (packed != 0 && l.active != 0) {
             switch (l.stride) {
                 case 32:
-                    add_row<8>(l, cur, packed, lane);
+                    add_row_tile<8>(l, cur, packed, lane);
                     break;
                 case 16:
-                    add_row<4>(l, cur, packed, lane);
+                    add_row_tile<4>(l, cur, packed, lane);
                     break;
                 case 8:
-                    add_row<2>(l, cur, packed, lane);
+                    add_row_tile<2>(l, cur, packed, lane);
                     break;
                 default:
-                    add_row<1>(l, cur, packed, lane);
+                    add_row_tile<1>(l, cur, packed, lane);
                     break;
             }
         }
@@ -287,24 +297,24 @@ __device__ __forceinline__ void add_staged(const LaneTile* lt, uint32_t nt, uint
                 const uint32_t sw = stage_swap(lane);
                 const uint4 x = lds128(a + 16 * sw), y = lds128(a + 16 * (sw ^ 1u));
                 w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w, w[4] = y.x, w[5] = y.y, w[6] = y.z, w[7] = y.w;
-                add_row<8>(l, w, packed, lane);
+                add_row_tile<8>(l, w, packed, lane);
                 break;
             }
             case 16: {
                 const uint4 x = lds128(a);
                 w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w;
-                add_row<4>(l, w, packed, lane);
+                add_row_tile<4>(l, w, packed, lane);
                 break;
             }
             case 8: {
                 const uint2 x = lds64(a);
                 w[0] = x.x, w[1] = x.y;
-                add_row<2>(l, w, packed, lane);
+                add_row_tile<2>(l, w, packed, lane);
                 break;
             }
             default:
                 w[0] = lds32(a);
-                add_row<1>(l, w, packed, lane);
+                add_row_tile<1>(l, w, packed, lane);
                 break;
         }
     }
@@ -321,10 +331,11 @@ struct RowSource {
 // Whole CTA: positions [b0, b1) of `src` into the unit's packed shared arrays (`lt`, `nt` tiles). Warp w takes
 // batches w, w + 16, ... of 32 positions; it keeps `depth` of them (<= kMaxStageDepth) in flight in its slots
 // (`stage`: the CTA's staging area, `slot_bytes` per slot) and adds the oldest as it lands. With `depth` 0 (no room
-// for staging) the lanes load their rows' bytes themselves.
+// for staging) the lanes load their rows' bytes themselves. With `count`, each lane also adds its positions'
+// unpacked gradients to (tg, th): the rows' totals, from which recover_dominant_bins restores skipped bins.
 __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, const RowSource& src, uint32_t b0,
                                             uint32_t b1, uint32_t stage, uint32_t slot_bytes, uint32_t depth,
-                                            uint64_t pol) {
+                                            uint64_t pol, bool count, int& tg, int& th) {
     constexpr uint32_t kWarps = kHistThreads / 32;
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t nb = b1 > b0 ? static_cast<uint32_t>(ceil_div(b1 - b0, 32)) : 0u;
@@ -341,6 +352,11 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
             } else {
                 row = __ldcg(src.rows + p);  // written by this step's scatter: not through the read-only path
                 packed = static_cast<uint32_t>(__ldcg(src.gh + p));
+            }
+            if (count) {
+                const int g = static_cast<int16_t>(packed & 0xFFFFu);  // quantize.rs:140-143
+                tg += g;
+                th += static_cast<int>((packed - static_cast<uint32_t>(g)) >> 16);
             }
         }
     };
@@ -560,15 +576,21 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
     // Rows per flush: all of them when the slabs hold packed sums (the range fits a packed round), else rounds of
     // at most round_rows rows.
     const uint32_t round = fs.packed ? 0xFFFFFFFFu : max(1u, fs.round_rows);
+    // With skipping tiles, the first wanted unit's pass also sums the rows' unpacked gradients (every position of
+    // the range once), for the slab's totals.
+    int tg = 0, th = 0;
+    bool counted = h.totals == 0;
     for (uint32_t u = 0; u < h.num_units; ++u) {
         HistCta* c = u < cached ? units + u : spare;
         if (u >= cached) histogram_prepare_unit(h, u, sh, spare);
         const bool want = fused_unit_begin(*c, active, s_lt);
         const uint32_t nt = c->unit.num_tiles;
+        const bool count = want && !counted;
+        counted = counted || want;
         uint32_t r0 = b0;
         while (true) {
             const uint32_t r1 = want ? (b1 - r0 > round ? r0 + round : b1) : b1;
-            if (want) hist_stream(s_lt, nt, src, r0, r1, fs.stage, fs.slot_bytes, fs.depth, pol);
+            if (want) hist_stream(s_lt, nt, src, r0, r1, fs.stage, fs.slot_bytes, fs.depth, pol, count, tg, th);
             const bool last = r1 >= b1;
             // Packed slabs: one flush at the end. Unpacked: a flush per round, stored the first time, added after.
             if (last || !fs.packed)
@@ -578,6 +600,25 @@ inline __device__ void fused_step_cta(const TrainArgs& a, const HistArgs& h, con
             r0 = r1;
         }
         region += 2 * c->unit.slots;
+    }
+    if (h.totals != 0) {
+        // The CTA's totals into the slab (zeros when no unit was wanted: then no bin is recovered from them).
+        tg = __reduce_add_sync(0xffffffffu, tg);
+        th = __reduce_add_sync(0xffffffffu, th);
+        if (lane == 0) {
+            scan[2 * warp] = static_cast<uint32_t>(tg);
+            scan[2 * warp + 1] = static_cast<uint32_t>(th);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t sg = 0, sh_ = 0;
+            for (uint32_t k = 0; k < kWarps; ++k) {
+                sg += scan[2 * k];
+                sh_ += scan[2 * k + 1];
+            }
+            __stcg(reinterpret_cast<int2*>(slab + h.totals), make_int2(static_cast<int>(sg), static_cast<int>(sh_)));
+        }
+        __syncthreads();  // the scan words are free again
     }
 }
 
@@ -943,6 +984,44 @@ __device__ __forceinline__ void reduce_feature_bins_staged(const DevFeature& fea
     __syncthreads();
 }
 
+// A feature of a Tile::skip tile (DevFeature::mfb): its built-child bins `bufs` (shared, [g, h] per stored bin,
+// num_bins of them, as reduced from the slabs) back in bin order. Stored bin 0, its dominant bin mfb, added nothing:
+// since every row adds to exactly one bin of every feature, bin mfb is the rows' totals (kept per slab, from slab
+// `first` on over `chunks`) minus every other stored bin, and stored bin mfb is bin 0. Whole CTA (kHistThreads);
+// bufs[kMaxBins ..] holds the warps' partial sums. Two's-complement sums: exact wherever the bin's own sum fits
+// an int32, as every histogram bin must.
+__device__ __forceinline__ void recover_dominant_bins(const HistArgs& h, const DevFeature& feat, uint32_t first,
+                                                      uint32_t chunks, int2* bufs) {
+    constexpr uint32_t kWarps = kHistThreads / 32;
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    int2* part = bufs + kMaxBins;
+    uint32_t g = 0, hh = 0;
+    for (uint32_t c = t; c < chunks; c += kHistThreads) {
+        const int2 v = __ldcg(reinterpret_cast<const int2*>(h.slabs + static_cast<size_t>(first + c) * h.slab_ints + h.totals));
+        g += static_cast<uint32_t>(v.x);
+        hh += static_cast<uint32_t>(v.y);
+    }
+    if (t >= 1 && t < feat.num_bins) {
+        g -= static_cast<uint32_t>(bufs[t].x);
+        hh -= static_cast<uint32_t>(bufs[t].y);
+    }
+    g = __reduce_add_sync(0xffffffffu, g);
+    hh = __reduce_add_sync(0xffffffffu, hh);
+    if (lane == 0) part[warp] = make_int2(static_cast<int>(g), static_cast<int>(hh));
+    __syncthreads();
+    if (t == 0) {
+        uint32_t sg = 0, sh = 0;
+        for (uint32_t k = 0; k < kWarps; ++k) {
+            sg += static_cast<uint32_t>(part[k].x);
+            sh += static_cast<uint32_t>(part[k].y);
+        }
+        const uint32_t m = feat.mfb & 0xFFu;
+        if (m != 0) bufs[0] = bufs[m];
+        bufs[m] = make_int2(static_cast<int>(sg), static_cast<int>(sh));
+    }
+    __syncthreads();
+}
+
 // What a rank does with an item's built-child bins: searches them alone (one rank), pushes them to the feature's
 // owner (another rank owns it), or adds every other rank's to them (it owns the feature).
 enum class BinsMode { kLocal, kPush, kGather };
@@ -986,6 +1065,8 @@ __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const St
     } else {
         reduce_feature_bins_halves<false>(h, feat, first, chunks, bufs + kMaxBins, bufs);
     }
+    // Each rank restores its own dominant bins (its own totals and most frequent bins) before any exchange.
+    if (feat.mfb & kDominantSkip) recover_dominant_bins(h, feat, first, chunks, bufs);
     if (mode == BinsMode::kPush) {
         push_bins(x, L, epoch, j, f, feat.num_bins, bufs);
         return true;

@@ -69,7 +69,8 @@ struct HistArgs {
     uint32_t num_quads;           // every unit's slots in fours
     const QuadMeta* quads;
     uint32_t quad_split;          // threads per quad in the reduction (a power of two <= 32)
-    uint32_t pad_;
+    uint32_t totals;              // the tree kernel's slabs: ints before a slab's rows' totals [g, h] (0: no
+                                  // tile skips its dominant bins, and no totals are kept)
 };
 
 // The CTAs a unit uses for a job of `count` rows (the histogram and its reduction agree on it).

@@ -30,6 +30,8 @@ struct LaneTile {
     uint32_t active;      // bit f: feature lane f is wanted (0: the tile is skipped)
     uint32_t stage_off;   // where a batch's rows of this tile start in a staging slot (the tree kernel's histogram)
     uint32_t pitch;       // bytes from one row to the next (Tile::pitch)
+    uint32_t skip;        // Tile::skip: the tree kernel adds no stored bin 0 (each feature's dominant bin)
+    uint32_t pad_;
 };
 
 // Rows whose packed gradients one packed histogram can sum exactly: every bin's |sum g| <= 32767 and sum h <=
@@ -84,6 +86,13 @@ __device__ __forceinline__ void shared_add(uint32_t addr, uint32_t v) {
     asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v));
 }
 
+// shared_add where `bin` is not 0, as one predicated instruction (no branch: lanes never diverge).
+__device__ __forceinline__ void shared_add_nonzero(uint32_t addr, uint32_t v, uint32_t bin) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p red.shared.add.u32 [%0], %1;\n\t}" ::"r"(addr), "r"(v),
+        "r"(bin));
+}
+
 // Issues the loads of one row of a tile (stride 4, 8, 16 or 32 bytes) into w[0 .. stride / 4). Streaming loads
 // (evict first): a histogram reads its rows' bins once, and the leaf histograms, partition buffers and metadata the
 // next phases read should stay in L2 instead.
@@ -108,8 +117,9 @@ __device__ __forceinline__ void load_row(const LaneTile& t, uint32_t row, uint32
 // i ^ k for i = 0 .. S-1, k = lane mod S. Slot (bin, f) is word bin * S + f, so the S lanes of every step hit S
 // different features, i.e. S different banks; with the array aligned to 4 S bytes the slot's address is
 // bin * 4S + (base | 4k) ^ 4i, one multiply-add per element. Every feature of the tile is added, wanted or not:
-// only wanted features' bins are ever read back.
-template <int W>
+// only wanted features' bins are ever read back. With kSkip, stored bin 0 (each feature's dominant bin in a
+// Tile::skip tile) adds nothing: the tree kernel recovers it from the rows' totals.
+template <int W, bool kSkip = false>
 __device__ __forceinline__ void add_row(const LaneTile& t, const uint32_t (&wrow)[8], uint32_t packed, uint32_t lane) {
     constexpr uint32_t kStride = 4 * W;
     uint32_t w[W];
@@ -121,7 +131,10 @@ __device__ __forceinline__ void add_row(const LaneTile& t, const uint32_t (&wrow
 #pragma unroll
     for (int i = 0; i < static_cast<int>(kStride); ++i) {
         const uint32_t bin = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-        shared_add(bin * (4 * kStride) + (base ^ (4u * i)), packed);
+        if (kSkip)
+            shared_add_nonzero(bin * (4 * kStride) + (base ^ (4u * i)), packed, bin);
+        else
+            shared_add(bin * (4 * kStride) + (base ^ (4u * i)), packed);
     }
 }
 
@@ -173,6 +186,8 @@ inline __device__ void histogram_prepare_unit(const HistArgs& a, uint32_t u, con
             lt.active = 0;
             lt.stage_off = 0;
             lt.pitch = tile.pitch;
+            lt.skip = tile.skip;
+            lt.pad_ = 0;
             c->tiles[warp] = lt;
         }
     }
@@ -367,11 +382,11 @@ __device__ __forceinline__ void global_add_pair(int* p, int32_t g, int32_t h) {
 }
 
 // One loaded row of a tile of `W` words into the output: step i adds feature i ^ (lane mod S), as in add_row.
-// `off_lane` is the output bin offset of feature lane `lane` (-1: not wanted); rows with `add` false only take part
-// in the shuffles.
+// `off_lane` is the output bin offset of feature lane `lane` (-1: not wanted) and `mfb_lane` its DevFeature::mfb
+// (its tile bytes 0 and mfb trade places); rows with `add` false only take part in the shuffles.
 template <int W>
-__device__ __forceinline__ void direct_row(int* out, const uint32_t (&wrow)[8], int32_t off_lane, int32_t g,
-                                           int32_t h, bool add, uint32_t lane) {
+__device__ __forceinline__ void direct_row(int* out, const uint32_t (&wrow)[8], int32_t off_lane, uint32_t mfb_lane,
+                                           int32_t g, int32_t h, bool add, uint32_t lane) {
     constexpr uint32_t kStride = 4 * W;
     uint32_t w[W];
 #pragma unroll
@@ -381,7 +396,8 @@ __device__ __forceinline__ void direct_row(int* out, const uint32_t (&wrow)[8], 
 #pragma unroll
     for (int i = 0; i < static_cast<int>(kStride); ++i) {
         const int32_t off = __shfl_sync(0xffffffffu, off_lane, static_cast<int>(i ^ k));
-        const uint32_t bin = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        const uint32_t mfb = __shfl_sync(0xffffffffu, mfb_lane, static_cast<int>(i ^ k));
+        const uint32_t bin = swap_dominant((w[i >> 2] >> (8 * (i & 3))) & 0xFFu, mfb);
         if (add && off >= 0) global_add_pair(out + 2 * (static_cast<uint32_t>(off) + bin), g, h);
     }
 }
@@ -413,8 +429,11 @@ inline __device__ void histogram_direct_cta(const HistArgs& a, const HistJob& jo
         }
         const int32_t f = a.d.lane_feature[t * kTileLanes + lane];
         int32_t off = -1;
-        if (f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0))
+        uint32_t mfb = 0;
+        if (f >= 0 && (a.active == nullptr || __ldcg(a.active + f) != 0)) {
             off = static_cast<int32_t>(a.d.features[f].hist_offset);
+            mfb = a.d.features[f].mfb & 0xFFu;
+        }
         if (__ballot_sync(0xffffffffu, off >= 0) == 0) continue;  // no wanted feature in the tile
         const Tile tile = a.d.tiles[t];
         LaneTile lt;
@@ -429,16 +448,16 @@ inline __device__ void histogram_direct_cta(const HistArgs& a, const HistJob& jo
         const bool add = packed != 0;
         switch (tile.stride) {
             case 32:
-                direct_row<8>(a.out, wd, off, g, h, add, lane);
+                direct_row<8>(a.out, wd, off, mfb, g, h, add, lane);
                 break;
             case 16:
-                direct_row<4>(a.out, wd, off, g, h, add, lane);
+                direct_row<4>(a.out, wd, off, mfb, g, h, add, lane);
                 break;
             case 8:
-                direct_row<2>(a.out, wd, off, g, h, add, lane);
+                direct_row<2>(a.out, wd, off, mfb, g, h, add, lane);
                 break;
             default:
-                direct_row<1>(a.out, wd, off, g, h, add, lane);
+                direct_row<1>(a.out, wd, off, mfb, g, h, add, lane);
                 break;
         }
     }

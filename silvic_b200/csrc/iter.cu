@@ -12,6 +12,8 @@
 //                   row in exactly one leaf without bagging), the same f32 add CpuBackend::add_tree makes.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "iter.cuh"
 
 namespace sb2 {
@@ -631,7 +633,14 @@ __global__ void tiles_kernel(DevData d, uint8_t* bins) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     for (uint32_t l = warp; l < tile.stride; l += warps) {
         const int32_t f = l < tile.nfeat ? d.lane_feature[blockIdx.y * kTileLanes + l] : -1;
-        const uint32_t v = f >= 0 ? *reinterpret_cast<const uint32_t*>(d.columns + static_cast<uint64_t>(f) * d.column_stride + r0 + 4 * lane) : 0u;
+        uint32_t v = f >= 0 ? *reinterpret_cast<const uint32_t*>(d.columns + static_cast<uint64_t>(f) * d.column_stride + r0 + 4 * lane) : 0u;
+        const uint32_t mfb = f >= 0 ? d.features[f].mfb : 0u;
+        if (mfb & kDominantSkip) {  // the feature's bins 0 and mfb trade places (swap_dominant)
+            uint32_t x = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) x |= swap_dominant((v >> (8 * q)) & 0xFFu, mfb & 0xFFu) << (8 * q);
+            v = x;
+        }
         *reinterpret_cast<uint32_t*>(sh + l * kPitch + 4 * lane) = v;
     }
     __syncthreads();
@@ -643,6 +652,38 @@ __global__ void tiles_kernel(DevData d, uint8_t* bins) {
         for (int q = 0; q < 4; ++q) v |= static_cast<uint32_t>(sh[(4 * wb + q) * kPitch + row]) << (8 * q);
         *reinterpret_cast<uint32_t*>(bins + tile.base + (r0 + row) * tile.pitch + 4 * wb) = v;
     }
+}
+
+// How many rows of column feats[k] hold each bin, added into counts[k * 256 + bin]: one CTA per kCountRows rows of
+// one column (blockIdx.y + y0), each thread 16 bytes at a time; the equal bins of a warp's step are added once
+// (match.any) into the CTA's shared counts, which go to `counts` at the end. The column's stride (a multiple of
+// 128 bytes) covers the 16 bytes read at any row below `rows`; bytes past `rows` are not counted.
+constexpr uint32_t kCountThreads = 256, kCountLoads = 8;
+constexpr uint64_t kCountRows = 16ull * kCountThreads * kCountLoads;
+__global__ void __launch_bounds__(kCountThreads) bin_counts_kernel(const uint8_t* columns, uint64_t column_stride,
+                                                                   uint64_t rows, const int32_t* feats, uint32_t y0,
+                                                                   unsigned int* counts) {
+    __shared__ unsigned int sh[256];
+    sh[threadIdx.x] = 0;
+    __syncthreads();
+    const uint32_t k = y0 + blockIdx.y, lane = threadIdx.x & 31;
+    const uint8_t* col = columns + static_cast<uint64_t>(feats[k]) * column_stride;
+    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kCountRows;
+    for (uint32_t i = 0; i < kCountLoads; ++i) {
+        const uint64_t r = r0 + 16ull * (i * kCountThreads + threadIdx.x);
+        const bool in = r < rows;
+        const uint4 v = in ? __ldcs(reinterpret_cast<const uint4*>(col + r)) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int b = 0; b < 16; ++b) {
+            const bool valid = in && r + b < rows;
+            const uint32_t bin = valid ? (w[b >> 2] >> (8 * (b & 3))) & 0xFFu : 256u;
+            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+            if (valid && lane == static_cast<uint32_t>(__ffs(peers) - 1)) atomicAdd(&sh[bin], __popc(peers));
+        }
+    }
+    __syncthreads();
+    if (sh[threadIdx.x] != 0) atomicAdd(&counts[static_cast<uint64_t>(k) * 256 + threadIdx.x], sh[threadIdx.x]);
 }
 
 __global__ void fill_kernel(float* out, uint64_t n, float value) {
@@ -739,6 +780,16 @@ void launch_tiles(const DevData& d, uint8_t* bins, cudaStream_t s) {
     if (d.num_tiles == 0 || d.num_rows == 0) return;
     const dim3 grid(static_cast<unsigned>(ceil_div(d.num_rows, 128)), d.num_tiles);
     tiles_kernel<<<grid, 256, 0, s>>>(d, bins);
+}
+
+void launch_bin_counts(const uint8_t* columns, uint64_t column_stride, uint64_t rows, const int32_t* feats,
+                       uint32_t num_feats, unsigned int* counts, cudaStream_t s) {
+    if (rows == 0) return;
+    const unsigned gx = static_cast<unsigned>(ceil_div(rows, kCountRows));
+    for (uint32_t y0 = 0; y0 < num_feats; y0 += 65535) {
+        const dim3 grid(gx, std::min<uint32_t>(num_feats - y0, 65535));
+        bin_counts_kernel<<<grid, kCountThreads, 0, s>>>(columns, column_stride, rows, feats, y0, counts);
+    }
 }
 
 void launch_fill(float* out, uint64_t n, float value, cudaStream_t s) {

@@ -113,6 +113,9 @@ void launch_group_columns(const uint8_t* src, uint64_t rows, uint32_t row_stride
                           const uint32_t* col_bins, uint8_t* columns, uint64_t column_stride, unsigned int* bad,
                           cudaStream_t s);
 void launch_tiles(const DevData& d, uint8_t* bins, cudaStream_t s);
+// Per column feats[k] of the feature-major copy, its rows per bin added into counts[k * 256 + bin] (zeroed first).
+void launch_bin_counts(const uint8_t* columns, uint64_t column_stride, uint64_t rows, const int32_t* feats,
+                       uint32_t num_feats, unsigned int* counts, cudaStream_t s);
 // Counts the operand pairs where the split scan's division (div_rn) differs from CUDA's correctly rounded one.
 void launch_division_check(uint64_t n, uint32_t seed, unsigned long long* mismatches, int grid, cudaStream_t s);
 void launch_api_find_split(const DevData& d, const int* hist, const uint8_t* evaluate, double ug, double uh,

@@ -32,6 +32,9 @@ inline __device__ void partition_flags_cta(const TrainArgs& a, const Step& st, u
     cta_words(st.count, cta, ctas, w_lo, w_hi);
     const Tile tile = a.d.tiles[st.split_tile];
     const uint8_t* column = a.d.bins + tile.base + st.split_lane;
+    // the tile stores the feature's bins 0 and mfb exchanged (swap_dominant)
+    const int32_t split_f = a.d.lane_feature[st.split_tile * kTileLanes + st.split_lane];
+    const uint32_t mfb = split_f >= 0 ? (a.d.features[split_f].mfb & 0xFFu) : 0u;
     const uint32_t* rows = a.rows[st.which & 1] + st.begin;
     uint32_t mine = 0;
     // kBatch words per warp at a time: their row ids, then their bins, are in flight together.
@@ -54,7 +57,8 @@ inline __device__ void partition_flags_cta(const TrainArgs& a, const Step& st, u
                 left[j] = static_cast<double>(uniform01(st.bag_seed, 2u, st.bag_round, st.row_offset + row[j])) <
                           st.bag_fraction;
             else
-                left[j] = bin_goes_left(st.left_bins, __ldg(column + static_cast<uint64_t>(row[j]) * tile.pitch));
+                left[j] = bin_goes_left(st.left_bins,
+                                        swap_dominant(__ldg(column + static_cast<uint64_t>(row[j]) * tile.pitch), mfb));
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {

@@ -5,7 +5,9 @@ sb2_bin_dense), joins the ranks with the chosen exchange (NVLink inside the tree
 trains. Rank 0 then trains the whole dataset on its one GPU and with the CPU oracle, and writes whether the N-rank
 trees equal both, field by field, as JSON to the output path.
 
-usage: torchrun ... multirank_worker.py <output.json> <auto|nccl> <config> <rows> <trees> <num_leaves>
+usage: torchrun ... multirank_worker.py <output.json> <auto|nccl> <config> <rows> <trees> <num_leaves> [share]
+
+With `share`, every handle skips the dominant bins of the tiles that share picks (sb2_set_dominant_share).
 """
 
 from __future__ import annotations
@@ -23,6 +25,7 @@ sys.path.insert(0, str(ROOT / "tests"))
 
 def main():
     out_path, mode, config, rows, trees, leaves = sys.argv[1], sys.argv[2], sys.argv[3], *map(int, sys.argv[4:7])
+    share = float(sys.argv[7]) if len(sys.argv) > 7 else None
     import torch
     import torch.distributed as dist
 
@@ -43,6 +46,8 @@ def main():
         lo, hi = rows * rank // world, rows * (rank + 1) // world
         data = bench.build_dataset(lo, hi, dev)
         b = B200Backend(local)
+        if share is not None:
+            b.set_dominant_share(share)
         b.load(data, p.objective, p.sigmoid)
         b.set_rank_exchange(_abi.EXCHANGE_NCCL if mode == "nccl" else _abi.EXCHANGE_AUTO)
         uid = [B200Backend.nccl_unique_id() if rank == 0 else None]
@@ -55,6 +60,8 @@ def main():
         if rank == 0:
             full = bench.build_dataset(0, rows, dev)
             one = B200Backend(local)
+            if share is not None:
+                one.set_dominant_share(share)
             one.load(full, p.objective, p.sigmoid)
             single = one.train(p, s0)
             one.close()

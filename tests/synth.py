@@ -27,9 +27,10 @@ def unit(stream: int, rows: np.ndarray) -> np.ndarray:
 
 
 def random_binned(rows: int, bins_per_feature: list[int], nan_bins: list[bool] | None = None, seed: int = 1,
-                  skew: float = 0.0, label_kind: str = "regression") -> BinnedDataset:
-    """Rows with hash-drawn bins per feature (a `skew` share of rows in bin 0) and a label that depends on a few
-    bins, so trees have structure."""
+                  skew: float = 0.0, label_kind: str = "regression",
+                  skew_bins: list[int] | None = None) -> BinnedDataset:
+    """Rows with hash-drawn bins per feature (a `skew` share of rows in bin 0, or in feature f's skew_bins[f]) and a
+    label that depends on a few bins, so trees have structure."""
     r = np.arange(rows, dtype=np.uint64)
     nf = len(bins_per_feature)
     nan_bins = nan_bins or [False] * nf
@@ -39,7 +40,7 @@ def random_binned(rows: int, bins_per_feature: list[int], nan_bins: list[bool] |
         b = (u * nb).astype(np.int64)
         if skew > 0:
             zero = unit(seed * 1000 + 500 + f, r) < skew
-            b[zero] = 0
+            b[zero] = skew_bins[f] if skew_bins is not None else 0
         bins[:, f] = np.minimum(b, nb - 1).astype(np.uint8)
     signal = np.zeros(rows)
     for f in range(min(nf, 6)):

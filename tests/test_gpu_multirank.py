@@ -24,23 +24,29 @@ ROOT = Path(__file__).resolve().parent.parent
 WORKER = Path(__file__).resolve().parent / "multirank_worker.py"
 
 
+# config c2's shape (100 features, binary) at 1M rows: 255-leaf trees run grid steps of eight splits; c5's (2,000
+# features, 80% of them 95% zeros) at 200K rows with the dominant-bin skip: every rank skips its own most frequent
+# bins and recovers them from its own totals before the exchange
+CASES = [("c2", 1_000_000, 3, 255, None), ("c5", 200_000, 3, 31, 0.125)]
+
+
+@pytest.mark.parametrize("config,rows,trees,leaves,share", CASES, ids=[c[0] for c in CASES])
 @pytest.mark.parametrize("mode", ["auto", "nccl"])
-def test_two_ranks_grow_the_trees_of_one_gpu(device, mode, tmp_path):
+def test_two_ranks_grow_the_trees_of_one_gpu(device, mode, config, rows, trees, leaves, share, tmp_path):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     out = tmp_path / "result.json"
-    port = 29500 + (os.getpid() + (0 if mode == "auto" else 7)) % 2000
-    # config c2's shape (100 features, binary) at 1M rows: 255-leaf trees run grid steps of eight splits
+    port = 29500 + (os.getpid() + (0 if mode == "auto" else 7) + (0 if config == "c2" else 13)) % 2000
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", f"--master-port={port}", str(WORKER), str(out), mode,
-           "c2", "1000000", "3", "255"]
+           config, str(rows), str(trees), str(leaves)] + ([str(share)] if share is not None else [])
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT))
     run = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
     assert run.returncode == 0, (run.stdout[-4000:], run.stderr[-4000:])
     res = json.loads(out.read_text())
-    assert res["world"] == 2 and res["trees"] == 3
+    assert res["world"] == 2 and res["trees"] == trees
     assert res["tree_kernel_exchange"] == (mode == "auto"), res
     assert res["identical_to_one_gpu"], res["differences"]
     assert res["identical_to_oracle"], res["differences"]

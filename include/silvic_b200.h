@@ -149,16 +149,22 @@ typedef struct sb2_bag_spec {
 
 enum { SB2_LEFT = 0, SB2_RIGHT = 1 }; /* Side (crates/silvic-core/src/backend/mod.rs:94-113) */
 
-/* SplitConfig (crates/silvic-core/src/split.rs:50-61), numerical fields. */
+/* SplitConfig (crates/silvic-core/src/split.rs:50-61). The categorical fields matter only for categorical features;
+ * the reference's defaults are 100, 10, 10, 4 and 32 (config.rs:145-149). */
 typedef struct sb2_split_config {
     int64_t min_data_in_leaf;
     double min_sum_hessian_in_leaf;
     double lambda_l1;
     double lambda_l2;
     double min_gain_to_split;
+    int64_t min_data_per_group;
+    double cat_l2;
+    double cat_smooth;
+    int32_t max_cat_to_onehot;  /* a categorical feature of at most this many bins gets the one-hot scan */
+    int32_t max_cat_threshold;  /* most categories a sorted categorical split sends left */
 } sb2_split_config;
 
-/* SplitInfo (crates/silvic-core/src/split.rs:122-132) of a numerical split, plus LeafSplit::splittable. */
+/* SplitInfo (crates/silvic-core/src/split.rs:122-132), plus LeafSplit::splittable. */
 typedef struct sb2_split_info {
     int32_t found;        /* 0: the leaf has no split (LeafSplit::best == None) */
     int32_t feature;
@@ -170,6 +176,9 @@ typedef struct sb2_split_info {
     double right_grad, right_hess;
     int64_t right_count;
     double left_output, right_output;
+    int32_t categorical;           /* SplitRule::Categorical: the bins set in cat_bins go left, every other bin right */
+    int32_t pad_;
+    uint32_t cat_bins[8];
 } sb2_split_info;
 
 /* Training parameters (crates/silvic-core/src/config.rs:73-116, defaults :123-165), the subset this backend
@@ -203,6 +212,11 @@ typedef struct sb2_params {
     const double* label_gain;             /* NULL: the default gains */
     uint32_t num_label_gain;
     uint32_t pad2_;
+    int32_t max_cat_to_onehot;            /* categorical features: as in sb2_split_config */
+    int32_t max_cat_threshold;
+    double cat_l2;
+    double cat_smooth;
+    int64_t min_data_per_group;
 } sb2_params;
 
 /* One tree in LightGBM 3.3.5 array layout (crates/silvic-core/src/tree.rs:47-73). The arrays belong to the
@@ -224,6 +238,7 @@ typedef struct sb2_tree_view {
     const double* internal_value;
     const double* internal_weight;
     const int64_t* internal_count;
+    const uint32_t* cat_bins;      /* 8 words per split: the bins a categorical split sends left (0 for numerical) */
 } sb2_tree_view;
 
 typedef struct sb2_backend sb2_backend;
@@ -246,8 +261,8 @@ int sb2_last_error(const sb2_backend* b, char* buf, size_t len);
 /* Backend::name */
 int sb2_name(const sb2_backend* b, char* buf, size_t len);
 
-/* Backend::load: copies the training set to the device and lays it out in 32-feature tiles. Datasets with
- * categorical features return SB2_EUNSUPPORTED (no device categorical scan). */
+/* Backend::load: copies the training set to the device and lays it out in 32-feature tiles. Numerical and
+ * categorical features alike (the split search scans each by its kind). */
 int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* objective);
 /* Backend::init_scores (dataset 0, the training set) */
 int sb2_init_scores(sb2_backend* b, int dataset, double value);
@@ -283,7 +298,7 @@ int sb2_read_gradients(sb2_backend* b, float* grad, float* hess, size_t len);
 
 /* ---- split search: split::find_best_split (crates/silvic-core/src/split.rs:919-961) ------------------------ */
 
-/* The best numerical split of a leaf from its histogram `hist` (2 * total_bins doubles in histogram units,
+/* The best split of a leaf from its histogram `hist` (2 * total_bins doubles in histogram units,
  * integer-valued), over the features with evaluate[f] != 0, run on the device. splittable (num_features bytes)
  * receives LeafSplit::splittable. */
 int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const uint8_t* evaluate,
@@ -297,7 +312,7 @@ int sb2_find_best_split(sb2_backend* b, const double* hist, size_t len, const ui
  *   evaluate    num_features bytes, nonzero = search the feature
  *   out         one sb2_split_info, written
  *   splittable  num_features bytes, written
- * The call allocates nothing: its scratch is a fixed 320 KiB array in this library's device module, enough for
+ * The call allocates nothing: its scratch is a fixed 480 KiB array in this library's device module, enough for
  * datasets of at most 4096 features; larger ones return SB2_EUNSUPPORTED. The first call on each handle looks up
  * that array's address on the handle's device (cudaGetSymbolAddress, which may load the module) and keeps it for
  * the handle's life, so make that first call before any stream capture. A cudaDeviceReset ends the handle with

@@ -880,11 +880,15 @@ struct Best {
     double left_units[2];
 };
 
+// CandidateKind (split.rs:318-327)
+enum CandidateKind { kNumerical = 0, kOneHot = 1, kSortedForward = 2, kSortedReverse = 3 };
+
 struct Candidate {
     int64_t feature;
     double gain;
     Best best;
     bool default_left;
+    int kind = kNumerical;
 };
 
 // reverse_best (split.rs:557-567)
@@ -965,6 +969,164 @@ bool find_numerical(const LeafCtx& ctx, int64_t feature, const double* hist, siz
     return have;
 }
 
+// LeafCtx::bin_count (split.rs:236-239)
+inline int64_t bin_count(const LeafCtx& ctx, double hess_units) {
+    return round_int(hess_units * ctx.scale.hess * ctx.cnt_factor);
+}
+
+// Check and LeafCtx::check (split.rs:241-261)
+enum class Check { Continue, Break, Evaluate };
+
+// Side (split.rs:269-296): the side of a scan that accumulates bins; its real hessian starts at kEpsilon.
+struct Side {
+    double units[2] = {0.0, 0.0};
+    int64_t count = 0;
+    double hess = K_EPSILON;
+    void add(const LeafCtx& ctx, const double* bin) {
+        units[0] += bin[0];
+        units[1] += bin[1];
+        count += bin_count(ctx, bin[1]);
+        hess = K_EPSILON + units[1] * ctx.scale.hess;
+    }
+};
+
+Check check(const LeafCtx& ctx, const Side& grow, int64_t shrink_count, double shrink_hess) {
+    const sb2_split_config& c = *ctx.cfg;
+    if (grow.count < c.min_data_in_leaf || grow.count <= 0 || grow.hess < c.min_sum_hessian_in_leaf ||
+        grow.units[1] <= 0.0)
+        return Check::Continue;
+    if (shrink_count < c.min_data_in_leaf || shrink_count <= 0) return Check::Break;
+    if (shrink_hess < c.min_sum_hessian_in_leaf || ctx.units.hess - grow.units[1] <= 0.0) return Check::Break;
+    return Check::Evaluate;
+}
+
+// find_onehot (split.rs:694-737): one category left, the rest right.
+bool find_onehot(const LeafCtx& ctx, int64_t feature, const double* hist, size_t num_bins, bool& splittable,
+                 Candidate& cand) {
+    const sb2_split_config& c = *ctx.cfg;
+    splittable = false;
+    bool have = false;
+    Best best{};
+    for (size_t t = 1; t < num_bins; ++t) {
+        const double* bin = hist + 2 * t;
+        Side left;
+        left.add(ctx, bin);
+        const int64_t other_count = ctx.num_data - left.count;
+        // the bin's raw hessian is tested, and kEpsilon comes off the other side
+        const double raw_hess = bin[1] * ctx.scale.hess;
+        const double other_hess = ctx.sum_hess - raw_hess - K_EPSILON;
+        Side grow = left;
+        grow.hess = raw_hess;
+        if (check(ctx, grow, other_count, other_hess) != Check::Evaluate) continue;
+        const double grad = left.units[0] * ctx.scale.grad;
+        const double gain = split_gain(ctx.sum_grad - grad, grad, other_hess, raw_hess + K_EPSILON, c.lambda_l1,
+                                       c.lambda_l2);
+        if (std::isnan(gain) || gain <= ctx.min_gain_shift) continue;
+        splittable = true;
+        if (!have || gain > best.gain) {
+            best = Best{gain, static_cast<uint32_t>(t), grad, raw_hess + K_EPSILON, left.count,
+                        {left.units[0], left.units[1]}};
+            have = true;
+        }
+    }
+    if (have) {
+        cand.feature = feature;
+        cand.gain = best.gain - ctx.min_gain_shift;
+        cand.best = best;
+        cand.default_left = false;
+        cand.kind = kOneHot;
+    }
+    return have;
+}
+
+// f64::total_cmp's key: the bits with every bit but the sign flipped for negative values, compared as i64.
+inline int64_t total_order_key(double v) {
+    int64_t bits;
+    std::memcpy(&bits, &v, sizeof(bits));
+    return bits ^ static_cast<int64_t>(static_cast<uint64_t>(bits >> 63) >> 1);
+}
+
+// sorted_categories (split.rs:739-761): the categories (bins 1..) with at least cat_smooth estimated rows, sorted by
+// sum_g / (sum_h + cat_smooth) (total order), equal ratios in ascending bin order; returns how many.
+size_t sorted_categories(const LeafCtx& ctx, const double* hist, size_t num_bins, uint32_t* order) {
+    const sb2_split_config& c = *ctx.cfg;
+    const size_t nb = std::min(num_bins, MAX_BINS);
+    size_t used = 0;
+    for (size_t t = 1; t < nb; ++t)
+        if (static_cast<double>(bin_count(ctx, hist[2 * t + 1])) >= c.cat_smooth) order[used++] = static_cast<uint32_t>(t);
+    auto ctr = [&](uint32_t t) { return (hist[2 * t] * ctx.scale.grad) / (hist[2 * t + 1] * ctx.scale.hess + c.cat_smooth); };
+    std::sort(order, order + used, [&](uint32_t a, uint32_t b) {
+        const int64_t ka = total_order_key(ctr(a)), kb = total_order_key(ctr(b));
+        return ka != kb ? ka < kb : a < b;
+    });
+    return used;
+}
+
+// SortedScan::run (split.rs:792-845): the best prefix of order(0 .. steps); threshold holds its length minus one.
+template <class Order>
+bool sorted_scan(const LeafCtx& ctx, const double* hist, double l2, size_t steps, Order order, bool& splittable,
+                 Best& best) {
+    const sb2_split_config& c = *ctx.cfg;
+    Side left;
+    int64_t cnt_cur_group = 0;
+    bool have = false;
+    for (size_t i = 0; i < steps; ++i) {
+        const size_t t = order(i);
+        const int64_t before = left.count;
+        left.add(ctx, hist + 2 * t);
+        cnt_cur_group += left.count - before;
+        const int64_t right_count = ctx.num_data - left.count;
+        const double right_hess = ctx.sum_hess - left.hess;
+        const Check k = check(ctx, left, right_count, right_hess);
+        if (k == Check::Continue) continue;
+        if (k == Check::Break) break;
+        if (right_count < c.min_data_per_group) break;
+        if (cnt_cur_group < c.min_data_per_group) continue;
+        cnt_cur_group = 0;
+        const double left_grad = left.units[0] * ctx.scale.grad;
+        const double gain = split_gain(left_grad, ctx.sum_grad - left_grad, left.hess, right_hess, c.lambda_l1, l2);
+        if (std::isnan(gain) || gain <= ctx.min_gain_shift) continue;
+        splittable = true;
+        if (!have || gain > best.gain) {
+            best = Best{gain, static_cast<uint32_t>(i), left_grad, left.hess, left.count, {left.units[0], left.units[1]}};
+            have = true;
+        }
+    }
+    return have;
+}
+
+// find_sorted_categorical (split.rs:763-788): prefixes of up to max_cat_threshold categories from either end of the
+// sorted order, the low end first; the high end replaces it only when strictly better.
+bool find_sorted_categorical(const LeafCtx& ctx, int64_t feature, const double* hist, size_t num_bins,
+                             bool& splittable, Candidate& cand) {
+    const sb2_split_config& c = *ctx.cfg;
+    uint32_t sorted[MAX_BINS];
+    const size_t used = sorted_categories(ctx, hist, num_bins, sorted);
+    const size_t max_num_cat = std::min<size_t>(static_cast<size_t>(std::max(c.max_cat_threshold, 0)), (used + 1) / 2);
+    const double l2 = c.lambda_l2 + c.cat_l2;
+    splittable = false;
+    bool have = false;
+    Best best{};
+    bool best_forward = true;
+    for (bool forward : {true, false}) {
+        Best b{};
+        auto order = [&](size_t i) { return static_cast<size_t>(forward ? sorted[i] : sorted[used - 1 - i]); };
+        if (sorted_scan(ctx, hist, l2, std::min(used, max_num_cat), order, splittable, b) && (!have || b.gain > best.gain)) {
+            best = b;
+            best_forward = forward;
+            have = true;
+        }
+    }
+    if (have) {
+        cand.feature = feature;
+        cand.gain = best.gain - ctx.min_gain_shift;
+        cand.best = best;
+        cand.default_left = false;
+        cand.kind = best_forward ? kSortedForward : kSortedReverse;
+    }
+    return have;
+}
+
 // better (split.rs:866-873): higher gain (NaN as kMinScore), then the lower feature.
 bool better(const Candidate& a, const Candidate& b) {
     double ga = std::isnan(a.gain) ? MIN_SCORE : a.gain;
@@ -974,16 +1136,31 @@ bool better(const Candidate& a, const Candidate& b) {
     return a.feature < b.feature;
 }
 
-// finish (split.rs:632-651)
-sb2_split_info finish(const LeafCtx& ctx, const Candidate& c) {
+// finish (split.rs:632-651) through split_info (:654-691): a categorical split's left bins are its one category or
+// the first threshold + 1 categories of the sorted order from the chosen end, with the categorical l2.
+sb2_split_info finish(const LeafCtx& ctx, const Candidate& c, const double* hist, size_t num_bins) {
     const Best& b = c.best;
-    const double l1 = ctx.cfg->lambda_l1, l2 = ctx.cfg->lambda_l2;
+    const double l1 = ctx.cfg->lambda_l1;
+    const double l2 = c.kind == kSortedForward || c.kind == kSortedReverse ? ctx.cfg->lambda_l2 + ctx.cfg->cat_l2
+                                                                          : ctx.cfg->lambda_l2;
     sb2_split_info s{};
     s.found = 1;
     s.feature = static_cast<int32_t>(c.feature);
     s.gain = b.gain - ctx.min_gain_shift;
-    s.threshold = b.threshold;
+    s.threshold = c.kind == kNumerical ? b.threshold : 0u;
     s.default_left = c.default_left;
+    if (c.kind == kOneHot) {
+        s.categorical = 1;
+        s.cat_bins[b.threshold / 32] |= 1u << (b.threshold % 32);
+    } else if (c.kind != kNumerical) {
+        s.categorical = 1;
+        uint32_t sorted[MAX_BINS];
+        const size_t used = sorted_categories(ctx, hist, num_bins, sorted);
+        for (size_t i = 0; i <= b.threshold; ++i) {
+            const uint32_t bin = c.kind == kSortedForward ? sorted[i] : sorted[used - 1 - i];
+            s.cat_bins[bin / 32] |= 1u << (bin % 32);
+        }
+    }
     s.left_grad = b.left_units[0];
     s.left_hess = b.left_units[1];
     s.left_count = b.left_count;
@@ -995,8 +1172,7 @@ sb2_split_info finish(const LeafCtx& ctx, const Candidate& c) {
     return s;
 }
 
-// find_best_split (split.rs:919-961), numerical features; categorical features are out of the device's scope and
-// make the search fail.
+// find_best_split (split.rs:919-961)
 bool find_best_split(const sb2_dataset& d, const double* hist, const uint8_t* evaluate, LeafSums sums,
                      HistScale scale, const sb2_split_config* cfg, sb2_split_info& out, uint8_t* splittable) {
     std::memset(splittable, 0, d.num_features);
@@ -1011,24 +1187,31 @@ bool find_best_split(const sb2_dataset& d, const double* hist, const uint8_t* ev
     parallel_tasks(static_cast<size_t>(F), [&](size_t f) {
         const sb2_feature& m = d.features[f];
         if (!evaluate[f] || m.num_bins == 0 || m.kind == SB2_TRIVIAL) return;
-        if (m.kind != SB2_NUMERICAL) {
-            bad_flag = true;
-            return;
-        }
+        const double* fh = hist + 2 * static_cast<size_t>(m.hist_offset);
         bool sp = false;
-        have[f] = find_numerical(ctx, f, hist + 2 * static_cast<size_t>(m.hist_offset), m.num_bins, m.nan_bin != 0,
-                                 sp, per[f]);
+        // find_feature (split.rs:848-862)
+        if (m.kind == SB2_NUMERICAL)
+            have[f] = find_numerical(ctx, f, fh, m.num_bins, m.nan_bin != 0, sp, per[f]);
+        else if (m.kind == SB2_CATEGORICAL && static_cast<int64_t>(m.num_bins) <= cfg->max_cat_to_onehot)
+            have[f] = find_onehot(ctx, f, fh, m.num_bins, sp, per[f]);
+        else if (m.kind == SB2_CATEGORICAL)
+            have[f] = find_sorted_categorical(ctx, f, fh, m.num_bins, sp, per[f]);
+        else
+            bad_flag = true;
         splittable[f] = sp;
     });
     bad = bad_flag;
     if (bad) {
-        g_error = "categorical features are not supported";
+        g_error = "unknown feature kind";
         return false;
     }
     const Candidate* best = nullptr;
     for (int64_t f = 0; f < F; ++f)
         if (have[f] && (!best || better(per[f], *best))) best = &per[f];
-    if (best) out = finish(ctx, *best);
+    if (best) {
+        const sb2_feature& m = d.features[best->feature];
+        out = finish(ctx, *best, hist + 2 * static_cast<size_t>(m.hist_offset), m.num_bins);
+    }
     return true;
 }
 
@@ -1056,6 +1239,7 @@ void feature_mask(const sb2_dataset& d, double fraction, uint32_t seed, uint32_t
 
 // ---- tree.rs ----------------------------------------------------------------------------------------------------
 
+constexpr int8_t CATEGORICAL_MASK = 1;                         // tree.rs:10
 constexpr int8_t DEFAULT_LEFT_MASK = 2;                        // tree.rs:11
 constexpr double ZERO_THRESHOLD = static_cast<double>(1e-35f); // tree.rs:13
 
@@ -1074,6 +1258,8 @@ struct Tree {
     std::vector<int64_t> leaf_count{0};
     std::vector<double> internal_value, internal_weight;
     std::vector<int64_t> internal_count;
+    std::vector<uint32_t> cat_bins;  // 8 words per split: the bins a categorical split sends left (0: numerical)
+    int32_t num_cat = 0;
     double shrinkage = 1.0;
     std::vector<int32_t> leaf_parent{-1}, leaf_depth{0};
 
@@ -1089,6 +1275,19 @@ struct Tree {
                             bool nan_missing, const Children& c) {
         int8_t dt = static_cast<int8_t>((nan_missing ? 2 : 0) << 2);
         if (default_left) dt |= DEFAULT_LEFT_MASK;
+        const uint32_t none[8] = {};
+        return split(leaf, feature, thr, thr_bin, dt, none, c);
+    }
+    // Tree::split_categorical (tree.rs:125-141): the threshold is the split's index among the tree's categorical
+    // splits, MissingType::NaN; the category bitset (cat_threshold) is built from the left bins' category values
+    // when the model is written, so the tree keeps the bins.
+    int32_t split_categorical(int32_t leaf, int32_t feature, const uint32_t* left_bins, const Children& c) {
+        const double index = static_cast<double>(num_cat++);
+        return split(leaf, feature, index, 0u, static_cast<int8_t>(CATEGORICAL_MASK | (2 << 2)), left_bins, c);
+    }
+    int32_t split(int32_t leaf, int32_t feature, double thr, uint32_t thr_bin, int8_t dt, const uint32_t* bins,
+                  const Children& c) {
+        cat_bins.insert(cat_bins.end(), bins, bins + 8);
         int32_t node = num_leaves - 1, new_leaf = num_leaves;
         int32_t parent = leaf_parent[leaf];
         if (parent >= 0) {
@@ -1202,6 +1401,11 @@ struct Learner {
         cfg.lambda_l1 = p.lambda_l1;
         cfg.lambda_l2 = p.lambda_l2;
         cfg.min_gain_to_split = p.min_gain_to_split;
+        cfg.min_data_per_group = p.min_data_per_group;  // SplitConfig::new (split.rs:64-77)
+        cfg.cat_l2 = p.cat_l2;
+        cfg.cat_smooth = p.cat_smooth;
+        cfg.max_cat_to_onehot = p.max_cat_to_onehot;
+        cfg.max_cat_threshold = p.max_cat_threshold;
         for (uint32_t f = 0; f < d0.num_features; ++f)
             if (d0.features[f].num_bins != 0) {
                 sums_feature = f;
@@ -1248,6 +1452,10 @@ struct Learner {
         sb2_bin_split s{};
         s.group = m.group;
         s.column = m.column;
+        if (info.categorical) {
+            std::memcpy(s.left_bins, info.cat_bins, sizeof(s.left_bins));
+            return s;
+        }
         for (uint32_t b = 0; b <= info.threshold; ++b) s.left_bins[b / 32] |= 1u << (b % 32);
         if (info.default_left && m.kind == SB2_NUMERICAL && m.nan_bin) {
             uint32_t b = m.num_bins - 1;
@@ -1342,11 +1550,17 @@ struct Learner {
         c.left_weight = info.left_hess * scale.hess;
         c.right_weight = info.right_hess * scale.hess;
         c.gain = static_cast<float>(info.gain + cfg.min_gain_to_split);
-        // apply_split (learner.rs:459-485): the threshold is the bin's upper bound, f64::MAX for +inf.
-        double bound = meta.upper_bounds[info.threshold];
-        double thr = std::isfinite(bound) ? bound : std::numeric_limits<double>::max();
-        int32_t right_index = tree.split_numerical(static_cast<int32_t>(index), info.feature, thr, info.threshold,
-                                                   info.default_left != 0, meta.nan_bin != 0, c);
+        // apply_split (learner.rs:459-485): the threshold is the bin's upper bound, f64::MAX for +inf; a categorical
+        // split keeps its left bins.
+        int32_t right_index;
+        if (info.categorical) {
+            right_index = tree.split_categorical(static_cast<int32_t>(index), info.feature, info.cat_bins, c);
+        } else {
+            double bound = meta.upper_bounds[info.threshold];
+            double thr = std::isfinite(bound) ? bound : std::numeric_limits<double>::max();
+            right_index = tree.split_numerical(static_cast<int32_t>(index), info.feature, thr, info.threshold,
+                                               info.default_left != 0, meta.nan_bin != 0, c);
+        }
         if (static_cast<size_t>(right_index) != leaves.size()) throw std::runtime_error("leaf numbering");
         std::vector<double> parent_hist = std::move(leaves[index].hist);
         Leaf left, right;
@@ -1419,8 +1633,6 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
         rk.partition.reserve(n);
         w.ranks.push_back(std::move(rk));
     }
-    for (uint32_t f = 0; f < shards[0].num_features; ++f)
-        if (shards[0].features[f].kind == SB2_CATEGORICAL) throw std::runtime_error("categorical features");
     sb2_objective obj{};
     obj.kind = p.objective;
     obj.sigmoid = p.sigmoid;
@@ -1520,6 +1732,8 @@ ModelOut train(const sb2_dataset* shards, int num_shards, const sb2_params& p) {
             sb2_split_info info{};
             info.threshold = tree.threshold_bin[k];
             info.default_left = (tree.decision_type[k] & DEFAULT_LEFT_MASK) != 0;
+            info.categorical = (tree.decision_type[k] & CATEGORICAL_MASK) != 0;
+            std::memcpy(info.cat_bins, tree.cat_bins.data() + 8 * static_cast<size_t>(k), sizeof(info.cat_bins));
             splits.push_back(Learner::bin_split(d0.features[tree.split_feature[k]], info));
         }
         std::vector<sb2_device_node> nodes;
@@ -1717,6 +1931,7 @@ int orc_model_tree(const orc_model* m, int index, sb2_tree_view* v) {
     v->internal_value = t.internal_value.data();
     v->internal_weight = t.internal_weight.data();
     v->internal_count = t.internal_count.data();
+    v->cat_bins = t.cat_bins.data();
     return SB2_OK;
 }
 double orc_model_init_score(const orc_model* m) { return m->m.init_score; }

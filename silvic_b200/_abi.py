@@ -120,6 +120,11 @@ class SplitConfig(C.Structure):
         ("lambda_l1", C.c_double),
         ("lambda_l2", C.c_double),
         ("min_gain_to_split", C.c_double),
+        ("min_data_per_group", C.c_int64),
+        ("cat_l2", C.c_double),
+        ("cat_smooth", C.c_double),
+        ("max_cat_to_onehot", C.c_int32),
+        ("max_cat_threshold", C.c_int32),
     ]
 
 
@@ -138,10 +143,15 @@ class SplitInfo(C.Structure):
         ("right_count", C.c_int64),
         ("left_output", C.c_double),
         ("right_output", C.c_double),
+        ("categorical", C.c_int32),
+        ("pad_", C.c_int32),
+        ("cat_bins", C.c_uint32 * 8),
     ]
 
     def as_tuple(self):
-        return tuple(getattr(self, name) for name, _ in self._fields_)
+        """Every field's value (arrays as tuples), for comparisons."""
+        return tuple(tuple(v) if isinstance(v, C.Array) else v
+                     for v in (getattr(self, name) for name, _ in self._fields_))
 
 
 class Params(C.Structure):
@@ -174,6 +184,11 @@ class Params(C.Structure):
         ("label_gain", C.POINTER(C.c_double)),
         ("num_label_gain", C.c_uint32),
         ("pad2_", C.c_uint32),
+        ("max_cat_to_onehot", C.c_int32),
+        ("max_cat_threshold", C.c_int32),
+        ("cat_l2", C.c_double),
+        ("cat_smooth", C.c_double),
+        ("min_data_per_group", C.c_int64),
     ]
 
 
@@ -195,6 +210,7 @@ class TreeView(C.Structure):
         ("internal_value", C.POINTER(C.c_double)),
         ("internal_weight", C.POINTER(C.c_double)),
         ("internal_count", C.POINTER(C.c_int64)),
+        ("cat_bins", C.POINTER(C.c_uint32)),
     ]
 
 

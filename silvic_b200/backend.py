@@ -43,6 +43,11 @@ _PARAM_ALIASES = {
     "lambdarank_truncation_level": [],
     "lambdarank_norm": [],
     "label_gain": [],
+    "max_cat_to_onehot": [],
+    "max_cat_threshold": [],
+    "cat_l2": [],
+    "cat_smooth": [],
+    "min_data_per_group": [],
 }
 _OBJECTIVES = {"regression": _abi.REGRESSION, "regression_l2": _abi.REGRESSION, "l2": _abi.REGRESSION,
                "mean_squared_error": _abi.REGRESSION, "mse": _abi.REGRESSION, "binary": _abi.BINARY,
@@ -375,10 +380,11 @@ class Tree:
     internal_value: np.ndarray
     internal_weight: np.ndarray
     internal_count: np.ndarray
+    cat_bins: np.ndarray  # [splits, 8] u32: the bins a categorical split sends left (zeros for numerical)
 
     FIELDS = ("split_feature", "split_gain", "threshold", "threshold_bin", "decision_type", "left_child",
               "right_child", "leaf_value", "leaf_weight", "leaf_count", "internal_value", "internal_weight",
-              "internal_count")
+              "internal_count", "cat_bins")
 
     @staticmethod
     def from_view(v: _abi.TreeView) -> "Tree":
@@ -387,12 +393,16 @@ class Tree:
         return Tree(nl, v.shrinkage, arr(v.split_feature, n), arr(v.split_gain, n), arr(v.threshold, n),
                     arr(v.threshold_bin, n), arr(v.decision_type, n), arr(v.left_child, n), arr(v.right_child, n),
                     arr(v.leaf_value, nl), arr(v.leaf_weight, nl), arr(v.leaf_count, nl), arr(v.internal_value, n),
-                    arr(v.internal_weight, n), arr(v.internal_count, n))
+                    arr(v.internal_weight, n), arr(v.internal_count, n),
+                    (arr(v.cat_bins, 8 * n) if v.cat_bins else np.zeros(8 * n, dtype=np.uint32)).reshape(n, 8))
 
     def leaf_index(self, row: np.ndarray) -> int:
-        """`Tree::GetLeaf` with NumericalDecision (crates/silvic-core/src/model/predict.rs:98-141)."""
+        """`Tree::GetLeaf` with NumericalDecision (crates/silvic-core/src/model/predict.rs:98-141); trees with
+        categorical splits predict through their model text (silvic_b200.model_text), which holds the categories."""
         if self.num_leaves <= 1:
             return 0
+        if any(int(d) & 1 for d in self.decision_type):
+            raise ValueError("a categorical split: predict through the model text")
         zero = float(np.float32(1e-35))
         node = 0
         while node >= 0:

@@ -56,6 +56,7 @@ struct HostTree {
     std::vector<int64_t> leaf_count;
     std::vector<double> internal_value, internal_weight;
     std::vector<int64_t> internal_count;
+    std::vector<uint32_t> cat_bins;  // 8 words per split: a categorical split's left bins (0 for numerical)
 };
 
 }  // namespace
@@ -410,6 +411,11 @@ void sb2_default_params(sb2_params* p) {
     p->lambdarank_truncation_level = 30;
     p->label_gain = nullptr;               // config.rs:118-121: 2^i - 1 for i < 31
     p->num_label_gain = 0;
+    p->max_cat_to_onehot = 4;              // config.rs:145-149
+    p->max_cat_threshold = 32;
+    p->cat_l2 = 10.0;
+    p->cat_smooth = 10.0;
+    p->min_data_per_group = 100;
 }
 
 int sb2_create(int device, sb2_backend** out) {
@@ -611,9 +617,6 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     std::vector<uint32_t> used;
     for (uint32_t f = 0; f < F; ++f) {
         const sb2_feature& m = train->features[f];
-        if (m.kind == SB2_CATEGORICAL)
-            return b->fail(SB2_EUNSUPPORTED, "categorical feature " + std::to_string(f) +
-                                                 ": the device split search is numerical only");
         if (m.num_bins > 256) return b->fail(SB2_EDATA, "feature with more than 256 bins");
         if (m.kind == SB2_NUMERICAL && m.num_bins > 0) {
             size_t nb = m.num_bins - (m.nan_bin ? 1 : 0);
@@ -1435,7 +1438,7 @@ struct TrainBuffers {
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
 int carve_tree(sb2_backend* b, DeviceBuffer& buf, size_t count, size_t L, DevTree& t) {
-    const size_t sizes[] = {4, 4, 4, 1, 4, 4, 8, 8, 8, 8, 8, 8, 4, 4};  // bytes per entry of each array below
+    const size_t sizes[] = {4, 4, 4, 1, 4, 4, 8, 8, 8, 8, 8, 8, 4, 4, 32};  // bytes per entry of each array below
     size_t total = (sizeof(int32_t) * count + 255) / 256 * 256;
     for (size_t s : sizes) total += (s * count * L + 255) / 256 * 256;
     SB2_CUDA(b, buf.alloc(total));
@@ -1461,6 +1464,7 @@ int carve_tree(sb2_backend* b, DeviceBuffer& buf, size_t count, size_t L, DevTre
     t.leaf_count = reinterpret_cast<int64_t*>(take(8 * n));
     t.leaf_parent = reinterpret_cast<int32_t*>(take(4 * n));
     t.leaf_depth = reinterpret_cast<int32_t*>(take(4 * n));
+    t.cat_bins = reinterpret_cast<uint32_t*>(take(32 * n));
     if (static_cast<size_t>(p - buf.as<char>()) > buf.bytes) return b->fail(SB2_EINTERNAL, "tree buffer overrun");
     return SB2_OK;
 }
@@ -1727,6 +1731,11 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     t.cfg.lambda_l1 = p->lambda_l1;
     t.cfg.lambda_l2 = p->lambda_l2;
     t.cfg.min_gain_to_split = p->min_gain_to_split;
+    t.cfg.min_data_per_group = p->min_data_per_group;
+    t.cfg.cat_l2 = p->cat_l2;
+    t.cfg.cat_smooth = p->cat_smooth;
+    t.cfg.max_cat_to_onehot = p->max_cat_to_onehot;
+    t.cfg.max_cat_threshold = p->max_cat_threshold;
     t.max_leaves = L;
     t.max_depth = p->max_depth;
     t.sums_feature = -1;
@@ -1782,6 +1791,8 @@ int collect_model(sb2_backend* b, Training& tr, std::unique_ptr<sb2_model>& mode
     std::vector<int8_t> dt;
     std::vector<double> iv, iw, lv, lw;
     std::vector<int64_t> ic, lcnt;
+    std::vector<uint32_t> cb;
+    SB2_TRY(download(b, cb, rec.cat_bins, 8 * n));
     SB2_TRY(download(b, sf, rec.split_feature, n));
     SB2_TRY(download(b, sg, rec.split_gain, n));
     SB2_TRY(download(b, tbin, rec.threshold_bin, n));
@@ -1801,14 +1812,21 @@ int collect_model(sb2_backend* b, Training& tr, std::unique_ptr<sb2_model>& mode
         const int nl = heads[k].num_leaves;
         ht.num_leaves = nl;
         ht.shrinkage = heads[k].shrinkage;
+        int32_t num_cat = 0;
         for (int j = 0; j + 1 < nl; ++j) {
             const int32_t f = sf[o + j];
             ht.split_feature.push_back(f);
             ht.split_gain.push_back(sg[o + j]);
             ht.threshold_bin.push_back(tbin[o + j]);
-            // apply_split (learner.rs:470-475): the bin's upper bound, f64::MAX for the +inf bound.
-            double bound = b->upper_bounds[f].at(tbin[o + j]);
-            ht.threshold.push_back(std::isfinite(bound) ? bound : std::numeric_limits<double>::max());
+            ht.cat_bins.insert(ht.cat_bins.end(), cb.begin() + 8 * (o + j), cb.begin() + 8 * (o + j + 1));
+            if (dt[o + j] & 1) {
+                // Tree::split_categorical (tree.rs:125-141): the split's index among the tree's categorical splits
+                ht.threshold.push_back(static_cast<double>(num_cat++));
+            } else {
+                // apply_split (learner.rs:470-475): the bin's upper bound, f64::MAX for the +inf bound.
+                double bound = b->upper_bounds[f].at(tbin[o + j]);
+                ht.threshold.push_back(std::isfinite(bound) ? bound : std::numeric_limits<double>::max());
+            }
             ht.decision_type.push_back(dt[o + j]);
             ht.left_child.push_back(lc[o + j]);
             ht.right_child.push_back(rc[o + j]);
@@ -2145,6 +2163,7 @@ int sb2_model_tree(const sb2_model* m, int index, sb2_tree_view* v) {
     v->split_gain = t.split_gain.data();
     v->threshold = t.threshold.data();
     v->threshold_bin = t.threshold_bin.data();
+    v->cat_bins = t.cat_bins.data();
     v->decision_type = t.decision_type.data();
     v->left_child = t.left_child.data();
     v->right_child = t.right_child.data();

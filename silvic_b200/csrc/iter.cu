@@ -471,6 +471,8 @@ __global__ void __launch_bounds__(kRowThreads) finalize_kernel(IterArgs a) {
         a.record_tree.decision_type[base + k] = t.decision_type[k];
         a.record_tree.left_child[base + k] = t.left_child[k];
         a.record_tree.right_child[base + k] = t.right_child[k];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) a.record_tree.cat_bins[8 * (base + k) + w] = t.cat_bins[8 * static_cast<size_t>(k) + w];
     }
     __syncthreads();
     if (threadIdx.x == 0) {

@@ -227,9 +227,291 @@ __device__ void forward_best(const Ctx& x, const Grown& l, FeatureCandidate& o) 
     o.left_units_hess = l.uh;
 }
 
-// find_numerical (split.rs:584-620) for one feature.
+// ---- categorical features (split.rs:694-845) ------------------------------------------------------------
+//
+// A categorical feature is scanned by one warp: the one-hot scan (at most max_cat_to_onehot bins) evaluates every
+// category at once; the sorted scan ranks the categories by ctr with all-pairs comparisons, then walks both ends of
+// the order in chunks of 32 steps: the left side's sums are lane prefix sums, LightGBM's sequential rules (the first
+// `break`, and the min_data_per_group grouping that only resets where a candidate is evaluated) are a walk over the
+// chunk's ballots, and the gains of the evaluated steps are computed in parallel. The same IEEE operations on the same
+// exact integer sums as split.rs: the results are the CPU search's bit for bit.
+
+// LeafCtx::bin_count (split.rs:236-239)
+__device__ __forceinline__ int64_t bin_count(const Ctx& x, double hess_units) {
+    return round_int(dmul(dmul(hess_units, x.hs), x.cnt_factor));
+}
+
+// LeafCtx::check (split.rs:241-261) of a growing side (count, real hessian, hessian units) against the shrinking
+// one: 0 continue, 1 break, 2 evaluate.
+__device__ __forceinline__ int side_check(const Ctx& x, const sb2_split_config& c, int64_t count, double hess,
+                                          double units_hess, int64_t shrink_count, double shrink_hess) {
+    if (count < c.min_data_in_leaf || count <= 0 || hess < c.min_sum_hessian_in_leaf || units_hess <= 0.0) return 0;
+    if (shrink_count < c.min_data_in_leaf || shrink_count <= 0) return 1;
+    if (shrink_hess < c.min_sum_hessian_in_leaf || dsub(x.units_hess, units_hess) <= 0.0) return 1;
+    return 2;
+}
+
+// f64::total_cmp's key (IEEE totalOrder): every bit but the sign flipped for negative values, compared as i64.
+__device__ __forceinline__ int64_t total_order_key(double v) {
+    const int64_t b = __double_as_longlong(v);
+    return b ^ static_cast<int64_t>(static_cast<uint64_t>(b >> 63) >> 1);
+}
+
+// The warp's best (gain, index) of the lanes that have one: the higher gain, the lower index on equal gains.
+__device__ __forceinline__ void warp_best(bool& have, double& gain, int& index) {
+    for (int o = 16; o > 0; o >>= 1) {
+        const bool oh = __shfl_xor_sync(0xffffffffu, have, o);
+        const double og = __shfl_xor_sync(0xffffffffu, gain, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, index, o);
+        if (oh && (!have || og > gain || (og == gain && oi < index))) {
+            have = true;
+            gain = og;
+            index = oi;
+        }
+    }
+}
+
+// find_onehot (split.rs:694-737): one category left, the rest right (the bin's raw hessian is tested, and kEpsilon
+// comes off the other side). Whole warp; every lane gets the result.
+__device__ FeatureCandidate scan_onehot(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
+                                        const sb2_split_config& c) {
+    const int lane = threadIdx.x & 31, nb = static_cast<int>(f.num_bins);
+    FeatureCandidate o{};
+    o.feature = feature;
+    bool have = false, splittable = false;
+    double bg = 0.0;
+    int bt = 0x7FFFFFFF;
+    for (int t0 = 1; t0 < nb; t0 += 32) {
+        const int t = t0 + lane;
+        if (t >= nb) continue;
+        const int2 v = hist[t];
+        const double h = static_cast<double>(v.y);
+        const int64_t count = bin_count(x, h);
+        const double raw_hess = dmul(h, x.hs);
+        const double other_hess = dsub(dsub(x.sum_hess, raw_hess), kEpsilon);
+        if (side_check(x, c, count, raw_hess, h, x.num_data - count, other_hess) != 2) continue;
+        const double grad = dmul(static_cast<double>(v.x), x.gs);
+        const double gain = dadd(leaf_gain(dsub(x.sum_grad, grad), other_hess, c.lambda_l1, c.lambda_l2),
+                                 leaf_gain(grad, dadd(raw_hess, kEpsilon), c.lambda_l1, c.lambda_l2));
+        if (gain != gain || gain <= x.min_gain_shift) continue;
+        splittable = true;
+        if (!have || gain > bg) {
+            have = true;
+            bg = gain;
+            bt = t;
+        }
+    }
+    warp_best(have, bg, bt);
+    o.splittable = __any_sync(0xffffffffu, splittable);
+    if (have) {
+        const int2 v = hist[bt];
+        const double h = static_cast<double>(v.y);
+        o.found = 1;
+        o.kind = kCandOneHot;
+        o.best_gain = bg;
+        o.threshold = static_cast<uint32_t>(bt);
+        o.left_grad = dmul(static_cast<double>(v.x), x.gs);
+        o.left_hess = dadd(dmul(h, x.hs), kEpsilon);
+        o.left_count = bin_count(x, h);
+        o.left_units_grad = static_cast<double>(v.x);
+        o.left_units_hess = h;
+        o.cat_bins[bt >> 5] = 1u << (bt & 31);
+    }
+    o.gain = dsub(o.best_gain, x.min_gain_shift);
+    return o;
+}
+
+// find_sorted_categorical with sorted_categories and SortedScan::run (split.rs:739-845): the categories (bins 1..)
+// with at least cat_smooth estimated rows in ascending sum_g / (sum_h + cat_smooth) (total order, then the bin),
+// prefixes of up to min(max_cat_threshold, ceil(used / 2)) of them from the low end, then the high end, which
+// replaces the low end's best only when strictly better. Whole warp; `order` is kMaxBins u16 of the warp's shared
+// memory. Every lane gets the result.
+__device__ FeatureCandidate scan_sorted(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
+                                        const sb2_split_config& c, uint16_t* order) {
+    const int lane = threadIdx.x & 31;
+    const int nb = min(static_cast<int>(f.num_bins), kMaxBins);
+    const int regs = (nb + 31) / 32;
+    FeatureCandidate o{};
+    o.feature = feature;
+    // The used categories and their ctr keys: bin lane + 32 k in register k.
+    int64_t key[kPerLane];
+    bool used[kPerLane];
+    int rank[kPerLane];
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+        const int t = lane + 32 * k;
+        used[k] = false;
+        key[k] = 0;
+        rank[k] = 0;
+        if (t >= 1 && t < nb) {
+            const int2 v = hist[t];
+            const double h = static_cast<double>(v.y);
+            if (static_cast<double>(bin_count(x, h)) >= c.cat_smooth) {
+                used[k] = true;
+                key[k] = total_order_key(ddiv(dmul(static_cast<double>(v.x), x.gs), dadd(dmul(h, x.hs), c.cat_smooth)));
+            }
+        }
+    }
+    // Each used category's rank: the used categories before it in (key, bin) order.
+#pragma unroll
+    for (int sk = 0; sk < kPerLane; ++sk) {
+        if (sk >= regs) break;
+        for (int sl = 0; sl < 32; ++sl) {
+            const int64_t ok_ = shfl_i64(key[sk], sl);
+            const bool ou = __shfl_sync(0xffffffffu, used[sk], sl);
+            const int ot = sl + 32 * sk;
+#pragma unroll
+            for (int k = 0; k < kPerLane; ++k) {
+                const int t = lane + 32 * k;
+                if (ou && used[k] && (ok_ < key[k] || (ok_ == key[k] && ot < t))) ++rank[k];
+            }
+        }
+    }
+    int mine = 0;
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+        if (used[k]) order[rank[k]] = static_cast<uint16_t>(lane + 32 * k);
+        mine += used[k] ? 1 : 0;
+    }
+    __syncwarp();
+    const int n_used = __reduce_add_sync(0xffffffffu, mine);
+    const int max_num_cat = min(max(c.max_cat_threshold, 0), (n_used + 1) / 2);
+    const int steps = min(n_used, max_num_cat);
+    const double l2 = dadd(c.lambda_l2, c.cat_l2);
+    bool have = false, splittable = false;
+    double bg = 0.0;
+    int bi = 0, bdir = 0;
+    for (int dir = 0; dir < 2; ++dir) {  // 0: from the low end of the order, 1: from the high end
+        int64_t carry_g = 0, carry_h = 0, carry_c = 0, last_reset = 0;
+        bool dhave = false;
+        double dg = 0.0;
+        int di = 0;
+        for (int s0 = 0; s0 < steps; s0 += 32) {
+            const int s = s0 + lane;
+            const bool valid = s < steps;
+            int64_t g = 0, h = 0, cnt = 0;
+            if (valid) {
+                const int2 v = hist[order[dir == 0 ? s : n_used - 1 - s]];
+                g = v.x;
+                h = v.y;
+                cnt = bin_count(x, static_cast<double>(h));
+            }
+            int64_t G = g, H = h, C = cnt;  // inclusive prefix sums over the chunk's steps
+            for (int d = 1; d < 32; d <<= 1) {
+                const int64_t ug = shfl_up_i64(G, d), uh = shfl_up_i64(H, d), uc = shfl_up_i64(C, d);
+                if (lane >= d) {
+                    G += ug;
+                    H += uh;
+                    C += uc;
+                }
+            }
+            G += carry_g;
+            H += carry_h;
+            C += carry_c;
+            const double uh = static_cast<double>(H);
+            const double left_hess = dadd(kEpsilon, dmul(uh, x.hs));
+            const int64_t right_count = x.num_data - C;
+            const double right_hess = dsub(x.sum_hess, left_hess);
+            int st = valid ? side_check(x, c, C, left_hess, uh, right_count, right_hess) : 0;
+            if (st == 2 && right_count < c.min_data_per_group) st = 1;
+            const uint32_t brk = __ballot_sync(0xffffffffu, valid && st == 1);
+            const int first_break = brk ? __ffs(brk) - 1 : 32;
+            uint32_t eval = __ballot_sync(0xffffffffu, valid && st == 2);
+            if (first_break < 32) eval &= (1u << first_break) - 1u;
+            // min_data_per_group: a candidate is evaluated once the rows since the last evaluated one reach it
+            uint32_t resets = 0;
+            for (uint32_t m = eval; m != 0; m &= m - 1u) {
+                const int i = __ffs(m) - 1;
+                const int64_t ci = shfl_i64(C, i);
+                if (ci - last_reset >= c.min_data_per_group) {
+                    resets |= 1u << i;
+                    last_reset = ci;
+                }
+            }
+            bool ok = false;
+            double gain = 0.0;
+            if ((resets >> lane) & 1u) {
+                const double lg = dmul(static_cast<double>(G), x.gs);
+                gain = dadd(leaf_gain(lg, left_hess, c.lambda_l1, l2), leaf_gain(dsub(x.sum_grad, lg), right_hess, c.lambda_l1, l2));
+                ok = !(gain != gain) && gain > x.min_gain_shift;
+            }
+            splittable = splittable || __any_sync(0xffffffffu, ok);
+            bool ch = ok;
+            double cg = gain;
+            int ci = s;
+            warp_best(ch, cg, ci);
+            if (ch && (!dhave || cg > dg)) {
+                dhave = true;
+                dg = cg;
+                di = ci;
+            }
+            carry_g = shfl_i64(G, 31);
+            carry_h = shfl_i64(H, 31);
+            carry_c = shfl_i64(C, 31);
+            if (first_break < 32) break;
+        }
+        if (dhave && (!have || dg > bg)) {
+            have = true;
+            bg = dg;
+            bi = di;
+            bdir = dir;
+        }
+    }
+    o.splittable = splittable;
+    if (have) {
+        // the winner's left side: the first bi + 1 categories from its end
+        int64_t G = 0, H = 0, C = 0;
+        for (int s = lane; s <= bi; s += 32) {
+            const int2 v = hist[order[bdir == 0 ? s : n_used - 1 - s]];
+            G += v.x;
+            H += v.y;
+            C += bin_count(x, static_cast<double>(v.y));
+        }
+        for (int d = 16; d > 0; d >>= 1) {
+            G += shfl_i64(G, lane ^ d);
+            H += shfl_i64(H, lane ^ d);
+            C += shfl_i64(C, lane ^ d);
+        }
+        uint32_t bits[8] = {};
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const int t = lane + 32 * k;
+            if (used[k] && (bdir == 0 ? rank[k] <= bi : rank[k] >= n_used - 1 - bi)) bits[t >> 5] |= 1u << (t & 31);
+        }
+#pragma unroll
+        for (int w = 0; w < 8; ++w) o.cat_bins[w] = __reduce_or_sync(0xffffffffu, bits[w]);
+        o.found = 1;
+        o.kind = bdir == 0 ? kCandSortedForward : kCandSortedReverse;
+        o.best_gain = bg;
+        o.threshold = static_cast<uint32_t>(bi);
+        o.left_units_grad = static_cast<double>(G);
+        o.left_units_hess = static_cast<double>(H);
+        o.left_grad = dmul(o.left_units_grad, x.gs);
+        o.left_hess = dadd(kEpsilon, dmul(o.left_units_hess, x.hs));
+        o.left_count = C;
+    }
+    o.gain = dsub(o.best_gain, x.min_gain_shift);
+    __syncwarp();  // `order` is free again
+    return o;
+}
+
+// find_feature's categorical arms (split.rs:855-859). Whole warp.
+__device__ FeatureCandidate scan_categorical(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
+                                             const sb2_split_config& c, uint16_t* order) {
+    if (!x.valid) {
+        FeatureCandidate o{};
+        o.feature = feature;
+        return o;
+    }
+    if (static_cast<int64_t>(f.num_bins) <= c.max_cat_to_onehot) return scan_onehot(hist, f, feature, x, c);
+    return scan_sorted(hist, f, feature, x, c, order);
+}
+
+// find_feature (split.rs:848-862) for one feature: find_numerical (:584-620), or the categorical scans with
+// `order` (kMaxBins u16 of the warp's shared memory). Whole warp.
 __device__ FeatureCandidate scan_feature(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
-                                         const sb2_split_config& c) {
+                                         const sb2_split_config& c, uint16_t* order) {
+    if (f.kind == SB2_CATEGORICAL) return scan_categorical(hist, f, feature, x, c, order);
     FeatureCandidate o{};
     o.feature = feature;
     o.found = 0;
@@ -287,6 +569,7 @@ struct ScanShared {
     int32_t imin[kScanWarps];    // warp minima: the first break, then the best candidate
     double dmax[kScanWarps];     // warp maxima of the gains
     Grown best;
+    uint16_t order[kMaxBins];    // a categorical feature's sorted categories (scan_sorted)
 };
 
 __device__ __forceinline__ void group_sync(int bar) {
@@ -391,13 +674,18 @@ __device__ Grown group_scan(const int2* hist, int top, bool reverse, int m, cons
     return sh.best;
 }
 
-// scan_feature over the group (the same find_numerical, split.rs:584-620).
+// scan_feature over the group (the same find_numerical, split.rs:584-620); a categorical feature is scanned by the
+// group's first warp alone, whose lanes get the candidate.
 __device__ FeatureCandidate scan_feature_group(const int2* hist, const DevFeature& f, int feature, const Ctx& x,
                                                const sb2_split_config& c, ScanShared& sh, int bar) {
     FeatureCandidate o{};
     o.feature = feature;
     o.found = 0;
     o.splittable = 0;
+    if (f.kind == SB2_CATEGORICAL) {
+        if ((threadIdx.x % kScanThreads) < 32) o = scan_categorical(hist, f, feature, x, c, sh.order);
+        return o;
+    }
     if (!x.valid) return o;
     const int nb = static_cast<int>(f.num_bins);
     if (f.nan_bin && nb > 2) {
@@ -460,22 +748,28 @@ __device__ __forceinline__ bool better(const FeatureCandidate& a, const FeatureC
     return a.feature < b.feature;
 }
 
-// finish (split.rs:632-651)
+// finish (split.rs:632-651) through split_info (:654-691): a categorical split sends its candidate's bins left, and
+// the sorted scan's outputs take cat_l2 too.
 __device__ sb2_split_info finish(const Ctx& x, const FeatureCandidate& b, const sb2_split_config& c) {
     sb2_split_info s{};
     s.found = 1;
     s.feature = b.feature;
     s.gain = dsub(b.best_gain, x.min_gain_shift);
-    s.threshold = b.threshold;
+    s.threshold = b.kind == kCandNumerical ? b.threshold : 0u;
     s.default_left = b.default_left;
+    s.categorical = b.kind != kCandNumerical;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s.cat_bins[w] = b.cat_bins[w];
+    const double l2 = b.kind == kCandSortedForward || b.kind == kCandSortedReverse ? dadd(c.lambda_l2, c.cat_l2)
+                                                                                  : c.lambda_l2;
     s.left_grad = b.left_units_grad;
     s.left_hess = b.left_units_hess;
     s.left_count = b.left_count;
     s.right_grad = dsub(x.units_grad, b.left_units_grad);
     s.right_hess = dsub(x.units_hess, b.left_units_hess);
     s.right_count = x.num_data - b.left_count;
-    s.left_output = leaf_output(b.left_grad, b.left_hess, c.lambda_l1, c.lambda_l2);
-    s.right_output = leaf_output(dsub(x.sum_grad, b.left_grad), dsub(x.sum_hess, b.left_hess), c.lambda_l1, c.lambda_l2);
+    s.left_output = leaf_output(b.left_grad, b.left_hess, c.lambda_l1, l2);
+    s.right_output = leaf_output(dsub(x.sum_grad, b.left_grad), dsub(x.sum_hess, b.left_hess), c.lambda_l1, l2);
     return s;
 }
 
@@ -532,6 +826,11 @@ __device__ void tree_split_at(const DevTree& t, int32_t leaf, int32_t nl, const 
     }
     int8_t dt = static_cast<int8_t>((f.nan_bin ? 2 : 0) << 2);
     if (info.default_left) dt |= 2;
+    // Tree::split_categorical (tree.rs:125-141): the categorical mask and MissingType::NaN; the node keeps its left
+    // bins, and the host numbers the tree's categorical splits in node order (their thresholds)
+    if (info.categorical) dt = static_cast<int8_t>(1 | (2 << 2));
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t.cat_bins[8 * static_cast<size_t>(node) + w] = info.categorical ? info.cat_bins[w] : 0u;
     t.split_feature[node] = info.feature;
     t.split_gain[node] = static_cast<float>(dadd(info.gain, min_gain_to_split));
     t.threshold_bin[node] = info.threshold;
@@ -625,11 +924,12 @@ __device__ __forceinline__ uint32_t search_items(const TrainArgs& a, const Step&
 }
 
 // One warp, one item (child `ch`, feature `f`): the child's bins into the warp's `buf` (kMaxBins int2 of shared
-// memory), its scan into `cands[ch * F + f]`. Child 0 is the built one, straight from staging; child 1 is the
+// memory; `order`: kMaxBins u16 for a categorical feature's scan), its scan into `cands[ch * F + f]`. Child 0 is the built one, straight from staging; child 1 is the
 // sibling, parent - built (learner.rs:365-367), and its warp also writes both children's slots (it alone reads
 // the parent's slot, which the built child may take over), or, at the root, child 0's warp writes the root's slot.
 // Every lane loads its bins (lane, lane + 32, ...) before using any, so a warp waits on memory once.
-__device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t item, int2* buf) {
+__device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t item, int2* buf,
+                            uint16_t* order) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t F = a.num_features;
     const uint32_t f = item % F, ch = item / F;
@@ -688,7 +988,7 @@ __device__ void search_item(const TrainArgs& a, const Step& st, const SearchCtx&
         }
     }
     __syncwarp();
-    const FeatureCandidate c = scan_feature(buf, feat, static_cast<int>(f), s.ctx[ch], a.cfg);
+    const FeatureCandidate c = scan_feature(buf, feat, static_cast<int>(f), s.ctx[ch], a.cfg, order);
     if (lane == 0) {
         cands[static_cast<size_t>(ch) * F + f] = c;
         if (a.cand_flags) {  // what the persistent kernel's finish compares, apart from the full candidate
@@ -763,6 +1063,28 @@ __device__ void search_item_group(const TrainArgs& a, const Step& st, const Sear
     group_sync(bar);  // buf and the scratch are free for the group's next item
 }
 
+// The warp's best of its lanes' candidates by `better` (on found, gain and feature alone; the winner's full record
+// is read back from `cands`, indexed by feature). Every lane gets it.
+__device__ __forceinline__ FeatureCandidate best_of_warp(const FeatureCandidate& mine, const FeatureCandidate* cands) {
+    const uint32_t lane = threadIdx.x & 31;
+    FeatureCandidate best{};
+    best.found = mine.found;
+    best.gain = mine.gain;
+    best.feature = mine.feature;
+    for (int o = 16; o > 0; o >>= 1) {
+        FeatureCandidate other{};
+        const int src = static_cast<int>(lane) ^ o;
+        other.found = __shfl_sync(0xffffffffu, best.found, src);
+        other.gain = __shfl_sync(0xffffffffu, best.gain, src);
+        other.feature = __shfl_sync(0xffffffffu, best.feature, src);
+        if (better(other, best)) best = other;
+    }
+    if (!best.found) return best;
+    FeatureCandidate full = load_candidate(cands + best.feature);
+    full.splittable = 0;
+    return full;
+}
+
 // The best candidate of child `ch` over every feature (one warp; `better` is a total order, so the reduction order
 // does not matter), with the child's splittable flags written on the way.
 __device__ FeatureCandidate best_candidate(const TrainArgs& a, const SearchCtx& s, int ch) {
@@ -790,24 +1112,7 @@ __device__ FeatureCandidate best_candidate(const TrainArgs& a, const SearchCtx& 
             }
         }
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        FeatureCandidate other;
-        const int src = lane ^ o;
-        other.found = __shfl_sync(0xffffffffu, best.found, src);
-        other.splittable = 0;
-        other.feature = __shfl_sync(0xffffffffu, best.feature, src);
-        other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
-        other.gain = __shfl_sync(0xffffffffu, best.gain, src);
-        other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
-        other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
-        other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
-        other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
-        other.left_count = shfl_i64(best.left_count, src);
-        other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
-        other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
-        if (better(other, best)) best = other;
-    }
-    return best;
+    return best_of_warp(best, cands);
 }
 
 // (gain, leaf) of the better of two leaves in best_leaf's order (learner.rs:418-429): the higher gain, on equal
@@ -821,6 +1126,11 @@ __device__ __forceinline__ void prefer_leaf(double& gain, int32_t& leaf, double 
 
 // bin_split (learner.rs:432-452): bins 0..=threshold go left, and the NaN bin when missing values go left.
 __device__ __forceinline__ void left_bins_of(const sb2_split_info& info, const DevFeature& f, uint32_t (&bins)[8]) {
+    if (info.categorical) {  // SplitRule::Categorical: its bins
+#pragma unroll
+        for (int w = 0; w < 8; ++w) bins[w] = info.cat_bins[w];
+        return;
+    }
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
         const int64_t first = 32 * w, t = static_cast<int64_t>(info.threshold);

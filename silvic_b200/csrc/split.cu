@@ -11,6 +11,7 @@ namespace {
 // Every feature of the step's children, a warp each; the last CTA to finish applies the split and chooses the next.
 __global__ void __launch_bounds__(kSearchThreads) search_kernel(TrainArgs a) {
     __shared__ int2 sh_hist[kSearchThreads / 32][kMaxBins];
+    __shared__ uint16_t sh_order[kSearchThreads / 32][kMaxBins];
     __shared__ bool s_last;
     const Step st = *a.step;
     if (!st.active) return;
@@ -20,7 +21,7 @@ __global__ void __launch_bounds__(kSearchThreads) search_kernel(TrainArgs a) {
     if (s.searched)
         for (uint32_t item = blockIdx.x * (kSearchThreads / 32) + warp; item < search_items(a, st);
              item += gridDim.x * (kSearchThreads / 32))
-            search_item(a, st, s, item, sh_hist[warp]);
+            search_item(a, st, s, item, sh_hist[warp], sh_order[warp]);
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) s_last = atomicAdd(a.done_counter, 1u) == gridDim.x - 1;
@@ -50,6 +51,7 @@ __global__ void __launch_bounds__(kSearchThreads) api_find_split_kernel(DevData 
                                                                         unsigned int* counter, sb2_split_info* out,
                                                                         uint8_t* splittable) {
     __shared__ int2 sh_hist[kSearchThreads / 32][kMaxBins];
+    __shared__ uint16_t sh_order[kSearchThreads / 32][kMaxBins];
     __shared__ bool s_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t F = d.num_features;
@@ -62,7 +64,7 @@ __global__ void __launch_bounds__(kSearchThreads) api_find_split_kernel(DevData 
             for (uint32_t b = lane; b < feat.num_bins; b += 32)
                 sh_hist[warp][b] = make_int2(hist[2 * (feat.hist_offset + b)], hist[2 * (feat.hist_offset + b) + 1]);
             __syncwarp();
-            c = scan_feature(sh_hist[warp], feat, static_cast<int>(f), x, cfg);
+            c = scan_feature(sh_hist[warp], feat, static_cast<int>(f), x, cfg, sh_order[warp]);
             __syncwarp();
         }
         if (lane == 0) cands[f] = c;
@@ -79,22 +81,7 @@ __global__ void __launch_bounds__(kSearchThreads) api_find_split_kernel(DevData 
         splittable[f] = static_cast<uint8_t>(c.splittable);
         if (better(c, best)) best = c;
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        FeatureCandidate other{};
-        const int src = lane ^ o;
-        other.found = __shfl_sync(0xffffffffu, best.found, src);
-        other.feature = __shfl_sync(0xffffffffu, best.feature, src);
-        other.default_left = __shfl_sync(0xffffffffu, best.default_left, src);
-        other.gain = __shfl_sync(0xffffffffu, best.gain, src);
-        other.best_gain = __shfl_sync(0xffffffffu, best.best_gain, src);
-        other.threshold = __shfl_sync(0xffffffffu, best.threshold, src);
-        other.left_grad = __shfl_sync(0xffffffffu, best.left_grad, src);
-        other.left_hess = __shfl_sync(0xffffffffu, best.left_hess, src);
-        other.left_count = shfl_i64(best.left_count, src);
-        other.left_units_grad = __shfl_sync(0xffffffffu, best.left_units_grad, src);
-        other.left_units_hess = __shfl_sync(0xffffffffu, best.left_units_hess, src);
-        if (better(other, best)) best = other;
-    }
+    best = best_of_warp(best, cands);
     if (lane == 0) {
         *counter = 0;
         sb2_split_info s{};

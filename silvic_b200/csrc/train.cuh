@@ -66,6 +66,7 @@ struct DevTree {
     int64_t* leaf_count;
     int32_t* leaf_parent;
     int32_t* leaf_depth;
+    uint32_t* cat_bins;         // 8 words per node: a categorical split's left bins (0 for a numerical one)
 };
 
 // Iteration state (boosting.rs:227-285).
@@ -136,7 +137,13 @@ struct FeatureCandidate {
     double left_grad, left_hess;  // real sums as LightGBM keeps them (split.rs:300-307)
     int64_t left_count;
     double left_units_grad, left_units_hess;
+    int32_t kind;                 // CandidateKind (split.rs:318-327): numerical, one-hot, sorted from either end
+    int32_t pad2_;
+    uint32_t cat_bins[8];         // a categorical candidate's left bins
 };
+
+// FeatureCandidate::kind
+enum : int32_t { kCandNumerical = 0, kCandOneHot = 1, kCandSortedForward = 2, kCandSortedReverse = 3 };
 
 static_assert(sizeof(FeatureCandidate) % 8 == 0, "candidates are copied as 64-bit words");
 

@@ -26,6 +26,7 @@ class FeatureMeta:
     num_bins: int = 0          # NaN bin included; 0 for a trivial feature
     nan_bin: bool = False
     upper_bounds: np.ndarray | None = None  # ascending, the last +inf
+    categories: list[int] | None = None     # categorical: categories[b - 1] is bin b's value; bin 0 is "other"
     min_value: float = 0.0
     max_value: float = 0.0
     group: int = 0
@@ -75,7 +76,8 @@ class BinnedDataset:
         offset = 0
         for index, m in enumerate(mappers):
             meta = FeatureMeta(name=m.name, kind=m.kind, num_bins=m.num_bins, nan_bin=m.nan_bin,
-                               upper_bounds=m.upper_bounds, min_value=m.min_value, max_value=m.max_value)
+                               upper_bounds=m.upper_bounds, categories=m.categories, min_value=m.min_value,
+                               max_value=m.max_value)
             if meta.num_bins == 0:
                 meta.group, meta.column, meta.hist_offset = 0, 0, offset
                 features.append(meta)
@@ -177,3 +179,10 @@ def numerical_mapper(name: str, num_bins: int, nan_bin: bool = False) -> Feature
     ub[-1] = np.inf
     return FeatureMeta(name=name, num_bins=num_bins, nan_bin=nan_bin, upper_bounds=ub, min_value=0.0,
                        max_value=float(numeric))
+
+
+def categorical_mapper(name: str, categories: list[int]) -> FeatureMeta:
+    """A categorical mapper (bin_mapper.rs:36-39): bin b >= 1 holds category categories[b - 1], bin 0 every
+    negative, NaN or unseen value."""
+    return FeatureMeta(name=name, kind=_abi.CATEGORICAL, num_bins=len(categories) + 1,
+                       categories=[int(c) for c in categories])

@@ -400,9 +400,8 @@ def _parse_tree(fields, num_features: int) -> TextTree:
 
 def model_parameters(params: _abi.Params) -> list:
     """`Params::model_parameters` (config.rs:444-498) for the parameters a device-trained model carries (lambdarank's
-    three after the quantization ones, config.rs:486-493); the
-    binning and categorical parameters the device trainer does not take keep the reference's defaults
-    (config.rs:123-167)."""
+    three after the quantization ones, config.rs:486-493); the binning parameters the device trainer does not take
+    keep the reference's defaults (config.rs:123-167)."""
     objective = {_abi.REGRESSION: "regression", _abi.BINARY: "binary"}.get(params.objective, "lambdarank")
     g = format_g
     out = [("boosting", "gbdt"), ("objective", objective), ("num_iterations", str(params.num_iterations)),
@@ -413,7 +412,8 @@ def model_parameters(params: _abi.Params) -> list:
            ("bagging_seed", str(params.bagging_seed)), ("feature_fraction", g(params.feature_fraction)),
            ("feature_fraction_seed", str(params.feature_fraction_seed)), ("lambda_l1", g(params.lambda_l1)),
            ("lambda_l2", g(params.lambda_l2)), ("min_gain_to_split", g(params.min_gain_to_split)),
-           ("max_cat_threshold", "32"), ("cat_l2", g(10.0)), ("cat_smooth", g(10.0)), ("max_cat_to_onehot", "4"),
+           ("max_cat_threshold", str(params.max_cat_threshold)), ("cat_l2", g(params.cat_l2)),
+           ("cat_smooth", g(params.cat_smooth)), ("max_cat_to_onehot", str(params.max_cat_to_onehot)),
            ("max_bin", "255"), ("min_data_in_bin", "3"), ("bin_construct_sample_cnt", "200000"),
            ("data_random_seed", "1"), ("boost_from_average", str(int(bool(params.boost_from_average)))),
            ("use_quantized_grad", str(int(bool(params.use_quantized_grad)))),
@@ -434,10 +434,39 @@ def model_parameters(params: _abi.Params) -> list:
 
 
 def feature_info(meta) -> str:
-    """`BinMapper::info_string` (bin_mapper.rs:362-377) of a numerical or trivial feature."""
+    """`BinMapper::info_string` (bin_mapper.rs:362-377): `[min:max]`, `-1:c1:c2:...` (the "other" bin listed as
+    category -1) or `none`."""
     if meta.is_trivial:
         return "none"
+    if meta.kind == _abi.CATEGORICAL:
+        return ":".join(["-1"] + [str(int(c)) for c in meta.categories])
     return f"[{format_g17(meta.min_value)}:{format_g17(meta.max_value)}]"
+
+
+def to_bitset(values) -> list[int]:
+    """`to_bitset` (tree.rs:230-237): the non-negative values as bits of u32 words, max / 32 + 1 words."""
+    vals = [int(v) for v in values if int(v) >= 0]
+    words = [0] * (max(vals, default=0) // 32 + 1)
+    for v in vals:
+        words[v // 32] |= 1 << (v % 32)
+    return words
+
+
+def _categorical_splits(tr, n: int, dataset):
+    """A trained tree's categorical splits as LightGBM writes them (Tree::split_categorical, tree.rs:125-141): per
+    categorical node in node order, the bitset of the categories of the bins it sends left, and the boundaries."""
+    boundaries, words = [0], []
+    for k in range(n):
+        if not int(tr.decision_type[k]) & CATEGORICAL_MASK:
+            continue
+        meta = dataset.features[int(tr.split_feature[k])]
+        bins = [b for b in range(1, meta.num_bins) if (int(tr.cat_bins[k][b // 32]) >> (b % 32)) & 1]
+        bits = to_bitset(meta.categories[b - 1] for b in bins)
+        if float(tr.threshold[k]) != len(boundaries) - 1:
+            raise ModelFormatError(f"categorical node {k} has index {tr.threshold[k]}, not {len(boundaries) - 1}")
+        words += bits
+        boundaries.append(boundaries[-1] + len(bits))
+    return len(boundaries) - 1, boundaries, words
 
 
 def from_trained(model, dataset, params: _abi.Params) -> TextModel:
@@ -448,14 +477,16 @@ def from_trained(model, dataset, params: _abi.Params) -> TextModel:
     trees = []
     for tr in model.trees:
         n = max(tr.num_leaves - 1, 0)
+        num_cat, boundaries, words = _categorical_splits(tr, n, dataset)
         trees.append(TextTree(
-            num_leaves=tr.num_leaves, num_cat=0, split_feature=[int(v) for v in tr.split_feature[:n]],
+            num_leaves=tr.num_leaves, num_cat=num_cat, split_feature=[int(v) for v in tr.split_feature[:n]],
             split_gain=[float(v) for v in tr.split_gain[:n]], threshold=[float(v) for v in tr.threshold[:n]],
             decision_type=[int(v) for v in tr.decision_type[:n]], left_child=[int(v) for v in tr.left_child[:n]],
             right_child=[int(v) for v in tr.right_child[:n]], leaf_value=[float(v) for v in tr.leaf_value],
             leaf_weight=[float(v) for v in tr.leaf_weight], leaf_count=[int(v) for v in tr.leaf_count],
             internal_value=[float(v) for v in tr.internal_value[:n]],
             internal_weight=[float(v) for v in tr.internal_weight[:n]],
-            internal_count=[int(v) for v in tr.internal_count[:n]], shrinkage=float(tr.shrinkage)))
+            internal_count=[int(v) for v in tr.internal_count[:n]], shrinkage=float(tr.shrinkage),
+            cat_boundaries=boundaries if num_cat else [], cat_threshold=words))
     return TextModel(objective, [m.name for m in dataset.features], [feature_info(m) for m in dataset.features],
                      trees, sigmoid=float(params.sigmoid), parameters=model_parameters(params))

@@ -315,7 +315,9 @@ def default_params(**overrides) -> _abi.Params:
                     min_gain_to_split=0.0, bagging_fraction=1.0, bagging_freq=0, bagging_seed=3,
                     feature_fraction=1.0, feature_fraction_seed=2, data_random_seed=1, boost_from_average=1,
                     use_quantized_grad=1, sigmoid=1.0, num_grad_quant_bins=4, quant_train_renew_leaf=1,
-                    stochastic_rounding=1, lambdarank_norm=1, lambdarank_truncation_level=30)
+                    stochastic_rounding=1, lambdarank_norm=1, lambdarank_truncation_level=30,
+                    max_cat_to_onehot=4, max_cat_threshold=32, cat_l2=10.0, cat_smooth=10.0,
+                    min_data_per_group=100)
     defaults.update(overrides)
     for k, v in defaults.items():
         setattr(p, k, v)

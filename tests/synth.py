@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from silvic_b200.dataset import BinnedDataset, numerical_mapper
+from silvic_b200.dataset import BinnedDataset, categorical_mapper, numerical_mapper
 
 
 def mix32(x: np.ndarray) -> np.ndarray:
@@ -91,3 +91,23 @@ def ranking_binned(rows: int, bins_per_feature: list[int], seed: int = 1, mean_q
     data.label = label
     data.query_boundaries = qb
     return data
+
+
+def categorical_binned(rows: int, seed: int = 9, label_kind: str = "regression") -> BinnedDataset:
+    """Two categorical features (3 bins: one-hot; 40 bins: sorted) whose categories carry the label, beside four
+    63-bin numerical ones; bin 0 ("other") holds a tenth of the rows."""
+    r = np.arange(rows, dtype=np.uint64)
+    cats = [[7, 3], list(range(100, 139))]
+    bins = np.zeros((rows, 6), dtype=np.uint8)
+    for f, cs in enumerate(cats):
+        u = unit(seed * 1000 + f, r)
+        bins[:, f] = np.where(unit(seed * 1000 + 50 + f, r) < 0.1, 0, 1 + (u * len(cs)).astype(np.int64))
+    for f in range(2, 6):
+        bins[:, f] = np.minimum((unit(seed * 1000 + f, r) * 63).astype(np.int64), 62)
+    effect = np.sin(np.arange(40) * 1.7) * 2.0
+    signal = effect[bins[:, 1]] + 1.5 * (bins[:, 0] == 2) + bins[:, 2] / 62.0
+    noise = unit(seed * 1000 + 999, r) - 0.5
+    label = ((signal + noise) > 0.5).astype(np.float32) if label_kind == "binary" else (signal + 0.3 * noise)
+    mappers = [categorical_mapper(f"c{f}", cs) for f, cs in enumerate(cats)]
+    mappers += [numerical_mapper(f"n{f}", 63) for f in range(2, 6)]
+    return BinnedDataset.from_bins(bins, mappers, label.astype(np.float32))

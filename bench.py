@@ -295,30 +295,20 @@ def bin_mappers(device):
     return out
 
 
-def dataset_layout(mappers):
-    """silvic's group layout of the config's features (data/build.rs:336-382): features in order, a new group
-    when the next feature's bins would take the group past 8192."""
-    from silvic_b200.dataset import FeatureGroup, FeatureMeta
+def feature_metas(mappers):
+    """The config's numerical mappers ((upper bounds, min, max) per feature) as FeatureMeta, named as LightGBM names
+    unnamed columns."""
+    from silvic_b200.dataset import FeatureMeta
 
-    features, groups, members, offset, group_bins = [], [], [], 0, 0
-    for f, (ub, lo, hi) in enumerate(mappers):
-        nb = len(ub)
-        if members and group_bins + nb > 8192:
-            groups.append(members)
-            members, group_bins = [], 0
-        features.append(FeatureMeta(name=f"Column_{f}", num_bins=nb, upper_bounds=ub, min_value=lo, max_value=hi,
-                                    group=len(groups), column=len(members), hist_offset=offset))
-        members.append(f)
-        group_bins += nb
-        offset += nb
-    if members:
-        groups.append(members)
-    out = []
-    for gi, feats in enumerate(groups):
-        hist_offset = features[feats[0]].hist_offset
-        total = sum(features[f].num_bins for f in feats)
-        out.append(FeatureGroup(feats, (len(feats) + 3) // 4 * 4, hist_offset, total, np.zeros((0, 4), np.uint8)))
-    return features, out, offset
+    return [FeatureMeta(name=f"Column_{f}", num_bins=len(ub), upper_bounds=ub, min_value=lo, max_value=hi)
+            for f, (ub, lo, hi) in enumerate(mappers)]
+
+
+def dataset_layout(mappers):
+    """silvic's group layout of the config's features (silvic_b200.dataset.layout, data/build.rs:336-382)."""
+    from silvic_b200.dataset import layout
+
+    return layout(feature_metas(mappers))
 
 
 def build_dataset(begin: int, end: int, device, chunk: int = 2_000_000):
@@ -342,28 +332,33 @@ def build_dataset(begin: int, end: int, device, chunk: int = 2_000_000):
         from silvic_b200 import B200Backend
 
         binner = B200Backend(device.index or 0)
-    try:
+    def chunks():
+        # the chunk's raw features made on the device, its labels into the label array on the way
         for lo in range(0, n, chunk):
             hi = min(n, lo + chunk)
             rows = torch.arange(begin + lo, begin + hi, dtype=torch.int64, device=device)
-            x = features_of(rows, device)
             label[lo:hi] = labels_of(rows).cpu().numpy()
-            if binner is not None:
-                binner.bin_dense(x, features, shells, out=[h[lo:hi] for h in host])
-            else:
+            yield lo, features_of(rows, device)
+
+    try:
+        if binner is not None:
+            # streaming construction through the product: each chunk binned on the device into the pinned rows
+            data = BinnedDataset.from_chunks(chunks(), n, feature_metas(mappers), label, binner, row_offset=begin,
+                                             out=host)
+        else:
+            for lo, x in chunks():
                 for gi, g in enumerate(shells):
-                    blk = torch.zeros((hi - lo, g.row_stride), dtype=torch.uint8)
+                    blk = torch.zeros((x.shape[0], g.row_stride), dtype=torch.uint8)
                     for col, f in enumerate(g.features):
                         ub = torch.from_numpy(features[f].upper_bounds).to(torch.float64)
                         blk[:, col] = torch.bucketize(x[:, f].double(), ub, right=False).to(torch.uint8)
-                    host[gi][lo:hi] = blk.numpy()
-            del x
+                    host[gi][lo:lo + x.shape[0]] = blk.numpy()
+            groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, host[gi])
+                      for gi, g in enumerate(shells)]
+            data = BinnedDataset(n, begin, features, groups, total_bins, label)
     finally:
         if binner is not None:
             binner.close()
-    groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, host[gi])
-              for gi, g in enumerate(shells)]
-    data = BinnedDataset(n, begin, features, groups, total_bins, label)
     if CFG.objective == "lambdarank":
         qb = query_boundaries()
         lo, hi = np.searchsorted(qb, [begin, end])

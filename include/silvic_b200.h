@@ -56,6 +56,10 @@ typedef struct sb2_feature {
     uint32_t num_upper_bounds;
     uint32_t pad_;
     double min_value, max_value; /* sampled min and max (feature_infos) */
+    const int32_t* categories;   /* categorical: categories[b - 1] is bin b's category (bin 0: every other value);
+                                    read by sb2_bin_dense only */
+    uint32_t num_categories;     /* num_bins - 1 */
+    uint32_t pad2_;
 } sb2_feature;
 
 /* FeatureGroup (crates/silvic-core/src/data/mod.rs:49-59): row-major bins, data[row * row_stride + column]. */
@@ -368,12 +372,15 @@ int sb2_profile_steps(sb2_backend* b, const sb2_params* params, double init_scor
 
 /* data::binning::bin_rows (crates/silvic-core/src/data/binning.rs:71-135) on the handle's device: the values of a
  * rows × cols matrix (`row_major`: values[row * cols + feature], else values[feature * rows + row]), f32
- * (`value_bytes` 4) or f64 (8), in host or device memory, are binned with each numerical feature's upper bounds
- * (BinMapper::value_to_bin, data/bin_mapper.rs:343-360: the number of bounds below the value; NaN to the NaN bin,
- * or to 0.0's bin) into the groups' rows. The matrix column of feature f is f. `group_data[g]` is a host buffer of
- * rows × groups[g].row_stride bytes that receives group g's rows (padding columns 0); `features` and `groups` are
- * as in sb2_dataset (each group's features, columns and row stride; `data` unused). A categorical feature in a
- * group returns SB2_EUNSUPPORTED; a group whose bounds exceed 200 KiB, SB2_EUNSUPPORTED. Returns when done. */
+ * (`value_bytes` 4) or f64 (8), in host or device memory, are binned into the groups' rows by each feature's mapper
+ * (BinMapper::value_to_bin, data/bin_mapper.rs:343-392): a numerical feature's bin is the number of its upper
+ * bounds below the value (NaN to the NaN bin, or to 0.0's bin); a categorical feature's is the bin of the value's
+ * category (the value truncated to i32), 0 for NaN, negative and unlisted values. The matrix column of feature f is
+ * f. `group_data[g]` is a buffer of rows × groups[g].row_stride bytes in host memory that receives group g's rows
+ * (padding columns 0); `features` and `groups` are as in sb2_dataset (each group's features, columns and row
+ * stride; `data` unused). Building a large dataset in chunks of rows: call once per chunk, with the chunk's values
+ * and each group_data[g] advanced by the chunk's first row × row_stride. A group whose bounds and categories
+ * exceed 200 KiB returns SB2_EUNSUPPORTED. Returns when done. */
 int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
                   const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
                   uint8_t* const* group_data);

@@ -1848,6 +1848,19 @@ uint8_t padded_numerical_bin(const double (&bounds)[256], uint8_t nan, double va
     return static_cast<uint8_t>(pos);
 }
 
+// categorical_bin (data/bin_mapper.rs:379-391): the value truncates to i32 (Rust's saturating `as`); NaN, negative
+// and unlisted values are bin 0, category categories[i] is bin i + 1.
+uint8_t categorical_bin(const int32_t* categories, uint32_t n, double value) {
+    if (value != value) return 0;
+    const int32_t category = value >= 2147483647.0    ? 2147483647
+                             : value <= -2147483648.0 ? static_cast<int32_t>(-2147483647 - 1)
+                                                      : static_cast<int32_t>(value);
+    if (category < 0) return 0;
+    for (uint32_t i = 0; i < n; ++i)
+        if (categories[i] == category) return static_cast<uint8_t>(i + 1);
+    return 0;
+}
+
 }  // namespace
 
 // data/binning.rs:71-135 (bin_rows / bin_column / fill), one row chunk after another.
@@ -1862,6 +1875,16 @@ int orc_bin_rows(const void* values, int value_bytes, uint64_t rows, uint32_t co
             const uint32_t f = grp.features[k];
             if (f >= num_features || f >= cols) return SB2_EDATA;
             const sb2_feature& m = features[f];
+            if (m.kind == SB2_CATEGORICAL) {
+                if (!m.categories || m.num_categories == 0 || m.num_categories > 255) return SB2_EDATA;
+                for (uint64_t r = 0; r < rows; ++r) {
+                    const uint64_t at = row_major ? r * cols + f : static_cast<uint64_t>(f) * rows + r;
+                    const double v = value_bytes == 8 ? static_cast<const double*>(values)[at]
+                                                      : static_cast<double>(static_cast<const float*>(values)[at]);
+                    group_data[g][r * grp.row_stride + m.column] = categorical_bin(m.categories, m.num_categories, v);
+                }
+                continue;
+            }
             if (m.kind != SB2_NUMERICAL) return SB2_EUNSUPPORTED;
             if (m.num_upper_bounds == 0 || m.num_upper_bounds > 256) return SB2_EDATA;
             double bounds[256];

@@ -41,6 +41,9 @@ class Feature(C.Structure):
         ("pad_", C.c_uint32),
         ("min_value", C.c_double),
         ("max_value", C.c_double),
+        ("categories", C.POINTER(C.c_int32)),
+        ("num_categories", C.c_uint32),
+        ("pad2_", C.c_uint32),
     ]
 
 

@@ -2045,7 +2045,7 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
         const sb2_group& grp = groups[g];
         if (!group_data[g]) return b->fail(SB2_EDATA, "group " + std::to_string(g) + " has no output buffer");
         std::vector<uint32_t> feat, column, off{0};
-        std::vector<uint8_t> nan;
+        std::vector<uint8_t> nan, categorical;
         std::vector<double> bounds;
         for (uint32_t k = 0; k < grp.num_features; ++k) {
             const uint32_t f = grp.features[k];
@@ -2053,32 +2053,50 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
                 return b->fail(SB2_EDATA, "group " + std::to_string(g) + " names feature " + std::to_string(f) +
                                               " beyond the matrix's columns");
             const sb2_feature& m = features[f];
-            if (m.kind == SB2_CATEGORICAL)
-                return b->fail(SB2_EUNSUPPORTED, "categorical feature " + std::to_string(f) + ": the device binning is numerical only");
-            if (m.kind != SB2_NUMERICAL || !m.upper_bounds || m.num_upper_bounds == 0 || m.num_upper_bounds > 256)
-                return b->fail(SB2_EDATA, "grouped feature " + std::to_string(f) + " without 1..256 upper bounds");
             if (m.column >= grp.row_stride)
                 return b->fail(SB2_EDATA, "feature " + std::to_string(f) + "'s column lies outside its group's rows");
             feat.push_back(f);
             column.push_back(m.column);
+            if (m.kind == SB2_CATEGORICAL) {
+                // categorical_bin (data/bin_mapper.rs:379-391): the categories ascending, then their bins
+                if (!m.categories || m.num_categories == 0 || m.num_categories > 255 || m.num_bins != m.num_categories + 1)
+                    return b->fail(SB2_EDATA, "categorical feature " + std::to_string(f) + " without 1..255 categories");
+                std::vector<std::pair<int32_t, uint32_t>> sorted;
+                for (uint32_t c = 0; c < m.num_categories; ++c) sorted.emplace_back(m.categories[c], c + 1);
+                std::sort(sorted.begin(), sorted.end());
+                for (size_t c = 1; c < sorted.size(); ++c)
+                    if (sorted[c].first == sorted[c - 1].first)
+                        return b->fail(SB2_EDATA, "categorical feature " + std::to_string(f) + " lists category " +
+                                                      std::to_string(sorted[c].first) + " twice");
+                for (const auto& e : sorted) bounds.push_back(static_cast<double>(e.first));
+                for (const auto& e : sorted) bounds.push_back(static_cast<double>(e.second));
+                off.push_back(static_cast<uint32_t>(bounds.size()));
+                nan.push_back(0);
+                categorical.push_back(1);
+                continue;
+            }
+            if (m.kind != SB2_NUMERICAL || !m.upper_bounds || m.num_upper_bounds == 0 || m.num_upper_bounds > 256)
+                return b->fail(SB2_EDATA, "grouped feature " + std::to_string(f) + " without 1..256 upper bounds");
             bounds.insert(bounds.end(), m.upper_bounds, m.upper_bounds + m.num_upper_bounds);
             off.push_back(static_cast<uint32_t>(bounds.size()));
             // value_to_bin(NaN) (bin_mapper.rs:347-352): the NaN bin, or the bin of 0.0
             uint32_t zero = 0;
             while (zero < m.num_upper_bounds && m.upper_bounds[zero] < 0.0) ++zero;
             nan.push_back(static_cast<uint8_t>(m.nan_bin ? m.num_upper_bounds : zero));
+            categorical.push_back(0);
         }
         GroupPlan& p = plans[g];
         p.nf = static_cast<uint32_t>(feat.size());
         p.total = static_cast<uint32_t>(bounds.size());
         if (sizeof(double) * p.total > 200 * 1024)
-            return b->fail(SB2_EUNSUPPORTED, "group " + std::to_string(g) + " has more bounds than shared memory holds");
-        // meta: feature [nf], column [nf], bound_off [nf + 1], nan [nf] (bytes)
-        std::vector<uint8_t> meta(4 * (3 * p.nf + 1) + p.nf);
+            return b->fail(SB2_EUNSUPPORTED, "group " + std::to_string(g) + " has more bounds and categories than shared memory holds");
+        // meta: feature [nf], column [nf], bound_off [nf + 1], nan [nf] (bytes), categorical [nf] (bytes)
+        std::vector<uint8_t> meta(4 * (3 * p.nf + 1) + 2 * p.nf);
         std::memcpy(meta.data(), feat.data(), 4 * p.nf);
         std::memcpy(meta.data() + 4 * p.nf, column.data(), 4 * p.nf);
         std::memcpy(meta.data() + 8 * p.nf, off.data(), 4 * (p.nf + 1));
         std::memcpy(meta.data() + 4 * (3 * p.nf + 1), nan.data(), p.nf);
+        std::memcpy(meta.data() + 4 * (3 * p.nf + 1) + p.nf, categorical.data(), p.nf);
         SB2_CUDA(b, p.meta.alloc(meta.size()));
         SB2_CUDA(b, p.bounds.alloc(sizeof(double) * std::max<uint32_t>(p.total, 1)));
         SB2_CUDA(b, cudaMemcpyAsync(p.meta.ptr, meta.data(), meta.size(), cudaMemcpyHostToDevice, b->stream));
@@ -2134,6 +2152,7 @@ int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t 
             a.column = reinterpret_cast<const uint32_t*>(meta + 4 * p.nf);
             a.bound_off = reinterpret_cast<const uint32_t*>(meta + 8 * p.nf);
             a.nan_bin = meta + 4 * (3 * p.nf + 1);
+            a.categorical = meta + 4 * (3 * p.nf + 1) + p.nf;
             a.bounds = p.bounds.as<double>();
             a.total_bounds = p.total;
             a.stride = stride;

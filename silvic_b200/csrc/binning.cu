@@ -9,7 +9,8 @@
 // column-major: consecutive row quads of a feature. A value's bin is the number of upper bounds below it
 // (`partition_point(bound < value)`; the last bound is +inf), found by binary lifting over the feature's own
 // bounds: the same count as the reference's branch-free search over bounds padded to 256 with +inf
-// (binning.rs:51-61). NaN goes to the NaN bin, or to zero's bin when the feature has none.
+// (binning.rs:51-61). NaN goes to the NaN bin, or to zero's bin when the feature has none. A categorical feature's
+// categories, ascending with their bins, take the bounds' place.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -25,6 +26,14 @@ constexpr uint32_t kTileRows = 128;
 constexpr int kBinThreads = 256;
 
 constexpr uint32_t kQuad = 4;  // rows of one feature a thread bins at once: four searches in flight
+
+// Rust's `f64 as i32`: toward zero, saturating at the i32 range, NaN to 0.
+__device__ __forceinline__ int32_t rust_f64_to_i32(double v) {
+    if (v != v) return 0;
+    if (v >= 2147483647.0) return 2147483647;
+    if (v <= -2147483648.0) return static_cast<int32_t>(0x80000000u);
+    return static_cast<int32_t>(v);
+}
 
 __global__ void __launch_bounds__(kBinThreads) bin_group_kernel(BinGroupArgs a) {
     extern __shared__ double bounds[];  // the group's features' bounds, back to back (a.bound_off)
@@ -54,20 +63,32 @@ __global__ void __launch_bounds__(kBinThreads) bin_group_kernel(BinGroupArgs a) 
                 }
             }
             // The number of bounds below each value, by binary lifting over the feature's n bounds (the count is
-            // built from the powers of two at or below n, largest first).
-            const uint32_t off = a.bound_off[k], n = a.bound_off[k + 1] - off;
+            // built from the powers of two at or below n, largest first). A categorical feature searches its
+            // ascending categories for the value truncated to i32 the same way (categorical_bin,
+            // data/bin_mapper.rs:379-391: NaN and negative values are bin 0, so is a category it does not list).
+            const bool cat = a.categorical[k] != 0;
+            const uint32_t off = a.bound_off[k], n = (a.bound_off[k + 1] - off) >> (cat ? 1 : 0);
             const double* b = bounds + off;
+            double key[kQuad];
+#pragma unroll
+            for (uint32_t i = 0; i < kQuad; ++i) key[i] = cat ? static_cast<double>(rust_f64_to_i32(v[i])) : v[i];
             uint32_t pos[kQuad] = {0, 0, 0, 0};
             for (uint32_t step = n ? 1u << (31 - __clz(n)) : 0u; step; step >>= 1) {
 #pragma unroll
                 for (uint32_t i = 0; i < kQuad; ++i)
-                    if (pos[i] + step <= n && b[pos[i] + step - 1] < v[i]) pos[i] += step;
+                    if (pos[i] + step <= n && b[pos[i] + step - 1] < key[i]) pos[i] += step;
             }
 #pragma unroll
             for (uint32_t i = 0; i < kQuad; ++i) {
                 const uint64_t row = row0 + i;
                 if (row >= a.chunk_rows) break;
-                const uint32_t bin = v[i] != v[i] ? a.nan_bin[k] : pos[i];
+                uint32_t bin;
+                if (cat)
+                    bin = v[i] != v[i] || key[i] < 0.0 || pos[i] >= n || b[pos[i]] != key[i]
+                              ? 0u
+                              : static_cast<uint32_t>(b[n + pos[i]]);
+                else
+                    bin = v[i] != v[i] ? a.nan_bin[k] : pos[i];
                 a.out[row * a.stride + a.column[k]] = static_cast<uint8_t>(bin);
             }
         }

@@ -21,7 +21,9 @@ struct BinGroupArgs {
     const uint32_t* column;     // [num_features]: byte column in the group's row
     const uint32_t* bound_off;  // [num_features + 1]: each feature's bounds in `bounds`
     const uint8_t* nan_bin;     // [num_features]: the bin of NaN
-    const double* bounds;       // the features' upper bounds, back to back
+    const uint8_t* categorical; // [num_features]: 1 for a categorical feature, whose `bounds` hold its n categories
+                                // ascending, then their n bins (2 n entries)
+    const double* bounds;       // the features' upper bounds (or categories and bins), back to back
     uint32_t total_bounds;
     uint32_t stride;            // the group's row stride
     uint8_t* out;               // the chunk's rows of the group: chunk_rows × stride bytes

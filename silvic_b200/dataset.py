@@ -71,37 +71,42 @@ class BinnedDataset:
         bins = np.asarray(bins, dtype=np.uint8)
         rows, nf = bins.shape
         assert nf == len(mappers)
-        features: list[FeatureMeta] = []
-        groups: list[dict] = []
-        offset = 0
-        for index, m in enumerate(mappers):
-            meta = FeatureMeta(name=m.name, kind=m.kind, num_bins=m.num_bins, nan_bin=m.nan_bin,
-                               upper_bounds=m.upper_bounds, categories=m.categories, min_value=m.min_value,
-                               max_value=m.max_value)
-            if meta.num_bins == 0:
-                meta.group, meta.column, meta.hist_offset = 0, 0, offset
-                features.append(meta)
-                continue
-            if not groups or groups[-1]["total_bins"] + meta.num_bins > GROUP_BIN_BUDGET:
-                groups.append({"features": [], "hist_offset": offset, "total_bins": 0})
-            g = groups[-1]
-            meta.group = len(groups) - 1
-            meta.column = len(g["features"])
-            meta.hist_offset = offset
-            g["features"].append(index)
-            g["total_bins"] += meta.num_bins
-            offset += meta.num_bins
-            features.append(meta)
+        features, shells, total_bins = layout(mappers)
         out_groups = []
-        for g in groups:
-            stride = (len(g["features"]) + 3) // 4 * 4
-            data = np.zeros((rows, stride), dtype=np.uint8)
-            data[:, : len(g["features"])] = bins[:, g["features"]]
-            out_groups.append(FeatureGroup(g["features"], stride, g["hist_offset"], g["total_bins"], data))
+        for g in shells:
+            data = np.zeros((rows, g.row_stride), dtype=np.uint8)
+            data[:, : len(g.features)] = bins[:, g.features]
+            out_groups.append(FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, data))
         label = np.ascontiguousarray(label, dtype=np.float32)
         weight = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
         qb = None if query_boundaries is None else np.ascontiguousarray(query_boundaries, dtype=np.uint32)
-        return BinnedDataset(rows, row_offset, features, out_groups, offset, label, weight, qb)
+        return BinnedDataset(rows, row_offset, features, out_groups, total_bins, label, weight, qb)
+
+    @staticmethod
+    def from_chunks(chunks, rows: int, mappers: list[FeatureMeta], label: np.ndarray, binner, *, weight=None,
+                    row_offset: int = 0, query_boundaries=None, out: list[np.ndarray] | None = None) -> "BinnedDataset":
+        """Streaming construction (BinnedDataset::construct's bin_rows, data/build.rs:81-126 and
+        data/binning.rs:71-135, with the mappers given): `chunks` yields (first row, values) for consecutive row
+        ranges covering 0 .. rows, each values a chunk × features matrix (numpy, or a CUDA tensor made on the
+        device); `binner` (a B200Backend) bins each into its rows of the groups, so the raw matrix never exists
+        whole. `out` (optional, e.g. page-locked) receives the groups' rows: C-contiguous uint8 arrays of rows ×
+        row_stride per group of layout(mappers)."""
+        features, shells, total_bins = layout(mappers)
+        data = out if out is not None else [np.zeros((rows, g.row_stride), dtype=np.uint8) for g in shells]
+        done = 0
+        for first, values in chunks:
+            n = int(values.shape[0])
+            if first != done or first + n > rows:
+                raise ValueError(f"chunk of rows {first}..{first + n}: expected it to start at {done} and end by {rows}")
+            binner.bin_dense(values, features, shells, out=[d[first:first + n] for d in data])
+            done += n
+        if done != rows:
+            raise ValueError(f"the chunks covered {done} of {rows} rows")
+        groups = [FeatureGroup(g.features, g.row_stride, g.hist_offset, g.total_bins, d) for g, d in zip(shells, data)]
+        label = np.ascontiguousarray(label, dtype=np.float32)
+        weight = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+        qb = None if query_boundaries is None else np.ascontiguousarray(query_boundaries, dtype=np.uint32)
+        return BinnedDataset(rows, row_offset, features, groups, total_bins, label, weight, qb)
 
     def bin(self, feature: int, row: int) -> int:
         m = self.features[feature]
@@ -142,6 +147,11 @@ class BinnedDataset:
                 f.upper_bounds = ub.ctypes.data_as(C.POINTER(C.c_double))
                 f.num_upper_bounds = len(ub)
             f.min_value, f.max_value = m.min_value, m.max_value
+            if m.categories is not None:
+                cats = np.ascontiguousarray(m.categories, dtype=np.int32)
+                keep.append(cats)
+                f.categories = cats.ctypes.data_as(C.POINTER(C.c_int32))
+                f.num_categories = len(cats)
         groups = (_abi.Group * max(len(self.groups), 1))()
         for i, g in enumerate(self.groups):
             data = np.ascontiguousarray(g.data, dtype=np.uint8)
@@ -169,6 +179,36 @@ class BinnedDataset:
             d.query_boundaries = qb.ctypes.data_as(C.POINTER(C.c_uint32))
         d._keep = keep  # ctypes keeps Python attributes on the struct object alive with it
         return d
+
+
+def layout(mappers: list[FeatureMeta]) -> tuple[list[FeatureMeta], list[FeatureGroup], int]:
+    """`layout` (data/build.rs:336-382): the features with their groups, columns and histogram offsets, and the
+    groups (no rows yet): the non-trivial features in input order, a new group whenever the next feature's bins would
+    take the current one over GROUP_BIN_BUDGET. Returns (features, groups, total_bins)."""
+    features: list[FeatureMeta] = []
+    groups: list[dict] = []
+    offset = 0
+    for index, m in enumerate(mappers):
+        meta = FeatureMeta(name=m.name, kind=m.kind, num_bins=m.num_bins, nan_bin=m.nan_bin,
+                           upper_bounds=m.upper_bounds, categories=m.categories, min_value=m.min_value,
+                           max_value=m.max_value)
+        if meta.num_bins == 0:
+            meta.group, meta.column, meta.hist_offset = 0, 0, offset
+            features.append(meta)
+            continue
+        if not groups or groups[-1]["total_bins"] + meta.num_bins > GROUP_BIN_BUDGET:
+            groups.append({"features": [], "hist_offset": offset, "total_bins": 0})
+        g = groups[-1]
+        meta.group = len(groups) - 1
+        meta.column = len(g["features"])
+        meta.hist_offset = offset
+        g["features"].append(index)
+        g["total_bins"] += meta.num_bins
+        offset += meta.num_bins
+        features.append(meta)
+    shells = [FeatureGroup(g["features"], (len(g["features"]) + 3) // 4 * 4, g["hist_offset"], g["total_bins"],
+                           np.zeros((0, (len(g["features"]) + 3) // 4 * 4), np.uint8)) for g in groups]
+    return features, shells, offset
 
 
 def numerical_mapper(name: str, num_bins: int, nan_bin: bool = False) -> FeatureMeta:

@@ -7,6 +7,8 @@ trees equal both, field by field, as JSON to the output path.
 
 usage: torchrun ... multirank_worker.py <output.json> <auto|nccl> <config> <rows> <trees> <num_leaves> [share]
 
+<config> is a bench configuration, or `categorical` for tests/synth.py's categorical dataset.
+
 With `share`, every handle skips the dominant bins of the tiles that share picks (sb2_set_dominant_share).
 """
 
@@ -38,13 +40,23 @@ def main():
         import oracle_lib as orc
         from silvic_b200 import B200Backend, _abi, init_score, params_from_dict
 
-        bench.set_config(config)
-        bench.set_rows(rows)
         dev = torch.device("cuda", local)
-        p = params_from_dict(dict(bench.params_dict(trees), num_leaves=leaves))
-        s0 = init_score(p, bench.all_labels(dev))
         lo, hi = rows * rank // world, rows * (rank + 1) // world
-        data = bench.build_dataset(lo, hi, dev)
+        if config == "categorical":
+            # two categorical features (one-hot and sorted scans) beside four numerical ones (tests/synth.py)
+            from synth import categorical_binned
+
+            whole = categorical_binned(rows, seed=17, label_kind="binary")
+            p = params_from_dict(dict(objective="binary", num_iterations=trees, num_leaves=leaves,
+                                      min_data_per_group=50, max_cat_threshold=16))
+            s0 = init_score(p, whole.label)
+            data = whole.shard(lo, hi)
+        else:
+            bench.set_config(config)
+            bench.set_rows(rows)
+            p = params_from_dict(dict(bench.params_dict(trees), num_leaves=leaves))
+            s0 = init_score(p, bench.all_labels(dev))
+            data = bench.build_dataset(lo, hi, dev)
         b = B200Backend(local)
         if share is not None:
             b.set_dominant_share(share)
@@ -58,16 +70,17 @@ def main():
         b.close()
         dist.barrier()
         if rank == 0:
-            full = bench.build_dataset(0, rows, dev)
+            full = whole if config == "categorical" else bench.build_dataset(0, rows, dev)
             one = B200Backend(local)
             if share is not None:
                 one.set_dominant_share(share)
             one.load(full, p.objective, p.sigmoid)
             single = one.train(p, s0)
             one.close()
-            ref = orc.train([full], orc.default_params(objective=p.objective, num_leaves=leaves,
-                                                       num_iterations=trees, learning_rate=p.learning_rate,
-                                                       num_grad_quant_bins=p.num_grad_quant_bins))
+            ref = orc.train([full], p if config == "categorical" else
+                            orc.default_params(objective=p.objective, num_leaves=leaves, num_iterations=trees,
+                                               learning_rate=p.learning_rate,
+                                               num_grad_quant_bins=p.num_grad_quant_bins))
 
             def differences(a, b_):
                 if len(a) != len(b_):

@@ -26,8 +26,9 @@ WORKER = Path(__file__).resolve().parent / "multirank_worker.py"
 
 # config c2's shape (100 features, binary) at 1M rows: 255-leaf trees run grid steps of eight splits; c5's (2,000
 # features, 80% of them 95% zeros) at 200K rows with the dominant-bin skip: every rank skips its own most frequent
-# bins and recovers them from its own totals before the exchange
-CASES = [("c2", 1_000_000, 3, 255, None), ("c5", 200_000, 3, 31, 0.125)]
+# bins and recovers them from its own totals before the exchange; categorical features, whose candidates carry their
+# left bins through the exchange
+CASES = [("c2", 1_000_000, 3, 255, None), ("c5", 200_000, 3, 31, 0.125), ("categorical", 400_000, 3, 63, None)]
 
 
 @pytest.mark.parametrize("config,rows,trees,leaves,share", CASES, ids=[c[0] for c in CASES])
@@ -38,7 +39,7 @@ def test_two_ranks_grow_the_trees_of_one_gpu(device, mode, config, rows, trees, 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     out = tmp_path / "result.json"
-    port = 29500 + (os.getpid() + (0 if mode == "auto" else 7) + (0 if config == "c2" else 13)) % 2000
+    port = 29500 + (os.getpid() + (0 if mode == "auto" else 7) + 13 * [c[0] for c in CASES].index(config)) % 2000
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", f"--master-port={port}", str(WORKER), str(out), mode,
            config, str(rows), str(trees), str(leaves)] + ([str(share)] if share is not None else [])

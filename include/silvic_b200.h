@@ -360,10 +360,11 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
  * (crates/silvic-core/tests/train_cpu.rs:434-484). `out` (may be NULL) receives the model. */
 int sb2_profile_train(sb2_backend* b, const sb2_params* params, double init_score, double* seconds_by_op,
                       size_t num_ops, sb2_model** out);
-/* The same run; `rows` (max_steps rows of 8 doubles) receives one row per grid step of the last tree's kernel (row
+/* The same run; `rows` (max_steps rows of 9 doubles) receives one row per grid step of the last tree's kernel (row
  * 0 the root; a grid step runs up to eight splits side by side): seconds in the partitions with the built children's
  * histograms, search contexts, slab reductions with the searches, finish, grid barriers (device clock of the tree
- * kernel's first CTA), then the rows of the step's histograms, the splits it ran and the splits it committed.
+ * kernel's first CTA), then the rows of the step's histograms, the splits it ran, the splits it committed, and the
+ * splits it took ready from an earlier step that ran and dropped them (no partition, histogram or search).
  * *num_steps gets the rows written. Single GPU only (SB2_EUNSUPPORTED otherwise). */
 int sb2_profile_steps(sb2_backend* b, const sb2_params* params, double init_score, double* rows, size_t max_steps,
                       size_t* num_steps);

@@ -312,7 +312,7 @@ class B200Backend:
             self._lib.sb2_model_free(m)
 
     STEP_FIELDS = ("partition_histogram", "search_context", "reduce_search", "finish", "barriers", "hist_rows",
-                   "splits", "committed")
+                   "splits", "committed", "kept")
 
     def profile_steps(self, params: _abi.Params, init_score: float, max_steps: int = 1 << 17) -> np.ndarray:
         """Per split step of the last tree (row 0 the root): the tree kernel's phase seconds and the step's sizes,

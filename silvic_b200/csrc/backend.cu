@@ -1433,7 +1433,7 @@ namespace {
 
 struct TrainBuffers {
     DeviceBuffer leaves, leaf_gain, splittable, evaluate, masks, slots, tree_bufs, leaf_sums, leaf_values, records,
-        record_bufs, cursors, leaf_of_row;
+        record_bufs, cursors, leaf_of_row, prep, prep_split;
 };
 
 // Carves DevTree arrays for `count` trees of `L` leaves out of one buffer.
@@ -1691,8 +1691,10 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     SB2_CUDA(b, tb.splittable.alloc(static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.evaluate.alloc(std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.masks.alloc(static_cast<size_t>(std::max(iters, 1)) * std::max<uint32_t>(F, 1)));
-    // one slot per leaf, then the tree kernel's spare slots
-    SB2_CUDA(b, tb.slots.alloc(sizeof(int) * (static_cast<size_t>(L) + kSplits - 1) * 2 * b->total_bins));
+    // one slot per leaf, then the tree kernel's two prepared slots per leaf, and its records of dropped splits
+    SB2_CUDA(b, tb.slots.alloc(sizeof(int) * 3 * static_cast<size_t>(L) * 2 * b->total_bins));
+    SB2_CUDA(b, tb.prep.alloc(sizeof(PrepSplit) * L));
+    SB2_CUDA(b, tb.prep_split.alloc(2 * static_cast<size_t>(L) * std::max<uint32_t>(F, 1)));
     SB2_CUDA(b, tb.leaf_sums.alloc(sizeof(int64_t) * 2 * L));
     SB2_CUDA(b, tb.leaf_values.alloc(sizeof(float) * L));
     SB2_CUDA(b, tb.leaf_of_row.alloc(sizeof(uint16_t) * std::max<uint64_t>(b->num_rows, 1)));
@@ -1753,6 +1755,8 @@ int setup_training(sb2_backend* b, const sb2_params* p, double init_score, Train
     t.evaluate = tb.evaluate.as<uint8_t>();
     t.masks = tb.masks.as<uint8_t>();
     t.slots = tb.slots.as<int>();
+    t.prep = tb.prep.as<PrepSplit>();
+    t.prep_split = tb.prep_split.as<uint8_t>();
     t.tree = work;
     ia.r = b->row_args();
     ia.k.num_grad_quant_bins = p->num_grad_quant_bins;
@@ -2014,7 +2018,9 @@ int sb2_profile_steps(sb2_backend* b, const sb2_params* p, double init_score, do
     SB2_TRY(profile_run(b, p, init_score, last, trace, model));
     if (trace.empty()) return b->fail(SB2_EUNSUPPORTED, "step traces come from the single-GPU tree kernel only");
     size_t steps = 0;  // the grid steps that ran: each ran at least one split
-    while (steps < trace.size() / kStepTrace && trace[steps * kStepTrace + kGrowPhases + 1] > 0) ++steps;
+    while (steps < trace.size() / kStepTrace &&
+           trace[steps * kStepTrace + kGrowPhases + 1] + trace[steps * kStepTrace + kGrowPhases + 3] > 0)
+        ++steps;
     *num_steps = std::min(steps, max_steps);
     for (size_t s = 0; s < *num_steps; ++s)
         for (int k = 0; k < kStepTrace; ++k) {

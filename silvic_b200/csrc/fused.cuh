@@ -1075,11 +1075,12 @@ __device__ bool feature_bins_cta(const TrainArgs& a, const HistArgs& h, const St
     return true;
 }
 
-// The histogram slot split j of a step writes child `c`'s bins to: the child's own (learner.rs:365-367), except
-// that the child which keeps the parent's index takes a spare slot (max_leaves + j - 1) when the split is
-// speculative (j >= 1), so that the parent's bins survive a dropped split; the finish copies it over on commit.
+// The histogram slot split j of a step writes child `c`'s bins to: the child's own (learner.rs:365-367) for the
+// step's first split, which always commits; a speculative split's (j >= 1) go to its leaf's prepared slots, so the
+// parent's bins survive a dropped split and the children's are kept for a later commit (the finish copies them to
+// the children's slots when the split commits).
 __device__ __forceinline__ size_t child_slot(const TrainArgs& a, const Step& st, const SearchCtx& s, uint32_t j, int c) {
-    return j > 0 && s.child[c] == st.leaf ? static_cast<size_t>(a.max_leaves) + j - 1 : static_cast<size_t>(s.child[c]);
+    return j > 0 ? prep_slot(a, st.leaf, c) : static_cast<size_t>(s.child[c]);
 }
 
 // feature_scan_cta: with the built child's bins in `bufs`, group 0 scans the built child and group 1 the sibling

@@ -75,12 +75,14 @@ __device__ __forceinline__ void clock_step(const GrowArgs& g, PhaseClock& c, int
     c.row = step + 1 < g.trace_steps ? g.phase_ns + kGrowPhases + static_cast<size_t>(step + 1) * kStepTrace : nullptr;
 }
 
-// The grid step's sizes in its trace row: the rows of its histograms and its splits (the committed ones are added
-// at its finish).
-__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, uint32_t splits) {
+// The grid step's sizes in its trace row: the rows of its histograms, the splits it runs and the ones it takes
+// ready (the committed ones are added at its finish).
+__device__ __forceinline__ void clock_describe(const GrowArgs& g, PhaseClock& c, uint32_t job_rows, uint32_t splits,
+                                               uint32_t kept) {
     if (!clock_owner(g) || c.row == nullptr) return;
     c.row[kGrowPhases] = job_rows;
     c.row[kGrowPhases + 1] = splits;
+    c.row[kGrowPhases + 3] = kept;
 }
 
 // `*p`, which another CTA may have written in this launch, copied into shared memory once per CTA (one 32-bit word
@@ -202,6 +204,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         }
     }
     if (threadIdx.x == 0) s_n = st[0].active ? 1 : 0;
+    // No leaf has a dropped split yet (the first finish that reads these records comes after two grid barriers).
+    for (uint32_t l = cta * kGrowThreads + threadIdx.x; l < static_cast<uint32_t>(a.max_leaves); l += ctas * kGrowThreads)
+        a.prep[l].valid = 0;
     __syncthreads();
 
     // Grid step gs (-1: the root) runs the splits st[0 .. n).
@@ -215,9 +220,11 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             // Lane j plans split j. Its work: its partition, about one unit per parent row, and its histogram,
             // `hist_weight` units per built row (the built side's share of the split's rows, as the split's counts
             // estimate it).
-            // In floats, summed in a fixed order: every CTA computes the same shares from the same steps.
+            // In floats, summed in a fixed order: every CTA computes the same shares from the same steps. A prepared
+            // split (its work kept from an earlier grid step) takes no CTA.
             const uint32_t lane = threadIdx.x & 31;
-            const bool on = lane < static_cast<uint32_t>(n);
+            const bool on = lane < static_cast<uint32_t>(n) && !st[lane].prepared;
+            const uint32_t nw = __popc(__ballot_sync(0xffffffffu, on));  // the splits that work
             uint32_t count = 0;
             float w = 0.0f;
             bool hist = false;
@@ -233,8 +240,8 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             float total = w;
             for (int o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xffffffffu, total, o);
             total = __shfl_sync(0xffffffffu, total, 0);
-            const float share = on && total > 0.0f ? static_cast<float>(ctas - n) * (w / total) : 0.0f;
-            const uint32_t budget = on ? 1u + min(static_cast<uint32_t>(share), ctas - n) : 0u;
+            const float share = on && total > 0.0f ? static_cast<float>(ctas - nw) * (w / total) : 0.0f;
+            const uint32_t budget = on ? 1u + min(static_cast<uint32_t>(share), ctas - nw) : 0u;
             uint32_t base = budget;  // inclusive prefix, then exclusive
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t up = __shfl_up_sync(0xffffffffu, base, o);
@@ -244,9 +251,11 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
             if (on) {
                 const uint32_t chunks = fused_chunks(count, budget);
                 plan[lane] = SplitPlan{base, chunks, count, fused_packed(count, chunks, round_rows) ? 1u : 0u};
+            } else if (lane < static_cast<uint32_t>(n)) {
+                plan[lane] = SplitPlan{base, 0u, count, 0u};  // no CTA, no slab
             }
             const uint32_t hist_rows = __reduce_add_sync(0xffffffffu, hist ? count : 0u);
-            if (lane == 0) clock_describe(g, clock, hist_rows, static_cast<uint32_t>(n));
+            if (lane == 0) clock_describe(g, clock, hist_rows, nw, static_cast<uint32_t>(n) - nw);
         }
         __syncthreads();
         int mine = -1;
@@ -279,8 +288,12 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         // The left counts and the splits' search contexts (every CTA: the finish is replicated), then the search:
         // items (split j, feature f) = j F + f, CTA c taking items c, c + ctas, ...: the built child's bins reduced
         // from the split's slabs and both children scanned.
-        if (threadIdx.x < static_cast<uint32_t>(n))
-            s_left[threadIdx.x] = st[threadIdx.x].root ? 0u : __ldcg(a.cursors + 2 * (static_cast<size_t>(gs + 1) * kSplits + threadIdx.x));
+        if (threadIdx.x < static_cast<uint32_t>(n)) {
+            const Step& sj = st[threadIdx.x];
+            s_left[threadIdx.x] = sj.root       ? 0u
+                                  : sj.prepared ? __ldcg(&a.prep[sj.leaf].left)
+                                                : __ldcg(a.cursors + 2 * (static_cast<size_t>(gs + 1) * kSplits + threadIdx.x));
+        }
         __syncthreads();
         const uint32_t epoch = g.x.epoch0 + static_cast<uint32_t>(gs + 2);  // this grid step's, on every rank
         const bool ranks = g.x.world > 1;
@@ -297,8 +310,11 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         const uint32_t pcap = scratch != nullptr ? g.stage_depth * (kGrowThreads / 32) * g.slot_bytes - 16384u : 0u;
         if (ranks && !st[0].root && cta == 0 && threadIdx.x < 32) publish_left(g.x, L, epoch, s_left, n);
         const uint32_t items = static_cast<uint32_t>(n) * F;
-        // Split j's built-child histogram was made in phase A (else there is nothing to reduce or exchange).
-        auto built = [&](uint32_t j) { return st[j].root ? root_job.active != 0 : st[j].may_search != 0; };
+        // Split j's built-child histogram was made in phase A (else there is nothing to reduce or exchange; a
+        // prepared split's children were searched when it ran).
+        auto built = [&](uint32_t j) {
+            return st[j].root ? root_job.active != 0 : st[j].may_search != 0 && !st[j].prepared;
+        };
         auto features_of = [&](uint32_t j) -> const uint8_t* { return st[j].root ? mask : eval + static_cast<size_t>(j) * F; };
         // Copies item i's slab bins ahead into pbuf (when they fit); true when it did.
         auto prefetch = [&](uint32_t i) {
@@ -351,7 +367,9 @@ __global__ void __launch_bounds__(kGrowThreads, 1) grow_tree_kernel(GrowArgs g) 
         clock_mark(g, clock, 1);
         // The searches: every item (one rank) or the items of the features this rank owns, each with every rank's
         // bins added; items (split j, feature f) = j F + f, CTA c taking items c, c + ctas, ...
-        auto searched = [&](uint32_t i) { return sc[i / F].searched && (!ranks || owner_of(g.x, i % F) == g.x.rank); };
+        auto searched = [&](uint32_t i) {
+            return sc[i / F].searched && !st[i / F].prepared && (!ranks || owner_of(g.x, i % F) == g.x.rank);
+        };
         const BinsMode mode = ranks ? BinsMode::kGather : BinsMode::kLocal;
         uint32_t prefetched = 0xFFFFFFFFu;  // the item whose bins are in pbuf
         for (uint32_t i = cta; i < items; i += ctas) {

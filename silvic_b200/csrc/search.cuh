@@ -861,6 +861,11 @@ __device__ int32_t tree_split(const DevTree& t, int32_t leaf, const sb2_split_in
     return nl;
 }
 
+// Slot of child c (0: the built one) of leaf `leaf`'s speculative split in the tree kernel (TrainArgs::slots).
+__device__ __forceinline__ size_t prep_slot(const TrainArgs& a, int32_t leaf, int c) {
+    return static_cast<size_t>(a.max_leaves) + 2 * static_cast<size_t>(leaf) + static_cast<size_t>(c);
+}
+
 // The children of a step as the search sees them.
 struct SearchCtx {
     bool searched;

@@ -9,12 +9,18 @@
 // splits of X1 .. Xn together (n <= kSplits, each a whole partition, histogram and search) and, at its finish,
 // commits X1 and then each next Xj while the rule holds; the first Xj that a new child outranks, and all after it,
 // are dropped: their leaves stay leaves, as they were, and are ranked again. The committed sequence is the
-// learner's own, so the tree is identical. On trees of config 2 the next split is a child of the previous one for
-// about 1.5% of splits, so a step commits nearly all of its splits.
+// learner's own, so the tree is identical. On the first trees of config 2 the next split is a child of the previous
+// one for about 1.5% of splits, so a step commits nearly all of its splits; late in a job, with small gradients, a
+// tree runs four splits for every one it commits.
 //
-// A dropped split leaves no trace: its partition wrote only the other buffer's copy of its own positions (its leaf
-// record still names the buffer that holds its rows), its children's histograms went to spare slots (copied to the
-// children's slots only when committed), and its candidates and records are overwritten by later steps.
+// A dropped split's work is kept for the step that commits it (PrepSplit): its partition wrote only the other
+// buffer's copy of its own positions (its leaf record still names the buffer that holds its rows, and nothing else
+// writes them), its children's histograms went to its leaf's two prepared slots (copied to the children's slots only
+// on commit), and the finish records its left count, its children (with their best splits) and their splittable
+// rows. When the leaf is ranked into a later step, the split comes back `prepared`: no CTA partitions, histograms or
+// searches it, and its finish reads the record. Its children were searched under the step's leaf count then; a
+// step with fewer leaves left searches them no more (their records lose their histograms and best splits), and one
+// that would search children not searched then runs the split again.
 #pragma once
 
 #include "search.cuh"
@@ -30,6 +36,7 @@ struct StepsFinish {
     DevLeaf other[kSplits];              // their records
     DevLeaf pending[kSplits];            // the records of the step's own leaves (split j >= 1), kept if dropped
     int32_t pending_leaf[kSplits];       // their indices (-1: split 0)
+    uint32_t left[kSplits];              // this rank's left count of every split
     int32_t committed;                   // splits committed by this step
     int32_t next_n;                      // splits of the next step
     Step next[kSplits];
@@ -87,8 +94,16 @@ __device__ void steps_finish_prepare(const TrainArgs& a, const Step* st, int n, 
     if (warp == 0 && lane < static_cast<uint32_t>(n)) {
         const int j = static_cast<int>(lane);
         const Step& s = st[j];
+        fs.left[j] = left[j];
         if (!s.root) fs.split_feat[j] = a.d.features[s.info.feature];
-        if (s.root) {
+        if (s.prepared) {
+            // Kept from the grid step that ran it; under a step whose children are no longer searched (fewer leaves
+            // left), they have no histograms and no best splits.
+            DevLeaf c0 = load_cg(&a.prep[s.leaf].child[0]), c1 = load_cg(&a.prep[s.leaf].child[1]);
+            if (!s.may_search) c0.has_hist = c1.has_hist = c0.has_best = c1.has_best = 0;
+            fs.child[j][0] = c0;
+            fs.child[j][1] = c1;
+        } else if (s.root) {
             DevLeaf l = load_cg(a.leaves);  // begin, count, which, depth: set before the launch
             l.units_grad = sc[j].ctx[0].units_grad;
             l.units_hess = sc[j].ctx[0].units_hess;
@@ -217,7 +232,14 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
     static_assert(2 * kSplits <= kHistThreads / 32, "a warp per child");
     if (warp < static_cast<uint32_t>(2 * n)) {
         const int j = static_cast<int>(warp) / 2, ch = static_cast<int>(warp) % 2;
-        if (ch < children) {
+        if (ch < children && st[j].prepared) {
+            // The child's record came whole from the split's PrepSplit; its splittable row was kept beside it.
+            uint8_t* rowc = csplit + static_cast<size_t>(2 * j + ch) * F;
+            const uint8_t* kept = a.prep_split + (2 * static_cast<size_t>(st[j].leaf) + ch) * F;
+            const bool has_hist = fs.child[j][ch].has_hist != 0;
+            for (uint32_t f = lane; f < F; f += 32) rowc[f] = has_hist ? __ldcg(kept + f) : 0;
+            if (lane == 0 && fs.child[j][ch].has_best) fs.child_feat[j][ch] = a.d.features[fs.child[j][ch].best.feature];
+        } else if (ch < children) {
             // The best candidate of the child over every feature by `better` (found, then the higher gain, then the
             // lower feature), from the compact gains and flags; then the winner's full candidate.
             FeatureCandidate best{};
@@ -379,28 +401,50 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
             a.leaf_gain[leaf] = r.has_best ? r.best.gain : -INFINITY;
         }
     }
-    if (writes_part(cta, 2) && warp < static_cast<uint32_t>(2 * committed)) {
+    if (writes_part(cta, 2) && warp < static_cast<uint32_t>(2 * n)) {
+        // warp 2 i + c: child c of split i's splittable row, into the child's row when the split commits, else
+        // (a split run here and dropped) into its leaf's PrepSplit rows
         const int i = static_cast<int>(warp) / 2, c = static_cast<int>(warp) % 2;
-        if (c < children) {
-            uint8_t* row = a.splittable + static_cast<size_t>(child_index(st[i], c)) * F;
-            const uint8_t* src = csplit + static_cast<size_t>(2 * i + c) * F;
+        const uint8_t* src = csplit + static_cast<size_t>(2 * i + c) * F;
+        uint8_t* row = nullptr;
+        if (c < children && i < committed)
+            row = a.splittable + static_cast<size_t>(child_index(st[i], c)) * F;
+        else if (c < children && !st[i].prepared && !st[0].root)
+            row = a.prep_split + (2 * static_cast<size_t>(st[i].leaf) + c) * F;
+        if (row)
             for (uint32_t f = lane; f < F; f += 32) row[f] = src[f];
-        }
     }
-    if (committed > 1) {
-        // the spare slot of each committed speculative split's child that keeps the parent's index (child_slot)
+    // The children's bins of each committed split that did not write them in place (a speculative split, or a
+    // prepared one: child_slot), copied from its leaf's prepared slots into the children's slots by every CTA.
+    {
         const size_t slot_len = a.total_bins;  // [g, h] pairs
-        const size_t total = static_cast<size_t>(committed - 1) * slot_len;
+        const size_t total = static_cast<size_t>(committed) * 2 * slot_len;
         for (size_t q = static_cast<size_t>(cta) * blockDim.x + threadIdx.x; q < total;
              q += static_cast<size_t>(gridDim.x) * blockDim.x) {
-            const int i = 1 + static_cast<int>(q / slot_len);
-            if (!sc[i].searched) continue;
+            const int i = static_cast<int>(q / (2 * slot_len)), c = static_cast<int>(q / slot_len) % 2;
+            if ((i == 0 && !st[i].prepared) || st[i].root || !sc[i].searched) continue;
             const size_t e = q % slot_len;
-            const int2* src = reinterpret_cast<const int2*>(a.slots) + (static_cast<size_t>(a.max_leaves) + i - 1) * slot_len;
-            int2* dst = reinterpret_cast<int2*>(a.slots) + static_cast<size_t>(st[i].leaf) * slot_len;
+            const int2* src = reinterpret_cast<const int2*>(a.slots) + prep_slot(a, st[i].leaf, c) * slot_len;
+            int2* dst = reinterpret_cast<int2*>(a.slots) + static_cast<size_t>(child_index(st[i], c)) * slot_len;
             __stcg(dst + e, __ldcg(src + e));
         }
     }
+    // PrepSplit records: a committed split's leaf has none (its index now names its left child); a split run here
+    // and dropped keeps its left count, children and their rows for the step that commits it.
+    if (writes_part(cta, 1) && warp == 1 && lane < static_cast<uint32_t>(n) && !st[0].root) {
+        const int j = static_cast<int>(lane);
+        PrepSplit* rec = a.prep + st[j].leaf;
+        if (j < committed) {
+            rec->valid = 0;
+        } else if (!st[j].prepared) {
+            rec->may_search = st[j].may_search;
+            rec->left = fs.left[j];
+            rec->child[0] = fs.child[j][0];
+            rec->child[1] = fs.child[j][1];
+            rec->valid = 1;
+        }
+    }
+
 
     // The next step's splits: their records, steps and features (learner.rs:249-286).
     const int next_n = fs.next_n;
@@ -426,7 +470,20 @@ __device__ void steps_finish(const TrainArgs& a, Step* st, int& n, const SearchC
         }
         uint8_t* ev = eval + static_cast<size_t>(k) * F;
         for (uint32_t f = lane; f < F; f += 32) ev[f] = static_cast<uint8_t>(mask[f] && split_ok[f]);
-        if (lane == 0) fs.next[k] = next_step(a, *rec, leaf_index, leaves_after + k, *feat);
+        if (lane == 0) {
+            Step nx = next_step(a, *rec, leaf_index, leaves_after + k, *feat);
+            // Its work is kept (PrepSplit) when an earlier step ran it and dropped it, and its children were searched
+            // then exactly when they are now, or then but no longer (fewer leaves left: they are searched no more).
+            int kept = -1;  // the may_search it ran under, -1: not run
+            if (src >= kPoolPending) {
+                const Step& was = st[src - kPoolPending];
+                kept = was.prepared ? __ldcg(&a.prep[leaf_index].may_search) : was.may_search;
+            } else if (src < kPoolChild && __ldcg(&a.prep[leaf_index].valid)) {
+                kept = __ldcg(&a.prep[leaf_index].may_search);
+            }
+            nx.prepared = kept >= 0 && (kept == nx.may_search || (kept != 0 && !nx.may_search));
+            fs.next[k] = nx;
+        }
     }
     __syncthreads();
     if (threadIdx.x < static_cast<uint32_t>(kSplits)) {

@@ -47,6 +47,8 @@ struct Step {
     uint32_t bag_round;
     double bag_fraction;
     uint64_t row_offset;
+    int32_t prepared;     // the tree kernel: an earlier grid step ran this split and kept its work (PrepSplit)
+    int32_t pad_;
 };
 
 // Tree arrays of one tree in LightGBM layout (tree.rs:47-73), `max_leaves` entries each.
@@ -85,6 +87,18 @@ struct IterState {
     unsigned long long root_units[2];
 };
 
+// The tree kernel's record of a split it ran speculatively and dropped, kept until the leaf is split (learner.rs's
+// split of a leaf depends on the leaf alone, so the work stays valid): the partition of the leaf's rows into the
+// other buffer stays in place (only the leaf's own splits write its positions), the children's histograms sit in
+// the leaf's two prepared slots, and this record holds the rest.
+struct PrepSplit {
+    int32_t valid;
+    int32_t may_search;      // Step::may_search when it ran: the children were searched under it
+    uint32_t left;           // this rank's left count
+    int32_t pad_;
+    DevLeaf child[2];        // the children's records, best splits included (0: the built child)
+};
+
 // Everything the training kernels read, by value.
 struct TrainArgs {
     DevData d;
@@ -104,8 +118,10 @@ struct TrainArgs {
     uint8_t* evaluate;          // [num_features]: the current step's evaluated features
     const uint8_t* masks;       // [num_iterations * num_features]: per-iteration feature_mask
     int* staging;               // [2 * total_bins + 2]: the step's new histogram and, after it, the left count
-    int* slots;                 // [(max_leaves + kSplits - 1) * 2 * total_bins]: one histogram per leaf, then the
-                                // tree kernel's spare slots
+    int* slots;                 // [3 * max_leaves * 2 * total_bins]: one histogram per leaf, then the tree kernel's
+                                // two prepared slots per leaf (prep_slot)
+    PrepSplit* prep;            // [max_leaves]: the tree kernel's dropped splits, by leaf
+    uint8_t* prep_split;        // [max_leaves * 2 * num_features]: their children's splittable rows
     HistJob* hist_job;
     IterState* iter;
     DevTree tree;               // the tree being grown
@@ -157,11 +173,11 @@ cudaError_t grow_configure(int smem_bytes, int* blocks_per_sm);
 // `phase_ns` (optional, kGrowPhases entries) receives the nanoseconds CTA 0 spent per phase: the partition with
 // the built child's histogram, the children's search context, the slab reduction with the search, the finish, the
 // grid barriers. With `trace_steps` > 0
-// it is followed by one row of kStepTrace values per step (up to trace_steps): the same phase times of that step,
-// then the rows of its histogram, whether the slabs held packed sums (1) or unpacked ones (0), and the rows of the
-// leaf it split.
+// it is followed by one row of kStepTrace values per grid step (up to trace_steps): the same phase times of that
+// step, then the rows of its histograms, the splits it ran, the splits it committed, and the splits it took ready
+// from earlier steps (PrepSplit).
 constexpr int kGrowPhases = 5;
-constexpr int kStepTrace = kGrowPhases + 3;
+constexpr int kStepTrace = kGrowPhases + 4;
 // The layout of its dynamic shared memory (`bytes` in all): the histogram's arrays first, the partition's scan
 // words (2 * 512 + 64) at `scan_offset`, the histogram's staging slots (16 warps x `stage_depth` slots of
 // `slot_bytes`, 128-byte aligned) at `stage_offset`, its per-feature flags ((5 kSplits + 1) F bytes) at

@@ -249,9 +249,10 @@ def test_training_matches_oracle(device, name, bins, rows, params):
 
 
 def test_speculative_splits_drop_and_match_oracle(device):
-    """The tree kernel runs the next leaves' splits beside the best one's and drops those a fresh child outranks.
-    On data where the best leaf is often a child of the last split, some grid steps drop splits; the trees stay the
-    oracle's, and the last tree's committed splits are its leaves (the root counts one)."""
+    """The tree kernel runs the next leaves' splits beside the best one's and drops those a fresh child outranks,
+    keeping their work for the step that commits them. On data where the best leaf is often a child of the last
+    split, some grid steps drop splits and later ones commit them ready; the trees stay the oracle's, and the last
+    tree's committed splits are its leaves (the root counts one)."""
     data = nested_binned(20_000)
     p = orc.default_params(objective=_abi.REGRESSION, num_leaves=31, num_iterations=3)
     ref = orc.train([data], p)
@@ -266,5 +267,9 @@ def test_speculative_splits_drop_and_match_oracle(device):
     fields = B200Backend.STEP_FIELDS
     splits = int(steps[:, fields.index("splits")].sum())
     committed = int(steps[:, fields.index("committed")].sum())
+    kept = int(steps[:, fields.index("kept")].sum())
     assert committed == ref.trees[-1].num_leaves
-    assert splits > committed, "no speculative split was dropped"
+    # every committed split ran once, here or in the step that dropped it and kept its work
+    assert splits - (committed - kept) > 0, "no speculative split was dropped"
+    assert kept <= splits - (committed - kept)
+    assert kept > 0, "no dropped split was committed from its kept work"

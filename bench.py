@@ -593,6 +593,8 @@ def run_b200(args, rank: int, world: int):
     timed_trees = model.trees[args.warmup:args.warmup + args.steps]
     # The standalone root histogram (every row, every feature).
     hist_s = backend.time_histogram(10)
+    # What bounds it: red.shared.add.u32 alone at the histogram's address pattern (lane adds per second).
+    adds_alone = backend.time_shared_adds(0)[0]
     backend.close()
     launches_persistent = bool(model.tree_seconds)
     timed, hist_s = _max_over_ranks([timed, hist_s], world, dev)
@@ -625,6 +627,9 @@ def run_b200(args, rank: int, world: int):
                      "achieved": bytes_root / hist_s / 1e9, "launch_ms": hist_s * 1000.0,
                      "algorithmic_bytes": bytes_root}
     hist_roofline["frac"] = hist_roofline["achieved"] / peak
+    # One shared atomic per (row, feature): the histogram's atomic rate against the atomic unit's rate alone.
+    hist_roofline["shared_adds"] = {"histogram_per_s": n_local * CFG.features / hist_s, "alone_per_s": adds_alone,
+                                    "frac": n_local * CFG.features / hist_s / adds_alone}
     if tree_s and len(tree_s) == len(timed_trees):
         # The dominant kernel: the persistent tree kernel, one launch per tree.
         tree_bytes = [tree_algorithmic_bytes(tr, n_local, S, T, CFG.num_leaves, world) for tr in timed_trees]

@@ -350,6 +350,15 @@ int sb2_test_unanswered_peer(sb2_backend* b, uint32_t spin_limit);
  * sb2_train). */
 int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* seconds);
 
+/* No counterpart in the reference: the rate of the operation that bounds the quantized histogram, a 32-bit shared
+ * memory reduction (red.shared.add.u32), measured alone on the handle's device (no dataset needed): one CTA of 512
+ * threads per SM adds at the histogram's addresses (word bin * 32 + lane of a 256-bin array: 32 banks per
+ * instruction) with its bins in registers, so no global memory is read. `pattern` 0: every lane its own bins (the
+ * lanes' words in 32 different 128-byte rows, as in a histogram of random rows); 1: the same bin on every lane at
+ * each step (one 128-byte row per instruction). *adds_per_second and *adds_per_sm_clock get lane adds per second
+ * (CUDA events) and per SM clock cycle (the CTAs' clock64). */
+int sb2_time_shared_adds(sb2_backend* b, int pattern, double* adds_per_second, double* adds_per_sm_clock);
+
 /* sb2_train without the CUDA graph, each operation bracketed by CUDA events: seconds_by_op receives the device
  * time of the last iteration per operation, in the order gradients, quantize (and the iteration's start),
  * histogram, partition, split search, leaf sums, finalize (renewal and the tree record), score update, NCCL

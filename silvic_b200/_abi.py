@@ -251,6 +251,7 @@ SIGNATURES = {
                                               C.c_double, C.c_double, P(SplitConfig), VP, VP]),
     "sb2_check_division": (C.c_int, [VP, C.c_uint64, C.c_uint32, P(C.c_uint64)]),
     "sb2_time_histogram": (C.c_int, [VP, C.c_uint64, C.c_int, P(C.c_double)]),
+    "sb2_time_shared_adds": (C.c_int, [VP, C.c_int, P(C.c_double), P(C.c_double)]),
     "sb2_profile_train": (C.c_int, [VP, P(Params), C.c_double, P(C.c_double), C.c_size_t, P(VP)]),
     "sb2_profile_steps": (C.c_int, [VP, P(Params), C.c_double, P(C.c_double), C.c_size_t, P(C.c_size_t)]),
     "sb2_nccl_unique_id": (C.c_int, [P(C.c_uint8), C.c_size_t]),

@@ -297,6 +297,13 @@ class B200Backend:
         self._check(self._lib.sb2_time_histogram(self._h, rows, repeats, C.byref(secs)))
         return secs.value
 
+    def time_shared_adds(self, pattern: int = 0) -> tuple[float, float]:
+        """(lane adds per second, per SM clock) of red.shared.add.u32 alone at the histogram's address pattern
+        (0: every lane its own bins; 1: one bin per instruction)."""
+        per_s, per_clk = C.c_double(), C.c_double()
+        self._check(self._lib.sb2_time_shared_adds(self._h, pattern, C.byref(per_s), C.byref(per_clk)))
+        return per_s.value, per_clk.value
+
     PROFILE_OPS = ("gradients", "quantize", "histogram", "partition", "search", "leaf_sums", "finalize",
                    "add_tree", "collectives", "tree", "tree.partition_histogram", "tree.search_context",
                    "tree.reduce_search", "tree.finish", "tree.barriers")

@@ -19,7 +19,7 @@ CSRC = PACKAGE / "csrc"
 LIB_DIR = PACKAGE / "_lib"
 BUILD_DIR = PACKAGE.parent / "_build" / "silvic_b200"
 LIBRARY = LIB_DIR / "libsilvic_b200.so"
-SOURCES = ["hist.cu", "partition.cu", "split.cu", "grow.cu", "iter.cu", "lambdarank.cu", "binning.cu", "backend.cu"]
+SOURCES = ["hist.cu", "partition.cu", "split.cu", "grow.cu", "iter.cu", "lambdarank.cu", "binning.cu", "diag.cu", "backend.cu"]
 HEADERS = ["common.cuh", "hist.cuh", "hist_device.cuh", "partition.cuh", "search.cuh", "train.cuh", "iter.cuh",
            "fused.cuh", "steps.cuh", "binning.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -1340,6 +1340,17 @@ int sb2_time_histogram(sb2_backend* b, uint64_t rows, int repeats, double* secon
     return SB2_OK;
 }
 
+int sb2_time_shared_adds(sb2_backend* b, int pattern, double* adds_per_second, double* adds_per_sm_clock) {
+    if (!b || !adds_per_second || !adds_per_sm_clock) return SB2_EDEVICE;
+    if (pattern != 0 && pattern != 1) return b->fail(SB2_EDEVICE, "sb2_time_shared_adds: pattern must be 0 or 1");
+    SB2_CUDA(b, cudaSetDevice(b->device));
+    double adds = 0.0, cycles = 0.0, seconds = 0.0;
+    SB2_CUDA(b, time_shared_adds(pattern, b->sms, 64, b->stream, &adds, &cycles, &seconds));
+    *adds_per_second = seconds > 0.0 ? adds / seconds : 0.0;
+    *adds_per_sm_clock = cycles > 0.0 ? adds / cycles : 0.0;  // cycles summed over the CTAs, one CTA per SM
+    return SB2_OK;
+}
+
 }  // extern "C"
 
 namespace {

@@ -13,7 +13,9 @@
 //
 // The histogram streams its rows' bins into shared memory with cp.async: each warp keeps `depth` batches of 32 rows
 // in flight in its own staging slots while it adds an earlier batch, so the gathers of a leaf's scattered rows
-// overlap the shared atomics instead of waiting for them.
+// overlap the shared atomics instead of waiting for them. The full tiles' bytes move in row chunks (a copy
+// instruction reads whole rows, a shared read 512 consecutive bytes), so the L1 data pipe, which the shared atomics
+// keep busy, spends few wavefronts on the loads.
 //
 // A CTA's packed shared sums are exact for at most `round_rows` rows (packed_round_rows); when its range is that
 // short it flushes the packed sums as they are (half the bytes) and the reduction unpacks them, else it flushes
@@ -247,76 +249,85 @@ __device__ __forceinline__ void cp_async_wait(uint32_t pending) {
 }
 
 
-// Staging slot of a batch: per tile, 32 rows of `stride` bytes (lane k's row at k * stride), then the batch's 32
-// packed gradients. A 32-byte row's two halves are swapped on lanes with bit 2 set, so that the eight lanes of a
-// 128-bit shared load hit 32 different banks.
-__device__ __forceinline__ uint32_t stage_swap(uint32_t lane) { return (lane >> 2) & 1u; }
+// Staging slot of a batch: the rows of the unit's full tiles (32 features each, side by side: 32 F bytes a row, row
+// i at i * 32 F), then a partial tile's 32 rows of `stride` bytes (lane k's row at LaneTile::stage_off + k * stride),
+// then the batch's 32 packed gradients. The full tiles move in row chunks (ChunkLane, hist_device.cuh): copy g of a
+// lane is chunk 32 g + lane, so a copy instruction reads whole rows (4 rows of 128 bytes: 4 lines, where a piece of
+// each of 32 rows touches 32) and a shared read takes 512 consecutive bytes.
 
-// Lane's copies of row `row`'s bytes of every wanted tile into slot `slot`.
-__device__ __forceinline__ void stage_row(const LaneTile* lt, uint32_t nt, uint32_t slot, uint32_t row,
-                                          uint32_t lane, uint64_t pol) {
+// Whole warp: the copies of a batch's full-tile rows into slot `slot`: chunk m = 32 i + lane is chunk m mod 2F of
+// the batch's row m / 2F, whose row id and packed gradient lane m / 2F holds (`row`, `packed`); rows with a zero
+// gradient are not copied (they add nothing). `wanted`: bit t, full tile t has a wanted feature.
+template <int F>
+__device__ __forceinline__ void stage_full(const LaneTile* lt, uint32_t wanted, uint32_t slot, uint32_t row,
+                                           uint32_t packed, uint32_t lane, uint64_t pol) {
+    constexpr uint32_t C = 2 * F;
+    const uint8_t* base = lt[0].base;
+    const uint32_t pitch = lt[0].pitch;
 #pragma unroll
-    for (int t = 0; t < kMaxUnitTiles; ++t) {
-        if (t >= static_cast<int>(nt)) break;
-        const LaneTile l = lt[t];
-        if (l.active == 0) continue;
-        const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.pitch;
-        const uint32_t dst = slot + l.stage_off + lane * l.stride;
-        switch (l.stride) {
-            case 32: {
-                const uint32_t sw = stage_swap(lane);
-                cp_async16(dst + 16 * sw, src, pol);
-                cp_async16(dst + 16 * (sw ^ 1u), src + 16, pol);
-                break;
-            }
-            case 16:
-                cp_async16(dst, src, pol);
-                break;
-            case 8:
-                cp_async8(dst, src, pol);
-                break;
-            default:
-                cp_async4(dst, src, pol);
-                break;
-        }
+    for (uint32_t i = 0; i < C; ++i) {
+        const uint32_t m = 32 * i + lane;
+        const uint32_t src_lane = m / C, c = m % C;
+        const uint32_t rw = __shfl_sync(0xffffffffu, row, static_cast<int>(src_lane));
+        const uint32_t pk = __shfl_sync(0xffffffffu, packed, static_cast<int>(src_lane));
+        if (pk != 0 && ((wanted >> (c >> 1)) & 1u))
+            cp_async16(slot + 16 * m, base + static_cast<uint64_t>(rw) * pitch + 16 * c, pol);
     }
 }
 
-// Adds the lane's staged row of slot `slot` (packed gradient `packed`, nonzero) at every wanted tile.
-__device__ __forceinline__ void add_staged(const LaneTile* lt, uint32_t nt, uint32_t slot, uint32_t packed,
-                                           uint32_t lane) {
+// Whole warp: a landed batch's full-tile rows of slot `slot` (packed gradients at `gh`) into the shared sums.
+template <int F>
+__device__ __forceinline__ void add_staged_full(const ChunkLane& k, uint32_t slot, uint32_t gh, uint32_t lane) {
+    constexpr uint32_t C = 2 * F;
 #pragma unroll
-    for (int t = 0; t < kMaxUnitTiles; ++t) {
-        if (t >= static_cast<int>(nt)) break;
-        const LaneTile l = lt[t];
-        if (l.active == 0) continue;
-        const uint32_t a = slot + l.stage_off + lane * l.stride;
-        uint32_t w[8];
-        switch (l.stride) {
-            case 32: {
-                const uint32_t sw = stage_swap(lane);
-                const uint4 x = lds128(a + 16 * sw), y = lds128(a + 16 * (sw ^ 1u));
-                w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w, w[4] = y.x, w[5] = y.y, w[6] = y.z, w[7] = y.w;
-                add_row_tile<8>(l, w, packed, lane);
-                break;
-            }
-            case 16: {
-                const uint4 x = lds128(a);
-                w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w;
-                add_row_tile<4>(l, w, packed, lane);
-                break;
-            }
-            case 8: {
-                const uint2 x = lds64(a);
-                w[0] = x.x, w[1] = x.y;
-                add_row_tile<2>(l, w, packed, lane);
-                break;
-            }
-            default:
-                w[0] = lds32(a);
-                add_row_tile<1>(l, w, packed, lane);
-                break;
+    for (uint32_t g = 0; g < C; ++g) {
+        const uint32_t m = 32 * g + lane, c = m % C;
+        if (!((k.wanted >> (c >> 1)) & 1u)) continue;
+        const uint32_t packed = lds32(gh + 4 * (m / C));
+        if (packed == 0) continue;  // past the range, or a zero gradient: not copied, adds nothing
+        add_chunk(k, c >> 1, lds128(slot + 16 * m), packed);
+    }
+}
+
+// Lane's copies of row `row`'s bytes of the unit's partial tile (tile `t`, stride below 32) into slot `slot`.
+__device__ __forceinline__ void stage_partial(const LaneTile& l, uint32_t slot, uint32_t row, uint32_t lane,
+                                              uint64_t pol) {
+    const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.pitch;
+    const uint32_t dst = slot + l.stage_off + lane * l.stride;
+    switch (l.stride) {
+        case 16:
+            cp_async16(dst, src, pol);
+            break;
+        case 8:
+            cp_async8(dst, src, pol);
+            break;
+        default:
+            cp_async4(dst, src, pol);
+            break;
+    }
+}
+
+// Adds the lane's staged row of the partial tile `l` (packed gradient `packed`, nonzero).
+__device__ __forceinline__ void add_staged_partial(const LaneTile& l, uint32_t slot, uint32_t packed, uint32_t lane) {
+    const uint32_t a = slot + l.stage_off + lane * l.stride;
+    uint32_t w[8];
+    switch (l.stride) {
+        case 16: {
+            const uint4 x = lds128(a);
+            w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w;
+            add_row_tile<4>(l, w, packed, lane);
+            break;
         }
+        case 8: {
+            const uint2 x = lds64(a);
+            w[0] = x.x, w[1] = x.y;
+            add_row_tile<2>(l, w, packed, lane);
+            break;
+        }
+        default:
+            w[0] = lds32(a);
+            add_row_tile<1>(l, w, packed, lane);
+            break;
     }
 }
 
@@ -369,6 +380,14 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
         }
         return;
     }
+    // The unit's full tiles (the leading ones, stride 32) move in row chunks; a partial tile lane per row.
+    uint32_t nfull = 0, wanted = 0;
+    while (nfull < nt && lt[nfull].stride == 32) {
+        if (lt[nfull].active != 0) wanted |= 1u << nfull;
+        ++nfull;
+    }
+    const bool partial = nfull < nt && lt[nfull].active != 0;
+    const ChunkLane ck = chunk_lane(lt, nfull, lane);
     const uint32_t mine = stage + warp * depth * slot_bytes;
     const uint32_t gh_off = slot_bytes - 128;  // the slot's packed gradients
     uint32_t next_row, next_packed;  // the position of batch `issued`, loaded one issue ahead
@@ -377,18 +396,36 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
     for (uint32_t i = 0; i < n; ++i) {
         while (issued < n && issued < i + depth) {
             const uint32_t slot = mine + issue_slot * slot_bytes;
+            __syncwarp();  // every lane is done reading the slot's previous batch (lanes read each other's copies)
             sts32(slot + gh_off + 4 * lane, next_packed);
-            if (next_packed != 0) stage_row(lt, nt, slot, next_row, lane, pol);  // a zero gradient adds nothing
+            switch (nfull) {
+                case 1: stage_full<1>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
+                case 2: stage_full<2>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
+                case 3: stage_full<3>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
+                case 4: stage_full<4>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
+                default: break;
+            }
+            if (partial && next_packed != 0) stage_partial(lt[nfull], slot, next_row, lane, pol);  // zero adds nothing
             cp_async_commit();
             ++issued;
             issue_slot = issue_slot + 1 == depth ? 0 : issue_slot + 1;
             if (issued < n) position(issued, next_row, next_packed);
         }
         cp_async_wait(issued - i - 1);  // batch i's copies (this lane's) have landed
+        __syncwarp();                   // ... and every lane's: a lane adds chunks other lanes copied
         const uint32_t slot = mine + use_slot * slot_bytes;
         use_slot = use_slot + 1 == depth ? 0 : use_slot + 1;
-        const uint32_t packed = lds32(slot + gh_off + 4 * lane);
-        if (packed != 0) add_staged(lt, nt, slot, packed, lane);
+        switch (nfull) {
+            case 1: add_staged_full<1>(ck, slot, slot + gh_off, lane); break;
+            case 2: add_staged_full<2>(ck, slot, slot + gh_off, lane); break;
+            case 3: add_staged_full<3>(ck, slot, slot + gh_off, lane); break;
+            case 4: add_staged_full<4>(ck, slot, slot + gh_off, lane); break;
+            default: break;
+        }
+        if (partial) {
+            const uint32_t packed = lds32(slot + gh_off + 4 * lane);
+            if (packed != 0) add_staged_partial(lt[nfull], slot, packed, lane);
+        }
     }
 }
 

@@ -8,12 +8,13 @@
 // `round_rows` rows (packed_round_rows) before it flushes: it unpacks the slots into its slab of separate int32 g and
 // h arrays (stored the first time, added afterwards) and clears them.
 //
-// Work per warp: 32 consecutive positions of the leaf, lane k owning position k's row. A lane loads its row's tile
-// bytes with 128-bit loads (a 32-byte row is one sector; a warp's 32 rows are in flight together), permutes them by
-// its lane index, and walks them: at step i lane k adds its row's packed gradient at feature i XOR (k mod stride), so
-// in a full tile the 32 lanes of every atomic hit 32 different features, i.e. 32 different banks. The arrays are
-// aligned so that an element costs one multiply-add for its address and one shared reduction. Rows whose packed
-// gradient is zero add nothing and skip their atomics.
+// Work per warp: a range of consecutive positions of the leaf. The unit's full tiles (32 features each, side by side
+// in rows of up to 128 bytes) are read in row chunks (add_full_tiles): lane k loads 16 bytes of a row such that one
+// 128-bit load of the warp covers whole rows, permutes them by a lane constant and walks them, so that the 32 lanes
+// of every atomic hit 32 different features, i.e. 32 different banks. A partial tile (fewer than 32 features, in its
+// own region) is read lane per row: lane k loads position k's row and at step i adds feature i XOR (k mod stride).
+// The arrays are aligned so that an element costs one multiply-add for its address and one shared reduction. Rows
+// whose packed gradient is zero add nothing and skip their loads and atomics.
 #pragma once
 
 #include "hist.cuh"
@@ -135,6 +136,137 @@ __device__ __forceinline__ void add_row(const LaneTile& t, const uint32_t (&wrow
             shared_add_nonzero(bin * (4 * kStride) + (base ^ (4u * i)), packed, bin);
         else
             shared_add(bin * (4 * kStride) + (base ^ (4u * i)), packed);
+    }
+}
+
+// Where a histogram's positions take their rows and packed gradients from: a partition buffer's row ids and
+// ordered gradients at positions `begin + p`, or (`identity`) rows `begin + p` themselves with gradients by row.
+struct PositionSource {
+    const uint32_t* rows;
+    const int32_t* gh;
+    uint32_t begin;
+    bool identity;
+};
+
+__device__ __forceinline__ void position_of(const PositionSource& s, uint32_t p, uint32_t& row, uint32_t& packed) {
+    const uint32_t pos = s.begin + p;
+    if (s.identity) {
+        row = pos;
+        packed = static_cast<uint32_t>(__ldcs(s.gh + pos));
+    } else {
+        row = __ldcg(s.rows + pos);  // written by a partition of the same stream: not through the read-only path
+        packed = static_cast<uint32_t>(__ldcg(s.gh + pos));
+    }
+}
+
+// The lane constants of row-chunk work over a unit's full tiles (its first F tiles: 32 features each, side by side
+// in rows of 32 F bytes). A batch of 32 rows is 64 F chunks of 16 bytes, chunk m = row * 2F + c holding features
+// 16 (c mod 2) .. of tile c / 2; instruction g of the batch gives lane k chunk m = 32 g + k, so a warp's load (or
+// copy, or shared read) covers 512 consecutive bytes of whole rows, where a lane-per-row load of 32 scattered rows
+// touches 32 lines for the same bytes. Lane k permutes its 16 bytes by r = k / 2 (xor_bytes) and at step s adds
+// feature 16 (k mod 2) + (s ^ r) of its chunk's tile (chunk m has the parity of k): the 32 atomics of a step hit 32
+// different feature lanes, i.e. 32 banks, for any F.
+struct ChunkLane {
+    uint32_t r;                      // the byte permutation: lane / 2
+    uint32_t addr[kMaxUnitTiles];    // per full tile: shared address of this lane's feature lane 16 (lane mod 2) + r
+    uint32_t skip;                   // bit t: full tile t skips stored bin 0 (Tile::skip)
+    uint32_t wanted;                 // bit t: full tile t has a wanted feature
+};
+
+__device__ __forceinline__ ChunkLane chunk_lane(const LaneTile* lt, uint32_t nfull, uint32_t lane) {
+    ChunkLane k;
+    k.r = lane >> 1;
+    k.skip = 0;
+    k.wanted = 0;
+    const uint32_t off = 4u * ((lane & 1u) * 16u + k.r);
+#pragma unroll
+    for (int t = 0; t < kMaxUnitTiles; ++t) {
+        k.addr[t] = 0;
+        if (t >= static_cast<int>(nfull)) continue;
+        const LaneTile l = lt[t];
+        k.addr[t] = l.addr | off;  // the tile's array is 128-byte aligned
+        if (l.skip) k.skip |= 1u << t;
+        if (l.active != 0) k.wanted |= 1u << t;
+    }
+    return k;
+}
+
+// One lane's 16 bytes of full tile `t`, added at their features (stored bin 0 skipped in a Tile::skip tile).
+__device__ __forceinline__ void add_chunk(const ChunkLane& k, uint32_t t, uint4 v, uint32_t packed) {
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    xor_bytes<4>(w, k.r);
+    const uint32_t base = k.addr[0] * (t == 0) + k.addr[1] * (t == 1) + k.addr[2] * (t == 2) + k.addr[3] * (t == 3);
+    if ((k.skip >> t) & 1u) {
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+            const uint32_t bin = (w[s >> 2] >> (8 * (s & 3))) & 0xFFu;
+            shared_add_nonzero(bin * 128u + (base ^ (4u * s)), packed, bin);
+        }
+    } else {
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+            const uint32_t bin = (w[s >> 2] >> (8 * (s & 3))) & 0xFFu;
+            shared_add(bin * 128u + (base ^ (4u * s)), packed);
+        }
+    }
+}
+
+// Adds one loaded row of a partial tile (stride 4, 8 or 16) at every feature: add_row by stride.
+__device__ __forceinline__ void add_partial_row(const LaneTile& l, const uint32_t (&w)[8], uint32_t packed,
+                                                uint32_t lane) {
+    switch (l.stride) {
+        case 16:
+            add_row<4>(l, w, packed, lane);
+            break;
+        case 8:
+            add_row<2>(l, w, packed, lane);
+            break;
+        default:
+            add_row<1>(l, w, packed, lane);
+            break;
+    }
+}
+
+// Whole warp: positions [p_lo, p_hi) of `src` into the unit's shared sums, in batches of 32 positions: the F full
+// tiles in row chunks (ChunkLane), a partial tile `lp` (when `partial`) lane per row. Lane k loads position k's row
+// and packed gradient one batch ahead; a chunk's row and gradient come from the lane that loaded them.
+template <int F>
+__device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, const PositionSource& src,
+                                          uint32_t p_lo, uint32_t p_hi, uint32_t lane) {
+    constexpr uint32_t C = 2 * F;
+    const ChunkLane k = chunk_lane(lt, F, lane);
+    const LaneTile lp = lt[partial ? F : 0];
+    const uint8_t* rows0 = lt[0].base;
+    const uint32_t pitch = lt[0].pitch;
+    auto position = [&](uint32_t p, uint32_t& row, uint32_t& packed) {
+        row = 0;
+        packed = 0;
+        if (p < p_hi) position_of(src, p, row, packed);
+    };
+    uint32_t next_row, next_packed;
+    position(p_lo + lane, next_row, next_packed);
+    for (uint32_t p0 = p_lo; p0 < p_hi; p0 += 32) {
+        const uint32_t row = next_row, packed = next_packed;
+        uint4 v[C];
+        uint32_t pk[C];
+#pragma unroll
+        for (uint32_t g = 0; g < C; ++g) {
+            const uint32_t m = 32 * g + lane, c = m % C;
+            const uint32_t rw = __shfl_sync(0xffffffffu, row, static_cast<int>(m / C));
+            pk[g] = __shfl_sync(0xffffffffu, packed, static_cast<int>(m / C));
+            v[g] = make_uint4(0, 0, 0, 0);
+            if (pk[g] != 0 && ((k.wanted >> (c >> 1)) & 1u))
+                v[g] = __ldcs(reinterpret_cast<const uint4*>(rows0 + static_cast<uint64_t>(rw) * pitch + 16 * c));
+        }
+        uint32_t wp[8] = {};
+        if (partial && packed != 0) load_row(lp, row, wp);
+        position(p0 + 32 + lane, next_row, next_packed);
+#pragma unroll
+        for (uint32_t g = 0; g < C; ++g) {
+            const uint32_t c = (32 * g + lane) % C;
+            if (pk[g] != 0 && ((k.wanted >> (c >> 1)) & 1u)) add_chunk(k, c >> 1, v[g], pk[g]);
+        }
+        if (partial && packed != 0) add_partial_row(lp, wp, packed, lane);
     }
 }
 
@@ -302,6 +434,11 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
 
     const uint32_t* rows = a.rows[job.which & 1];
     const int32_t* ordered = a.ordered[job.which & 1];
+    const PositionSource src{rows, job.identity ? a.packed : ordered, job.begin, job.identity != 0};
+    // The unit's leading full tiles (and a partial tile after them) go through hist_rows; a unit of one partial tile
+    // through the lane-per-row loop below.
+    uint32_t nfull = 0;
+    while (nfull < num_tiles && s_lt[nfull].stride == 32) ++nfull;
     int4* sh4 = reinterpret_cast<int4*>(sh);
     uint32_t r0 = lo;
     do {
@@ -315,53 +452,33 @@ inline __device__ void histogram_cta(const HistArgs& a, const HistJob& job, uint
             row = 0;
             packed = 0;
             if (p < w_hi) {
-                const uint32_t pos = job.begin + p;
-                if (job.identity) {
-                    row = pos;
-                    packed = __ldcs(a.packed + pos);
-                } else {
-                    row = __ldcg(rows + pos);  // written by this step's partition: not through the read-only path
-                    packed = __ldcg(ordered + pos);
-                }
+                uint32_t pk;
+                position_of(src, p, row, pk);
+                packed = static_cast<int32_t>(pk);
             }
         };
+        const bool partial = nfull < num_tiles && s_lt[nfull].active != 0;
         if (w_lo < w_hi) {
+            switch (nfull) {
+                case 1: hist_rows<1>(s_lt, partial, src, w_lo, w_hi, lane); break;
+                case 2: hist_rows<2>(s_lt, partial, src, w_lo, w_hi, lane); break;
+                case 3: hist_rows<3>(s_lt, partial, src, w_lo, w_hi, lane); break;
+                case 4: hist_rows<4>(s_lt, partial, src, w_lo, w_hi, lane); break;
+                default: break;
+            }
+        }
+        if (w_lo < w_hi && nfull == 0 && s_lt[0].active != 0) {
+            // a unit of one partial tile (the dataset's last): lane per row
             uint32_t next_row;
             int32_t next_packed;
             position(w_lo + lane, next_row, next_packed);
             for (uint32_t p0 = w_lo; p0 < w_hi; p0 += 32) {
                 const uint32_t row = next_row;
                 const uint32_t packed = static_cast<uint32_t>(next_packed);
-                // One tile ahead: tile t + 1's bytes are in flight while tile t's atomics issue (the first tile's
-                // together with the next batch's positions).
-                uint32_t cur[8] = {}, nxt[8] = {};
-                if (s_lt[0].active != 0) load_row(s_lt[0], row, cur);
+                uint32_t w[8] = {};
+                if (packed != 0) load_row(s_lt[0], row, w);
                 position(p0 + 32 + lane, next_row, next_packed);
-#pragma unroll
-                for (int t = 0; t < kMaxUnitTiles; ++t) {
-                    if (t >= static_cast<int>(num_tiles)) break;
-                    if (t + 1 < static_cast<int>(num_tiles) && s_lt[t + 1].active != 0)
-                        load_row(s_lt[t + 1], row, nxt);
-                    const LaneTile lt = s_lt[t];
-                    if (packed != 0 && lt.active != 0) {  // a zero row adds nothing
-                        switch (lt.stride) {
-                            case 32:
-                                add_row<8>(lt, cur, packed, lane);
-                                break;
-                            case 16:
-                                add_row<4>(lt, cur, packed, lane);
-                                break;
-                            case 8:
-                                add_row<2>(lt, cur, packed, lane);
-                                break;
-                            default:
-                                add_row<1>(lt, cur, packed, lane);
-                                break;
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
-                }
+                if (packed != 0) add_partial_row(s_lt[0], w, packed, lane);  // a zero row adds nothing
             }
         }
         __syncthreads();

@@ -118,6 +118,11 @@ void launch_bin_counts(const uint8_t* columns, uint64_t column_stride, uint64_t 
                        uint32_t num_feats, unsigned int* counts, cudaStream_t s);
 // Counts the operand pairs where the split scan's division (div_rn) differs from CUDA's correctly rounded one.
 void launch_division_check(uint64_t n, uint32_t seed, unsigned long long* mismatches, int grid, cudaStream_t s);
+// diag.cu: `red.shared.add.u32` alone at the histogram's address patterns (0: every lane its own bins; 1: one bin
+// per instruction), `ctas` CTAs of 512 threads; *adds lane adds made, *cycles SM clock cycles summed over the CTAs,
+// *seconds the launch's duration.
+cudaError_t time_shared_adds(int pattern, int ctas, uint32_t passes, cudaStream_t stream, double* adds, double* cycles,
+                             double* seconds);
 void launch_api_find_split(const DevData& d, const int* hist, const uint8_t* evaluate, double ug, double uh,
                            int64_t count, double gs, double hs, const sb2_split_config& cfg, void* cands,
                            unsigned int* counter, sb2_split_info* out, uint8_t* splittable, int grid, cudaStream_t s);

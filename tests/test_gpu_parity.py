@@ -35,6 +35,9 @@ SHAPES = [
     ([255] * 28, 60_000),
     ([255] * 70 + [64] * 30, 40_000),
     ([63] * 40 + [2, 3, 200], 30_000),
+    # units of two and of four full tiles (row-chunk loads of 64- and 128-byte unit rows), then a unit of one
+    ([255] * 64 + [31] * 2, 30_000),
+    ([255] * 128 + [15] * 160, 20_000),
 ]
 
 

@@ -275,17 +275,20 @@ __device__ __forceinline__ void stage_full(const LaneTile* lt, uint32_t wanted, 
     }
 }
 
-// Whole warp: a landed batch's full-tile rows of slot `slot` (packed gradients at `gh`) into the shared sums.
-template <int F>
-__device__ __forceinline__ void add_staged_full(const ChunkLane& k, uint32_t slot, uint32_t gh, uint32_t lane) {
-    constexpr uint32_t C = 2 * F;
+// Whole warp: a landed batch's full-tile rows of slot `slot` (packed gradients at `gh`) into the shared sums: lane
+// k reads chunk k mod P of row g R + k / P (P = chunk_period, R = 32 / P) and adds only its own tile's chunks
+// (FixedChunk); kSkip: the unit has a Tile::skip tile.
+template <int F, bool kSkip>
+__device__ __forceinline__ void add_staged_full(const FixedChunk& f, uint32_t slot, uint32_t gh, uint32_t lane) {
+    constexpr uint32_t C = chunk_period<F>(), R = 32 / C;
+    if (!f.on) return;
+    const uint32_t c = lane % C;
 #pragma unroll
     for (uint32_t g = 0; g < C; ++g) {
-        const uint32_t m = 32 * g + lane, c = m % C;
-        if (!((k.wanted >> (c >> 1)) & 1u)) continue;
-        const uint32_t packed = lds32(gh + 4 * (m / C));
+        const uint32_t row = g * R + lane / C;
+        const uint32_t packed = lds32(gh + 4 * row);
         if (packed == 0) continue;  // past the range, or a zero gradient: not copied, adds nothing
-        add_chunk(k, c >> 1, lds128(slot + 16 * m), packed);
+        add_fixed<kSkip>(f, lds128(slot + row * (32 * F) + 16 * c), packed);
     }
 }
 
@@ -387,7 +390,10 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
         ++nfull;
     }
     const bool partial = nfull < nt && lt[nfull].active != 0;
-    const ChunkLane ck = chunk_lane(lt, nfull, lane);
+    const ChunkLane ck = chunk_lane(lt, nfull, lane, true);
+    const uint32_t period = nfull == 3 ? 8u : 2u * nfull;  // chunk_period
+    const FixedChunk fk = fixed_chunk(ck, nfull > 0 ? (lane % period) >> 1 : 0);
+    const bool skips = ck.skip != 0;
     const uint32_t mine = stage + warp * depth * slot_bytes;
     const uint32_t gh_off = slot_bytes - 128;  // the slot's packed gradients
     uint32_t next_row, next_packed;  // the position of batch `issued`, loaded one issue ahead
@@ -415,11 +421,15 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
         __syncwarp();                   // ... and every lane's: a lane adds chunks other lanes copied
         const uint32_t slot = mine + use_slot * slot_bytes;
         use_slot = use_slot + 1 == depth ? 0 : use_slot + 1;
-        switch (nfull) {
-            case 1: add_staged_full<1>(ck, slot, slot + gh_off, lane); break;
-            case 2: add_staged_full<2>(ck, slot, slot + gh_off, lane); break;
-            case 3: add_staged_full<3>(ck, slot, slot + gh_off, lane); break;
-            case 4: add_staged_full<4>(ck, slot, slot + gh_off, lane); break;
+        switch (nfull * 2 + (skips ? 1 : 0)) {
+            case 2: add_staged_full<1, false>(fk, slot, slot + gh_off, lane); break;
+            case 3: add_staged_full<1, true>(fk, slot, slot + gh_off, lane); break;
+            case 4: add_staged_full<2, false>(fk, slot, slot + gh_off, lane); break;
+            case 5: add_staged_full<2, true>(fk, slot, slot + gh_off, lane); break;
+            case 6: add_staged_full<3, false>(fk, slot, slot + gh_off, lane); break;
+            case 7: add_staged_full<3, true>(fk, slot, slot + gh_off, lane); break;
+            case 8: add_staged_full<4, false>(fk, slot, slot + gh_off, lane); break;
+            case 9: add_staged_full<4, true>(fk, slot, slot + gh_off, lane); break;
             default: break;
         }
         if (partial) {

@@ -173,7 +173,9 @@ struct ChunkLane {
     uint32_t wanted;                 // bit t: full tile t has a wanted feature
 };
 
-__device__ __forceinline__ ChunkLane chunk_lane(const LaneTile* lt, uint32_t nfull, uint32_t lane) {
+// `skips`: Tile::skip tiles skip their stored bin 0 (the tree kernel, which recovers those bins from the rows'
+// totals); the standalone histogram adds every stored bin and maps the exchanged bins back in its reduction.
+__device__ __forceinline__ ChunkLane chunk_lane(const LaneTile* lt, uint32_t nfull, uint32_t lane, bool skips) {
     ChunkLane k;
     k.r = lane >> 1;
     k.skip = 0;
@@ -185,30 +187,10 @@ __device__ __forceinline__ ChunkLane chunk_lane(const LaneTile* lt, uint32_t nfu
         if (t >= static_cast<int>(nfull)) continue;
         const LaneTile l = lt[t];
         k.addr[t] = l.addr | off;  // the tile's array is 128-byte aligned
-        if (l.skip) k.skip |= 1u << t;
+        if (skips && l.skip) k.skip |= 1u << t;
         if (l.active != 0) k.wanted |= 1u << t;
     }
     return k;
-}
-
-// One lane's 16 bytes of full tile `t`, added at their features (stored bin 0 skipped in a Tile::skip tile).
-__device__ __forceinline__ void add_chunk(const ChunkLane& k, uint32_t t, uint4 v, uint32_t packed) {
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    xor_bytes<4>(w, k.r);
-    const uint32_t base = k.addr[0] * (t == 0) + k.addr[1] * (t == 1) + k.addr[2] * (t == 2) + k.addr[3] * (t == 3);
-    if ((k.skip >> t) & 1u) {
-#pragma unroll
-        for (int s = 0; s < 16; ++s) {
-            const uint32_t bin = (w[s >> 2] >> (8 * (s & 3))) & 0xFFu;
-            shared_add_nonzero(bin * 128u + (base ^ (4u * s)), packed, bin);
-        }
-    } else {
-#pragma unroll
-        for (int s = 0; s < 16; ++s) {
-            const uint32_t bin = (w[s >> 2] >> (8 * (s & 3))) & 0xFFu;
-            shared_add(bin * 128u + (base ^ (4u * s)), packed);
-        }
-    }
 }
 
 // Adds one loaded row of a partial tile (stride 4, 8 or 16) at every feature: add_row by stride.
@@ -227,16 +209,73 @@ __device__ __forceinline__ void add_partial_row(const LaneTile& l, const uint32_
     }
 }
 
+// When lane k's chunk c is the same in every instruction (chunk_period), its tile is fixed and every per-step
+// quantity is a lane constant: the step's shared address at bin 0, the byte selector that
+// extracts the step's byte (its word swapped into place once per chunk), and whether stored bin 0 adds. An element
+// then costs a byte_perm, a multiply-add and the atomic.
+struct FixedChunk {
+    uint32_t off[16];   // step s: shared address of feature 16 (lane mod 2) + (s ^ r) of the lane's tile at bin 0
+    uint32_t bsel[4];   // step s: __byte_perm selector of byte (s ^ r) mod 4 (zero-extended)
+    uint32_t wq;        // r / 4: the chunk's words are swapped by it (word j to j ^ wq)
+    bool skip;          // the lane's tile skips stored bin 0 (Tile::skip, tree kernel only)
+    bool on;            // the lane's tile has a wanted feature
+};
+
+__device__ __forceinline__ FixedChunk fixed_chunk(const ChunkLane& k, uint32_t t) {
+    FixedChunk f;
+    const uint32_t base = k.addr[0] * (t == 0) + k.addr[1] * (t == 1) + k.addr[2] * (t == 2) + k.addr[3] * (t == 3);
+#pragma unroll
+    for (int s = 0; s < 16; ++s) f.off[s] = base ^ (4u * s);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) f.bsel[q] = ((static_cast<uint32_t>(q) ^ k.r) & 3u) | 0x4440u;
+    f.wq = k.r >> 2;
+    f.skip = (k.skip >> t) & 1u;
+    f.on = (k.wanted >> t) & 1u;
+    return f;
+}
+
+// One lane's 16 bytes of its fixed tile added at their features; kSkip: stored bin 0 adds nothing where f.skip.
+template <bool kSkip>
+__device__ __forceinline__ void add_fixed(const FixedChunk& f, uint4 v, uint32_t packed) {
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    // word j of the chunk to position j ^ wq
+    {
+        const bool s1 = f.wq & 1u, s2 = f.wq & 2u;
+        uint32_t a = s1 ? w[1] : w[0], b = s1 ? w[0] : w[1], c = s1 ? w[3] : w[2], d = s1 ? w[2] : w[3];
+        w[0] = s2 ? c : a;
+        w[1] = s2 ? d : b;
+        w[2] = s2 ? a : c;
+        w[3] = s2 ? b : d;
+    }
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+        const uint32_t bin = __byte_perm(w[s >> 2], 0u, f.bsel[s & 3]);
+        if (kSkip && f.skip)
+            shared_add_nonzero(bin * 128u + f.off[s], packed, bin);
+        else
+            shared_add(bin * 128u + f.off[s], packed);
+    }
+}
+
+// The lanes' chunk period of F full tiles: 2F chunks a row, except F = 3, whose 6 chunks a row take 8 lanes (the
+// last two idle) so that a lane's chunk, and with it its tile, is the same in every instruction.
+template <int F>
+__host__ __device__ constexpr uint32_t chunk_period() { return F == 3 ? 8u : 2u * F; }
+
 // Whole warp: positions [p_lo, p_hi) of `src` into the unit's shared sums, in batches of 32 positions: the F full
-// tiles in row chunks (ChunkLane), a partial tile `lp` (when `partial`) lane per row. Lane k loads position k's row
-// and packed gradient one batch ahead; a chunk's row and gradient come from the lane that loaded them.
+// tiles in row chunks, R = 32 / P rows an instruction (P = chunk_period), lane k taking chunk k mod P of row k / P
+// and adding only its own tile (FixedChunk); a partial tile `lp` (when `partial`) lane per row. Lane k loads
+// position k's row and packed gradient one batch ahead; a chunk's row and gradient come from the lane that loaded
+// them.
 template <int F>
 __device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, const PositionSource& src,
                                           uint32_t p_lo, uint32_t p_hi, uint32_t lane) {
-    constexpr uint32_t C = 2 * F;
-    const ChunkLane k = chunk_lane(lt, F, lane);
+    constexpr uint32_t C = chunk_period<F>(), R = 32 / C;
+    const ChunkLane k = chunk_lane(lt, F, lane, false);
+    const uint32_t c = lane % C;
+    const FixedChunk f = fixed_chunk(k, c >> 1);  // with F = 3, lanes of chunks 6 and 7 are off (no tile 3)
     const LaneTile lp = lt[partial ? F : 0];
-    const uint8_t* rows0 = lt[0].base;
+    const uint8_t* chunk = lt[0].base + 16 * c;
     const uint32_t pitch = lt[0].pitch;
     auto position = [&](uint32_t p, uint32_t& row, uint32_t& packed) {
         row = 0;
@@ -251,21 +290,18 @@ __device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, cons
         uint32_t pk[C];
 #pragma unroll
         for (uint32_t g = 0; g < C; ++g) {
-            const uint32_t m = 32 * g + lane, c = m % C;
-            const uint32_t rw = __shfl_sync(0xffffffffu, row, static_cast<int>(m / C));
-            pk[g] = __shfl_sync(0xffffffffu, packed, static_cast<int>(m / C));
+            const int src_lane = static_cast<int>(g * R + lane / C);
+            const uint32_t rw = __shfl_sync(0xffffffffu, row, src_lane);
+            pk[g] = __shfl_sync(0xffffffffu, packed, src_lane);
             v[g] = make_uint4(0, 0, 0, 0);
-            if (pk[g] != 0 && ((k.wanted >> (c >> 1)) & 1u))
-                v[g] = __ldcs(reinterpret_cast<const uint4*>(rows0 + static_cast<uint64_t>(rw) * pitch + 16 * c));
+            if (pk[g] != 0 && f.on) v[g] = __ldcs(reinterpret_cast<const uint4*>(chunk + static_cast<uint64_t>(rw) * pitch));
         }
         uint32_t wp[8] = {};
         if (partial && packed != 0) load_row(lp, row, wp);
         position(p0 + 32 + lane, next_row, next_packed);
 #pragma unroll
-        for (uint32_t g = 0; g < C; ++g) {
-            const uint32_t c = (32 * g + lane) % C;
-            if (pk[g] != 0 && ((k.wanted >> (c >> 1)) & 1u)) add_chunk(k, c >> 1, v[g], pk[g]);
-        }
+        for (uint32_t g = 0; g < C; ++g)
+            if (pk[g] != 0 && f.on) add_fixed<false>(f, v[g], pk[g]);
         if (partial && packed != 0) add_partial_row(lp, wp, packed, lane);
     }
 }

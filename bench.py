@@ -84,7 +84,7 @@ CONFIGS = {
     "c2": Config("c2", 1, 10_000_000, "binary", 255, 255, 500, ["gauss"] * 70 + ["unif"] * 30, 885.0),
     "c3": Config("c3", 2, 2_000_000, "lambdarank", 255, 127, 300,
                  ["gauss"] * 60 + ["lognormal"] * 40 + ["zeros30"] * 36),
-    "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256, 1902.0),
+    "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256, 1797.0),
     # 80% of the features zero-dominant (every fifth feature is N(0,1), the rest 95% zeros)
     "c5": Config("c5", 4, 5_000_000, "binary", 63, 31, 200,
                  ["gauss" if f % 5 == 0 else "sparse95" for f in range(2000)]),

@@ -390,7 +390,9 @@ int sb2_profile_steps(sb2_backend* b, const sb2_params* params, double init_scor
  * (padding columns 0); `features` and `groups` are as in sb2_dataset (each group's features, columns and row
  * stride; `data` unused). Building a large dataset in chunks of rows: call once per chunk, with the chunk's values
  * and each group_data[g] advanced by the chunk's first row × row_stride. A group whose bounds and categories
- * exceed 200 KiB returns SB2_EUNSUPPORTED. Returns when done. */
+ * exceed 200 KiB returns SB2_EUNSUPPORTED. Values in device memory must be on the handle's device (else SB2_EDATA)
+ * and completely written before the call: it reads them on the handle's own stream, which is not ordered after the
+ * caller's streams, so the caller synchronizes the stream that produced them first. Returns when done. */
 int sb2_bin_dense(sb2_backend* b, const void* values, int value_bytes, uint64_t rows, uint32_t cols, int row_major,
                   const sb2_feature* features, uint32_t num_features, const sb2_group* groups, uint32_t num_groups,
                   uint8_t* const* group_data);

@@ -97,17 +97,21 @@ def params_from_dict(params: dict) -> _abi.Params:
 
 def _matrix_view(values):
     """(pointer, rows, cols, value bytes, row-major, keep-alive) of a 2-D float32/float64 matrix: a numpy array
-    (C- or Fortran-ordered) or a CUDA torch tensor (contiguous or its transpose)."""
+    (C- or Fortran-ordered) or a CUDA torch tensor (contiguous or its transpose). A tensor's producing work is
+    finished first: the library's stream is not ordered after torch's, so a kernel still writing the tensor would
+    race with the call's reads."""
     if hasattr(values, "data_ptr") and getattr(values, "is_cuda", False):
+        import torch
+
         if values.dim() != 2 or values.element_size() not in (4, 8) or not values.is_floating_point():
             raise ValueError("a 2-D float32 or float64 tensor")
         rows, cols = values.shape
+        if not values.is_contiguous() and not values.t().is_contiguous():
+            values = values.contiguous()
+        torch.cuda.current_stream(values.device).synchronize()
         if values.is_contiguous():
             return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), True, values
-        if values.t().is_contiguous():
-            return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), False, values
-        values = values.contiguous()
-        return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), True, values
+        return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), False, values
     a = np.asarray(values)
     if a.ndim != 2 or a.dtype not in (np.float32, np.float64):
         raise ValueError("a 2-D float32 or float64 array")

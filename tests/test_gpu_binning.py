@@ -42,6 +42,26 @@ def test_hashed_matrices(device):
     b.close()
 
 
+def test_device_input_written_by_a_late_kernel(device):
+    """A CUDA tensor whose last write is still queued on torch's stream when bin_dense is called: the values are
+    binned as written, not as the memory held before (the library's stream is not ordered after torch's; the
+    binding waits for the producing stream). The write is held back by a spin on torch's stream."""
+    import torch
+
+    b = B200Backend(0)
+    values, feats, groups = hashed_case(50_000, 24, seed=21, dtype=np.float32, per_group=8)
+    want = orc.bin_rows(values, feats, groups)
+    src = torch.from_numpy(values).cuda()
+    for _ in range(2):
+        t = torch.full_like(src, float("nan"))
+        torch.cuda.synchronize()
+        torch.cuda._sleep(200_000_000)  # about 0.1 s of SM cycles on torch's stream before the copy
+        t.copy_(src)
+        got = b.bin_dense(t, feats, groups)
+        assert all(np.array_equal(x, y) for x, y in zip(got, want))
+    b.close()
+
+
 def test_device_input_and_chunks(device):
     """A CUDA tensor as input (row-major and its transpose), and 600,000 × 128 f32 values: two chunks."""
     import torch

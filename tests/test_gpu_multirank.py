@@ -27,8 +27,9 @@ WORKER = Path(__file__).resolve().parent / "multirank_worker.py"
 # config c2's shape (100 features, binary) at 1M rows: 255-leaf trees run grid steps of eight splits; c5's (2,000
 # features, 80% of them 95% zeros) at 200K rows with the dominant-bin skip: every rank skips its own most frequent
 # bins and recovers them from its own totals before the exchange; categorical features, whose candidates carry their
-# left bins through the exchange
-CASES = [("c2", 1_000_000, 3, 255, None), ("c5", 200_000, 3, 31, 0.125), ("categorical", 400_000, 3, 63, None)]
+# left bins through the exchange; c4's (256 features in two histogram units, L2 with a constant hessian)
+CASES = [("c2", 1_000_000, 3, 255, None), ("c5", 200_000, 3, 31, 0.125), ("categorical", 400_000, 3, 63, None),
+         ("c4", 2_000_000, 2, 255, None)]
 
 
 def run_ranks(world, mode, config, rows, trees, leaves, share, tmp_path, port):

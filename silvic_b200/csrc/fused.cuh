@@ -11,11 +11,10 @@
 // that buffer, which the CTA histograms itself, every lane busy, and flushes to its slab. The grid meets once, after
 // which the slabs are reduced and the children searched.
 //
-// The histogram streams its rows' bins into shared memory with cp.async: each warp keeps `depth` batches of 32 rows
-// in flight in its own staging slots while it adds an earlier batch, so the gathers of a leaf's scattered rows
-// overlap the shared atomics instead of waiting for them. The full tiles' bytes move in row chunks (a copy
-// instruction reads whole rows, a shared read 512 consecutive bytes), so the L1 data pipe, which the shared atomics
-// keep busy, spends few wavefronts on the loads.
+// The histogram reads its rows' bins straight into registers in row chunks (hist_rows, hist_device.cuh): a warp's
+// load covers whole rows, and each warp keeps the next batch's positions in flight while it adds the current one. A
+// unit of one partial tile streams its rows through shared memory with cp.async instead, `depth` batches of 32 rows
+// in flight per warp.
 //
 // A CTA's packed shared sums are exact for at most `round_rows` rows (packed_round_rows); when its range is that
 // short it flushes the packed sums as they are (half the bytes) and the reduction unpacks them, else it flushes
@@ -249,48 +248,8 @@ __device__ __forceinline__ void cp_async_wait(uint32_t pending) {
 }
 
 
-// Staging slot of a batch: the rows of the unit's full tiles (32 features each, side by side: 32 F bytes a row, row
-// i at i * 32 F), then a partial tile's 32 rows of `stride` bytes (lane k's row at LaneTile::stage_off + k * stride),
-// then the batch's 32 packed gradients. The full tiles move in row chunks (ChunkLane, hist_device.cuh): copy g of a
-// lane is chunk 32 g + lane, so a copy instruction reads whole rows (4 rows of 128 bytes: 4 lines, where a piece of
-// each of 32 rows touches 32) and a shared read takes 512 consecutive bytes.
-
-// Whole warp: the copies of a batch's full-tile rows into slot `slot`: chunk m = 32 i + lane is chunk m mod 2F of
-// the batch's row m / 2F, whose row id and packed gradient lane m / 2F holds (`row`, `packed`); rows with a zero
-// gradient are not copied (they add nothing). `wanted`: bit t, full tile t has a wanted feature.
-template <int F>
-__device__ __forceinline__ void stage_full(const LaneTile* lt, uint32_t wanted, uint32_t slot, uint32_t row,
-                                           uint32_t packed, uint32_t lane, uint64_t pol) {
-    constexpr uint32_t C = 2 * F;
-    const uint8_t* base = lt[0].base;
-    const uint32_t pitch = lt[0].pitch;
-#pragma unroll
-    for (uint32_t i = 0; i < C; ++i) {
-        const uint32_t m = 32 * i + lane;
-        const uint32_t src_lane = m / C, c = m % C;
-        const uint32_t rw = __shfl_sync(0xffffffffu, row, static_cast<int>(src_lane));
-        const uint32_t pk = __shfl_sync(0xffffffffu, packed, static_cast<int>(src_lane));
-        if (pk != 0 && ((wanted >> (c >> 1)) & 1u))
-            cp_async16(slot + 16 * m, base + static_cast<uint64_t>(rw) * pitch + 16 * c, pol);
-    }
-}
-
-// Whole warp: a landed batch's full-tile rows of slot `slot` (packed gradients at `gh`) into the shared sums: lane
-// k reads chunk k mod P of row g R + k / P (P = chunk_period, R = 32 / P) and adds only its own tile's chunks
-// (FixedChunk); kSkip: the unit has a Tile::skip tile.
-template <int F, bool kSkip>
-__device__ __forceinline__ void add_staged_full(const FixedChunk& f, uint32_t slot, uint32_t gh, uint32_t lane) {
-    constexpr uint32_t C = chunk_period<F>(), R = 32 / C;
-    if (!f.on) return;
-    const uint32_t c = lane % C;
-#pragma unroll
-    for (uint32_t g = 0; g < C; ++g) {
-        const uint32_t row = g * R + lane / C;
-        const uint32_t packed = lds32(gh + 4 * row);
-        if (packed == 0) continue;  // past the range, or a zero gradient: not copied, adds nothing
-        add_fixed<kSkip>(f, lds128(slot + row * (32 * F) + 16 * c), packed);
-    }
-}
+// Staging slot of a batch (a unit of one partial tile): its 32 rows of `stride` bytes (lane k's row at k * stride),
+// then the batch's 32 packed gradients.
 
 // Lane's copies of row `row`'s bytes of the unit's partial tile (tile `t`, stride below 32) into slot `slot`.
 __device__ __forceinline__ void stage_partial(const LaneTile& l, uint32_t slot, uint32_t row, uint32_t lane,
@@ -352,6 +311,36 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
                                             uint64_t pol, bool count, int& tg, int& th) {
     constexpr uint32_t kWarps = kHistThreads / 32;
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // A unit with full tiles (and a partial tile after them): each warp a contiguous share of the positions, its
+    // rows' bytes loaded straight into registers in row chunks (hist_rows), one batch of 32 positions at a time with
+    // the next batch's positions in flight: no staging, so the warp never waits for a copy to land before it adds.
+    uint32_t nfull = 0;
+    bool skips = false;
+    for (uint32_t t = 0; t < nt; ++t) skips = skips || lt[t].skip != 0;
+    while (nfull < nt && lt[nfull].stride == 32) ++nfull;
+    if (nfull > 0) {
+        const bool partial = nfull < nt && lt[nfull].active != 0;
+        const uint32_t span = b1 > b0 ? b1 - b0 : 0u;
+        const uint32_t per_warp = static_cast<uint32_t>(ceil_div(ceil_div(span, kWarps), 32) * 32);
+        const uint32_t w_lo = b0 + min(span, per_warp * warp), w_hi = b0 + min(span, per_warp * (warp + 1));
+        if (w_lo >= w_hi) return;
+        const PositionSource ps{src.rows, src.gh, 0u, src.identity};
+        int* ptg = count ? &tg : nullptr;
+        int* pth = count ? &th : nullptr;
+        switch (nfull * 2 + (skips ? 1 : 0)) {
+            case 2: hist_rows<1, false>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 3: hist_rows<1, true>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 4: hist_rows<2, false>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 5: hist_rows<2, true>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 6: hist_rows<3, false>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 7: hist_rows<3, true>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 8: hist_rows<4, false>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            case 9: hist_rows<4, true>(lt, partial, ps, w_lo, w_hi, lane, ptg, pth); break;
+            default: break;
+        }
+        return;
+    }
+    // A unit of one partial tile (the dataset's last, narrower than 32 features): its rows staged lane per row.
     const uint32_t nb = b1 > b0 ? static_cast<uint32_t>(ceil_div(b1 - b0, 32)) : 0u;
     const uint32_t n = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0u;  // this warp's batches
     // The row and packed gradient of lane's position in the warp's batch i (packed 0 past the range).
@@ -383,17 +372,7 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
         }
         return;
     }
-    // The unit's full tiles (the leading ones, stride 32) move in row chunks; a partial tile lane per row.
-    uint32_t nfull = 0, wanted = 0;
-    while (nfull < nt && lt[nfull].stride == 32) {
-        if (lt[nfull].active != 0) wanted |= 1u << nfull;
-        ++nfull;
-    }
-    const bool partial = nfull < nt && lt[nfull].active != 0;
-    const ChunkLane ck = chunk_lane(lt, nfull, lane, true);
-    const uint32_t period = nfull == 3 ? 8u : 2u * nfull;  // chunk_period
-    const FixedChunk fk = fixed_chunk(ck, nfull > 0 ? (lane % period) >> 1 : 0);
-    const bool skips = ck.skip != 0;
+    const LaneTile& lp = lt[0];  // the unit's one tile
     const uint32_t mine = stage + warp * depth * slot_bytes;
     const uint32_t gh_off = slot_bytes - 128;  // the slot's packed gradients
     uint32_t next_row, next_packed;  // the position of batch `issued`, loaded one issue ahead
@@ -402,40 +381,18 @@ __device__ __forceinline__ void hist_stream(const LaneTile* lt, uint32_t nt, con
     for (uint32_t i = 0; i < n; ++i) {
         while (issued < n && issued < i + depth) {
             const uint32_t slot = mine + issue_slot * slot_bytes;
-            __syncwarp();  // every lane is done reading the slot's previous batch (lanes read each other's copies)
             sts32(slot + gh_off + 4 * lane, next_packed);
-            switch (nfull) {
-                case 1: stage_full<1>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
-                case 2: stage_full<2>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
-                case 3: stage_full<3>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
-                case 4: stage_full<4>(lt, wanted, slot, next_row, next_packed, lane, pol); break;
-                default: break;
-            }
-            if (partial && next_packed != 0) stage_partial(lt[nfull], slot, next_row, lane, pol);  // zero adds nothing
+            if (next_packed != 0) stage_partial(lp, slot, next_row, lane, pol);  // a zero gradient adds nothing
             cp_async_commit();
             ++issued;
             issue_slot = issue_slot + 1 == depth ? 0 : issue_slot + 1;
             if (issued < n) position(issued, next_row, next_packed);
         }
-        cp_async_wait(issued - i - 1);  // batch i's copies (this lane's) have landed
-        __syncwarp();                   // ... and every lane's: a lane adds chunks other lanes copied
+        cp_async_wait(issued - i - 1);  // batch i's copies (this lane's own row) have landed
         const uint32_t slot = mine + use_slot * slot_bytes;
         use_slot = use_slot + 1 == depth ? 0 : use_slot + 1;
-        switch (nfull * 2 + (skips ? 1 : 0)) {
-            case 2: add_staged_full<1, false>(fk, slot, slot + gh_off, lane); break;
-            case 3: add_staged_full<1, true>(fk, slot, slot + gh_off, lane); break;
-            case 4: add_staged_full<2, false>(fk, slot, slot + gh_off, lane); break;
-            case 5: add_staged_full<2, true>(fk, slot, slot + gh_off, lane); break;
-            case 6: add_staged_full<3, false>(fk, slot, slot + gh_off, lane); break;
-            case 7: add_staged_full<3, true>(fk, slot, slot + gh_off, lane); break;
-            case 8: add_staged_full<4, false>(fk, slot, slot + gh_off, lane); break;
-            case 9: add_staged_full<4, true>(fk, slot, slot + gh_off, lane); break;
-            default: break;
-        }
-        if (partial) {
-            const uint32_t packed = lds32(slot + gh_off + 4 * lane);
-            if (packed != 0) add_staged_partial(lt[nfull], slot, packed, lane);
-        }
+        const uint32_t packed = lds32(slot + gh_off + 4 * lane);
+        if (packed != 0 && lp.active != 0) add_staged_partial(lp, slot, packed, lane);
     }
 }
 

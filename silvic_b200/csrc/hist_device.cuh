@@ -9,7 +9,7 @@
 // h arrays (stored the first time, added afterwards) and clears them.
 //
 // Work per warp: a range of consecutive positions of the leaf. The unit's full tiles (32 features each, side by side
-// in rows of up to 128 bytes) are read in row chunks (add_full_tiles): lane k loads 16 bytes of a row such that one
+// in rows of up to 128 bytes) are read in row chunks (hist_rows): lane k loads 16 bytes of a row such that one
 // 128-bit load of the warp covers whole rows, permutes them by a lane constant and walks them, so that the 32 lanes
 // of every atomic hit 32 different features, i.e. 32 different banks. A partial tile (fewer than 32 features, in its
 // own region) is read lane per row: lane k loads position k's row and at step i adds feature i XOR (k mod stride).
@@ -193,18 +193,21 @@ __device__ __forceinline__ ChunkLane chunk_lane(const LaneTile* lt, uint32_t nfu
     return k;
 }
 
-// Adds one loaded row of a partial tile (stride 4, 8 or 16) at every feature: add_row by stride.
+// Adds one loaded row of a partial tile (stride 4, 8 or 16) at every feature: add_row by stride; with kSkip, a
+// Tile::skip tile adds no stored bin 0.
+template <bool kSkip = false>
 __device__ __forceinline__ void add_partial_row(const LaneTile& l, const uint32_t (&w)[8], uint32_t packed,
                                                 uint32_t lane) {
+    const bool skip = kSkip && l.skip;
     switch (l.stride) {
         case 16:
-            add_row<4>(l, w, packed, lane);
+            if (skip) add_row<4, true>(l, w, packed, lane); else add_row<4>(l, w, packed, lane);
             break;
         case 8:
-            add_row<2>(l, w, packed, lane);
+            if (skip) add_row<2, true>(l, w, packed, lane); else add_row<2>(l, w, packed, lane);
             break;
         default:
-            add_row<1>(l, w, packed, lane);
+            if (skip) add_row<1, true>(l, w, packed, lane); else add_row<1>(l, w, packed, lane);
             break;
     }
 }
@@ -267,11 +270,12 @@ __host__ __device__ constexpr uint32_t chunk_period() { return F == 3 ? 8u : 2u 
 // and adding only its own tile (FixedChunk); a partial tile `lp` (when `partial`) lane per row. Lane k loads
 // position k's row and packed gradient one batch ahead; a chunk's row and gradient come from the lane that loaded
 // them.
-template <int F>
+template <int F, bool kSkip = false>
 __device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, const PositionSource& src,
-                                          uint32_t p_lo, uint32_t p_hi, uint32_t lane) {
+                                          uint32_t p_lo, uint32_t p_hi, uint32_t lane, int* tg = nullptr,
+                                          int* th = nullptr) {
     constexpr uint32_t C = chunk_period<F>(), R = 32 / C;
-    const ChunkLane k = chunk_lane(lt, F, lane, false);
+    const ChunkLane k = chunk_lane(lt, F, lane, kSkip);
     const uint32_t c = lane % C;
     const FixedChunk f = fixed_chunk(k, c >> 1);  // with F = 3, lanes of chunks 6 and 7 are off (no tile 3)
     const LaneTile lp = lt[partial ? F : 0];
@@ -280,7 +284,14 @@ __device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, cons
     auto position = [&](uint32_t p, uint32_t& row, uint32_t& packed) {
         row = 0;
         packed = 0;
-        if (p < p_hi) position_of(src, p, row, packed);
+        if (p < p_hi) {
+            position_of(src, p, row, packed);
+            if (tg != nullptr) {  // the rows' totals (quantize.rs:140-143), for the recovery of skipped bins
+                const int g = static_cast<int16_t>(packed & 0xFFFFu);
+                *tg += g;
+                *th += static_cast<int>((packed - static_cast<uint32_t>(g)) >> 16);
+            }
+        }
     };
     uint32_t next_row, next_packed;
     position(p_lo + lane, next_row, next_packed);
@@ -301,8 +312,8 @@ __device__ __forceinline__ void hist_rows(const LaneTile* lt, bool partial, cons
         position(p0 + 32 + lane, next_row, next_packed);
 #pragma unroll
         for (uint32_t g = 0; g < C; ++g)
-            if (pk[g] != 0 && f.on) add_fixed<false>(f, v[g], pk[g]);
-        if (partial && packed != 0) add_partial_row(lp, wp, packed, lane);
+            if (pk[g] != 0 && f.on) add_fixed<kSkip>(f, v[g], pk[g]);
+        if (partial && packed != 0) add_partial_row<kSkip>(lp, wp, packed, lane);
     }
 }
 

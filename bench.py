@@ -81,7 +81,7 @@ class Config:
 
 CONFIGS = {
     "c1": Config("c1", 0, 1_000_000, "regression", 255, 63, 100, ["gauss"] * 28),
-    "c2": Config("c2", 1, 10_000_000, "binary", 255, 255, 500, ["gauss"] * 70 + ["unif"] * 30),
+    "c2": Config("c2", 1, 10_000_000, "binary", 255, 255, 500, ["gauss"] * 70 + ["unif"] * 30, 1207.0),
     "c3": Config("c3", 2, 2_000_000, "lambdarank", 255, 127, 300,
                  ["gauss"] * 60 + ["lognormal"] * 40 + ["zeros30"] * 36),
     "c4": Config("c4", 3, 100_000_000, "regression", 255, 255, 200, ["gauss"] * 256, 1797.0),

@@ -160,12 +160,11 @@ __device__ __forceinline__ void position_of(const PositionSource& s, uint32_t p,
 }
 
 // The lane constants of row-chunk work over a unit's full tiles (its first F tiles: 32 features each, side by side
-// in rows of 32 F bytes). A batch of 32 rows is 64 F chunks of 16 bytes, chunk m = row * 2F + c holding features
-// 16 (c mod 2) .. of tile c / 2; instruction g of the batch gives lane k chunk m = 32 g + k, so a warp's load (or
-// copy, or shared read) covers 512 consecutive bytes of whole rows, where a lane-per-row load of 32 scattered rows
-// touches 32 lines for the same bytes. Lane k permutes its 16 bytes by r = k / 2 (xor_bytes) and at step s adds
-// feature 16 (k mod 2) + (s ^ r) of its chunk's tile (chunk m has the parity of k): the 32 atomics of a step hit 32
-// different feature lanes, i.e. 32 banks, for any F.
+// in rows of 32 F bytes). A row is 2F chunks of 16 bytes, chunk c holding features 16 (c mod 2) .. of tile c / 2.
+// In load g of a batch, lane k takes chunk k mod P of row g R + k / P (P = chunk_period, R = 32 / P rows a load), so
+// a warp's load covers R whole rows, where a lane-per-row load of 32 scattered rows touches 32 lines for the same
+// bytes. Lane k permutes its 16 bytes by r = k / 2 and at step s adds feature 16 (k mod 2) + (s ^ r) of its chunk's
+// tile (chunk c has the parity of k): the 32 atomics of a step hit 32 different feature lanes, i.e. 32 banks.
 struct ChunkLane {
     uint32_t r;                      // the byte permutation: lane / 2
     uint32_t addr[kMaxUnitTiles];    // per full tile: shared address of this lane's feature lane 16 (lane mod 2) + r

@@ -251,7 +251,7 @@ __device__ __forceinline__ void cp_async_wait(uint32_t pending) {
 // Staging slot of a batch (a unit of one partial tile): its 32 rows of `stride` bytes (lane k's row at k * stride),
 // then the batch's 32 packed gradients.
 
-// Lane's copies of row `row`'s bytes of the unit's partial tile (tile `t`, stride below 32) into slot `slot`.
+// Lane's copies of row `row`'s bytes of partial tile `l` (stride below 32) into slot `slot`.
 __device__ __forceinline__ void stage_partial(const LaneTile& l, uint32_t slot, uint32_t row, uint32_t lane,
                                               uint64_t pol) {
     const uint8_t* src = l.base + static_cast<uint64_t>(row) * l.pitch;

@@ -740,10 +740,12 @@ int sb2_load(sb2_backend* b, const sb2_dataset* train, const sb2_objective* obje
     per_sm = std::max(per_sm, 1);
     // The persistent tree kernel runs every phase in the same CTAs: its shared memory also holds the partition's
     // scan and the search's bins.
-    // Layout (GrowSmem): the histogram's arrays, the partition's scan words, the histogram's staging slots (all three
-    // used in the same phase), then the per-feature flags ((5 kSplits + 1) F bytes); the search's bins (kMaxBins [g, h] pairs per
-    // group of warps, 4 KB in all) reuse the scan words. Staging gets what is left of the CTA's shared memory, up to
-    // kMaxStageDepth slots per warp.
+    // Layout (GrowSmem): the histogram's arrays, the partition's scan words, the staging area (all three used in the
+    // same phase), then the per-feature flags ((5 kSplits + 1) F bytes); the search's bins (kMaxBins [g, h] pairs per
+    // group of warps, 4 KB in all) reuse the scan words. The staging area gets what is left of the CTA's shared
+    // memory, up to kMaxStageDepth slots of a unit's 32 rows per warp: the histogram stages the rows of a unit of one
+    // partial tile there (full tiles go straight to registers), the flush transposes the shared sums through it, and
+    // the search reduces and prefetches slab bins in it.
     {
         GrowSmem& m = b->grow_smem;
         m.scan_offset = static_cast<uint32_t>((b->hist_smem + 15) / 16 * 16);

@@ -97,8 +97,8 @@ def params_from_dict(params: dict) -> _abi.Params:
 
 def _matrix_view(values):
     """(pointer, rows, cols, value bytes, row-major, keep-alive) of a 2-D float32/float64 matrix: a numpy array
-    (C- or Fortran-ordered) or a CUDA torch tensor (contiguous or its transpose). A tensor's producing work is
-    finished first: the library's stream is not ordered after torch's, so a kernel still writing the tensor would
+    (C- or Fortran-ordered) or a CUDA torch tensor (contiguous or its transpose). A tensor's device finishes its queued
+    work first: the library's stream is not ordered after torch's streams, so a kernel still writing the tensor would
     race with the call's reads."""
     if hasattr(values, "data_ptr") and getattr(values, "is_cuda", False):
         import torch
@@ -108,7 +108,7 @@ def _matrix_view(values):
         rows, cols = values.shape
         if not values.is_contiguous() and not values.t().is_contiguous():
             values = values.contiguous()
-        torch.cuda.current_stream(values.device).synchronize()
+        torch.cuda.synchronize(values.device)  # whichever of torch's streams wrote it
         if values.is_contiguous():
             return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), True, values
         return C.c_void_p(values.data_ptr()), rows, cols, values.element_size(), False, values

@@ -45,7 +45,7 @@ def test_hashed_matrices(device):
 def test_device_input_written_by_a_late_kernel(device):
     """A CUDA tensor whose last write is still queued on torch's stream when bin_dense is called: the values are
     binned as written, not as the memory held before (the library's stream is not ordered after torch's; the
-    binding waits for the producing stream). The write is held back by a spin on torch's stream."""
+    binding waits for the tensor's device). The write is held back by a spin on torch's stream."""
     import torch
 
     b = B200Backend(0)
